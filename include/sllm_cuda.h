@@ -1,0 +1,254 @@
+/*
+ * sllm_cuda.h -- the C ABI of the B200 (sm_100a) backend for saphira-llm's
+ * I2_S ternary decode path.
+ *
+ * Everything here is plain C: pointers, sizes and int status codes. No CUDA,
+ * torch or C++ type crosses this boundary, so saphira-llm's C11 host code can
+ * include this header and link libsllm_cuda.so directly. A stream is passed as
+ * `void *` (a cudaStream_t value; NULL means the legacy default stream).
+ *
+ * Each entry point names the reference interface it replaces, as
+ * path:line inside the saphira-llm source tree.
+ *
+ * Conventions, held by every function below:
+ *   - Status codes are numerically identical to saphira-llm's sllm_status
+ *     (include/saphira_llm/status.h:26-56), so a caller can return them
+ *     unchanged. Three new negative codes name device-side failures.
+ *   - The kernel-level functions take DEVICE pointers and are asynchronous on
+ *     the given stream. The model-level functions take HOST pointers and
+ *     return when their results are on the host.
+ *   - Once this backend is selected there is no CPU fallback. A missing or
+ *     unsuitable device is reported as SLLM_CUDA_ERR_UNSUPPORTED, never
+ *     silently computed on the host.
+ */
+#ifndef SLLM_CUDA_H
+#define SLLM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#  define SLLM_CUDA_API __attribute__((visibility("default")))
+#else
+#  define SLLM_CUDA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ */
+/* status codes                                                        */
+/* ------------------------------------------------------------------ */
+
+#define SLLM_CUDA_OK               0    /* SLLM_OK                  */
+#define SLLM_CUDA_ERR_ARG         (-1)  /* SLLM_ERR_ARG             */
+#define SLLM_CUDA_ERR_NOMEM       (-2)  /* SLLM_ERR_NOMEM: host or device allocation failed */
+#define SLLM_CUDA_ERR_IO          (-3)  /* SLLM_ERR_IO              */
+#define SLLM_CUDA_ERR_UNSUPPORTED (-4)  /* SLLM_ERR_UNSUPPORTED: no sm_100 device, or a shape this backend does not run */
+#define SLLM_CUDA_ERR_TOO_LARGE   (-36) /* SLLM_ERR_TOO_LARGE       */
+#define SLLM_CUDA_ERR_DEVICE      (-60) /* a CUDA runtime call or kernel launch failed */
+#define SLLM_CUDA_ERR_TIMEOUT     (-61) /* a bounded device-side wait ran out; the context stays usable */
+#define SLLM_CUDA_ERR_COMM        (-62) /* a collective between devices failed */
+
+/* Stable, human-readable name for a status. Never NULL. */
+SLLM_CUDA_API const char * sllm_cuda_status_string(int status);
+
+/* The message recorded with the most recent failure on this thread, or "". */
+SLLM_CUDA_API const char * sllm_cuda_last_error(void);
+
+/*
+ * Capability probe for the dispatch row (src/dispatch.c:246
+ * sllm_dispatch_resolve, src/i2s_gemm.c:315 sllm_i2s_select_auto).
+ * Reports the device count and the compute capability of device 0.
+ * Returns SLLM_CUDA_ERR_UNSUPPORTED when no device of compute capability
+ * 10.x is visible. Any output pointer may be NULL.
+ */
+SLLM_CUDA_API int sllm_cuda_probe(int * n_devices, int * cc_major, int * cc_minor);
+
+/* ------------------------------------------------------------------ */
+/* kernel level: device pointers, asynchronous on `stream`             */
+/* ------------------------------------------------------------------ */
+
+/* Layout-identical to sllm_i2s_act (include/saphira_llm/i2s_gemm.h:37-40). */
+typedef struct sllm_cuda_act {
+    float   scale;   /* 127 / amax, or 0 for an all-zero row */
+    int32_t sum;     /* sum of the quantised values          */
+} sllm_cuda_act;
+
+/*
+ * Per-token int8 absmax quantisation of one row of `n` floats.
+ * Replaces sllm_i2s_quant_act (include/saphira_llm/i2s_gemm.h:57,
+ * src/i2s_gemm.c:45-83) with identical results: amax without a floor,
+ * scale = 127/amax (IEEE division), q = clamp(roundf(x*scale)), sum of q.
+ * `act_out` is one device struct. n must be >= 1 and <= 65536.
+ */
+SLLM_CUDA_API int sllm_cuda_i2s_quant_act(const float * x, size_t n, int8_t * q_out,
+                            sllm_cuda_act * act_out, void * stream);
+
+/*
+ * Raw I2_S GEMV: rows_out[r] = sum over k of code(w, r, k) * q[k], the
+ * 2-bit code (0, 1 or 2) times the int8 activation, in int32.
+ * Replaces sllm_i2s_gemv (include/saphira_llm/i2s_gemm.h:81,
+ * src/i2s_gemm.c:260-269) bit for bit. `w` is the packed tensor as stored in
+ * the GGUF (rows of n/4 bytes, I2_S interleaved layout). Unlike the reference,
+ * which silently returns 0 for n < 128, this returns SLLM_CUDA_ERR_ARG for
+ * n % 128 != 0 (the loader refuses such tensors anyway, src/forward.c:306-316).
+ * n must be <= 65536.
+ */
+SLLM_CUDA_API int sllm_cuda_i2s_gemv(const uint8_t * w, size_t n_rows, size_t n,
+                       const int8_t * q, int32_t * rows_out, void * stream);
+
+/*
+ * Fused float GEMV: quantise x (as sllm_cuda_i2s_quant_act), run the raw GEMV
+ * and apply the epilogue y[r] = (float)(dot[r] - act.sum) * (w_scale / act.scale),
+ * where w_scale is the f32 stored after the packed weights
+ * (src/quant.c:102-106). This is the sequence src/forward.c:651-655 runs for
+ * every projection, and the epilogue grouping is sllm_i2s_epilogue's
+ * (src/i2s_gemm.c:271-290). `dots` (nullable) receives the raw int32 dots.
+ */
+SLLM_CUDA_API int sllm_cuda_i2s_gemv_f32(const uint8_t * w, size_t n_rows, size_t n,
+                           const float * x, float * y, int32_t * dots,
+                           void * stream);
+
+/* ------------------------------------------------------------------ */
+/* model level: host pointers                                          */
+/* ------------------------------------------------------------------ */
+
+/*
+ * One bitnet-b1.58 layer as the reference loader records it
+ * (src/forward.c:47-54, filled at src/forward.c:391-444). The I2_S pointers
+ * address packed tensors INCLUDING their scale tail (rows * cols / 4 bytes of
+ * codes, then the f32 scale and 28 pad bytes). All pointers are host memory
+ * and are only read during sllm_cuda_model_upload.
+ */
+typedef struct sllm_cuda_layer_desc {
+    const uint8_t * wq;        /* n_embd     x n_embd  */
+    const uint8_t * wk;        /* n_embd_gqa x n_embd  */
+    const uint8_t * wv;        /* n_embd_gqa x n_embd  */
+    const uint8_t * wo;        /* n_embd     x n_embd  */
+    const uint8_t * ffn_gate;  /* n_ff       x n_embd  */
+    const uint8_t * ffn_up;    /* n_ff       x n_embd  */
+    const uint8_t * ffn_down;  /* n_embd     x n_ff    */
+    const float   * attn_norm;      /* n_embd */
+    const float   * attn_sub_norm;  /* n_embd */
+    const float   * ffn_norm;       /* n_embd */
+    const float   * ffn_sub_norm;   /* n_ff   */
+} sllm_cuda_layer_desc;
+
+/*
+ * The model hyperparameters and tensors (src/forward.c:56-76; metadata keys
+ * read at src/forward.c:348-366). `tok_embd` is the F16 [n_vocab][n_embd]
+ * embedding that is also the tied output head.
+ */
+typedef struct sllm_cuda_model_desc {
+    int32_t n_layer;
+    int32_t n_embd;
+    int32_t n_ff;
+    int32_t n_head;
+    int32_t n_head_kv;
+    int32_t n_vocab;
+    int32_t n_rot;
+    int32_t n_ctx_train;
+    float   f_rms_eps;
+    float   rope_freq_base;
+    const uint16_t * tok_embd;     /* F16 bits, n_vocab * n_embd */
+    const float    * output_norm;  /* n_embd */
+    const sllm_cuda_layer_desc * layers;  /* n_layer entries */
+} sllm_cuda_model_desc;
+
+typedef struct sllm_cuda_model sllm_cuda_model;
+typedef struct sllm_cuda_ctx   sllm_cuda_ctx;
+
+/*
+ * Copy a model to device `device` once; the device copy is immutable and may
+ * be shared by several contexts. Validates the same shape rules as
+ * sllm_model_load (src/forward.c:368-444): returns SLLM_CUDA_ERR_ARG for a
+ * NULL desc or tensor, SLLM_CUDA_ERR_UNSUPPORTED for widths this backend does
+ * not run (n_embd or n_ff not a multiple of 128 or above 65536, a head dim
+ * n_embd / n_head other than 128, n_rot other than the head dim,
+ * n_head % n_head_kv != 0), SLLM_CUDA_ERR_NOMEM when device memory runs out.
+ * Pairs with sllm_model_load / sllm_model_free (include/saphira_llm/forward.h:32-33).
+ */
+SLLM_CUDA_API int  sllm_cuda_model_upload(const sllm_cuda_model_desc * desc, int device,
+                            sllm_cuda_model ** out);
+SLLM_CUDA_API void sllm_cuda_model_free(sllm_cuda_model * m);
+
+/*
+ * A context owns the device-resident KV cache (fp32, [layer][head_kv][pos][dim],
+ * src/forward.c:81-83) and the scratch of one sequence.
+ * Replaces sllm_ctx_new / sllm_ctx_free / sllm_ctx_reset
+ * (include/saphira_llm/forward.h:44-48, src/forward.c:466-562).
+ */
+SLLM_CUDA_API int  sllm_cuda_ctx_new(const sllm_cuda_model * m, int32_t n_ctx,
+                       sllm_cuda_ctx ** out);
+SLLM_CUDA_API void sllm_cuda_ctx_free(sllm_cuda_ctx * c);
+SLLM_CUDA_API void sllm_cuda_ctx_reset(sllm_cuda_ctx * c);
+
+/* Tokens consumed so far (the reference's n_past). */
+SLLM_CUDA_API int32_t sllm_cuda_ctx_n_past(const sllm_cuda_ctx * c);
+
+/*
+ * Run `n` tokens at absolute positions [base, base+n) and write n * n_vocab
+ * logits to `logits_out` (host, may be NULL when only `argmax_out` is wanted).
+ * `argmax_out` (host, nullable) receives the argmax of each position's logits
+ * (lowest index on ties, src/forward.c:876-883). Argument rules and status
+ * codes follow sllm_forward_chunk (include/saphira_llm/forward.h:107-109,
+ * src/forward.c:589-609): n in [1, 256], base >= n_past, base + n <= n_ctx,
+ * tokens in [0, n_vocab).
+ */
+SLLM_CUDA_API int sllm_cuda_forward_chunk(const sllm_cuda_model * m, sllm_cuda_ctx * c,
+                            const int32_t * tokens, int32_t n, int32_t base,
+                            float * logits_out, int32_t * argmax_out);
+
+/*
+ * Greedy generation, replacing sllm_generate_greedy
+ * (include/saphira_llm/forward.h:136-138, src/forward.c:885-938), including
+ * its BOS fallback (128000) and its continuation from the last logits when
+ * n_prompt == 0. The whole loop runs on the device: one token id crosses back
+ * per generated token only at the end, in `out` (n_new ids).
+ */
+SLLM_CUDA_API int sllm_cuda_generate_greedy(const sllm_cuda_model * m, sllm_cuda_ctx * c,
+                              const int32_t * prompt, int32_t n_prompt,
+                              int32_t n_new, int32_t * out);
+
+/*
+ * The projection chain of layers [layer_begin, layer_begin + n_layers) without
+ * attention -- the workload the benchmark measures as "one layer's seven I2_S
+ * GEMVs with RMSNorm between them": attn_norm -> quant -> Q, K, V; Q stands in
+ * for the attention output -> attn_sub_norm -> quant -> O -> + x; ffn_norm ->
+ * quant -> gate, up -> silu(gate) * up -> ffn_sub_norm -> quant -> down ->
+ * + residual. Every step is the decode layer's own (src/forward.c:631-801),
+ * with the same rounding. `x_in` / `x_out` are host arrays of n_embd floats
+ * (they may alias). Uses the context's scratch and stream; it does not touch
+ * the KV cache or n_past.
+ */
+SLLM_CUDA_API int sllm_cuda_layer_chain(const sllm_cuda_model * m, sllm_cuda_ctx * c,
+                          int32_t layer_begin, int32_t n_layers,
+                          const float * x_in, float * x_out);
+
+/*
+ * The same chain on a device vector `x` (n_embd floats, 16-byte aligned,
+ * updated in place), asynchronous on `stream`. It uses the context's scratch
+ * buffers, so it must not overlap other work on the same context.
+ */
+SLLM_CUDA_API int sllm_cuda_layer_chain_device(const sllm_cuda_model * m, sllm_cuda_ctx * c,
+                                 int32_t layer_begin, int32_t n_layers,
+                                 float * x, void * stream);
+
+/* Bytes of weights one decode step streams: every I2_S tensor with its scale
+ * tail, every norm, and the F16 embedding / output head. */
+SLLM_CUDA_API size_t sllm_cuda_model_weight_bytes(const sllm_cuda_model * m);
+
+/*
+ * Copy the most recent position's logits (n_vocab floats) to host memory.
+ * Replaces sllm_ctx_last_logits (include/saphira_llm/forward.h:77).
+ * Returns SLLM_CUDA_ERR_ARG if nothing has been forwarded yet.
+ */
+SLLM_CUDA_API int sllm_cuda_ctx_last_logits(const sllm_cuda_ctx * c, float * host_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SLLM_CUDA_H */

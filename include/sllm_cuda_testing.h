@@ -1,0 +1,31 @@
+/*
+ * sllm_cuda_testing.h -- test hooks of libsllm_cuda.so. Not part of the
+ * product interface: no reference call site corresponds to these, and a
+ * production caller never needs them.
+ */
+#ifndef SLLM_CUDA_TESTING_H
+#define SLLM_CUDA_TESTING_H
+
+#include "sllm_cuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/*
+ * Force every certified double-precision sum (RMSNorm mean, softmax
+ * normaliser) to take its reference-order fallback, so tests can show that
+ * the fallback gives the same bits as the fast path. Read when a kernel is
+ * launched, and baked into a context's decode graph when the graph is first
+ * captured (its first forward), so set it before creating the context.
+ */
+SLLM_CUDA_API void sllm_cuda_test_set_force_fallback(int on);
+
+/* How many times a fallback ran in this process (or -1 without a device). */
+SLLM_CUDA_API int sllm_cuda_test_fallback_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SLLM_CUDA_TESTING_H */

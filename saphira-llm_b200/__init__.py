@@ -1,0 +1,206 @@
+"""saphira-llm B200 backend: Python binding of libsllm_cuda.so (include/sllm_cuda.h).
+
+The product is the C ABI in libsllm_cuda.so; saphira-llm's C11 host code calls
+it directly. This module binds the same entry points with
+ctypes for the tests, the benchmark and Python callers. Device buffers are
+passed as raw pointers (or torch CUDA tensors, whose data_ptr() is used); the
+library never falls back to the CPU: loading fails loudly if the built library
+is missing, and every call returns its status as an exception.
+"""
+import ctypes as C
+import os
+
+from . import abi
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libsllm_cuda.so")
+
+_lib = None
+
+
+class SllmCudaError(RuntimeError):
+    def __init__(self, status, where, msg=""):
+        self.status = status
+        super().__init__(f"{where}: {abi.STATUS_NAMES.get(status, status)} ({status}) {msg}".rstrip())
+
+
+def build():
+    """Compile libsllm_cuda.so in place (nvcc, sm_100a)."""
+    import subprocess
+    subprocess.run(["make", "-s", "-C", HERE, "-j4"], check=True)
+
+
+def lib():
+    """The loaded libsllm_cuda.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise FileNotFoundError(f"{LIB_PATH} is not built: run `make -C saphira-llm_b200`")
+    L = C.CDLL(LIB_PATH)
+    vp, sz, i32 = C.c_void_p, C.c_size_t, C.c_int32
+    L.sllm_cuda_status_string.argtypes = [C.c_int]
+    L.sllm_cuda_status_string.restype = C.c_char_p
+    L.sllm_cuda_last_error.restype = C.c_char_p
+    L.sllm_cuda_probe.argtypes = [C.POINTER(C.c_int)] * 3
+    L.sllm_cuda_i2s_quant_act.argtypes = [vp, sz, vp, vp, vp]
+    L.sllm_cuda_i2s_gemv.argtypes = [vp, sz, sz, vp, vp, vp]
+    L.sllm_cuda_i2s_gemv_f32.argtypes = [vp, sz, sz, vp, vp, vp, vp]
+    L.sllm_cuda_model_upload.argtypes = [C.POINTER(abi.ModelDesc), C.c_int, C.POINTER(vp)]
+    L.sllm_cuda_model_free.argtypes = [vp]
+    L.sllm_cuda_model_weight_bytes.argtypes = [vp]
+    L.sllm_cuda_model_weight_bytes.restype = sz
+    L.sllm_cuda_ctx_new.argtypes = [vp, i32, C.POINTER(vp)]
+    L.sllm_cuda_ctx_free.argtypes = [vp]
+    L.sllm_cuda_ctx_reset.argtypes = [vp]
+    L.sllm_cuda_ctx_n_past.argtypes = [vp]
+    L.sllm_cuda_ctx_n_past.restype = i32
+    L.sllm_cuda_forward_chunk.argtypes = [vp, vp, vp, i32, i32, vp, vp]
+    L.sllm_cuda_generate_greedy.argtypes = [vp, vp, vp, i32, i32, vp]
+    L.sllm_cuda_ctx_last_logits.argtypes = [vp, vp]
+    L.sllm_cuda_layer_chain.argtypes = [vp, vp, i32, i32, vp, vp]
+    L.sllm_cuda_layer_chain_device.argtypes = [vp, vp, i32, i32, vp, vp]
+    L.sllm_cuda_test_set_force_fallback.argtypes = [C.c_int]
+    L.sllm_cuda_test_fallback_count.restype = C.c_int
+    _lib = L
+    return L
+
+
+def _check(rc, where):
+    if rc != abi.OK:
+        raise SllmCudaError(rc, where, lib().sllm_cuda_last_error().decode(errors="replace"))
+
+
+def _ptr(t):
+    """A raw device (or host) address from a torch tensor, numpy array or int."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    if hasattr(t, "data_ptr"):
+        return t.data_ptr()
+    if hasattr(t, "ctypes"):
+        return t.ctypes.data
+    raise TypeError(type(t))
+
+
+def _stream(s):
+    if s is None:
+        return None
+    if isinstance(s, int):
+        return s
+    return s.cuda_stream
+
+
+def probe():
+    n, ma, mi = C.c_int(), C.c_int(), C.c_int()
+    rc = lib().sllm_cuda_probe(C.byref(n), C.byref(ma), C.byref(mi))
+    return rc, n.value, (ma.value, mi.value)
+
+
+# kernel level (device pointers, asynchronous) ---------------------------------
+def quant_act(x, n, q, act, stream=None):
+    _check(lib().sllm_cuda_i2s_quant_act(_ptr(x), n, _ptr(q), _ptr(act), _stream(stream)), "quant_act")
+
+
+def gemv(w, n_rows, n, q, out, stream=None):
+    _check(lib().sllm_cuda_i2s_gemv(_ptr(w), n_rows, n, _ptr(q), _ptr(out), _stream(stream)), "gemv")
+
+
+def gemv_f32(w, n_rows, n, x, y, dots=None, stream=None):
+    _check(lib().sllm_cuda_i2s_gemv_f32(_ptr(w), n_rows, n, _ptr(x), _ptr(y), _ptr(dots), _stream(stream)),
+           "gemv_f32")
+
+
+def set_force_fallback(on):
+    lib().sllm_cuda_test_set_force_fallback(1 if on else 0)
+
+
+def fallback_count():
+    return lib().sllm_cuda_test_fallback_count()
+
+
+# model level (host pointers) -------------------------------------------------
+class Model:
+    """A model uploaded to one device (sllm_cuda_model_upload)."""
+
+    def __init__(self, desc, device=0):
+        self.desc = desc
+        self.h = C.c_void_p()
+        _check(lib().sllm_cuda_model_upload(C.byref(desc), device, C.byref(self.h)), "model_upload")
+
+    def weight_bytes(self):
+        return lib().sllm_cuda_model_weight_bytes(self.h)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().sllm_cuda_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def ctx(self, n_ctx):
+        return Ctx(self, n_ctx)
+
+
+class Ctx:
+    """One sequence's device state: KV cache, scratch, decode graph."""
+
+    def __init__(self, model, n_ctx):
+        import numpy as np
+        self._np = np
+        self.model = model
+        self.n_vocab = model.desc.n_vocab
+        self.n_embd = model.desc.n_embd
+        self.h = C.c_void_p()
+        _check(lib().sllm_cuda_ctx_new(model.h, n_ctx, C.byref(self.h)), "ctx_new")
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().sllm_cuda_ctx_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def reset(self):
+        lib().sllm_cuda_ctx_reset(self.h)
+
+    def n_past(self):
+        return lib().sllm_cuda_ctx_n_past(self.h)
+
+    def forward_chunk(self, tokens, base, want_logits=True):
+        np = self._np
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty((tokens.size, self.n_vocab), np.float32) if want_logits else None
+        am = np.empty(tokens.size, np.int32)
+        rc = lib().sllm_cuda_forward_chunk(self.model.h, self.h, tokens.ctypes.data, tokens.size, base,
+                                           None if logits is None else logits.ctypes.data, am.ctypes.data)
+        return rc, logits, am
+
+    def generate(self, prompt, n_new):
+        np = self._np
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros(max(n_new, 1), np.int32)
+        rc = lib().sllm_cuda_generate_greedy(self.model.h, self.h, prompt.ctypes.data if prompt.size else None,
+                                             prompt.size, n_new, out.ctypes.data)
+        return rc, out[:n_new]
+
+    def last_logits(self):
+        np = self._np
+        out = np.empty(self.n_vocab, np.float32)
+        rc = lib().sllm_cuda_ctx_last_logits(self.h, out.ctypes.data)
+        return None if rc != 0 else out
+
+    def layer_chain(self, layer_begin, n_layers, x):
+        np = self._np
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        _check(lib().sllm_cuda_layer_chain(self.model.h, self.h, layer_begin, n_layers, x.ctypes.data,
+                                           out.ctypes.data), "layer_chain")
+        return out
+
+    def layer_chain_device(self, layer_begin, n_layers, x_dev, stream=None):
+        _check(lib().sllm_cuda_layer_chain_device(self.model.h, self.h, layer_begin, n_layers, _ptr(x_dev),
+                                                  _stream(stream)), "layer_chain_device")

@@ -1,0 +1,626 @@
+// backend.cu -- the C ABI of include/sllm_cuda.h: kernel-level entry points,
+// device model upload, per-sequence contexts and the decode loop.
+//
+// One decode step (embedding, 30 x {QKV GEMV, attention, O GEMV, gate/up
+// GEMV, down GEMV}, lm_head + argmax) is captured once per context into a
+// CUDA graph. The token of each position, the position itself and the greedy
+// feedback live in device memory, so a whole prompt + generation is a run of
+// graph launches with no host round trip until the ids are copied back.
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "decode.cuh"
+#include "gemv.cuh"
+#include "../../include/sllm_cuda.h"
+#include "../../include/sllm_cuda_testing.h"
+
+using namespace sllm;
+
+// ---------------------------------------------------------------------------
+// status and errors
+// ---------------------------------------------------------------------------
+static thread_local std::string g_last_error;
+static int g_force_fallback = 0;
+static int* g_fallback_counter = nullptr;   // device int, lazily allocated per process
+
+static int fail(int status, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return status;
+}
+
+static int cuda_fail(cudaError_t e, const char* what) {
+    const int st = (e == cudaErrorMemoryAllocation) ? SLLM_CUDA_ERR_NOMEM : SLLM_CUDA_ERR_DEVICE;
+    cudaGetLastError();   // clear a sticky launch error where possible
+    return fail(st, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CK(call, what)                                        \
+    do {                                                      \
+        cudaError_t e_ = (call);                              \
+        if (e_ != cudaSuccess) return cuda_fail(e_, (what));  \
+    } while (0)
+
+extern "C" const char* sllm_cuda_status_string(int st) {
+    switch (st) {
+        case SLLM_CUDA_OK: return "ok";
+        case SLLM_CUDA_ERR_ARG: return "invalid argument";
+        case SLLM_CUDA_ERR_NOMEM: return "out of memory";
+        case SLLM_CUDA_ERR_IO: return "i/o error";
+        case SLLM_CUDA_ERR_UNSUPPORTED: return "unsupported";
+        case SLLM_CUDA_ERR_TOO_LARGE: return "too large";
+        case SLLM_CUDA_ERR_DEVICE: return "CUDA device error";
+        case SLLM_CUDA_ERR_TIMEOUT: return "device wait timed out";
+        case SLLM_CUDA_ERR_COMM: return "collective failed";
+        default: return "unknown status";
+    }
+}
+
+extern "C" const char* sllm_cuda_last_error(void) { return g_last_error.c_str(); }
+
+// ---------------------------------------------------------------------------
+// devices
+// ---------------------------------------------------------------------------
+static int num_sms_of(int dev) {
+    static std::mutex mu;
+    static std::vector<int> cache;
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)cache.size() <= dev) cache.resize(dev + 1, 0);
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+static int current_sms() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return num_sms_of(dev);
+}
+
+extern "C" int sllm_cuda_probe(int* n_devices, int* cc_major, int* cc_minor) {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (n_devices) *n_devices = (e == cudaSuccess) ? n : 0;
+    if (cc_major) *cc_major = 0;
+    if (cc_minor) *cc_minor = 0;
+    if (e != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(SLLM_CUDA_ERR_UNSUPPORTED, "no CUDA device: %s", cudaGetErrorString(e));
+    }
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, 0), "cudaGetDeviceProperties");
+    if (cc_major) *cc_major = prop.major;
+    if (cc_minor) *cc_minor = prop.minor;
+    if (prop.major != 10) return fail(SLLM_CUDA_ERR_UNSUPPORTED, "device 0 is sm_%d%d, this build runs sm_100a",
+                                      prop.major, prop.minor);
+    return SLLM_CUDA_OK;
+}
+
+static int* fallback_counter() {
+    if (g_fallback_counter == nullptr) {
+        if (cudaMalloc(&g_fallback_counter, sizeof(int)) != cudaSuccess) { g_fallback_counter = nullptr; return nullptr; }
+        cudaMemset(g_fallback_counter, 0, sizeof(int));
+    }
+    return g_fallback_counter;
+}
+
+extern "C" void sllm_cuda_test_set_force_fallback(int on) { g_force_fallback = on; }
+
+extern "C" int sllm_cuda_test_fallback_count(void) {
+    int* p = fallback_counter();
+    int v = -1;
+    if (p != nullptr && cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) v = -1;
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// kernel level
+// ---------------------------------------------------------------------------
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+extern "C" int sllm_cuda_i2s_quant_act(const float* x, size_t n, int8_t* q_out, sllm_cuda_act* act_out,
+                                       void* stream) {
+    if (x == nullptr || q_out == nullptr || act_out == nullptr || n == 0 || n > (size_t)kMaxK)
+        return fail(SLLM_CUDA_ERR_ARG, "quant_act: bad arguments (n=%zu)", n);
+    CK(launch_quant_act(x, (int)n, q_out, act_out, (cudaStream_t)stream), "quant_act launch");
+    return SLLM_CUDA_OK;
+}
+
+static int check_gemv_shape(const void* w, size_t n_rows, size_t n, const void* out) {
+    if (w == nullptr || out == nullptr || n_rows == 0 || n_rows > (1u << 30))
+        return fail(SLLM_CUDA_ERR_ARG, "gemv: bad arguments");
+    if (n % kQK != 0 || n == 0) return fail(SLLM_CUDA_ERR_ARG, "gemv: n=%zu is not a multiple of 128", n);
+    if (n > (size_t)gemv_max_k()) return fail(SLLM_CUDA_ERR_UNSUPPORTED, "gemv: n=%zu above %d", n, gemv_max_k());
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_i2s_gemv(const uint8_t* w, size_t n_rows, size_t n, const int8_t* q, int32_t* rows_out,
+                                  void* stream) {
+    int rc = check_gemv_shape(w, n_rows, n, rows_out);
+    if (rc != SLLM_CUDA_OK) return rc;
+    if (q == nullptr || !aligned16(q)) return fail(SLLM_CUDA_ERR_ARG, "gemv: q must be 16-byte aligned");
+    if (!aligned16(w)) return fail(SLLM_CUDA_ERR_ARG, "gemv: w must be 16-byte aligned");
+    // The raw API has no act: an all-zero act makes the prologue a plain copy.
+    static sllm_cuda_act* zero_act = nullptr;
+    if (zero_act == nullptr) {
+        CK(cudaMalloc(&zero_act, sizeof(sllm_cuda_act)), "cudaMalloc");
+        CK(cudaMemset(zero_act, 0, sizeof(sllm_cuda_act)), "cudaMemset");
+    }
+    GemvParams p{};
+    p.K = (int)n;
+    p.nseg = 1;
+    p.seg[0] = GemvSeg{w, (int)n_rows, nullptr, rows_out};
+    p.q_in = q;
+    p.act_in = zero_act;
+    CK(launch_gemv(p, PRO_Q8, EPI_DOTS, current_sms(), (cudaStream_t)stream), "gemv launch");
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_i2s_gemv_f32(const uint8_t* w, size_t n_rows, size_t n, const float* x, float* y,
+                                      int32_t* dots, void* stream) {
+    int rc = check_gemv_shape(w, n_rows, n, y);
+    if (rc != SLLM_CUDA_OK) return rc;
+    if (x == nullptr || !aligned16(x) || !aligned16(w)) return fail(SLLM_CUDA_ERR_ARG, "gemv_f32: x and w must be 16-byte aligned");
+    GemvParams p{};
+    p.K = (int)n;
+    p.nseg = 1;
+    p.seg[0] = GemvSeg{w, (int)n_rows, y, dots};
+    p.x = x;
+    CK(launch_gemv(p, PRO_QUANT, EPI_F32, current_sms(), (cudaStream_t)stream), "gemv_f32 launch");
+    return SLLM_CUDA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// model
+// ---------------------------------------------------------------------------
+struct DevLayer {
+    const uint8_t *wq, *wk, *wv, *wo, *gate, *up, *down;
+    const float *attn_norm, *attn_sub_norm, *ffn_norm, *ffn_sub_norm;
+};
+
+struct sllm_cuda_model {
+    int device = 0;
+    int n_layer = 0, n_embd = 0, n_ff = 0, n_head = 0, n_head_kv = 0, n_vocab = 0, n_rot = 0, n_ctx_train = 0;
+    int head_dim = 0, n_embd_gqa = 0;
+    float eps = 0.0f, rope_base = 0.0f;
+    uint8_t* blob = nullptr;        // every I2_S tensor and f32 norm, 256-byte aligned
+    uint16_t* tok_embd = nullptr;   // f16 [V][E]
+    float* output_norm = nullptr;
+    std::vector<DevLayer> layers;
+    size_t weight_bytes = 0;        // bytes one decode step streams
+};
+
+static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+extern "C" int sllm_cuda_model_upload(const sllm_cuda_model_desc* d, int device, sllm_cuda_model** out) {
+    if (d == nullptr || out == nullptr) return fail(SLLM_CUDA_ERR_ARG, "model_upload: NULL argument");
+    *out = nullptr;
+    if (d->n_layer <= 0 || d->n_embd <= 0 || d->n_head <= 0 || d->n_head_kv <= 0 || d->n_ff <= 0 ||
+        d->n_vocab <= 0 || d->n_head % d->n_head_kv != 0 || d->n_embd % d->n_head != 0 || d->layers == nullptr ||
+        d->tok_embd == nullptr || d->output_norm == nullptr)
+        return fail(SLLM_CUDA_ERR_ARG, "model_upload: invalid hyperparameters or tensors");
+    const int E = d->n_embd, F = d->n_ff, hd = E / d->n_head, G = hd * d->n_head_kv;
+    if (hd != 128 || d->n_rot != hd || E % kQK != 0 || F % kQK != 0 || E > gemv_max_k() || F > gemv_max_k())
+        return fail(SLLM_CUDA_ERR_UNSUPPORTED, "model_upload: shape E=%d F=%d head_dim=%d n_rot=%d not supported",
+                    E, F, hd, d->n_rot);
+    for (int l = 0; l < d->n_layer; ++l) {
+        const sllm_cuda_layer_desc& L = d->layers[l];
+        if (!L.wq || !L.wk || !L.wv || !L.wo || !L.ffn_gate || !L.ffn_up || !L.ffn_down || !L.attn_norm ||
+            !L.attn_sub_norm || !L.ffn_norm || !L.ffn_sub_norm)
+            return fail(SLLM_CUDA_ERR_ARG, "model_upload: layer %d has a NULL tensor", l);
+    }
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+        cudaGetLastError();
+        return fail(SLLM_CUDA_ERR_UNSUPPORTED, "model_upload: device %d not present", device);
+    }
+    CK(cudaSetDevice(device), "cudaSetDevice");
+
+    auto* m = new sllm_cuda_model();
+    m->device = device;
+    m->n_layer = d->n_layer; m->n_embd = E; m->n_ff = F; m->n_head = d->n_head; m->n_head_kv = d->n_head_kv;
+    m->n_vocab = d->n_vocab; m->n_rot = d->n_rot; m->n_ctx_train = d->n_ctx_train;
+    m->head_dim = hd; m->n_embd_gqa = G; m->eps = d->f_rms_eps; m->rope_base = d->rope_freq_base;
+
+    struct Item { const void* src; size_t bytes; size_t off; };
+    std::vector<Item> items;
+    size_t total = 0;
+    auto add = [&](const void* src, size_t bytes) { items.push_back({src, bytes, total}); total += align256(bytes); return items.size() - 1; };
+    auto i2s = [](int rows, int cols) { return (size_t)rows * (size_t)cols / 4 + 32; };
+    std::vector<size_t> idx;
+    for (int l = 0; l < d->n_layer; ++l) {
+        const sllm_cuda_layer_desc& L = d->layers[l];
+        idx.push_back(add(L.wq, i2s(E, E)));
+        idx.push_back(add(L.wk, i2s(G, E)));
+        idx.push_back(add(L.wv, i2s(G, E)));
+        idx.push_back(add(L.wo, i2s(E, E)));
+        idx.push_back(add(L.ffn_gate, i2s(F, E)));
+        idx.push_back(add(L.ffn_up, i2s(F, E)));
+        idx.push_back(add(L.ffn_down, i2s(E, F)));
+        idx.push_back(add(L.attn_norm, (size_t)E * 4));
+        idx.push_back(add(L.attn_sub_norm, (size_t)E * 4));
+        idx.push_back(add(L.ffn_norm, (size_t)E * 4));
+        idx.push_back(add(L.ffn_sub_norm, (size_t)F * 4));
+    }
+    const size_t out_norm = add(d->output_norm, (size_t)E * 4);
+    cudaError_t e = cudaMalloc(&m->blob, total);
+    if (e == cudaSuccess) e = cudaMalloc(&m->tok_embd, (size_t)d->n_vocab * (size_t)E * 2);
+    if (e != cudaSuccess) { sllm_cuda_model_free(m); return cuda_fail(e, "model_upload: cudaMalloc"); }
+    for (const Item& it : items) {
+        e = cudaMemcpy(m->blob + it.off, it.src, it.bytes, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) { sllm_cuda_model_free(m); return cuda_fail(e, "model_upload: weights"); }
+    }
+    e = cudaMemcpy(m->tok_embd, d->tok_embd, (size_t)d->n_vocab * (size_t)E * 2, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) { sllm_cuda_model_free(m); return cuda_fail(e, "model_upload: tok_embd"); }
+    m->layers.resize(d->n_layer);
+    for (int l = 0; l < d->n_layer; ++l) {
+        const size_t* ix = &idx[(size_t)l * 11];
+        DevLayer& L = m->layers[l];
+        L.wq = m->blob + items[ix[0]].off;  L.wk = m->blob + items[ix[1]].off;
+        L.wv = m->blob + items[ix[2]].off;  L.wo = m->blob + items[ix[3]].off;
+        L.gate = m->blob + items[ix[4]].off; L.up = m->blob + items[ix[5]].off;
+        L.down = m->blob + items[ix[6]].off;
+        L.attn_norm = (const float*)(m->blob + items[ix[7]].off);
+        L.attn_sub_norm = (const float*)(m->blob + items[ix[8]].off);
+        L.ffn_norm = (const float*)(m->blob + items[ix[9]].off);
+        L.ffn_sub_norm = (const float*)(m->blob + items[ix[10]].off);
+    }
+    m->output_norm = (float*)(m->blob + items[out_norm].off);
+    for (const Item& it : items) m->weight_bytes += it.bytes;
+    m->weight_bytes += (size_t)d->n_vocab * (size_t)E * 2;
+    *out = m;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" void sllm_cuda_model_free(sllm_cuda_model* m) {
+    if (m == nullptr) return;
+    cudaSetDevice(m->device);
+    cudaFree(m->blob);
+    cudaFree(m->tok_embd);
+    delete m;
+}
+
+extern "C" size_t sllm_cuda_model_weight_bytes(const sllm_cuda_model* m) { return m ? m->weight_bytes : 0; }
+
+// ---------------------------------------------------------------------------
+// context
+// ---------------------------------------------------------------------------
+struct sllm_cuda_ctx {
+    const sllm_cuda_model* m = nullptr;
+    int n_ctx = 0;
+    int n_past = 0;
+    bool have_logits = false;
+    cudaStream_t stream = nullptr;
+    float *k_cache = nullptr, *v_cache = nullptr;   // [layer][kvh][128][n_ctx], [layer][kvh][n_ctx][128]
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+    float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *ffn_inp = nullptr, *h = nullptr;
+    float* logits = nullptr;
+    float* chunk_logits = nullptr;
+    size_t chunk_cap = 0;
+    float* part_v = nullptr;
+    int* part_i = nullptr;
+    int* counter = nullptr;
+    int* argmax = nullptr;
+    int32_t *pos = nullptr, *tok_seq = nullptr, *prompt_end = nullptr, *argmax_hist = nullptr;
+    int32_t* pinned = nullptr;                       // small host staging
+    cudaGraphExec_t step = nullptr;
+    int lm_grid = 0;
+};
+
+// the reference's angle recurrence (src/ops.c:529-549), on the host libm
+static void rope_table(int n_ctx, int n_rot, float base, std::vector<float>& cs, std::vector<float>& sn) {
+    const int half = n_rot / 2;
+    cs.resize((size_t)n_ctx * half);
+    sn.resize((size_t)n_ctx * half);
+    volatile float vbase = base;                  // keep powf a run-time call
+    volatile float vexp = -2.0f / (float)n_rot;
+    const float theta_scale = powf(vbase, vexp);
+    for (int pos = 0; pos < n_ctx; ++pos) {
+        float th = (float)pos;
+        for (int k = 0; k < half; ++k) {
+            const float f = 1.0f * th;
+            cs[(size_t)pos * half + k] = cosf(f);
+            sn[(size_t)pos * half + k] = sinf(f);
+            th *= theta_scale;
+        }
+    }
+}
+
+extern "C" void sllm_cuda_ctx_free(sllm_cuda_ctx* c) {
+    if (c == nullptr) return;
+    cudaSetDevice(c->m->device);
+    if (c->step) cudaGraphExecDestroy(c->step);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    cudaFree(c->k_cache); cudaFree(c->v_cache); cudaFree(c->rope_cos); cudaFree(c->rope_sin);
+    cudaFree(c->x); cudaFree(c->q); cudaFree(c->k); cudaFree(c->v); cudaFree(c->attn);
+    cudaFree(c->ffn_inp); cudaFree(c->h); cudaFree(c->logits); cudaFree(c->chunk_logits);
+    cudaFree(c->part_v); cudaFree(c->part_i); cudaFree(c->counter); cudaFree(c->argmax);
+    cudaFree(c->pos); cudaFree(c->tok_seq); cudaFree(c->prompt_end); cudaFree(c->argmax_hist);
+    cudaFreeHost(c->pinned);
+    delete c;
+}
+
+extern "C" int sllm_cuda_ctx_new(const sllm_cuda_model* m, int32_t n_ctx, sllm_cuda_ctx** out) {
+    if (m == nullptr || out == nullptr || n_ctx <= 0) return fail(SLLM_CUDA_ERR_ARG, "ctx_new: bad arguments");
+    *out = nullptr;
+    if (n_ctx > attention_max_ctx())
+        return fail(SLLM_CUDA_ERR_TOO_LARGE, "ctx_new: n_ctx %d above %d", n_ctx, attention_max_ctx());
+    CK(cudaSetDevice(m->device), "cudaSetDevice");
+    CK(prepare_decode_kernels(), "kernel attributes");
+    auto* c = new sllm_cuda_ctx();
+    c->m = m;
+    c->n_ctx = n_ctx;
+    const size_t kv = (size_t)m->n_layer * (size_t)m->n_embd_gqa * (size_t)n_ctx;
+    const size_t E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa, V = m->n_vocab;
+    c->lm_grid = lm_head_grid(num_sms_of(m->device));
+    cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    auto A = [&](void** p, size_t bytes) { if (e == cudaSuccess) e = cudaMalloc(p, bytes); };
+    A((void**)&c->k_cache, kv * 4); A((void**)&c->v_cache, kv * 4);
+    A((void**)&c->rope_cos, (size_t)n_ctx * 64 * 4); A((void**)&c->rope_sin, (size_t)n_ctx * 64 * 4);
+    A((void**)&c->x, E * 4); A((void**)&c->q, E * 4); A((void**)&c->k, G * 4); A((void**)&c->v, G * 4);
+    A((void**)&c->attn, E * 4); A((void**)&c->ffn_inp, E * 4); A((void**)&c->h, F * 4);
+    A((void**)&c->logits, V * 4);
+    A((void**)&c->part_v, (size_t)c->lm_grid * 4); A((void**)&c->part_i, (size_t)c->lm_grid * 4);
+    A((void**)&c->counter, 4); A((void**)&c->argmax, 4);
+    A((void**)&c->pos, 4); A((void**)&c->tok_seq, (size_t)n_ctx * 4 + 4); A((void**)&c->prompt_end, 4);
+    A((void**)&c->argmax_hist, (size_t)n_ctx * 4);
+    if (e == cudaSuccess) e = cudaMallocHost(&c->pinned, 64);
+    if (e == cudaSuccess) e = cudaMemset(c->k_cache, 0, kv * 4);
+    if (e == cudaSuccess) e = cudaMemset(c->v_cache, 0, kv * 4);
+    if (e == cudaSuccess) e = cudaMemset(c->counter, 0, 4);
+    if (e == cudaSuccess) e = cudaMemset(c->pos, 0, 4);
+    if (e == cudaSuccess) e = cudaMemset(c->tok_seq, 0, (size_t)n_ctx * 4 + 4);
+    if (e == cudaSuccess) e = cudaMemset(c->prompt_end, 0, 4);
+    if (e != cudaSuccess) { sllm_cuda_ctx_free(c); return cuda_fail(e, "ctx_new"); }
+    std::vector<float> cs, sn;
+    rope_table(n_ctx, m->n_rot, m->rope_base, cs, sn);
+    e = cudaMemcpy(c->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(c->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) { sllm_cuda_ctx_free(c); return cuda_fail(e, "ctx_new: rope table"); }
+    *out = c;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" void sllm_cuda_ctx_reset(sllm_cuda_ctx* c) {
+    if (c == nullptr) return;
+    // Setting n_past = 0 is what makes a reset correct (every position is
+    // written before it is read); clearing the cache is defence in depth,
+    // as in src/forward.c:530-562.
+    cudaSetDevice(c->m->device);
+    const size_t kv = (size_t)c->m->n_layer * (size_t)c->m->n_embd_gqa * (size_t)c->n_ctx;
+    cudaMemsetAsync(c->k_cache, 0, kv * 4, c->stream);
+    cudaMemsetAsync(c->v_cache, 0, kv * 4, c->stream);
+    cudaStreamSynchronize(c->stream);
+    c->n_past = 0;
+    c->have_logits = false;
+}
+
+extern "C" int32_t sllm_cuda_ctx_n_past(const sllm_cuda_ctx* c) { return c ? c->n_past : 0; }
+
+// The projection chain of one layer (four fused GEMV launches).
+struct ChainBufs { float* x; float* q; float* k; float* v; float* ffn_inp; float* h; const float* attn; };
+
+static cudaError_t launch_layer(const sllm_cuda_model* m, int l, const ChainBufs& b, int* fb, int force,
+                                cudaStream_t st, bool with_attention, const AttnParams* ap) {
+    const DevLayer& L = m->layers[l];
+    const int E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa, sms = num_sms_of(m->device);
+    GemvParams p{};
+    p.eps = m->eps;
+    p.fallback_count = fb;
+    p.force_fallback = force;
+    // attn_norm -> Q, K, V (src/forward.c:631-666)
+    p.K = E; p.nseg = 3;
+    p.seg[0] = GemvSeg{L.wq, E, b.q, nullptr};
+    p.seg[1] = GemvSeg{L.wk, G, b.k, nullptr};
+    p.seg[2] = GemvSeg{L.wv, G, b.v, nullptr};
+    p.x = b.x; p.norm_w = L.attn_norm;
+    cudaError_t e = launch_gemv(p, PRO_NORM, EPI_F32, sms, st);
+    if (e != cudaSuccess) return e;
+    const float* attn_out = b.q;    // the benchmark chain feeds Q in place of attention
+    if (with_attention) {
+        e = launch_attention(*ap, m->n_head, st);
+        if (e != cudaSuccess) return e;
+        attn_out = b.attn;
+    }
+    // attn_sub_norm -> O, + residual (src/forward.c:728-750)
+    GemvParams o = p;
+    o.nseg = 1;
+    o.seg[0] = GemvSeg{L.wo, E, b.ffn_inp, nullptr};
+    o.x = attn_out; o.norm_w = L.attn_sub_norm; o.resid = b.x;
+    e = launch_gemv(o, PRO_NORM, EPI_RESID, sms, st);
+    if (e != cudaSuccess) return e;
+    // ffn_norm -> gate, up, silu(gate) * up (src/forward.c:752-779)
+    GemvParams f = p;
+    f.nseg = 2;
+    f.seg[0] = GemvSeg{L.gate, F, nullptr, nullptr};
+    f.seg[1] = GemvSeg{L.up, F, nullptr, nullptr};
+    f.x = b.ffn_inp; f.norm_w = L.ffn_norm; f.h_out = b.h;
+    e = launch_gemv(f, PRO_NORM, EPI_SILU, sms, st);
+    if (e != cudaSuccess) return e;
+    // ffn_sub_norm -> down, + residual (src/forward.c:781-801)
+    GemvParams dn = p;
+    dn.K = F; dn.nseg = 1;
+    dn.seg[0] = GemvSeg{L.down, E, b.x, nullptr};
+    dn.x = b.h; dn.norm_w = L.ffn_sub_norm; dn.resid = b.ffn_inp;
+    return launch_gemv(dn, PRO_NORM, EPI_RESID, sms, st);
+}
+
+static cudaError_t enqueue_step(sllm_cuda_ctx* c, cudaStream_t st) {
+    const sllm_cuda_model* m = c->m;
+    int* fb = fallback_counter();
+    cudaError_t e = launch_embed(m->tok_embd, c->tok_seq, c->pos, m->n_embd, m->n_vocab, c->x, st);
+    if (e != cudaSuccess) return e;
+    const size_t kv_layer = (size_t)m->n_embd_gqa * (size_t)c->n_ctx;
+    for (int l = 0; l < m->n_layer; ++l) {
+        AttnParams ap{};
+        ap.q = c->q; ap.k = c->k; ap.v = c->v;
+        ap.k_cache = c->k_cache + (size_t)l * kv_layer;
+        ap.v_cache = c->v_cache + (size_t)l * kv_layer;
+        ap.rope_cos = c->rope_cos; ap.rope_sin = c->rope_sin;
+        ap.pos_ptr = c->pos; ap.out = c->attn; ap.n_ctx = c->n_ctx;
+        ap.group = m->n_head / m->n_head_kv;
+        ap.attn_scale = 1.0f / sqrtf((float)m->head_dim);
+        ap.fallback_count = fb; ap.force_fallback = g_force_fallback;
+        ChainBufs b{c->x, c->q, c->k, c->v, c->ffn_inp, c->h, c->attn};
+        e = launch_layer(m, l, b, fb, g_force_fallback, st, true, &ap);
+        if (e != cudaSuccess) return e;
+    }
+    LmParams lp{};
+    lp.x = c->x; lp.norm_w = m->output_norm; lp.eps = m->eps; lp.embd = m->tok_embd;
+    lp.E = m->n_embd; lp.V = m->n_vocab; lp.logits = c->logits;
+    lp.part_v = c->part_v; lp.part_i = c->part_i; lp.counter = c->counter; lp.argmax_out = c->argmax;
+    lp.pos_ptr = c->pos; lp.tok_seq = c->tok_seq; lp.prompt_end = c->prompt_end; lp.argmax_hist = c->argmax_hist;
+    lp.n_ctx = c->n_ctx; lp.fallback_count = fb; lp.force_fallback = g_force_fallback;
+    return launch_lm_head(lp, c->lm_grid, st);
+}
+
+static int ensure_step_graph(sllm_cuda_ctx* c) {
+    if (c->step != nullptr) return SLLM_CUDA_OK;
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    cudaError_t e = enqueue_step(c, c->stream);
+    cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
+    if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); return cuda_fail(e, "capture decode step"); }
+    if (e2 != cudaSuccess) return cuda_fail(e2, "end capture");
+    e = cudaGraphInstantiate(&c->step, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) { c->step = nullptr; return cuda_fail(e, "instantiate decode step"); }
+    return SLLM_CUDA_OK;
+}
+
+// Run positions [base, base + n) whose tokens are already in tok_seq.
+static int run_steps(sllm_cuda_ctx* c, int base, int n, int prompt_end, float* chunk_logits_dev) {
+    int rc = ensure_step_graph(c);
+    if (rc != SLLM_CUDA_OK) return rc;
+    c->pinned[0] = base;
+    c->pinned[1] = prompt_end;
+    CK(cudaMemcpyAsync(c->pos, &c->pinned[0], 4, cudaMemcpyHostToDevice, c->stream), "set pos");
+    CK(cudaMemcpyAsync(c->prompt_end, &c->pinned[1], 4, cudaMemcpyHostToDevice, c->stream), "set prompt end");
+    const size_t V = c->m->n_vocab;
+    for (int t = 0; t < n; ++t) {
+        CK(cudaGraphLaunch(c->step, c->stream), "decode step");
+        if (chunk_logits_dev != nullptr)
+            CK(cudaMemcpyAsync(chunk_logits_dev + (size_t)t * V, c->logits, V * 4, cudaMemcpyDeviceToDevice, c->stream),
+               "copy logits");
+    }
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_forward_chunk(const sllm_cuda_model* m, sllm_cuda_ctx* c, const int32_t* tokens, int32_t n,
+                                       int32_t base, float* logits_out, int32_t* argmax_out) {
+    if (m == nullptr || c == nullptr || tokens == nullptr || (logits_out == nullptr && argmax_out == nullptr) ||
+        c->m != m)
+        return fail(SLLM_CUDA_ERR_ARG, "forward_chunk: bad arguments");
+    if (n < 1 || n > 256) return fail(SLLM_CUDA_ERR_ARG, "forward_chunk: n=%d outside [1, 256]", n);
+    if (base < c->n_past || base + n > c->n_ctx)
+        return fail(SLLM_CUDA_ERR_ARG, "forward_chunk: positions [%d, %d) outside [n_past=%d, n_ctx=%d]", base,
+                    base + n, c->n_past, c->n_ctx);
+    for (int t = 0; t < n; ++t)
+        if (tokens[t] < 0 || tokens[t] >= m->n_vocab) return fail(SLLM_CUDA_ERR_ARG, "forward_chunk: token %d out of range", tokens[t]);
+    CK(cudaSetDevice(m->device), "cudaSetDevice");
+    const size_t V = m->n_vocab;
+    if (logits_out != nullptr && c->chunk_cap < (size_t)n) {
+        cudaFree(c->chunk_logits);
+        c->chunk_logits = nullptr;
+        c->chunk_cap = 0;
+        CK(cudaMalloc(&c->chunk_logits, (size_t)n * V * 4), "chunk logits");
+        c->chunk_cap = n;
+    }
+    CK(cudaMemcpyAsync(c->tok_seq + base, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream), "tokens");
+    int rc = run_steps(c, base, n, base + n, logits_out ? c->chunk_logits : nullptr);
+    if (rc != SLLM_CUDA_OK) return rc;
+    if (logits_out != nullptr)
+        CK(cudaMemcpyAsync(logits_out, c->chunk_logits, (size_t)n * V * 4, cudaMemcpyDeviceToHost, c->stream), "logits");
+    if (argmax_out != nullptr)
+        CK(cudaMemcpyAsync(argmax_out, c->argmax_hist + base, (size_t)n * 4, cudaMemcpyDeviceToHost, c->stream), "argmax");
+    CK(cudaStreamSynchronize(c->stream), "forward_chunk sync");
+    c->n_past = base + n;
+    c->have_logits = true;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_generate_greedy(const sllm_cuda_model* m, sllm_cuda_ctx* c, const int32_t* prompt,
+                                         int32_t n_prompt, int32_t n_new, int32_t* out) {
+    if (m == nullptr || c == nullptr || out == nullptr || n_prompt < 0 || n_new < 0 || c->m != m ||
+        (n_prompt > 0 && prompt == nullptr))
+        return fail(SLLM_CUDA_ERR_ARG, "generate_greedy: bad arguments");
+    if ((int64_t)n_prompt + n_new + c->n_past > c->n_ctx)
+        return fail(SLLM_CUDA_ERR_TOO_LARGE, "generate_greedy: %d + %d tokens after %d exceed n_ctx %d", n_prompt,
+                    n_new, c->n_past, c->n_ctx);
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= m->n_vocab) return fail(SLLM_CUDA_ERR_ARG, "generate_greedy: token %d out of range", prompt[i]);
+    CK(cudaSetDevice(m->device), "cudaSetDevice");
+    const int base = c->n_past;
+    if (n_prompt == 0 && base == 0) {
+        // no prompt and no history: the model's BOS (src/forward.c:909)
+        if (n_new == 0) return SLLM_CUDA_OK;
+        if (128000 >= m->n_vocab) return fail(SLLM_CUDA_ERR_ARG, "generate_greedy: BOS 128000 outside the vocabulary");
+        c->pinned[2] = 128000;
+        CK(cudaMemcpyAsync(c->tok_seq, &c->pinned[2], 4, cudaMemcpyHostToDevice, c->stream), "bos");
+    } else if (n_prompt > 0) {
+        CK(cudaMemcpyAsync(c->tok_seq + base, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, c->stream), "prompt");
+    }
+    // with no prompt and a history, tok_seq[base] already holds the argmax of
+    // the last logits, written by the step that produced them
+    const int steps = n_prompt + n_new;
+    if (steps > 0) {
+        int rc = run_steps(c, base, steps, base + n_prompt, nullptr);
+        if (rc != SLLM_CUDA_OK) return rc;
+    }
+    if (n_new > 0)
+        CK(cudaMemcpyAsync(out, c->tok_seq + base + n_prompt, (size_t)n_new * 4, cudaMemcpyDeviceToHost, c->stream), "ids");
+    CK(cudaStreamSynchronize(c->stream), "generate sync");
+    c->n_past = base + steps;
+    if (steps > 0) c->have_logits = true;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_ctx_last_logits(const sllm_cuda_ctx* c, float* host_out) {
+    if (c == nullptr || host_out == nullptr || !c->have_logits) return fail(SLLM_CUDA_ERR_ARG, "last_logits: nothing forwarded");
+    CK(cudaSetDevice(c->m->device), "cudaSetDevice");
+    CK(cudaMemcpy(host_out, c->logits, (size_t)c->m->n_vocab * 4, cudaMemcpyDeviceToHost), "last logits");
+    return SLLM_CUDA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// the layer projection chain (benchmark configuration 1)
+// ---------------------------------------------------------------------------
+extern "C" int sllm_cuda_layer_chain_device(const sllm_cuda_model* m, sllm_cuda_ctx* c, int32_t layer_begin,
+                                            int32_t n_layers, float* x, void* stream) {
+    if (m == nullptr || c == nullptr || x == nullptr || c->m != m || layer_begin < 0 || n_layers < 0 ||
+        layer_begin + n_layers > m->n_layer || !aligned16(x))
+        return fail(SLLM_CUDA_ERR_ARG, "layer_chain: bad arguments");
+    int* fb = fallback_counter();
+    ChainBufs b{x, c->q, c->k, c->v, c->ffn_inp, c->h, nullptr};
+    for (int l = layer_begin; l < layer_begin + n_layers; ++l)
+        CK(launch_layer(m, l, b, fb, g_force_fallback, (cudaStream_t)stream, false, nullptr), "layer chain");
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_layer_chain(const sllm_cuda_model* m, sllm_cuda_ctx* c, int32_t layer_begin,
+                                     int32_t n_layers, const float* x_in, float* x_out) {
+    if (m == nullptr || c == nullptr || x_in == nullptr || x_out == nullptr || c->m != m)
+        return fail(SLLM_CUDA_ERR_ARG, "layer_chain: bad arguments");
+    CK(cudaSetDevice(m->device), "cudaSetDevice");
+    const size_t bytes = (size_t)m->n_embd * 4;
+    CK(cudaMemcpyAsync(c->x, x_in, bytes, cudaMemcpyHostToDevice, c->stream), "chain input");
+    int rc = sllm_cuda_layer_chain_device(m, c, layer_begin, n_layers, c->x, c->stream);
+    if (rc != SLLM_CUDA_OK) return rc;
+    CK(cudaMemcpyAsync(x_out, c->x, bytes, cudaMemcpyDeviceToHost, c->stream), "chain output");
+    CK(cudaStreamSynchronize(c->stream), "chain sync");
+    return SLLM_CUDA_OK;
+}

@@ -1,0 +1,54 @@
+// decode.cuh -- parameters of the decode-step kernels (decode.cu).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace sllm {
+
+struct AttnParams {
+    const float* q;          // [n_head * 128] projected, before RoPE
+    const float* k;          // [n_head_kv * 128]
+    const float* v;          // [n_head_kv * 128]
+    float* k_cache;          // this layer: [n_head_kv][128][n_ctx] (K stored transposed)
+    float* v_cache;          // this layer: [n_head_kv][n_ctx][128]
+    const float* rope_cos;   // [n_ctx][64]
+    const float* rope_sin;   // [n_ctx][64]
+    const int32_t* pos_ptr;  // absolute position of the query (device)
+    float* out;              // [n_head * 128]
+    int n_ctx;
+    int group;               // query heads per kv head
+    float attn_scale;        // 1.0f / sqrtf(128.0f)
+    int* fallback_count;     // nullable
+    int force_fallback;
+};
+
+struct LmParams {
+    const float* x;          // residual stream [E]
+    const float* norm_w;     // output_norm [E]
+    float eps;
+    const uint16_t* embd;    // tied head, f16 [V][E]
+    int E, V;
+    float* logits;           // [V]
+    float* part_v;           // [grid] per-CTA best value
+    int* part_i;             // [grid] per-CTA best index
+    int* counter;            // zero between launches
+    int* argmax_out;         // [1]
+    int32_t* pos_ptr;        // advanced by one at the end of the step
+    int32_t* tok_seq;        // token of each position; greedy writes pos + 1
+    const int32_t* prompt_end;
+    int32_t* argmax_hist;    // nullable: argmax of each position
+    int n_ctx;
+    int* fallback_count;
+    int force_fallback;
+};
+
+cudaError_t launch_embed(const uint16_t* tok_embd, const int32_t* tok_seq, const int32_t* pos_ptr, int E, int V,
+                         float* x, cudaStream_t st);
+int attention_max_ctx();
+cudaError_t prepare_decode_kernels();
+cudaError_t launch_attention(const AttnParams& p, int n_head, cudaStream_t st);
+int lm_head_grid(int num_sms);
+cudaError_t launch_lm_head(const LmParams& p, int grid, cudaStream_t st);
+
+}  // namespace sllm

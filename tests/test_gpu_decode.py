@@ -1,0 +1,143 @@
+"""GPU parity of the model-level C ABI: the decode chain against the oracle
+restatement (and, where committed, the reference library's own outputs).
+
+Bar: greedy tokens identical; logits bit-identical (north_star asks for
+1e-3 relative; the device reproduces the reference's float order, so the
+test demands exact bits and would report the largest relative difference
+if that ever broke).
+"""
+import numpy as np
+import pytest
+
+from conftest import bits
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    return float(np.max(np.abs(a - b) / np.maximum(np.abs(b), 1e-30)))
+
+
+def _pair(cuda, orc, synth, cfg_kw, seed, n_ctx):
+    cfg = synth.small_config(**cfg_kw)
+    m = synth.SynthModel(cfg, seed=seed)
+    model = cuda.Model(m.desc())
+    return cfg, m, model, model.ctx(n_ctx), orc.ctx(m.desc(), n_ctx)
+
+
+CONFIGS = [
+    (dict(n_layer=3, n_embd=256, n_ff=512, n_head=2, n_head_kv=1, n_vocab=1000), 7),
+    (dict(n_layer=2, n_embd=512, n_ff=1536, n_head=4, n_head_kv=2, n_vocab=5003), 8),
+    (dict(n_layer=2, n_embd=1024, n_ff=2816, n_head=8, n_head_kv=8, n_vocab=777), 9),
+]
+
+
+@pytest.mark.parametrize("cfg_kw,seed", CONFIGS)
+def test_greedy_decode_matches_oracle(cuda, orc, synth, cfg_kw, seed):
+    cfg, m, model, gc, oc = _pair(cuda, orc, synth, cfg_kw, seed, 96)
+    prompt = np.random.default_rng(seed).integers(0, cfg.n_vocab, 13).astype(np.int32)
+    r1, t1 = gc.generate(prompt, 40)
+    r2, t2 = oc.generate(prompt, 40)
+    assert r1 == r2 == 0
+    assert t1.tolist() == t2.tolist()
+    g, o = gc.last_logits(), oc.last_logits()
+    assert np.array_equal(bits(g), bits(o)), f"max rel diff {_rel(g, o)}"
+    assert gc.n_past() == oc.n_past() == 53
+    # continuation from the last logits, with no prompt (src/forward.c:910-920)
+    r1, t1 = gc.generate(np.zeros(0, np.int32), 9)
+    r2, t2 = oc.generate(np.zeros(0, np.int32), 9)
+    assert r1 == r2 == 0 and t1.tolist() == t2.tolist()
+
+
+@pytest.mark.parametrize("cfg_kw,seed", CONFIGS[:2])
+def test_forward_chunk_logits_bit_exact(cuda, orc, synth, cfg_kw, seed):
+    cfg, m, model, gc, oc = _pair(cuda, orc, synth, cfg_kw, seed, 64)
+    toks = np.random.default_rng(seed + 5).integers(0, cfg.n_vocab, 17).astype(np.int32)
+    r1, lg, am = gc.forward_chunk(toks, 0)
+    r2, lo = oc.forward_chunk(toks, 0)
+    assert r1 == r2 == 0
+    assert np.array_equal(bits(lg), bits(lo)), f"max rel diff {_rel(lg, lo)}"
+    assert am.tolist() == [int(np.argmax(r)) for r in lo]
+    # a second chunk continues the same sequence
+    r1, lg, _ = gc.forward_chunk(toks[:5], 17)
+    r2, lo = oc.forward_chunk(toks[:5], 17)
+    assert r1 == r2 == 0 and np.array_equal(bits(lg), bits(lo))
+    # reset, then the same chunk reproduces the first result exactly
+    gc.reset(); oc.reset()
+    r1, lg2, _ = gc.forward_chunk(toks, 0)
+    r2, lo2 = oc.forward_chunk(toks, 0)
+    assert np.array_equal(bits(lg2), bits(lo2))
+
+
+def test_argument_rules_match_the_reference(cuda, orc, synth):
+    cfg, m, model, gc, oc = _pair(cuda, orc, synth, CONFIGS[0][0], 3, 16)
+    toks = np.array([1, 2, 3], np.int32)
+    assert gc.forward_chunk(toks, 0)[0] == 0
+    assert gc.forward_chunk(toks, 0)[0] == -1           # rewinding behind n_past
+    assert gc.forward_chunk(toks, 14)[0] == -1          # past n_ctx
+    assert gc.forward_chunk(np.array([cfg.n_vocab], np.int32), 3)[0] == -1
+    assert gc.generate(toks, 20)[0] == -36              # SLLM_ERR_TOO_LARGE
+    gc.reset()
+    assert gc.generate(np.zeros(0, np.int32), 2)[0] == -1   # BOS 128000 outside a 1000-token vocabulary
+
+
+def test_certified_sum_fallback_gives_the_same_bits(cuda, orc, synth):
+    """Force every certified f64 sum (RMSNorm mean, softmax normaliser) onto
+    its reference-order fallback: outputs must not change."""
+    cfg_kw, seed = CONFIGS[0]
+    cfg, m, model, gc, oc = _pair(cuda, orc, synth, cfg_kw, seed, 48)
+    prompt = np.random.default_rng(seed).integers(0, cfg.n_vocab, 11).astype(np.int32)
+    r0, t0 = gc.generate(prompt, 12)
+    before = cuda.fallback_count()
+    cuda.set_force_fallback(True)
+    try:
+        fc = model.ctx(48)                               # graph captured with the hook on
+        r1, t1 = fc.generate(prompt, 12)
+        after = cuda.fallback_count()
+        l1 = fc.last_logits()
+    finally:
+        cuda.set_force_fallback(False)
+    r2, t2 = oc.generate(prompt, 12)
+    assert r0 == r1 == r2 == 0
+    assert t0.tolist() == t1.tolist() == t2.tolist()
+    assert np.array_equal(bits(l1), bits(oc.last_logits()))
+    assert after > before
+
+
+def test_committed_reference_decode_fixtures(cuda, synth):
+    """Tokens and last-logit hashes produced by the reference library itself."""
+    import fixtures
+    for case in fixtures.load_decode_cases():
+        m = fixtures.decode_model(synth, case)
+        model = cuda.Model(m.desc())
+        c = model.ctx(case["n_ctx"])
+        rc, toks = c.generate(np.array(case["prompt"], np.int32), case["n_new"])
+        assert rc == 0 and toks.tolist() == case["tokens"], case["name"]
+        assert fixtures.fnv1a64(bits(c.last_logits()).tobytes()) == case["last_logits_fnv"], case["name"]
+
+
+def test_bitnet_2b_shape_two_layers(cuda, orc, synth):
+    """The 2B-4T geometry (E 2560, F 6912, 20/5 heads, 128256-token head) with
+    two layers: every GEMV shape and the full lm_head of the real model."""
+    cfg = synth.Config(n_layer=2)
+    m = synth.SynthModel(cfg, seed=2024)
+    model = cuda.Model(m.desc())
+    gc, oc = model.ctx(40), orc.ctx(m.desc(), 40)
+    prompt = np.random.default_rng(4).integers(0, cfg.n_vocab, 6).astype(np.int32)
+    r1, t1 = gc.generate(prompt, 4)
+    r2, t2 = oc.generate(prompt, 4)
+    assert r1 == r2 == 0 and t1.tolist() == t2.tolist()
+    assert np.array_equal(bits(gc.last_logits()), bits(oc.last_logits()))
+
+
+def test_layer_chain_matches_oracle(cuda, orc, synth):
+    cfg = synth.Config(n_layer=3, n_vocab=512)
+    m = synth.SynthModel(cfg, seed=77)
+    model = cuda.Model(m.desc())
+    c = model.ctx(8)
+    x = np.random.default_rng(77).standard_normal(cfg.n_embd).astype(np.float32)
+    got = c.layer_chain(0, 3, x)
+    want = x
+    for layer in range(3):
+        want = orc.layer_chain(m.desc(), layer, want)
+    assert np.array_equal(bits(got), bits(want))
