@@ -1,27 +1,33 @@
-"""Benchmark: I2_S GEMV HBM GB/s on a bitnet-b1.58-2B-4T layer chain (B200).
+"""Benchmark: I2_S GEMV HBM GB/s on bitnet-b1.58-2B-4T layers, plus greedy decode (B200).
 
-Workload: the seven I2_S GEMVs of one 2B-4T layer
-at batch 1 -- Q 2560x2560, K/V 640x2560, O 2560x2560, gate/up 6912x2560,
-down 2560x6912 -- with RMSNorm + int8 quantisation before every projection
-(attn_norm, attn_sub_norm, ffn_norm, ffn_sub_norm), SiLU gating and the two
-residual adds: the decode layer without attention, run by
-sllm_cuda_layer_chain_device. One STEP runs that chain through 32 distinct
-layer copies (556 MB of packed weights, more than 4x the 126 MB L2), so every
-step streams its weights from HBM and no L2 flush is needed.
+Headline workload (as stated there): the seven I2_S
+GEMV shapes of one 2B-4T layer at batch 1 -- Q 2560x2560, K/V 640x2560,
+O 2560x2560, gate/up 6912x2560, down 2560x6912 -- each on its own f32 N(0,1)
+activation, RMSNorm'd (eps 1e-5, norm weights N(1, 0.02)) and int8-quantised
+per token, run back to back (sllm_cuda_layer_projections_device). One STEP
+runs them through 32 distinct layer copies (556 MB of packed weights, more
+than 4x the 126 MB L2), so every step streams its weights from HBM and no
+L2 flush is needed.
 
-  value     whole-job GB/s: algorithmic bytes of all ranks / max device time
-  e2e       the same metric through the host-buffer C ABI call
-            sllm_cuda_layer_chain (pinned input copied in, output copied back
-            every step), wall clock
-  roofline  the GEMV kernel (every launch in the step is one): algorithmic
-            bytes per launch / average launch time, against the measured HBM
-            copy bandwidth
-  cpu_baseline  the reference saphira-llm library (oracle/_ref, compiled
-            from its own sources) running the same chain on the host cores
+Also in the same JSON line, measured in the same run:
+  chain    the decode layer's projection chain (each GEMV's input is the
+           previous one's output: norm -> QKV -> O + residual -> gate/up,
+           SiLU -> down + residual), sllm_cuda_layer_chain_device
+  decode   configs[2]: random-init 2B-4T model, 64-token prompt, 256 greedy
+           tokens, tokens/s through sllm_cuda_generate_greedy, with a bounded
+           sample of the reference CPU decode beside it
 
-  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+  value         whole-job GB/s: algorithmic bytes of all ranks / max device time
+  e2e           the same metric through the host-buffer C ABI call
+                sllm_cuda_layer_projections (pinned inputs copied in, every
+                output copied back each step), wall clock
+  roofline      the GEMV kernel (every launch of the step is one)
+  cpu_baseline  the reference saphira-llm library (oracle/_ref, compiled from
+                its own sources) running the same projections on the host cores
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--no-decode]
 Multi-GPU: one process per GPU (torchrun); each rank runs its own replica
-(the chain does not shard: replicas only), weak scaling.
+(the projections do not shard: replicas only), weak scaling.
 """
 import argparse
 import importlib
@@ -29,6 +35,7 @@ import json
 import os
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -39,7 +46,7 @@ for _p in (ROOT, os.path.join(ROOT, "oracle")):
         sys.path.insert(0, _p)
 
 N_COPIES = 32
-METRIC = "I2_S GEMV HBM GB/s (bitnet-b1.58-2B-4T layer chain: 7 GEMVs + RMSNorm, batch 1)"
+METRIC = "I2_S GEMV HBM GB/s (bitnet-b1.58-2B-4T: the 7 GEMVs of a layer with RMSNorm + int8 quant, batch 1)"
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -52,35 +59,55 @@ def peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def projection_bytes(cfg, m):
+    """Algorithmic bytes of one layer's seven independent projections: every
+    packed weight byte (with its scale tail) once, every GEMV's input vector
+    and norm vector once, every output once."""
+    E, F, G = cfg.n_embd, cfg.n_ff, cfg.n_embd_gqa
+    w = sum(m.tensors[f"blk.0.{n}.weight"].nbytes for n in
+            ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"))
+    inputs = 2 * 4 * (6 * E + F)                       # input vectors + their norm vectors
+    outputs = 4 * (3 * E + 2 * G + 2 * F)
+    return w + inputs + outputs
+
+
 def chain_bytes(cfg, m):
-    """Algorithmic bytes of one layer's chain: every weight byte once (packed
-    codes with their scale tail, the four norm vectors) plus every activation
+    """Algorithmic bytes of one layer's dependent chain: every weight byte once
+    (codes with scale tails, the four norm vectors) plus every activation
     vector each GEMV reads or writes once."""
     E, F, G = cfg.n_embd, cfg.n_ff, cfg.n_embd_gqa
-    w = m.layer_weight_bytes(0)
-    act = 4 * ((E + E + 2 * G)           # QKV: x in, q k v out
-               + (E + E + E)             # O: q in, residual in, ffn_inp out
-               + (E + F)                 # gate/up: ffn_inp in, h out
-               + (F + E + E))            # down: h in, residual in, x out
-    return w + act
+    act = 4 * ((E + E + 2 * G) + (E + E + E) + (E + F) + (F + E + E))
+    return m.layer_weight_bytes(0) + act
 
 
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
 def clocks_start():
-    """Sample SM clocks and throttle reasons while the timed region runs."""
+    """Sample SM clocks and throttle reasons while a timed region runs."""
     try:
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        q = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-        import tempfile
         tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         p = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100"],
-                             stdout=tmp, stderr=subprocess.DEVNULL)
+                             stdout=tmp, stderr=subprocess.STDOUT)
         return p, tmp.name
     except Exception:
         return None, None
 
 
-def clocks_stop(handle, dev_index):
+def device_uuid(local):
+    try:
+        import torch
+        u = str(torch.cuda.get_device_properties(local).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return None
+
+
+def clocks_stop(handle, uuid):
+    """Median SM clock and any throttle reason seen on this rank's GPU."""
     p, path = handle
     if p is None:
         return None
@@ -89,38 +116,87 @@ def clocks_stop(handle, dev_index):
         p.wait(timeout=5)
     except Exception:
         p.kill()
-    sm, mx, reasons = [], None, set()
+    sm, mx, reasons, seen = [], None, set(), set()
     names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-    try:
-        for line in open(path):
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9 or f[0] != str(dev_index):
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        os.unlink(path)
-    except Exception:
-        return None
+    lines = open(path).read().splitlines()
+    os.unlink(path)
+    for line in lines:
+        f = [x.strip() for x in line.split(",")]
+        if len(f) < 9:
+            continue
+        seen.add(f[0])
+        if uuid is not None and f[0] != uuid and len(seen) > 1:
+            continue
+        try:
+            sm.append(float(f[1]))
+            mx = float(f[2])
+        except ValueError:
+            continue
+        for n, v in zip(names, f[5:9]):
+            if v.lower() == "active":
+                reasons.add(n)
     if not sm:
-        return None
+        return {"error": (lines[0] if lines else "no nvidia-smi output")[:200]}
     return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def dist_init():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
+# ---------------------------------------------------------------------------
+# reference (CPU) legs
+# ---------------------------------------------------------------------------
+class RefProjections:
+    """The reference library on the host cores, same inputs and layers."""
+
+    def __init__(self, cfg, m, x):
+        import oracle
+        self.ref = oracle.Reference()
+        self.cores = os.cpu_count() or 1
+        self.pool = self.ref.pool(self.cores)
+        self.cfg, self.m, self.d = cfg, m, m.desc()
+        E, F = cfg.n_embd, cfg.n_ff
+        self.x = [x[i * E:(i + 1) * E] for i in range(6)] + [x[6 * E: 6 * E + F]]
+        self.dots = np.zeros(max(E, F), np.int32)
+
+    def layer(self, il):
+        """One layer: for each projection sllm_rms_norm -> sllm_i2s_quant_act ->
+        pooled sllm_i2s_gemv -> the epilogue of src/forward.c:653-655."""
+        cfg = self.cfg
+        E, F, G = cfg.n_embd, cfg.n_ff, cfg.n_embd_gqa
+        L = self.m.tensors
+        p = f"blk.{il}."
+        specs = [("attn_q", E, E, "attn_norm"), ("attn_k", G, E, "attn_norm"), ("attn_v", G, E, "attn_norm"),
+                 ("attn_output", E, E, "attn_sub_norm"), ("ffn_gate", F, E, "ffn_norm"),
+                 ("ffn_up", F, E, "ffn_norm"), ("ffn_down", E, F, "ffn_sub_norm")]
+        out = []
+        for (name, rows, n, norm), xin in zip(specs, self.x):
+            xn = self.ref.rms_norm(xin, L[p + norm + ".weight"].view(np.float32), cfg.eps)
+            q, s, total = self.ref.quant_act(xn)
+            w = L[p + name + ".weight"]
+            self.pool.gemv(w, rows, n, q, self.dots)
+            ws = np.float32(w[rows * n // 4: rows * n // 4 + 4].view(np.float32)[0])
+            post = ws / np.float32(s)
+            out.append((self.dots[:rows] - total).astype(np.float32) * post)
+        return out
+
+
+def cpu_baseline_sample(cfg, m, x, seconds=10.0):
+    import oracle
+    if not oracle.reference_available():
+        return None
+    rp = RefProjections(cfg, m, x)
+    rp.layer(0)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        rp.layer(n % cfg.n_layer)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(projection_bytes(cfg, m) * n / dt / 1e9, 3), "unit": "GB/s", "cores": rp.pool.threads,
+            "kind": "reference",
+            "sample": f"{n} layers' seven projections (of the same {cfg.n_layer} layer copies) in {dt:.1f} s, "
+                      f"reference ISA level {rp.ref.isa}"}
 
 
 def reference_arm(args, world, rank):
-    """The reference CPU implementation on this box's host cores."""
+    """bench.py --impl reference: the reference CPU implementation on this box."""
     if rank != 0:
         return
     import oracle
@@ -128,70 +204,109 @@ def reference_arm(args, world, rank):
     if not oracle.reference_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libsllm_ref.so was not built"}))
         return
-    ref = oracle.Reference()
     cfg = synth.Config(n_layer=N_COPIES, n_vocab=256)
     m = synth.SynthModel(cfg, seed=1)
-    d = m.desc()
-    cores = os.cpu_count() or 1
-    pool = ref.pool(cores)
-    E, F, G = cfg.n_embd, cfg.n_ff, cfg.n_embd_gqa
-    x = np.random.default_rng(0).standard_normal(E).astype(np.float32)
-    scratch = np.zeros(4 * E + 2 * G + 3 * F, np.float32)
-    qbuf = np.zeros(max(E, F), np.int8)
-    dots = np.zeros(max(E, F), np.int32)
-    # a step is a bounded sample of the chain: 8 of the 32 layer copies
-    per_step = 8
-
-    def step(i):
-        for j in range(per_step):
-            pool.layer_chain(d, (i * per_step + j) % N_COPIES, x, scratch, qbuf, dots)
-
+    xs = np.random.default_rng(0).standard_normal(6 * cfg.n_embd + cfg.n_ff).astype(np.float32)
+    rp = RefProjections(cfg, m, xs)
+    per_step = 8          # a bounded sample: 8 of the 32 layer copies per step
     for i in range(args.warmup):
-        step(i)
+        for j in range(per_step):
+            rp.layer((i * per_step + j) % N_COPIES)
     t0 = time.perf_counter()
     for i in range(args.steps):
-        step(args.warmup + i)
+        for j in range(per_step):
+            rp.layer(((args.warmup + i) * per_step + j) % N_COPIES)
     dt = time.perf_counter() - t0
-    gbs = chain_bytes(cfg, m) * per_step * args.steps / dt / 1e9
-    sample = f"{per_step} of the {N_COPIES} layer copies per step, {args.steps} steps"
+    gbs = projection_bytes(cfg, m) * per_step * args.steps / dt / 1e9
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xternary->int32, f32",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 x ternary -> int32, f32",
         "data": "synthetic (seeded random-init 2B-4T layers)",
-        "config": {"workload": "layer_chain_2b4t", "layers_per_step": per_step, "threads": pool.threads,
-                   "isa_level": ref.isa},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": pool.threads, "kind": "reference",
-                         "sample": sample},
+        "config": {"workload": "layer_projections_2b4t", "layers_per_step": per_step, "threads": rp.pool.threads,
+                   "isa_level": rp.ref.isa},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": rp.pool.threads, "kind": "reference",
+                         "sample": f"{per_step} of the {N_COPIES} layer copies per step, {args.steps} steps"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
 
 
-def cpu_baseline_sample(cfg, m):
-    """Rank 0 only: the reference library on the host cores, ~10 s bounded."""
-    import oracle
-    if not oracle.reference_available():
-        return None
-    ref = oracle.Reference()
-    cores = os.cpu_count() or 1
-    pool = ref.pool(cores)
-    d = m.desc()
-    E, F, G = cfg.n_embd, cfg.n_ff, cfg.n_embd_gqa
-    x = np.random.default_rng(0).standard_normal(E).astype(np.float32)
-    scratch = np.zeros(4 * E + 2 * G + 3 * F, np.float32)
-    qbuf = np.zeros(max(E, F), np.int8)
-    dots = np.zeros(max(E, F), np.int32)
-    for layer in range(2):
-        pool.layer_chain(d, layer, x, scratch, qbuf, dots)
-    n, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < 10.0:
-        pool.layer_chain(d, n % cfg.n_layer, x, scratch, qbuf, dots)
-        n += 1
-    dt = time.perf_counter() - t0
-    return {"value": round(chain_bytes(cfg, m) * n / dt / 1e9, 3), "unit": "GB/s", "cores": pool.threads,
-            "kind": "reference",
-            "sample": f"{n} layer chains over the same {cfg.n_layer} layer copies in {dt:.1f} s "
-                      f"(reference ISA level {ref.isa})"}
+# ---------------------------------------------------------------------------
+# GPU legs
+# ---------------------------------------------------------------------------
+def time_device(fn, steps, warmup, stream, world):
+    """Device time of `steps` calls of fn() after `warmup`, max over ranks."""
+    import torch
+    for _ in range(max(warmup, 3)):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    ev[0].record(stream)
+    for i in range(steps):
+        fn()
+        ev[i + 1].record(stream)
+    torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[steps])
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item()), per
+
+
+def decode_leg(pkg, synth, local, rank, world, args):
+    """2B-4T random init, prompt 64, 256 greedy tokens."""
+    import torch
+    cfg = synth.Config()
+    m = synth.SynthModel(cfg, seed=4242 + rank)
+    model = pkg.Model(m.desc(), local)
+    ctx = model.ctx(64 + 256)
+    prompt = np.random.default_rng(7 + rank).integers(0, cfg.n_vocab, 64).astype(np.int32)
+    rc, toks = ctx.generate(prompt, 256)         # warm-up (captures the step graph)
+    assert rc == 0, pkg.lib().sllm_cuda_last_error()
+    runs = []
+    for _ in range(3):
+        ctx.reset()
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        t0 = time.perf_counter()
+        rc, toks2 = ctx.generate(prompt, 256)
+        runs.append(time.perf_counter() - t0)
+        assert rc == 0 and toks2.tolist() == toks.tolist()
+    best = min(runs)
+    tb = torch.tensor([best], dtype=torch.float64, device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(tb, op=torch.distributed.ReduceOp.MAX)
+    best = float(tb.item())
+    out = {"workload": "greedy_decode_2b4t", "prompt": 64, "new_tokens": 256,
+           "tokens_per_s": round((64 + 256) * world / best, 1), "ms_per_token": round(best / 320 * 1e3, 4),
+           "weight_gbs": round(model.weight_bytes() * 320 * world / best / 1e9, 1),
+           "api": "sllm_cuda_generate_greedy (host prompt in, ids out, wall clock; best of 3)",
+           "token_checksum": int(np.sum(toks.astype(np.int64) * np.arange(1, 257)) % 1000003)}
+    if rank == 0 and not args.no_cpu_baseline:
+        import oracle
+        if oracle.reference_available():
+            ref = oracle.Reference()
+            cores = os.cpu_count() or 1
+            rm = ref.model(m.image, 64, cores)
+            n_new = 8
+            rm.generate(prompt[:8], 1)
+            rm.reset()
+            t0 = time.perf_counter()
+            rcr, rt = rm.generate(prompt[:8], n_new)
+            dt = time.perf_counter() - t0
+            ctx.reset()
+            rc, g = ctx.generate(prompt[:8], n_new)
+            out["cpu_reference"] = {"tokens_per_s": round((8 + n_new) / dt, 2), "cores": cores,
+                                    "sample": f"prompt 8 + {n_new} greedy tokens through sllm_generate_greedy",
+                                    "tokens_identical": bool(rcr == 0 and g.tolist() == rt.tolist())}
+            del rm
+    ctx.close()
+    model.close()
+    return out
 
 
 def main():
@@ -201,8 +316,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--copies", type=int, default=N_COPIES,
+                    help="layer copies per step (default 32; smaller only for profiler captures)")
     args = ap.parse_args()
-    world, rank, local = dist_init()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, world, rank)
         return
@@ -216,100 +336,93 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
 
-    cfg = synth.Config(n_layer=N_COPIES, n_vocab=256)
+    copies = args.copies
+    cfg = synth.Config(n_layer=copies, n_vocab=256)
     m = synth.SynthModel(cfg, seed=1 + rank)
     model = pkg.Model(m.desc(), local)
     ctx = model.ctx(8)
     E = cfg.n_embd
-    x0 = torch.from_numpy(np.random.default_rng(rank).standard_normal(E).astype(np.float32)).cuda()
-    x = x0.clone()
     stream = torch.cuda.current_stream()
-    per_step_bytes = chain_bytes(cfg, m) * N_COPIES
-    launches_per_step = 4 * N_COPIES
+    xs_n, ys_n = pkg.projection_sizes(model)
+    xs_host = np.random.default_rng(rank).standard_normal(xs_n).astype(np.float32)
+    xs = torch.from_numpy(xs_host).cuda()
+    ys = torch.empty(ys_n * copies, dtype=torch.float32, device="cuda")
+    step_bytes = projection_bytes(cfg, m) * copies
+    launches = 7 * copies
 
-    def step():
-        ctx.layer_chain_device(0, N_COPIES, x, stream)
-
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
+    # headline: independent projections
     clk = clocks_start()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
-    torch.cuda.synchronize()
-    start.record(stream)
-    ev[0].record(stream)
-    for i in range(args.steps):
-        step()
-        ev[i + 1].record(stream)
-    end.record(stream)
-    torch.cuda.synchronize()
-    clocks = clocks_stop(clk, local)
-    ms = start.elapsed_time(end)
-    per_step_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms_max = float(t.item())
-    value = per_step_bytes * args.steps * world / (ms_max / 1e3) / 1e9
+    ms, per = time_device(lambda: ctx.layer_projections_device(0, copies, xs, ys, stream),
+                          args.steps, args.warmup, stream, world)
+    clocks = clocks_stop(clk, device_uuid(local))
+    value = step_bytes * args.steps * world / (ms / 1e3) / 1e9
 
-    # e2e through the host-buffer C ABI (pinned input, output read back)
-    host_in = torch.from_numpy(np.random.default_rng(rank).standard_normal(E).astype(np.float32)).pin_memory()
-    host_out = torch.empty(E, dtype=torch.float32).pin_memory()
+    # e2e: host buffers through sllm_cuda_layer_projections
+    host_in = torch.from_numpy(xs_host).pin_memory()
+    host_out = torch.empty(ys_n * copies, dtype=torch.float32).pin_memory()
     lib = pkg.lib()
     for _ in range(2):
-        lib.sllm_cuda_layer_chain(model.h, ctx.h, 0, N_COPIES, host_in.data_ptr(), host_out.data_ptr())
+        assert lib.sllm_cuda_layer_projections(model.h, ctx.h, 0, copies, host_in.data_ptr(),
+                                               host_out.data_ptr()) == 0
     if world > 1:
         torch.distributed.barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        rc = lib.sllm_cuda_layer_chain(model.h, ctx.h, 0, N_COPIES, host_in.data_ptr(), host_out.data_ptr())
-        assert rc == 0
-    e2e_s = time.perf_counter() - t0
-    te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        assert lib.sllm_cuda_layer_projections(model.h, ctx.h, 0, copies, host_in.data_ptr(),
+                                               host_out.data_ptr()) == 0
+    te = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device="cuda")
     if world > 1:
         torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
-    e2e = per_step_bytes * args.steps * world / float(te.item()) / 1e9
+    e2e = step_bytes * args.steps * world / float(te.item()) / 1e9
+
+    # secondary: the dependent chain
+    xc = torch.from_numpy(np.random.default_rng(rank).standard_normal(E).astype(np.float32)).cuda()
+    cms, _ = time_device(lambda: ctx.layer_chain_device(0, copies, xc, stream), args.steps, args.warmup,
+                         stream, world)
+    chain_gbs = chain_bytes(cfg, m) * copies * args.steps * world / (cms / 1e3) / 1e9
 
     peak, peak_kind = peaks()
-    per_launch_bytes = per_step_bytes / launches_per_step
-    per_launch_s = (ms / 1e3) / (args.steps * launches_per_step)
-    achieved = per_launch_bytes / per_launch_s / 1e9
+    per_launch_bytes = step_bytes / launches
+    achieved = per_launch_bytes / ((ms / 1e3) / (args.steps * launches)) / 1e9
     traffic = None
-    prof = os.path.join(ROOT, "profiles", "i2s_gemv_layer_chain_traffic.txt")
+    prof = os.path.join(ROOT, "profiles", "i2s_gemv_projections_traffic.txt")
     if os.path.exists(prof):
         for line in open(prof):
             if line.startswith("traffic_bytes_per_launch"):
                 traffic = int(line.split()[1])
     out = {
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": max(args.warmup, 3), "ms_per_step": round(ms_max / args.steps, 4),
+        "warmup": max(args.warmup, 3), "ms_per_step": round(ms / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8xternary->int32, f32", "data": "synthetic (seeded random-init 2B-4T layers)",
-        "config": {"workload": "layer_chain_2b4t", "layer_copies_per_step": N_COPIES,
-                   "weights_mb_per_step": round(m.layer_weight_bytes(0) * N_COPIES / 1e6, 1),
-                   "bytes_per_step": per_step_bytes,
-                   "l2": "inputs larger than L2: 32 distinct layer copies (>4x the 126 MB L2) per step, no flush",
+        "dtype": "int8 x ternary -> int32, f32", "data": "synthetic (seeded random-init 2B-4T layers, N(0,1) inputs)",
+        "config": {"workload": "layer_projections_2b4t", "layer_copies_per_step": copies,
+                   "weights_mb_per_step": round(step_bytes / 1e6, 1), "bytes_per_step": step_bytes,
+                   "l2": "inputs larger than L2: 32 distinct layer copies (4.4x the 126 MB L2) per step, no flush",
                    "parallelism": f"replicas x{world}", "batch": 1},
-        "roofline": {"bound": "hbm", "kernel": "i2s_gemv_kernel (all 4 launches per layer)",
+        "roofline": {"bound": "hbm", "kernel": "i2s_gemv_kernel (all 7 launches per layer)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "bytes_per_launch": int(per_launch_bytes), "traffic": traffic},
-        "e2e": {"value": round(e2e, 3), "unit": "GB/s", "h2d_bytes_per_step": 4 * E, "d2h_bytes_per_step": 4 * E,
-                "api": "sllm_cuda_layer_chain (host buffers, wall clock)"},
-        "gpu_launches": launches_per_step * args.steps,
-        "step_ms_min_median_max": [round(min(per_step_ms), 4), round(float(np.median(per_step_ms)), 4),
-                                   round(max(per_step_ms), 4)],
+        "e2e": {"value": round(e2e, 3), "unit": "GB/s", "h2d_bytes_per_step": 4 * xs_n,
+                "d2h_bytes_per_step": 4 * ys_n * copies,
+                "api": "sllm_cuda_layer_projections (host buffers, wall clock)"},
+        "gpu_launches": launches * args.steps,
+        "step_ms_min_median_max": [round(min(per), 4), round(float(np.median(per)), 4), round(max(per), 4)],
         "clocks": clocks,
+        "chain": {"workload": "layer_chain_2b4t (dependent: decode layer without attention)",
+                  "value": round(chain_gbs, 3), "unit": "GB/s", "frac": round(chain_gbs / world / peak, 4),
+                  "ms_per_step": round(cms / args.steps, 4),
+                  "us_per_layer": round(cms / args.steps / copies * 1e3, 3)},
     }
     if rank == 0 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline_sample(cfg, m)
-    if rank == 0:
-        print(json.dumps(out))
+        out["cpu_baseline"] = cpu_baseline_sample(cfg, m, xs_host)
     ctx.close()
     model.close()
+    del m
+    if not args.no_decode:
+        out["decode"] = decode_leg(pkg, synth, local, rank, world, args)
+    if rank == 0:
+        print(json.dumps(out))
     if world > 1:
         torch.distributed.destroy_process_group()
 

@@ -236,6 +236,32 @@ SLLM_CUDA_API int sllm_cuda_layer_chain_device(const sllm_cuda_model * m, sllm_c
                                  int32_t layer_begin, int32_t n_layers,
                                  float * x, void * stream);
 
+/*
+ * The seven projections of layers [layer_begin, layer_begin + n_layers), each
+ * on its OWN input vector -- the benchmark's configuration 1 taken literally
+ * ("each uses an f32 N(0,1) activation ... with RMSNorm between them"). For
+ * every layer, GEMV p normalises input p with the norm its projection uses in
+ * the decode layer (Q, K, V: attn_norm; O: attn_sub_norm; gate, up: ffn_norm;
+ * down: ffn_sub_norm), quantises it per token and writes f32 outputs; nothing
+ * feeds one projection into another, so consecutive GEMVs overlap on the
+ * device.
+ *   x: 6 * n_embd + n_ff floats, inputs of Q, K, V, O, gate, up (n_embd each)
+ *      and down (n_ff), shared by every layer;
+ *   y: n_layers blocks of 3 * n_embd + 2 * n_embd_gqa + 2 * n_ff floats:
+ *      Q (n_embd), K, V (n_embd_gqa), O (n_embd), gate, up (n_ff), down (n_embd).
+ * sllm_cuda_layer_projections_sizes returns the input length and stores the
+ * per-layer output length. The _device form takes 16-byte aligned device
+ * vectors and is asynchronous on `stream`.
+ */
+SLLM_CUDA_API size_t sllm_cuda_layer_projections_sizes(const sllm_cuda_model * m,
+                                                       size_t * y_floats_per_layer);
+SLLM_CUDA_API int sllm_cuda_layer_projections(const sllm_cuda_model * m, sllm_cuda_ctx * c,
+                                              int32_t layer_begin, int32_t n_layers,
+                                              const float * x_host, float * y_host);
+SLLM_CUDA_API int sllm_cuda_layer_projections_device(const sllm_cuda_model * m, sllm_cuda_ctx * c,
+                                                     int32_t layer_begin, int32_t n_layers,
+                                                     const float * x, float * y, void * stream);
+
 /* Bytes of weights one decode step streams: every I2_S tensor with its scale
  * tail, every norm, and the F16 embedding / output head. */
 SLLM_CUDA_API size_t sllm_cuda_model_weight_bytes(const sllm_cuda_model * m);

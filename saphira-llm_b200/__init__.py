@@ -60,6 +60,10 @@ def lib():
     L.sllm_cuda_ctx_last_logits.argtypes = [vp, vp]
     L.sllm_cuda_layer_chain.argtypes = [vp, vp, i32, i32, vp, vp]
     L.sllm_cuda_layer_chain_device.argtypes = [vp, vp, i32, i32, vp, vp]
+    L.sllm_cuda_layer_projections_sizes.argtypes = [vp, C.POINTER(sz)]
+    L.sllm_cuda_layer_projections_sizes.restype = sz
+    L.sllm_cuda_layer_projections.argtypes = [vp, vp, i32, i32, vp, vp]
+    L.sllm_cuda_layer_projections_device.argtypes = [vp, vp, i32, i32, vp, vp, vp]
     L.sllm_cuda_test_set_force_fallback.argtypes = [C.c_int]
     L.sllm_cuda_test_fallback_count.restype = C.c_int
     _lib = L
@@ -134,7 +138,10 @@ class Model:
 
     def close(self):
         if getattr(self, "h", None):
-            lib().sllm_cuda_model_free(self.h)
+            try:
+                lib().sllm_cuda_model_free(self.h)
+            except (TypeError, AttributeError):      # interpreter shutdown
+                pass
             self.h = None
 
     def __del__(self):
@@ -158,7 +165,10 @@ class Ctx:
 
     def close(self):
         if getattr(self, "h", None):
-            lib().sllm_cuda_ctx_free(self.h)
+            try:
+                lib().sllm_cuda_ctx_free(self.h)
+            except (TypeError, AttributeError):      # interpreter shutdown
+                pass
             self.h = None
 
     def __del__(self):
@@ -201,6 +211,27 @@ class Ctx:
                                            out.ctypes.data), "layer_chain")
         return out
 
+    def layer_projections(self, layer_begin, n_layers, x):
+        np = self._np
+        xs, ys = projection_sizes(self.model)
+        x = np.ascontiguousarray(x, np.float32)
+        assert x.size == xs
+        y = np.empty(ys * n_layers, np.float32)
+        _check(lib().sllm_cuda_layer_projections(self.model.h, self.h, layer_begin, n_layers, x.ctypes.data,
+                                                 y.ctypes.data), "layer_projections")
+        return y.reshape(n_layers, ys)
+
+    def layer_projections_device(self, layer_begin, n_layers, x_dev, y_dev, stream=None):
+        _check(lib().sllm_cuda_layer_projections_device(self.model.h, self.h, layer_begin, n_layers, _ptr(x_dev),
+                                                        _ptr(y_dev), _stream(stream)), "layer_projections_device")
+
     def layer_chain_device(self, layer_begin, n_layers, x_dev, stream=None):
         _check(lib().sllm_cuda_layer_chain_device(self.model.h, self.h, layer_begin, n_layers, _ptr(x_dev),
                                                   _stream(stream)), "layer_chain_device")
+
+
+def projection_sizes(model):
+    """(input floats, output floats per layer) of the layer-projection API."""
+    ys = C.c_size_t()
+    xs = lib().sllm_cuda_layer_projections_sizes(model.h, C.byref(ys))
+    return int(xs), int(ys.value)

@@ -110,10 +110,13 @@ extern "C" int sllm_cuda_probe(int* n_devices, int* cc_major, int* cc_minor) {
     return SLLM_CUDA_OK;
 }
 
+// Allocated on first use OUTSIDE any stream capture (ctx_new and the chain
+// entry points call it before capturing); a graph then bakes the pointer in.
 static int* fallback_counter() {
     if (g_fallback_counter == nullptr) {
         if (cudaMalloc(&g_fallback_counter, sizeof(int)) != cudaSuccess) { g_fallback_counter = nullptr; return nullptr; }
-        cudaMemset(g_fallback_counter, 0, sizeof(int));
+        if (cudaMemset(g_fallback_counter, 0, sizeof(int)) != cudaSuccess) return nullptr;
+        if (cudaDeviceSynchronize() != cudaSuccess) return nullptr;
     }
     return g_fallback_counter;
 }
@@ -319,6 +322,17 @@ struct sllm_cuda_ctx {
     int32_t* pinned = nullptr;                       // small host staging
     cudaGraphExec_t step = nullptr;
     int lm_grid = 0;
+    // the layer chain as a graph, for the last (begin, n, x) it was asked for
+    cudaGraphExec_t chain = nullptr;
+    int chain_begin = -1, chain_n = -1;
+    float* chain_x = nullptr;
+    // the independent-input projections as a graph, likewise
+    cudaGraphExec_t proj = nullptr;
+    int proj_begin = -1, proj_n = -1;
+    const float* proj_x = nullptr;
+    float* proj_y = nullptr;
+    void* io = nullptr;              // device staging of the host-buffer entry points
+    size_t io_cap = 0;
 };
 
 // the reference's angle recurrence (src/ops.c:529-549), on the host libm
@@ -344,6 +358,8 @@ extern "C" void sllm_cuda_ctx_free(sllm_cuda_ctx* c) {
     if (c == nullptr) return;
     cudaSetDevice(c->m->device);
     if (c->step) cudaGraphExecDestroy(c->step);
+    if (c->chain) cudaGraphExecDestroy(c->chain);
+    if (c->proj) cudaGraphExecDestroy(c->proj);
     if (c->stream) cudaStreamDestroy(c->stream);
     cudaFree(c->k_cache); cudaFree(c->v_cache); cudaFree(c->rope_cos); cudaFree(c->rope_sin);
     cudaFree(c->x); cudaFree(c->q); cudaFree(c->k); cudaFree(c->v); cudaFree(c->attn);
@@ -351,6 +367,7 @@ extern "C" void sllm_cuda_ctx_free(sllm_cuda_ctx* c) {
     cudaFree(c->part_v); cudaFree(c->part_i); cudaFree(c->counter); cudaFree(c->argmax);
     cudaFree(c->pos); cudaFree(c->tok_seq); cudaFree(c->prompt_end); cudaFree(c->argmax_hist);
     cudaFreeHost(c->pinned);
+    cudaFree(c->io);
     delete c;
 }
 
@@ -361,6 +378,7 @@ extern "C" int sllm_cuda_ctx_new(const sllm_cuda_model* m, int32_t n_ctx, sllm_c
         return fail(SLLM_CUDA_ERR_TOO_LARGE, "ctx_new: n_ctx %d above %d", n_ctx, attention_max_ctx());
     CK(cudaSetDevice(m->device), "cudaSetDevice");
     CK(prepare_decode_kernels(), "kernel attributes");
+    if (fallback_counter() == nullptr) return fail(SLLM_CUDA_ERR_NOMEM, "ctx_new: diagnostics counter");
     auto* c = new sllm_cuda_ctx();
     c->m = m;
     c->n_ctx = n_ctx;
@@ -428,7 +446,7 @@ static cudaError_t launch_layer(const sllm_cuda_model* m, int l, const ChainBufs
     p.seg[1] = GemvSeg{L.wk, G, b.k, nullptr};
     p.seg[2] = GemvSeg{L.wv, G, b.v, nullptr};
     p.x = b.x; p.norm_w = L.attn_norm;
-    cudaError_t e = launch_gemv(p, PRO_NORM, EPI_F32, sms, st);
+    cudaError_t e = launch_gemv(p, PRO_NORM, EPI_F32, sms, st, GEMV_DEPENDENT);
     if (e != cudaSuccess) return e;
     const float* attn_out = b.q;    // the benchmark chain feeds Q in place of attention
     if (with_attention) {
@@ -441,7 +459,7 @@ static cudaError_t launch_layer(const sllm_cuda_model* m, int l, const ChainBufs
     o.nseg = 1;
     o.seg[0] = GemvSeg{L.wo, E, b.ffn_inp, nullptr};
     o.x = attn_out; o.norm_w = L.attn_sub_norm; o.resid = b.x;
-    e = launch_gemv(o, PRO_NORM, EPI_RESID, sms, st);
+    e = launch_gemv(o, PRO_NORM, EPI_RESID, sms, st, GEMV_DEPENDENT);
     if (e != cudaSuccess) return e;
     // ffn_norm -> gate, up, silu(gate) * up (src/forward.c:752-779)
     GemvParams f = p;
@@ -449,14 +467,14 @@ static cudaError_t launch_layer(const sllm_cuda_model* m, int l, const ChainBufs
     f.seg[0] = GemvSeg{L.gate, F, nullptr, nullptr};
     f.seg[1] = GemvSeg{L.up, F, nullptr, nullptr};
     f.x = b.ffn_inp; f.norm_w = L.ffn_norm; f.h_out = b.h;
-    e = launch_gemv(f, PRO_NORM, EPI_SILU, sms, st);
+    e = launch_gemv(f, PRO_NORM, EPI_SILU, sms, st, GEMV_DEPENDENT);
     if (e != cudaSuccess) return e;
     // ffn_sub_norm -> down, + residual (src/forward.c:781-801)
     GemvParams dn = p;
     dn.K = F; dn.nseg = 1;
     dn.seg[0] = GemvSeg{L.down, E, b.x, nullptr};
     dn.x = b.h; dn.norm_w = L.ffn_sub_norm; dn.resid = b.ffn_inp;
-    return launch_gemv(dn, PRO_NORM, EPI_RESID, sms, st);
+    return launch_gemv(dn, PRO_NORM, EPI_RESID, sms, st, GEMV_DEPENDENT);
 }
 
 static cudaError_t enqueue_step(sllm_cuda_ctx* c, cudaStream_t st) {
@@ -604,10 +622,30 @@ extern "C" int sllm_cuda_layer_chain_device(const sllm_cuda_model* m, sllm_cuda_
     if (m == nullptr || c == nullptr || x == nullptr || c->m != m || layer_begin < 0 || n_layers < 0 ||
         layer_begin + n_layers > m->n_layer || !aligned16(x))
         return fail(SLLM_CUDA_ERR_ARG, "layer_chain: bad arguments");
+    if (n_layers == 0) return SLLM_CUDA_OK;
+    CK(cudaSetDevice(m->device), "cudaSetDevice");
     int* fb = fallback_counter();
-    ChainBufs b{x, c->q, c->k, c->v, c->ffn_inp, c->h, nullptr};
-    for (int l = layer_begin; l < layer_begin + n_layers; ++l)
-        CK(launch_layer(m, l, b, fb, g_force_fallback, (cudaStream_t)stream, false, nullptr), "layer chain");
+    if (fb == nullptr) return fail(SLLM_CUDA_ERR_NOMEM, "layer_chain: diagnostics counter");
+    if (c->chain == nullptr || c->chain_begin != layer_begin || c->chain_n != n_layers || c->chain_x != x) {
+        // capture the 4 * n_layers launches once; replays cost one launch
+        if (c->chain) { cudaGraphExecDestroy(c->chain); c->chain = nullptr; }
+        ChainBufs b{x, c->q, c->k, c->v, c->ffn_inp, c->h, nullptr};
+        cudaGraph_t g = nullptr;
+        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+        cudaError_t e = cudaSuccess;
+        for (int l = layer_begin; l < layer_begin + n_layers && e == cudaSuccess; ++l)
+            e = launch_layer(m, l, b, fb, g_force_fallback, c->stream, false, nullptr);
+        cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
+        if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); return cuda_fail(e, "capture layer chain"); }
+        if (e2 != cudaSuccess) return cuda_fail(e2, "end capture");
+        e = cudaGraphInstantiate(&c->chain, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) { c->chain = nullptr; return cuda_fail(e, "instantiate layer chain"); }
+        c->chain_begin = layer_begin;
+        c->chain_n = n_layers;
+        c->chain_x = x;
+    }
+    CK(cudaGraphLaunch(c->chain, (cudaStream_t)stream), "layer chain");
     return SLLM_CUDA_OK;
 }
 
@@ -622,5 +660,114 @@ extern "C" int sllm_cuda_layer_chain(const sllm_cuda_model* m, sllm_cuda_ctx* c,
     if (rc != SLLM_CUDA_OK) return rc;
     CK(cudaMemcpyAsync(x_out, c->x, bytes, cudaMemcpyDeviceToHost, c->stream), "chain output");
     CK(cudaStreamSynchronize(c->stream), "chain sync");
+    return SLLM_CUDA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// the seven projections of a layer on independent inputs (configuration 1 as
+// the benchmark states it: each GEMV has its own f32 activation, RMSNorm'd
+// with its layer norm and quantised per token)
+// ---------------------------------------------------------------------------
+extern "C" size_t sllm_cuda_layer_projections_sizes(const sllm_cuda_model* m, size_t* y_floats_per_layer) {
+    if (m == nullptr) return 0;
+    const size_t E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa;
+    if (y_floats_per_layer) *y_floats_per_layer = 3 * E + 2 * G + 2 * F;
+    return 6 * E + F;
+}
+
+static cudaError_t launch_projections(const sllm_cuda_model* m, int l, const float* x, float* y, int* fb,
+                                      cudaStream_t st) {
+    const DevLayer& L = m->layers[l];
+    const int E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa, sms = num_sms_of(m->device);
+    // inputs: Q K V O gate up (E each), down (F); outputs: Q(E) K(G) V(G) O(E) gate(F) up(F) down(E)
+    struct P { const uint8_t* w; int rows; int K; const float* norm; size_t xoff; size_t yoff; };
+    const P ps[7] = {
+        {L.wq, E, E, L.attn_norm, 0 * (size_t)E, 0},
+        {L.wk, G, E, L.attn_norm, 1 * (size_t)E, (size_t)E},
+        {L.wv, G, E, L.attn_norm, 2 * (size_t)E, (size_t)E + G},
+        {L.wo, E, E, L.attn_sub_norm, 3 * (size_t)E, (size_t)E + 2 * G},
+        {L.gate, F, E, L.ffn_norm, 4 * (size_t)E, 2 * (size_t)E + 2 * G},
+        {L.up, F, E, L.ffn_norm, 5 * (size_t)E, 2 * (size_t)E + 2 * G + F},
+        {L.down, E, F, L.ffn_sub_norm, 6 * (size_t)E, 2 * (size_t)E + 2 * G + 2 * (size_t)F},
+    };
+    for (const P& q : ps) {
+        GemvParams p{};
+        p.K = q.K;
+        p.nseg = 1;
+        p.seg[0] = GemvSeg{q.w, q.rows, y + q.yoff, nullptr};
+        p.x = x + q.xoff;
+        p.norm_w = q.norm;
+        p.eps = m->eps;
+        p.fallback_count = fb;
+        p.force_fallback = g_force_fallback;
+        cudaError_t e = launch_gemv(p, PRO_NORM, EPI_F32, sms, st, GEMV_INDEPENDENT);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+extern "C" int sllm_cuda_layer_projections_device(const sllm_cuda_model* m, sllm_cuda_ctx* c, int32_t layer_begin,
+                                                  int32_t n_layers, const float* x, float* y, void* stream) {
+    if (m == nullptr || c == nullptr || x == nullptr || y == nullptr || c->m != m || layer_begin < 0 ||
+        n_layers < 0 || layer_begin + n_layers > m->n_layer || !aligned16(x) || !aligned16(y))
+        return fail(SLLM_CUDA_ERR_ARG, "layer_projections: bad arguments");
+    if (n_layers == 0) return SLLM_CUDA_OK;
+    CK(cudaSetDevice(m->device), "cudaSetDevice");
+    int* fb = fallback_counter();
+    if (fb == nullptr) return fail(SLLM_CUDA_ERR_NOMEM, "layer_projections: diagnostics counter");
+    size_t ystride = 0;
+    sllm_cuda_layer_projections_sizes(m, &ystride);
+    if (c->proj == nullptr || c->proj_begin != layer_begin || c->proj_n != n_layers || c->proj_x != x ||
+        c->proj_y != y) {
+        if (c->proj) { cudaGraphExecDestroy(c->proj); c->proj = nullptr; }
+        cudaGraph_t g = nullptr;
+        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+        cudaError_t e = cudaSuccess;
+        for (int l = 0; l < n_layers && e == cudaSuccess; ++l)
+            e = launch_projections(m, layer_begin + l, x, y + (size_t)l * ystride, fb, c->stream);
+        cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
+        if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); return cuda_fail(e, "capture projections"); }
+        if (e2 != cudaSuccess) return cuda_fail(e2, "end capture");
+        e = cudaGraphInstantiate(&c->proj, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) { c->proj = nullptr; return cuda_fail(e, "instantiate projections"); }
+        c->proj_begin = layer_begin; c->proj_n = n_layers; c->proj_x = x; c->proj_y = y;
+    }
+    CK(cudaGraphLaunch(c->proj, (cudaStream_t)stream), "projections");
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_layer_projections(const sllm_cuda_model* m, sllm_cuda_ctx* c, int32_t layer_begin,
+                                           int32_t n_layers, const float* x_host, float* y_host) {
+    if (m == nullptr || c == nullptr || x_host == nullptr || y_host == nullptr || c->m != m || n_layers < 0 ||
+        layer_begin < 0 || layer_begin + n_layers > m->n_layer)
+        return fail(SLLM_CUDA_ERR_ARG, "layer_projections: bad arguments");
+    CK(cudaSetDevice(m->device), "cudaSetDevice");
+    size_t ystride = 0;
+    const size_t xn = sllm_cuda_layer_projections_sizes(m, &ystride);
+    const size_t xbytes = xn * 4, ybytes = ystride * 4 * (size_t)n_layers;
+    if (c->io_cap < xbytes + ybytes) {
+        cudaFree(c->io);
+        c->io = nullptr;
+        c->io_cap = 0;
+        CK(cudaMalloc(&c->io, xbytes + ybytes), "projection buffers");
+        c->io_cap = xbytes + ybytes;
+    }
+    float* dx = (float*)c->io;
+    float* dy = (float*)((uint8_t*)c->io + ((xbytes + 255) & ~(size_t)255));
+    if (((xbytes + 255) & ~(size_t)255) + ybytes > c->io_cap) {
+        cudaFree(c->io);
+        c->io = nullptr;
+        c->io_cap = 0;
+        CK(cudaMalloc(&c->io, xbytes + ybytes + 256), "projection buffers");
+        c->io_cap = xbytes + ybytes + 256;
+        dx = (float*)c->io;
+        dy = (float*)((uint8_t*)c->io + ((xbytes + 255) & ~(size_t)255));
+    }
+    CK(cudaMemcpyAsync(dx, x_host, xbytes, cudaMemcpyHostToDevice, c->stream), "projection inputs");
+    int rc = sllm_cuda_layer_projections_device(m, c, layer_begin, n_layers, dx, dy, c->stream);
+    if (rc != SLLM_CUDA_OK) return rc;
+    CK(cudaMemcpyAsync(y_host, dy, ybytes, cudaMemcpyDeviceToHost, c->stream), "projection outputs");
+    CK(cudaStreamSynchronize(c->stream), "projections sync");
     return SLLM_CUDA_OK;
 }

@@ -108,6 +108,19 @@ __device__ __forceinline__ bool certify_mean(double S, int n, float* mean) {
     return f2u(mlo) == f2u(mhi);
 }
 
+// The same certificate without a double division: a = S * (1/n) carries two
+// more roundings, so the interval is widened by 8 * 2^-53 on top of the
+// summation bound; RN(ss/n) lies in [a(1-E), a(1+E)] and narrows uniquely
+// when both ends do.
+__device__ __forceinline__ bool certify_mean_mul(double S, int n, double inv_n, float* mean) {
+    const double E = (double)(n + 72) * 0x1p-52;
+    const double a = __dmul_rn(S, inv_n);
+    const float mlo = __double2float_rn(__dmul_rd(a, 1.0 - E));
+    const float mhi = __double2float_rn(__dmul_ru(a, 1.0 + E));
+    *mean = mlo;
+    return f2u(mlo) == f2u(mhi);
+}
+
 // The reference's own order for n % 8 == 0 (src/ops.c:262-286): lane k adds
 // (double)(x[8b+k]^2) then (double)(x[8b+4+k]^2) for b ascending; the lanes
 // are summed 0..3. Only the fallback path runs this.

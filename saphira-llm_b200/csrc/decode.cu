@@ -15,6 +15,24 @@
 
 namespace sllm {
 
+__device__ __forceinline__ void pdl_trigger_d() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait_d() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... Args, typename Kern>
+static cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 // ---------------------------------------------------------------------------
 // embedding: x = f16_to_f32(tok_embd[token]) (src/forward.c:621-626)
 // ---------------------------------------------------------------------------
@@ -44,6 +62,8 @@ attention_kernel(const AttnParams p) {
     __shared__ float s_inv;
     const int h = blockIdx.x, t = threadIdx.x;
     const int kvh = h / p.group;
+    pdl_trigger_d();
+    pdl_wait_d();                 // q, k, v come from the previous kernel
     const int pos = *p.pos_ptr;
     const int npast = pos + 1;
     const int nctx = p.n_ctx;
@@ -193,6 +213,7 @@ lm_head_kernel(const LmParams p) {
     __shared__ int bi_s[kLmWarps];
     __shared__ int s_last;
     const int E = p.E, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_wait_d();                 // x comes from the last layer
 
     // output_norm (src/forward.c:805-809), f32, certified mean
     double ss = 0.0;
@@ -208,7 +229,7 @@ lm_head_kernel(const LmParams p) {
         double S = 0.0;
         for (int i = 0; i < kLmWarps; ++i) S = __dadd_rn(S, dred[i]);
         float mean;
-        if (!certify_mean(S, E, &mean) || p.force_fallback) {
+        if (!certify_mean_mul(S, E, 1.0 / (double)E, &mean) || p.force_fallback) {
             mean = __double2float_rn(__ddiv_rn(rms_ss_reference_order(xs, E), (double)E));
             if (p.fallback_count != nullptr && blockIdx.x == 0) atomicAdd(p.fallback_count, 1);
         }
@@ -320,16 +341,14 @@ cudaError_t prepare_decode_kernels() {
 
 cudaError_t launch_attention(const AttnParams& p, int n_head, cudaStream_t st) {
     const size_t smem = (size_t)p.n_ctx * sizeof(float);
-    attention_kernel<<<n_head, kAttnThreads, smem, st>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(attention_kernel, dim3(n_head), dim3(kAttnThreads), smem, st, true, p);
 }
 
 int lm_head_grid(int num_sms) { return 2 * num_sms; }
 
 cudaError_t launch_lm_head(const LmParams& p, int grid, cudaStream_t st) {
     const size_t smem = (size_t)p.E * sizeof(float);
-    lm_head_kernel<<<grid, kLmThreads, smem, st>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(lm_head_kernel, dim3(grid), dim3(kLmThreads), smem, st, true, p);
 }
 
 }  // namespace sllm

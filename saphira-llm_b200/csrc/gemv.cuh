@@ -36,10 +36,20 @@ struct GemvParams {
     sllm_cuda_act* act_out;       // nullable
     int* fallback_count;          // nullable: counts reference-order RMSNorm sums
     int force_fallback;           // test hook: always take the reference-order sum
+    double inv_k;                 // 1.0 / K, set by launch_gemv
 };
 
+// How a launch relates to the kernel before it in the stream:
+//   GEMV_PLAIN        an ordinary launch
+//   GEMV_DEPENDENT    programmatic dependent launch; the input vector is the
+//                     previous kernel's output (waits before reading it)
+//   GEMV_INDEPENDENT  programmatic dependent launch over an input nothing in
+//                     flight writes (waits only before exiting)
+enum GemvMode { GEMV_PLAIN = 0, GEMV_DEPENDENT = 1, GEMV_INDEPENDENT = 2 };
+
 int gemv_max_k();
-cudaError_t launch_gemv(const GemvParams& p, int pro, int epi, int num_sms, cudaStream_t st);
+cudaError_t launch_gemv(const GemvParams& p, int pro, int epi, int num_sms, cudaStream_t st,
+                        int mode = GEMV_PLAIN);
 cudaError_t launch_quant_act(const float* x, int n, int8_t* q, sllm_cuda_act* act, cudaStream_t st);
 
 }  // namespace sllm

@@ -15,8 +15,20 @@
 // is one warp REDUX; integer sums are exact in any order, so the result is
 // bit-identical to the reference's scalar oracle (src/i2s_gemm.c:89-112).
 //
-// The weight loads of a warp's first rows are issued before the prologue, so
-// the DRAM latency of the first bytes overlaps the activation quantisation.
+// Latency. A GEMV of one layer moves 0.4-9 MB, a few microseconds at HBM
+// speed, so the fixed costs decide the achieved bandwidth:
+//   - the first weight words of every warp are requested before anything
+//     else, so DRAM latency overlaps the whole prologue;
+//   - the prologue keeps x and the norm weight in registers and needs three
+//     CTA barriers, each followed by a shuffle reduction of the 16 warp
+//     partials (no serial loops, no double division);
+//   - programmatic dependent launch: every CTA releases the next kernel in
+//     the stream at its start, so the next GEMV's CTAs become resident and
+//     start their own weight loads while this one finishes. A dependent
+//     kernel (the decode chain) waits for its predecessor with
+//     griddepcontrol.wait before reading its input vector; an independent one
+//     (separate inputs) waits only before it exits, which keeps completion in
+//     stream order.
 
 #include "common.cuh"
 #include "gemv.cuh"
@@ -26,161 +38,164 @@ namespace sllm {
 constexpr int kGemvThreads = 512;
 constexpr int kGemvWarps = kGemvThreads / 32;
 
-// ---------------------------------------------------------------------------
-// block reductions
-// ---------------------------------------------------------------------------
-template <int NT>
-__device__ __forceinline__ float block_max(float v, float* red) {
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Cross-warp reductions: warp w has left its partial in red[w]; after a
+// barrier every warp reduces the 16 partials with shuffles, so every thread
+// holds the result without a serial loop.
+__device__ __forceinline__ float cta_max(float v, float* red) {
     v = warp_max(v);
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
-    if (l == 0) red[w] = v;
-    __syncthreads();
-    float r = red[0];
-    for (int i = 1; i < NT / 32; ++i) r = fmaxf(r, red[i]);
-    return r;
+    v = red[threadIdx.x & (kGemvWarps - 1)];
+    for (int o = kGemvWarps / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
 }
 
-template <int NT>
-__device__ __forceinline__ int block_sum_i(int v, int* red) {
+__device__ __forceinline__ int cta_sum_i(int v, int* red) {
     v = __reduce_add_sync(0xffffffffu, v);
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
-    if (l == 0) red[w] = v;
-    __syncthreads();
-    int r = 0;
-    for (int i = 0; i < NT / 32; ++i) r += red[i];
-    return r;
+    v = red[threadIdx.x & (kGemvWarps - 1)];
+    for (int o = kGemvWarps / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
 }
 
-template <int NT>
-__device__ __forceinline__ double block_sum_d(double v, double* red) {
+__device__ __forceinline__ double cta_sum_d(double v, double* red) {
     v = warp_sum_d(v);
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
-    if (l == 0) red[w] = v;
-    __syncthreads();
-    double r = 0.0;
-    for (int i = 0; i < NT / 32; ++i) r = __dadd_rn(r, red[i]);
-    return r;
+    v = red[threadIdx.x & (kGemvWarps - 1)];
+    for (int o = kGemvWarps / 2; o > 0; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
 }
 
 struct ProSmem {
-    double dred[32];
-    float fred[32];
-    int ired[32];
-    float post[3];
-    float rms_scale;
-    sllm_cuda_act act;
+    double dred[kGemvWarps];
+    float fred[kGemvWarps];
+    int ired[kGemvWarps];
+    float fallback_mean;
 };
 
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+    return (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) | ((uint32_t)(c & 0xff) << 16) | ((uint32_t)d << 24);
+}
+
 // ---------------------------------------------------------------------------
-// Prologue: leave int8 activations in qs[K] and {scale, sum} in ps.act.
+// Prologue: int8 activations into qs[K]; returns {scale, sum}, in every thread.
 //   PRO_Q8    copy a ready row (the raw GEMV API)
 //   PRO_QUANT quantise x (src/i2s_gemm.c:45-83)
 //   PRO_NORM  RMSNorm x with norm_w (src/ops.c:254-322), then quantise
-// ys is K floats of scratch for PRO_QUANT/PRO_NORM.
+// KPT float4 of x per thread (K <= 8192 = 512 threads x 4 float4).
+// xs is K floats of scratch, touched only by the reference-order fallback.
 // ---------------------------------------------------------------------------
-template <int PRO, int NT>
-__device__ void gemv_prologue(const GemvParams& p, int8_t* qs, float* ys, ProSmem& ps) {
-    const int K = p.K, tid = threadIdx.x;
+template <int PRO, int KPT, bool DEP>
+__device__ __forceinline__ sllm_cuda_act gemv_prologue(const GemvParams& p, int8_t* qs, float* xs, ProSmem& ps) {
+    const int K = p.K, tid = threadIdx.x, K4 = K >> 2;
+    sllm_cuda_act act;
     if (PRO == PRO_Q8) {
+        if (DEP) pdl_wait();
         const int4* src = reinterpret_cast<const int4*>(p.q_in);
         int4* dst = reinterpret_cast<int4*>(qs);
-        for (int i = tid; i < K / 16; i += NT) dst[i] = src[i];
-        if (tid == 0) ps.act = *p.act_in;
+        for (int i = tid; i < K / 16; i += kGemvThreads) dst[i] = src[i];
+        act = *p.act_in;
         __syncthreads();
-        return;
+        return act;
     }
+    float4 w[KPT], x[KPT];
+    if (PRO == PRO_NORM) {
+        const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
+        #pragma unroll
+        for (int j = 0; j < KPT; ++j) {
+            const int i = tid + j * kGemvThreads;
+            w[j] = i < K4 ? w4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    if (DEP) pdl_wait();
     const float4* x4 = reinterpret_cast<const float4*>(p.x);
-    float4* y4 = reinterpret_cast<float4*>(ys);
+    #pragma unroll
+    for (int j = 0; j < KPT; ++j) {
+        const int i = tid + j * kGemvThreads;
+        x[j] = i < K4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     if (PRO == PRO_NORM) {
         double ss = 0.0;
-        for (int i = tid; i < K / 4; i += NT) {
-            const float4 v = x4[i];
-            y4[i] = v;
-            ss = __dadd_rn(ss, (double)__fmul_rn(v.x, v.x));
-            ss = __dadd_rn(ss, (double)__fmul_rn(v.y, v.y));
-            ss = __dadd_rn(ss, (double)__fmul_rn(v.z, v.z));
-            ss = __dadd_rn(ss, (double)__fmul_rn(v.w, v.w));
+        #pragma unroll
+        for (int j = 0; j < KPT; ++j) {
+            ss = __dadd_rn(ss, (double)__fmul_rn(x[j].x, x[j].x));
+            ss = __dadd_rn(ss, (double)__fmul_rn(x[j].y, x[j].y));
+            ss = __dadd_rn(ss, (double)__fmul_rn(x[j].z, x[j].z));
+            ss = __dadd_rn(ss, (double)__fmul_rn(x[j].w, x[j].w));
         }
-        const double S = block_sum_d<NT>(ss, ps.dred);
-        if (tid == 0) {
-            float mean;
-            const bool ok = certify_mean(S, K, &mean) && !p.force_fallback;
-            if (!ok) {
-                mean = __double2float_rn(__ddiv_rn(rms_ss_reference_order(ys, K), (double)K));
+        const double S = cta_sum_d(ss, ps.dred);
+        float mean;
+        const bool ok = certify_mean_mul(S, K, p.inv_k, &mean) && !p.force_fallback;   // uniform in the CTA
+        if (!ok) {
+            #pragma unroll
+            for (int j = 0; j < KPT; ++j) {
+                const int i = tid + j * kGemvThreads;
+                if (i < K4) reinterpret_cast<float4*>(xs)[i] = x[j];
+            }
+            __syncthreads();
+            if (tid == 0) {
+                ps.fallback_mean = __double2float_rn(__ddiv_rn(rms_ss_reference_order(xs, K), (double)K));
                 if (p.fallback_count != nullptr && blockIdx.x == 0) atomicAdd(p.fallback_count, 1);
             }
-            ps.rms_scale = rms_scale(mean, p.eps);
+            __syncthreads();
+            mean = ps.fallback_mean;
         }
-        __syncthreads();
-        const float sc = ps.rms_scale;
-        const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
-        float amax = 0.0f;
-        for (int i = tid; i < K / 4; i += NT) {
-            float4 v = y4[i];
-            const float4 w = w4[i];
-            v.x = __fmul_rn(__fmul_rn(sc, v.x), w.x);
-            v.y = __fmul_rn(__fmul_rn(sc, v.y), w.y);
-            v.z = __fmul_rn(__fmul_rn(sc, v.z), w.z);
-            v.w = __fmul_rn(__fmul_rn(sc, v.w), w.w);
-            y4[i] = v;
-            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        const float sc = rms_scale(mean, p.eps);
+        #pragma unroll
+        for (int j = 0; j < KPT; ++j) {
+            x[j].x = __fmul_rn(__fmul_rn(sc, x[j].x), w[j].x);
+            x[j].y = __fmul_rn(__fmul_rn(sc, x[j].y), w[j].y);
+            x[j].z = __fmul_rn(__fmul_rn(sc, x[j].z), w[j].z);
+            x[j].w = __fmul_rn(__fmul_rn(sc, x[j].w), w[j].w);
         }
-        amax = block_max<NT>(amax, ps.fred);
-        const float s = quant_scale(amax);
-        int sum = 0;
-        for (int i = tid; i < K / 4; i += NT) {
-            const float4 v = y4[i];
-            const int a = quant_one(v.x, s), b = quant_one(v.y, s), c = quant_one(v.z, s), d = quant_one(v.w, s);
-            sum += a + b + c + d;
-            reinterpret_cast<uint32_t*>(qs)[i] =
-                (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) | ((uint32_t)(c & 0xff) << 16) | ((uint32_t)d << 24);
-        }
-        sum = block_sum_i<NT>(sum, ps.ired);
-        if (tid == 0) { ps.act.scale = s; ps.act.sum = sum; }
-        __syncthreads();
-        return;
     }
-    // PRO_QUANT
+    // amax: NaN never raises it (src/i2s_gemm.c:64-69 compares a > amax)
     float amax = 0.0f;
-    for (int i = tid; i < K / 4; i += NT) {
-        const float4 v = x4[i];
-        y4[i] = v;
-        // NaN never raises amax (src/i2s_gemm.c:64-69 compares a > amax).
-        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    }
-    amax = block_max<NT>(amax, ps.fred);
+    #pragma unroll
+    for (int j = 0; j < KPT; ++j)
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(x[j].x), fabsf(x[j].y)), fmaxf(fabsf(x[j].z), fabsf(x[j].w))));
+    amax = cta_max(amax, ps.fred);
     const float s = quant_scale(amax);
     int sum = 0;
-    for (int i = tid; i < K / 4; i += NT) {
-        const float4 v = y4[i];
-        const int a = quant_one(v.x, s), b = quant_one(v.y, s), c = quant_one(v.z, s), d = quant_one(v.w, s);
-        sum += a + b + c + d;
-        reinterpret_cast<uint32_t*>(qs)[i] =
-            (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) | ((uint32_t)(c & 0xff) << 16) | ((uint32_t)d << 24);
+    #pragma unroll
+    for (int j = 0; j < KPT; ++j) {
+        const int i = tid + j * kGemvThreads;
+        if (i < K4) {
+            const int a = quant_one(x[j].x, s), b = quant_one(x[j].y, s);
+            const int c = quant_one(x[j].z, s), d = quant_one(x[j].w, s);
+            sum += a + b + c + d;
+            reinterpret_cast<uint32_t*>(qs)[i] = pack4(a, b, c, d);
+        }
     }
-    sum = block_sum_i<NT>(sum, ps.ired);
-    if (tid == 0) { ps.act.scale = s; ps.act.sum = sum; }
-    __syncthreads();
+    sum = cta_sum_i(sum, ps.ired);     // its barrier also publishes qs
+    act.scale = s;
+    act.sum = sum;
+    return act;
 }
 
 // ---------------------------------------------------------------------------
 // the GEMV
 // ---------------------------------------------------------------------------
-template <int WPL, int U, int PRO, int EPI>
+template <int WPL, int U, int PRO, int EPI, bool DEP>
 __global__ void __launch_bounds__(kGemvThreads)
 i2s_gemv_kernel(const GemvParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ ProSmem ps;
+    constexpr int KPT = (WPL + 3) / 4;
     const int K = p.K;
     const int W = K >> 4;                      // 32-bit words per row
     int8_t* qs = reinterpret_cast<int8_t*>(smem);
-    float* ys = reinterpret_cast<float*>(smem + K);
+    float* xs = reinterpret_cast<float*>(smem + K);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
-    const bool pair = (EPI == EPI_SILU);
+    pdl_trigger();
+
+    constexpr bool pair = (EPI == EPI_SILU);
     const int rows0 = p.seg[0].rows;
     const int rows1 = p.nseg > 1 ? p.seg[1].rows : 0;
     const int total = pair ? rows0 : rows0 + rows1 + (p.nseg > 2 ? p.seg[2].rows : 0);
@@ -222,21 +237,25 @@ i2s_gemv_kernel(const GemvParams p) {
 
     if (task < ntasks) load_task(task);
 
-    gemv_prologue<PRO, kGemvThreads>(p, qs, ys, ps);
-
-    if (EPI != EPI_DOTS && threadIdx.x < p.nseg) {
-        // (the raw-dot API never reads the scale tail: its caller need not pass one)
-        const GemvSeg& sg = p.seg[threadIdx.x];
-        // the per-tensor scale follows the packed codes (src/quant.c:102-106)
-        const float ws = *reinterpret_cast<const float*>(sg.w + (size_t)sg.rows * (size_t)(K >> 2));
-        ps.post[threadIdx.x] = __fdiv_rn(ws, ps.act.scale);
+    // the per-tensor scales follow the packed codes (src/quant.c:102-106);
+    // the raw-dot API never reads them (its caller need not pass a tail)
+    float ws[3] = {0.f, 0.f, 0.f};
+    if (EPI != EPI_DOTS) {
+        #pragma unroll
+        for (int s = 0; s < 3; ++s)
+            if (s < p.nseg)
+                ws[s] = *reinterpret_cast<const float*>(p.seg[s].w + (size_t)p.seg[s].rows * (size_t)(K >> 2));
     }
+
+    const sllm_cuda_act act = gemv_prologue<PRO, KPT, DEP>(p, qs, xs, ps);
+    float post[3];
+    #pragma unroll
+    for (int s = 0; s < 3; ++s) post[s] = __fdiv_rn(ws[s], act.scale);
     if (blockIdx.x == 0 && p.q_out != nullptr) {
         for (int i = threadIdx.x; i < K / 16; i += kGemvThreads)
             reinterpret_cast<int4*>(p.q_out)[i] = reinterpret_cast<const int4*>(qs)[i];
-        if (threadIdx.x == 0 && p.act_out != nullptr) *p.act_out = ps.act;
+        if (threadIdx.x == 0 && p.act_out != nullptr) *p.act_out = act;
     }
-    __syncthreads();
 
     // the int8 activations this lane's words pair with
     const uint32_t* q32 = reinterpret_cast<const uint32_t*>(qs);
@@ -248,7 +267,7 @@ i2s_gemv_kernel(const GemvParams p) {
         for (int f = 0; f < 4; ++f)
             aq[i][f] = wi < W ? (int)q32[(wi >> 3) * 32 + 8 * f + (wi & 7)] : 0;
     }
-    const int asum = ps.act.sum;
+    const int asum = act.sum;
 
     while (task < ntasks) {
         int dot[R];
@@ -265,37 +284,30 @@ i2s_gemv_kernel(const GemvParams p) {
         #pragma unroll
         for (int j = 0; j < R; ++j) dot[j] = __reduce_add_sync(0xffffffffu, dot[j]);
 
-        if (EPI == EPI_SILU) {
-            // row r of gate (seg 0) and of up (seg 1): h = silu(g) * u
-            // (src/forward.c:765-778, src/ops.c:452-456)
-            if (lane < U) {
-                int s, r;
-                locate(cur, lane, s, r);
-                int d0 = dot[0], d1 = dot[U];
-                #pragma unroll
-                for (int j = 1; j < U; ++j) if (lane == j) { d0 = dot[j]; d1 = dot[U + j]; }
-                if (s >= 0) {
-                    const float g = __fmul_rn(__int2float_rn(d0 - asum), ps.post[0]);
-                    const float u = __fmul_rn(__int2float_rn(d1 - asum), ps.post[1]);
+        if (lane < U) {
+            int s, r;
+            locate(cur, lane, s, r);
+            int d0 = dot[0], d1 = pair ? dot[U] : 0;
+            #pragma unroll
+            for (int j = 1; j < U; ++j)
+                if (lane == j) { d0 = dot[j]; if (pair) d1 = dot[U + j]; }
+            if (s >= 0) {
+                if (EPI == EPI_SILU) {
+                    // row r of gate (seg 0) and of up (seg 1): h = silu(g) * u
+                    // (src/forward.c:765-778, src/ops.c:452-456)
+                    const float g = __fmul_rn(__int2float_rn(d0 - asum), post[0]);
+                    const float u = __fmul_rn(__int2float_rn(d1 - asum), post[1]);
                     if (p.seg[0].y) p.seg[0].y[r] = g;
                     if (p.seg[1].y) p.seg[1].y[r] = u;
                     if (p.seg[0].dots) p.seg[0].dots[r] = d0;
                     if (p.seg[1].dots) p.seg[1].dots[r] = d1;
                     p.h_out[r] = __fmul_rn(silu_block(g), u);
-                }
-            }
-        } else {
-            if (lane < U) {
-                int s, r;
-                locate(cur, lane, s, r);
-                int d = dot[0];
-                #pragma unroll
-                for (int j = 1; j < U; ++j) if (lane == j) d = dot[j];
-                if (s >= 0) {
+                } else {
+                    const float ps_ = s == 0 ? post[0] : (s == 1 ? post[1] : post[2]);
                     const GemvSeg& sg = p.seg[s];
-                    if (sg.dots) sg.dots[r] = d;
+                    if (sg.dots) sg.dots[r] = d0;
                     if (EPI != EPI_DOTS && sg.y) {
-                        float v = __fmul_rn(__int2float_rn(d - asum), ps.post[s]);
+                        float v = __fmul_rn(__int2float_rn(d0 - asum), ps_);
                         if (EPI == EPI_RESID) v = __fadd_rn(v, p.resid[r]);
                         sg.y[r] = v;
                     }
@@ -303,17 +315,18 @@ i2s_gemv_kernel(const GemvParams p) {
             }
         }
     }
+    if (!DEP) pdl_wait();   // complete in stream order
 }
 
 // standalone quantisation (sllm_cuda_i2s_quant_act): one CTA
 __global__ void __launch_bounds__(kGemvThreads)
 quant_act_kernel(const float* x, int n, int8_t* q, sllm_cuda_act* act) {
-    __shared__ float fred[32];
-    __shared__ int ired[32];
+    __shared__ float fred[kGemvWarps];
+    __shared__ int ired[kGemvWarps];
     const int tid = threadIdx.x;
     float amax = 0.0f;
     for (int i = tid; i < n; i += kGemvThreads) amax = fmaxf(amax, fabsf(x[i]));
-    amax = block_max<kGemvThreads>(amax, fred);
+    amax = cta_max(amax, fred);
     const float s = quant_scale(amax);
     int sum = 0;
     for (int i = tid; i < n; i += kGemvThreads) {
@@ -321,26 +334,35 @@ quant_act_kernel(const float* x, int n, int8_t* q, sllm_cuda_act* act) {
         q[i] = (int8_t)v;
         sum += v;
     }
-    sum = block_sum_i<kGemvThreads>(sum, ired);
+    sum = cta_sum_i(sum, ired);
     if (tid == 0) { act->scale = s; act->sum = sum; }
 }
 
 // ---------------------------------------------------------------------------
 // host-side dispatch over the compile-time shapes
 // ---------------------------------------------------------------------------
-template <int WPL, int U, int PRO, int EPI>
-static cudaError_t launch_one(const GemvParams& p, int grid, cudaStream_t st) {
+template <int WPL, int U, int PRO, int EPI, bool DEP>
+static cudaError_t launch_one(const GemvParams& p, int grid, cudaStream_t st, bool pdl) {
     // K <= 8192: at most 40 KB of dynamic shared memory, inside the default
     // 48 KB, so no attribute call is needed (launches may be graph-captured)
-    const size_t smem = (size_t)p.K + (PRO == PRO_Q8 ? 0 : (size_t)p.K * 4);
-    i2s_gemv_kernel<WPL, U, PRO, EPI><<<grid, kGemvThreads, smem, st>>>(p);
-    return cudaGetLastError();
+    const size_t smem = (size_t)p.K * 5;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, i2s_gemv_kernel<WPL, U, PRO, EPI, DEP>, p);
 }
 
-template <int U, int PRO, int EPI>
-static cudaError_t launch_wpl(const GemvParams& p, int wpl, int grid, cudaStream_t st) {
+template <int U, int PRO, int EPI, bool DEP>
+static cudaError_t launch_wpl(const GemvParams& p, int wpl, int grid, cudaStream_t st, bool pdl) {
     switch (wpl) {
-#define SLLM_WPL_CASE(n) case n: return launch_one<n, U, PRO, EPI>(p, grid, st);
+#define SLLM_WPL_CASE(n) case n: return launch_one<n, U, PRO, EPI, DEP>(p, grid, st, pdl);
         SLLM_WPL_CASE(1) SLLM_WPL_CASE(2) SLLM_WPL_CASE(3) SLLM_WPL_CASE(4)
         SLLM_WPL_CASE(5) SLLM_WPL_CASE(6) SLLM_WPL_CASE(7) SLLM_WPL_CASE(8)
         SLLM_WPL_CASE(9) SLLM_WPL_CASE(10) SLLM_WPL_CASE(11) SLLM_WPL_CASE(12)
@@ -352,7 +374,9 @@ static cudaError_t launch_wpl(const GemvParams& p, int wpl, int grid, cudaStream
 
 int gemv_max_k() { return 16 * 32 * 16; }   // WPL 16: 8192
 
-cudaError_t launch_gemv(const GemvParams& p, int pro, int epi, int num_sms, cudaStream_t st) {
+cudaError_t launch_gemv(const GemvParams& p_in, int pro, int epi, int num_sms, cudaStream_t st, int mode) {
+    GemvParams p = p_in;
+    p.inv_k = 1.0 / (double)p.K;
     const int W = p.K / 16;
     const int wpl = (W + 31) / 32;
     if (p.K % kQK != 0 || wpl < 1 || wpl > 16) return cudaErrorInvalidValue;
@@ -364,11 +388,18 @@ cudaError_t launch_gemv(const GemvParams& p, int pro, int epi, int num_sms, cuda
     const int cap = 2 * num_sms;
     if (grid > cap) grid = cap;
     if (grid < 1) grid = 1;
-    if (pro == PRO_Q8 && epi == EPI_DOTS) return launch_wpl<U, PRO_Q8, EPI_DOTS>(p, wpl, grid, st);
-    if (pro == PRO_QUANT && epi == EPI_F32) return launch_wpl<U, PRO_QUANT, EPI_F32>(p, wpl, grid, st);
-    if (pro == PRO_NORM && epi == EPI_F32) return launch_wpl<U, PRO_NORM, EPI_F32>(p, wpl, grid, st);
-    if (pro == PRO_NORM && epi == EPI_RESID) return launch_wpl<U, PRO_NORM, EPI_RESID>(p, wpl, grid, st);
-    if (pro == PRO_NORM && epi == EPI_SILU) return launch_wpl<U, PRO_NORM, EPI_SILU>(p, wpl, grid, st);
+    const bool pdl = mode != GEMV_PLAIN;
+    if (mode == GEMV_INDEPENDENT) {
+        if (pro == PRO_NORM && epi == EPI_F32) return launch_wpl<U, PRO_NORM, EPI_F32, false>(p, wpl, grid, st, pdl);
+        return cudaErrorInvalidValue;
+    }
+    // plain launches and dependent (decode-chain) launches share the DEP form:
+    // without the launch attribute griddepcontrol.wait returns at once
+    if (pro == PRO_Q8 && epi == EPI_DOTS) return launch_wpl<U, PRO_Q8, EPI_DOTS, true>(p, wpl, grid, st, pdl);
+    if (pro == PRO_QUANT && epi == EPI_F32) return launch_wpl<U, PRO_QUANT, EPI_F32, true>(p, wpl, grid, st, pdl);
+    if (pro == PRO_NORM && epi == EPI_F32) return launch_wpl<U, PRO_NORM, EPI_F32, true>(p, wpl, grid, st, pdl);
+    if (pro == PRO_NORM && epi == EPI_RESID) return launch_wpl<U, PRO_NORM, EPI_RESID, true>(p, wpl, grid, st, pdl);
+    if (pro == PRO_NORM && epi == EPI_SILU) return launch_wpl<U, PRO_NORM, EPI_SILU, true>(p, wpl, grid, st, pdl);
     return cudaErrorInvalidValue;
 }
 

@@ -67,5 +67,10 @@ def cuda(pkg):
 
 
 def bits(a):
-    """Bit patterns of a float32 array, for exact comparisons (NaN-safe)."""
-    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+    """Bit patterns of a float32 array, for exact comparisons. Every NaN maps
+    to one pattern: x86 produces the negative default NaN (0xffc00000) where a
+    GPU produces 0x7fffffff, and both mean the same value."""
+    a = np.ascontiguousarray(a, np.float32)
+    u = a.view(np.uint32).copy()
+    u[np.isnan(a)] = 0x7FC00000
+    return u

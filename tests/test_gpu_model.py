@@ -141,3 +141,29 @@ def test_layer_chain_matches_oracle(cuda, orc, synth):
     for layer in range(3):
         want = orc.layer_chain(m.desc(), layer, want)
     assert np.array_equal(bits(got), bits(want))
+
+
+def test_layer_projections_match_oracle(cuda, orc, synth):
+    """The seven projections on independent inputs (benchmark configuration
+    1): each output equals the oracle's norm -> quant -> GEMV -> epilogue."""
+    import importlib
+    cfg = synth.Config(n_layer=2, n_vocab=256)
+    m = synth.SynthModel(cfg, seed=55)
+    model = cuda.Model(m.desc())
+    c = model.ctx(8)
+    xs_n, ys_n = cuda.projection_sizes(model)
+    E, F, G = cfg.n_embd, cfg.n_ff, cfg.n_embd_gqa
+    assert xs_n == 6 * E + F and ys_n == 3 * E + 2 * G + 2 * F
+    x = np.random.default_rng(5).standard_normal(xs_n).astype(np.float32)
+    y = c.layer_projections(0, 2, x)
+    specs = [("attn_q", E, E, "attn_norm"), ("attn_k", G, E, "attn_norm"), ("attn_v", G, E, "attn_norm"),
+             ("attn_output", E, E, "attn_sub_norm"), ("ffn_gate", F, E, "ffn_norm"),
+             ("ffn_up", F, E, "ffn_norm"), ("ffn_down", E, F, "ffn_sub_norm")]
+    for il in range(2):
+        xo = yo = 0
+        for name, rows, n, norm in specs:
+            xn = orc.rms_norm(x[xo:xo + n], m.tensors[f"blk.{il}.{norm}.weight"].view(np.float32), cfg.eps)
+            want, _ = orc.gemv_f32(m.tensors[f"blk.{il}.{name}.weight"], rows, n, xn)
+            assert np.array_equal(bits(y[il, yo:yo + rows]), bits(want)), (il, name)
+            xo += n
+            yo += rows
