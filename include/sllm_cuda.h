@@ -262,6 +262,28 @@ SLLM_CUDA_API int sllm_cuda_layer_projections_device(const sllm_cuda_model * m, 
                                                      int32_t layer_begin, int32_t n_layers,
                                                      const float * x, float * y, void * stream);
 
+/*
+ * sllm_cuda_layer_chain_device without any allocation. This entry point has
+ * no counterpart in the reference: it serves callers that cannot call
+ * cudaMalloc -- code recording a CUDA graph under a strict capture mode, hosts
+ * whose own allocator already holds the device's memory, loops that cannot
+ * take cudaMalloc's implicit synchronisation -- and that hold a model but no
+ * context. Same results as sllm_cuda_layer_chain_device, bit for bit.
+ *
+ * Its scratch (2*n_embd + 2*n_embd_gqa + n_ff floats) is a fixed 128 KB
+ * device array inside the library (32768 floats), held by every device that
+ * loads the library until the process exits; a larger model is refused with
+ * SLLM_CUDA_ERR_TOO_LARGE. The first call on a device looks up the array's
+ * address (cudaGetSymbolAddress); make that first call before any stream
+ * capture. Every call on a device shares the one array, so calls that can
+ * overlap on the GPU (different streams, or different threads) race: order
+ * them on one stream. `x` is a device vector of n_embd floats, 16-byte
+ * aligned, updated in place; asynchronous on `stream`.
+ */
+SLLM_CUDA_API int sllm_cuda_layer_chain_device_noalloc(const sllm_cuda_model * m,
+                                                       int32_t layer_begin, int32_t n_layers,
+                                                       float * x, void * stream);
+
 /* Bytes of weights one decode step streams: every I2_S tensor with its scale
  * tail, every norm, and the F16 embedding / output head. */
 SLLM_CUDA_API size_t sllm_cuda_model_weight_bytes(const sllm_cuda_model * m);

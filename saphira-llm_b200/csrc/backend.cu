@@ -771,3 +771,61 @@ extern "C" int sllm_cuda_layer_projections(const sllm_cuda_model* m, sllm_cuda_c
     CK(cudaStreamSynchronize(c->stream), "projections sync");
     return SLLM_CUDA_OK;
 }
+
+// ---------------------------------------------------------------------------
+// The layer chain with no allocation at all.
+//
+// For callers that must not allocate device memory: code recording into a
+// CUDA graph under a strict capture mode (cudaMalloc is illegal while the
+// stream captures), hosts whose own allocator has already reserved the
+// device's memory (a late cudaMalloc fails or fragments it), and real-time
+// loops that cannot afford cudaMalloc's implicit device synchronisation. They
+// have a model but no context, so the chain's five scratch vectors (q, k, v,
+// ffn_inp: n_embd / n_embd_gqa floats; h: n_ff floats) live in this file-scope
+// device array instead of a context. The array is loaded with the library and
+// every device that loads it holds it until the process exits.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchFloats = 32768;   // 128 KB: 2*n_embd + 2*n_embd_gqa + n_ff must fit
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+// The array's device address, looked up once per device with that device
+// current (the host-side symbol is only a stand-in and must never reach a
+// kernel). The first call on a device does this lookup.
+static int noalloc_scratch(int dev, float** out) {
+    static std::mutex mu;
+    static std::vector<float*> ptrs;
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)ptrs.size() <= dev) ptrs.resize(dev + 1, nullptr);
+    if (ptrs[dev] == nullptr) {
+        float* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress((void**)&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) return cuda_fail(e, "layer_chain_noalloc: cudaGetSymbolAddress");
+        ptrs[dev] = p;
+    }
+    *out = ptrs[dev];
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_layer_chain_device_noalloc(const sllm_cuda_model* m, int32_t layer_begin,
+                                                    int32_t n_layers, float* x, void* stream) {
+    if (m == nullptr || x == nullptr || layer_begin < 0 || n_layers < 0 || layer_begin + n_layers > m->n_layer ||
+        !aligned16(x))
+        return fail(SLLM_CUDA_ERR_ARG, "layer_chain_noalloc: bad arguments");
+    const size_t E = m->n_embd, G = m->n_embd_gqa, F = m->n_ff;
+    const size_t need = 2 * E + 2 * G + F;
+    if (need > kNoAllocScratchFloats)
+        return fail(SLLM_CUDA_ERR_TOO_LARGE,
+                    "layer_chain_noalloc: the model needs %zu scratch floats (2*n_embd + 2*n_embd_gqa + n_ff); "
+                    "the static scratch holds %zu", need, kNoAllocScratchFloats);
+    if (n_layers == 0) return SLLM_CUDA_OK;
+    CK(cudaSetDevice(m->device), "cudaSetDevice");
+    float* s = nullptr;
+    int rc = noalloc_scratch(m->device, &s);
+    if (rc != SLLM_CUDA_OK) return rc;
+    // every scratch vector is written before it is read within one call
+    // (Q/K/V -> q, k, v; O -> ffn_inp; gate/up -> h), so nothing is cleared
+    ChainBufs b{x, s, s + E, s + E + G, s + E + 2 * G, s + 2 * E + 2 * G, nullptr};
+    for (int l = layer_begin; l < layer_begin + n_layers; ++l)
+        CK(launch_layer(m, l, b, nullptr, 0, (cudaStream_t)stream, false, nullptr), "layer_chain_noalloc");
+    return SLLM_CUDA_OK;
+}
