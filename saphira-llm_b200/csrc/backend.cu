@@ -17,6 +17,7 @@
 
 #include "common.cuh"
 #include "decode.cuh"
+#include "engine.cuh"
 #include "gemv.cuh"
 #include "../../include/sllm_cuda.h"
 #include "../../include/sllm_cuda_testing.h"
@@ -28,6 +29,7 @@ using namespace sllm;
 // ---------------------------------------------------------------------------
 static thread_local std::string g_last_error;
 static int g_force_fallback = 0;
+static float g_engine_eps = 0.0f;          // set just before an engine program is captured
 static int* g_fallback_counter = nullptr;   // device int, lazily allocated per process
 
 static int fail(int status, const char* fmt, ...) {
@@ -193,7 +195,15 @@ extern "C" int sllm_cuda_i2s_gemv_f32(const uint8_t* w, size_t n_rows, size_t n,
 struct DevLayer {
     const uint8_t *wq, *wk, *wv, *wo, *gate, *up, *down;
     const float *attn_norm, *attn_sub_norm, *ffn_norm, *ffn_sub_norm;
+    // per-tensor scales, read from the host copies at upload (src/quant.c:102-106)
+    float s_wq, s_wk, s_wv, s_wo, s_gate, s_up, s_down;
 };
+
+static float host_i2s_scale(const uint8_t* w, size_t rows, size_t cols) {
+    float s;
+    std::memcpy(&s, w + rows * cols / 4, sizeof s);
+    return s;
+}
 
 struct sllm_cuda_model {
     int device = 0;
@@ -281,6 +291,14 @@ extern "C" int sllm_cuda_model_upload(const sllm_cuda_model_desc* d, int device,
         L.attn_sub_norm = (const float*)(m->blob + items[ix[8]].off);
         L.ffn_norm = (const float*)(m->blob + items[ix[9]].off);
         L.ffn_sub_norm = (const float*)(m->blob + items[ix[10]].off);
+        const sllm_cuda_layer_desc& H = d->layers[l];
+        L.s_wq = host_i2s_scale(H.wq, E, E);
+        L.s_wk = host_i2s_scale(H.wk, G, E);
+        L.s_wv = host_i2s_scale(H.wv, G, E);
+        L.s_wo = host_i2s_scale(H.wo, E, E);
+        L.s_gate = host_i2s_scale(H.ffn_gate, F, E);
+        L.s_up = host_i2s_scale(H.ffn_up, F, E);
+        L.s_down = host_i2s_scale(H.ffn_down, E, F);
     }
     m->output_norm = (float*)(m->blob + items[out_norm].off);
     for (const Item& it : items) m->weight_bytes += it.bytes;
@@ -298,6 +316,104 @@ extern "C" void sllm_cuda_model_free(sllm_cuda_model* m) {
 }
 
 extern "C" size_t sllm_cuda_model_weight_bytes(const sllm_cuda_model* m) { return m ? m->weight_bytes : 0; }
+
+// ---------------------------------------------------------------------------
+// engine programs (engine.cu): device copies of the group / op / start tables
+// ---------------------------------------------------------------------------
+struct EngineProgram {
+    EngGroup* groups = nullptr;
+    EngOp* ops = nullptr;
+    EngCursor* starts = nullptr;
+    unsigned* barrier = nullptr;
+    int* error = nullptr;
+    int n_stages = 0;
+    int grid = 0;
+    cudaGraphExec_t exec = nullptr;
+    // what the program was built for
+    int key_begin = -1, key_n = -1;
+    const void* key_x = nullptr;
+    const void* key_y = nullptr;
+};
+
+static void engine_program_free(EngineProgram& p) {
+    if (p.exec) cudaGraphExecDestroy(p.exec);
+    cudaFree(p.groups); cudaFree(p.ops); cudaFree(p.starts); cudaFree(p.barrier); cudaFree(p.error);
+    p = EngineProgram();
+}
+
+// Split every stage's rows over `grid` CTAs so that each CTA streams the same
+// number of weight bytes (a row of a gate/up pair weighs two rows).
+static std::vector<EngCursor> engine_starts(const std::vector<EngOp>& ops, const std::vector<int>& stage_first,
+                                            int grid) {
+    const int n_stages = (int)stage_first.size() - 1;
+    std::vector<EngCursor> st((size_t)n_stages * (grid + 1));
+    for (int s = 0; s < n_stages; ++s) {
+        const int o0 = stage_first[s], o1 = stage_first[s + 1];
+        double total = 0.0;
+        for (int o = o0; o < o1; ++o) total += (double)ops[o].rows * (ops[o].K / 4) * (ops[o].epi == EPI_SILU ? 2 : 1);
+        EngCursor* out = &st[(size_t)s * (grid + 1)];
+        int o = o0;
+        double before = 0.0;           // cost of ops [o0, o)
+        for (int c = 0; c <= grid; ++c) {
+            if (c == grid) { out[c] = EngCursor{o1, 0}; break; }
+            const double target = total * c / grid;
+            while (o < o1) {
+                const double rc = (double)(ops[o].K / 4) * (ops[o].epi == EPI_SILU ? 2 : 1);
+                const double cost = ops[o].rows * rc;
+                if (before + cost > target) {
+                    int row = (int)std::ceil((target - before) / rc);
+                    if (row >= ops[o].rows) { before += cost; ++o; continue; }
+                    out[c] = EngCursor{o, row < 0 ? 0 : row};
+                    break;
+                }
+                before += cost;
+                ++o;
+            }
+            if (o >= o1) out[c] = EngCursor{o1, 0};
+        }
+    }
+    return st;
+}
+
+static int engine_program_build(EngineProgram& p, const std::vector<EngGroup>& groups, const std::vector<EngOp>& ops,
+                                const std::vector<int>& stage_first, int device, cudaStream_t capture_stream,
+                                int* fallback) {
+    engine_program_free(p);
+    p.grid = engine_grid(device);
+    p.n_stages = (int)stage_first.size() - 1;
+    const std::vector<EngCursor> st = engine_starts(ops, stage_first, p.grid);
+    cudaError_t e = cudaMalloc(&p.groups, groups.size() * sizeof(EngGroup));
+    if (e == cudaSuccess) e = cudaMalloc(&p.ops, ops.size() * sizeof(EngOp));
+    if (e == cudaSuccess) e = cudaMalloc(&p.starts, st.size() * sizeof(EngCursor));
+    if (e == cudaSuccess) e = cudaMalloc(&p.barrier, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMalloc(&p.error, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemcpy(p.groups, groups.data(), groups.size() * sizeof(EngGroup), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(p.ops, ops.data(), ops.size() * sizeof(EngOp), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(p.starts, st.data(), st.size() * sizeof(EngCursor), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(p.error, 0, sizeof(int));
+    if (e != cudaSuccess) { engine_program_free(p); return cuda_fail(e, "engine program"); }
+    if (engine_smem_bytes((int)groups.size(), (int)ops.size(), p.n_stages) == 0) {
+        engine_program_free(p);
+        return fail(SLLM_CUDA_ERR_TOO_LARGE, "engine program: %zu ops do not fit in shared memory", ops.size());
+    }
+    CK(prepare_engine(), "engine attributes");
+    EngParams ep{};
+    ep.groups = p.groups; ep.ops = p.ops; ep.starts = p.starts; ep.n_stages = p.n_stages;
+    ep.n_groups = (int)groups.size(); ep.n_ops = (int)ops.size();
+    ep.barrier = p.barrier; ep.error = p.error; ep.fallback_count = fallback; ep.force_fallback = g_force_fallback;
+    ep.eps = g_engine_eps;     // every group of a program comes from one model
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(capture_stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    e = cudaMemsetAsync(p.barrier, 0, sizeof(unsigned), capture_stream);
+    if (e == cudaSuccess) e = launch_engine(ep, p.grid, capture_stream);
+    cudaError_t e2 = cudaStreamEndCapture(capture_stream, &g);
+    if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); engine_program_free(p); return cuda_fail(e, "capture engine"); }
+    if (e2 != cudaSuccess) { engine_program_free(p); return cuda_fail(e2, "end capture"); }
+    e = cudaGraphInstantiate(&p.exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) { p.exec = nullptr; engine_program_free(p); return cuda_fail(e, "instantiate engine"); }
+    return SLLM_CUDA_OK;
+}
 
 // ---------------------------------------------------------------------------
 // context
@@ -333,6 +449,8 @@ struct sllm_cuda_ctx {
     float* proj_y = nullptr;
     void* io = nullptr;              // device staging of the host-buffer entry points
     size_t io_cap = 0;
+    EngineProgram eng_chain;         // the layer chain on the persistent engine
+    EngineProgram eng_proj;          // the independent projections on the persistent engine
 };
 
 // the reference's angle recurrence (src/ops.c:529-549), on the host libm
@@ -368,6 +486,8 @@ extern "C" void sllm_cuda_ctx_free(sllm_cuda_ctx* c) {
     cudaFree(c->pos); cudaFree(c->tok_seq); cudaFree(c->prompt_end); cudaFree(c->argmax_hist);
     cudaFreeHost(c->pinned);
     cudaFree(c->io);
+    engine_program_free(c->eng_chain);
+    engine_program_free(c->eng_proj);
     delete c;
 }
 
@@ -617,6 +737,51 @@ extern "C" int sllm_cuda_ctx_last_logits(const sllm_cuda_ctx* c, float* host_out
 // ---------------------------------------------------------------------------
 // the layer projection chain (benchmark configuration 1)
 // ---------------------------------------------------------------------------
+// The chain as an engine program: per layer four stages (Q/K/V, O, gate/up,
+// down), each behind a grid barrier because its input is the whole output of
+// the stage before.
+static int chain_program(const sllm_cuda_model* m, sllm_cuda_ctx* c, int begin, int n, float* x, int* fb) {
+    const int E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa;
+    std::vector<EngGroup> groups;
+    std::vector<EngOp> ops;
+    std::vector<int> stage_first;
+    auto op = [&](const uint8_t* w, const uint8_t* w2, float* y, const float* resid, float* h, int rows, int K,
+                  int epi, int group, float ws, float ws2) {
+        EngOp o{};
+        o.w = w; o.w2 = w2; o.y = y; o.resid = resid; o.h = h; o.rows = rows; o.K = K; o.epi = epi; o.group = group;
+        o.chunk_rows = engine_chunk_rows(K, epi);
+        o.ws = ws; o.ws2 = ws2;
+        ops.push_back(o);
+    };
+    for (int l = begin; l < begin + n; ++l) {
+        const DevLayer& L = m->layers[l];
+        stage_first.push_back((int)ops.size());
+        groups.push_back(EngGroup{x, L.attn_norm, E, PRO_NORM});
+        op(L.wq, nullptr, c->q, nullptr, nullptr, E, E, EPI_F32, (int)groups.size() - 1, L.s_wq, 0.f);
+        op(L.wk, nullptr, c->k, nullptr, nullptr, G, E, EPI_F32, (int)groups.size() - 1, L.s_wk, 0.f);
+        op(L.wv, nullptr, c->v, nullptr, nullptr, G, E, EPI_F32, (int)groups.size() - 1, L.s_wv, 0.f);
+        stage_first.push_back((int)ops.size());
+        groups.push_back(EngGroup{c->q, L.attn_sub_norm, E, PRO_NORM});
+        op(L.wo, nullptr, c->ffn_inp, x, nullptr, E, E, EPI_RESID, (int)groups.size() - 1, L.s_wo, 0.f);
+        stage_first.push_back((int)ops.size());
+        groups.push_back(EngGroup{c->ffn_inp, L.ffn_norm, E, PRO_NORM});
+        op(L.gate, L.up, nullptr, nullptr, c->h, F, E, EPI_SILU, (int)groups.size() - 1, L.s_gate, L.s_up);
+        stage_first.push_back((int)ops.size());
+        groups.push_back(EngGroup{c->h, L.ffn_sub_norm, F, PRO_NORM});
+        op(L.down, nullptr, x, c->ffn_inp, nullptr, E, F, EPI_RESID, (int)groups.size() - 1, L.s_down, 0.f);
+    }
+    stage_first.push_back((int)ops.size());
+    g_engine_eps = m->eps;
+    return engine_program_build(c->eng_chain, groups, ops, stage_first, m->device, c->stream, fb);
+}
+
+static int engine_error(const EngineProgram& p) {
+    int err = 0;
+    if (p.error != nullptr && cudaMemcpy(&err, p.error, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && err != 0)
+        return fail(SLLM_CUDA_ERR_TIMEOUT, "engine: a bounded device wait gave up (code %d)", err);
+    return SLLM_CUDA_OK;
+}
+
 extern "C" int sllm_cuda_layer_chain_device(const sllm_cuda_model* m, sllm_cuda_ctx* c, int32_t layer_begin,
                                             int32_t n_layers, float* x, void* stream) {
     if (m == nullptr || c == nullptr || x == nullptr || c->m != m || layer_begin < 0 || n_layers < 0 ||
@@ -626,26 +791,13 @@ extern "C" int sllm_cuda_layer_chain_device(const sllm_cuda_model* m, sllm_cuda_
     CK(cudaSetDevice(m->device), "cudaSetDevice");
     int* fb = fallback_counter();
     if (fb == nullptr) return fail(SLLM_CUDA_ERR_NOMEM, "layer_chain: diagnostics counter");
-    if (c->chain == nullptr || c->chain_begin != layer_begin || c->chain_n != n_layers || c->chain_x != x) {
-        // capture the 4 * n_layers launches once; replays cost one launch
-        if (c->chain) { cudaGraphExecDestroy(c->chain); c->chain = nullptr; }
-        ChainBufs b{x, c->q, c->k, c->v, c->ffn_inp, c->h, nullptr};
-        cudaGraph_t g = nullptr;
-        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
-        cudaError_t e = cudaSuccess;
-        for (int l = layer_begin; l < layer_begin + n_layers && e == cudaSuccess; ++l)
-            e = launch_layer(m, l, b, fb, g_force_fallback, c->stream, false, nullptr);
-        cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
-        if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); return cuda_fail(e, "capture layer chain"); }
-        if (e2 != cudaSuccess) return cuda_fail(e2, "end capture");
-        e = cudaGraphInstantiate(&c->chain, g, 0);
-        cudaGraphDestroy(g);
-        if (e != cudaSuccess) { c->chain = nullptr; return cuda_fail(e, "instantiate layer chain"); }
-        c->chain_begin = layer_begin;
-        c->chain_n = n_layers;
-        c->chain_x = x;
+    EngineProgram& p = c->eng_chain;
+    if (p.exec == nullptr || p.key_begin != layer_begin || p.key_n != n_layers || p.key_x != x) {
+        int rc = chain_program(m, c, layer_begin, n_layers, x, fb);
+        if (rc != SLLM_CUDA_OK) return rc;
+        p.key_begin = layer_begin; p.key_n = n_layers; p.key_x = x;
     }
-    CK(cudaGraphLaunch(c->chain, (cudaStream_t)stream), "layer chain");
+    CK(cudaGraphLaunch(p.exec, (cudaStream_t)stream), "layer chain");
     return SLLM_CUDA_OK;
 }
 
@@ -660,7 +812,7 @@ extern "C" int sllm_cuda_layer_chain(const sllm_cuda_model* m, sllm_cuda_ctx* c,
     if (rc != SLLM_CUDA_OK) return rc;
     CK(cudaMemcpyAsync(x_out, c->x, bytes, cudaMemcpyDeviceToHost, c->stream), "chain output");
     CK(cudaStreamSynchronize(c->stream), "chain sync");
-    return SLLM_CUDA_OK;
+    return engine_error(c->eng_chain);
 }
 
 // ---------------------------------------------------------------------------
@@ -675,35 +827,40 @@ extern "C" size_t sllm_cuda_layer_projections_sizes(const sllm_cuda_model* m, si
     return 6 * E + F;
 }
 
-static cudaError_t launch_projections(const sllm_cuda_model* m, int l, const float* x, float* y, int* fb,
-                                      cudaStream_t st) {
-    const DevLayer& L = m->layers[l];
-    const int E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa, sms = num_sms_of(m->device);
-    // inputs: Q K V O gate up (E each), down (F); outputs: Q(E) K(G) V(G) O(E) gate(F) up(F) down(E)
-    struct P { const uint8_t* w; int rows; int K; const float* norm; size_t xoff; size_t yoff; };
-    const P ps[7] = {
-        {L.wq, E, E, L.attn_norm, 0 * (size_t)E, 0},
-        {L.wk, G, E, L.attn_norm, 1 * (size_t)E, (size_t)E},
-        {L.wv, G, E, L.attn_norm, 2 * (size_t)E, (size_t)E + G},
-        {L.wo, E, E, L.attn_sub_norm, 3 * (size_t)E, (size_t)E + 2 * G},
-        {L.gate, F, E, L.ffn_norm, 4 * (size_t)E, 2 * (size_t)E + 2 * G},
-        {L.up, F, E, L.ffn_norm, 5 * (size_t)E, 2 * (size_t)E + 2 * G + F},
-        {L.down, E, F, L.ffn_sub_norm, 6 * (size_t)E, 2 * (size_t)E + 2 * G + 2 * (size_t)F},
-    };
-    for (const P& q : ps) {
-        GemvParams p{};
-        p.K = q.K;
-        p.nseg = 1;
-        p.seg[0] = GemvSeg{q.w, q.rows, y + q.yoff, nullptr};
-        p.x = x + q.xoff;
-        p.norm_w = q.norm;
-        p.eps = m->eps;
-        p.fallback_count = fb;
-        p.force_fallback = g_force_fallback;
-        cudaError_t e = launch_gemv(p, PRO_NORM, EPI_F32, sms, st, GEMV_INDEPENDENT);
-        if (e != cudaSuccess) return e;
+// The seven projections of each layer as one engine stage: every GEMV has its
+// own input, so nothing waits for anything and the weights stream back to back.
+static int projections_program(const sllm_cuda_model* m, sllm_cuda_ctx* c, int begin, int n, const float* x,
+                               float* y, int* fb) {
+    const int E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa;
+    size_t ystride = 0;
+    sllm_cuda_layer_projections_sizes(m, &ystride);
+    std::vector<EngGroup> groups;
+    std::vector<EngOp> ops;
+    for (int l = 0; l < n; ++l) {
+        const DevLayer& L = m->layers[begin + l];
+        float* yl = y + (size_t)l * ystride;
+        struct P { const uint8_t* w; int rows; int K; const float* norm; size_t xoff; size_t yoff; float ws; };
+        const P ps[7] = {
+            {L.wq, E, E, L.attn_norm, 0 * (size_t)E, 0, L.s_wq},
+            {L.wk, G, E, L.attn_norm, 1 * (size_t)E, (size_t)E, L.s_wk},
+            {L.wv, G, E, L.attn_norm, 2 * (size_t)E, (size_t)E + G, L.s_wv},
+            {L.wo, E, E, L.attn_sub_norm, 3 * (size_t)E, (size_t)E + 2 * G, L.s_wo},
+            {L.gate, F, E, L.ffn_norm, 4 * (size_t)E, 2 * (size_t)E + 2 * G, L.s_gate},
+            {L.up, F, E, L.ffn_norm, 5 * (size_t)E, 2 * (size_t)E + 2 * G + F, L.s_up},
+            {L.down, E, F, L.ffn_sub_norm, 6 * (size_t)E, 2 * (size_t)E + 2 * G + 2 * (size_t)F, L.s_down},
+        };
+        for (const P& q : ps) {
+            groups.push_back(EngGroup{x + q.xoff, q.norm, q.K, PRO_NORM});
+            EngOp o{};
+            o.w = q.w; o.y = yl + q.yoff; o.rows = q.rows; o.K = q.K; o.epi = EPI_F32; o.ws = q.ws;
+            o.group = (int)groups.size() - 1;
+            o.chunk_rows = engine_chunk_rows(q.K, EPI_F32);
+            ops.push_back(o);
+        }
     }
-    return cudaSuccess;
+    std::vector<int> stage_first{0, (int)ops.size()};
+    g_engine_eps = m->eps;
+    return engine_program_build(c->eng_proj, groups, ops, stage_first, m->device, c->stream, fb);
 }
 
 extern "C" int sllm_cuda_layer_projections_device(const sllm_cuda_model* m, sllm_cuda_ctx* c, int32_t layer_begin,
@@ -715,25 +872,13 @@ extern "C" int sllm_cuda_layer_projections_device(const sllm_cuda_model* m, sllm
     CK(cudaSetDevice(m->device), "cudaSetDevice");
     int* fb = fallback_counter();
     if (fb == nullptr) return fail(SLLM_CUDA_ERR_NOMEM, "layer_projections: diagnostics counter");
-    size_t ystride = 0;
-    sllm_cuda_layer_projections_sizes(m, &ystride);
-    if (c->proj == nullptr || c->proj_begin != layer_begin || c->proj_n != n_layers || c->proj_x != x ||
-        c->proj_y != y) {
-        if (c->proj) { cudaGraphExecDestroy(c->proj); c->proj = nullptr; }
-        cudaGraph_t g = nullptr;
-        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
-        cudaError_t e = cudaSuccess;
-        for (int l = 0; l < n_layers && e == cudaSuccess; ++l)
-            e = launch_projections(m, layer_begin + l, x, y + (size_t)l * ystride, fb, c->stream);
-        cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
-        if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); return cuda_fail(e, "capture projections"); }
-        if (e2 != cudaSuccess) return cuda_fail(e2, "end capture");
-        e = cudaGraphInstantiate(&c->proj, g, 0);
-        cudaGraphDestroy(g);
-        if (e != cudaSuccess) { c->proj = nullptr; return cuda_fail(e, "instantiate projections"); }
-        c->proj_begin = layer_begin; c->proj_n = n_layers; c->proj_x = x; c->proj_y = y;
+    EngineProgram& p = c->eng_proj;
+    if (p.exec == nullptr || p.key_begin != layer_begin || p.key_n != n_layers || p.key_x != x || p.key_y != y) {
+        int rc = projections_program(m, c, layer_begin, n_layers, x, y, fb);
+        if (rc != SLLM_CUDA_OK) return rc;
+        p.key_begin = layer_begin; p.key_n = n_layers; p.key_x = x; p.key_y = y;
     }
-    CK(cudaGraphLaunch(c->proj, (cudaStream_t)stream), "projections");
+    CK(cudaGraphLaunch(p.exec, (cudaStream_t)stream), "projections");
     return SLLM_CUDA_OK;
 }
 
@@ -769,7 +914,7 @@ extern "C" int sllm_cuda_layer_projections(const sllm_cuda_model* m, sllm_cuda_c
     if (rc != SLLM_CUDA_OK) return rc;
     CK(cudaMemcpyAsync(y_host, dy, ybytes, cudaMemcpyDeviceToHost, c->stream), "projection outputs");
     CK(cudaStreamSynchronize(c->stream), "projections sync");
-    return SLLM_CUDA_OK;
+    return engine_error(c->eng_proj);
 }
 
 // ---------------------------------------------------------------------------

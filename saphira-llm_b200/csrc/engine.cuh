@@ -1,0 +1,80 @@
+// engine.cuh -- the persistent I2_S GEMV engine (engine.cu).
+//
+// One cooperative launch runs a whole program of GEMVs: a list of stages,
+// each a list of ops whose rows are split over the CTAs by bytes. Inside a
+// CTA a producer warp streams the weight rows of every chunk it will need, in
+// program order, into a ring of shared-memory slots with TMA bulk copies,
+// running ahead across op and stage boundaries (weights never depend on
+// activations); sixteen consumer warps compute from shared memory. Stages are
+// separated by a grid barrier, because a stage's input vector is the whole
+// output of the stage before.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "gemv.cuh"
+
+namespace sllm {
+
+constexpr int kEngConsumerWarps = 15;    // + 1 producer: 16 warps, 4 per SM sub-partition
+constexpr int kEngThreads = (kEngConsumerWarps + 1) * 32;
+constexpr int kEngSlotBytes = 32 * 1024;
+constexpr int kEngSlots = 5;
+
+// an input vector and how each CTA turns it into int8 activations
+struct EngGroup {
+    const float* x;          // input (read through L2: other CTAs may have written it)
+    const float* norm_w;     // PRO_NORM weight (nullable for PRO_QUANT)
+    int K;
+    int pro;                 // PRO_NORM or PRO_QUANT
+};
+
+// one weight tensor (or a gate/up pair for EPI_SILU)
+struct EngOp {
+    const uint8_t* w;        // rows x K/4 bytes, scale tail after them
+    const uint8_t* w2;       // EPI_SILU: the up tensor (same shape)
+    float* y;                // EPI_F32 / EPI_RESID output
+    const float* resid;      // EPI_RESID: y = proj + resid
+    float* h;                // EPI_SILU: h = silu(gate) * up
+    int rows;
+    int K;
+    int epi;                 // EPI_F32, EPI_RESID or EPI_SILU
+    int group;               // index into the groups
+    int chunk_rows;          // rows per slot
+    float ws;                // the per-tensor scale of w (src/quant.c:102-106), read at upload
+    float ws2;               // ... of w2
+};
+
+// a position in the op list: row `row` of op `op`
+struct EngCursor {
+    int op;
+    int row;
+};
+
+struct EngParams {
+    const EngGroup* groups;
+    const EngOp* ops;
+    const EngCursor* starts;     // [n_stages][grid + 1]: CTA c of stage s runs [starts[s][c], starts[s][c+1])
+    int n_groups;
+    int n_ops;
+    int n_stages;
+    unsigned int* barrier;       // zero at launch; counts CTA arrivals over all stages
+    int* error;                  // 0, or why a bounded wait gave up
+    float eps;
+    int* fallback_count;         // nullable
+    int force_fallback;
+};
+
+enum EngError { ENG_OK = 0, ENG_TIMEOUT_FULL = 1, ENG_TIMEOUT_EMPTY = 2, ENG_TIMEOUT_GRID = 3 };
+
+// rows of an op per slot, so that a chunk fills at most one slot
+int engine_chunk_rows(int K, int epi);
+// dynamic shared memory of a program: the ring, the int8 activations, and the
+// group / op / cursor tables every CTA copies in at start (0 when too large)
+int engine_smem_bytes(int n_groups, int n_ops, int n_stages);
+int engine_grid(int device);
+cudaError_t prepare_engine();     // once, outside any stream capture
+cudaError_t launch_engine(const EngParams& p, int grid, cudaStream_t st);
+
+}  // namespace sllm

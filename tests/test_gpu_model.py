@@ -167,3 +167,57 @@ def test_layer_projections_match_oracle(cuda, orc, synth):
             assert np.array_equal(bits(y[il, yo:yo + rows]), bits(want)), (il, name)
             xo += n
             yo += rows
+
+
+@pytest.mark.parametrize("cfg_kw", [
+    dict(n_layer=2, n_embd=256, n_ff=512, n_head=2, n_head_kv=1, n_vocab=64),
+    dict(n_layer=2, n_embd=1152, n_ff=3072, n_head=9, n_head_kv=3, n_vocab=64),
+    dict(n_layer=1, n_embd=8192, n_ff=8192, n_head=64, n_head_kv=8, n_vocab=64),
+])
+def test_engine_shapes_chain_and_projections(cuda, orc, synth, cfg_kw):
+    """The persistent engine on widths the 2B model does not use (K = 256 to
+    8192, odd head counts), for the dependent chain and the projections."""
+    cfg = synth.small_config(**cfg_kw)
+    m = synth.SynthModel(cfg, seed=17)
+    model = cuda.Model(m.desc())
+    c = model.ctx(8)
+    x = np.random.default_rng(17).standard_normal(cfg.n_embd).astype(np.float32)
+    got = c.layer_chain(0, cfg.n_layer, x)
+    want = x
+    for layer in range(cfg.n_layer):
+        want = orc.layer_chain(m.desc(), layer, want)
+    assert np.array_equal(bits(got), bits(want))
+    xs_n, ys_n = cuda.projection_sizes(model)
+    xp = np.random.default_rng(18).standard_normal(xs_n).astype(np.float32)
+    y = c.layer_projections(0, cfg.n_layer, xp)
+    E, F, G = cfg.n_embd, cfg.n_ff, cfg.n_embd_gqa
+    specs = [("attn_q", E, E, "attn_norm"), ("attn_k", G, E, "attn_norm"), ("attn_v", G, E, "attn_norm"),
+             ("attn_output", E, E, "attn_sub_norm"), ("ffn_gate", F, E, "ffn_norm"),
+             ("ffn_up", F, E, "ffn_norm"), ("ffn_down", E, F, "ffn_sub_norm")]
+    for il in range(cfg.n_layer):
+        xo = yo = 0
+        for name, rows, n, norm in specs:
+            xn = orc.rms_norm(xp[xo:xo + n], m.tensors[f"blk.{il}.{norm}.weight"].view(np.float32), cfg.eps)
+            want_y, _ = orc.gemv_f32(m.tensors[f"blk.{il}.{name}.weight"], rows, n, xn)
+            assert np.array_equal(bits(y[il, yo:yo + rows]), bits(want_y)), (il, name)
+            xo += n
+            yo += rows
+
+
+def test_engine_fallback_path(cuda, orc, synth):
+    """The engine's certified-sum fallback gives the same bits."""
+    cfg = synth.Config(n_layer=2, n_vocab=64)
+    m = synth.SynthModel(cfg, seed=23)
+    model = cuda.Model(m.desc())
+    x = np.random.default_rng(23).standard_normal(cfg.n_embd).astype(np.float32)
+    cuda.set_force_fallback(True)
+    try:
+        c = model.ctx(8)                  # programs are built (and the hook read) on first use
+        before = cuda.fallback_count()
+        got = c.layer_chain(0, 2, x)
+        after = cuda.fallback_count()
+    finally:
+        cuda.set_force_fallback(False)
+    want = orc.layer_chain(m.desc(), 1, orc.layer_chain(m.desc(), 0, x))
+    assert np.array_equal(bits(got), bits(want))
+    assert after > before
