@@ -377,7 +377,7 @@ static std::vector<EngCursor> engine_starts(const std::vector<EngOp>& ops, const
 
 static int engine_program_build(EngineProgram& p, const std::vector<EngGroup>& groups, const std::vector<EngOp>& ops,
                                 const std::vector<int>& stage_first, int device, cudaStream_t capture_stream,
-                                int* fallback) {
+                                int* fallback, int wa, int wb) {
     engine_program_free(p);
     p.grid = engine_grid(device);
     p.n_stages = (int)stage_first.size() - 1;
@@ -405,7 +405,7 @@ static int engine_program_build(EngineProgram& p, const std::vector<EngGroup>& g
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(capture_stream, cudaStreamCaptureModeThreadLocal), "begin capture");
     e = cudaMemsetAsync(p.barrier, 0, sizeof(unsigned), capture_stream);
-    if (e == cudaSuccess) e = launch_engine(ep, p.grid, capture_stream);
+    if (e == cudaSuccess) e = launch_engine(ep, p.grid, capture_stream, wa, wb);
     cudaError_t e2 = cudaStreamEndCapture(capture_stream, &g);
     if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); engine_program_free(p); return cuda_fail(e, "capture engine"); }
     if (e2 != cudaSuccess) { engine_program_free(p); return cuda_fail(e2, "end capture"); }
@@ -772,7 +772,8 @@ static int chain_program(const sllm_cuda_model* m, sllm_cuda_ctx* c, int begin, 
     }
     stage_first.push_back((int)ops.size());
     g_engine_eps = m->eps;
-    return engine_program_build(c->eng_chain, groups, ops, stage_first, m->device, c->stream, fb);
+    return engine_program_build(c->eng_chain, groups, ops, stage_first, m->device, c->stream, fb,
+                                engine_wpl(E), engine_wpl(F));
 }
 
 static int engine_error(const EngineProgram& p) {
@@ -791,6 +792,28 @@ extern "C" int sllm_cuda_layer_chain_device(const sllm_cuda_model* m, sllm_cuda_
     CK(cudaSetDevice(m->device), "cudaSetDevice");
     int* fb = fallback_counter();
     if (fb == nullptr) return fail(SLLM_CUDA_ERR_NOMEM, "layer_chain: diagnostics counter");
+    if (!engine_supports(engine_wpl(m->n_embd), engine_wpl(m->n_ff))) {
+        // widths the engine is not compiled for: one fused GEMV launch per
+        // projection, programmatically chained, captured as a graph
+        if (c->chain == nullptr || c->chain_begin != layer_begin || c->chain_n != n_layers || c->chain_x != x) {
+            if (c->chain) { cudaGraphExecDestroy(c->chain); c->chain = nullptr; }
+            ChainBufs b{x, c->q, c->k, c->v, c->ffn_inp, c->h, nullptr};
+            cudaGraph_t g = nullptr;
+            CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+            cudaError_t e = cudaSuccess;
+            for (int l = layer_begin; l < layer_begin + n_layers && e == cudaSuccess; ++l)
+                e = launch_layer(m, l, b, fb, g_force_fallback, c->stream, false, nullptr);
+            cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
+            if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); return cuda_fail(e, "capture layer chain"); }
+            if (e2 != cudaSuccess) return cuda_fail(e2, "end capture");
+            e = cudaGraphInstantiate(&c->chain, g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) { c->chain = nullptr; return cuda_fail(e, "instantiate layer chain"); }
+            c->chain_begin = layer_begin; c->chain_n = n_layers; c->chain_x = x;
+        }
+        CK(cudaGraphLaunch(c->chain, (cudaStream_t)stream), "layer chain");
+        return SLLM_CUDA_OK;
+    }
     EngineProgram& p = c->eng_chain;
     if (p.exec == nullptr || p.key_begin != layer_begin || p.key_n != n_layers || p.key_x != x) {
         int rc = chain_program(m, c, layer_begin, n_layers, x, fb);
@@ -827,6 +850,38 @@ extern "C" size_t sllm_cuda_layer_projections_sizes(const sllm_cuda_model* m, si
     return 6 * E + F;
 }
 
+// The seven projections of a layer as seven independent fused GEMV launches
+// (the fallback for widths the engine is not compiled for).
+static cudaError_t launch_projections(const sllm_cuda_model* m, int l, const float* x, float* y, int* fb,
+                                      cudaStream_t st) {
+    const DevLayer& L = m->layers[l];
+    const int E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa, sms = num_sms_of(m->device);
+    struct P { const uint8_t* w; int rows; int K; const float* norm; size_t xoff; size_t yoff; };
+    const P ps[7] = {
+        {L.wq, E, E, L.attn_norm, 0 * (size_t)E, 0},
+        {L.wk, G, E, L.attn_norm, 1 * (size_t)E, (size_t)E},
+        {L.wv, G, E, L.attn_norm, 2 * (size_t)E, (size_t)E + G},
+        {L.wo, E, E, L.attn_sub_norm, 3 * (size_t)E, (size_t)E + 2 * G},
+        {L.gate, F, E, L.ffn_norm, 4 * (size_t)E, 2 * (size_t)E + 2 * G},
+        {L.up, F, E, L.ffn_norm, 5 * (size_t)E, 2 * (size_t)E + 2 * G + F},
+        {L.down, E, F, L.ffn_sub_norm, 6 * (size_t)E, 2 * (size_t)E + 2 * G + 2 * (size_t)F},
+    };
+    for (const P& q : ps) {
+        GemvParams p{};
+        p.K = q.K;
+        p.nseg = 1;
+        p.seg[0] = GemvSeg{q.w, q.rows, y + q.yoff, nullptr};
+        p.x = x + q.xoff;
+        p.norm_w = q.norm;
+        p.eps = m->eps;
+        p.fallback_count = fb;
+        p.force_fallback = g_force_fallback;
+        cudaError_t e = launch_gemv(p, PRO_NORM, EPI_F32, sms, st, GEMV_INDEPENDENT);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
 // The seven projections of each layer as one engine stage: every GEMV has its
 // own input, so nothing waits for anything and the weights stream back to back.
 static int projections_program(const sllm_cuda_model* m, sllm_cuda_ctx* c, int begin, int n, const float* x,
@@ -860,7 +915,8 @@ static int projections_program(const sllm_cuda_model* m, sllm_cuda_ctx* c, int b
     }
     std::vector<int> stage_first{0, (int)ops.size()};
     g_engine_eps = m->eps;
-    return engine_program_build(c->eng_proj, groups, ops, stage_first, m->device, c->stream, fb);
+    return engine_program_build(c->eng_proj, groups, ops, stage_first, m->device, c->stream, fb,
+                                engine_wpl(E), engine_wpl(F));
 }
 
 extern "C" int sllm_cuda_layer_projections_device(const sllm_cuda_model* m, sllm_cuda_ctx* c, int32_t layer_begin,
@@ -872,6 +928,28 @@ extern "C" int sllm_cuda_layer_projections_device(const sllm_cuda_model* m, sllm
     CK(cudaSetDevice(m->device), "cudaSetDevice");
     int* fb = fallback_counter();
     if (fb == nullptr) return fail(SLLM_CUDA_ERR_NOMEM, "layer_projections: diagnostics counter");
+    if (!engine_supports(engine_wpl(m->n_embd), engine_wpl(m->n_ff))) {
+        size_t ystride = 0;
+        sllm_cuda_layer_projections_sizes(m, &ystride);
+        if (c->proj == nullptr || c->proj_begin != layer_begin || c->proj_n != n_layers || c->proj_x != x ||
+            c->proj_y != y) {
+            if (c->proj) { cudaGraphExecDestroy(c->proj); c->proj = nullptr; }
+            cudaGraph_t g = nullptr;
+            CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+            cudaError_t e = cudaSuccess;
+            for (int l = 0; l < n_layers && e == cudaSuccess; ++l)
+                e = launch_projections(m, layer_begin + l, x, y + (size_t)l * ystride, fb, c->stream);
+            cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
+            if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); return cuda_fail(e, "capture projections"); }
+            if (e2 != cudaSuccess) return cuda_fail(e2, "end capture");
+            e = cudaGraphInstantiate(&c->proj, g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) { c->proj = nullptr; return cuda_fail(e, "instantiate projections"); }
+            c->proj_begin = layer_begin; c->proj_n = n_layers; c->proj_x = x; c->proj_y = y;
+        }
+        CK(cudaGraphLaunch(c->proj, (cudaStream_t)stream), "projections");
+        return SLLM_CUDA_OK;
+    }
     EngineProgram& p = c->eng_proj;
     if (p.exec == nullptr || p.key_begin != layer_begin || p.key_n != n_layers || p.key_x != x || p.key_y != y) {
         int rc = projections_program(m, c, layer_begin, n_layers, x, y, fb);

@@ -54,7 +54,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 65536;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
         : "r"(smem_u32(bar)), "r"(parity)
@@ -92,6 +92,28 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 }
 
 __device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+// unsigned bytes of a times signed bytes of b, summed into c
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// One 32-bit weight word against its four activation words, into four field
+// accumulators: field f is masked in place (not shifted), so accumulator f
+// collects 4^(3-f) times its dot; they are shifted down once per row.
+// Every term is exact in int32 (|acc| < 64 * 2 * 128 * K/4 < 2^25).
+__device__ __forceinline__ void i2s_word_fields(uint32_t w, const int4& a, int& f0, int& f1, int& f2, int& f3) {
+    f0 = dp4a_us(w & 0xC0C0C0C0u, a.x, f0);
+    f1 = dp4a_us(w & 0x30303030u, a.y, f1);
+    f2 = dp4a_us(w & 0x0C0C0C0Cu, a.z, f2);
+    f3 = dp4a_us(w & 0x03030303u, a.w, f3);
+}
+
+__device__ __forceinline__ int fields_total(int f0, int f1, int f2, int f3) {
+    return (f0 >> 6) + (f1 >> 4) + (f2 >> 2) + f3;
+}
 
 // reduction slots: one per consumer warp, padded to 16 with the identity
 constexpr int kRed = 16;
@@ -246,8 +268,12 @@ __device__ sllm_cuda_act eng_prologue(const EngGroup& g, const EngParams& P, int
             const int a = quant_one(x[j].x, s), b = quant_one(x[j].y, s);
             const int c = quant_one(x[j].z, s), d = quant_one(x[j].w, s);
             sum += a + b + c + d;
-            reinterpret_cast<uint32_t*>(qs)[i] = (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) |
-                                                 ((uint32_t)(c & 0xff) << 16) | ((uint32_t)d << 24);
+            // activation word i pairs with field f = (i % 32) / 8 of weight word
+            // wi = (i / 32) * 8 + i % 8; stored at [wi][f] so that a lane
+            // fetches the four words of one weight word in one 16-byte load
+            const int wi = ((i >> 5) << 3) + (i & 7), f = (i >> 3) & 3;
+            reinterpret_cast<uint32_t*>(qs)[wi * 4 + f] = (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) |
+                                                          ((uint32_t)(c & 0xff) << 16) | ((uint32_t)d << 24);
         }
     }
     sum = csum_i(sum, es.ired, warp, lane);     // its barrier also publishes qs
@@ -258,79 +284,152 @@ __device__ sllm_cuda_act eng_prologue(const EngGroup& g, const EngParams& P, int
 }
 
 // ---------------------------------------------------------------------------
-// one chunk of rows from a ring slot
+// consumers: every chunk of one op, activations held in registers
 // ---------------------------------------------------------------------------
-template <int WPL>
-__device__ __forceinline__ void eng_chunk(const EngOp& op, int r0, int n, const uint8_t* slot, const int8_t* qs,
-                                          int asum, float post, float post2, int warp, int lane) {
+// rows per consumer warp per chunk: the chunk fills most of a 32 KB slot
+__host__ __device__ constexpr int eng_rows_per_warp(int wpl, bool pair) {
+    return pair ? (wpl <= 2 ? 4 : (wpl <= 4 ? 2 : 1))
+                : (wpl <= 4 ? 4 : (wpl == 5 ? 3 : (wpl <= 8 ? 2 : 1)));
+}
+
+__device__ __forceinline__ bool consumer_wait_full(EngSmem& es, const EngParams& P, int slot, uint32_t use) {
+    if (*(volatile int*)&es.abort_flag) return false;
+    if (mbar_wait(&es.full[slot], use & 1)) return true;
+    es.abort_flag = 1;
+    atomicExch(P.error, ENG_TIMEOUT_FULL);
+    return false;
+}
+
+// R rows per warp of a plain (one-tensor) chunk. PRED guards the chunk's
+// last rows and a row width that is not a whole number of warp words.
+template <int WPL, int R, bool PRED>
+__device__ __forceinline__ void plain_rows(const int4 (&aq)[WPL], const uint8_t* base, int n, int rb, int W,
+                                           int warp, int lane, int (&dot)[R]) {
+    int acc[R][4];
+    #pragma unroll
+    for (int t = 0; t < R; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
+    const uint32_t* rp[R];
+    #pragma unroll
+    for (int t = 0; t < R; ++t)
+        rp[t] = reinterpret_cast<const uint32_t*>(base + (size_t)(warp + kEngConsumerWarps * t) * rb) + lane;
+    #pragma unroll
+    for (int i = 0; i < WPL; ++i) {
+        #pragma unroll
+        for (int t = 0; t < R; ++t) {
+            if (!PRED || (lane + 32 * i < W && warp + kEngConsumerWarps * t < n)) {
+                const uint32_t w = rp[t][32 * i];
+                i2s_word_fields(w, aq[i], acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
+            }
+        }
+    }
+    #pragma unroll
+    for (int t = 0; t < R; ++t)
+        dot[t] = __reduce_add_sync(0xffffffffu, fields_total(acc[t][0], acc[t][1], acc[t][2], acc[t][3]));
+}
+
+template <int WPL, int R, bool PRED>
+__device__ __forceinline__ void pair_rows(const int4 (&aq)[WPL], const uint8_t* base, int n, int rb, int W,
+                                          int warp, int lane, int (&dg)[R], int (&du)[R]) {
+    #pragma unroll
+    for (int t = 0; t < R; ++t) {
+        const int j = warp + kEngConsumerWarps * t;
+        int g0 = 0, g1 = 0, g2 = 0, g3 = 0, u0 = 0, u1 = 0, u2 = 0, u3 = 0;
+        const uint32_t* rg = reinterpret_cast<const uint32_t*>(base + (size_t)j * rb) + lane;
+        const uint32_t* ru = reinterpret_cast<const uint32_t*>(base + (size_t)(n + j) * rb) + lane;
+        #pragma unroll
+        for (int i = 0; i < WPL; ++i) {
+            if (!PRED || (lane + 32 * i < W && j < n)) {
+                i2s_word_fields(rg[32 * i], aq[i], g0, g1, g2, g3);
+                i2s_word_fields(ru[32 * i], aq[i], u0, u1, u2, u3);
+            }
+        }
+        dg[t] = __reduce_add_sync(0xffffffffu, fields_total(g0, g1, g2, g3));
+        du[t] = __reduce_add_sync(0xffffffffu, fields_total(u0, u1, u2, u3));
+    }
+}
+
+// Every consecutive chunk of op `o`, activations loaded once into registers.
+// All walk state is passed by reference into this inlined body, so it stays
+// in registers.
+template <int WPL, bool PAIR>
+__device__ __forceinline__ void eng_run_op(const EngOp& op, uint32_t& k, int& o, int& r, int& n, bool& have,
+                                           ChunkWalk& walk, uint8_t* ring, EngSmem& es, const int8_t* qs,
+                                           int asum, float post, float post2, const EngParams& P, int warp,
+                                           int lane) {
+    constexpr int R = eng_rows_per_warp(WPL, PAIR);
     const int K = op.K, W = K >> 4, rb = K >> 2;
-    const uint32_t* q32 = reinterpret_cast<const uint32_t*>(qs);
-    int aq[WPL][4];
+    const int cur = o;
+    const bool full_width = (W == 32 * WPL);
+    int4 aq[WPL];
     #pragma unroll
     for (int i = 0; i < WPL; ++i) {
         const int wi = lane + 32 * i;
-        #pragma unroll
-        for (int f = 0; f < 4; ++f) aq[i][f] = wi < W ? (int)q32[(wi >> 3) * 32 + 8 * f + (wi & 7)] : 0;
+        aq[i] = wi < W ? reinterpret_cast<const int4*>(qs)[wi] : make_int4(0, 0, 0, 0);
     }
-    if (op.epi == EPI_SILU) {
-        const uint8_t* up = slot + (size_t)n * rb;
-        for (int j = warp; j < n; j += kEngConsumerWarps) {
-            const uint32_t* rg = reinterpret_cast<const uint32_t*>(slot + (size_t)j * rb);
-            const uint32_t* ru = reinterpret_cast<const uint32_t*>(up + (size_t)j * rb);
-            int ag = 0, au = 0;
-            #pragma unroll
-            for (int i = 0; i < WPL; ++i) {
-                const int wi = lane + 32 * i;
-                const uint32_t wg = wi < W ? rg[wi] : 0u, wu = wi < W ? ru[wi] : 0u;
-                ag = i2s_dot_word(wg, aq[i][0], aq[i][1], aq[i][2], aq[i][3], ag);
-                au = i2s_dot_word(wu, aq[i][0], aq[i][1], aq[i][2], aq[i][3], au);
-            }
-            ag = __reduce_add_sync(0xffffffffu, ag);
-            au = __reduce_add_sync(0xffffffffu, au);
-            if (lane == 0) {
+    while (true) {
+        const int slot = (int)(k % kEngSlots);
+        if (consumer_wait_full(es, P, slot, k / kEngSlots)) {
+            const uint8_t* base = ring + (size_t)slot * kEngSlotBytes;
+            const bool fast = full_width && n == kEngConsumerWarps * R;
+            if (PAIR) {
+                int dg[R], du[R];
+                if (fast) pair_rows<WPL, R, false>(aq, base, n, rb, W, warp, lane, dg, du);
+                else pair_rows<WPL, R, true>(aq, base, n, rb, W, warp, lane, dg, du);
                 // h = silu(gate) * up (src/forward.c:765-778, src/ops.c:452-456)
-                const float g = __fmul_rn(__int2float_rn(ag - asum), post);
-                const float u = __fmul_rn(__int2float_rn(au - asum), post2);
-                op.h[r0 + j] = __fmul_rn(silu_block(g), u);
+                #pragma unroll
+                for (int t = 0; t < R; ++t) {
+                    const int j = warp + kEngConsumerWarps * t;
+                    if (lane == t && j < n) {
+                        const float g = __fmul_rn(__int2float_rn(dg[t] - asum), post);
+                        const float u = __fmul_rn(__int2float_rn(du[t] - asum), post2);
+                        op.h[r + j] = __fmul_rn(silu_block(g), u);
+                    }
+                }
+            } else {
+                int dot[R];
+                if (fast) plain_rows<WPL, R, false>(aq, base, n, rb, W, warp, lane, dot);
+                else plain_rows<WPL, R, true>(aq, base, n, rb, W, warp, lane, dot);
+                int mine = dot[0];
+                #pragma unroll
+                for (int t = 1; t < R; ++t)
+                    if (lane == t) mine = dot[t];
+                const int j = warp + kEngConsumerWarps * lane;
+                if (lane < R && j < n) {
+                    float v = __fmul_rn(__int2float_rn(mine - asum), post);
+                    if (op.epi == EPI_RESID) v = __fadd_rn(v, __ldcg(op.resid + r + j));
+                    op.y[r + j] = v;
+                }
             }
         }
-        return;
-    }
-    for (int j = warp; j < n; j += kEngConsumerWarps) {
-        const uint32_t* rw = reinterpret_cast<const uint32_t*>(slot + (size_t)j * rb);
-        int acc = 0;
-        #pragma unroll
-        for (int i = 0; i < WPL; ++i) {
-            const int wi = lane + 32 * i;
-            acc = i2s_dot_word(wi < W ? rw[wi] : 0u, aq[i][0], aq[i][1], aq[i][2], aq[i][3], acc);
-        }
-        acc = __reduce_add_sync(0xffffffffu, acc);
-        if (lane == 0) {
-            float v = __fmul_rn(__int2float_rn(acc - asum), post);
-            if (op.epi == EPI_RESID) v = __fadd_rn(v, __ldcg(op.resid + r0 + j));
-            op.y[r0 + j] = v;
-        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&es.empty[k % kEngSlots]);
+        ++k;
+        have = walk.next(o, r, n);
+        if (!have || o != cur) return;
     }
 }
 
-__device__ __forceinline__ void eng_chunk_dispatch(const EngOp& op, int r0, int n, const uint8_t* slot,
-                                                   const int8_t* qs, int asum, float post, float post2, int warp,
-                                                   int lane) {
-    const int wpl = ((op.K >> 4) + 31) >> 5;
-    switch (wpl) {
-#define SLLM_ENG_CASE(N) case N: eng_chunk<N>(op, r0, n, slot, qs, asum, post, post2, warp, lane); break;
-        SLLM_ENG_CASE(1) SLLM_ENG_CASE(2) SLLM_ENG_CASE(3) SLLM_ENG_CASE(4)
-        SLLM_ENG_CASE(5) SLLM_ENG_CASE(6) SLLM_ENG_CASE(7) SLLM_ENG_CASE(8)
-        SLLM_ENG_CASE(9) SLLM_ENG_CASE(10) SLLM_ENG_CASE(11) SLLM_ENG_CASE(12)
-        SLLM_ENG_CASE(13) SLLM_ENG_CASE(14) SLLM_ENG_CASE(15) SLLM_ENG_CASE(16)
-#undef SLLM_ENG_CASE
-        default: break;
+// an op whose width this instantiation does not carry: keep the ring moving
+// and flag the program (the host never builds such a program)
+__device__ __forceinline__ void eng_skip_op(uint32_t& k, int& o, int& r, int& n, bool& have, ChunkWalk& walk,
+                                            EngSmem& es, const EngParams& P, int lane) {
+    const int cur = o;
+    if (lane == 0) atomicExch(P.error, ENG_BAD_PROGRAM);
+    while (true) {
+        consumer_wait_full(es, P, (int)(k % kEngSlots), k / kEngSlots);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&es.empty[k % kEngSlots]);
+        ++k;
+        have = walk.next(o, r, n);
+        if (!have || o != cur) return;
     }
 }
 
 // ---------------------------------------------------------------------------
-// the kernel
+// the kernel: WA, WB are the two row widths (in 32-bit words per lane) of a
+// model's programs -- n_embd (every projection but down) and n_ff (down)
 // ---------------------------------------------------------------------------
+template <int WA, int WB>
 __global__ void __launch_bounds__(kEngThreads, 1)
 i2s_engine_kernel(const EngParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -422,10 +521,10 @@ i2s_engine_kernel(const EngParams P) {
 
     // ---------------- consumers ----------------
     uint32_t k = 0;
+    int o = 0, r = 0, n = 0;
+    bool have = false;
     int cur_group = -1;
     sllm_cuda_act act{0.0f, 0};
-    int cur_op = -1;
-    float post = 0.0f, post2 = 0.0f;
     for (int s = 0; s < P.n_stages; ++s) {
         if (s > 0) {
             // the stage's input is the previous stage's output from every CTA
@@ -446,37 +545,27 @@ i2s_engine_kernel(const EngParams P) {
             }
             consumer_sync();
             cur_group = -1;
-            cur_op = -1;
         }
         ChunkWalk walk{s_ops, s_cur[2 * s].op, s_cur[2 * s].row, s_cur[2 * s + 1]};
-        int o, r, n;
-        while (walk.next(o, r, n)) {
+        have = walk.next(o, r, n);
+        while (have) {
             const EngOp& op = s_ops[o];
             if (op.group != cur_group) {
                 act = eng_prologue(s_groups[op.group], P, qs, es, tid, warp, lane);
                 cur_group = op.group;
-                cur_op = -1;
             }
-            if (o != cur_op) {
-                // per-tensor scales (src/quant.c:102-106), one division per tensor
-                post = __fdiv_rn(op.ws, act.scale);
-                post2 = op.epi == EPI_SILU ? __fdiv_rn(op.ws2, act.scale) : 0.0f;
-                cur_op = o;
-            }
-            const int slot = (int)(k % kEngSlots);
-            const uint32_t use = k / kEngSlots;
-            bool have = !*(volatile int*)&es.abort_flag;
-            if (have && !mbar_wait(&es.full[slot], use & 1)) {
-                es.abort_flag = 1;
-                atomicExch(P.error, ENG_TIMEOUT_FULL);
-                have = false;
-            }
-            if (have)
-                eng_chunk_dispatch(op, r, n, ring + (size_t)slot * kEngSlotBytes, qs, act.sum, post, post2, warp,
-                                   lane);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&es.empty[slot]);
-            ++k;
+            // per-tensor scales (src/quant.c:102-106): one division per tensor
+            const float post = __fdiv_rn(op.ws, act.scale);
+            const float post2 = op.epi == EPI_SILU ? __fdiv_rn(op.ws2, act.scale) : 0.0f;
+            const int wpl = ((op.K >> 4) + 31) >> 5;
+            if (wpl == WA && op.epi == EPI_SILU)
+                eng_run_op<WA, true>(op, k, o, r, n, have, walk, ring, es, qs, act.sum, post, post2, P, warp, lane);
+            else if (wpl == WA)
+                eng_run_op<WA, false>(op, k, o, r, n, have, walk, ring, es, qs, act.sum, post, post2, P, warp, lane);
+            else if (wpl == WB && op.epi != EPI_SILU)
+                eng_run_op<WB, false>(op, k, o, r, n, have, walk, ring, es, qs, act.sum, post, post2, P, warp, lane);
+            else
+                eng_skip_op(k, o, r, n, have, walk, es, P, lane);
         }
         // publish this CTA's outputs of the stage, then arrive
         consumer_sync();
@@ -484,16 +573,21 @@ i2s_engine_kernel(const EngParams P) {
     }
 }
 
+// the (WA, WB) pairs compiled in: the 2B-4T model and the widths the tests use
+#define SLLM_ENGINE_SHAPES(X) \
+    X(5, 14) X(1, 1) X(1, 2) X(1, 3) X(2, 6) X(3, 6) X(16, 16) X(16, 14) X(16, 7)
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 int engine_chunk_rows(int K, int epi) {
-    // as many rows as fill a slot, in whole rounds of the consumer warps
-    const int rb = (K / 4) * (epi == EPI_SILU ? 2 : 1);
-    int rows = kEngSlotBytes / rb;
-    if (rows > 4 * kEngConsumerWarps) rows = 4 * kEngConsumerWarps;
-    if (rows >= kEngConsumerWarps) rows -= rows % kEngConsumerWarps;
-    return rows < 1 ? 1 : rows;
+    // whole rounds of the consumer warps (each warp takes R rows), within a slot
+    const bool pair = epi == EPI_SILU;
+    const int wpl = ((K / 16) + 31) / 32;
+    const int rb = (K / 4) * (pair ? 2 : 1);
+    int rows = kEngConsumerWarps * eng_rows_per_warp(wpl, pair);
+    while (rows > 1 && rows * rb > kEngSlotBytes) --rows;   // only very wide pairs
+    return rows;
 }
 
 int engine_smem_bytes(int n_groups, int n_ops, int n_stages) {
@@ -509,13 +603,27 @@ int engine_grid(int device) {
     return sms;
 }
 
-cudaError_t prepare_engine() {
-    // the largest dynamic shared memory any program may ask for
-    return cudaFuncSetAttribute(i2s_engine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                227 * 1024 - (int)sizeof(EngSmem) - 64);
+int engine_wpl(int K) { return ((K / 16) + 31) / 32; }
+
+bool engine_supports(int wa, int wb) {
+#define SLLM_ENG_SUP(A, B) if (wa == A && wb == B) return true;
+    SLLM_ENGINE_SHAPES(SLLM_ENG_SUP)
+#undef SLLM_ENG_SUP
+    return false;
 }
 
-cudaError_t launch_engine(const EngParams& p, int grid, cudaStream_t st) {
+cudaError_t prepare_engine() {
+    // the largest dynamic shared memory any program may ask for
+    const int bytes = 227 * 1024 - (int)sizeof(EngSmem) - 64;
+    cudaError_t e = cudaSuccess;
+#define SLLM_ENG_PREP(A, B) \
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(i2s_engine_kernel<A, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    SLLM_ENGINE_SHAPES(SLLM_ENG_PREP)
+#undef SLLM_ENG_PREP
+    return e;
+}
+
+cudaError_t launch_engine(const EngParams& p, int grid, cudaStream_t st, int wa, int wb) {
     const int smem = engine_smem_bytes(p.n_groups, p.n_ops, p.n_stages);
     if (smem == 0) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
@@ -528,7 +636,11 @@ cudaError_t launch_engine(const EngParams& p, int grid, cudaStream_t st) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, i2s_engine_kernel, p);
+#define SLLM_ENG_LAUNCH(A, B) \
+    if (wa == A && wb == B) return cudaLaunchKernelEx(&cfg, i2s_engine_kernel<A, B>, p);
+    SLLM_ENGINE_SHAPES(SLLM_ENG_LAUNCH)
+#undef SLLM_ENG_LAUNCH
+    return cudaErrorNotSupported;
 }
 
 }  // namespace sllm

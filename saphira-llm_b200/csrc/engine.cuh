@@ -66,7 +66,7 @@ struct EngParams {
     int force_fallback;
 };
 
-enum EngError { ENG_OK = 0, ENG_TIMEOUT_FULL = 1, ENG_TIMEOUT_EMPTY = 2, ENG_TIMEOUT_GRID = 3 };
+enum EngError { ENG_OK = 0, ENG_TIMEOUT_FULL = 1, ENG_TIMEOUT_EMPTY = 2, ENG_TIMEOUT_GRID = 3, ENG_BAD_PROGRAM = 4 };
 
 // rows of an op per slot, so that a chunk fills at most one slot
 int engine_chunk_rows(int K, int epi);
@@ -74,7 +74,11 @@ int engine_chunk_rows(int K, int epi);
 // group / op / cursor tables every CTA copies in at start (0 when too large)
 int engine_smem_bytes(int n_groups, int n_ops, int n_stages);
 int engine_grid(int device);
+// the engine is compiled for pairs (wpl(n_embd), wpl(n_ff)) of row widths,
+// wpl(K) = 32-bit words per lane = ceil(K / 512)
+int engine_wpl(int K);
+bool engine_supports(int wa, int wb);
 cudaError_t prepare_engine();     // once, outside any stream capture
-cudaError_t launch_engine(const EngParams& p, int grid, cudaStream_t st);
+cudaError_t launch_engine(const EngParams& p, int grid, cudaStream_t st, int wa, int wb);
 
 }  // namespace sllm

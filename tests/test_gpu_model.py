@@ -173,10 +173,12 @@ def test_layer_projections_match_oracle(cuda, orc, synth):
     dict(n_layer=2, n_embd=256, n_ff=512, n_head=2, n_head_kv=1, n_vocab=64),
     dict(n_layer=2, n_embd=1152, n_ff=3072, n_head=9, n_head_kv=3, n_vocab=64),
     dict(n_layer=1, n_embd=8192, n_ff=8192, n_head=64, n_head_kv=8, n_vocab=64),
+    dict(n_layer=2, n_embd=640, n_ff=1280, n_head=5, n_head_kv=5, n_vocab=64),   # widths (2, 3): fallback path
 ])
 def test_engine_shapes_chain_and_projections(cuda, orc, synth, cfg_kw):
     """The persistent engine on widths the 2B model does not use (K = 256 to
-    8192, odd head counts), for the dependent chain and the projections."""
+    8192, odd head counts), for the dependent chain and the projections, and
+    the per-GEMV fallback for a width pair the engine is not compiled for."""
     cfg = synth.small_config(**cfg_kw)
     m = synth.SynthModel(cfg, seed=17)
     model = cuda.Model(m.desc())
