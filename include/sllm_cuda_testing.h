@@ -24,6 +24,14 @@ SLLM_CUDA_API void sllm_cuda_test_set_force_fallback(int on);
 /* How many times a fallback ran in this process (or -1 without a device). */
 SLLM_CUDA_API int sllm_cuda_test_fallback_count(void);
 
+/*
+ * How many kernels this library has put on streams in this process: each
+ * launch of one of its CUDA graphs adds the graph's kernel nodes, each direct
+ * kernel launch adds one. Kernels enqueued while the caller is capturing a
+ * stream count when enqueued, not when the caller's graph runs.
+ */
+SLLM_CUDA_API long long sllm_cuda_test_kernel_launches(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -66,6 +66,7 @@ def lib():
     L.sllm_cuda_layer_projections_device.argtypes = [vp, vp, i32, i32, vp, vp, vp]
     L.sllm_cuda_test_set_force_fallback.argtypes = [C.c_int]
     L.sllm_cuda_test_fallback_count.restype = C.c_int
+    L.sllm_cuda_test_kernel_launches.restype = C.c_longlong
     _lib = L
     return L
 
@@ -122,6 +123,12 @@ def set_force_fallback(on):
 
 def fallback_count():
     return lib().sllm_cuda_test_fallback_count()
+
+
+def kernel_launches():
+    """Kernels the library has put on streams in this process (graph launches
+    count their kernel nodes)."""
+    return lib().sllm_cuda_test_kernel_launches()
 
 
 # model level (host pointers) -------------------------------------------------

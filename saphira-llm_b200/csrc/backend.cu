@@ -7,12 +7,14 @@
 // feedback live in device memory, so a whole prompt + generation is a run of
 // graph launches with no host round trip until the ids are copied back.
 
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "common.cuh"
@@ -31,6 +33,13 @@ static thread_local std::string g_last_error;
 static int g_force_fallback = 0;
 static float g_engine_eps = 0.0f;          // set just before an engine program is captured
 static int* g_fallback_counter = nullptr;   // device int, lazily allocated per process
+
+// Kernels this library has put on a stream, for the benchmark's launch count:
+// a graph adds its kernel nodes each time it is launched, a direct launch
+// adds one.
+static std::atomic<long long> g_kernel_launches{0};
+static std::mutex g_graph_mu;
+static std::unordered_map<cudaGraphExec_t, int> g_graph_kernels;
 
 static int fail(int status, const char* fmt, ...) {
     char buf[512];
@@ -114,6 +123,48 @@ extern "C" int sllm_cuda_probe(int* n_devices, int* cc_major, int* cc_minor) {
 
 // Allocated on first use OUTSIDE any stream capture (ctx_new and the chain
 // entry points call it before capturing); a graph then bakes the pointer in.
+// instantiate a captured graph, remembering how many kernel nodes it holds
+static cudaError_t instantiate(cudaGraphExec_t* exec, cudaGraph_t g) {
+    size_t n = 0;
+    cudaError_t e = cudaGraphGetNodes(g, nullptr, &n);
+    std::vector<cudaGraphNode_t> nodes(n);
+    if (e == cudaSuccess && n > 0) e = cudaGraphGetNodes(g, nodes.data(), &n);
+    int kernels = 0;
+    for (size_t i = 0; e == cudaSuccess && i < n; ++i) {
+        cudaGraphNodeType t;
+        e = cudaGraphNodeGetType(nodes[i], &t);
+        if (e == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+    }
+    if (e != cudaSuccess) return e;
+    e = cudaGraphInstantiate(exec, g, 0);
+    if (e == cudaSuccess) {
+        std::lock_guard<std::mutex> lk(g_graph_mu);
+        g_graph_kernels[*exec] = kernels;
+    }
+    return e;
+}
+
+static void graph_exec_destroy(cudaGraphExec_t exec) {
+    if (exec == nullptr) return;
+    {
+        std::lock_guard<std::mutex> lk(g_graph_mu);
+        g_graph_kernels.erase(exec);
+    }
+    cudaGraphExecDestroy(exec);
+}
+
+static cudaError_t graph_launch(cudaGraphExec_t exec, cudaStream_t st) {
+    const cudaError_t e = cudaGraphLaunch(exec, st);
+    if (e == cudaSuccess) {
+        std::lock_guard<std::mutex> lk(g_graph_mu);
+        auto it = g_graph_kernels.find(exec);
+        if (it != g_graph_kernels.end()) g_kernel_launches += it->second;
+    }
+    return e;
+}
+
+extern "C" long long sllm_cuda_test_kernel_launches(void) { return g_kernel_launches.load(); }
+
 static int* fallback_counter() {
     if (g_fallback_counter == nullptr) {
         if (cudaMalloc(&g_fallback_counter, sizeof(int)) != cudaSuccess) { g_fallback_counter = nullptr; return nullptr; }
@@ -142,6 +193,7 @@ extern "C" int sllm_cuda_i2s_quant_act(const float* x, size_t n, int8_t* q_out, 
     if (x == nullptr || q_out == nullptr || act_out == nullptr || n == 0 || n > (size_t)kMaxK)
         return fail(SLLM_CUDA_ERR_ARG, "quant_act: bad arguments (n=%zu)", n);
     CK(launch_quant_act(x, (int)n, q_out, act_out, (cudaStream_t)stream), "quant_act launch");
+    ++g_kernel_launches;
     return SLLM_CUDA_OK;
 }
 
@@ -172,6 +224,7 @@ extern "C" int sllm_cuda_i2s_gemv(const uint8_t* w, size_t n_rows, size_t n, con
     p.q_in = q;
     p.act_in = zero_act;
     CK(launch_gemv(p, PRO_Q8, EPI_DOTS, current_sms(), (cudaStream_t)stream), "gemv launch");
+    ++g_kernel_launches;
     return SLLM_CUDA_OK;
 }
 
@@ -186,6 +239,7 @@ extern "C" int sllm_cuda_i2s_gemv_f32(const uint8_t* w, size_t n_rows, size_t n,
     p.seg[0] = GemvSeg{w, (int)n_rows, y, dots};
     p.x = x;
     CK(launch_gemv(p, PRO_QUANT, EPI_F32, current_sms(), (cudaStream_t)stream), "gemv_f32 launch");
+    ++g_kernel_launches;
     return SLLM_CUDA_OK;
 }
 
@@ -336,7 +390,7 @@ struct EngineProgram {
 };
 
 static void engine_program_free(EngineProgram& p) {
-    if (p.exec) cudaGraphExecDestroy(p.exec);
+    graph_exec_destroy(p.exec);
     cudaFree(p.groups); cudaFree(p.ops); cudaFree(p.starts); cudaFree(p.barrier); cudaFree(p.error);
     p = EngineProgram();
 }
@@ -409,7 +463,7 @@ static int engine_program_build(EngineProgram& p, const std::vector<EngGroup>& g
     cudaError_t e2 = cudaStreamEndCapture(capture_stream, &g);
     if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); engine_program_free(p); return cuda_fail(e, "capture engine"); }
     if (e2 != cudaSuccess) { engine_program_free(p); return cuda_fail(e2, "end capture"); }
-    e = cudaGraphInstantiate(&p.exec, g, 0);
+    e = instantiate(&p.exec, g);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) { p.exec = nullptr; engine_program_free(p); return cuda_fail(e, "instantiate engine"); }
     return SLLM_CUDA_OK;
@@ -475,9 +529,9 @@ static void rope_table(int n_ctx, int n_rot, float base, std::vector<float>& cs,
 extern "C" void sllm_cuda_ctx_free(sllm_cuda_ctx* c) {
     if (c == nullptr) return;
     cudaSetDevice(c->m->device);
-    if (c->step) cudaGraphExecDestroy(c->step);
-    if (c->chain) cudaGraphExecDestroy(c->chain);
-    if (c->proj) cudaGraphExecDestroy(c->proj);
+    graph_exec_destroy(c->step);
+    graph_exec_destroy(c->chain);
+    graph_exec_destroy(c->proj);
     if (c->stream) cudaStreamDestroy(c->stream);
     cudaFree(c->k_cache); cudaFree(c->v_cache); cudaFree(c->rope_cos); cudaFree(c->rope_sin);
     cudaFree(c->x); cudaFree(c->q); cudaFree(c->k); cudaFree(c->v); cudaFree(c->attn);
@@ -634,7 +688,7 @@ static int ensure_step_graph(sllm_cuda_ctx* c) {
     cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
     if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); return cuda_fail(e, "capture decode step"); }
     if (e2 != cudaSuccess) return cuda_fail(e2, "end capture");
-    e = cudaGraphInstantiate(&c->step, g, 0);
+    e = instantiate(&c->step, g);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) { c->step = nullptr; return cuda_fail(e, "instantiate decode step"); }
     return SLLM_CUDA_OK;
@@ -650,7 +704,7 @@ static int run_steps(sllm_cuda_ctx* c, int base, int n, int prompt_end, float* c
     CK(cudaMemcpyAsync(c->prompt_end, &c->pinned[1], 4, cudaMemcpyHostToDevice, c->stream), "set prompt end");
     const size_t V = c->m->n_vocab;
     for (int t = 0; t < n; ++t) {
-        CK(cudaGraphLaunch(c->step, c->stream), "decode step");
+        CK(graph_launch(c->step, c->stream), "decode step");
         if (chunk_logits_dev != nullptr)
             CK(cudaMemcpyAsync(chunk_logits_dev + (size_t)t * V, c->logits, V * 4, cudaMemcpyDeviceToDevice, c->stream),
                "copy logits");
@@ -796,7 +850,7 @@ extern "C" int sllm_cuda_layer_chain_device(const sllm_cuda_model* m, sllm_cuda_
         // widths the engine is not compiled for: one fused GEMV launch per
         // projection, programmatically chained, captured as a graph
         if (c->chain == nullptr || c->chain_begin != layer_begin || c->chain_n != n_layers || c->chain_x != x) {
-            if (c->chain) { cudaGraphExecDestroy(c->chain); c->chain = nullptr; }
+            graph_exec_destroy(c->chain); c->chain = nullptr;
             ChainBufs b{x, c->q, c->k, c->v, c->ffn_inp, c->h, nullptr};
             cudaGraph_t g = nullptr;
             CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
@@ -806,12 +860,12 @@ extern "C" int sllm_cuda_layer_chain_device(const sllm_cuda_model* m, sllm_cuda_
             cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
             if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); return cuda_fail(e, "capture layer chain"); }
             if (e2 != cudaSuccess) return cuda_fail(e2, "end capture");
-            e = cudaGraphInstantiate(&c->chain, g, 0);
+            e = instantiate(&c->chain, g);
             cudaGraphDestroy(g);
             if (e != cudaSuccess) { c->chain = nullptr; return cuda_fail(e, "instantiate layer chain"); }
             c->chain_begin = layer_begin; c->chain_n = n_layers; c->chain_x = x;
         }
-        CK(cudaGraphLaunch(c->chain, (cudaStream_t)stream), "layer chain");
+        CK(graph_launch(c->chain, (cudaStream_t)stream), "layer chain");
         return SLLM_CUDA_OK;
     }
     EngineProgram& p = c->eng_chain;
@@ -820,7 +874,7 @@ extern "C" int sllm_cuda_layer_chain_device(const sllm_cuda_model* m, sllm_cuda_
         if (rc != SLLM_CUDA_OK) return rc;
         p.key_begin = layer_begin; p.key_n = n_layers; p.key_x = x;
     }
-    CK(cudaGraphLaunch(p.exec, (cudaStream_t)stream), "layer chain");
+    CK(graph_launch(p.exec, (cudaStream_t)stream), "layer chain");
     return SLLM_CUDA_OK;
 }
 
@@ -933,7 +987,7 @@ extern "C" int sllm_cuda_layer_projections_device(const sllm_cuda_model* m, sllm
         sllm_cuda_layer_projections_sizes(m, &ystride);
         if (c->proj == nullptr || c->proj_begin != layer_begin || c->proj_n != n_layers || c->proj_x != x ||
             c->proj_y != y) {
-            if (c->proj) { cudaGraphExecDestroy(c->proj); c->proj = nullptr; }
+            graph_exec_destroy(c->proj); c->proj = nullptr;
             cudaGraph_t g = nullptr;
             CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
             cudaError_t e = cudaSuccess;
@@ -942,12 +996,12 @@ extern "C" int sllm_cuda_layer_projections_device(const sllm_cuda_model* m, sllm
             cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
             if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); return cuda_fail(e, "capture projections"); }
             if (e2 != cudaSuccess) return cuda_fail(e2, "end capture");
-            e = cudaGraphInstantiate(&c->proj, g, 0);
+            e = instantiate(&c->proj, g);
             cudaGraphDestroy(g);
             if (e != cudaSuccess) { c->proj = nullptr; return cuda_fail(e, "instantiate projections"); }
             c->proj_begin = layer_begin; c->proj_n = n_layers; c->proj_x = x; c->proj_y = y;
         }
-        CK(cudaGraphLaunch(c->proj, (cudaStream_t)stream), "projections");
+        CK(graph_launch(c->proj, (cudaStream_t)stream), "projections");
         return SLLM_CUDA_OK;
     }
     EngineProgram& p = c->eng_proj;
@@ -956,7 +1010,7 @@ extern "C" int sllm_cuda_layer_projections_device(const sllm_cuda_model* m, sllm
         if (rc != SLLM_CUDA_OK) return rc;
         p.key_begin = layer_begin; p.key_n = n_layers; p.key_x = x; p.key_y = y;
     }
-    CK(cudaGraphLaunch(p.exec, (cudaStream_t)stream), "projections");
+    CK(graph_launch(p.exec, (cudaStream_t)stream), "projections");
     return SLLM_CUDA_OK;
 }
 
@@ -1050,5 +1104,6 @@ extern "C" int sllm_cuda_layer_chain_device_noalloc(const sllm_cuda_model* m, in
     ChainBufs b{x, s, s + E, s + E + G, s + E + 2 * G, s + 2 * E + 2 * G, nullptr};
     for (int l = layer_begin; l < layer_begin + n_layers; ++l)
         CK(launch_layer(m, l, b, nullptr, 0, (cudaStream_t)stream, false, nullptr), "layer_chain_noalloc");
+        g_kernel_launches += 4;
     return SLLM_CUDA_OK;
 }

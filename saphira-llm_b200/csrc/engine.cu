@@ -300,26 +300,30 @@ __device__ __forceinline__ bool consumer_wait_full(EngSmem& es, const EngParams&
     return false;
 }
 
-// R rows per warp of a plain (one-tensor) chunk. PRED guards the chunk's
-// last rows and a row width that is not a whole number of warp words.
-template <int WPL, int R, bool PRED>
-__device__ __forceinline__ void plain_rows(const int4 (&aq)[WPL], const uint8_t* base, int n, int rb, int W,
-                                           int warp, int lane, int (&dot)[R]) {
+// R rows per warp of a plain (one-tensor) chunk, branch-free. A warp whose
+// row lies past the chunk's end (a short last chunk) recomputes the chunk's
+// last row and never stores it; a lane whose last word lies past a partial
+// row width reads the bytes after the row (inside the slot: the host leaves
+// that margin, see engine_chunk_rows) and masks them to zero codes. So no
+// predicate sits in the loop.
+template <int WPL, int R>
+__device__ __forceinline__ void plain_rows(const int4 (&aq)[WPL], const uint8_t* base, int n, int rb,
+                                           bool last_full, int warp, int lane, int (&dot)[R]) {
     int acc[R][4];
     #pragma unroll
     for (int t = 0; t < R; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
     const uint32_t* rp[R];
     #pragma unroll
     for (int t = 0; t < R; ++t)
-        rp[t] = reinterpret_cast<const uint32_t*>(base + (size_t)(warp + kEngConsumerWarps * t) * rb) + lane;
+        rp[t] = reinterpret_cast<const uint32_t*>(base + (size_t)min(warp + kEngConsumerWarps * t, n - 1) * rb) + lane;
+    const uint32_t last_mask = last_full ? 0xffffffffu : 0u;
     #pragma unroll
     for (int i = 0; i < WPL; ++i) {
         #pragma unroll
         for (int t = 0; t < R; ++t) {
-            if (!PRED || (lane + 32 * i < W && warp + kEngConsumerWarps * t < n)) {
-                const uint32_t w = rp[t][32 * i];
-                i2s_word_fields(w, aq[i], acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
-            }
+            uint32_t w = rp[t][32 * i];
+            if (i == WPL - 1) w &= last_mask;
+            i2s_word_fields(w, aq[i], acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
         }
     }
     #pragma unroll
@@ -327,21 +331,22 @@ __device__ __forceinline__ void plain_rows(const int4 (&aq)[WPL], const uint8_t*
         dot[t] = __reduce_add_sync(0xffffffffu, fields_total(acc[t][0], acc[t][1], acc[t][2], acc[t][3]));
 }
 
-template <int WPL, int R, bool PRED>
-__device__ __forceinline__ void pair_rows(const int4 (&aq)[WPL], const uint8_t* base, int n, int rb, int W,
+template <int WPL, int R>
+__device__ __forceinline__ void pair_rows(const int4 (&aq)[WPL], const uint8_t* base, int n, int rb, bool last_full,
                                           int warp, int lane, int (&dg)[R], int (&du)[R]) {
+    const uint32_t last_mask = last_full ? 0xffffffffu : 0u;
     #pragma unroll
     for (int t = 0; t < R; ++t) {
-        const int j = warp + kEngConsumerWarps * t;
+        const int j = min(warp + kEngConsumerWarps * t, n - 1);
         int g0 = 0, g1 = 0, g2 = 0, g3 = 0, u0 = 0, u1 = 0, u2 = 0, u3 = 0;
         const uint32_t* rg = reinterpret_cast<const uint32_t*>(base + (size_t)j * rb) + lane;
         const uint32_t* ru = reinterpret_cast<const uint32_t*>(base + (size_t)(n + j) * rb) + lane;
         #pragma unroll
         for (int i = 0; i < WPL; ++i) {
-            if (!PRED || (lane + 32 * i < W && j < n)) {
-                i2s_word_fields(rg[32 * i], aq[i], g0, g1, g2, g3);
-                i2s_word_fields(ru[32 * i], aq[i], u0, u1, u2, u3);
-            }
+            uint32_t wg = rg[32 * i], wu = ru[32 * i];
+            if (i == WPL - 1) { wg &= last_mask; wu &= last_mask; }
+            i2s_word_fields(wg, aq[i], g0, g1, g2, g3);
+            i2s_word_fields(wu, aq[i], u0, u1, u2, u3);
         }
         dg[t] = __reduce_add_sync(0xffffffffu, fields_total(g0, g1, g2, g3));
         du[t] = __reduce_add_sync(0xffffffffu, fields_total(u0, u1, u2, u3));
@@ -359,7 +364,7 @@ __device__ __forceinline__ void eng_run_op(const EngOp& op, uint32_t& k, int& o,
     constexpr int R = eng_rows_per_warp(WPL, PAIR);
     const int K = op.K, W = K >> 4, rb = K >> 2;
     const int cur = o;
-    const bool full_width = (W == 32 * WPL);
+    const bool last_full = lane + 32 * (WPL - 1) < W;     // this lane's last word lies in the row
     int4 aq[WPL];
     #pragma unroll
     for (int i = 0; i < WPL; ++i) {
@@ -370,11 +375,9 @@ __device__ __forceinline__ void eng_run_op(const EngOp& op, uint32_t& k, int& o,
         const int slot = (int)(k % kEngSlots);
         if (consumer_wait_full(es, P, slot, k / kEngSlots)) {
             const uint8_t* base = ring + (size_t)slot * kEngSlotBytes;
-            const bool fast = full_width && n == kEngConsumerWarps * R;
             if (PAIR) {
                 int dg[R], du[R];
-                if (fast) pair_rows<WPL, R, false>(aq, base, n, rb, W, warp, lane, dg, du);
-                else pair_rows<WPL, R, true>(aq, base, n, rb, W, warp, lane, dg, du);
+                pair_rows<WPL, R>(aq, base, n, rb, last_full, warp, lane, dg, du);
                 // h = silu(gate) * up (src/forward.c:765-778, src/ops.c:452-456)
                 #pragma unroll
                 for (int t = 0; t < R; ++t) {
@@ -387,8 +390,7 @@ __device__ __forceinline__ void eng_run_op(const EngOp& op, uint32_t& k, int& o,
                 }
             } else {
                 int dot[R];
-                if (fast) plain_rows<WPL, R, false>(aq, base, n, rb, W, warp, lane, dot);
-                else plain_rows<WPL, R, true>(aq, base, n, rb, W, warp, lane, dot);
+                plain_rows<WPL, R>(aq, base, n, rb, last_full, warp, lane, dot);
                 int mine = dot[0];
                 #pragma unroll
                 for (int t = 1; t < R; ++t)
@@ -581,12 +583,16 @@ i2s_engine_kernel(const EngParams P) {
 // host side
 // ---------------------------------------------------------------------------
 int engine_chunk_rows(int K, int epi) {
-    // whole rounds of the consumer warps (each warp takes R rows), within a slot
+    // Whole rounds of the consumer warps (each warp computes R rows) when they
+    // fit a slot; fewer rows for very wide gate/up pairs. A lane's last word
+    // may lie past a partial row's end (rows are read as whole warp words):
+    // those bytes must still lie in the slot, so they count here.
     const bool pair = epi == EPI_SILU;
     const int wpl = ((K / 16) + 31) / 32;
-    const int rb = (K / 4) * (pair ? 2 : 1);
+    const size_t rb = (size_t)(K / 4) * (pair ? 2 : 1);
+    const size_t overhang = (size_t)wpl * 128 - (size_t)(K / 4);
     int rows = kEngConsumerWarps * eng_rows_per_warp(wpl, pair);
-    while (rows > 1 && rows * rb > kEngSlotBytes) --rows;   // only very wide pairs
+    while (rows > 1 && rows * rb + overhang > (size_t)kEngSlotBytes) --rows;
     return rows;
 }
 
