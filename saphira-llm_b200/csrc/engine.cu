@@ -1,16 +1,17 @@
 // engine.cu -- the persistent I2_S GEMV engine for sm_100a (see engine.cuh).
 //
-// Per CTA (one per SM, 17 warps):
-//   warp 16 (producer): walks the CTA's chunks of every stage in program
+// Per CTA (one per SM, 16 warps):
+//   warp 15 (producer): walks the CTA's chunks of every stage in program
 //     order and, for each, waits for a free ring slot and issues one TMA bulk
 //     copy (two for a gate/up pair) of the chunk's contiguous weight rows into
 //     it, with the slot's mbarrier counting the bytes. It never waits for
 //     activations, so weights stream ahead across op and stage boundaries.
-//   warps 0-15 (consumers): for each chunk, (re)build the int8 activations
-//     of the chunk's input group when it changes (the certified RMSNorm +
-//     absmax prologue of i2s_gemv.cu, shared by the 512 consumer threads),
-//     wait for the slot, run the dp4a dots from shared memory, apply the
-//     epilogue and release the slot.
+//   warps 0-14 (consumers): for each op, (re)build the int8 activations of
+//     the op's input group when it changes (the certified RMSNorm + absmax
+//     prologue of i2s_gemv.cu, shared by the 480 consumer threads), load them
+//     into registers, then for each chunk wait for its slot, run the dp4a
+//     dots from shared memory (R rows per warp), apply the epilogue and
+//     release the slot.
 //   At a stage boundary the consumers publish their outputs and meet every
 //     other CTA at a grid barrier before reading the next stage's input.
 //
@@ -286,29 +287,56 @@ __device__ sllm_cuda_act eng_prologue(const EngGroup& g, const EngParams& P, int
 // ---------------------------------------------------------------------------
 // consumers: every chunk of one op, activations held in registers
 // ---------------------------------------------------------------------------
-// rows per consumer warp per chunk: the chunk fills most of a 32 KB slot
+// Rows per consumer warp per chunk: as many as a slot holds for the widest
+// rows of that width (K = 512 * wpl), at most 8; two for widths 13 and 14
+// (n_ff = 6912 has 1728-byte rows: 28 of the 30 fit a slot, the host gives
+// the chunk 28 rows and two warps recompute a row they do not store).
 __host__ __device__ constexpr int eng_rows_per_warp(int wpl, bool pair) {
-    return pair ? (wpl <= 2 ? 4 : (wpl <= 4 ? 2 : 1))
-                : (wpl <= 4 ? 4 : (wpl == 5 ? 3 : (wpl <= 8 ? 2 : 1)));
+    return pair ? (kEngSlotBytes / (2 * kEngConsumerWarps * 128 * wpl) >= 8
+                       ? 8
+                       : (kEngSlotBytes / (2 * kEngConsumerWarps * 128 * wpl) < 1
+                              ? 1
+                              : kEngSlotBytes / (2 * kEngConsumerWarps * 128 * wpl)))
+                : (wpl == 13 || wpl == 14
+                       ? 2
+                       : (kEngSlotBytes / (kEngConsumerWarps * 128 * wpl) >= 8
+                              ? 8
+                              : (kEngSlotBytes / (kEngConsumerWarps * 128 * wpl) < 1
+                                     ? 1
+                                     : kEngSlotBytes / (kEngConsumerWarps * 128 * wpl))));
 }
 
-__device__ __forceinline__ bool consumer_wait_full(EngSmem& es, const EngParams& P, int slot, uint32_t use) {
+// the slow path of a consumer's wait for a full slot: bounded, and quick to
+// give up once the CTA is aborting
+__device__ __noinline__ bool consumer_wait_full_slow(EngSmem& es, const EngParams& P, uint64_t* bar,
+                                                     uint32_t parity) {
     if (*(volatile int*)&es.abort_flag) return false;
-    if (mbar_wait(&es.full[slot], use & 1)) return true;
-    es.abort_flag = 1;
-    atomicExch(P.error, ENG_TIMEOUT_FULL);
-    return false;
+    const uint64_t t0 = gtimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*(volatile int*)&es.abort_flag) return false;
+        if (gtimer() - t0 > kEngWaitNs) {
+            es.abort_flag = 1;
+            atomicExch(P.error, ENG_TIMEOUT_FULL);
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ bool consumer_wait_full(EngSmem& es, const EngParams& P, uint32_t slot, uint32_t phase) {
+    if (mbar_try_wait(&es.full[slot], phase)) return true;
+    return consumer_wait_full_slow(es, P, &es.full[slot], phase);
 }
 
 // R rows per warp of a plain (one-tensor) chunk, branch-free. A warp whose
-// row lies past the chunk's end (a short last chunk) recomputes the chunk's
-// last row and never stores it; a lane whose last word lies past a partial
-// row width reads the bytes after the row (inside the slot: the host leaves
-// that margin, see engine_chunk_rows) and masks them to zero codes. So no
+// row lies past the chunk's end (a short chunk) recomputes the chunk's last
+// row and never stores it; a lane whose last word lies past a partial row
+// width reads the bytes after the row (inside the slot: the host leaves that
+// margin, see engine_chunk_rows) and masks them to zero codes. So no
 // predicate sits in the loop.
 template <int WPL, int R>
 __device__ __forceinline__ void plain_rows(const int4 (&aq)[WPL], const uint8_t* base, int n, int rb,
-                                           bool last_full, int warp, int lane, int (&dot)[R]) {
+                                           uint32_t last_mask, int warp, int lane, int (&dot)[R]) {
     int acc[R][4];
     #pragma unroll
     for (int t = 0; t < R; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
@@ -316,7 +344,6 @@ __device__ __forceinline__ void plain_rows(const int4 (&aq)[WPL], const uint8_t*
     #pragma unroll
     for (int t = 0; t < R; ++t)
         rp[t] = reinterpret_cast<const uint32_t*>(base + (size_t)min(warp + kEngConsumerWarps * t, n - 1) * rb) + lane;
-    const uint32_t last_mask = last_full ? 0xffffffffu : 0u;
     #pragma unroll
     for (int i = 0; i < WPL; ++i) {
         #pragma unroll
@@ -332,9 +359,8 @@ __device__ __forceinline__ void plain_rows(const int4 (&aq)[WPL], const uint8_t*
 }
 
 template <int WPL, int R>
-__device__ __forceinline__ void pair_rows(const int4 (&aq)[WPL], const uint8_t* base, int n, int rb, bool last_full,
-                                          int warp, int lane, int (&dg)[R], int (&du)[R]) {
-    const uint32_t last_mask = last_full ? 0xffffffffu : 0u;
+__device__ __forceinline__ void pair_rows(const int4 (&aq)[WPL], const uint8_t* base, int n, int rb,
+                                          uint32_t last_mask, int warp, int lane, int (&dg)[R], int (&du)[R]) {
     #pragma unroll
     for (int t = 0; t < R; ++t) {
         const int j = min(warp + kEngConsumerWarps * t, n - 1);
@@ -353,44 +379,55 @@ __device__ __forceinline__ void pair_rows(const int4 (&aq)[WPL], const uint8_t* 
     }
 }
 
-// Every consecutive chunk of op `o`, activations loaded once into registers.
-// All walk state is passed by reference into this inlined body, so it stays
-// in registers.
+// The ring position of the consumers: chunk k sits in slot k % kEngSlots and
+// completes phase (k / kEngSlots) & 1 of that slot's barriers.
+struct RingPos {
+    uint32_t slot = 0, phase = 0;
+    __device__ __forceinline__ void advance() {
+        if (++slot == (uint32_t)kEngSlots) { slot = 0; phase ^= 1u; }
+    }
+};
+
+// Every chunk of op `o` that this CTA runs in the current stage, from row r0
+// to r_end, activations loaded once into registers. The chunks follow the
+// producer's order (ChunkWalk::next): n = min(chunk_rows, r_end - r).
 template <int WPL, bool PAIR>
-__device__ __forceinline__ void eng_run_op(const EngOp& op, uint32_t& k, int& o, int& r, int& n, bool& have,
-                                           ChunkWalk& walk, uint8_t* ring, EngSmem& es, const int8_t* qs,
-                                           int asum, float post, float post2, const EngParams& P, int warp,
-                                           int lane) {
+__device__ __forceinline__ void eng_run_op(const EngOp& op, int r0, int r_end, RingPos& rp, uint8_t* ring,
+                                           EngSmem& es, const int8_t* qs, int asum, float post, float post2,
+                                           const EngParams& P, int warp, int lane) {
     constexpr int R = eng_rows_per_warp(WPL, PAIR);
-    const int K = op.K, W = K >> 4, rb = K >> 2;
-    const int cur = o;
-    const bool last_full = lane + 32 * (WPL - 1) < W;     // this lane's last word lies in the row
+    const int K = op.K, W = K >> 4, rb = K >> 2, chunk_rows = op.chunk_rows;
+    float* const out = PAIR ? op.h : op.y;
+    const float* const resid = op.epi == EPI_RESID ? op.resid : nullptr;
+    // this lane's last word lies in the row: else it reads past the row and is masked
+    const uint32_t last_mask = lane + 32 * (WPL - 1) < W ? 0xffffffffu : 0u;
     int4 aq[WPL];
     #pragma unroll
     for (int i = 0; i < WPL; ++i) {
         const int wi = lane + 32 * i;
         aq[i] = wi < W ? reinterpret_cast<const int4*>(qs)[wi] : make_int4(0, 0, 0, 0);
     }
-    while (true) {
-        const int slot = (int)(k % kEngSlots);
-        if (consumer_wait_full(es, P, slot, k / kEngSlots)) {
-            const uint8_t* base = ring + (size_t)slot * kEngSlotBytes;
+    for (int r = r0; r < r_end;) {
+        const int n = min(chunk_rows, r_end - r);
+        if (consumer_wait_full(es, P, rp.slot, rp.phase)) {
+            const uint8_t* base = ring + (size_t)rp.slot * kEngSlotBytes;
             if (PAIR) {
                 int dg[R], du[R];
-                pair_rows<WPL, R>(aq, base, n, rb, last_full, warp, lane, dg, du);
+                pair_rows<WPL, R>(aq, base, n, rb, last_mask, warp, lane, dg, du);
                 // h = silu(gate) * up (src/forward.c:765-778, src/ops.c:452-456)
+                int mg = dg[0], mu = du[0];
                 #pragma unroll
-                for (int t = 0; t < R; ++t) {
-                    const int j = warp + kEngConsumerWarps * t;
-                    if (lane == t && j < n) {
-                        const float g = __fmul_rn(__int2float_rn(dg[t] - asum), post);
-                        const float u = __fmul_rn(__int2float_rn(du[t] - asum), post2);
-                        op.h[r + j] = __fmul_rn(silu_block(g), u);
-                    }
+                for (int t = 1; t < R; ++t)
+                    if (lane == t) { mg = dg[t]; mu = du[t]; }
+                const int j = warp + kEngConsumerWarps * lane;
+                if (lane < R && j < n) {
+                    const float g = __fmul_rn(__int2float_rn(mg - asum), post);
+                    const float u = __fmul_rn(__int2float_rn(mu - asum), post2);
+                    out[r + j] = __fmul_rn(silu_block(g), u);
                 }
             } else {
                 int dot[R];
-                plain_rows<WPL, R>(aq, base, n, rb, last_full, warp, lane, dot);
+                plain_rows<WPL, R>(aq, base, n, rb, last_mask, warp, lane, dot);
                 int mine = dot[0];
                 #pragma unroll
                 for (int t = 1; t < R; ++t)
@@ -398,32 +435,30 @@ __device__ __forceinline__ void eng_run_op(const EngOp& op, uint32_t& k, int& o,
                 const int j = warp + kEngConsumerWarps * lane;
                 if (lane < R && j < n) {
                     float v = __fmul_rn(__int2float_rn(mine - asum), post);
-                    if (op.epi == EPI_RESID) v = __fadd_rn(v, __ldcg(op.resid + r + j));
-                    op.y[r + j] = v;
+                    if (resid != nullptr) v = __fadd_rn(v, __ldcg(resid + r + j));
+                    out[r + j] = v;
                 }
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&es.empty[k % kEngSlots]);
-        ++k;
-        have = walk.next(o, r, n);
-        if (!have || o != cur) return;
+        if (lane == 0) mbar_arrive(&es.empty[rp.slot]);
+        rp.advance();
+        r += n;
     }
 }
 
 // an op whose width this instantiation does not carry: keep the ring moving
 // and flag the program (the host never builds such a program)
-__device__ __forceinline__ void eng_skip_op(uint32_t& k, int& o, int& r, int& n, bool& have, ChunkWalk& walk,
-                                            EngSmem& es, const EngParams& P, int lane) {
-    const int cur = o;
+__device__ __forceinline__ void eng_skip_op(const EngOp& op, int r0, int r_end, RingPos& rp, EngSmem& es,
+                                            const EngParams& P, int lane) {
     if (lane == 0) atomicExch(P.error, ENG_BAD_PROGRAM);
-    while (true) {
-        consumer_wait_full(es, P, (int)(k % kEngSlots), k / kEngSlots);
+    for (int r = r0; r < r_end;) {
+        const int n = min(op.chunk_rows, r_end - r);
+        consumer_wait_full(es, P, rp.slot, rp.phase);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&es.empty[k % kEngSlots]);
-        ++k;
-        have = walk.next(o, r, n);
-        if (!have || o != cur) return;
+        if (lane == 0) mbar_arrive(&es.empty[rp.slot]);
+        rp.advance();
+        r += n;
     }
 }
 
@@ -522,9 +557,7 @@ i2s_engine_kernel(const EngParams P) {
     }
 
     // ---------------- consumers ----------------
-    uint32_t k = 0;
-    int o = 0, r = 0, n = 0;
-    bool have = false;
+    RingPos rp;
     int cur_group = -1;
     sllm_cuda_act act{0.0f, 0};
     for (int s = 0; s < P.n_stages; ++s) {
@@ -549,9 +582,12 @@ i2s_engine_kernel(const EngParams P) {
             cur_group = -1;
         }
         ChunkWalk walk{s_ops, s_cur[2 * s].op, s_cur[2 * s].row, s_cur[2 * s + 1]};
-        have = walk.next(o, r, n);
-        while (have) {
+        int o, r, n;
+        while (walk.next(o, r, n)) {
             const EngOp& op = s_ops[o];
+            // this CTA's rows of op o in this stage: [r, r_end)
+            const int r_end = o == walk.end.op ? walk.end.row : op.rows;
+            walk.row = r_end;
             if (op.group != cur_group) {
                 act = eng_prologue(s_groups[op.group], P, qs, es, tid, warp, lane);
                 cur_group = op.group;
@@ -561,13 +597,13 @@ i2s_engine_kernel(const EngParams P) {
             const float post2 = op.epi == EPI_SILU ? __fdiv_rn(op.ws2, act.scale) : 0.0f;
             const int wpl = ((op.K >> 4) + 31) >> 5;
             if (wpl == WA && op.epi == EPI_SILU)
-                eng_run_op<WA, true>(op, k, o, r, n, have, walk, ring, es, qs, act.sum, post, post2, P, warp, lane);
+                eng_run_op<WA, true>(op, r, r_end, rp, ring, es, qs, act.sum, post, post2, P, warp, lane);
             else if (wpl == WA)
-                eng_run_op<WA, false>(op, k, o, r, n, have, walk, ring, es, qs, act.sum, post, post2, P, warp, lane);
+                eng_run_op<WA, false>(op, r, r_end, rp, ring, es, qs, act.sum, post, post2, P, warp, lane);
             else if (wpl == WB && op.epi != EPI_SILU)
-                eng_run_op<WB, false>(op, k, o, r, n, have, walk, ring, es, qs, act.sum, post, post2, P, warp, lane);
+                eng_run_op<WB, false>(op, r, r_end, rp, ring, es, qs, act.sum, post, post2, P, warp, lane);
             else
-                eng_skip_op(k, o, r, n, have, walk, es, P, lane);
+                eng_skip_op(op, r, r_end, rp, es, P, lane);
         }
         // publish this CTA's outputs of the stage, then arrive
         consumer_sync();

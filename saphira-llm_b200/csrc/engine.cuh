@@ -5,7 +5,7 @@
 // CTA a producer warp streams the weight rows of every chunk it will need, in
 // program order, into a ring of shared-memory slots with TMA bulk copies,
 // running ahead across op and stage boundaries (weights never depend on
-// activations); sixteen consumer warps compute from shared memory. Stages are
+// activations); fifteen consumer warps compute from shared memory. Stages are
 // separated by a grid barrier, because a stage's input vector is the whole
 // output of the stage before.
 #pragma once
@@ -19,8 +19,8 @@ namespace sllm {
 
 constexpr int kEngConsumerWarps = 15;    // + 1 producer: 16 warps, 4 per SM sub-partition
 constexpr int kEngThreads = (kEngConsumerWarps + 1) * 32;
-constexpr int kEngSlotBytes = 32 * 1024;
-constexpr int kEngSlots = 5;
+constexpr int kEngSlotBytes = 48 * 1024;   // a slot holds one chunk: whole weight rows of one op
+constexpr int kEngSlots = 4;
 
 // an input vector and how each CTA turns it into int8 activations
 struct EngGroup {
