@@ -403,7 +403,7 @@ def main():
     per_launch_bytes = step_bytes / launches
     achieved = per_launch_bytes / ((ms / 1e3) / (args.steps * launches)) / 1e9
     traffic = None
-    prof = os.path.join(ROOT, "profiles", "i2s_gemv_projections_traffic.txt")
+    prof = os.path.join(ROOT, "profiles", "i2s_engine_projections_traffic.txt")
     if os.path.exists(prof):
         for line in open(prof):
             if line.startswith("traffic_bytes_per_launch"):
