@@ -112,6 +112,44 @@ SLLM_CUDA_API int sllm_cuda_i2s_gemv_f32(const uint8_t * w, size_t n_rows, size_
                            void * stream);
 
 /* ------------------------------------------------------------------ */
+/* multi-token (prefill) kernels: device pointers                      */
+/* ------------------------------------------------------------------ */
+
+/*
+ * Per-token activation quantisation of a row-major [m][n] batch: row t of q
+ * and acts[t] are sllm_i2s_quant_act of row t of x
+ * (include/saphira_llm/i2s_gemm.h:59, src/i2s_gemm.c:45-83), the per-token
+ * quantisation the prefill runs before each projection (src/forward.c:756-764).
+ */
+SLLM_CUDA_API int sllm_cuda_i2s_quant_act_rows(const float * x, size_t m, size_t n,
+                                 int8_t * q, sllm_cuda_act * acts, void * stream);
+
+/*
+ * Prefill GEMM on the tensor cores: for every token t < m and row r <
+ * n_rows, dots[t][r] = sum over k of code(w, r, k) * q[t][k] (int32), which is
+ * sllm_i2s_gemv of token t (src/i2s_gemm.c:260-269) bit for bit, and
+ * y[t][r] = (float)(dots[t][r] - acts[t].sum) * (w_scale / acts[t].scale),
+ * the per-token epilogue of src/forward.c:653-655. The reference has no GEMM:
+ * its prefill runs the GEMV once per token; this computes all of them in one
+ * int8 contraction. q is row-major [m][n]; dots and y are row-major
+ * [m][n_rows] and either may be NULL (not both). n % 128 == 0, n <= 65536;
+ * w and q 16-byte aligned. Asynchronous on `stream`.
+ */
+SLLM_CUDA_API int sllm_cuda_i2s_gemm(const uint8_t * w, size_t n_rows, size_t n, size_t m,
+                       const int8_t * q, const sllm_cuda_act * acts,
+                       int32_t * dots, float * y, void * stream);
+
+/*
+ * The gate/up pair of the prefill FFN in one pass: h[t][r] =
+ * silu(gate[t][r]) * up[t][r], each projection with the epilogue above and
+ * SiLU as sllm_silu_inplace computes it (src/forward.c:756-779,
+ * src/ops.c:428-461). w_gate and w_up have the same shape.
+ */
+SLLM_CUDA_API int sllm_cuda_i2s_gemm_silu(const uint8_t * w_gate, const uint8_t * w_up, size_t n_rows,
+                            size_t n, size_t m, const int8_t * q,
+                            const sllm_cuda_act * acts, float * h, void * stream);
+
+/* ------------------------------------------------------------------ */
 /* model level: host pointers                                          */
 /* ------------------------------------------------------------------ */
 

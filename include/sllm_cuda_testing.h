@@ -25,6 +25,13 @@ SLLM_CUDA_API void sllm_cuda_test_set_force_fallback(int on);
 SLLM_CUDA_API int sllm_cuda_test_fallback_count(void);
 
 /*
+ * The device error word of the prefill GEMM kernels (0: no bounded wait gave
+ * up since the last call of this function, which clears it). Synchronises
+ * the device; -1 without a device.
+ */
+SLLM_CUDA_API int sllm_cuda_test_gemm_error(void);
+
+/*
  * How many kernels this library has put on streams in this process: each
  * launch of one of its CUDA graphs adds the graph's kernel nodes, each direct
  * kernel launch adds one. Kernels enqueued while the caller is capturing a

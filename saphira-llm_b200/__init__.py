@@ -46,6 +46,10 @@ def lib():
     L.sllm_cuda_i2s_quant_act.argtypes = [vp, sz, vp, vp, vp]
     L.sllm_cuda_i2s_gemv.argtypes = [vp, sz, sz, vp, vp, vp]
     L.sllm_cuda_i2s_gemv_f32.argtypes = [vp, sz, sz, vp, vp, vp, vp]
+    L.sllm_cuda_i2s_quant_act_rows.argtypes = [vp, sz, sz, vp, vp, vp]
+    L.sllm_cuda_i2s_gemm.argtypes = [vp, sz, sz, sz, vp, vp, vp, vp, vp]
+    L.sllm_cuda_i2s_gemm_silu.argtypes = [vp, vp, sz, sz, sz, vp, vp, vp, vp]
+    L.sllm_cuda_test_gemm_error.restype = C.c_int
     L.sllm_cuda_model_upload.argtypes = [C.POINTER(abi.ModelDesc), C.c_int, C.POINTER(vp)]
     L.sllm_cuda_model_free.argtypes = [vp]
     L.sllm_cuda_model_weight_bytes.argtypes = [vp]
@@ -115,6 +119,31 @@ def gemv(w, n_rows, n, q, out, stream=None):
 def gemv_f32(w, n_rows, n, x, y, dots=None, stream=None):
     _check(lib().sllm_cuda_i2s_gemv_f32(_ptr(w), n_rows, n, _ptr(x), _ptr(y), _ptr(dots), _stream(stream)),
            "gemv_f32")
+
+
+def quant_act_rows(x, m, n, q, acts, stream=None):
+    """Per-token quantisation of a row-major [m][n] batch (device pointers)."""
+    _check(lib().sllm_cuda_i2s_quant_act_rows(_ptr(x), m, n, _ptr(q), _ptr(acts), _stream(stream)),
+           "quant_act_rows")
+
+
+def gemm(w, n_rows, n, m, q, acts, dots=None, y=None, stream=None):
+    """Prefill GEMM on the tensor cores: per-token GEMV dots and/or the f32
+    epilogue for m tokens at once (device pointers)."""
+    _check(lib().sllm_cuda_i2s_gemm(_ptr(w), n_rows, n, m, _ptr(q), _ptr(acts), _ptr(dots), _ptr(y),
+                                    _stream(stream)), "gemm")
+
+
+def gemm_silu(w_gate, w_up, n_rows, n, m, q, acts, h, stream=None):
+    """h = silu(gate) * up for m tokens at once (device pointers)."""
+    _check(lib().sllm_cuda_i2s_gemm_silu(_ptr(w_gate), _ptr(w_up), n_rows, n, m, _ptr(q), _ptr(acts), _ptr(h),
+                                         _stream(stream)), "gemm_silu")
+
+
+def gemm_error():
+    """The prefill kernels' device error word (0 = every bounded wait
+    completed); synchronises and clears it."""
+    return lib().sllm_cuda_test_gemm_error()
 
 
 def set_force_fallback(on):

@@ -20,6 +20,7 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "engine.cuh"
+#include "gemm.cuh"
 #include "gemv.cuh"
 #include "../../include/sllm_cuda.h"
 #include "../../include/sllm_cuda_testing.h"
@@ -241,6 +242,69 @@ extern "C" int sllm_cuda_i2s_gemv_f32(const uint8_t* w, size_t n_rows, size_t n,
     CK(launch_gemv(p, PRO_QUANT, EPI_F32, current_sms(), (cudaStream_t)stream), "gemv_f32 launch");
     ++g_kernel_launches;
     return SLLM_CUDA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// multi-token (prefill) kernels
+// ---------------------------------------------------------------------------
+static int* g_gemm_error = nullptr;     // device int: why a GEMM's bounded wait gave up
+
+static int* gemm_error_word() {
+    if (g_gemm_error == nullptr) {
+        if (cudaMalloc(&g_gemm_error, sizeof(int)) != cudaSuccess) { g_gemm_error = nullptr; return nullptr; }
+        if (cudaMemset(g_gemm_error, 0, sizeof(int)) != cudaSuccess) return nullptr;
+    }
+    return g_gemm_error;
+}
+
+extern "C" int sllm_cuda_test_gemm_error(void) {
+    int* p = gemm_error_word();
+    if (p == nullptr || cudaDeviceSynchronize() != cudaSuccess) return -1;
+    int v = 0;
+    if (cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    cudaMemset(p, 0, sizeof(int));
+    return v;
+}
+
+extern "C" int sllm_cuda_i2s_quant_act_rows(const float* x, size_t m, size_t n, int8_t* q, sllm_cuda_act* acts,
+                                            void* stream) {
+    if (x == nullptr || q == nullptr || acts == nullptr || m == 0 || n == 0 || n > (size_t)kMaxK || m > (1u << 24))
+        return fail(SLLM_CUDA_ERR_ARG, "quant_act_rows: bad arguments (m=%zu, n=%zu)", m, n);
+    CK(launch_quant_act_rows(x, (int)m, (int)n, q, acts, (cudaStream_t)stream), "quant_act_rows launch");
+    ++g_kernel_launches;
+    return SLLM_CUDA_OK;
+}
+
+static int gemm_run(const GemmArgs& a, void* stream) {
+    const char* why = nullptr;
+    const int rc = gemm_check(a, &why);
+    if (rc != SLLM_CUDA_OK) return fail(rc, "%s", why);
+    int* err = gemm_error_word();
+    if (err == nullptr) return fail(SLLM_CUDA_ERR_NOMEM, "gemm: error word");
+    CK(launch_i2s_gemm(a, err, (cudaStream_t)stream), "gemm launch");
+    ++g_kernel_launches;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_i2s_gemm(const uint8_t* w, size_t n_rows, size_t n, size_t m, const int8_t* q,
+                                  const sllm_cuda_act* acts, int32_t* dots, float* y, void* stream) {
+    if (n_rows == 0 || n_rows > (1u << 24) || m == 0 || m > (1u << 24) || n == 0 || n > (size_t)kMaxK)
+        return fail(SLLM_CUDA_ERR_ARG, "gemm: bad shape (rows=%zu, n=%zu, m=%zu)", n_rows, n, m);
+    GemmArgs a{};
+    a.w = w; a.w2 = nullptr; a.q = q; a.acts = acts; a.dots = dots; a.y = y;
+    a.m = (int)m; a.n_rows = (int)n_rows; a.K = (int)n;
+    return gemm_run(a, stream);
+}
+
+extern "C" int sllm_cuda_i2s_gemm_silu(const uint8_t* w_gate, const uint8_t* w_up, size_t n_rows, size_t n, size_t m,
+                                       const int8_t* q, const sllm_cuda_act* acts, float* h, void* stream) {
+    if (w_up == nullptr || n_rows == 0 || n_rows > (1u << 24) || m == 0 || m > (1u << 24) || n == 0 ||
+        n > (size_t)kMaxK)
+        return fail(SLLM_CUDA_ERR_ARG, "gemm_silu: bad arguments (rows=%zu, n=%zu, m=%zu)", n_rows, n, m);
+    GemmArgs a{};
+    a.w = w_gate; a.w2 = w_up; a.q = q; a.acts = acts; a.dots = nullptr; a.y = h;
+    a.m = (int)m; a.n_rows = (int)n_rows; a.K = (int)n;
+    return gemm_run(a, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -1,0 +1,33 @@
+// gemm.cuh -- the multi-token I2_S GEMM on the tcgen05 tensor cores (i2s_gemm.cu).
+//
+// For every token m of a batch and every weight row r:
+//   dots[m][r] = sum_k code[r][k] * q[m][k]            (int32, exact)
+//   y[m][r]    = (float)(dots[m][r] - act[m].sum) * (ws / act[m].scale)
+// which is, token by token, sllm_i2s_gemv + the forward pass's epilogue
+// (src/i2s_gemm.c:260-269, src/forward.c:653-655). The gate/up form fuses
+// h = silu(gate) * up (src/forward.c:756-779).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/sllm_cuda.h"
+
+namespace sllm {
+
+struct GemmArgs {
+    const uint8_t* w;            // [n_rows][K/4] I2_S codes, scale tail after them
+    const uint8_t* w2;           // gate/up: the up tensor (same shape), else null
+    const int8_t* q;             // [m][K] int8 activations, row-major
+    const sllm_cuda_act* acts;   // [m]
+    int32_t* dots;               // [m][n_rows] or null (single tensor only)
+    float* y;                    // [m][n_rows] or null; gate/up: h
+    int m, n_rows, K;
+};
+
+// 0 when the shapes are supported (K % 128 == 0, 16-byte aligned rows and
+// pointers); a negative sllm status and a message otherwise
+int gemm_check(const GemmArgs& a, const char** why);
+cudaError_t launch_i2s_gemm(const GemmArgs& a, int* error, cudaStream_t st);
+
+}  // namespace sllm

@@ -51,5 +51,7 @@ int gemv_max_k();
 cudaError_t launch_gemv(const GemvParams& p, int pro, int epi, int num_sms, cudaStream_t st,
                         int mode = GEMV_PLAIN);
 cudaError_t launch_quant_act(const float* x, int n, int8_t* q, sllm_cuda_act* act, cudaStream_t st);
+// rows independent vectors of a row-major [rows][n] batch, one block each
+cudaError_t launch_quant_act_rows(const float* x, int rows, int n, int8_t* q, sllm_cuda_act* acts, cudaStream_t st);
 
 }  // namespace sllm

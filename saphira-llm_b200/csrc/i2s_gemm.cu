@@ -1,0 +1,474 @@
+// i2s_gemm.cu -- the multi-token I2_S GEMM (prefill) on the sm_100a tcgen05
+// tensor cores, for configs[3]: 512 tokens through the gate/up and down
+// projections of a 2B-4T layer.
+//
+// One CTA computes a [128 tokens x BN weight rows] tile (two tiles, gate and
+// up, for the fused SiLU form) with the int32 accumulator in tensor memory:
+//
+//   warp 0 (one lane)   TMA: per k-step of 128 elements, the activation tile
+//                       [128 x 128 B] (128-byte swizzle, the UMMA K-major
+//                       canonical layout) and the packed weight tile
+//                       [BN x 32 B] into a stage of a shared-memory ring.
+//   warps 2-5           unpack: each thread turns one weight row's 32 packed
+//                       bytes into 128 int8 codes {0, 1, 2} in the same
+//                       swizzled K-major layout. The I2_S packing makes this two
+//                       logic ops per output word: field f of packed word i
+//                       holds elements 32f + 4i .. 32f + 4i + 3, i.e. exactly the
+//                       int8 word at element 32f + 4i of natural order.
+//   warp 1 (one lane)   tcgen05.mma.cta_group::1.kind::i8 (s8 x s8 -> s32,
+//                       M = 128, N = BN, K = 32) x 4 per k-step and tensor, then
+//                       tcgen05.commit to the stage's "empty" barrier.
+//   warps 2-5 again     epilogue: tcgen05.ld of the accumulator (warp w reads
+//                       TMEM lanes 32 (w % 4) ..), minus the token's code sum,
+//                       times ws / scale, SiLU(gate) * up when fused.
+//
+// The integer sum is exact in any order, so every dot equals the reference's
+// per-token sllm_i2s_gemv bit for bit; the epilogue is the GEMV epilogue's
+// float sequence. Every wait is bounded by the global timer; a wait that
+// gives up records an error, the CTA stops issuing work, drains what it has
+// in flight (bounded) and frees its tensor memory before it exits.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace sllm {
+namespace {
+
+constexpr int kBM = 128;          // tokens per tile (TMEM lanes)
+constexpr int kBK = 128;          // elements (= activation bytes) per k-step
+constexpr int kPK = kBK / 4;      // packed weight bytes per row per k-step
+constexpr int kGmThreads = 192;   // 6 warps
+constexpr uint64_t kGmWaitNs = 2000000000ull;
+
+enum GemmError { GM_OK = 0, GM_TIMEOUT = 1 };
+
+template <int BN, bool PAIR>
+struct GemmCfg {
+    static constexpr int NM = PAIR ? 2 : 1;
+    static constexpr int A_BYTES = kBM * kBK;
+    static constexpr int B_BYTES = BN * kBK;
+    static constexpr int P_BYTES = BN * kPK;
+    static constexpr int STAGE = A_BYTES + NM * (B_BYTES + P_BYTES);   // a multiple of 1024
+    static constexpr int S = (196608 / STAGE) > 6 ? 6 : (196608 / STAGE);
+    static constexpr int SMEM = S * STAGE + 1024;                       // + room to align to 1024
+    static constexpr int TMEM_COLS = NM * BN;                           // 64, 128 or 256
+    static_assert(STAGE % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
+    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "tile width");
+};
+
+struct GemmKParams {
+    const sllm_cuda_act* acts;
+    const float* ws;       // the scale tail of w
+    const float* ws2;      // ... of w2 (PAIR)
+    int32_t* dots;
+    float* y;
+    int M, N, K;
+    int* error;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 65536;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// bounded wait: false when the phase did not complete in time, or when the
+// CTA is aborting
+__device__ __noinline__ bool gm_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* error) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = gtimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort_flag) return false;
+        if (gtimer() - t0 > kGmWaitNs) {
+            *abort_flag = 1;
+            atomicExch(error, GM_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+// drain: wait for a phase that must complete (work already in flight);
+// bounded, never looks at the abort flag
+__device__ __noinline__ void gm_drain(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = gtimer();
+    while (!mbar_try_wait(bar, parity))
+        if (gtimer() - t0 > kGmWaitNs) return;
+}
+
+// a 2-D TMA tile load (no multicast) completing on bar
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// UMMA shared-memory descriptor of a K-major tile in the 128-byte swizzle
+// canonical layout: rows of 128 bytes, 8-row groups 1024 bytes apart
+// (SBO), the 16-byte chunk index of row r XOR-ed with r % 8. LBO is unused
+// for swizzled K-major layouts (1 by convention); version 1 (sm_100);
+// layout type 2 = 128-byte swizzle. The tile base is 1024-byte aligned, so
+// base_offset is 0 and a K offset inside the 128-byte row is added to the
+// start address.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;
+    d |= (uint64_t)(1024u >> 4) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)2u << 61;
+    return d;
+}
+
+// instruction descriptor, kind::i8: D s32, A s8, B s8, both K-major, M, N
+__host__ __device__ constexpr uint32_t umma_idesc_i8(int M, int N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 consecutive accumulator columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// the codes of one packed word, field f: four int8 codes of consecutive elements
+__device__ __forceinline__ uint32_t field_codes(uint32_t w, int f) { return (w >> (6 - 2 * f)) & 0x03030303u; }
+
+template <int BN, bool PAIR>
+__global__ void __launch_bounds__(kGmThreads, 1)
+i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
+                const __grid_constant__ CUtensorMap tm_w2, const GemmKParams p) {
+    using C = GemmCfg<BN, PAIR>;
+    extern __shared__ uint8_t gsm_raw[];
+    __shared__ uint64_t bar_loaded[C::S], bar_unpacked[C::S], bar_empty[C::S], bar_acc;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int abort_flag;
+    uint8_t* const gsm = gsm_raw + ((1024u - (smem_u32(gsm_raw) & 1023u)) & 1023u);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
+    const int KB = p.K / kBK;
+    auto A = [&](int s) { return gsm + (size_t)s * C::STAGE; };
+    auto B = [&](int s, int mat) { return gsm + (size_t)s * C::STAGE + C::A_BYTES + mat * C::B_BYTES; };
+    auto P = [&](int s, int mat) {
+        return gsm + (size_t)s * C::STAGE + C::A_BYTES + C::NM * C::B_BYTES + mat * C::P_BYTES;
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::S; ++s) {
+            mbar_init(&bar_loaded[s], 1);
+            mbar_init(&bar_unpacked[s], 4);
+            mbar_init(&bar_empty[s], 1);
+        }
+        mbar_init(&bar_acc, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                     "r"((uint32_t)C::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    volatile int* const abort_v = &abort_flag;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int issued = 0;
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % C::S;
+                const uint32_t use = (uint32_t)(kb / C::S);
+                if (use > 0 && !gm_wait(&bar_empty[s], (use - 1) & 1u, abort_v, p.error)) break;
+                mbar_expect_tx(&bar_loaded[s], (uint32_t)(C::A_BYTES + C::NM * C::P_BYTES));
+                tma_load_2d(A(s), &tm_a, kb * kBK, m0, &bar_loaded[s]);
+                tma_load_2d(P(s, 0), &tm_w, kb * kPK, n0, &bar_loaded[s]);
+                if (PAIR) tma_load_2d(P(s, 1), &tm_w2, kb * kPK, n0, &bar_loaded[s]);
+                ++issued;
+            }
+            // every copy issued lands before the CTA may exit
+            for (int kb = issued > C::S ? issued - C::S : 0; kb < issued; ++kb)
+                gm_drain(&bar_loaded[kb % C::S], (uint32_t)(kb / C::S) & 1u);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_i8(kBM, BN);
+            int issued = 0;
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % C::S;
+                const uint32_t ph = (uint32_t)(kb / C::S) & 1u;
+                if (!gm_wait(&bar_loaded[s], ph, abort_v, p.error)) break;
+                if (!gm_wait(&bar_unpacked[s], ph, abort_v, p.error)) break;
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(A(s));
+                #pragma unroll
+                for (int mat = 0; mat < C::NM; ++mat) {
+                    const uint32_t b0 = smem_u32(B(s, mat));
+                    #pragma unroll
+                    for (int kk = 0; kk < kBK / 32; ++kk)
+                        umma_i8(tmem + (uint32_t)(mat * BN), umma_desc_sw128(a0 + 32u * kk),
+                                umma_desc_sw128(b0 + 32u * kk), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(&bar_empty[s]);     // the stage may be refilled once these MMAs have read it
+                ++issued;
+            }
+            umma_commit(&bar_acc);              // the accumulator is complete (or the CTA aborted)
+            // the MMAs issued have finished reading shared memory before exit
+            if (issued > 0) gm_drain(&bar_empty[(issued - 1) % C::S], (uint32_t)((issued - 1) / C::S) & 1u);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- unpack, then epilogue (warps 2-5) ----------------
+        const int t = threadIdx.x - 64;     // 0..127
+        bool ok = true;
+        for (int kb = 0; kb < KB && ok; ++kb) {
+            const int s = kb % C::S;
+            const uint32_t ph = (uint32_t)(kb / C::S) & 1u;
+            ok = gm_wait(&bar_loaded[s], ph, abort_v, p.error);
+            if (ok) {
+                // items: (matrix, half, row); eight consecutive threads take eight
+                // consecutive rows, so their 16-byte stores hit eight distinct
+                // swizzled chunks (no bank conflict)
+                #pragma unroll
+                for (int it = t; it < C::NM * 2 * BN; it += 128) {
+                    const int row = it % BN, h = (it / BN) & 1, mat = it / (2 * BN);
+                    const uint4 v = *reinterpret_cast<const uint4*>(P(s, mat) + row * kPK + h * 16);
+                    uint8_t* brow = B(s, mat) + row * kBK;
+                    #pragma unroll
+                    for (int f = 0; f < 4; ++f) {
+                        uint4 o;
+                        o.x = field_codes(v.x, f);
+                        o.y = field_codes(v.y, f);
+                        o.z = field_codes(v.z, f);
+                        o.w = field_codes(v.w, f);
+                        const int chunk = (2 * f + h) ^ (row & 7);
+                        *reinterpret_cast<uint4*>(brow + chunk * 16) = o;
+                    }
+                }
+                fence_proxy_async_smem();       // the tensor core reads through the async proxy
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_unpacked[s]);
+            ok = __all_sync(0xffffffffu, ok);
+        }
+        // epilogue
+        const bool acc_ok = __all_sync(0xffffffffu, ok && gm_wait(&bar_acc, 0u, abort_v, p.error)) &&
+                            __all_sync(0xffffffffu, *abort_v == 0);
+        if (acc_ok) {
+            tc_fence_after();
+            const int quarter = warp & 3;
+            const int m = m0 + 32 * quarter + lane;
+            const bool live = m < p.M;
+            sllm_cuda_act act{1.0f, 0};
+            if (live) act = p.acts[m];
+            // per-tensor scale over the token's activation scale (src/forward.c:653-655)
+            const float post = __fdiv_rn(__ldg(p.ws), act.scale);
+            const float post2 = PAIR ? __fdiv_rn(__ldg(p.ws2), act.scale) : 0.0f;
+            const uint32_t lane_base = tmem + ((uint32_t)(32 * quarter) << 16);
+            #pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t g[32];
+                tmem_ld32(lane_base + (uint32_t)c0, g);
+                if (PAIR) {
+                    uint32_t u[32];
+                    tmem_ld32(lane_base + (uint32_t)(BN + c0), u);
+                    tmem_ld_wait();
+                    if (live) {
+                        float* yrow = p.y + (size_t)m * p.N;
+                        #pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int n = n0 + c0 + j;
+                            if (n < p.N) {
+                                // h = silu(gate) * up (src/forward.c:765-778, src/ops.c:452-456)
+                                const float gv = __fmul_rn(__int2float_rn((int)g[j] - act.sum), post);
+                                const float uv = __fmul_rn(__int2float_rn((int)u[j] - act.sum), post2);
+                                yrow[n] = __fmul_rn(silu_block(gv), uv);
+                            }
+                        }
+                    }
+                } else {
+                    tmem_ld_wait();
+                    if (live) {
+                        #pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int n = n0 + c0 + j;
+                            if (n < p.N) {
+                                if (p.dots != nullptr) p.dots[(size_t)m * p.N + n] = (int)g[j];
+                                if (p.y != nullptr)
+                                    p.y[(size_t)m * p.N + n] = __fmul_rn(__int2float_rn((int)g[j] - act.sum), post);
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (fn == nullptr) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+// a row-major [rows][cols] byte matrix, tiles of box_rows x box_cols bytes
+bool encode_2d(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
+               CUtensorMapSwizzle swizzle) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (enc == nullptr) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, bool PAIR>
+cudaError_t launch_tile(const GemmArgs& a, int* error, cudaStream_t st) {
+    using C = GemmCfg<BN, PAIR>;
+    CUtensorMap tm_a, tm_w, tm_w2;
+    if (!encode_2d(&tm_a, a.q, (uint64_t)a.K, (uint64_t)a.m, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_2d(&tm_w, a.w, (uint64_t)(a.K / 4), (uint64_t)a.n_rows, kPK, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return cudaErrorInvalidValue;
+    if (PAIR) {
+        if (!encode_2d(&tm_w2, a.w2, (uint64_t)(a.K / 4), (uint64_t)a.n_rows, kPK, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return cudaErrorInvalidValue;
+    } else {
+        tm_w2 = tm_w;
+    }
+    GemmKParams p{};
+    p.acts = a.acts;
+    const size_t tail = (size_t)a.n_rows * (size_t)(a.K / 4);
+    p.ws = reinterpret_cast<const float*>(a.w + tail);
+    p.ws2 = PAIR ? reinterpret_cast<const float*>(a.w2 + tail) : p.ws;
+    p.dots = a.dots;
+    p.y = a.y;
+    p.M = a.m;
+    p.N = a.n_rows;
+    p.K = a.K;
+    p.error = error;
+    cudaError_t e = cudaFuncSetAttribute(i2s_gemm_kernel<BN, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    const dim3 grid((unsigned)((a.n_rows + BN - 1) / BN), (unsigned)((a.m + kBM - 1) / kBM));
+    i2s_gemm_kernel<BN, PAIR><<<grid, kGmThreads, C::SMEM, st>>>(tm_a, tm_w, tm_w2, p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+int gemm_check(const GemmArgs& a, const char** why) {
+    auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+    if (a.w == nullptr || a.q == nullptr || a.acts == nullptr || a.m <= 0 || a.n_rows <= 0 || a.K <= 0) {
+        *why = "gemm: null pointer or empty shape";
+        return SLLM_CUDA_ERR_ARG;
+    }
+    if (a.K % kBK != 0) {
+        *why = "gemm: K must be a multiple of 128";
+        return SLLM_CUDA_ERR_ARG;
+    }
+    if (a.K > kMaxK) {
+        *why = "gemm: K above the supported maximum";
+        return SLLM_CUDA_ERR_UNSUPPORTED;
+    }
+    if (!al16(a.w) || !al16(a.q) || (a.w2 != nullptr && !al16(a.w2))) {
+        *why = "gemm: w and q must be 16-byte aligned";
+        return SLLM_CUDA_ERR_ARG;
+    }
+    if (a.w2 != nullptr ? a.y == nullptr : (a.y == nullptr && a.dots == nullptr)) {
+        *why = "gemm: no output";
+        return SLLM_CUDA_ERR_ARG;
+    }
+    return SLLM_CUDA_OK;
+}
+
+cudaError_t launch_i2s_gemm(const GemmArgs& a, int* error, cudaStream_t st) {
+    if (a.w2 != nullptr) return launch_tile<128, true>(a, error, st);
+    return launch_tile<128, false>(a, error, st);
+}
+
+}  // namespace sllm

@@ -324,6 +324,10 @@ quant_act_kernel(const float* x, int n, int8_t* q, sllm_cuda_act* act) {
     __shared__ float fred[kGemvWarps];
     __shared__ int ired[kGemvWarps];
     const int tid = threadIdx.x;
+    // block b quantises row b of a row-major [rows][n] batch (one row per token)
+    x += (size_t)blockIdx.x * n;
+    q += (size_t)blockIdx.x * n;
+    act += blockIdx.x;
     float amax = 0.0f;
     for (int i = tid; i < n; i += kGemvThreads) amax = fmaxf(amax, fabsf(x[i]));
     amax = cta_max(amax, fred);
@@ -405,6 +409,11 @@ cudaError_t launch_gemv(const GemvParams& p_in, int pro, int epi, int num_sms, c
 
 cudaError_t launch_quant_act(const float* x, int n, int8_t* q, sllm_cuda_act* act, cudaStream_t st) {
     quant_act_kernel<<<1, kGemvThreads, 0, st>>>(x, n, q, act);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quant_act_rows(const float* x, int rows, int n, int8_t* q, sllm_cuda_act* acts, cudaStream_t st) {
+    quant_act_kernel<<<rows, kGemvThreads, 0, st>>>(x, n, q, acts);
     return cudaGetLastError();
 }
 
