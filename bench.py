@@ -262,6 +262,91 @@ def time_device(fn, steps, warmup, stream, world):
     return float(t.item()), per
 
 
+PREFILL_TOKENS = 512
+
+
+def int8_peak():
+    """Dense int8 tensor peak: twice the measured bf16 dense (cuBLAS burst)
+    rate, as on every Blackwell part (nominal 4.5 vs 2.25 P ops/s)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return 2.0 * float(json.load(f)["bf16_tflops"]), "2x measured bf16 dense (burst)"
+    except Exception:
+        return 2.0 * 1590.0, "2x fallback bf16 dense"
+
+
+def prefill_leg(pkg, synth, local, rank, world, args):
+    """512 tokens of fp32 N(0,1) activations through one 2B-4T
+    layer's FFN projections on the tcgen05 tensor cores: per-token int8
+    quantisation, gate/up with the SiLU product fused, then down. One step =
+    the four launches; ops = 2 * 512 * (6912*2560*2 + 2560*6912)."""
+    import torch
+    cfg = synth.Config(n_layer=1, n_vocab=256)
+    m = synth.SynthModel(cfg, seed=77 + rank)
+    E, F, M = cfg.n_embd, cfg.n_ff, PREFILL_TOKENS
+    L = m.tensors
+    wg, wu, wd = (torch.from_numpy(np.ascontiguousarray(L[f"blk.0.{n}.weight"])).cuda()
+                  for n in ("ffn_gate", "ffn_up", "ffn_down"))
+    rng = np.random.default_rng(100 + rank)
+    xa_h = rng.standard_normal((M, E)).astype(np.float32)
+    xd_h = rng.standard_normal((M, F)).astype(np.float32)
+    xa, xd = torch.from_numpy(xa_h).cuda(), torch.from_numpy(xd_h).cuda()
+    qa = torch.empty((M, E), dtype=torch.int8, device="cuda")
+    qd = torch.empty((M, F), dtype=torch.int8, device="cuda")
+    aa = torch.empty((M, 2), dtype=torch.int32, device="cuda")
+    ad = torch.empty((M, 2), dtype=torch.int32, device="cuda")
+    h = torch.empty((M, F), dtype=torch.float32, device="cuda")
+    y = torch.empty((M, E), dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream()
+
+    def gemms():
+        pkg.gemm_silu(wg, wu, F, E, M, qa, aa, h, st)
+        pkg.gemm(wd, E, F, M, qd, ad, None, y, st)
+
+    def step():
+        pkg.quant_act_rows(xa, M, E, qa, aa, st)
+        pkg.quant_act_rows(xd, M, F, qd, ad, st)
+        gemms()
+
+    ops = 2.0 * M * (2 * F * E + E * F)
+    ms, _ = time_device(step, args.steps, args.warmup, st, world)
+    gms, _ = time_device(gemms, args.steps, args.warmup, st, world)
+    err = pkg.gemm_error()
+    peak, kind = int8_peak()
+    tops = ops * args.steps * world / (ms / 1e3) / 1e12
+    gtops = ops * args.steps / (gms / 1e3) / 1e12
+    out = {"workload": "prefill_ffn_2b4t (512 tokens: quant + gate/up SiLU + quant + down)",
+           "value": round(tops, 2), "unit": "int8 TOP/s", "ms_per_step": round(ms / args.steps, 4),
+           "ops_per_step": ops, "device_error": err,
+           "roofline": {"bound": "tensor", "kernel": "i2s_gemm_kernel (gate/up pair + down)",
+                        "achieved": round(gtops, 1), "peak": round(peak, 1), "unit": "TOP/s",
+                        "frac": round(gtops / peak, 4), "peak_source": kind,
+                        "gemm_ms_per_step": round(gms / args.steps, 4)}}
+    if rank == 0 and not args.no_cpu_baseline:
+        import oracle
+        if oracle.reference_available():
+            ref = oracle.Reference()
+            pool = ref.pool(os.cpu_count() or 1)
+            dots = np.zeros(F, np.int32)
+            wgh, wuh, wdh = (L[f"blk.0.{n}.weight"] for n in ("ffn_gate", "ffn_up", "ffn_down"))
+            n_tok, t0 = 0, time.perf_counter()
+            while time.perf_counter() - t0 < 5.0 and n_tok < M:
+                # per token, as the reference's prefill: quantise, GEMV (pooled)
+                q, _, _ = ref.quant_act(xa_h[n_tok])
+                pool.gemv(wgh, F, E, q, dots)
+                pool.gemv(wuh, F, E, q, dots)
+                q, _, _ = ref.quant_act(xd_h[n_tok])
+                pool.gemv(wdh, E, F, q, dots)
+                n_tok += 1
+            dt = time.perf_counter() - t0
+            out["cpu_reference"] = {"value": round(2.0 * (2 * F * E + E * F) * n_tok / dt / 1e12, 4),
+                                    "unit": "int8 TOP/s", "cores": pool.threads, "kind": "reference",
+                                    "sample": f"{n_tok} of the 512 tokens, per-token quant + 3 pooled GEMVs, "
+                                              f"{dt:.1f} s"}
+    del m
+    return out
+
+
 def decode_leg(pkg, synth, local, rank, world, args):
     """2B-4T random init, prompt 64, 256 greedy tokens."""
     import torch
@@ -323,6 +408,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--copies", type=int, default=N_COPIES,
                     help="layer copies per step (default 32; smaller only for profiler captures)")
     args = ap.parse_args()
@@ -440,6 +526,8 @@ def main():
     ctx.close()
     model.close()
     del m
+    if not args.no_prefill:
+        out["prefill"] = prefill_leg(pkg, synth, local, rank, world, args)
     if not args.no_decode:
         out["decode"] = decode_leg(pkg, synth, local, rank, world, args)
     if rank == 0:
