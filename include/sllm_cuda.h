@@ -333,6 +333,81 @@ SLLM_CUDA_API size_t sllm_cuda_model_weight_bytes(const sllm_cuda_model * m);
  */
 SLLM_CUDA_API int sllm_cuda_ctx_last_logits(const sllm_cuda_ctx * c, float * host_out);
 
+/* ------------------------------------------------------------------ */
+/* tensor-parallel decode across the GPUs of one node                  */
+/* ------------------------------------------------------------------ */
+/*
+ * The reference decodes on one host (src/forward.c:589-835); these entry
+ * points shard the same forward pass over N GPUs, one process (rank) per
+ * GPU: Q/K/V and gate/up split by rows (heads, FFN rows), O and down by
+ * contraction columns with an int32 all-reduce of the partial dots (exact in
+ * any order), the tied f16 head by vocabulary rows. Every rank calls every
+ * entry point with the same arguments (SPMD); the results equal the
+ * single-GPU path's, bit for bit. NCCL carries the exchanges.
+ */
+#define SLLM_CUDA_TP_ID_BYTES 128
+
+typedef struct sllm_cuda_tp_comm sllm_cuda_tp_comm;
+typedef struct sllm_cuda_tp_model sllm_cuda_tp_model;
+typedef struct sllm_cuda_tp_ctx sllm_cuda_tp_ctx;
+
+/* the group's identity: rank 0 creates it and hands the bytes to the others */
+SLLM_CUDA_API int sllm_cuda_tp_unique_id(uint8_t * id_out);
+SLLM_CUDA_API int sllm_cuda_tp_comm_init(const uint8_t * id, int32_t n_ranks, int32_t rank,
+                           int32_t device, sllm_cuda_tp_comm ** out);
+SLLM_CUDA_API void sllm_cuda_tp_comm_free(sllm_cuda_tp_comm * c);
+
+/*
+ * Rank `rank`'s shard of a model given as host tensors (the same description
+ * as sllm_cuda_model_upload). n_head, n_head_kv, n_embd / n_ranks and
+ * n_ff / n_ranks must divide evenly (multiples of 128 for the widths); head
+ * dim 128, n_embd <= 8192, n_ff <= 28672.
+ */
+SLLM_CUDA_API int sllm_cuda_tp_model_upload(const sllm_cuda_model_desc * d, int32_t n_ranks,
+                              int32_t rank, int32_t device, sllm_cuda_tp_model ** out);
+
+/*
+ * A seeded synthetic model generated on the device, shard by shard (the
+ * benchmark's configs[4]: 80 layers, 8192 / 28672, 64 / 8 heads, vocab
+ * 128256): ternary codes i.i.d. over {-1, 0, 1} from a counter-based hash of
+ * (seed, layer, tensor, row, column), per-tensor scales in [0.01, 0.1), norm
+ * weights ~N(1, 0.02), the f16 table ~N(0, 0.02). Every shard is a slice of
+ * the same model for every rank count.
+ */
+typedef struct sllm_cuda_tp_synth_desc {
+    int32_t  n_layer, n_embd, n_ff, n_head, n_head_kv, n_vocab;
+    float    f_rms_eps, rope_freq_base;
+    uint64_t seed;
+} sllm_cuda_tp_synth_desc;
+
+SLLM_CUDA_API int sllm_cuda_tp_model_synth(const sllm_cuda_tp_synth_desc * d, int32_t n_ranks,
+                             int32_t rank, int32_t device, sllm_cuda_tp_model ** out);
+SLLM_CUDA_API void sllm_cuda_tp_model_free(sllm_cuda_tp_model * m);
+SLLM_CUDA_API size_t sllm_cuda_tp_model_bytes(const sllm_cuda_tp_model * m);
+/* this shard's vocabulary rows [*v0, *v0 + *n) */
+SLLM_CUDA_API int sllm_cuda_tp_vocab_range(const sllm_cuda_tp_model * m, int32_t * v0, int32_t * n);
+
+/*
+ * a decode context over one shard. sllm_cuda_tp_generate_greedy needs comm
+ * whenever the model has more than one rank; a context without one serves a
+ * single rank, or a one-process test group.
+ */
+SLLM_CUDA_API int sllm_cuda_tp_ctx_new(const sllm_cuda_tp_model * m, sllm_cuda_tp_comm * comm,
+                         int32_t n_ctx, sllm_cuda_tp_ctx ** out);
+SLLM_CUDA_API void sllm_cuda_tp_ctx_free(sllm_cuda_tp_ctx * c);
+SLLM_CUDA_API int sllm_cuda_tp_ctx_reset(sllm_cuda_tp_ctx * c);
+
+/*
+ * sllm_generate_greedy (src/forward.c:885-938) over the shards: argument
+ * rules, BOS fallback and outputs as sllm_cuda_generate_greedy. A step whose
+ * exchanges make no progress for 120 s aborts the communicator and returns
+ * SLLM_CUDA_ERR_TIMEOUT.
+ */
+SLLM_CUDA_API int sllm_cuda_tp_generate_greedy(sllm_cuda_tp_ctx * c, const int32_t * prompt,
+                                 int32_t n_prompt, int32_t n_new, int32_t * out);
+/* the last step's logits of this shard's vocabulary rows */
+SLLM_CUDA_API int sllm_cuda_tp_last_logits(const sllm_cuda_tp_ctx * c, float * host_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -32,6 +32,16 @@ SLLM_CUDA_API int sllm_cuda_test_fallback_count(void);
 SLLM_CUDA_API int sllm_cuda_test_gemm_error(void);
 
 /*
+ * Greedy decode over the N contexts of ranks 0..N-1 of one tensor-parallel
+ * model, all on one device and in one process, with the exchanges done by
+ * device copies instead of NCCL: the same phases, the same bits, testable on
+ * a single GPU. out receives the tokens (every rank's are the same).
+ */
+SLLM_CUDA_API int sllm_cuda_test_tp_generate_group(sllm_cuda_tp_ctx ** cs, int32_t n,
+                                     const int32_t * prompt, int32_t n_prompt,
+                                     int32_t n_new, int32_t * out);
+
+/*
  * How many kernels this library has put on streams in this process: each
  * launch of one of its CUDA graphs adds the graph's kernel nodes, each direct
  * kernel launch adds one. Kernels enqueued while the caller is capturing a

@@ -1,7 +1,7 @@
 """saphira-llm B200 backend: Python binding of libsllm_cuda.so (include/sllm_cuda.h).
 
 The product is the C ABI in libsllm_cuda.so; saphira-llm's C11 host code calls
-it directly (see INTEGRATION.md). This module binds the same entry points with
+it directly. This module binds the same entry points with
 ctypes for the tests, the benchmark and Python callers. Device buffers are
 passed as raw pointers (or torch CUDA tensors, whose data_ptr() is used); the
 library never falls back to the CPU: loading fails loudly if the built library
@@ -9,6 +9,8 @@ is missing, and every call returns its status as an exception.
 """
 import ctypes as C
 import os
+
+import numpy as np
 
 from . import abi
 
@@ -50,6 +52,21 @@ def lib():
     L.sllm_cuda_i2s_gemm.argtypes = [vp, sz, sz, sz, vp, vp, vp, vp, vp]
     L.sllm_cuda_i2s_gemm_silu.argtypes = [vp, vp, sz, sz, sz, vp, vp, vp, vp]
     L.sllm_cuda_test_gemm_error.restype = C.c_int
+    L.sllm_cuda_tp_unique_id.argtypes = [vp]
+    L.sllm_cuda_tp_comm_init.argtypes = [vp, i32, i32, i32, C.POINTER(vp)]
+    L.sllm_cuda_tp_comm_free.argtypes = [vp]
+    L.sllm_cuda_tp_model_upload.argtypes = [C.POINTER(abi.ModelDesc), i32, i32, i32, C.POINTER(vp)]
+    L.sllm_cuda_tp_model_synth.argtypes = [C.POINTER(abi.TpSynthDesc), i32, i32, i32, C.POINTER(vp)]
+    L.sllm_cuda_tp_model_free.argtypes = [vp]
+    L.sllm_cuda_tp_model_bytes.argtypes = [vp]
+    L.sllm_cuda_tp_model_bytes.restype = sz
+    L.sllm_cuda_tp_vocab_range.argtypes = [vp, C.POINTER(i32), C.POINTER(i32)]
+    L.sllm_cuda_tp_ctx_new.argtypes = [vp, vp, i32, C.POINTER(vp)]
+    L.sllm_cuda_tp_ctx_free.argtypes = [vp]
+    L.sllm_cuda_tp_ctx_reset.argtypes = [vp]
+    L.sllm_cuda_tp_generate_greedy.argtypes = [vp, vp, i32, i32, vp]
+    L.sllm_cuda_tp_last_logits.argtypes = [vp, vp]
+    L.sllm_cuda_test_tp_generate_group.argtypes = [C.POINTER(vp), i32, vp, i32, i32, vp]
     L.sllm_cuda_model_upload.argtypes = [C.POINTER(abi.ModelDesc), C.c_int, C.POINTER(vp)]
     L.sllm_cuda_model_free.argtypes = [vp]
     L.sllm_cuda_model_weight_bytes.argtypes = [vp]
@@ -271,3 +288,94 @@ def projection_sizes(model):
     ys = C.c_size_t()
     xs = lib().sllm_cuda_layer_projections_sizes(model.h, C.byref(ys))
     return int(xs), int(ys.value)
+
+
+# tensor parallel (one rank per GPU) ---------------------------------------------
+def tp_unique_id():
+    """The group identity rank 0 creates and hands to the other ranks (bytes)."""
+    buf = (C.c_uint8 * abi.TP_ID_BYTES)()
+    _check(lib().sllm_cuda_tp_unique_id(buf), "tp_unique_id")
+    return bytes(buf)
+
+
+class TpComm:
+    def __init__(self, uid, n_ranks, rank, device):
+        self.h = C.c_void_p()
+        buf = (C.c_uint8 * abi.TP_ID_BYTES).from_buffer_copy(uid)
+        _check(lib().sllm_cuda_tp_comm_init(buf, n_ranks, rank, device, C.byref(self.h)), "tp_comm_init")
+
+    def close(self):
+        if self.h:
+            lib().sllm_cuda_tp_comm_free(self.h)
+            self.h = C.c_void_p()
+
+
+class TpModel:
+    """Rank `rank`'s shard of a model: from host tensors (`desc`, a ModelDesc)
+    or generated on the device (`synth`, a TpSynthDesc)."""
+
+    def __init__(self, n_ranks, rank, device=0, desc=None, synth=None):
+        self.h = C.c_void_p()
+        self._keep = desc
+        if desc is not None:
+            _check(lib().sllm_cuda_tp_model_upload(C.byref(desc), n_ranks, rank, device, C.byref(self.h)),
+                   "tp_model_upload")
+        else:
+            _check(lib().sllm_cuda_tp_model_synth(C.byref(synth), n_ranks, rank, device, C.byref(self.h)),
+                   "tp_model_synth")
+
+    def vocab_range(self):
+        v0, n = C.c_int32(), C.c_int32()
+        _check(lib().sllm_cuda_tp_vocab_range(self.h, C.byref(v0), C.byref(n)), "tp_vocab_range")
+        return v0.value, n.value
+
+    def bytes(self):
+        return lib().sllm_cuda_tp_model_bytes(self.h)
+
+    def ctx(self, n_ctx, comm=None):
+        return TpCtx(self, n_ctx, comm)
+
+    def close(self):
+        if self.h:
+            lib().sllm_cuda_tp_model_free(self.h)
+            self.h = C.c_void_p()
+
+
+class TpCtx:
+    def __init__(self, model, n_ctx, comm=None):
+        self.model = model
+        self.h = C.c_void_p()
+        _check(lib().sllm_cuda_tp_ctx_new(model.h, comm.h if comm is not None else None, n_ctx, C.byref(self.h)),
+               "tp_ctx_new")
+
+    def generate(self, prompt, n_new):
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros(max(n_new, 1), np.int32)
+        rc = lib().sllm_cuda_tp_generate_greedy(self.h, prompt.ctypes.data if prompt.size else None, prompt.size,
+                                                 n_new, out.ctypes.data)
+        return rc, out[:n_new]
+
+    def last_logits(self):
+        v0, n = self.model.vocab_range()
+        out = np.zeros(n, np.float32)
+        _check(lib().sllm_cuda_tp_last_logits(self.h, out.ctypes.data), "tp_last_logits")
+        return v0, out
+
+    def reset(self):
+        _check(lib().sllm_cuda_tp_ctx_reset(self.h), "tp_ctx_reset")
+
+    def close(self):
+        if self.h:
+            lib().sllm_cuda_tp_ctx_free(self.h)
+            self.h = C.c_void_p()
+
+
+def tp_generate_group(ctxs, prompt, n_new):
+    """Greedy decode over the contexts of ranks 0..N-1 on one device (device
+    copies instead of NCCL; a test of the sharding on one GPU)."""
+    prompt = np.ascontiguousarray(prompt, np.int32)
+    arr = (C.c_void_p * len(ctxs))(*[c.h.value for c in ctxs])
+    out = np.zeros(max(n_new, 1), np.int32)
+    rc = lib().sllm_cuda_test_tp_generate_group(arr, len(ctxs), prompt.ctypes.data if prompt.size else None,
+                                                prompt.size, n_new, out.ctypes.data)
+    return rc, out[:n_new]

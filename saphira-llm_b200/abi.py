@@ -51,3 +51,15 @@ class ModelDesc(C.Structure):
 
 LAYER_I2S = ("wq", "wk", "wv", "wo", "ffn_gate", "ffn_up", "ffn_down")
 LAYER_NORMS = ("attn_norm", "attn_sub_norm", "ffn_norm", "ffn_sub_norm")
+
+
+class TpSynthDesc(C.Structure):
+    """sllm_cuda_tp_synth_desc: a seeded synthetic model generated on the device."""
+    _fields_ = [
+        ("n_layer", C.c_int32), ("n_embd", C.c_int32), ("n_ff", C.c_int32),
+        ("n_head", C.c_int32), ("n_head_kv", C.c_int32), ("n_vocab", C.c_int32),
+        ("f_rms_eps", C.c_float), ("rope_freq_base", C.c_float), ("seed", C.c_uint64),
+    ]
+
+
+TP_ID_BYTES = 128

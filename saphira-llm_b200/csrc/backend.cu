@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "decode.cuh"
+#include "backend.cuh"
 #include "engine.cuh"
 #include "gemm.cuh"
 #include "gemv.cuh"
@@ -42,7 +43,7 @@ static std::atomic<long long> g_kernel_launches{0};
 static std::mutex g_graph_mu;
 static std::unordered_map<cudaGraphExec_t, int> g_graph_kernels;
 
-static int fail(int status, const char* fmt, ...) {
+int sllm::fail(int status, const char* fmt, ...) {
     char buf[512];
     va_list ap;
     va_start(ap, fmt);
@@ -52,17 +53,13 @@ static int fail(int status, const char* fmt, ...) {
     return status;
 }
 
-static int cuda_fail(cudaError_t e, const char* what) {
+int sllm::cuda_fail(cudaError_t e, const char* what) {
     const int st = (e == cudaErrorMemoryAllocation) ? SLLM_CUDA_ERR_NOMEM : SLLM_CUDA_ERR_DEVICE;
     cudaGetLastError();   // clear a sticky launch error where possible
     return fail(st, "%s: %s", what, cudaGetErrorString(e));
 }
 
-#define CK(call, what)                                        \
-    do {                                                      \
-        cudaError_t e_ = (call);                              \
-        if (e_ != cudaSuccess) return cuda_fail(e_, (what));  \
-    } while (0)
+
 
 extern "C" const char* sllm_cuda_status_string(int st) {
     switch (st) {
@@ -84,7 +81,7 @@ extern "C" const char* sllm_cuda_last_error(void) { return g_last_error.c_str();
 // ---------------------------------------------------------------------------
 // devices
 // ---------------------------------------------------------------------------
-static int num_sms_of(int dev) {
+int sllm::num_sms_of(int dev) {
     static std::mutex mu;
     static std::vector<int> cache;
     std::lock_guard<std::mutex> lk(mu);
@@ -125,7 +122,7 @@ extern "C" int sllm_cuda_probe(int* n_devices, int* cc_major, int* cc_minor) {
 // Allocated on first use OUTSIDE any stream capture (ctx_new and the chain
 // entry points call it before capturing); a graph then bakes the pointer in.
 // instantiate a captured graph, remembering how many kernel nodes it holds
-static cudaError_t instantiate(cudaGraphExec_t* exec, cudaGraph_t g) {
+cudaError_t sllm::instantiate(cudaGraphExec_t* exec, cudaGraph_t g) {
     size_t n = 0;
     cudaError_t e = cudaGraphGetNodes(g, nullptr, &n);
     std::vector<cudaGraphNode_t> nodes(n);
@@ -145,7 +142,7 @@ static cudaError_t instantiate(cudaGraphExec_t* exec, cudaGraph_t g) {
     return e;
 }
 
-static void graph_exec_destroy(cudaGraphExec_t exec) {
+void sllm::graph_exec_destroy(cudaGraphExec_t exec) {
     if (exec == nullptr) return;
     {
         std::lock_guard<std::mutex> lk(g_graph_mu);
@@ -154,7 +151,7 @@ static void graph_exec_destroy(cudaGraphExec_t exec) {
     cudaGraphExecDestroy(exec);
 }
 
-static cudaError_t graph_launch(cudaGraphExec_t exec, cudaStream_t st) {
+cudaError_t sllm::graph_launch(cudaGraphExec_t exec, cudaStream_t st) {
     const cudaError_t e = cudaGraphLaunch(exec, st);
     if (e == cudaSuccess) {
         std::lock_guard<std::mutex> lk(g_graph_mu);
@@ -166,7 +163,10 @@ static cudaError_t graph_launch(cudaGraphExec_t exec, cudaStream_t st) {
 
 extern "C" long long sllm_cuda_test_kernel_launches(void) { return g_kernel_launches.load(); }
 
-static int* fallback_counter() {
+void sllm::count_launches(long long n) { g_kernel_launches += n; }
+int sllm::force_fallback_flag() { return g_force_fallback; }
+
+int* sllm::fallback_counter() {
     if (g_fallback_counter == nullptr) {
         if (cudaMalloc(&g_fallback_counter, sizeof(int)) != cudaSuccess) { g_fallback_counter = nullptr; return nullptr; }
         if (cudaMemset(g_fallback_counter, 0, sizeof(int)) != cudaSuccess) return nullptr;
@@ -187,7 +187,7 @@ extern "C" int sllm_cuda_test_fallback_count(void) {
 // ---------------------------------------------------------------------------
 // kernel level
 // ---------------------------------------------------------------------------
-static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+bool sllm::aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 extern "C" int sllm_cuda_i2s_quant_act(const float* x, size_t n, int8_t* q_out, sllm_cuda_act* act_out,
                                        void* stream) {
@@ -572,7 +572,7 @@ struct sllm_cuda_ctx {
 };
 
 // the reference's angle recurrence (src/ops.c:529-549), on the host libm
-static void rope_table(int n_ctx, int n_rot, float base, std::vector<float>& cs, std::vector<float>& sn) {
+void sllm::rope_table(int n_ctx, int n_rot, float base, std::vector<float>& cs, std::vector<float>& sn) {
     const int half = n_rot / 2;
     cs.resize((size_t)n_ctx * half);
     sn.resize((size_t)n_ctx * half);

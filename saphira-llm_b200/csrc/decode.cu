@@ -306,6 +306,13 @@ lm_head_kernel(const LmParams p) {
         const int i = *(volatile int*)&p.part_i[b];
         if (better(v, i, bv, bi)) { bv = v; bi = i; }
     }
+    if (p.tp_out != nullptr) {
+        p.tp_out[0] = __float_as_int(bv);
+        p.tp_out[1] = bi == 0x7fffffff ? 0x7fffffff : bi + p.row_base;
+        p.tp_out[2] = isnan(*(volatile const float*)&p.logits[0]) ? 1 : 0;
+        *p.counter = 0;
+        return;
+    }
     // first index of the maximum with '>' (src/forward.c:876-883): a NaN at
     // index 0 wins outright, a NaN elsewhere never does
     int next = bi;

@@ -41,6 +41,12 @@ struct LmParams {
     int n_ctx;
     int* fallback_count;
     int force_fallback;
+    // tensor-parallel vocabulary slice (nullable): rows are global rows
+    // row_base .. row_base + V - 1; the last CTA writes {best value bits,
+    // best global row, isnan(logits[0])} here and leaves the argmax across
+    // slices, the greedy feedback and the position advance to the caller
+    int32_t* tp_out;
+    int row_base;
 };
 
 cudaError_t launch_embed(const uint16_t* tok_embd, const int32_t* tok_seq, const int32_t* pos_ptr, int E, int V,

@@ -1,0 +1,1053 @@
+// tp.cu -- tensor-parallel decode across the GPUs of one node.
+//
+// Megatron-style shards of every layer, one process (or, for tests, one
+// context) per rank r of N:
+//   Q/K/V   rows of this rank's heads (H/N query heads, Hkv/N kv heads)
+//   O       every row, columns [r E/N, (r+1) E/N) of the contraction
+//   gate/up rows [r F/N, (r+1) F/N)
+//   down    every row, columns [r F/N, (r+1) F/N), stored as C chunks of at
+//           most 8192 columns each (a K range of an I2_S row is itself an
+//           I2_S row, so every chunk is an ordinary packed tensor)
+//   head    vocabulary rows [r V/N, (r+1) V/N) of the tied f16 table
+// Per layer and token (src/forward.c:628-801 with the exchange points):
+//   1. attn_norm + GEMV of the local Q/K/V rows, RoPE, KV append, attention
+//      over the local heads                          -> all-gather (f32)
+//   2. attn_sub_norm + quantisation of the whole attention output (every
+//      rank, identical), partial int32 dots of O over the local columns
+//                                                    -> all-reduce (int32 sum)
+//   3. epilogue + residual, ffn_norm + GEMV of the local gate/up rows with
+//      silu(gate) * up                               -> all-gather (f32)
+//   4. ffn_sub_norm + quantisation of all of h, partial int32 dots of down
+//                                                    -> all-reduce (int32 sum)
+//   5. epilogue + residual
+// The head: output_norm + the local vocabulary rows, the slice's argmax
+// -> all-gather, then the first maximum over slices (src/forward.c:876-883).
+//
+// Exactness: the exchanged dots are integers, so their sum is the same in
+// any order; every float operation happens identically on every rank or on
+// the rank that owns the value, in the single-GPU kernels' order. So TP = N
+// gives the bits of TP = 1, which gives the reference's.
+//
+// The exchanges are NCCL collectives on the context's stream, captured with
+// the step's kernels into one CUDA graph. For tests on one GPU, a group of N
+// contexts without a communicator runs the same phases and exchanges through
+// device copies (sllm_cuda_test_tp_generate_group).
+
+#include <chrono>
+#include <dlfcn.h>
+#include <cmath>
+#include <cstring>
+#include <thread>
+#include <type_traits>
+#include <vector>
+
+#include <nccl.h>
+
+#include "backend.cuh"
+#include "common.cuh"
+#include "decode.cuh"
+#include "gemv.cuh"
+#include "../../include/sllm_cuda.h"
+#include "../../include/sllm_cuda_testing.h"
+
+using namespace sllm;
+
+namespace {
+
+// NCCL, resolved at the first tensor-parallel call: the process's own
+// libnccl.so.2 when one is loaded already (a host that also runs a framework
+// with its own NCCL keeps a single copy), else the system's. Nothing links
+// against it, so the library loads where NCCL is absent.
+struct NcclApi {
+    ncclResult_t (*get_unique_id)(ncclUniqueId*);
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int);
+    ncclResult_t (*comm_destroy)(ncclComm_t);
+    ncclResult_t (*comm_abort)(ncclComm_t);
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+    const char* (*error_string)(ncclResult_t);
+};
+
+const NcclApi* nccl() {
+    static NcclApi api;
+    static int state = 0;      // 0 untried, 1 loaded, -1 unavailable
+    if (state != 0) return state > 0 ? &api : nullptr;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (h == nullptr) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (h == nullptr) { state = -1; return nullptr; }
+    bool ok = true;
+    auto sym = [&](auto& fn, const char* name) {
+        fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+        ok = ok && fn != nullptr;
+    };
+    sym(api.get_unique_id, "ncclGetUniqueId");
+    sym(api.comm_init_rank, "ncclCommInitRank");
+    sym(api.comm_destroy, "ncclCommDestroy");
+    sym(api.comm_abort, "ncclCommAbort");
+    sym(api.all_gather, "ncclAllGather");
+    sym(api.all_reduce, "ncclAllReduce");
+    sym(api.error_string, "ncclGetErrorString");
+    state = ok ? 1 : -1;
+    return ok ? &api : nullptr;
+}
+
+const char* nccl_err(ncclResult_t r) { return nccl() ? nccl()->error_string(r) : "NCCL unavailable"; }
+
+constexpr int kHeadDim = 128;
+constexpr int kMaxChunkK = 8192;
+constexpr int kNqThreads = 1024;
+constexpr int kNqKpt = 7;                 // float4 per thread: K <= 28672
+constexpr int kMaxRanks = 8;
+
+// ---------------------------------------------------------------------------
+// kernels
+// ---------------------------------------------------------------------------
+
+// RMSNorm (certified mean, src/ops.c:254-322) + per-token int8 quantisation
+// (src/i2s_gemm.c:45-83) of one vector, q in natural order, one CTA.
+__global__ void __launch_bounds__(kNqThreads)
+tp_norm_quant_kernel(const float* __restrict__ x, const float* __restrict__ w, int K, float eps, double inv_k,
+                     int8_t* __restrict__ q, sllm_cuda_act* act, int* fb, int force) {
+    __shared__ double dred[32];
+    __shared__ float fred[32];
+    __shared__ int ired[32];
+    __shared__ float s_bcast;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K4 = K >> 2;
+    float4 xv[kNqKpt];
+    #pragma unroll
+    for (int j = 0; j < kNqKpt; ++j) {
+        const int i = tid + j * kNqThreads;
+        xv[j] = i < K4 ? reinterpret_cast<const float4*>(x)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+    #pragma unroll
+    for (int j = 0; j < kNqKpt; ++j) {
+        s0 = __dadd_rn(s0, (double)__fmul_rn(xv[j].x, xv[j].x));
+        s1 = __dadd_rn(s1, (double)__fmul_rn(xv[j].y, xv[j].y));
+        s2 = __dadd_rn(s2, (double)__fmul_rn(xv[j].z, xv[j].z));
+        s3 = __dadd_rn(s3, (double)__fmul_rn(xv[j].w, xv[j].w));
+    }
+    double ss = warp_sum_d(__dadd_rn(__dadd_rn(s0, s1), __dadd_rn(s2, s3)));
+    if (lane == 0) dred[warp] = ss;
+    __syncthreads();
+    if (tid == 0) {
+        double S = 0.0;
+        for (int i = 0; i < kNqThreads / 32; ++i) S = __dadd_rn(S, dred[i]);
+        float mean;
+        if (!certify_mean_mul(S, K, inv_k, &mean) || force) {
+            mean = __double2float_rn(__ddiv_rn(rms_ss_reference_order(x, K), (double)K));
+            if (fb != nullptr) atomicAdd(fb, 1);
+        }
+        s_bcast = rms_scale(mean, eps);
+    }
+    __syncthreads();
+    const float sc = s_bcast;
+    float amax = 0.0f;
+    #pragma unroll
+    for (int j = 0; j < kNqKpt; ++j) {
+        const int i = tid + j * kNqThreads;
+        // the norm weight is read here, not held across the reduction (registers)
+        const float4 wv = i < K4 ? __ldg(reinterpret_cast<const float4*>(w) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        xv[j].x = __fmul_rn(__fmul_rn(sc, xv[j].x), wv.x);
+        xv[j].y = __fmul_rn(__fmul_rn(sc, xv[j].y), wv.y);
+        xv[j].z = __fmul_rn(__fmul_rn(sc, xv[j].z), wv.z);
+        xv[j].w = __fmul_rn(__fmul_rn(sc, xv[j].w), wv.w);
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(xv[j].x), fabsf(xv[j].y)), fmaxf(fabsf(xv[j].z), fabsf(xv[j].w))));
+    }
+    amax = warp_max(amax);
+    __syncthreads();
+    if (lane == 0) fred[warp] = amax;
+    __syncthreads();
+    if (tid == 0) {
+        float m = 0.0f;
+        for (int i = 0; i < kNqThreads / 32; ++i) m = fmaxf(m, fred[i]);
+        s_bcast = quant_scale(m);
+    }
+    __syncthreads();
+    const float s = s_bcast;
+    int sum = 0;
+    #pragma unroll
+    for (int j = 0; j < kNqKpt; ++j) {
+        const int i = tid + j * kNqThreads;
+        if (i < K4) {
+            const int a = quant_one(xv[j].x, s), b = quant_one(xv[j].y, s);
+            const int c = quant_one(xv[j].z, s), d = quant_one(xv[j].w, s);
+            sum += (a + b) + (c + d);
+            reinterpret_cast<uint32_t*>(q)[i] = (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) |
+                                                ((uint32_t)(c & 0xff) << 16) | ((uint32_t)d << 24);
+        }
+    }
+    sum = __reduce_add_sync(0xffffffffu, sum);
+    if (lane == 0) ired[warp] = sum;
+    __syncthreads();
+    if (tid == 0) {
+        int total = 0;
+        for (int i = 0; i < kNqThreads / 32; ++i) total += ired[i];
+        act->scale = s;
+        act->sum = total;
+    }
+}
+
+// y[r] = (float)(sum over chunks of dots - act.sum) * (ws / act.scale) + resid[r]
+// (src/forward.c:739-750, 790-801)
+__global__ void tp_epilogue_kernel(const int32_t* __restrict__ dots, int n_chunks, int rows, const sllm_cuda_act* act,
+                                   const float* __restrict__ ws, const float* __restrict__ resid, float* __restrict__ y) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    int d = 0;
+    for (int c = 0; c < n_chunks; ++c) d += dots[(size_t)c * rows + r];
+    const sllm_cuda_act a = *act;
+    const float post = __fdiv_rn(*ws, a.scale);
+    y[r] = __fadd_rn(__fmul_rn(__int2float_rn(d - a.sum), post), resid[r]);
+}
+
+// first maximum over the slices' bests, in rank (= row) order, then the
+// greedy feedback and position advance of the step (as lm_head_kernel)
+__device__ __forceinline__ bool tp_better(float v, int i, float bv, int bi) {
+    if (isnan(v)) return false;
+    if (isnan(bv)) return true;
+    return v > bv || (v == bv && i < bi);
+}
+
+__global__ void tp_finalize_kernel(const int32_t* trip_all, int n_ranks, int32_t* pos_ptr, int32_t* tok_seq,
+                                   const int32_t* prompt_end, int32_t* argmax_out, int32_t* hist, int n_ctx) {
+    float bv = NAN;
+    int bi = 0x7fffffff;
+    for (int r = 0; r < n_ranks; ++r) {
+        const float v = __int_as_float(trip_all[3 * r]);
+        const int i = trip_all[3 * r + 1];
+        if (i != 0x7fffffff && tp_better(v, i, bv, bi)) { bv = v; bi = i; }
+    }
+    int next = bi;
+    if (bi == 0x7fffffff || trip_all[2] != 0) next = 0;   // rank 0 holds row 0
+    *argmax_out = next;
+    const int pos = *pos_ptr;
+    if (pos + 1 >= *prompt_end && pos + 1 < n_ctx) tok_seq[pos + 1] = next;
+    if (hist != nullptr) hist[pos] = next;
+    *pos_ptr = pos + 1;
+}
+
+// element-wise int32 sum of up to kMaxRanks buffers into each of them (the
+// all-reduce of a one-process group)
+struct SumArgs {
+    int32_t* buf[kMaxRanks];
+    int n;
+    size_t count;
+};
+__global__ void tp_group_sum_kernel(SumArgs a) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < a.count; i += (size_t)gridDim.x * blockDim.x) {
+        int s = 0;
+        for (int r = 0; r < a.n; ++r) s += a.buf[r][i];
+        for (int r = 0; r < a.n; ++r) a.buf[r][i] = s;
+    }
+}
+
+// --- seeded synthetic weights, generated on the device -----------------------
+__host__ __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+
+__host__ __device__ __forceinline__ uint64_t tensor_key(uint64_t seed, int layer, int tensor) {
+    return splitmix64(seed ^ splitmix64(((uint64_t)(layer + 1) << 8) | (uint64_t)tensor));
+}
+
+// ternary code {0, 1, 2} (= t + 1) of element (row, col) of a tensor, each
+// value with probability 1/3 up to 2^-32
+__device__ __forceinline__ uint32_t synth_code(uint64_t key, int row, int col) {
+    const uint64_t h = splitmix64(key + (((uint64_t)row << 20) | (uint64_t)col));
+    return (uint32_t)(((h >> 32) * 3ull) >> 32);
+}
+
+__host__ __device__ __forceinline__ float synth_scale(uint64_t key) {
+    return 0.01f + 0.09f * (float)(splitmix64(key ^ 0x5CA1Eull) >> 40) * (1.0f / 16777216.0f);
+}
+
+// rows [row0, row0 + rows) and columns [col0, col0 + cols) of a ternary
+// tensor, packed as I2_S (element 32f + l of a 128-block in byte l at shift
+// 6 - 2f), scale tail after the rows
+__global__ void tp_gen_i2s_kernel(uint8_t* out, uint64_t key, int row0, int rows, int col0, int cols) {
+    const size_t rb = (size_t)cols / 4, total = (size_t)rows * rb;
+    for (size_t b = blockIdx.x * (size_t)blockDim.x + threadIdx.x; b < total; b += (size_t)gridDim.x * blockDim.x) {
+        const int r = (int)(b / rb);
+        const int j = (int)(b % rb);
+        const int blk = j >> 5, l = j & 31;
+        uint32_t byte = 0;
+        #pragma unroll
+        for (int f = 0; f < 4; ++f)
+            byte |= synth_code(key, row0 + r, col0 + blk * 128 + 32 * f + l) << (6 - 2 * f);
+        out[b] = (uint8_t)byte;
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        float* tail = reinterpret_cast<float*>(out + total);
+        tail[0] = synth_scale(key);
+        for (int i = 1; i < 8; ++i) tail[i] = 0.0f;
+    }
+}
+
+__device__ __forceinline__ float synth_normal(uint64_t key, int i) {
+    const uint64_t h = splitmix64(key + (uint64_t)i);
+    const float u1 = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = (float)((h >> 16) & 0xFFFFFFu) * (1.0f / 16777216.0f);
+    return sqrtf(-2.0f * logf(u1)) * cosf(6.283185307f * u2);
+}
+
+__global__ void tp_gen_norm_kernel(float* out, uint64_t key, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        out[i] = 1.0f + 0.02f * synth_normal(key, i);
+}
+
+__global__ void tp_gen_embd_kernel(uint16_t* out, uint64_t key, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = __half_as_ushort(__float2half_rn(0.02f * synth_normal(key, (int)(i & 0x7fffffff)) ));
+}
+
+// ---------------------------------------------------------------------------
+// host structures
+// ---------------------------------------------------------------------------
+struct TpLayer {
+    const uint8_t *wq, *wk, *wv, *wo, *gate, *up;
+    std::vector<const uint8_t*> down;       // chunks of down_k columns
+    const float *attn_norm, *attn_sub_norm, *ffn_norm, *ffn_sub_norm;
+};
+
+int down_chunks(int f_loc) {
+    int c = (f_loc + kMaxChunkK - 1) / kMaxChunkK;
+    while (f_loc % (c * 128) != 0) ++c;
+    return c;
+}
+
+size_t i2s_bytes(int rows, int cols) { return (size_t)rows * (size_t)cols / 4 + 32; }
+size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+}  // namespace
+
+struct sllm_cuda_tp_model {
+    int device = 0, n_ranks = 1, rank = 0;
+    int n_layer = 0, E = 0, F = 0, H = 0, Hkv = 0, V = 0;
+    int hq = 0, hk = 0, e_loc = 0, f_loc = 0, down_c = 1, down_k = 0, v0 = 0, v_loc = 0;
+    float eps = 1e-5f, rope_base = 500000.0f;
+    uint8_t* blob = nullptr;
+    size_t blob_bytes = 0;
+    std::vector<TpLayer> layers;
+    const uint16_t* tok_embd = nullptr;     // [V][E], every rank
+    const float* output_norm = nullptr;
+};
+
+struct sllm_cuda_tp_comm {
+    ncclComm_t comm = nullptr;
+    int n_ranks = 1, rank = 0, device = 0;
+};
+
+struct sllm_cuda_tp_ctx {
+    const sllm_cuda_tp_model* m = nullptr;
+    sllm_cuda_tp_comm* comm = nullptr;
+    int n_ctx = 0, n_past = 0, lm_grid = 0;
+    bool have_logits = false;
+    cudaStream_t stream = nullptr;
+    float *k_cache = nullptr, *v_cache = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    float *x = nullptr, *ffn_inp = nullptr, *q = nullptr, *k = nullptr, *v = nullptr;
+    float *attn_loc = nullptr, *attn_full = nullptr, *h_loc = nullptr, *h_full = nullptr, *logits = nullptr;
+    int8_t *qa = nullptr, *qh = nullptr;
+    sllm_cuda_act *act_a = nullptr, *act_h = nullptr;
+    int32_t *dots_o = nullptr, *dots_d = nullptr;
+    float* part_v = nullptr;
+    int* part_i = nullptr;
+    int* counter = nullptr;
+    int32_t *trip = nullptr, *trip_all = nullptr, *argmax = nullptr, *pos = nullptr, *prompt_end = nullptr;
+    int32_t *tok_seq = nullptr, *hist = nullptr;
+    int32_t* pinned = nullptr;
+    cudaGraphExec_t step = nullptr;
+    std::vector<void*> allocs;
+};
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// model construction
+// ---------------------------------------------------------------------------
+int check_geometry(int n_layer, int E, int F, int H, int Hkv, int V, int n_ranks, int rank) {
+    if (n_layer < 1 || E < 128 || F < 128 || H < 1 || Hkv < 1 || V < 1 || n_ranks < 1 || n_ranks > kMaxRanks ||
+        rank < 0 || rank >= n_ranks)
+        return fail(SLLM_CUDA_ERR_ARG, "tp: bad model geometry or rank");
+    if (E != H * kHeadDim || H % Hkv != 0) return fail(SLLM_CUDA_ERR_UNSUPPORTED, "tp: head dim must be 128");
+    if (H % n_ranks != 0 || Hkv % n_ranks != 0)
+        return fail(SLLM_CUDA_ERR_UNSUPPORTED, "tp: %d ranks do not divide %d q / %d kv heads", n_ranks, H, Hkv);
+    if ((E / n_ranks) % 128 != 0 || (F / n_ranks) % 128 != 0)
+        return fail(SLLM_CUDA_ERR_UNSUPPORTED, "tp: E/N and F/N must be multiples of 128");
+    if (E > kMaxChunkK) return fail(SLLM_CUDA_ERR_UNSUPPORTED, "tp: n_embd above %d", kMaxChunkK);
+    if (F > kNqThreads * kNqKpt * 4) return fail(SLLM_CUDA_ERR_UNSUPPORTED, "tp: n_ff above %d", kNqThreads * kNqKpt * 4);
+    return SLLM_CUDA_OK;
+}
+
+void fill_geometry(sllm_cuda_tp_model* m, int n_layer, int E, int F, int H, int Hkv, int V, int n_ranks, int rank) {
+    m->n_layer = n_layer; m->E = E; m->F = F; m->H = H; m->Hkv = Hkv; m->V = V;
+    m->n_ranks = n_ranks; m->rank = rank;
+    m->hq = H / n_ranks; m->hk = Hkv / n_ranks;
+    m->e_loc = E / n_ranks; m->f_loc = F / n_ranks;
+    m->down_c = down_chunks(m->f_loc);
+    m->down_k = m->f_loc / m->down_c;
+    const int vs = (V + n_ranks - 1) / n_ranks;
+    m->v0 = rank * vs < V ? rank * vs : V;
+    m->v_loc = (m->v0 + vs < V ? m->v0 + vs : V) - m->v0;
+}
+
+// device byte offsets of every tensor of the shard, in one blob
+struct Layout {
+    std::vector<size_t> off;
+    size_t total = 0;
+    size_t add(size_t bytes) {
+        off.push_back(total);
+        total += align256(bytes);
+        return off.back();
+    }
+};
+
+// order per layer: wq, wk, wv, wo, gate, up, down[C], 4 norms; then embd, output_norm
+Layout shard_layout(const sllm_cuda_tp_model* m) {
+    Layout L;
+    const int D = kHeadDim;
+    for (int l = 0; l < m->n_layer; ++l) {
+        L.add(i2s_bytes(m->hq * D, m->E));
+        L.add(i2s_bytes(m->hk * D, m->E));
+        L.add(i2s_bytes(m->hk * D, m->E));
+        L.add(i2s_bytes(m->E, m->e_loc));
+        L.add(i2s_bytes(m->f_loc, m->E));
+        L.add(i2s_bytes(m->f_loc, m->E));
+        for (int c = 0; c < m->down_c; ++c) L.add(i2s_bytes(m->E, m->down_k));
+        L.add((size_t)m->E * 4);
+        L.add((size_t)m->E * 4);
+        L.add((size_t)m->E * 4);
+        L.add((size_t)m->F * 4);
+    }
+    L.add((size_t)m->V * m->E * 2);
+    L.add((size_t)m->E * 4);
+    return L;
+}
+
+void bind_pointers(sllm_cuda_tp_model* m, const Layout& L) {
+    size_t i = 0;
+    auto P = [&](void) { return m->blob + L.off[i++]; };
+    m->layers.resize(m->n_layer);
+    for (int l = 0; l < m->n_layer; ++l) {
+        TpLayer& t = m->layers[l];
+        t.wq = P(); t.wk = P(); t.wv = P(); t.wo = P(); t.gate = P(); t.up = P();
+        t.down.resize(m->down_c);
+        for (int c = 0; c < m->down_c; ++c) t.down[c] = P();
+        t.attn_norm = reinterpret_cast<const float*>(P());
+        t.attn_sub_norm = reinterpret_cast<const float*>(P());
+        t.ffn_norm = reinterpret_cast<const float*>(P());
+        t.ffn_sub_norm = reinterpret_cast<const float*>(P());
+    }
+    m->tok_embd = reinterpret_cast<const uint16_t*>(P());
+    m->output_norm = reinterpret_cast<const float*>(P());
+}
+
+// host tensor rows [r0, r0 + rows) x columns [c0, c0 + cols) of an I2_S
+// tensor of `ncols` columns, with its scale tail, into a packed buffer
+void slice_i2s(const uint8_t* src, int src_rows, int ncols, int r0, int rows, int c0, int cols, std::vector<uint8_t>& out) {
+    const size_t srb = (size_t)ncols / 4, drb = (size_t)cols / 4;
+    out.assign(i2s_bytes(rows, cols), 0);
+    for (int r = 0; r < rows; ++r) memcpy(out.data() + (size_t)r * drb, src + (size_t)(r0 + r) * srb + c0 / 4, drb);
+    memcpy(out.data() + (size_t)rows * drb, src + (size_t)src_rows * srb, 4);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" int sllm_cuda_tp_unique_id(uint8_t* id_out) {
+    if (id_out == nullptr) return fail(SLLM_CUDA_ERR_ARG, "tp_unique_id: null");
+    if (nccl() == nullptr) return fail(SLLM_CUDA_ERR_UNSUPPORTED, "tp_unique_id: libnccl.so.2 not found");
+    ncclUniqueId id;
+    if (nccl()->get_unique_id(&id) != ncclSuccess) return fail(SLLM_CUDA_ERR_COMM, "ncclGetUniqueId failed");
+    static_assert(sizeof(id) == SLLM_CUDA_TP_ID_BYTES, "NCCL unique id size");
+    memcpy(id_out, &id, sizeof(id));
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_tp_comm_init(const uint8_t* id, int32_t n_ranks, int32_t rank, int32_t device,
+                                      sllm_cuda_tp_comm** out) {
+    if (id == nullptr || out == nullptr || n_ranks < 1 || n_ranks > kMaxRanks || rank < 0 || rank >= n_ranks)
+        return fail(SLLM_CUDA_ERR_ARG, "tp_comm_init: bad arguments");
+    *out = nullptr;
+    if (nccl() == nullptr) return fail(SLLM_CUDA_ERR_UNSUPPORTED, "tp_comm_init: libnccl.so.2 not found");
+    CK(cudaSetDevice(device), "cudaSetDevice");
+    ncclUniqueId uid;
+    memcpy(&uid, id, sizeof(uid));
+    auto* c = new sllm_cuda_tp_comm();
+    c->n_ranks = n_ranks; c->rank = rank; c->device = device;
+    const ncclResult_t r = nccl()->comm_init_rank(&c->comm, n_ranks, uid, rank);
+    if (r != ncclSuccess) {
+        delete c;
+        return fail(SLLM_CUDA_ERR_COMM, "ncclCommInitRank: %s", nccl_err(r));
+    }
+    *out = c;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" void sllm_cuda_tp_comm_free(sllm_cuda_tp_comm* c) {
+    if (c == nullptr) return;
+    cudaSetDevice(c->device);
+    if (c->comm != nullptr && nccl() != nullptr) nccl()->comm_destroy(c->comm);
+    delete c;
+}
+
+static int tp_model_alloc(sllm_cuda_tp_model* m, int device) {
+    m->device = device;
+    const Layout L = shard_layout(m);
+    m->blob_bytes = L.total;
+    CK(cudaSetDevice(device), "cudaSetDevice");
+    CK(cudaMalloc(&m->blob, L.total), "tp model blob");
+    bind_pointers(m, L);
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_tp_model_upload(const sllm_cuda_model_desc* d, int32_t n_ranks, int32_t rank, int32_t device,
+                                         sllm_cuda_tp_model** out) {
+    if (d == nullptr || out == nullptr || d->layers == nullptr || d->tok_embd == nullptr || d->output_norm == nullptr)
+        return fail(SLLM_CUDA_ERR_ARG, "tp_model_upload: bad arguments");
+    *out = nullptr;
+    int rc = check_geometry(d->n_layer, d->n_embd, d->n_ff, d->n_head, d->n_head_kv, d->n_vocab, n_ranks, rank);
+    if (rc != SLLM_CUDA_OK) return rc;
+    if (d->n_rot != kHeadDim) return fail(SLLM_CUDA_ERR_UNSUPPORTED, "tp_model_upload: n_rot must be 128");
+    auto* m = new sllm_cuda_tp_model();
+    fill_geometry(m, d->n_layer, d->n_embd, d->n_ff, d->n_head, d->n_head_kv, d->n_vocab, n_ranks, rank);
+    m->eps = d->f_rms_eps;
+    m->rope_base = d->rope_freq_base;
+    rc = tp_model_alloc(m, device);
+    if (rc != SLLM_CUDA_OK) { delete m; return rc; }
+    const int E = m->E, F = m->F, D = kHeadDim, G = m->Hkv * D;
+    std::vector<uint8_t> buf;
+    auto put = [&](const void* dst, const void* src, size_t n) {
+        return cudaMemcpy(const_cast<void*>(dst), src, n, cudaMemcpyHostToDevice);
+    };
+    cudaError_t e = cudaSuccess;
+    for (int l = 0; l < m->n_layer && e == cudaSuccess; ++l) {
+        const sllm_cuda_layer_desc& h = d->layers[l];
+        const TpLayer& t = m->layers[l];
+        slice_i2s(h.wq, E, E, rank * m->hq * D, m->hq * D, 0, E, buf); e = put(t.wq, buf.data(), buf.size());
+        slice_i2s(h.wk, G, E, rank * m->hk * D, m->hk * D, 0, E, buf); if (!e) e = put(t.wk, buf.data(), buf.size());
+        slice_i2s(h.wv, G, E, rank * m->hk * D, m->hk * D, 0, E, buf); if (!e) e = put(t.wv, buf.data(), buf.size());
+        slice_i2s(h.wo, E, E, 0, E, rank * m->e_loc, m->e_loc, buf); if (!e) e = put(t.wo, buf.data(), buf.size());
+        slice_i2s(h.ffn_gate, F, E, rank * m->f_loc, m->f_loc, 0, E, buf); if (!e) e = put(t.gate, buf.data(), buf.size());
+        slice_i2s(h.ffn_up, F, E, rank * m->f_loc, m->f_loc, 0, E, buf); if (!e) e = put(t.up, buf.data(), buf.size());
+        for (int c = 0; c < m->down_c && !e; ++c) {
+            slice_i2s(h.ffn_down, E, F, 0, E, rank * m->f_loc + c * m->down_k, m->down_k, buf);
+            e = put(t.down[c], buf.data(), buf.size());
+        }
+        if (!e) e = put(t.attn_norm, h.attn_norm, (size_t)E * 4);
+        if (!e) e = put(t.attn_sub_norm, h.attn_sub_norm, (size_t)E * 4);
+        if (!e) e = put(t.ffn_norm, h.ffn_norm, (size_t)E * 4);
+        if (!e) e = put(t.ffn_sub_norm, h.ffn_sub_norm, (size_t)F * 4);
+    }
+    if (!e) e = put(m->tok_embd, d->tok_embd, (size_t)m->V * E * 2);
+    if (!e) e = put(m->output_norm, d->output_norm, (size_t)E * 4);
+    if (e != cudaSuccess) {
+        cudaFree(m->blob);
+        delete m;
+        return cuda_fail(e, "tp_model_upload");
+    }
+    *out = m;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_tp_model_synth(const sllm_cuda_tp_synth_desc* d, int32_t n_ranks, int32_t rank,
+                                        int32_t device, sllm_cuda_tp_model** out) {
+    if (d == nullptr || out == nullptr) return fail(SLLM_CUDA_ERR_ARG, "tp_model_synth: bad arguments");
+    *out = nullptr;
+    int rc = check_geometry(d->n_layer, d->n_embd, d->n_ff, d->n_head, d->n_head_kv, d->n_vocab, n_ranks, rank);
+    if (rc != SLLM_CUDA_OK) return rc;
+    auto* m = new sllm_cuda_tp_model();
+    fill_geometry(m, d->n_layer, d->n_embd, d->n_ff, d->n_head, d->n_head_kv, d->n_vocab, n_ranks, rank);
+    m->eps = d->f_rms_eps;
+    m->rope_base = d->rope_freq_base;
+    rc = tp_model_alloc(m, device);
+    if (rc != SLLM_CUDA_OK) { delete m; return rc; }
+    const int E = m->E, D = kHeadDim, grid = 4 * num_sms_of(device), blk = 256;
+    const uint64_t seed = d->seed;
+    for (int l = 0; l < m->n_layer; ++l) {
+        const TpLayer& t = m->layers[l];
+        auto gen = [&](const uint8_t* dst, int tensor, int r0, int rows, int c0, int cols) {
+            tp_gen_i2s_kernel<<<grid, blk>>>(const_cast<uint8_t*>(dst), tensor_key(seed, l, tensor), r0, rows, c0, cols);
+        };
+        gen(t.wq, 0, rank * m->hq * D, m->hq * D, 0, E);
+        gen(t.wk, 1, rank * m->hk * D, m->hk * D, 0, E);
+        gen(t.wv, 2, rank * m->hk * D, m->hk * D, 0, E);
+        gen(t.wo, 3, 0, E, rank * m->e_loc, m->e_loc);
+        gen(t.gate, 4, rank * m->f_loc, m->f_loc, 0, E);
+        gen(t.up, 5, rank * m->f_loc, m->f_loc, 0, E);
+        for (int c = 0; c < m->down_c; ++c) gen(t.down[c], 6, 0, E, rank * m->f_loc + c * m->down_k, m->down_k);
+        tp_gen_norm_kernel<<<grid, blk>>>(const_cast<float*>(t.attn_norm), tensor_key(seed, l, 8), E);
+        tp_gen_norm_kernel<<<grid, blk>>>(const_cast<float*>(t.attn_sub_norm), tensor_key(seed, l, 9), E);
+        tp_gen_norm_kernel<<<grid, blk>>>(const_cast<float*>(t.ffn_norm), tensor_key(seed, l, 10), E);
+        tp_gen_norm_kernel<<<grid, blk>>>(const_cast<float*>(t.ffn_sub_norm), tensor_key(seed, l, 11), m->F);
+    }
+    tp_gen_embd_kernel<<<grid, blk>>>(const_cast<uint16_t*>(m->tok_embd), tensor_key(seed, -1, 12), (size_t)m->V * E);
+    tp_gen_norm_kernel<<<grid, blk>>>(const_cast<float*>(m->output_norm), tensor_key(seed, -1, 13), E);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        cudaFree(m->blob);
+        delete m;
+        return cuda_fail(e, "tp_model_synth");
+    }
+    *out = m;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" void sllm_cuda_tp_model_free(sllm_cuda_tp_model* m) {
+    if (m == nullptr) return;
+    cudaSetDevice(m->device);
+    cudaFree(m->blob);
+    delete m;
+}
+
+extern "C" size_t sllm_cuda_tp_model_bytes(const sllm_cuda_tp_model* m) { return m ? m->blob_bytes : 0; }
+
+// ---------------------------------------------------------------------------
+// context and the decode step
+// ---------------------------------------------------------------------------
+namespace {
+
+template <class T>
+cudaError_t ctx_alloc(sllm_cuda_tp_ctx* c, T** p, size_t count) {
+    void* v = nullptr;
+    const cudaError_t e = cudaMalloc(&v, align256(count * sizeof(T)));
+    if (e == cudaSuccess) {
+        c->allocs.push_back(v);
+        *p = static_cast<T*>(v);
+    }
+    return e;
+}
+
+// The exchange after a phase: NCCL on the context's stream, or, for a
+// one-process group, device copies across the group's contexts.
+enum Xchg { X_ATTN = 0, X_DOTS_O, X_H, X_DOTS_D, X_ARGMAX };
+
+void xchg_counts(const sllm_cuda_tp_model* m, int which, size_t* count, bool* gather) {
+    switch (which) {
+        case X_ATTN: *count = (size_t)m->hq * kHeadDim; *gather = true; break;
+        case X_DOTS_O: *count = (size_t)m->E; *gather = false; break;
+        case X_H: *count = (size_t)m->f_loc; *gather = true; break;
+        case X_DOTS_D: *count = (size_t)m->E * m->down_c; *gather = false; break;
+        default: *count = 3; *gather = true; break;
+    }
+}
+
+void xchg_buffers(sllm_cuda_tp_ctx* c, int which, void** src, void** dst) {
+    switch (which) {
+        case X_ATTN: *src = c->attn_loc; *dst = c->attn_full; break;
+        case X_DOTS_O: *src = c->dots_o; *dst = c->dots_o; break;
+        case X_H: *src = c->h_loc; *dst = c->h_full; break;
+        case X_DOTS_D: *src = c->dots_d; *dst = c->dots_d; break;
+        default: *src = c->trip; *dst = c->trip_all; break;
+    }
+}
+
+cudaError_t xchg_nccl(sllm_cuda_tp_ctx* c, int which, cudaStream_t st, ncclResult_t* nr) {
+    size_t count;
+    bool gather;
+    void *src, *dst;
+    xchg_counts(c->m, which, &count, &gather);
+    xchg_buffers(c, which, &src, &dst);
+    if (c->m->n_ranks == 1) {
+        if (gather && src != dst) return cudaMemcpyAsync(dst, src, count * 4, cudaMemcpyDeviceToDevice, st);
+        return cudaSuccess;
+    }
+    if (gather) {
+        *nr = nccl()->all_gather(src, dst, count, which == X_ARGMAX ? ncclInt32 : ncclFloat32, c->comm->comm, st);
+    } else {
+        *nr = nccl()->all_reduce(src, dst, count, ncclInt32, ncclSum, c->comm->comm, st);
+    }
+    return *nr == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
+}
+
+cudaError_t xchg_group(sllm_cuda_tp_ctx** cs, int n, int which, cudaStream_t st) {
+    size_t count;
+    bool gather;
+    xchg_counts(cs[0]->m, which, &count, &gather);
+    if (gather) {
+        for (int r = 0; r < n; ++r) {
+            void *dst, *unused;
+            xchg_buffers(cs[r], which, &unused, &dst);
+            for (int s = 0; s < n; ++s) {
+                void *src, *unused2;
+                xchg_buffers(cs[s], which, &src, &unused2);
+                const cudaError_t e = cudaMemcpyAsync(static_cast<char*>(dst) + (size_t)s * count * 4, src, count * 4,
+                                                      cudaMemcpyDeviceToDevice, st);
+                if (e != cudaSuccess) return e;
+            }
+        }
+        return cudaSuccess;
+    }
+    SumArgs a{};
+    a.n = n;
+    a.count = count;
+    for (int r = 0; r < n; ++r) {
+        void *src, *dst;
+        xchg_buffers(cs[r], which, &src, &dst);
+        a.buf[r] = static_cast<int32_t*>(dst);
+    }
+    tp_group_sum_kernel<<<64, 256, 0, st>>>(a);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+// phases of the step: 0 = embedding; per layer l: 1 + 4l + {0: Q/K/V +
+// attention, 1: O dots, 2: residual + gate/up, 3: down dots}; then the
+// residual of the last layer + the head; then the finalize. The exchange
+// after each phase is given by phase_xchg (-1: none).
+int n_phases(const sllm_cuda_tp_model* m) { return 1 + 4 * m->n_layer + 2; }
+
+int phase_xchg(const sllm_cuda_tp_model* m, int ph) {
+    if (ph == 0 || ph == n_phases(m) - 1) return -1;
+    if (ph == n_phases(m) - 2) return X_ARGMAX;
+    return (ph - 1) % 4;     // X_ATTN, X_DOTS_O, X_H, X_DOTS_D in order
+}
+
+cudaError_t launch_count(cudaError_t e, int n) {
+    if (e == cudaSuccess) count_launches(n);
+    return e;
+}
+
+cudaError_t enqueue_phase(sllm_cuda_tp_ctx* c, int ph, cudaStream_t st, bool counted) {
+    const sllm_cuda_tp_model* m = c->m;
+    const int E = m->E, D = kHeadDim, sms = num_sms_of(m->device);
+    int* fb = fallback_counter();
+    const int force = force_fallback_flag();
+    const int cnt = counted ? 1 : 0;
+    auto epi = [&](const int32_t* dots, int chunks, const sllm_cuda_act* act, const uint8_t* w, int rows, int cols,
+                   const float* resid, float* y) {
+        const float* ws = reinterpret_cast<const float*>(w + (size_t)rows * cols / 4);
+        tp_epilogue_kernel<<<(rows + 255) / 256, 256, 0, st>>>(dots, chunks, rows, act, ws, resid, y);
+        return launch_count(cudaGetLastError(), cnt);
+    };
+    if (ph == 0) return launch_count(launch_embed(m->tok_embd, c->tok_seq, c->pos, E, m->V, c->x, st), cnt);
+    if (ph == n_phases(m) - 1) {
+        tp_finalize_kernel<<<1, 1, 0, st>>>(c->trip_all, m->n_ranks, c->pos, c->tok_seq, c->prompt_end, c->argmax,
+                                            c->hist, c->n_ctx);
+        return launch_count(cudaGetLastError(), cnt);
+    }
+    if (ph == n_phases(m) - 2) {
+        const TpLayer& t = m->layers[m->n_layer - 1];
+        cudaError_t e = epi(c->dots_d, m->down_c, c->act_h, t.down[0], E, m->down_k, c->ffn_inp, c->x);
+        if (e != cudaSuccess) return e;
+        LmParams lp{};
+        lp.x = c->x; lp.norm_w = m->output_norm; lp.eps = m->eps;
+        lp.embd = m->tok_embd + (size_t)m->v0 * E;
+        lp.E = E; lp.V = m->v_loc; lp.logits = c->logits;
+        lp.part_v = c->part_v; lp.part_i = c->part_i; lp.counter = c->counter; lp.argmax_out = c->argmax;
+        lp.pos_ptr = c->pos; lp.tok_seq = c->tok_seq; lp.prompt_end = c->prompt_end; lp.argmax_hist = nullptr;
+        lp.n_ctx = c->n_ctx; lp.fallback_count = fb; lp.force_fallback = force;
+        lp.tp_out = c->trip; lp.row_base = m->v0;
+        return launch_count(launch_lm_head(lp, c->lm_grid, st), cnt);
+    }
+    const int l = (ph - 1) / 4, sub = (ph - 1) % 4;
+    const TpLayer& t = m->layers[l];
+    GemvParams p{};
+    p.eps = m->eps;
+    p.fallback_count = fb;
+    p.force_fallback = force;
+    if (sub == 0) {
+        if (l > 0) {
+            // the residual of the previous layer's down projection
+            const TpLayer& tp = m->layers[l - 1];
+            cudaError_t e = epi(c->dots_d, m->down_c, c->act_h, tp.down[0], E, m->down_k, c->ffn_inp, c->x);
+            if (e != cudaSuccess) return e;
+        }
+        // attn_norm -> local Q, K, V (src/forward.c:631-666)
+        p.K = E; p.nseg = 3;
+        p.seg[0] = GemvSeg{t.wq, m->hq * D, c->q, nullptr};
+        p.seg[1] = GemvSeg{t.wk, m->hk * D, c->k, nullptr};
+        p.seg[2] = GemvSeg{t.wv, m->hk * D, c->v, nullptr};
+        p.x = c->x; p.norm_w = t.attn_norm;
+        cudaError_t e = launch_count(launch_gemv(p, PRO_NORM, EPI_F32, sms, st), cnt);
+        if (e != cudaSuccess) return e;
+        const size_t kv_layer = (size_t)m->hk * D * (size_t)c->n_ctx;
+        AttnParams ap{};
+        ap.q = c->q; ap.k = c->k; ap.v = c->v;
+        ap.k_cache = c->k_cache + (size_t)l * kv_layer;
+        ap.v_cache = c->v_cache + (size_t)l * kv_layer;
+        ap.rope_cos = c->rope_cos; ap.rope_sin = c->rope_sin;
+        ap.pos_ptr = c->pos; ap.out = c->attn_loc; ap.n_ctx = c->n_ctx;
+        ap.group = m->hq / m->hk;
+        ap.attn_scale = 1.0f / sqrtf((float)D);
+        ap.fallback_count = fb; ap.force_fallback = force;
+        return launch_count(launch_attention(ap, m->hq, st), cnt);
+    }
+    if (sub == 1) {
+        // attn_sub_norm + quantisation of the whole attention output, then
+        // this rank's columns of O (src/forward.c:728-741)
+        tp_norm_quant_kernel<<<1, kNqThreads, 0, st>>>(c->attn_full, t.attn_sub_norm, E, m->eps, 1.0 / (double)E,
+                                                       c->qa, c->act_a, fb, force);
+        cudaError_t e = launch_count(cudaGetLastError(), cnt);
+        if (e != cudaSuccess) return e;
+        p.K = m->e_loc; p.nseg = 1;
+        p.seg[0] = GemvSeg{t.wo, E, nullptr, c->dots_o};
+        p.q_in = c->qa + (size_t)m->rank * m->e_loc;
+        p.act_in = c->act_a;
+        return launch_count(launch_gemv(p, PRO_Q8, EPI_DOTS, sms, st), cnt);
+    }
+    if (sub == 2) {
+        // O epilogue + residual, then ffn_norm -> local gate, up -> h (src/forward.c:742-779)
+        cudaError_t e = epi(c->dots_o, 1, c->act_a, t.wo, E, m->e_loc, c->x, c->ffn_inp);
+        if (e != cudaSuccess) return e;
+        p.K = E; p.nseg = 2;
+        p.seg[0] = GemvSeg{t.gate, m->f_loc, nullptr, nullptr};
+        p.seg[1] = GemvSeg{t.up, m->f_loc, nullptr, nullptr};
+        p.x = c->ffn_inp; p.norm_w = t.ffn_norm; p.h_out = c->h_loc;
+        return launch_count(launch_gemv(p, PRO_NORM, EPI_SILU, sms, st), cnt);
+    }
+    // ffn_sub_norm + quantisation of all of h, then this rank's columns of
+    // down, chunk by chunk (src/forward.c:781-792)
+    tp_norm_quant_kernel<<<1, kNqThreads, 0, st>>>(c->h_full, t.ffn_sub_norm, m->F, m->eps, 1.0 / (double)m->F,
+                                                   c->qh, c->act_h, fb, force);
+    cudaError_t e = launch_count(cudaGetLastError(), cnt);
+    for (int ch = 0; ch < m->down_c && e == cudaSuccess; ++ch) {
+        GemvParams d = p;
+        d.K = m->down_k; d.nseg = 1;
+        d.seg[0] = GemvSeg{t.down[ch], E, nullptr, c->dots_d + (size_t)ch * E};
+        d.q_in = c->qh + (size_t)m->rank * m->f_loc + (size_t)ch * m->down_k;
+        d.act_in = c->act_h;
+        e = launch_count(launch_gemv(d, PRO_Q8, EPI_DOTS, sms, st), cnt);
+    }
+    return e;
+}
+
+int ensure_tp_graph(sllm_cuda_tp_ctx* c) {
+    if (c->step != nullptr) return SLLM_CUDA_OK;
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    cudaError_t e = cudaSuccess;
+    ncclResult_t nr = ncclSuccess;
+    for (int ph = 0; ph < n_phases(c->m) && e == cudaSuccess; ++ph) {
+        e = enqueue_phase(c, ph, c->stream, false);
+        const int x = phase_xchg(c->m, ph);
+        if (e == cudaSuccess && x >= 0) e = xchg_nccl(c, x, c->stream, &nr);
+    }
+    const cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
+    if (nr != ncclSuccess) { if (g) cudaGraphDestroy(g); return fail(SLLM_CUDA_ERR_COMM, "tp step: %s", nccl_err(nr)); }
+    if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); return cuda_fail(e, "capture tp step"); }
+    if (e2 != cudaSuccess) return cuda_fail(e2, "end capture");
+    e = instantiate(&c->step, g);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) { c->step = nullptr; return cuda_fail(e, "instantiate tp step"); }
+    return SLLM_CUDA_OK;
+}
+
+// wait for the stream, bounded: a rank whose peers stopped answering aborts
+// its communicator instead of waiting for good
+int tp_sync(sllm_cuda_tp_ctx* c, double seconds) {
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        const cudaError_t e = cudaStreamQuery(c->stream);
+        if (e == cudaSuccess) return SLLM_CUDA_OK;
+        if (e != cudaErrorNotReady) return cuda_fail(e, "tp step");
+        if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > seconds) {
+            if (c->comm != nullptr && c->comm->comm != nullptr) {
+                nccl()->comm_abort(c->comm->comm);
+                c->comm->comm = nullptr;
+            }
+            return fail(SLLM_CUDA_ERR_TIMEOUT, "tp step: no progress in %.0f s (communicator aborted)", seconds);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+int tp_validate(const sllm_cuda_tp_ctx* c, const int32_t* prompt, int32_t n_prompt, int32_t n_new, int32_t* out) {
+    if (c == nullptr || out == nullptr || n_prompt < 0 || n_new < 0 || (n_prompt > 0 && prompt == nullptr))
+        return fail(SLLM_CUDA_ERR_ARG, "tp_generate_greedy: bad arguments");
+    if ((int64_t)n_prompt + n_new + c->n_past > c->n_ctx)
+        return fail(SLLM_CUDA_ERR_TOO_LARGE, "tp_generate_greedy: %d + %d tokens after %d exceed n_ctx %d", n_prompt,
+                    n_new, c->n_past, c->n_ctx);
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= c->m->V) return fail(SLLM_CUDA_ERR_ARG, "tp_generate_greedy: token %d out of range", prompt[i]);
+    if (n_prompt == 0 && c->n_past == 0 && n_new > 0 && 128000 >= c->m->V)
+        return fail(SLLM_CUDA_ERR_ARG, "tp_generate_greedy: BOS 128000 outside the vocabulary");
+    return SLLM_CUDA_OK;
+}
+
+// the prompt (or BOS, src/forward.c:909) and the step's position registers
+int tp_seed(sllm_cuda_tp_ctx* c, const int32_t* prompt, int32_t n_prompt) {
+    const int base = c->n_past;
+    if (n_prompt == 0 && base == 0) {
+        c->pinned[2] = 128000;
+        CK(cudaMemcpyAsync(c->tok_seq, &c->pinned[2], 4, cudaMemcpyHostToDevice, c->stream), "bos");
+    } else if (n_prompt > 0) {
+        CK(cudaMemcpyAsync(c->tok_seq + base, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, c->stream), "prompt");
+    }
+    c->pinned[0] = base;
+    c->pinned[1] = base + n_prompt;
+    CK(cudaMemcpyAsync(c->pos, &c->pinned[0], 4, cudaMemcpyHostToDevice, c->stream), "set pos");
+    CK(cudaMemcpyAsync(c->prompt_end, &c->pinned[1], 4, cudaMemcpyHostToDevice, c->stream), "set prompt end");
+    return SLLM_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" int sllm_cuda_tp_ctx_new(const sllm_cuda_tp_model* m, sllm_cuda_tp_comm* comm, int32_t n_ctx,
+                                    sllm_cuda_tp_ctx** out) {
+    if (m == nullptr || out == nullptr || n_ctx < 1 || n_ctx > attention_max_ctx())
+        return fail(SLLM_CUDA_ERR_ARG, "tp_ctx_new: bad arguments");
+    *out = nullptr;
+    if (comm != nullptr && (comm->n_ranks != m->n_ranks || comm->rank != m->rank || comm->device != m->device))
+        return fail(SLLM_CUDA_ERR_ARG, "tp_ctx_new: the communicator's rank does not match the shard's");
+    CK(cudaSetDevice(m->device), "cudaSetDevice");
+    CK(prepare_decode_kernels(), "decode kernel attributes");
+    if (fallback_counter() == nullptr) return fail(SLLM_CUDA_ERR_NOMEM, "tp_ctx_new: diagnostics counter");
+    auto* c = new sllm_cuda_tp_ctx();
+    c->m = m;
+    c->comm = comm;
+    c->n_ctx = n_ctx;
+    c->lm_grid = lm_head_grid(num_sms_of(m->device));
+    const int D = kHeadDim, E = m->E;
+    const size_t kv = (size_t)m->n_layer * m->hk * D * n_ctx;
+    cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (!e) e = ctx_alloc(c, &c->k_cache, kv);
+    if (!e) e = ctx_alloc(c, &c->v_cache, kv);
+    if (!e) e = ctx_alloc(c, &c->rope_cos, (size_t)n_ctx * D / 2);
+    if (!e) e = ctx_alloc(c, &c->rope_sin, (size_t)n_ctx * D / 2);
+    if (!e) e = ctx_alloc(c, &c->x, E);
+    if (!e) e = ctx_alloc(c, &c->ffn_inp, E);
+    if (!e) e = ctx_alloc(c, &c->q, (size_t)m->hq * D);
+    if (!e) e = ctx_alloc(c, &c->k, (size_t)m->hk * D);
+    if (!e) e = ctx_alloc(c, &c->v, (size_t)m->hk * D);
+    if (!e) e = ctx_alloc(c, &c->attn_loc, (size_t)m->hq * D);
+    if (!e) e = ctx_alloc(c, &c->attn_full, E);
+    if (!e) e = ctx_alloc(c, &c->h_loc, (size_t)m->f_loc);
+    if (!e) e = ctx_alloc(c, &c->h_full, (size_t)m->F);
+    if (!e) e = ctx_alloc(c, &c->logits, (size_t)(m->v_loc > 0 ? m->v_loc : 1));
+    if (!e) e = ctx_alloc(c, &c->qa, E);
+    if (!e) e = ctx_alloc(c, &c->qh, (size_t)m->F);
+    if (!e) e = ctx_alloc(c, &c->act_a, 1);
+    if (!e) e = ctx_alloc(c, &c->act_h, 1);
+    if (!e) e = ctx_alloc(c, &c->dots_o, E);
+    if (!e) e = ctx_alloc(c, &c->dots_d, (size_t)E * m->down_c);
+    if (!e) e = ctx_alloc(c, &c->part_v, c->lm_grid);
+    if (!e) e = ctx_alloc(c, &c->part_i, c->lm_grid);
+    if (!e) e = ctx_alloc(c, &c->counter, 1);
+    if (!e) e = ctx_alloc(c, &c->trip, 3);
+    if (!e) e = ctx_alloc(c, &c->trip_all, (size_t)3 * m->n_ranks);
+    if (!e) e = ctx_alloc(c, &c->argmax, 1);
+    if (!e) e = ctx_alloc(c, &c->pos, 1);
+    if (!e) e = ctx_alloc(c, &c->prompt_end, 1);
+    if (!e) e = ctx_alloc(c, &c->tok_seq, (size_t)n_ctx);
+    if (!e) e = ctx_alloc(c, &c->hist, (size_t)n_ctx);
+    if (!e) e = cudaMallocHost(&c->pinned, 16);
+    if (!e) e = cudaMemset(c->counter, 0, 4);
+    if (!e) e = cudaMemset(c->tok_seq, 0, (size_t)n_ctx * 4);
+    if (!e) {
+        std::vector<float> cs, sn;
+        rope_table(n_ctx, D, m->rope_base, cs, sn);
+        e = cudaMemcpy(c->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+        if (!e) e = cudaMemcpy(c->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+    }
+    if (e != cudaSuccess) {
+        sllm_cuda_tp_ctx_free(c);
+        return cuda_fail(e, "tp_ctx_new");
+    }
+    *out = c;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" void sllm_cuda_tp_ctx_free(sllm_cuda_tp_ctx* c) {
+    if (c == nullptr) return;
+    cudaSetDevice(c->m->device);
+    graph_exec_destroy(c->step);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    for (void* p : c->allocs) cudaFree(p);
+    if (c->pinned) cudaFreeHost(c->pinned);
+    delete c;
+}
+
+extern "C" int sllm_cuda_tp_generate_greedy(sllm_cuda_tp_ctx* c, const int32_t* prompt, int32_t n_prompt,
+                                            int32_t n_new, int32_t* out) {
+    int rc = tp_validate(c, prompt, n_prompt, n_new, out);
+    if (rc != SLLM_CUDA_OK) return rc;
+    if (n_prompt == 0 && c->n_past == 0 && n_new == 0) return SLLM_CUDA_OK;
+    CK(cudaSetDevice(c->m->device), "cudaSetDevice");
+    if (c->m->n_ranks > 1 && (c->comm == nullptr || c->comm->comm == nullptr))
+        return fail(SLLM_CUDA_ERR_COMM, "tp_generate_greedy: no communicator");
+    rc = ensure_tp_graph(c);
+    if (rc != SLLM_CUDA_OK) return rc;
+    const int base = c->n_past;
+    rc = tp_seed(c, prompt, n_prompt);
+    if (rc != SLLM_CUDA_OK) return rc;
+    const int steps = n_prompt + n_new;
+    for (int s = 0; s < steps; ++s) CK(graph_launch(c->step, c->stream), "tp step");
+    if (n_new > 0)
+        CK(cudaMemcpyAsync(out, c->tok_seq + base + n_prompt, (size_t)n_new * 4, cudaMemcpyDeviceToHost, c->stream), "ids");
+    rc = tp_sync(c, 120.0);
+    if (rc != SLLM_CUDA_OK) return rc;
+    c->n_past = base + steps;
+    c->have_logits = steps > 0;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_tp_ctx_reset(sllm_cuda_tp_ctx* c) {
+    if (c == nullptr) return fail(SLLM_CUDA_ERR_ARG, "tp_ctx_reset: null");
+    c->n_past = 0;
+    c->have_logits = false;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_tp_vocab_range(const sllm_cuda_tp_model* m, int32_t* v0, int32_t* n) {
+    if (m == nullptr || v0 == nullptr || n == nullptr) return fail(SLLM_CUDA_ERR_ARG, "tp_vocab_range: null");
+    *v0 = m->v0;
+    *n = m->v_loc;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_tp_last_logits(const sllm_cuda_tp_ctx* c, float* host_out) {
+    if (c == nullptr || host_out == nullptr || !c->have_logits)
+        return fail(SLLM_CUDA_ERR_ARG, "tp_last_logits: nothing forwarded");
+    CK(cudaSetDevice(c->m->device), "cudaSetDevice");
+    CK(cudaMemcpy(host_out, c->logits, (size_t)c->m->v_loc * 4, cudaMemcpyDeviceToHost), "tp last logits");
+    return SLLM_CUDA_OK;
+}
+
+// one process, one device, N contexts of the N shards: the same phases, the
+// exchanges by device copies (tests of the sharding on a single GPU)
+extern "C" int sllm_cuda_test_tp_generate_group(sllm_cuda_tp_ctx** cs, int32_t n, const int32_t* prompt,
+                                                int32_t n_prompt, int32_t n_new, int32_t* out) {
+    if (cs == nullptr || n < 1 || n > kMaxRanks) return fail(SLLM_CUDA_ERR_ARG, "tp group: bad arguments");
+    for (int r = 0; r < n; ++r) {
+        if (cs[r] == nullptr || cs[r]->m->n_ranks != n || cs[r]->m->rank != r || cs[r]->m->device != cs[0]->m->device ||
+            cs[r]->n_past != cs[0]->n_past || cs[r]->n_ctx != cs[0]->n_ctx)
+            return fail(SLLM_CUDA_ERR_ARG, "tp group: contexts do not form ranks 0..%d of one model on one device", n - 1);
+        int rc = tp_validate(cs[r], prompt, n_prompt, n_new, out);
+        if (rc != SLLM_CUDA_OK) return rc;
+    }
+    if (n_prompt == 0 && cs[0]->n_past == 0 && n_new == 0) return SLLM_CUDA_OK;
+    CK(cudaSetDevice(cs[0]->m->device), "cudaSetDevice");
+    cudaStream_t st = cs[0]->stream;
+    // every context's registers are set on the group's stream
+    for (int r = 0; r < n; ++r) {
+        cudaStream_t own = cs[r]->stream;
+        cs[r]->stream = st;
+        const int rc = tp_seed(cs[r], prompt, n_prompt);
+        cs[r]->stream = own;
+        if (rc != SLLM_CUDA_OK) return rc;
+    }
+    const int base = cs[0]->n_past, steps = n_prompt + n_new;
+    for (int s = 0; s < steps; ++s) {
+        for (int ph = 0; ph < n_phases(cs[0]->m); ++ph) {
+            for (int r = 0; r < n; ++r) CK(enqueue_phase(cs[r], ph, st, true), "tp group phase");
+            const int x = phase_xchg(cs[0]->m, ph);
+            if (x >= 0) CK(xchg_group(cs, n, x, st), "tp group exchange");
+        }
+    }
+    if (n_new > 0)
+        CK(cudaMemcpyAsync(out, cs[0]->tok_seq + base + n_prompt, (size_t)n_new * 4, cudaMemcpyDeviceToHost, st), "ids");
+    CK(cudaStreamSynchronize(st), "tp group sync");
+    for (int r = 0; r < n; ++r) {
+        cs[r]->n_past = base + steps;
+        cs[r]->have_logits = steps > 0;
+    }
+    return SLLM_CUDA_OK;
+}
