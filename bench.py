@@ -347,6 +347,57 @@ def prefill_leg(pkg, synth, local, rank, world, args):
     return out
 
 
+def tp_decode_leg(pkg, local, rank, world, args):
+    """greedy decode of the 80-layer 8192 / 28672 ternary model
+    (64 / 8 heads, vocab 128256), weights generated on each GPU from a seeded
+    hash, tensor-parallel over the `world` ranks with NCCL (one rank: no
+    exchange). Prompt 128 ids, 128 greedy tokens, batch 1; wall clock, max
+    over ranks. The token checksum is the same for every rank count."""
+    import torch
+    sd = pkg.abi.TpSynthDesc(n_layer=80, n_embd=8192, n_ff=28672, n_head=64, n_head_kv=8, n_vocab=128256,
+                             f_rms_eps=1e-5, rope_freq_base=500000.0, seed=4242)
+    n_prompt, n_new = 128, 128
+    comm = None
+    if world > 1:
+        obj = [pkg.tp_unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(obj, src=0)
+        comm = pkg.TpComm(obj[0], world, rank, local)
+    t0 = time.perf_counter()
+    model = pkg.TpModel(world, rank, local, synth=sd)
+    build_s = time.perf_counter() - t0
+    ctx = model.ctx(n_prompt + n_new + 8, comm)
+    prompt = np.random.default_rng(7).integers(0, sd.n_vocab, n_prompt).astype(np.int32)
+    rc, _ = ctx.generate(prompt[:8], 8)          # warm-up: builds the step graph
+    assert rc == 0, rc
+    ctx.reset()
+    if world > 1:
+        torch.distributed.barrier()
+    t0 = time.perf_counter()
+    rc, toks = ctx.generate(prompt, n_new)
+    dt = time.perf_counter() - t0
+    assert rc == 0, rc
+    t = torch.tensor([dt], dtype=torch.float64, device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    dt = float(t.item())
+    E, F, H, Hkv, V = sd.n_embd, sd.n_ff, sd.n_head, sd.n_head_kv, sd.n_vocab
+    i2s_layer = (E * E * 2 + 2 * (Hkv * 128) * E + 3 * F * E) // 4
+    per_gpu_bytes = (sd.n_layer * i2s_layer + V * E * 2) / world
+    steps = n_prompt + n_new
+    out = {"workload": "tp_decode_80L_8192 (configs[4], batch 1)", "tp": world,
+           "tokens_per_s": round(steps / dt, 2), "ms_per_token": round(dt / steps * 1e3, 4),
+           "steps": f"{n_prompt} prompt + {n_new} greedy, one token per step",
+           "weight_gbs_per_gpu": round(per_gpu_bytes * steps / dt / 1e9, 1),
+           "model_gb_per_gpu": round(model.bytes() / 1e9, 2), "build_s": round(build_s, 2),
+           "token_checksum": int(sum((i + 1) * int(v) for i, v in enumerate(toks))),
+           "exchange": "NCCL all-gather / int32 all-reduce in the step graph" if world > 1 else "none (one rank)"}
+    ctx.close()
+    model.close()
+    if comm is not None:
+        comm.close()
+    return out
+
+
 def decode_leg(pkg, synth, local, rank, world, args):
     """2B-4T random init, prompt 64, 256 greedy tokens."""
     import torch
@@ -409,6 +460,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-tp", action="store_true")
     ap.add_argument("--copies", type=int, default=N_COPIES,
                     help="layer copies per step (default 32; smaller only for profiler captures)")
     args = ap.parse_args()
@@ -528,6 +580,8 @@ def main():
     del m
     if not args.no_prefill:
         out["prefill"] = prefill_leg(pkg, synth, local, rank, world, args)
+    if not args.no_tp:
+        out["tp_decode"] = tp_decode_leg(pkg, local, rank, world, args)
     if not args.no_decode:
         out["decode"] = decode_leg(pkg, synth, local, rank, world, args)
     if rank == 0:
