@@ -37,6 +37,10 @@ SLLM_CUDA_API int sllm_cuda_test_gemm_error(void);
  * device copies instead of NCCL: the same phases, the same bits, testable on
  * a single GPU. out receives the tokens (every rank's are the same).
  */
+/* 1 when the context runs its layer GEMVs on the persistent engine, 0 when
+ * on the per-GEMV kernels (widths the engine is not compiled for) */
+SLLM_CUDA_API int sllm_cuda_test_tp_uses_engine(const sllm_cuda_tp_ctx * c);
+
 SLLM_CUDA_API int sllm_cuda_test_tp_generate_group(sllm_cuda_tp_ctx ** cs, int32_t n,
                                      const int32_t * prompt, int32_t n_prompt,
                                      int32_t n_new, int32_t * out);

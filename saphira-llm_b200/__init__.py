@@ -67,6 +67,7 @@ def lib():
     L.sllm_cuda_tp_generate_greedy.argtypes = [vp, vp, i32, i32, vp]
     L.sllm_cuda_tp_last_logits.argtypes = [vp, vp]
     L.sllm_cuda_test_tp_generate_group.argtypes = [C.POINTER(vp), i32, vp, i32, i32, vp]
+    L.sllm_cuda_test_tp_uses_engine.argtypes = [vp]
     L.sllm_cuda_model_upload.argtypes = [C.POINTER(abi.ModelDesc), C.c_int, C.POINTER(vp)]
     L.sllm_cuda_model_free.argtypes = [vp]
     L.sllm_cuda_model_weight_bytes.argtypes = [vp]
@@ -363,6 +364,9 @@ class TpCtx:
 
     def reset(self):
         _check(lib().sllm_cuda_tp_ctx_reset(self.h), "tp_ctx_reset")
+
+    def uses_engine(self):
+        return bool(lib().sllm_cuda_test_tp_uses_engine(self.h))
 
     def close(self):
         if self.h:

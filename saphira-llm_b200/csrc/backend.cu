@@ -461,8 +461,8 @@ static void engine_program_free(EngineProgram& p) {
 
 // Split every stage's rows over `grid` CTAs so that each CTA streams the same
 // number of weight bytes (a row of a gate/up pair weighs two rows).
-static std::vector<EngCursor> engine_starts(const std::vector<EngOp>& ops, const std::vector<int>& stage_first,
-                                            int grid) {
+std::vector<EngCursor> sllm::engine_starts(const std::vector<EngOp>& ops, const std::vector<int>& stage_first,
+                                           int grid) {
     const int n_stages = (int)stage_first.size() - 1;
     std::vector<EngCursor> st((size_t)n_stages * (grid + 1));
     for (int s = 0; s < n_stages; ++s) {

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <vector>
 
+#include "engine.cuh"
+
 namespace sllm {
 
 // record a failure for sllm_cuda_last_error and return `status`
@@ -22,6 +24,8 @@ cudaError_t instantiate(cudaGraphExec_t* exec, cudaGraph_t g);
 cudaError_t graph_launch(cudaGraphExec_t exec, cudaStream_t st);
 void graph_exec_destroy(cudaGraphExec_t exec);
 void count_launches(long long n);
+// split every stage's rows over `grid` CTAs by weight bytes (engine programs)
+std::vector<EngCursor> engine_starts(const std::vector<EngOp>& ops, const std::vector<int>& stage_first, int grid);
 
 }  // namespace sllm
 

@@ -195,6 +195,19 @@ __device__ sllm_cuda_act eng_prologue(const EngGroup& g, const EngParams& P, int
     constexpr int NT = kEngConsumerWarps * 32;
     constexpr int KPT = (8192 / 4 + NT - 1) / NT;     // float4 per thread for the widest K
     const int K = g.K, K4 = K >> 2;
+    if (g.pro == PRO_Q8) {
+        // already quantised (a slice of a vector another kernel normalised and
+        // quantised whole): only the lane-major layout is built here
+        for (int i = tid; i < K4; i += NT) {
+            const int wi = ((i >> 5) << 3) + (i & 7), f = (i >> 3) & 3;
+            reinterpret_cast<uint32_t*>(qs)[wi * 4 + f] = __ldcg(reinterpret_cast<const unsigned int*>(g.q8) + i);
+        }
+        consumer_sync();
+        sllm_cuda_act a;
+        a.scale = __ldcg(&g.act8->scale);
+        a.sum = __ldcg(&g.act8->sum);
+        return a;
+    }
     float4 x[KPT], w[KPT];
     if (g.pro == PRO_NORM) {
         #pragma unroll
@@ -399,6 +412,7 @@ __device__ __forceinline__ void eng_run_op(const EngOp& op, int r0, int r_end, R
     const int K = op.K, W = K >> 4, rb = K >> 2, chunk_rows = op.chunk_rows;
     float* const out = PAIR ? op.h : op.y;
     const float* const resid = op.epi == EPI_RESID ? op.resid : nullptr;
+    const bool dots_out = op.epi == EPI_DOTS;
     // this lane's last word lies in the row: else it reads past the row and is masked
     const uint32_t last_mask = lane + 32 * (WPL - 1) < W ? 0xffffffffu : 0u;
     int4 aq[WPL];
@@ -434,9 +448,13 @@ __device__ __forceinline__ void eng_run_op(const EngOp& op, int r0, int r_end, R
                     if (lane == t) mine = dot[t];
                 const int j = warp + kEngConsumerWarps * lane;
                 if (lane < R && j < n) {
-                    float v = __fmul_rn(__int2float_rn(mine - asum), post);
-                    if (resid != nullptr) v = __fadd_rn(v, __ldcg(resid + r + j));
-                    out[r + j] = v;
+                    if (dots_out) {
+                        reinterpret_cast<int*>(out)[r + j] = mine;     // raw code dot (src/i2s_gemm.c:260-269)
+                    } else {
+                        float v = __fmul_rn(__int2float_rn(mine - asum), post);
+                        if (resid != nullptr) v = __fadd_rn(v, __ldcg(resid + r + j));
+                        out[r + j] = v;
+                    }
                 }
             }
         }
@@ -613,7 +631,7 @@ i2s_engine_kernel(const EngParams P) {
 
 // the (WA, WB) pairs compiled in: the 2B-4T model and the widths the tests use
 #define SLLM_ENGINE_SHAPES(X) \
-    X(5, 14) X(1, 1) X(1, 2) X(1, 3) X(2, 6) X(3, 6) X(16, 16) X(16, 14) X(16, 7)
+    X(5, 14) X(1, 1) X(1, 2) X(1, 3) X(2, 6) X(3, 6) X(16, 16) X(16, 14) X(16, 7) X(16, 8) X(16, 4) X(16, 2)
 
 // ---------------------------------------------------------------------------
 // host side

@@ -27,19 +27,21 @@ struct EngGroup {
     const float* x;          // input (read through L2: other CTAs may have written it)
     const float* norm_w;     // PRO_NORM weight (nullable for PRO_QUANT)
     int K;
-    int pro;                 // PRO_NORM or PRO_QUANT
+    int pro;                 // PRO_NORM, PRO_QUANT or PRO_Q8
+    const int8_t* q8;        // PRO_Q8: K int8 activations, natural order, already quantised
+    const sllm_cuda_act* act8;   // PRO_Q8: their {scale, sum}
 };
 
 // one weight tensor (or a gate/up pair for EPI_SILU)
 struct EngOp {
     const uint8_t* w;        // rows x K/4 bytes, scale tail after them
     const uint8_t* w2;       // EPI_SILU: the up tensor (same shape)
-    float* y;                // EPI_F32 / EPI_RESID output
+    float* y;                // EPI_F32 / EPI_RESID output; EPI_DOTS: int32 raw dots
     const float* resid;      // EPI_RESID: y = proj + resid
     float* h;                // EPI_SILU: h = silu(gate) * up
     int rows;
     int K;
-    int epi;                 // EPI_F32, EPI_RESID or EPI_SILU
+    int epi;                 // EPI_F32, EPI_RESID, EPI_SILU or EPI_DOTS
     int group;               // index into the groups
     int chunk_rows;          // rows per slot
     float ws;                // the per-tensor scale of w (src/quant.c:102-106), read at upload

@@ -46,6 +46,7 @@
 #include "backend.cuh"
 #include "common.cuh"
 #include "decode.cuh"
+#include "engine.cuh"
 #include "gemv.cuh"
 #include "../../include/sllm_cuda.h"
 #include "../../include/sllm_cuda_testing.h"
@@ -362,6 +363,17 @@ struct sllm_cuda_tp_ctx {
     int32_t* pinned = nullptr;
     cudaGraphExec_t step = nullptr;
     std::vector<void*> allocs;
+    // the layer GEMVs on the persistent engine: [layer][phase] programs
+    // (Q/K/V, O partial dots, gate/up, down partial dots); empty when the
+    // model's widths have no compiled engine instance (per-GEMV kernels then)
+    struct Prog {
+        EngParams p;
+        int wa, wb;
+    };
+    std::vector<Prog> progs;
+    int grid = 0;
+    int* eng_error = nullptr;
+    unsigned* eng_barrier = nullptr;
 };
 
 namespace {
@@ -715,6 +727,17 @@ cudaError_t launch_count(cudaError_t e, int n) {
     return e;
 }
 
+// a layer GEMV phase: the context's engine program when it has one, else the
+// per-GEMV kernel with parameters p
+cudaError_t gemv_or_engine(sllm_cuda_tp_ctx* c, int l, int phase, const GemvParams& p, int pro, int epi, int sms,
+                           cudaStream_t st) {
+    if (!c->progs.empty()) {
+        const sllm_cuda_tp_ctx::Prog& pr = c->progs[(size_t)l * 4 + phase];
+        return launch_engine(pr.p, c->grid, st, pr.wa, pr.wb);
+    }
+    return launch_gemv(p, pro, epi, sms, st);
+}
+
 cudaError_t enqueue_phase(sllm_cuda_tp_ctx* c, int ph, cudaStream_t st, bool counted) {
     const sllm_cuda_tp_model* m = c->m;
     const int E = m->E, D = kHeadDim, sms = num_sms_of(m->device);
@@ -766,7 +789,7 @@ cudaError_t enqueue_phase(sllm_cuda_tp_ctx* c, int ph, cudaStream_t st, bool cou
         p.seg[1] = GemvSeg{t.wk, m->hk * D, c->k, nullptr};
         p.seg[2] = GemvSeg{t.wv, m->hk * D, c->v, nullptr};
         p.x = c->x; p.norm_w = t.attn_norm;
-        cudaError_t e = launch_count(launch_gemv(p, PRO_NORM, EPI_F32, sms, st), cnt);
+        cudaError_t e = launch_count(gemv_or_engine(c, l, 0, p, PRO_NORM, EPI_F32, sms, st), cnt);
         if (e != cudaSuccess) return e;
         const size_t kv_layer = (size_t)m->hk * D * (size_t)c->n_ctx;
         AttnParams ap{};
@@ -791,7 +814,7 @@ cudaError_t enqueue_phase(sllm_cuda_tp_ctx* c, int ph, cudaStream_t st, bool cou
         p.seg[0] = GemvSeg{t.wo, E, nullptr, c->dots_o};
         p.q_in = c->qa + (size_t)m->rank * m->e_loc;
         p.act_in = c->act_a;
-        return launch_count(launch_gemv(p, PRO_Q8, EPI_DOTS, sms, st), cnt);
+        return launch_count(gemv_or_engine(c, l, 1, p, PRO_Q8, EPI_DOTS, sms, st), cnt);
     }
     if (sub == 2) {
         // O epilogue + residual, then ffn_norm -> local gate, up -> h (src/forward.c:742-779)
@@ -801,13 +824,14 @@ cudaError_t enqueue_phase(sllm_cuda_tp_ctx* c, int ph, cudaStream_t st, bool cou
         p.seg[0] = GemvSeg{t.gate, m->f_loc, nullptr, nullptr};
         p.seg[1] = GemvSeg{t.up, m->f_loc, nullptr, nullptr};
         p.x = c->ffn_inp; p.norm_w = t.ffn_norm; p.h_out = c->h_loc;
-        return launch_count(launch_gemv(p, PRO_NORM, EPI_SILU, sms, st), cnt);
+        return launch_count(gemv_or_engine(c, l, 2, p, PRO_NORM, EPI_SILU, sms, st), cnt);
     }
     // ffn_sub_norm + quantisation of all of h, then this rank's columns of
     // down, chunk by chunk (src/forward.c:781-792)
     tp_norm_quant_kernel<<<1, kNqThreads, 0, st>>>(c->h_full, t.ffn_sub_norm, m->F, m->eps, 1.0 / (double)m->F,
                                                    c->qh, c->act_h, fb, force);
     cudaError_t e = launch_count(cudaGetLastError(), cnt);
+    if (e == cudaSuccess && !c->progs.empty()) return launch_count(gemv_or_engine(c, l, 3, p, 0, 0, sms, st), cnt);
     for (int ch = 0; ch < m->down_c && e == cudaSuccess; ++ch) {
         GemvParams d = p;
         d.K = m->down_k; d.nseg = 1;
@@ -817,6 +841,93 @@ cudaError_t enqueue_phase(sllm_cuda_tp_ctx* c, int ph, cudaStream_t st, bool cou
         e = launch_count(launch_gemv(d, PRO_Q8, EPI_DOTS, sms, st), cnt);
     }
     return e;
+}
+
+float read_scale(const uint8_t* w, int rows, int cols) {
+    float v = 0.0f;
+    cudaMemcpy(&v, w + (size_t)rows * cols / 4, 4, cudaMemcpyDeviceToHost);
+    return v;
+}
+
+int wpl_of(int K) { return engine_wpl(K); }
+
+// One single-stage engine program per layer and GEMV phase, tables in device
+// memory owned by the context. Returns OK and leaves c->progs empty when the
+// widths are not compiled in.
+int build_engine_programs(sllm_cuda_tp_ctx* c) {
+    const sllm_cuda_tp_model* m = c->m;
+    const int wa = wpl_of(m->E), wo = wpl_of(m->e_loc), wd = wpl_of(m->down_k);
+    if (m->E > kMaxChunkK || !engine_supports(wa, wo) || !engine_supports(wa, wd)) return SLLM_CUDA_OK;
+    CK(prepare_engine(), "engine attributes");
+    c->grid = engine_grid(m->device);
+    CK(ctx_alloc(c, &c->eng_error, 1), "engine error word");
+    CK(ctx_alloc(c, &c->eng_barrier, 4), "engine barrier");
+    CK(cudaMemset(c->eng_error, 0, 4), "engine error word");
+    CK(cudaMemset(c->eng_barrier, 0, 16), "engine barrier");
+    const int D = kHeadDim, E = m->E;
+    int* fb = fallback_counter();
+    for (int l = 0; l < m->n_layer; ++l) {
+        const TpLayer& t = m->layers[l];
+        for (int ph = 0; ph < 4; ++ph) {
+            std::vector<EngGroup> groups;
+            std::vector<EngOp> ops;
+            auto op = [&](const uint8_t* w, const uint8_t* w2, float* y, float* h, int rows, int K, int epi, int group) {
+                EngOp o{};
+                o.w = w; o.w2 = w2; o.y = y; o.h = h; o.rows = rows; o.K = K; o.epi = epi; o.group = group;
+                o.chunk_rows = engine_chunk_rows(K, epi);
+                o.ws = read_scale(w, rows, K);
+                o.ws2 = w2 != nullptr ? read_scale(w2, rows, K) : 0.0f;
+                ops.push_back(o);
+            };
+            int wb = wo;
+            if (ph == 0) {          // attn_norm -> local Q, K, V
+                EngGroup g{}; g.x = c->x; g.norm_w = t.attn_norm; g.K = E; g.pro = PRO_NORM;
+                groups.push_back(g);
+                op(t.wq, nullptr, c->q, nullptr, m->hq * D, E, EPI_F32, 0);
+                op(t.wk, nullptr, c->k, nullptr, m->hk * D, E, EPI_F32, 0);
+                op(t.wv, nullptr, c->v, nullptr, m->hk * D, E, EPI_F32, 0);
+            } else if (ph == 1) {   // this rank's columns of O: partial int32 dots
+                EngGroup g{}; g.q8 = c->qa + (size_t)m->rank * m->e_loc; g.act8 = c->act_a; g.K = m->e_loc; g.pro = PRO_Q8;
+                groups.push_back(g);
+                op(t.wo, nullptr, reinterpret_cast<float*>(c->dots_o), nullptr, E, m->e_loc, EPI_DOTS, 0);
+            } else if (ph == 2) {   // ffn_norm -> local gate, up -> h
+                EngGroup g{}; g.x = c->ffn_inp; g.norm_w = t.ffn_norm; g.K = E; g.pro = PRO_NORM;
+                groups.push_back(g);
+                op(t.gate, t.up, nullptr, c->h_loc, m->f_loc, E, EPI_SILU, 0);
+            } else {                // this rank's columns of down, chunk by chunk
+                wb = wd;
+                for (int ch = 0; ch < m->down_c; ++ch) {
+                    EngGroup g{};
+                    g.q8 = c->qh + (size_t)m->rank * m->f_loc + (size_t)ch * m->down_k;
+                    g.act8 = c->act_h; g.K = m->down_k; g.pro = PRO_Q8;
+                    groups.push_back(g);
+                    op(t.down[ch], nullptr, reinterpret_cast<float*>(c->dots_d + (size_t)ch * E), nullptr, E,
+                       m->down_k, EPI_DOTS, ch);
+                }
+            }
+            const std::vector<int> stage_first{0, (int)ops.size()};
+            const std::vector<EngCursor> st = engine_starts(ops, stage_first, c->grid);
+            if (engine_smem_bytes((int)groups.size(), (int)ops.size(), 1) == 0)
+                return fail(SLLM_CUDA_ERR_TOO_LARGE, "tp engine program does not fit in shared memory");
+            EngGroup* dg = nullptr;
+            EngOp* dop = nullptr;
+            EngCursor* ds = nullptr;
+            CK(ctx_alloc(c, &dg, groups.size()), "tp engine groups");
+            CK(ctx_alloc(c, &dop, ops.size()), "tp engine ops");
+            CK(ctx_alloc(c, &ds, st.size()), "tp engine cursors");
+            CK(cudaMemcpy(dg, groups.data(), groups.size() * sizeof(EngGroup), cudaMemcpyHostToDevice), "tables");
+            CK(cudaMemcpy(dop, ops.data(), ops.size() * sizeof(EngOp), cudaMemcpyHostToDevice), "tables");
+            CK(cudaMemcpy(ds, st.data(), st.size() * sizeof(EngCursor), cudaMemcpyHostToDevice), "tables");
+            sllm_cuda_tp_ctx::Prog pr{};
+            pr.p.groups = dg; pr.p.ops = dop; pr.p.starts = ds;
+            pr.p.n_groups = (int)groups.size(); pr.p.n_ops = (int)ops.size(); pr.p.n_stages = 1;
+            pr.p.barrier = c->eng_barrier; pr.p.error = c->eng_error; pr.p.eps = m->eps;
+            pr.p.fallback_count = fb; pr.p.force_fallback = force_fallback_flag();
+            pr.wa = wa; pr.wb = wb;
+            c->progs.push_back(pr);
+        }
+    }
+    return SLLM_CUDA_OK;
 }
 
 int ensure_tp_graph(sllm_cuda_tp_ctx* c) {
@@ -951,6 +1062,11 @@ extern "C" int sllm_cuda_tp_ctx_new(const sllm_cuda_tp_model* m, sllm_cuda_tp_co
         sllm_cuda_tp_ctx_free(c);
         return cuda_fail(e, "tp_ctx_new");
     }
+    const int rc = build_engine_programs(c);
+    if (rc != SLLM_CUDA_OK) {
+        sllm_cuda_tp_ctx_free(c);
+        return rc;
+    }
     *out = c;
     return SLLM_CUDA_OK;
 }
@@ -984,6 +1100,11 @@ extern "C" int sllm_cuda_tp_generate_greedy(sllm_cuda_tp_ctx* c, const int32_t* 
         CK(cudaMemcpyAsync(out, c->tok_seq + base + n_prompt, (size_t)n_new * 4, cudaMemcpyDeviceToHost, c->stream), "ids");
     rc = tp_sync(c, 120.0);
     if (rc != SLLM_CUDA_OK) return rc;
+    if (c->eng_error != nullptr) {
+        int err = 0;
+        CK(cudaMemcpy(&err, c->eng_error, 4, cudaMemcpyDeviceToHost), "engine error word");
+        if (err != 0) return fail(SLLM_CUDA_ERR_TIMEOUT, "tp step: an engine wait gave up (code %d)", err);
+    }
     c->n_past = base + steps;
     c->have_logits = steps > 0;
     return SLLM_CUDA_OK;
@@ -1050,4 +1171,8 @@ extern "C" int sllm_cuda_test_tp_generate_group(sllm_cuda_tp_ctx** cs, int32_t n
         cs[r]->have_logits = steps > 0;
     }
     return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_test_tp_uses_engine(const sllm_cuda_tp_ctx* c) {
+    return c != nullptr && !c->progs.empty() ? 1 : 0;
 }

@@ -105,6 +105,43 @@ def test_tp_synth_ranks_agree(cuda):
         assert np.array_equal(bits(lg), bits(l1)), f"TP={n}"
 
 
+WIDE_CFG = dict(n_layer=2, n_embd=8192, n_ff=16384, n_head=64, n_head_kv=8, n_vocab=3001)
+
+
+def test_tp_engine_path_matches_oracle(cuda, orc, synth):
+    """configs[4]'s widths (n_embd 8192): the layer GEMVs run as persistent-
+    engine programs (pre-quantised slices, raw partial dots); TP = 1 must still
+    equal the oracle exactly."""
+    cfg = synth.small_config(**WIDE_CFG)
+    m = synth.SynthModel(cfg, seed=31)
+    tm = cuda.TpModel(1, 0, 0, desc=m.desc())
+    tc = tm.ctx(32)
+    assert tc.uses_engine()
+    oc = orc.ctx(m.desc(), 32)
+    prompt = _tokens(8, 5, cfg.n_vocab)
+    r1, t1 = tc.generate(prompt, 6)
+    r2, t2 = oc.generate(prompt, 6)
+    assert r1 == r2 == 0
+    assert t1.tolist() == t2.tolist()
+    _, lg = tc.last_logits()
+    assert np.array_equal(bits(lg), bits(oc.last_logits()))
+    tc.close()
+    tm.close()
+
+
+def test_tp_engine_ranks_agree(cuda):
+    sd = cuda.abi.TpSynthDesc(n_layer=2, n_embd=8192, n_ff=16384, n_head=64, n_head_kv=8, n_vocab=3001,
+                              f_rms_eps=1e-5, rope_freq_base=500000.0, seed=77)
+    prompt = _tokens(9, 6, sd.n_vocab)
+    rc1, t1, l1 = _group_run(cuda, sd, 1, prompt, 8)
+    assert rc1 == 0
+    for n in (2, 4):
+        rc, t, lg = _group_run(cuda, sd, n, prompt, 8)
+        assert rc == 0
+        assert t.tolist() == t1.tolist(), f"TP={n}"
+        assert np.array_equal(bits(lg), bits(l1)), f"TP={n}"
+
+
 def _nccl_rank(rank, n, uid, prompt, n_new, q):
     import importlib
     import torch  # noqa: F401  (a process with torch keeps one NCCL copy)
