@@ -241,25 +241,28 @@ def reference_arm(args, world, rank):
 # GPU legs
 # ---------------------------------------------------------------------------
 def time_device(fn, steps, warmup, stream, world):
-    """Device time of `steps` calls of fn() after `warmup`, max over ranks."""
+    """Device time of `steps` back-to-back calls of fn() after `warmup`, from
+    an idle device to the end of the last step (synchronize, barrier, one
+    event before and one after: an event between steps would serialise the
+    launches and hide how consecutive steps overlap), max over ranks."""
     import torch
     for _ in range(max(warmup, 3)):
         fn()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
-    ev[0].record(stream)
-    for i in range(steps):
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
         fn()
-        ev[i + 1].record(stream)
+    ev1.record(stream)
     torch.cuda.synchronize()
-    ms = ev[0].elapsed_time(ev[steps])
-    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
+    ms = ev0.elapsed_time(ev1)
     t = torch.tensor([ms], dtype=torch.float64, device="cuda")
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    return float(t.item()), per
+    return float(t.item()), None
 
 
 PREFILL_TOKENS = 512
@@ -567,7 +570,6 @@ def main():
                 "d2h_bytes_per_step": 4 * ys_n * copies,
                 "api": "sllm_cuda_layer_projections (host buffers, wall clock)"},
         "gpu_launches": launches * args.steps,
-        "step_ms_min_median_max": [round(min(per), 4), round(float(np.median(per)), 4), round(max(per), 4)],
         "clocks": clocks,
         "chain": {"workload": "layer_chain_2b4t (dependent: decode layer without attention)",
                   "value": round(chain_gbs, 3), "unit": "GB/s", "frac": round(chain_gbs / world / peak, 4),

@@ -446,7 +446,10 @@ struct EngineProgram {
     int* error = nullptr;
     int n_stages = 0;
     int grid = 0;
-    cudaGraphExec_t exec = nullptr;
+    cudaGraphExec_t exec = nullptr;  // multi-stage: barrier memset + cooperative launch
+    bool built = false;
+    EngParams params{};              // single-stage: launched directly (programmatic dependent launch)
+    int wa = 0, wb = 0;
     // what the program was built for
     int key_begin = -1, key_n = -1;
     const void* key_x = nullptr;
@@ -459,35 +462,64 @@ static void engine_program_free(EngineProgram& p) {
     p = EngineProgram();
 }
 
-// Split every stage's rows over `grid` CTAs so that each CTA streams the same
-// number of weight bytes (a row of a gate/up pair weighs two rows).
+// Split every stage's rows over `grid` CTAs so that each CTA costs the same:
+// its weight bytes (a row of a gate/up pair weighs two rows), plus, for every
+// input group whose rows it runs, the time of that group's prologue (the
+// RMSNorm + quantisation every such CTA computes), counted in bytes the CTA
+// could have streamed meanwhile. A CTA that spans several small ops builds
+// several activation vectors, so it gets fewer bytes. The split is the
+// greedy fill under the smallest feasible per-CTA cost (binary search).
+static constexpr double kPrologueBytes = 192.0 * 1024.0;
+
 std::vector<EngCursor> sllm::engine_starts(const std::vector<EngOp>& ops, const std::vector<int>& stage_first,
                                            int grid) {
     const int n_stages = (int)stage_first.size() - 1;
     std::vector<EngCursor> st((size_t)n_stages * (grid + 1));
+    auto row_cost = [&](int o) { return (double)(ops[o].K / 4) * (ops[o].epi == EPI_SILU ? 2 : 1); };
     for (int s = 0; s < n_stages; ++s) {
         const int o0 = stage_first[s], o1 = stage_first[s + 1];
-        double total = 0.0;
-        for (int o = o0; o < o1; ++o) total += (double)ops[o].rows * (ops[o].K / 4) * (ops[o].epi == EPI_SILU ? 2 : 1);
         EngCursor* out = &st[(size_t)s * (grid + 1)];
-        int o = o0;
-        double before = 0.0;           // cost of ops [o0, o)
-        for (int c = 0; c <= grid; ++c) {
-            if (c == grid) { out[c] = EngCursor{o1, 0}; break; }
-            const double target = total * c / grid;
-            while (o < o1) {
-                const double rc = (double)(ops[o].K / 4) * (ops[o].epi == EPI_SILU ? 2 : 1);
-                const double cost = ops[o].rows * rc;
-                if (before + cost > target) {
-                    int row = (int)std::ceil((target - before) / rc);
-                    if (row >= ops[o].rows) { before += cost; ++o; continue; }
-                    out[c] = EngCursor{o, row < 0 ? 0 : row};
-                    break;
+        // greedy fill under budget M; returns the CTAs used, writes the cursors
+        auto fill = [&](double M, bool write) {
+            int cta = 0, group = -1;
+            double cost = 0.0;
+            if (write) out[0] = EngCursor{o0, 0};
+            for (int o = o0; o < o1; ++o) {
+                const double rc = row_cost(o);
+                int row = 0;
+                while (row < ops[o].rows) {
+                    const double enter = (ops[o].group != group) ? kPrologueBytes : 0.0;
+                    double room = M - cost - enter;
+                    int take = room >= rc ? (int)std::min<double>(ops[o].rows - row, std::floor(room / rc)) : 0;
+                    if (take == 0 && cost == 0.0) take = 1;          // an empty CTA always takes one row
+                    if (take == 0) {                                  // this CTA is full: open the next one
+                        ++cta;
+                        if (write && cta < grid) out[cta] = EngCursor{o, row};
+                        cost = 0.0;
+                        group = -1;
+                        continue;
+                    }
+                    cost += enter + take * rc;
+                    group = ops[o].group;
+                    row += take;
                 }
-                before += cost;
-                ++o;
             }
-            if (o >= o1) out[c] = EngCursor{o1, 0};
+            return cta + 1;
+        };
+        double total = 0.0;
+        for (int o = o0; o < o1; ++o) total += ops[o].rows * row_cost(o);
+        double lo = total / grid, hi = total / grid + kPrologueBytes * (o1 - o0 + 1) + 4 * 65536.0;
+        if (o1 > o0) {
+            while (fill(hi, false) > grid) hi *= 2;
+            for (int it = 0; it < 40; ++it) {
+                const double mid = 0.5 * (lo + hi);
+                if (fill(mid, false) <= grid) hi = mid; else lo = mid;
+            }
+        }
+        for (int c = 0; c <= grid; ++c) out[c] = EngCursor{o1, 0};
+        if (o1 > o0) {
+            const int used = fill(hi, true);
+            for (int c = used; c <= grid; ++c) out[c] = EngCursor{o1, 0};
         }
     }
     return st;
@@ -520,6 +552,13 @@ static int engine_program_build(EngineProgram& p, const std::vector<EngGroup>& g
     ep.n_groups = (int)groups.size(); ep.n_ops = (int)ops.size();
     ep.barrier = p.barrier; ep.error = p.error; ep.fallback_count = fallback; ep.force_fallback = g_force_fallback;
     ep.eps = g_engine_eps;     // every group of a program comes from one model
+    p.params = ep;
+    p.wa = wa;
+    p.wb = wb;
+    if (p.n_stages == 1) {     // no grid barrier: no memset, no graph
+        p.built = true;
+        return SLLM_CUDA_OK;
+    }
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(capture_stream, cudaStreamCaptureModeThreadLocal), "begin capture");
     e = cudaMemsetAsync(p.barrier, 0, sizeof(unsigned), capture_stream);
@@ -530,7 +569,15 @@ static int engine_program_build(EngineProgram& p, const std::vector<EngGroup>& g
     e = instantiate(&p.exec, g);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) { p.exec = nullptr; engine_program_free(p); return cuda_fail(e, "instantiate engine"); }
+    p.built = true;
     return SLLM_CUDA_OK;
+}
+
+static cudaError_t engine_program_launch(const EngineProgram& p, cudaStream_t st) {
+    if (p.exec != nullptr) return graph_launch(p.exec, st);
+    const cudaError_t e = launch_engine(p.params, p.grid, st, p.wa, p.wb);
+    if (e == cudaSuccess) count_launches(1);
+    return e;
 }
 
 // ---------------------------------------------------------------------------
@@ -933,12 +980,12 @@ extern "C" int sllm_cuda_layer_chain_device(const sllm_cuda_model* m, sllm_cuda_
         return SLLM_CUDA_OK;
     }
     EngineProgram& p = c->eng_chain;
-    if (p.exec == nullptr || p.key_begin != layer_begin || p.key_n != n_layers || p.key_x != x) {
+    if (!p.built || p.key_begin != layer_begin || p.key_n != n_layers || p.key_x != x) {
         int rc = chain_program(m, c, layer_begin, n_layers, x, fb);
         if (rc != SLLM_CUDA_OK) return rc;
         p.key_begin = layer_begin; p.key_n = n_layers; p.key_x = x;
     }
-    CK(graph_launch(p.exec, (cudaStream_t)stream), "layer chain");
+    CK(engine_program_launch(p, (cudaStream_t)stream), "layer chain");
     return SLLM_CUDA_OK;
 }
 
@@ -1069,12 +1116,12 @@ extern "C" int sllm_cuda_layer_projections_device(const sllm_cuda_model* m, sllm
         return SLLM_CUDA_OK;
     }
     EngineProgram& p = c->eng_proj;
-    if (p.exec == nullptr || p.key_begin != layer_begin || p.key_n != n_layers || p.key_x != x || p.key_y != y) {
+    if (!p.built || p.key_begin != layer_begin || p.key_n != n_layers || p.key_x != x || p.key_y != y) {
         int rc = projections_program(m, c, layer_begin, n_layers, x, y, fb);
         if (rc != SLLM_CUDA_OK) return rc;
         p.key_begin = layer_begin; p.key_n = n_layers; p.key_x = x; p.key_y = y;
     }
-    CK(graph_launch(p.exec, (cudaStream_t)stream), "projections");
+    CK(engine_program_launch(p, (cudaStream_t)stream), "projections");
     return SLLM_CUDA_OK;
 }
 

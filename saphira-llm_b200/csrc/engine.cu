@@ -489,6 +489,9 @@ __global__ void __launch_bounds__(kEngThreads, 1)
 i2s_engine_kernel(const EngParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ EngSmem es;
+    // dependents may launch now: they take each SM as this kernel's CTA there
+    // exits (a no-op unless the next launch asked for programmatic serialisation)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     uint8_t* ring = smem;                                     // kEngSlots x kEngSlotBytes
     int8_t* qs = reinterpret_cast<int8_t*>(smem + kEngSlots * kEngSlotBytes);   // up to 8192 bytes
     EngOp* s_ops = reinterpret_cast<EngOp*>(smem + kEngSlots * kEngSlotBytes + 8192);
@@ -530,19 +533,14 @@ i2s_engine_kernel(const EngParams P) {
             uint32_t k = 0;
             for (int s = 0; s < P.n_stages; ++s) {
                 ChunkWalk walk{s_ops, s_cur[2 * s].op, s_cur[2 * s].row, s_cur[2 * s + 1]};
-                {
-                    // the norm vectors this stage's prologues will read: into L2 now
-                    ChunkWalk pw = walk;
-                    int o, r, n, last = -1;
-                    while (pw.next(o, r, n)) {
-                        const int gi = s_ops[o].group;
-                        if (gi != last && s_groups[gi].norm_w != nullptr)
-                            prefetch_l2(s_groups[gi].norm_w, (uint32_t)s_groups[gi].K * 4u);
-                        last = gi;
-                    }
-                }
-                int o, r, n;
+                int o, r, n, last_group = -1;
                 while (walk.next(o, r, n)) {
+                    // the norm vector of a group this CTA reaches: into L2 as the
+                    // producer gets to it, up to a ring ahead of the prologue
+                    const int gi = s_ops[o].group;
+                    if (gi != last_group && s_groups[gi].norm_w != nullptr)
+                        prefetch_l2(s_groups[gi].norm_w, (uint32_t)s_groups[gi].K * 4u);
+                    last_group = gi;
                     const int slot = (int)(k % kEngSlots);
                     const uint32_t use = k / kEngSlots;
                     if (*(volatile int*)&es.abort_flag) break;
@@ -575,6 +573,10 @@ i2s_engine_kernel(const EngParams P) {
     }
 
     // ---------------- consumers ----------------
+    // the previous kernel's results (this program's inputs) and its reads of
+    // the buffers this program writes are complete from here on; the producer
+    // streams only weights, which no kernel writes, and needs no such wait
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     RingPos rp;
     int cur_group = -1;
     sllm_cuda_act act{0.0f, 0};
@@ -692,8 +694,16 @@ cudaError_t launch_engine(const EngParams& p, int grid, cudaStream_t st, int wa,
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;     // all CTAs co-resident: they meet at grid barriers
-    attr[0].val.cooperative = 1;
+    if (p.n_stages > 1) {
+        attr[0].id = cudaLaunchAttributeCooperative;     // all CTAs co-resident: they meet at grid barriers
+        attr[0].val.cooperative = 1;
+    } else {
+        // no grid barrier: a CTA of this launch may take an SM as soon as the
+        // previous kernel's CTA there exits (its consumers wait for that
+        // kernel's results before touching activations or outputs)
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+    }
     cfg.attrs = attr;
     cfg.numAttrs = 1;
 #define SLLM_ENG_LAUNCH(A, B) \
