@@ -401,7 +401,10 @@ SLLM_CUDA_API int sllm_cuda_tp_ctx_reset(sllm_cuda_tp_ctx * c);
  * sllm_generate_greedy (src/forward.c:885-938) over the shards: argument
  * rules, BOS fallback and outputs as sllm_cuda_generate_greedy. A step whose
  * exchanges make no progress for 120 s aborts the communicator and returns
- * SLLM_CUDA_ERR_TIMEOUT.
+ * SLLM_CUDA_ERR_TIMEOUT. The exchanges are NCCL collectives, or, with the
+ * environment variable SLLM_CUDA_TP_EXCHANGE=p2p at context creation, one-shot
+ * kernels that store into the peers' memory over NVLink (CUDA IPC) and wait
+ * on epoch flags (bounded).
  */
 SLLM_CUDA_API int sllm_cuda_tp_generate_greedy(sllm_cuda_tp_ctx * c, const int32_t * prompt,
                                  int32_t n_prompt, int32_t n_new, int32_t * out);

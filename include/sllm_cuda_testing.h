@@ -41,6 +41,10 @@ SLLM_CUDA_API int sllm_cuda_test_gemm_error(void);
  * on the per-GEMV kernels (widths the engine is not compiled for) */
 SLLM_CUDA_API int sllm_cuda_test_tp_uses_engine(const sllm_cuda_tp_ctx * c);
 
+/* how the context exchanges between ranks: 0 none (one rank), 1 NCCL
+ * collectives, 2 the one-shot peer-memory exchange */
+SLLM_CUDA_API int sllm_cuda_test_tp_exchange_kind(const sllm_cuda_tp_ctx * c);
+
 SLLM_CUDA_API int sllm_cuda_test_tp_generate_group(sllm_cuda_tp_ctx ** cs, int32_t n,
                                      const int32_t * prompt, int32_t n_prompt,
                                      int32_t n_new, int32_t * out);

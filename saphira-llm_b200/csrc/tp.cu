@@ -36,6 +36,7 @@
 #include <chrono>
 #include <dlfcn.h>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <thread>
 #include <type_traits>
@@ -103,6 +104,12 @@ constexpr int kMaxRanks = 8;
 // ---------------------------------------------------------------------------
 // kernels
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t gtimer_d() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 
 // RMSNorm (certified mean, src/ops.c:254-322) + per-token int8 quantisation
 // (src/i2s_gemm.c:45-83) of one vector, q in natural order, one CTA.
@@ -244,6 +251,89 @@ __global__ void tp_group_sum_kernel(SumArgs a) {
     }
 }
 
+// --- the one-shot peer exchange ----------------------------------------------
+// One CTA per rank and exchange: store this rank's `count` words into slot
+// `rank` of the destination area in every rank's region (plain stores over
+// NVLink to the peers' mapped regions), publish them (system fence, then a
+// release store of the exchange's epoch into flag[rank] of every region),
+// wait until every rank's flag in this region reaches the epoch (acquire,
+// bounded by the global timer), then read the area through L2: a gather
+// copies the N slots to `dst`, a reduction sums them (int32, exact in any
+// order) into `dst`.
+constexpr uint64_t kXchgWaitNs = 10000000000ull;     // 10 s: a peer may still be setting up
+
+struct XParams {
+    char* peer[kMaxRanks];      // every rank's region; peer[rank] is this rank's
+    const uint32_t* src;
+    uint32_t* dst;
+    size_t off;                 // the destination area's offset in every region
+    size_t off_flags;
+    uint32_t count;             // words per rank
+    int n, rank;
+    int reduce;                 // 0: gather (dst = [N][count]), 1: int32 sum (dst = [count])
+    uint32_t* epoch;            // this rank's exchange counter (device)
+    int* error;
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(1024) tp_exchange_kernel(const XParams x) {
+    __shared__ int s_ok;
+    const int tid = threadIdx.x;
+    const uint32_t epoch = *x.epoch + 1;
+    // 16-byte stores (count is a multiple of 4 for every exchange but the
+    // 3-word argmax triple, which goes word by word)
+    const uint32_t n4 = (x.count % 4 == 0) ? x.count / 4 : 0;
+    for (int p = 0; p < x.n; ++p) {
+        uint32_t* d = reinterpret_cast<uint32_t*>(x.peer[p] + x.off) + (size_t)x.rank * x.count;
+        if (n4 > 0) {
+            const uint4* s4 = reinterpret_cast<const uint4*>(x.src);
+            uint4* d4 = reinterpret_cast<uint4*>(d);
+            for (uint32_t i = tid; i < n4; i += blockDim.x) d4[i] = s4[i];
+        } else {
+            for (uint32_t i = tid; i < x.count; i += blockDim.x) d[i] = x.src[i];
+        }
+    }
+    // the barrier orders every thread's stores before the flag stores; a
+    // release store at system scope is cumulative over them
+    __syncthreads();
+    if (tid < x.n) st_release_sys(reinterpret_cast<uint32_t*>(x.peer[tid] + x.off_flags) + x.rank, epoch);
+    if (tid == 0) s_ok = 1;
+    __syncthreads();
+    if (tid < x.n) {
+        const uint32_t* f = reinterpret_cast<const uint32_t*>(x.peer[x.rank] + x.off_flags) + tid;
+        const uint64_t t0 = gtimer_d();
+        while (ld_acquire_sys(f) < epoch) {
+            if (gtimer_d() - t0 > kXchgWaitNs) {
+                s_ok = 0;
+                atomicExch(x.error, 1);
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    const uint32_t* area = reinterpret_cast<const uint32_t*>(x.peer[x.rank] + x.off);
+    if (x.reduce) {
+        for (uint32_t i = tid; i < x.count; i += blockDim.x) {
+            int sum = 0;
+            for (int r = 0; r < x.n; ++r) sum += (int)__ldcg(area + (size_t)r * x.count + i);
+            x.dst[i] = (uint32_t)sum;
+        }
+    } else {
+        for (uint32_t i = tid; i < x.n * x.count; i += blockDim.x) x.dst[i] = __ldcg(area + i);
+    }
+    if (tid == 0) *x.epoch = epoch;
+}
+
 // --- seeded synthetic weights, generated on the device -----------------------
 __host__ __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
     x += 0x9E3779B97F4A7C15ull;
@@ -374,6 +464,14 @@ struct sllm_cuda_tp_ctx {
     int grid = 0;
     int* eng_error = nullptr;
     unsigned* eng_barrier = nullptr;
+    // the one-shot peer exchange (n_ranks > 1): a receive region on this
+    // device that every rank stores into, the peers' regions mapped here
+    bool p2p = false;
+    char* region = nullptr;
+    char* peer[kMaxRanks] = {};
+    size_t off_flags = 0, off_attn = 0, off_h = 0, off_dots_o = 0, off_dots_d = 0, off_trip = 0;
+    uint32_t* epoch = nullptr;
+    int* x_error = nullptr;
 };
 
 namespace {
@@ -671,6 +769,23 @@ cudaError_t xchg_nccl(sllm_cuda_tp_ctx* c, int which, cudaStream_t st, ncclResul
         if (gather && src != dst) return cudaMemcpyAsync(dst, src, count * 4, cudaMemcpyDeviceToDevice, st);
         return cudaSuccess;
     }
+    if (c->p2p) {
+        XParams x{};
+        for (int r = 0; r < c->m->n_ranks; ++r) x.peer[r] = c->peer[r];
+        x.src = static_cast<const uint32_t*>(src);
+        x.dst = static_cast<uint32_t*>(dst);
+        x.off = which == X_ATTN ? c->off_attn : which == X_DOTS_O ? c->off_dots_o : which == X_H ? c->off_h
+                : which == X_DOTS_D ? c->off_dots_d : c->off_trip;
+        x.off_flags = c->off_flags;
+        x.count = (uint32_t)count;
+        x.n = c->m->n_ranks;
+        x.rank = c->m->rank;
+        x.reduce = gather ? 0 : 1;
+        x.epoch = c->epoch;
+        x.error = c->x_error;
+        tp_exchange_kernel<<<1, 1024, 0, st>>>(x);
+        return cudaGetLastError();
+    }
     if (gather) {
         *nr = nccl()->all_gather(src, dst, count, which == X_ARGMAX ? ncclInt32 : ncclFloat32, c->comm->comm, st);
     } else {
@@ -843,6 +958,69 @@ cudaError_t enqueue_phase(sllm_cuda_tp_ctx* c, int ph, cudaStream_t st, bool cou
     return e;
 }
 
+// The receive region of the peer exchange and the peers' mappings (CUDA IPC
+// handles swapped with one NCCL all-gather), when SLLM_CUDA_TP_EXCHANGE=p2p
+// asks for it; every rank uses it only when all ranks set it up (NCCL
+// min-reduce of the outcome), else NCCL carries the exchanges (the default:
+// on two B200s NCCL's collectives measured slightly faster than this).
+int setup_peer_exchange(sllm_cuda_tp_ctx* c) {
+    const sllm_cuda_tp_model* m = c->m;
+    const int N = m->n_ranks;
+    if (N < 2 || c->comm == nullptr || c->comm->comm == nullptr) return SLLM_CUDA_OK;
+    const char* env = getenv("SLLM_CUDA_TP_EXCHANGE");
+    if (env == nullptr || strcmp(env, "p2p") != 0) return SLLM_CUDA_OK;
+    const size_t E = m->E;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off += align256(bytes); return o; };
+    c->off_flags = take(4 * kMaxRanks);
+    c->off_attn = take(4 * E);
+    c->off_h = take(4 * (size_t)m->F);
+    c->off_dots_o = take(4 * E * N);
+    c->off_dots_d = take(4 * E * m->down_c * N);
+    c->off_trip = take(4 * 3 * (size_t)N);
+    int ok = 1;
+    cudaIpcMemHandle_t mine{};
+    if (cudaMalloc(&c->region, off) != cudaSuccess) { c->region = nullptr; ok = 0; }
+    if (ok && cudaMemset(c->region, 0, off) != cudaSuccess) ok = 0;
+    if (ok && cudaIpcGetMemHandle(&mine, c->region) != cudaSuccess) ok = 0;
+    char* dev = nullptr;
+    CK(cudaMalloc(&dev, sizeof(cudaIpcMemHandle_t) * (N + 1) + 16), "exchange set-up");
+    std::vector<cudaIpcMemHandle_t> all(N);
+    int* okd = reinterpret_cast<int*>(dev + sizeof(cudaIpcMemHandle_t) * (N + 1));
+    cudaError_t e = cudaMemcpy(dev, &mine, sizeof(mine), cudaMemcpyHostToDevice);
+    ncclResult_t nr = ncclSuccess;
+    if (e == cudaSuccess)
+        nr = nccl()->all_gather(dev, dev + sizeof(mine), sizeof(mine), ncclInt8, c->comm->comm, c->stream);
+    if (e == cudaSuccess && nr == ncclSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e == cudaSuccess && nr == ncclSuccess)
+        e = cudaMemcpy(all.data(), dev + sizeof(mine), sizeof(mine) * N, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess || nr != ncclSuccess) ok = 0;
+    for (int r = 0; r < N && ok; ++r) {
+        if (r == m->rank) { c->peer[r] = c->region; continue; }
+        void* ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) { ok = 0; break; }
+        c->peer[r] = static_cast<char*>(ptr);
+    }
+    cudaGetLastError();
+    // every rank must take the same path
+    int agreed = 0;
+    e = cudaMemcpy(okd, &ok, 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) nr = nccl()->all_reduce(okd, okd, 1, ncclInt32, ncclMin, c->comm->comm, c->stream);
+    if (e == cudaSuccess && nr == ncclSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e == cudaSuccess && nr == ncclSuccess) e = cudaMemcpy(&agreed, okd, 4, cudaMemcpyDeviceToHost);
+    cudaFree(dev);
+    if (e != cudaSuccess) return cuda_fail(e, "exchange set-up");
+    if (nr != ncclSuccess) return fail(SLLM_CUDA_ERR_COMM, "exchange set-up: %s", nccl_err(nr));
+    if (agreed == 1) {
+        CK(ctx_alloc(c, &c->epoch, 1), "exchange counter");
+        CK(ctx_alloc(c, &c->x_error, 1), "exchange error word");
+        CK(cudaMemset(c->epoch, 0, 4), "exchange counter");
+        CK(cudaMemset(c->x_error, 0, 4), "exchange error word");
+        c->p2p = true;
+    }
+    return SLLM_CUDA_OK;
+}
+
 float read_scale(const uint8_t* w, int rows, int cols) {
     float v = 0.0f;
     cudaMemcpy(&v, w + (size_t)rows * cols / 4, 4, cudaMemcpyDeviceToHost);
@@ -856,8 +1034,17 @@ int wpl_of(int K) { return engine_wpl(K); }
 // widths are not compiled in.
 int build_engine_programs(sllm_cuda_tp_ctx* c) {
     const sllm_cuda_tp_model* m = c->m;
+    // each phase's program needs a compiled (WA, WB) pair with WA = the n_embd
+    // width (Q/K/V, the gate/up pair) and its own width as WA or WB
     const int wa = wpl_of(m->E), wo = wpl_of(m->e_loc), wd = wpl_of(m->down_k);
-    if (m->E > kMaxChunkK || !engine_supports(wa, wo) || !engine_supports(wa, wd)) return SLLM_CUDA_OK;
+    auto partner = [&](int w) {
+        if (w != wa) return engine_supports(wa, w) ? w : -1;
+        for (int cand = 1; cand <= 16; ++cand)
+            if (engine_supports(wa, cand)) return cand;
+        return -1;
+    };
+    const int wb_main = partner(wa), wb_o = partner(wo), wb_d = partner(wd);
+    if (m->E > kMaxChunkK || wb_main < 0 || wb_o < 0 || wb_d < 0) return SLLM_CUDA_OK;
     CK(prepare_engine(), "engine attributes");
     c->grid = engine_grid(m->device);
     CK(ctx_alloc(c, &c->eng_error, 1), "engine error word");
@@ -879,7 +1066,6 @@ int build_engine_programs(sllm_cuda_tp_ctx* c) {
                 o.ws2 = w2 != nullptr ? read_scale(w2, rows, K) : 0.0f;
                 ops.push_back(o);
             };
-            int wb = wo;
             if (ph == 0) {          // attn_norm -> local Q, K, V
                 EngGroup g{}; g.x = c->x; g.norm_w = t.attn_norm; g.K = E; g.pro = PRO_NORM;
                 groups.push_back(g);
@@ -895,7 +1081,6 @@ int build_engine_programs(sllm_cuda_tp_ctx* c) {
                 groups.push_back(g);
                 op(t.gate, t.up, nullptr, c->h_loc, m->f_loc, E, EPI_SILU, 0);
             } else {                // this rank's columns of down, chunk by chunk
-                wb = wd;
                 for (int ch = 0; ch < m->down_c; ++ch) {
                     EngGroup g{};
                     g.q8 = c->qh + (size_t)m->rank * m->f_loc + (size_t)ch * m->down_k;
@@ -923,7 +1108,8 @@ int build_engine_programs(sllm_cuda_tp_ctx* c) {
             pr.p.n_groups = (int)groups.size(); pr.p.n_ops = (int)ops.size(); pr.p.n_stages = 1;
             pr.p.barrier = c->eng_barrier; pr.p.error = c->eng_error; pr.p.eps = m->eps;
             pr.p.fallback_count = fb; pr.p.force_fallback = force_fallback_flag();
-            pr.wa = wa; pr.wb = wb;
+            pr.wa = wa;
+            pr.wb = ph == 1 ? wb_o : ph == 3 ? wb_d : wb_main;
             c->progs.push_back(pr);
         }
     }
@@ -1062,7 +1248,8 @@ extern "C" int sllm_cuda_tp_ctx_new(const sllm_cuda_tp_model* m, sllm_cuda_tp_co
         sllm_cuda_tp_ctx_free(c);
         return cuda_fail(e, "tp_ctx_new");
     }
-    const int rc = build_engine_programs(c);
+    int rc = build_engine_programs(c);
+    if (rc == SLLM_CUDA_OK) rc = setup_peer_exchange(c);
     if (rc != SLLM_CUDA_OK) {
         sllm_cuda_tp_ctx_free(c);
         return rc;
@@ -1076,6 +1263,9 @@ extern "C" void sllm_cuda_tp_ctx_free(sllm_cuda_tp_ctx* c) {
     cudaSetDevice(c->m->device);
     graph_exec_destroy(c->step);
     if (c->stream) cudaStreamDestroy(c->stream);
+    for (int r = 0; r < kMaxRanks; ++r)
+        if (c->peer[r] != nullptr && c->peer[r] != c->region) cudaIpcCloseMemHandle(c->peer[r]);
+    if (c->region != nullptr) cudaFree(c->region);
     for (void* p : c->allocs) cudaFree(p);
     if (c->pinned) cudaFreeHost(c->pinned);
     delete c;
@@ -1100,6 +1290,11 @@ extern "C" int sllm_cuda_tp_generate_greedy(sllm_cuda_tp_ctx* c, const int32_t* 
         CK(cudaMemcpyAsync(out, c->tok_seq + base + n_prompt, (size_t)n_new * 4, cudaMemcpyDeviceToHost, c->stream), "ids");
     rc = tp_sync(c, 120.0);
     if (rc != SLLM_CUDA_OK) return rc;
+    if (c->x_error != nullptr) {
+        int err = 0;
+        CK(cudaMemcpy(&err, c->x_error, 4, cudaMemcpyDeviceToHost), "exchange error word");
+        if (err != 0) return fail(SLLM_CUDA_ERR_TIMEOUT, "tp step: a peer's exchange flag did not arrive in time");
+    }
     if (c->eng_error != nullptr) {
         int err = 0;
         CK(cudaMemcpy(&err, c->eng_error, 4, cudaMemcpyDeviceToHost), "engine error word");
@@ -1175,4 +1370,9 @@ extern "C" int sllm_cuda_test_tp_generate_group(sllm_cuda_tp_ctx** cs, int32_t n
 
 extern "C" int sllm_cuda_test_tp_uses_engine(const sllm_cuda_tp_ctx* c) {
     return c != nullptr && !c->progs.empty() ? 1 : 0;
+}
+
+extern "C" int sllm_cuda_test_tp_exchange_kind(const sllm_cuda_tp_ctx* c) {
+    if (c == nullptr || c->m->n_ranks < 2) return 0;
+    return c->p2p ? 2 : 1;
 }

@@ -7,7 +7,8 @@ split by vocabulary rows with a first-maximum argmax across slices. So:
   * TP = 1 equals the oracle (the reference's forward pass) bit for bit;
   * a group of N ranks equals TP = 1 bit for bit (tokens and logits), on one
     GPU with the exchanges done by device copies;
-  * on two GPUs with NCCL, the same (skipped when the box has one GPU).
+  * on two GPUs with the peer-memory exchange and with NCCL, the same
+    (skipped when the box has one GPU).
 """
 import os
 
@@ -142,17 +143,19 @@ def test_tp_engine_ranks_agree(cuda):
         assert np.array_equal(bits(lg), bits(l1)), f"TP={n}"
 
 
-def _nccl_rank(rank, n, uid, prompt, n_new, q):
+def _nccl_rank(rank, n, uid, prompt, n_new, kind, q):
     import importlib
     import torch  # noqa: F401  (a process with torch keeps one NCCL copy)
     try:
+        os.environ["SLLM_CUDA_TP_EXCHANGE"] = kind
         cuda = importlib.import_module("saphira-llm_b200")
         comm = cuda.TpComm(uid, n, rank, rank)
         tm = cuda.TpModel(n, rank, rank, synth=_synth_desc(cuda))
         tc = tm.ctx(64, comm)
+        got = tc.exchange_kind()
         rc, toks = tc.generate(prompt, n_new)
         v0, lg = tc.last_logits()
-        q.put((rank, rc, toks.tolist(), v0, lg))
+        q.put((rank, rc if got == kind else -998, toks.tolist(), v0, lg))
         tc.close()
         tm.close()
         comm.close()
@@ -160,7 +163,10 @@ def _nccl_rank(rank, n, uid, prompt, n_new, q):
         q.put((rank, -999, repr(e), 0, None))
 
 
-def test_tp_nccl_two_gpus_matches_one(cuda):
+@pytest.mark.parametrize("kind", ["p2p", "nccl"])
+def test_tp_two_gpus_matches_one(cuda, kind):
+    """Two processes, one GPU each: the one-shot peer-memory exchange (P2P
+    stores and epoch flags) and NCCL's collectives give TP = 1's bits."""
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -172,7 +178,7 @@ def test_tp_nccl_two_gpus_matches_one(cuda):
     uid = cuda.tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_nccl_rank, args=(r, 2, uid, prompt, 12, q)) for r in range(2)]
+    procs = [ctx.Process(target=_nccl_rank, args=(r, 2, uid, prompt, 12, kind, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
