@@ -1,0 +1,154 @@
+// attn.cuh -- one query head of decode attention (src/forward.c:698-726),
+// shared by the standalone attention kernel (decode.cu, 256 threads) and the
+// persistent engine's attention stage (engine.cu, its 480 consumer threads).
+//
+// RoPE NEOX on q and k from the host angle table, the K/V append of this
+// position (by the first query head of each kv group), scores as sequential
+// f32 dots scaled by 1/sqrt(128), the softmax with a certified f64 sum (any
+// thread count: the interval covers every summation order, and the rare
+// ambiguous case re-sums in the reference's 8-block order), then P.V
+// sequential in s. NT threads; `sync` is the barrier of those NT threads.
+// Shared scratch: sc[n_ctx], qs[128], kcur[128], fred and dred with a slot
+// per warp, one float for the reciprocal.
+#pragma once
+
+#include "common.cuh"
+#include "decode.cuh"
+#include "libm_expf.h"
+
+namespace sllm {
+
+constexpr int kHeadDim = 128;
+
+template <int NT, class Sync>
+__device__ __forceinline__ void attention_head(const AttnParams& p, int h, int t, float* sc, float* qs, float* kcur,
+                                               float* fred, double* dred, float* s_inv_p, Sync sync) {
+    const int kvh = h / p.group;
+    const int pos = *(volatile const int32_t*)p.pos_ptr;
+    const int npast = pos + 1;
+    const int nctx = p.n_ctx;
+    const float* cs = p.rope_cos + (size_t)pos * (kHeadDim / 2);
+    const float* sn = p.rope_sin + (size_t)pos * (kHeadDim / 2);
+
+    // RoPE NEOX on q and on this head's k: pairs (i, i+64), angle table from
+    // the host (src/ops.c:529-549): x' = (xa*c - xb*s, xa*s + xb*c)
+    if (t < kHeadDim / 2) {
+        const float c = cs[t], s = sn[t];
+        // through L2: inside the engine another CTA wrote q, k, v in this launch
+        const float qa = __ldcg(p.q + h * kHeadDim + t), qb = __ldcg(p.q + h * kHeadDim + t + 64);
+        qs[t] = __fsub_rn(__fmul_rn(qa, c), __fmul_rn(qb, s));
+        qs[t + 64] = __fadd_rn(__fmul_rn(qa, s), __fmul_rn(qb, c));
+    } else if (t < kHeadDim) {
+        const int i = t - 64;
+        const float c = cs[i], s = sn[i];
+        const float ka = __ldcg(p.k + kvh * kHeadDim + i), kb = __ldcg(p.k + kvh * kHeadDim + i + 64);
+        kcur[i] = __fsub_rn(__fmul_rn(ka, c), __fmul_rn(kb, s));
+        kcur[i + 64] = __fadd_rn(__fmul_rn(ka, s), __fmul_rn(kb, c));
+    }
+    sync();
+
+    float* kT = p.k_cache + (size_t)kvh * kHeadDim * nctx;   // [d][pos]
+    float* vC = p.v_cache + (size_t)kvh * nctx * kHeadDim;   // [pos][d]
+    // the first query head of the group stores this position's K and V
+    // (src/forward.c:683-696); every CTA uses kcur / v directly for pos
+    if (h % p.group == 0 && t < kHeadDim) {
+        kT[(size_t)t * nctx + pos] = kcur[t];
+        vC[(size_t)pos * kHeadDim + t] = __ldcg(p.v + kvh * kHeadDim + t);
+    }
+
+    // scores: sequential f32 dot over d, then * 1/sqrt(hd) (src/forward.c:710-715);
+    // the K column is loaded 32 values at a time (same order of the adds)
+    for (int s = t; s < npast; s += NT) {
+        float acc = 0.0f;
+        if (s == pos) {
+            #pragma unroll 8
+            for (int d = 0; d < kHeadDim; ++d) acc = __fadd_rn(acc, __fmul_rn(qs[d], kcur[d]));
+        } else {
+            const float* col = kT + s;
+            #pragma unroll
+            for (int d0 = 0; d0 < kHeadDim; d0 += 32) {
+                float kv[32];
+                #pragma unroll
+                for (int j = 0; j < 32; ++j) kv[j] = col[(size_t)(d0 + j) * nctx];
+                #pragma unroll
+                for (int j = 0; j < 32; ++j) acc = __fadd_rn(acc, __fmul_rn(qs[d0 + j], kv[j]));
+            }
+        }
+        sc[s] = __fmul_rn(acc, p.attn_scale);
+    }
+    sync();
+
+    // softmax (src/ops.c:386-422)
+    float mx = -INFINITY;
+    for (int s = t; s < npast; s += NT) mx = fmaxf(mx, sc[s]);
+    mx = warp_max(mx);
+    if ((t & 31) == 0) fred[t >> 5] = mx;
+    sync();
+    mx = fred[0];
+    for (int i = 1; i < NT / 32; ++i) mx = fmaxf(mx, fred[i]);
+    // the reference's max is the first-seen maximum with '>' ; with no NaN
+    // it is the same value (a NaN score propagates identically below).
+    const int nblk = npast & ~7;
+    double part = 0.0;
+    for (int s = t; s < npast; s += NT) {
+        const float d = __fsub_rn(sc[s], mx);
+        const float e = (s < nblk) ? v_expf(d) : sllm_libm_expf(d);
+        sc[s] = e;
+        part = __dadd_rn(part, (double)e);
+    }
+    part = warp_sum_d(part);
+    sync();
+    if ((t & 31) == 0) dred[t >> 5] = part;
+    sync();
+    if (t == 0) {
+        double S = 0.0;
+        for (int i = 0; i < NT / 32; ++i) S = __dadd_rn(S, dred[i]);
+        // certified: any order of these npast non-negative terms lies within
+        // (npast + 64) * 2^-52 relative of the reference's; 1/x is monotone.
+        const double e = (double)(npast + 64) * 0x1p-52;
+        const float ia = __double2float_rn(__ddiv_rn(1.0, __dmul_ru(S, 1.0 + e)));
+        const float ib = __double2float_rn(__ddiv_rn(1.0, __dmul_rd(S, 1.0 - e)));
+        float inv = ia;
+        if (f2u(ia) != f2u(ib) || p.force_fallback) {
+            // reference order: per 8-block ((t0+t1)+t2)+t3 with
+            // t_k = e_k + e_{k+4}; the tail one at a time
+            double sum = 0.0;
+            int i = 0;
+            for (; i + 7 < npast; i += 8) {
+                const double t0 = __dadd_rn((double)sc[i + 0], (double)sc[i + 4]);
+                const double t1 = __dadd_rn((double)sc[i + 1], (double)sc[i + 5]);
+                const double t2 = __dadd_rn((double)sc[i + 2], (double)sc[i + 6]);
+                const double t3 = __dadd_rn((double)sc[i + 3], (double)sc[i + 7]);
+                sum = __dadd_rn(sum, __dadd_rn(__dadd_rn(__dadd_rn(t0, t1), t2), t3));
+            }
+            for (; i < npast; ++i) sum = __dadd_rn(sum, (double)sc[i]);
+            inv = __double2float_rn(__ddiv_rn(1.0, sum));
+            if (p.fallback_count != nullptr) atomicAdd(p.fallback_count, 1);
+        }
+        *s_inv_p = inv;
+    }
+    sync();
+    const float inv = *s_inv_p;
+    for (int s = t; s < npast; s += NT) sc[s] = __fmul_rn(sc[s], inv);
+    sync();
+
+    // o[d] = sum over s of w_s * v[s][d], sequential in s (src/forward.c:718-724)
+    if (t < kHeadDim) {
+        float o = 0.0f;
+        const float vcur = __ldcg(p.v + kvh * kHeadDim + t);
+        int s = 0;
+        for (; s + 16 <= pos; s += 16) {
+            float vv[16];
+            #pragma unroll
+            for (int j = 0; j < 16; ++j) vv[j] = vC[(size_t)(s + j) * kHeadDim + t];
+            #pragma unroll
+            for (int j = 0; j < 16; ++j) o = __fadd_rn(o, __fmul_rn(sc[s + j], vv[j]));
+        }
+        for (; s < pos; ++s) o = __fadd_rn(o, __fmul_rn(sc[s], vC[(size_t)s * kHeadDim + t]));
+        o = __fadd_rn(o, __fmul_rn(sc[pos], vcur));
+        p.out[h * kHeadDim + t] = o;
+    }
+}
+
+
+}  // namespace sllm

@@ -442,6 +442,7 @@ struct EngineProgram {
     EngGroup* groups = nullptr;
     EngOp* ops = nullptr;
     EngCursor* starts = nullptr;
+    AttnParams* attn = nullptr;
     unsigned* barrier = nullptr;
     int* error = nullptr;
     int n_stages = 0;
@@ -458,7 +459,7 @@ struct EngineProgram {
 
 static void engine_program_free(EngineProgram& p) {
     graph_exec_destroy(p.exec);
-    cudaFree(p.groups); cudaFree(p.ops); cudaFree(p.starts); cudaFree(p.barrier); cudaFree(p.error);
+    cudaFree(p.groups); cudaFree(p.ops); cudaFree(p.starts); cudaFree(p.attn); cudaFree(p.barrier); cudaFree(p.error);
     p = EngineProgram();
 }
 
@@ -475,7 +476,12 @@ std::vector<EngCursor> sllm::engine_starts(const std::vector<EngOp>& ops, const 
                                            int grid) {
     const int n_stages = (int)stage_first.size() - 1;
     std::vector<EngCursor> st((size_t)n_stages * (grid + 1));
-    auto row_cost = [&](int o) { return (double)(ops[o].K / 4) * (ops[o].epi == EPI_SILU ? 2 : 1); };
+    // an attention head costs about what 64 KB of weights take to stream, so
+    // the heads of a layer spread over separate CTAs
+    auto row_cost = [&](int o) {
+        if (ops[o].epi == kEpiAttention) return 65536.0;
+        return (double)(ops[o].K / 4) * (ops[o].epi == EPI_SILU ? 2 : 1);
+    };
     for (int s = 0; s < n_stages; ++s) {
         const int o0 = stage_first[s], o1 = stage_first[s + 1];
         EngCursor* out = &st[(size_t)s * (grid + 1)];
@@ -527,7 +533,8 @@ std::vector<EngCursor> sllm::engine_starts(const std::vector<EngOp>& ops, const 
 
 static int engine_program_build(EngineProgram& p, const std::vector<EngGroup>& groups, const std::vector<EngOp>& ops,
                                 const std::vector<int>& stage_first, int device, cudaStream_t capture_stream,
-                                int* fallback, int wa, int wb) {
+                                int* fallback, int wa, int wb, const std::vector<AttnParams>* attn = nullptr,
+                                bool graph = true) {
     engine_program_free(p);
     p.grid = engine_grid(device);
     p.n_stages = (int)stage_first.size() - 1;
@@ -541,8 +548,12 @@ static int engine_program_build(EngineProgram& p, const std::vector<EngGroup>& g
     if (e == cudaSuccess) e = cudaMemcpy(p.ops, ops.data(), ops.size() * sizeof(EngOp), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(p.starts, st.data(), st.size() * sizeof(EngCursor), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(p.error, 0, sizeof(int));
+    const int n_attn = attn != nullptr ? (int)attn->size() : 0;
+    if (e == cudaSuccess && n_attn > 0) e = cudaMalloc(&p.attn, n_attn * sizeof(AttnParams));
+    if (e == cudaSuccess && n_attn > 0)
+        e = cudaMemcpy(p.attn, attn->data(), n_attn * sizeof(AttnParams), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) { engine_program_free(p); return cuda_fail(e, "engine program"); }
-    if (engine_smem_bytes((int)groups.size(), (int)ops.size(), p.n_stages) == 0) {
+    if (engine_smem_bytes((int)groups.size(), (int)ops.size(), p.n_stages, n_attn) == 0) {
         engine_program_free(p);
         return fail(SLLM_CUDA_ERR_TOO_LARGE, "engine program: %zu ops do not fit in shared memory", ops.size());
     }
@@ -552,10 +563,12 @@ static int engine_program_build(EngineProgram& p, const std::vector<EngGroup>& g
     ep.n_groups = (int)groups.size(); ep.n_ops = (int)ops.size();
     ep.barrier = p.barrier; ep.error = p.error; ep.fallback_count = fallback; ep.force_fallback = g_force_fallback;
     ep.eps = g_engine_eps;     // every group of a program comes from one model
+    ep.attn = p.attn;
+    ep.n_attn = n_attn;
     p.params = ep;
     p.wa = wa;
     p.wb = wb;
-    if (p.n_stages == 1) {     // no grid barrier: no memset, no graph
+    if (p.n_stages == 1 || !graph) {     // no grid barrier, or launched inside the caller's graph
         p.built = true;
         return SLLM_CUDA_OK;
     }
@@ -616,6 +629,7 @@ struct sllm_cuda_ctx {
     size_t io_cap = 0;
     EngineProgram eng_chain;         // the layer chain on the persistent engine
     EngineProgram eng_proj;          // the independent projections on the persistent engine
+    EngineProgram eng_decode;        // every layer of a decode step, attention included
 };
 
 // the reference's angle recurrence (src/ops.c:529-549), on the host libm
@@ -653,6 +667,7 @@ extern "C" void sllm_cuda_ctx_free(sllm_cuda_ctx* c) {
     cudaFree(c->io);
     engine_program_free(c->eng_chain);
     engine_program_free(c->eng_proj);
+    engine_program_free(c->eng_decode);
     delete c;
 }
 
@@ -767,6 +782,21 @@ static cudaError_t enqueue_step(sllm_cuda_ctx* c, cudaStream_t st) {
     int* fb = fallback_counter();
     cudaError_t e = launch_embed(m->tok_embd, c->tok_seq, c->pos, m->n_embd, m->n_vocab, c->x, st);
     if (e != cudaSuccess) return e;
+    if (c->eng_decode.built) {
+        // every layer in one engine launch: 5 stages each (Q/K/V, attention,
+        // O, gate/up, down) behind grid barriers
+        e = cudaMemsetAsync(c->eng_decode.barrier, 0, sizeof(unsigned), st);
+        if (e == cudaSuccess)
+            e = launch_engine(c->eng_decode.params, c->eng_decode.grid, st, c->eng_decode.wa, c->eng_decode.wb);
+        if (e != cudaSuccess) return e;
+        LmParams lp{};
+        lp.x = c->x; lp.norm_w = m->output_norm; lp.eps = m->eps; lp.embd = m->tok_embd;
+        lp.E = m->n_embd; lp.V = m->n_vocab; lp.logits = c->logits;
+        lp.part_v = c->part_v; lp.part_i = c->part_i; lp.counter = c->counter; lp.argmax_out = c->argmax;
+        lp.pos_ptr = c->pos; lp.tok_seq = c->tok_seq; lp.prompt_end = c->prompt_end; lp.argmax_hist = c->argmax_hist;
+        lp.n_ctx = c->n_ctx; lp.fallback_count = fb; lp.force_fallback = g_force_fallback;
+        return launch_lm_head(lp, c->lm_grid, st);
+    }
     const size_t kv_layer = (size_t)m->n_embd_gqa * (size_t)c->n_ctx;
     for (int l = 0; l < m->n_layer; ++l) {
         AttnParams ap{};
@@ -791,8 +821,12 @@ static cudaError_t enqueue_step(sllm_cuda_ctx* c, cudaStream_t st) {
     return launch_lm_head(lp, c->lm_grid, st);
 }
 
+static int decode_program(sllm_cuda_ctx* c);
+
 static int ensure_step_graph(sllm_cuda_ctx* c) {
     if (c->step != nullptr) return SLLM_CUDA_OK;
+    const int rc = decode_program(c);
+    if (rc != SLLM_CUDA_OK) return rc;
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
     cudaError_t e = enqueue_step(c, c->stream);
@@ -897,6 +931,68 @@ extern "C" int sllm_cuda_ctx_last_logits(const sllm_cuda_ctx* c, float* host_out
     CK(cudaSetDevice(c->m->device), "cudaSetDevice");
     CK(cudaMemcpy(host_out, c->logits, (size_t)c->m->n_vocab * 4, cudaMemcpyDeviceToHost), "last logits");
     return SLLM_CUDA_OK;
+}
+
+// The decode step's layers as one engine program: per layer Q/K/V, attention,
+// O + residual, gate/up, down + residual, each a stage behind a grid barrier
+// (src/forward.c:628-801). Built when the model's widths are compiled into
+// the engine, the context fits the attention scratch, and the tables fit in
+// shared memory; otherwise the step runs the per-GEMV kernels.
+static int decode_program(sllm_cuda_ctx* c) {
+    const sllm_cuda_model* m = c->m;
+    if (c->eng_decode.built) return SLLM_CUDA_OK;
+    const int E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa;
+    if (!engine_supports(engine_wpl(E), engine_wpl(F)) || c->n_ctx > kEngAttnMaxCtx || m->head_dim != 128)
+        return SLLM_CUDA_OK;
+    int* fb = fallback_counter();
+    std::vector<EngGroup> groups;
+    std::vector<EngOp> ops;
+    std::vector<int> stage_first;
+    std::vector<AttnParams> attn;
+    auto op = [&](const uint8_t* w, const uint8_t* w2, float* y, const float* resid, float* h, int rows, int K,
+                  int epi, int group, float ws, float ws2) {
+        EngOp o{};
+        o.w = w; o.w2 = w2; o.y = y; o.resid = resid; o.h = h; o.rows = rows; o.K = K; o.epi = epi; o.group = group;
+        o.chunk_rows = epi == kEpiAttention ? 1 : engine_chunk_rows(K, epi);
+        o.ws = ws; o.ws2 = ws2;
+        ops.push_back(o);
+    };
+    const size_t kv_layer = (size_t)G * (size_t)c->n_ctx;
+    for (int l = 0; l < m->n_layer; ++l) {
+        const DevLayer& L = m->layers[l];
+        stage_first.push_back((int)ops.size());
+        groups.push_back(EngGroup{c->x, L.attn_norm, E, PRO_NORM});
+        op(L.wq, nullptr, c->q, nullptr, nullptr, E, E, EPI_F32, (int)groups.size() - 1, L.s_wq, 0.f);
+        op(L.wk, nullptr, c->k, nullptr, nullptr, G, E, EPI_F32, (int)groups.size() - 1, L.s_wk, 0.f);
+        op(L.wv, nullptr, c->v, nullptr, nullptr, G, E, EPI_F32, (int)groups.size() - 1, L.s_wv, 0.f);
+        stage_first.push_back((int)ops.size());
+        AttnParams ap{};
+        ap.q = c->q; ap.k = c->k; ap.v = c->v;
+        ap.k_cache = c->k_cache + (size_t)l * kv_layer;
+        ap.v_cache = c->v_cache + (size_t)l * kv_layer;
+        ap.rope_cos = c->rope_cos; ap.rope_sin = c->rope_sin;
+        ap.pos_ptr = c->pos; ap.out = c->attn; ap.n_ctx = c->n_ctx;
+        ap.group = m->n_head / m->n_head_kv;
+        ap.attn_scale = 1.0f / sqrtf((float)m->head_dim);
+        ap.fallback_count = fb; ap.force_fallback = g_force_fallback;
+        attn.push_back(ap);
+        op(nullptr, nullptr, c->attn, nullptr, nullptr, m->n_head, c->n_ctx, kEpiAttention, l, 0.f, 0.f);
+        stage_first.push_back((int)ops.size());
+        groups.push_back(EngGroup{c->attn, L.attn_sub_norm, E, PRO_NORM});
+        op(L.wo, nullptr, c->ffn_inp, c->x, nullptr, E, E, EPI_RESID, (int)groups.size() - 1, L.s_wo, 0.f);
+        stage_first.push_back((int)ops.size());
+        groups.push_back(EngGroup{c->ffn_inp, L.ffn_norm, E, PRO_NORM});
+        op(L.gate, L.up, nullptr, nullptr, c->h, F, E, EPI_SILU, (int)groups.size() - 1, L.s_gate, L.s_up);
+        stage_first.push_back((int)ops.size());
+        groups.push_back(EngGroup{c->h, L.ffn_sub_norm, F, PRO_NORM});
+        op(L.down, nullptr, c->x, c->ffn_inp, nullptr, E, F, EPI_RESID, (int)groups.size() - 1, L.s_down, 0.f);
+    }
+    stage_first.push_back((int)ops.size());
+    if (engine_smem_bytes((int)groups.size(), (int)ops.size(), (int)stage_first.size() - 1, (int)attn.size()) == 0)
+        return SLLM_CUDA_OK;       // too many layers for the tables: the per-GEMV step
+    g_engine_eps = m->eps;
+    return engine_program_build(c->eng_decode, groups, ops, stage_first, m->device, c->stream, fb, engine_wpl(E),
+                                engine_wpl(F), &attn, false);
 }
 
 // ---------------------------------------------------------------------------

@@ -12,6 +12,7 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "libm_expf.h"
+#include "attn.cuh"
 
 namespace sllm {
 
@@ -51,7 +52,10 @@ __global__ void embed_kernel(const uint16_t* __restrict__ tok_embd, const int32_
 // attention for one query position, one CTA per query head
 // ---------------------------------------------------------------------------
 constexpr int kAttnThreads = 256;
-constexpr int kHeadDim = 128;
+
+struct CtaSync {
+    __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
 
 __global__ void __launch_bounds__(kAttnThreads)
 attention_kernel(const AttnParams p) {
@@ -60,126 +64,9 @@ attention_kernel(const AttnParams p) {
     __shared__ float fred[32];
     __shared__ double dred[32];
     __shared__ float s_inv;
-    const int h = blockIdx.x, t = threadIdx.x;
-    const int kvh = h / p.group;
     pdl_trigger_d();
     pdl_wait_d();                 // q, k, v come from the previous kernel
-    const int pos = *p.pos_ptr;
-    const int npast = pos + 1;
-    const int nctx = p.n_ctx;
-    const float* cs = p.rope_cos + (size_t)pos * (kHeadDim / 2);
-    const float* sn = p.rope_sin + (size_t)pos * (kHeadDim / 2);
-
-    // RoPE NEOX on q and on this head's k: pairs (i, i+64), angle table from
-    // the host (src/ops.c:529-549): x' = (xa*c - xb*s, xa*s + xb*c)
-    if (t < kHeadDim / 2) {
-        const float c = cs[t], s = sn[t];
-        const float qa = p.q[h * kHeadDim + t], qb = p.q[h * kHeadDim + t + 64];
-        qs[t] = __fsub_rn(__fmul_rn(qa, c), __fmul_rn(qb, s));
-        qs[t + 64] = __fadd_rn(__fmul_rn(qa, s), __fmul_rn(qb, c));
-    } else if (t < kHeadDim) {
-        const int i = t - 64;
-        const float c = cs[i], s = sn[i];
-        const float ka = p.k[kvh * kHeadDim + i], kb = p.k[kvh * kHeadDim + i + 64];
-        kcur[i] = __fsub_rn(__fmul_rn(ka, c), __fmul_rn(kb, s));
-        kcur[i + 64] = __fadd_rn(__fmul_rn(ka, s), __fmul_rn(kb, c));
-    }
-    __syncthreads();
-
-    float* kT = p.k_cache + (size_t)kvh * kHeadDim * nctx;   // [d][pos]
-    float* vC = p.v_cache + (size_t)kvh * nctx * kHeadDim;   // [pos][d]
-    // the first query head of the group stores this position's K and V
-    // (src/forward.c:683-696); every CTA uses kcur / v directly for pos
-    if (h % p.group == 0 && t < kHeadDim) {
-        kT[(size_t)t * nctx + pos] = kcur[t];
-        vC[(size_t)pos * kHeadDim + t] = p.v[kvh * kHeadDim + t];
-    }
-
-    // scores: sequential f32 dot over d, then * 1/sqrt(hd) (src/forward.c:710-715)
-    for (int s = t; s < npast; s += kAttnThreads) {
-        float acc = 0.0f;
-        if (s == pos) {
-            #pragma unroll 8
-            for (int d = 0; d < kHeadDim; ++d) acc = __fadd_rn(acc, __fmul_rn(qs[d], kcur[d]));
-        } else {
-            const float* col = kT + s;
-            #pragma unroll 16
-            for (int d = 0; d < kHeadDim; ++d) acc = __fadd_rn(acc, __fmul_rn(qs[d], col[(size_t)d * nctx]));
-        }
-        sc[s] = __fmul_rn(acc, p.attn_scale);
-    }
-    __syncthreads();
-
-    // softmax (src/ops.c:386-422)
-    float mx = -INFINITY;
-    for (int s = t; s < npast; s += kAttnThreads) mx = fmaxf(mx, sc[s]);
-    mx = warp_max(mx);
-    if ((t & 31) == 0) fred[t >> 5] = mx;
-    __syncthreads();
-    mx = fred[0];
-    for (int i = 1; i < kAttnThreads / 32; ++i) mx = fmaxf(mx, fred[i]);
-    // the reference's max is the first-seen maximum with '>' ; with no NaN
-    // it is the same value (a NaN score propagates identically below).
-    const int nblk = npast & ~7;
-    double part = 0.0;
-    for (int s = t; s < npast; s += kAttnThreads) {
-        const float d = __fsub_rn(sc[s], mx);
-        const float e = (s < nblk) ? v_expf(d) : sllm_libm_expf(d);
-        sc[s] = e;
-        part = __dadd_rn(part, (double)e);
-    }
-    part = warp_sum_d(part);
-    __syncthreads();
-    if ((t & 31) == 0) dred[t >> 5] = part;
-    __syncthreads();
-    if (t == 0) {
-        double S = 0.0;
-        for (int i = 0; i < kAttnThreads / 32; ++i) S = __dadd_rn(S, dred[i]);
-        // certified: any order of these npast non-negative terms lies within
-        // (npast + 64) * 2^-52 relative of the reference's; 1/x is monotone.
-        const double e = (double)(npast + 64) * 0x1p-52;
-        const float ia = __double2float_rn(__ddiv_rn(1.0, __dmul_ru(S, 1.0 + e)));
-        const float ib = __double2float_rn(__ddiv_rn(1.0, __dmul_rd(S, 1.0 - e)));
-        float inv = ia;
-        if (f2u(ia) != f2u(ib) || p.force_fallback) {
-            // reference order: per 8-block ((t0+t1)+t2)+t3 with
-            // t_k = e_k + e_{k+4}; the tail one at a time
-            double sum = 0.0;
-            int i = 0;
-            for (; i + 7 < npast; i += 8) {
-                const double t0 = __dadd_rn((double)sc[i + 0], (double)sc[i + 4]);
-                const double t1 = __dadd_rn((double)sc[i + 1], (double)sc[i + 5]);
-                const double t2 = __dadd_rn((double)sc[i + 2], (double)sc[i + 6]);
-                const double t3 = __dadd_rn((double)sc[i + 3], (double)sc[i + 7]);
-                sum = __dadd_rn(sum, __dadd_rn(__dadd_rn(__dadd_rn(t0, t1), t2), t3));
-            }
-            for (; i < npast; ++i) sum = __dadd_rn(sum, (double)sc[i]);
-            inv = __double2float_rn(__ddiv_rn(1.0, sum));
-            if (p.fallback_count != nullptr) atomicAdd(p.fallback_count, 1);
-        }
-        s_inv = inv;
-    }
-    __syncthreads();
-    const float inv = s_inv;
-    for (int s = t; s < npast; s += kAttnThreads) sc[s] = __fmul_rn(sc[s], inv);
-    __syncthreads();
-
-    // o[d] = sum over s of w_s * v[s][d], sequential in s (src/forward.c:718-724)
-    if (t < kHeadDim) {
-        float o = 0.0f;
-        const float vcur = p.v[kvh * kHeadDim + t];
-        int s = 0;
-        for (; s + 8 <= pos; s += 8) {
-            float vv[8];
-            #pragma unroll
-            for (int j = 0; j < 8; ++j) vv[j] = vC[(size_t)(s + j) * kHeadDim + t];
-            #pragma unroll
-            for (int j = 0; j < 8; ++j) o = __fadd_rn(o, __fmul_rn(sc[s + j], vv[j]));
-        }
-        for (; s < pos; ++s) o = __fadd_rn(o, __fmul_rn(sc[s], vC[(size_t)s * kHeadDim + t]));
-        o = __fadd_rn(o, __fmul_rn(sc[pos], vcur));
-        p.out[h * kHeadDim + t] = o;
-    }
+    attention_head<kAttnThreads>(p, blockIdx.x, threadIdx.x, sc, qs, kcur, fred, dred, &s_inv, CtaSync());
 }
 
 // ---------------------------------------------------------------------------
@@ -194,7 +81,6 @@ attention_kernel(const AttnParams p) {
 // ---------------------------------------------------------------------------
 constexpr int kLmThreads = 512;
 constexpr int kLmWarps = kLmThreads / 32;
-constexpr int kLmUnroll = 16;
 
 struct Best { float v; int i; };
 
@@ -240,43 +126,58 @@ lm_head_kernel(const LmParams p) {
     for (int i = tid; i < E; i += kLmThreads) xs[i] = __fmul_rn(__fmul_rn(sc, xs[i]), p.norm_w[i]);
     __syncthreads();
 
-    const int half = lane >> 4, c = lane & 15;
+    // Four lanes per vocabulary row, eight rows per warp. Lane j of a row
+    // owns the reference's accumulators acc[j][0..7] (src/ops.c:120-130):
+    // at step m it loads the 16 bytes of elements 32m + 8j .. 32m + 8j + 7 and
+    // runs one FMA chain per element slot, in the reference's order.
+    const int sub = lane >> 2, j4 = lane & 3;
     const int nsteps = E >> 5;
-    const int npairs = (p.V + 1) >> 1;
+    const int ngroups = (p.V + 7) >> 3;
     float bv = NAN;
     int bi = 0x7fffffff;
-    for (int pr = blockIdx.x * kLmWarps + warp; pr < npairs; pr += gridDim.x * kLmWarps) {
-        const int row = 2 * pr + half;
+    constexpr int U = 8;
+    for (int grp = blockIdx.x * kLmWarps + warp; grp < ngroups; grp += gridDim.x * kLmWarps) {
+        const int row = 8 * grp + sub;
         const bool valid = row < p.V;
-        const uint32_t* wrow = reinterpret_cast<const uint32_t*>(p.embd + (size_t)(valid ? row : 0) * (size_t)E);
-        float a0 = 0.0f, a1 = 0.0f;
-        for (int m0 = 0; m0 < nsteps; m0 += kLmUnroll) {
-            uint32_t wv[kLmUnroll];
+        const uint8_t* wrow = reinterpret_cast<const uint8_t*>(p.embd + (size_t)(valid ? row : 0) * (size_t)E) + 16 * j4;
+        float a[8];
+        #pragma unroll
+        for (int l = 0; l < 8; ++l) a[l] = 0.0f;
+        for (int m0 = 0; m0 < nsteps; m0 += U) {
+            uint4 wv[U];
             #pragma unroll
-            for (int j = 0; j < kLmUnroll; ++j)
-                wv[j] = (m0 + j < nsteps) ? ld_stream_u32(wrow + 16 * (m0 + j) + c) : 0u;
+            for (int u = 0; u < U; ++u) wv[u] = (m0 + u < nsteps) ? ld_stream_u128(wrow + 64 * (m0 + u)) : make_uint4(0, 0, 0, 0);
             #pragma unroll
-            for (int j = 0; j < kLmUnroll; ++j) {
-                if (m0 + j < nsteps) {
-                    const float2 wf = __half22float2(*reinterpret_cast<const __half2*>(&wv[j]));
-                    const float2 xf = *reinterpret_cast<const float2*>(xs + 32 * (m0 + j) + 2 * c);
-                    a0 = __fmaf_rn(wf.x, xf.x, a0);
-                    a1 = __fmaf_rn(wf.y, xf.y, a1);
+            for (int u = 0; u < U; ++u) {
+                if (m0 + u < nsteps) {
+                    const float4* xv = reinterpret_cast<const float4*>(xs + 32 * (m0 + u) + 8 * j4);
+                    const float4 x0 = xv[0], x1 = xv[1];
+                    const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u].x));
+                    const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u].y));
+                    const float2 w45 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u].z));
+                    const float2 w67 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u].w));
+                    a[0] = __fmaf_rn(w01.x, x0.x, a[0]);
+                    a[1] = __fmaf_rn(w01.y, x0.y, a[1]);
+                    a[2] = __fmaf_rn(w23.x, x0.z, a[2]);
+                    a[3] = __fmaf_rn(w23.y, x0.w, a[3]);
+                    a[4] = __fmaf_rn(w45.x, x1.x, a[4]);
+                    a[5] = __fmaf_rn(w45.y, x1.y, a[5]);
+                    a[6] = __fmaf_rn(w67.x, x1.z, a[6]);
+                    a[7] = __fmaf_rn(w67.y, x1.w, a[7]);
                 }
             }
         }
-        // tree, within each 16-lane half
-        a0 = __fadd_rn(a0, __shfl_down_sync(0xffffffffu, a0, 8));
-        a1 = __fadd_rn(a1, __shfl_down_sync(0xffffffffu, a1, 8));
-        a0 = __fadd_rn(a0, __shfl_down_sync(0xffffffffu, a0, 4));
-        a1 = __fadd_rn(a1, __shfl_down_sync(0xffffffffu, a1, 4));
-        a0 = __fadd_rn(a0, __shfl_down_sync(0xffffffffu, a0, 2));
-        a1 = __fadd_rn(a1, __shfl_down_sync(0xffffffffu, a1, 2));
-        // lane c=0 holds t0, t1; lane c=1 holds t2, t3
-        const float pairsum = __fadd_rn(a0, a1);
-        const float other = __shfl_down_sync(0xffffffffu, pairsum, 1);
-        const float logit = __fadd_rn(pairsum, other);
-        if (c == 0 && valid) {
+        // the reference's tree (src/ops.c:135-143): acc0 += acc2, acc1 += acc3
+        // (lanes j4 = 0, 1 add lanes 2, 3), then acc0 += acc1, then
+        // t_l = acc0[l] + acc0[l + 4] and (t0 + t1) + (t2 + t3)
+        #pragma unroll
+        for (int l = 0; l < 8; ++l) a[l] = __fadd_rn(a[l], __shfl_down_sync(0xffffffffu, a[l], 2));
+        #pragma unroll
+        for (int l = 0; l < 8; ++l) a[l] = __fadd_rn(a[l], __shfl_down_sync(0xffffffffu, a[l], 1));
+        const float t0 = __fadd_rn(a[0], a[4]), t1 = __fadd_rn(a[1], a[5]);
+        const float t2 = __fadd_rn(a[2], a[6]), t3 = __fadd_rn(a[3], a[7]);
+        const float logit = __fadd_rn(__fadd_rn(t0, t1), __fadd_rn(t2, t3));
+        if (j4 == 0 && valid) {
             p.logits[row] = logit;
             if (better(logit, row, bv, bi)) { bv = logit; bi = row; }
         }

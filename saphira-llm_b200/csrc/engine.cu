@@ -23,6 +23,7 @@
 // every barrier, so the kernel always terminates; the producer then waits
 // (bounded) for its own copies in flight before it exits.
 
+#include "attn.cuh"
 #include "common.cuh"
 #include "engine.cuh"
 
@@ -85,6 +86,10 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t b
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kEngConsumerWarps * 32) : "memory");
 }
+
+struct ConsumerSync {
+    __device__ __forceinline__ void operator()() const { consumer_sync(); }
+};
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
@@ -497,6 +502,7 @@ i2s_engine_kernel(const EngParams P) {
     EngOp* s_ops = reinterpret_cast<EngOp*>(smem + kEngSlots * kEngSlotBytes + 8192);
     EngGroup* s_groups = reinterpret_cast<EngGroup*>(s_ops + P.n_ops);
     EngCursor* s_cur = reinterpret_cast<EngCursor*>(s_groups + P.n_groups);   // [n_stages][2]
+    AttnParams* s_attn = reinterpret_cast<AttnParams*>(s_cur + 2 * P.n_stages);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, c = blockIdx.x;
 
@@ -514,6 +520,10 @@ i2s_engine_kernel(const EngParams P) {
             const int st = i >> 1;
             s_cur[i] = P.starts[(size_t)st * (G + 1) + c + (i & 1)];
         }
+        static_assert(sizeof(AttnParams) % 8 == 0 && sizeof(EngCursor) % 8 == 0, "table copy granularity");
+        const int2* asrc = reinterpret_cast<const int2*>(P.attn);
+        int2* adst = reinterpret_cast<int2*>(s_attn);
+        for (int i = tid; i < (int)(P.n_attn * sizeof(AttnParams) / 8); i += blockDim.x) adst[i] = __ldg(asrc + i);
     }
 
     if (tid == 0) {
@@ -535,6 +545,23 @@ i2s_engine_kernel(const EngParams P) {
                 ChunkWalk walk{s_ops, s_cur[2 * s].op, s_cur[2 * s].row, s_cur[2 * s + 1]};
                 int o, r, n, last_group = -1;
                 while (walk.next(o, r, n)) {
+                    if (s_ops[o].epi == kEpiAttention) {
+                        // no weights to stream; instead the KV cache its heads
+                        // will read (positions < pos), into L2 a stage ahead
+                        const AttnParams& ap = s_attn[s_ops[o].group];
+                        const int pos = *(volatile const int32_t*)ap.pos_ptr;
+                        for (int h = r; h < r + n && pos > 0; ++h) {
+                            const int kvh = h / ap.group;
+                            const float* vC = ap.v_cache + (size_t)kvh * ap.n_ctx * 128;
+                            prefetch_l2(vC, (uint32_t)pos * 128u * 4u);
+                            if ((ap.n_ctx & 3) == 0) {
+                                const float* kT = ap.k_cache + (size_t)kvh * 128 * ap.n_ctx;
+                                const uint32_t bytes = ((uint32_t)pos * 4u + 15u) & ~15u;
+                                for (int d = 0; d < 128; ++d) prefetch_l2(kT + (size_t)d * ap.n_ctx, bytes);
+                            }
+                        }
+                        continue;
+                    }
                     // the norm vector of a group this CTA reaches: into L2 as the
                     // producer gets to it, up to a ring ahead of the prologue
                     const int gi = s_ops[o].group;
@@ -608,6 +635,18 @@ i2s_engine_kernel(const EngParams P) {
             // this CTA's rows of op o in this stage: [r, r_end)
             const int r_end = o == walk.end.op ? walk.end.row : op.rows;
             walk.row = r_end;
+            if (op.epi == kEpiAttention) {
+                // decode attention, one query head per row; the scores use the
+                // activation area, so the next op rebuilds its activations
+                float* sc = reinterpret_cast<float*>(qs);
+                float* hq = sc + kEngAttnMaxCtx;
+                for (int head = r; head < r_end; ++head)
+                    attention_head<kEngConsumerWarps * 32>(s_attn[op.group], head, tid, sc, hq, hq + kHeadDim,
+                                                           es.fred, es.dred, &es.fallback_mean, ConsumerSync());
+                consumer_sync();
+                cur_group = -1;
+                continue;
+            }
             if (op.group != cur_group) {
                 act = eng_prologue(s_groups[op.group], P, qs, es, tid, warp, lane);
                 cur_group = op.group;
@@ -652,9 +691,11 @@ int engine_chunk_rows(int K, int epi) {
     return rows;
 }
 
-int engine_smem_bytes(int n_groups, int n_ops, int n_stages) {
+int engine_smem_bytes(int n_groups, int n_ops, int n_stages, int n_attn) {
+    static_assert(kEngAttnMaxCtx * 4 + 2 * kHeadDim * 4 <= 8192, "attention scratch fits the activation area");
     const size_t b = (size_t)kEngSlots * kEngSlotBytes + 8192 + (size_t)n_ops * sizeof(EngOp) +
-                     (size_t)n_groups * sizeof(EngGroup) + (size_t)n_stages * 2 * sizeof(EngCursor);
+                     (size_t)n_groups * sizeof(EngGroup) + (size_t)n_stages * 2 * sizeof(EngCursor) +
+                     (size_t)n_attn * sizeof(AttnParams);
     const size_t limit = 227 * 1024 - sizeof(EngSmem) - 64;
     return b <= limit ? (int)b : 0;
 }
@@ -686,7 +727,7 @@ cudaError_t prepare_engine() {
 }
 
 cudaError_t launch_engine(const EngParams& p, int grid, cudaStream_t st, int wa, int wb) {
-    const int smem = engine_smem_bytes(p.n_groups, p.n_ops, p.n_stages);
+    const int smem = engine_smem_bytes(p.n_groups, p.n_ops, p.n_stages, p.n_attn);
     if (smem == 0) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);

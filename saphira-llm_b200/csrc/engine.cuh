@@ -13,6 +13,7 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "decode.cuh"
 #include "gemv.cuh"
 
 namespace sllm {
@@ -21,6 +22,13 @@ constexpr int kEngConsumerWarps = 15;    // + 1 producer: 16 warps, 4 per SM sub
 constexpr int kEngThreads = (kEngConsumerWarps + 1) * 32;
 constexpr int kEngSlotBytes = 48 * 1024;   // a slot holds one chunk: whole weight rows of one op
 constexpr int kEngSlots = 4;
+
+// An op of this kind is one layer's decode attention: its rows are the query
+// heads, its `group` indexes EngParams::attn, and it streams no weights.
+constexpr int kEpiAttention = 4;
+// the longest context an attention op takes (its scores live in the CTA's
+// 8 KB activation area, beside two 128-float vectors)
+constexpr int kEngAttnMaxCtx = 1792;
 
 // an input vector and how each CTA turns it into int8 activations
 struct EngGroup {
@@ -66,6 +74,8 @@ struct EngParams {
     float eps;
     int* fallback_count;         // nullable
     int force_fallback;
+    const AttnParams* attn;      // [n_attn]: the attention ops' layers
+    int n_attn;
 };
 
 enum EngError { ENG_OK = 0, ENG_TIMEOUT_FULL = 1, ENG_TIMEOUT_EMPTY = 2, ENG_TIMEOUT_GRID = 3, ENG_BAD_PROGRAM = 4 };
@@ -74,7 +84,7 @@ enum EngError { ENG_OK = 0, ENG_TIMEOUT_FULL = 1, ENG_TIMEOUT_EMPTY = 2, ENG_TIM
 int engine_chunk_rows(int K, int epi);
 // dynamic shared memory of a program: the ring, the int8 activations, and the
 // group / op / cursor tables every CTA copies in at start (0 when too large)
-int engine_smem_bytes(int n_groups, int n_ops, int n_stages);
+int engine_smem_bytes(int n_groups, int n_ops, int n_stages, int n_attn = 0);
 int engine_grid(int device);
 // the engine is compiled for pairs (wpl(n_embd), wpl(n_ff)) of row widths,
 // wpl(K) = 32-bit words per lane = ceil(K / 512)

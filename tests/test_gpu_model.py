@@ -223,3 +223,20 @@ def test_engine_fallback_path(cuda, orc, synth):
     want = orc.layer_chain(m.desc(), 1, orc.layer_chain(m.desc(), 0, x))
     assert np.array_equal(bits(got), bits(want))
     assert after > before
+
+
+def test_decode_step_runs_on_the_engine(cuda, orc, synth):
+    """The decode step is one engine launch for every layer (attention as a
+    stage) between the embedding and the head: 3 kernels per token, and the
+    tokens and logits stay the oracle's."""
+    cfg, m, model, gc, oc = _pair(cuda, orc, synth, CONFIGS[1][0], 41, 64)
+    prompt = np.random.default_rng(41).integers(0, cfg.n_vocab, 6).astype(np.int32)
+    r1, t1 = gc.generate(prompt[:2], 1)       # builds the step graph
+    gc.reset()
+    k0 = cuda.kernel_launches()
+    r1, t1 = gc.generate(prompt, 10)
+    per_step = (cuda.kernel_launches() - k0) / (len(prompt) + 10)
+    r2, t2 = oc.generate(prompt, 10)
+    assert r1 == r2 == 0 and t1.tolist() == t2.tolist()
+    assert np.array_equal(bits(gc.last_logits()), bits(oc.last_logits()))
+    assert per_step == 3, per_step
