@@ -9,7 +9,16 @@
 // ambiguous case re-sums in the reference's 8-block order), then P.V
 // sequential in s. NT threads; `sync` is the barrier of those NT threads.
 // Shared scratch: sc[n_ctx], qs[128], kcur[128], fred and dred with a slot
-// per warp, one float for the reciprocal.
+// per warp.
+//
+// Every sum keeps the reference's order, so the time is latency: the chains
+// of dependent adds and the L2 round trips that feed them. The last 128
+// threads run P.V, one per dimension, with 64 V rows in flight: four batches
+// of 16 in registers, each refilled with the rows 64 further on as soon as it
+// has been added. The normalisation is folded into P.V: the weight
+// fl(e_s * inv) is formed as the reference stores it, then multiplied by v.
+// Two barriers separate scores, exponentials and P.V; every thread forms the
+// certified reciprocal itself.
 #pragma once
 
 #include "common.cuh"
@@ -22,13 +31,18 @@ constexpr int kHeadDim = 128;
 
 template <int NT, class Sync>
 __device__ __forceinline__ void attention_head(const AttnParams& p, int h, int t, float* sc, float* qs, float* kcur,
-                                               float* fred, double* dred, float* s_inv_p, Sync sync) {
+                                               float* fred, double* dred, Sync sync) {
+    static_assert(NT % 32 == 0 && NT >= 2 * kHeadDim, "two 128-thread teams at least");
     const int kvh = h / p.group;
     const int pos = *(volatile const int32_t*)p.pos_ptr;
     const int npast = pos + 1;
     const int nctx = p.n_ctx;
     const float* cs = p.rope_cos + (size_t)pos * (kHeadDim / 2);
     const float* sn = p.rope_sin + (size_t)pos * (kHeadDim / 2);
+    float* kT = p.k_cache + (size_t)kvh * kHeadDim * nctx;   // [d][pos]
+    float* vC = p.v_cache + (size_t)kvh * nctx * kHeadDim;   // [pos][d]
+    const int pv_d = t - (NT - kHeadDim);                   // this thread's P.V dimension, < 0: none
+
 
     // RoPE NEOX on q and on this head's k: pairs (i, i+64), angle table from
     // the host (src/ops.c:529-549): x' = (xa*c - xb*s, xa*s + xb*c)
@@ -47,18 +61,37 @@ __device__ __forceinline__ void attention_head(const AttnParams& p, int h, int t
     }
     sync();
 
-    float* kT = p.k_cache + (size_t)kvh * kHeadDim * nctx;   // [d][pos]
-    float* vC = p.v_cache + (size_t)kvh * nctx * kHeadDim;   // [pos][d]
     // the first query head of the group stores this position's K and V
-    // (src/forward.c:683-696); every CTA uses kcur / v directly for pos
+    // (src/forward.c:683-696); every head uses kcur / v directly for pos
     if (h % p.group == 0 && t < kHeadDim) {
         kT[(size_t)t * nctx + pos] = kcur[t];
         vC[(size_t)pos * kHeadDim + t] = __ldcg(p.v + kvh * kHeadDim + t);
     }
 
-    // scores: sequential f32 dot over d, then * 1/sqrt(hd) (src/forward.c:710-715);
-    // the K column is loaded 32 values at a time (same order of the adds)
-    for (int s = t; s < npast; s += NT) {
+    // scores: sequential f32 dot over d, then * 1/sqrt(hd) (src/forward.c:710-715)
+    float mx = -INFINITY;
+    if (t < pos) {
+        float acc = 0.0f;
+        const float* col = kT + t;
+        #pragma unroll
+        for (int d0 = 0; d0 < kHeadDim; d0 += 32) {
+            float kv[32];
+            #pragma unroll
+            for (int j = 0; j < 32; ++j) kv[j] = col[(size_t)(d0 + j) * nctx];
+            #pragma unroll
+            for (int j = 0; j < 32; ++j) acc = __fadd_rn(acc, __fmul_rn(qs[d0 + j], kv[j]));
+        }
+        sc[t] = __fmul_rn(acc, p.attn_scale);
+        mx = fmaxf(mx, sc[t]);
+    } else if (t == pos) {
+        float acc = 0.0f;
+        #pragma unroll 8
+        for (int d = 0; d < kHeadDim; ++d) acc = __fadd_rn(acc, __fmul_rn(qs[d], kcur[d]));
+        sc[t] = __fmul_rn(acc, p.attn_scale);
+        mx = fmaxf(mx, sc[t]);
+    }
+    // keys beyond the first NT (contexts longer than the thread count)
+    for (int s = t + NT; s < npast; s += NT) {
         float acc = 0.0f;
         if (s == pos) {
             #pragma unroll 8
@@ -75,19 +108,16 @@ __device__ __forceinline__ void attention_head(const AttnParams& p, int h, int t
             }
         }
         sc[s] = __fmul_rn(acc, p.attn_scale);
+        mx = fmaxf(mx, sc[s]);
     }
-    sync();
-
-    // softmax (src/ops.c:386-422)
-    float mx = -INFINITY;
-    for (int s = t; s < npast; s += NT) mx = fmaxf(mx, sc[s]);
     mx = warp_max(mx);
     if ((t & 31) == 0) fred[t >> 5] = mx;
     sync();
-    mx = fred[0];
-    for (int i = 1; i < NT / 32; ++i) mx = fmaxf(mx, fred[i]);
-    // the reference's max is the first-seen maximum with '>' ; with no NaN
-    // it is the same value (a NaN score propagates identically below).
+
+    // softmax (src/ops.c:386-422). The reference's max is the first-seen
+    // maximum with '>'; with no NaN it is the same value (a NaN score
+    // propagates identically below). Each thread exponentiates its own keys.
+    mx = warp_max((t & 31) < NT / 32 ? fred[t & 31] : -INFINITY);
     const int nblk = npast & ~7;
     double part = 0.0;
     for (int s = t; s < npast; s += NT) {
@@ -97,58 +127,76 @@ __device__ __forceinline__ void attention_head(const AttnParams& p, int h, int t
         part = __dadd_rn(part, (double)e);
     }
     part = warp_sum_d(part);
-    sync();
     if ((t & 31) == 0) dred[t >> 5] = part;
     sync();
-    if (t == 0) {
-        double S = 0.0;
-        for (int i = 0; i < NT / 32; ++i) S = __dadd_rn(S, dred[i]);
-        // certified: any order of these npast non-negative terms lies within
-        // (npast + 64) * 2^-52 relative of the reference's; 1/x is monotone.
-        const double e = (double)(npast + 64) * 0x1p-52;
-        const float ia = __double2float_rn(__ddiv_rn(1.0, __dmul_ru(S, 1.0 + e)));
-        const float ib = __double2float_rn(__ddiv_rn(1.0, __dmul_rd(S, 1.0 - e)));
-        float inv = ia;
-        if (f2u(ia) != f2u(ib) || p.force_fallback) {
-            // reference order: per 8-block ((t0+t1)+t2)+t3 with
-            // t_k = e_k + e_{k+4}; the tail one at a time
-            double sum = 0.0;
-            int i = 0;
-            for (; i + 7 < npast; i += 8) {
-                const double t0 = __dadd_rn((double)sc[i + 0], (double)sc[i + 4]);
-                const double t1 = __dadd_rn((double)sc[i + 1], (double)sc[i + 5]);
-                const double t2 = __dadd_rn((double)sc[i + 2], (double)sc[i + 6]);
-                const double t3 = __dadd_rn((double)sc[i + 3], (double)sc[i + 7]);
-                sum = __dadd_rn(sum, __dadd_rn(__dadd_rn(__dadd_rn(t0, t1), t2), t3));
-            }
-            for (; i < npast; ++i) sum = __dadd_rn(sum, (double)sc[i]);
-            inv = __double2float_rn(__ddiv_rn(1.0, sum));
-            if (p.fallback_count != nullptr) atomicAdd(p.fallback_count, 1);
+    // every thread forms the same certified reciprocal: any order of these
+    // npast non-negative terms lies within (npast + 64) * 2^-52 relative of
+    // the reference's sum, and 1/x is monotone
+    const double S = warp_sum_d((t & 31) < NT / 32 ? dred[t & 31] : 0.0);
+    const double eb = (double)(npast + 64) * 0x1p-52;
+    const float ia = __double2float_rn(__ddiv_rn(1.0, __dmul_ru(S, 1.0 + eb)));
+    const float ib = __double2float_rn(__ddiv_rn(1.0, __dmul_rd(S, 1.0 - eb)));
+    float inv = ia;
+    if (f2u(ia) != f2u(ib) || p.force_fallback) {
+        // reference order: per 8-block ((t0+t1)+t2)+t3 with t_k = e_k + e_{k+4};
+        // the tail one at a time
+        double sum = 0.0;
+        int i = 0;
+        for (; i + 7 < npast; i += 8) {
+            const double t0 = __dadd_rn((double)sc[i + 0], (double)sc[i + 4]);
+            const double t1 = __dadd_rn((double)sc[i + 1], (double)sc[i + 5]);
+            const double t2 = __dadd_rn((double)sc[i + 2], (double)sc[i + 6]);
+            const double t3 = __dadd_rn((double)sc[i + 3], (double)sc[i + 7]);
+            sum = __dadd_rn(sum, __dadd_rn(__dadd_rn(__dadd_rn(t0, t1), t2), t3));
         }
-        *s_inv_p = inv;
+        for (; i < npast; ++i) sum = __dadd_rn(sum, (double)sc[i]);
+        inv = __double2float_rn(__ddiv_rn(1.0, sum));
+        if (t == 0 && p.fallback_count != nullptr) atomicAdd(p.fallback_count, 1);
     }
-    sync();
-    const float inv = *s_inv_p;
-    for (int s = t; s < npast; s += NT) sc[s] = __fmul_rn(sc[s], inv);
-    sync();
 
-    // o[d] = sum over s of w_s * v[s][d], sequential in s (src/forward.c:718-724)
-    if (t < kHeadDim) {
+    // o[d] = sum over s of w_s * v[s][d], sequential in s, with
+    // w_s = fl(e_s * inv) (src/ops.c:418-421, src/forward.c:718-724).
+    // r holds rows s .. s+63 as four batches of 16; while whole blocks of 64
+    // rows follow, each batch is refilled with the rows 64 further on as soon
+    // as it has been added (no bounds predicates in that loop). Then the rows
+    // left in r, and the last ones in batches of 16.
+    if (pv_d >= 0) {
+        const float* vp = vC + pv_d;
+        const float vcur = __ldcg(p.v + kvh * kHeadDim + pv_d);
+        const int last = pos > 0 ? pos - 1 : 0;     // loads past the last stored row read that row
+        float r[64];
         float o = 0.0f;
-        const float vcur = __ldcg(p.v + kvh * kHeadDim + t);
         int s = 0;
-        for (; s + 16 <= pos; s += 16) {
-            float vv[16];
+        if (pos > 0) {
             #pragma unroll
-            for (int j = 0; j < 16; ++j) vv[j] = vC[(size_t)(s + j) * kHeadDim + t];
+            for (int j = 0; j < 64; ++j) r[j] = vp[(size_t)min(j, last) * kHeadDim];
+            #pragma unroll 1
+            for (; s + 64 < pos; s += 64) {
+                // rows s .. s+63 are all stored; refill with the next block
+                #pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    #pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        o = __fadd_rn(o, __fmul_rn(__fmul_rn(sc[s + 16 * b + j], inv), r[16 * b + j]));
+                    #pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        r[16 * b + j] = vp[(size_t)min(s + 64 + 16 * b + j, last) * kHeadDim];
+                }
+            }
+            // the last block: rows s .. pos-1
+            const int rem = pos - s;
             #pragma unroll
-            for (int j = 0; j < 16; ++j) o = __fadd_rn(o, __fmul_rn(sc[s + j], vv[j]));
+            for (int b = 0; b < 4; ++b) {
+                if (16 * b < rem) {
+                    #pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (16 * b + j < rem) o = __fadd_rn(o, __fmul_rn(__fmul_rn(sc[s + 16 * b + j], inv), r[16 * b + j]));
+                }
+            }
         }
-        for (; s < pos; ++s) o = __fadd_rn(o, __fmul_rn(sc[s], vC[(size_t)s * kHeadDim + t]));
-        o = __fadd_rn(o, __fmul_rn(sc[pos], vcur));
-        p.out[h * kHeadDim + t] = o;
+        o = __fadd_rn(o, __fmul_rn(__fmul_rn(sc[pos], inv), vcur));
+        p.out[h * kHeadDim + pv_d] = o;
     }
 }
-
 
 }  // namespace sllm

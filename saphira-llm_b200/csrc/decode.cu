@@ -63,21 +63,21 @@ attention_kernel(const AttnParams p) {
     __shared__ float qs[kHeadDim], kcur[kHeadDim];
     __shared__ float fred[32];
     __shared__ double dred[32];
-    __shared__ float s_inv;
     pdl_trigger_d();
     pdl_wait_d();                 // q, k, v come from the previous kernel
-    attention_head<kAttnThreads>(p, blockIdx.x, threadIdx.x, sc, qs, kcur, fred, dred, &s_inv, CtaSync());
+    attention_head<kAttnThreads>(p, blockIdx.x, threadIdx.x, sc, qs, kcur, fred, dred, CtaSync());
 }
 
 // ---------------------------------------------------------------------------
 // lm_head + argmax
 //
-// Half a warp per vocabulary row; lane c (0..15) owns the reference's
-// accumulators 2c and 2c+1 (acc[j][l] with 8j + l = 2c, 2c+1), so every step
-// reads one half2 per lane: 64 contiguous bytes per row, two rows per warp
-// instruction. After E/32 FMA steps the reference's tree (src/ops.c:135-143)
-// runs as shuffles: acc0+=acc2, acc1+=acc3; acc0+=acc1; t_l = acc0[l] +
-// acc0[l+4]; (t0+t1) + (t2+t3).
+// Four lanes per vocabulary row, eight rows per warp; lane j of a row owns the
+// reference's accumulators acc[j][0..7] and reads 16 bytes per step, so a warp
+// instruction covers 64 contiguous bytes of each of eight rows. After E/32
+// FMA steps the reference's tree (src/ops.c:135-143) runs as two shuffle
+// rounds (acc0+=acc2, acc1+=acc3; acc0+=acc1), then t_l = acc0[l] + acc0[l+4]
+// and (t0+t1) + (t2+t3) in the row's first lane. A persistent grid of two
+// CTAs per SM; the last CTA to finish reduces the per-CTA argmax partials.
 // ---------------------------------------------------------------------------
 constexpr int kLmThreads = 512;
 constexpr int kLmWarps = kLmThreads / 32;
@@ -99,7 +99,7 @@ lm_head_kernel(const LmParams p) {
     __shared__ int bi_s[kLmWarps];
     __shared__ int s_last;
     const int E = p.E, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    pdl_wait_d();                 // x comes from the last layer
+    pdl_wait_d();                 // x comes from the last layer (a no-op in an ordinary launch)
 
     // output_norm (src/forward.c:805-809), f32, certified mean
     double ss = 0.0;
@@ -200,13 +200,29 @@ lm_head_kernel(const LmParams p) {
         s_last = (done == (int)gridDim.x - 1);
     }
     __syncthreads();
-    if (!s_last || tid != 0) return;
+    if (!s_last) return;
+    // the last CTA: every thread takes a stride of the per-CTA partials, then
+    // a warp and a CTA reduction (the order of candidates is irrelevant: ties
+    // resolve to the lowest index)
     __threadfence();
-    for (int b = 0; b < (int)gridDim.x; ++b) {
-        const float v = *(volatile float*)&p.part_v[b];
-        const int i = *(volatile int*)&p.part_i[b];
+    bv = NAN;
+    bi = 0x7fffffff;
+    for (int b = tid; b < (int)gridDim.x; b += kLmThreads) {
+        const float v = __ldcg(&p.part_v[b]);
+        const int i = __ldcg(&p.part_i[b]);
         if (better(v, i, bv, bi)) { bv = v; bi = i; }
     }
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    __syncthreads();              // bv_s / bi_s reused
+    if (lane == 0) { bv_s[warp] = bv; bi_s[warp] = bi; }
+    __syncthreads();
+    if (tid != 0) return;
+    for (int w = 1; w < kLmWarps; ++w) if (better(bv_s[w], bi_s[w], bv, bi)) { bv = bv_s[w]; bi = bi_s[w]; }
     if (p.tp_out != nullptr) {
         p.tp_out[0] = __float_as_int(bv);
         p.tp_out[1] = bi == 0x7fffffff ? 0x7fffffff : bi + p.row_base;
@@ -254,9 +270,13 @@ cudaError_t launch_attention(const AttnParams& p, int n_head, cudaStream_t st) {
 
 int lm_head_grid(int num_sms) { return 2 * num_sms; }
 
+// An ordinary launch, not a programmatic dependent one: measured in the decode
+// step, the head's CTAs launched early behind the layer program streamed the
+// table at half the bandwidth for the whole kernel (238 us against 112 us per
+// token at 2B-4T), for a gain of a few microseconds of launch latency.
 cudaError_t launch_lm_head(const LmParams& p, int grid, cudaStream_t st) {
     const size_t smem = (size_t)p.E * sizeof(float);
-    return launch_pdl(lm_head_kernel, dim3(grid), dim3(kLmThreads), smem, st, true, p);
+    return launch_pdl(lm_head_kernel, dim3(grid), dim3(kLmThreads), smem, st, false, p);
 }
 
 }  // namespace sllm

@@ -642,7 +642,7 @@ i2s_engine_kernel(const EngParams P) {
                 float* hq = sc + kEngAttnMaxCtx;
                 for (int head = r; head < r_end; ++head)
                     attention_head<kEngConsumerWarps * 32>(s_attn[op.group], head, tid, sc, hq, hq + kHeadDim,
-                                                           es.fred, es.dred, &es.fallback_mean, ConsumerSync());
+                                                           es.fred, es.dred, ConsumerSync());
                 consumer_sync();
                 cur_group = -1;
                 continue;
