@@ -2,25 +2,30 @@
 // tensor cores, for configs[3]: 512 tokens through the gate/up and down
 // projections of a 2B-4T layer.
 //
-// One CTA computes a [128 tokens x BN weight rows] tile (two tiles, gate and
-// up, for the fused SiLU form) with the int32 accumulator in tensor memory:
+// One CTA computes MT tiles of [128 tokens x BN weight rows] (each twice,
+// gate and up, for the fused SiLU form) with the int32 accumulators in tensor
+// memory; the weight tile is unpacked once per k-step and used by all MT
+// token tiles:
 //
-//   warp 0 (one lane)   TMA: per k-step of 128 elements, the activation tile
-//                       [128 x 128 B] (128-byte swizzle, the UMMA K-major
+//   warp 0 (one lane)   TMA: per k-step of 128 elements, the MT activation
+//                       tiles [128 x 128 B] (128-byte swizzle, the UMMA K-major
 //                       canonical layout) and the packed weight tile
 //                       [BN x 32 B] into a stage of a shared-memory ring.
-//   warps 2-5           unpack: each thread turns one weight row's 32 packed
-//                       bytes into 128 int8 codes {0, 1, 2} in the same
-//                       swizzled K-major layout. The I2_S packing makes this two
-//                       logic ops per output word: field f of packed word i
-//                       holds elements 32f + 4i .. 32f + 4i + 3, i.e. exactly the
-//                       int8 word at element 32f + 4i of natural order.
+//   warps 2-9           unpack: each item turns 16 packed bytes of one weight
+//                       row into 64 int8 codes {0, 1, 2} in the same swizzled
+//                       K-major layout. The I2_S packing makes this two logic
+//                       ops per output word: field f of packed word i holds
+//                       elements 32f + 4i .. 32f + 4i + 3, i.e. exactly the int8
+//                       word at element 32f + 4i of natural order.
 //   warp 1 (one lane)   tcgen05.mma.cta_group::1.kind::i8 (s8 x s8 -> s32,
-//                       M = 128, N = BN, K = 32) x 4 per k-step and tensor, then
+//                       M = 128, K = 32, N = BN or 2 BN: the gate and up tiles
+//                       are one K-major tile of 2 BN rows) x 4 per k-step and
+//                       token tile, the token tiles interleaved, then
 //                       tcgen05.commit to the stage's "empty" barrier.
-//   warps 2-5 again     epilogue: tcgen05.ld of the accumulator (warp w reads
-//                       TMEM lanes 32 (w % 4) ..), minus the token's code sum,
-//                       times ws / scale, SiLU(gate) * up when fused.
+//   warps 2-9 again     epilogue: warps 2-5 take token tile 0, warps 6-9 tile
+//                       1; tcgen05.ld of the accumulator (warp w reads TMEM
+//                       lanes 32 (w % 4) ..), minus the token's code sum, times
+//                       ws / scale, SiLU(gate) * up when fused.
 //
 // The integer sum is exact in any order, so every dot equals the reference's
 // per-token sllm_i2s_gemv bit for bit; the epilogue is the GEMV epilogue's
@@ -40,23 +45,28 @@ namespace {
 constexpr int kBM = 128;          // tokens per tile (TMEM lanes)
 constexpr int kBK = 128;          // elements (= activation bytes) per k-step
 constexpr int kPK = kBK / 4;      // packed weight bytes per row per k-step
-constexpr int kGmThreads = 192;   // 6 warps
+constexpr int kGmUnpackWarps = 8;
+constexpr int kGmThreads = 64 + 32 * kGmUnpackWarps;   // TMA, MMA, 8 unpack / epilogue warps
 constexpr uint64_t kGmWaitNs = 2000000000ull;
 
 enum GemmError { GM_OK = 0, GM_TIMEOUT = 1 };
 
-template <int BN, bool PAIR>
+template <int BN, bool PAIR, int MT>
 struct GemmCfg {
     static constexpr int NM = PAIR ? 2 : 1;
     static constexpr int A_BYTES = kBM * kBK;
     static constexpr int B_BYTES = BN * kBK;
     static constexpr int P_BYTES = BN * kPK;
-    static constexpr int STAGE = A_BYTES + NM * (B_BYTES + P_BYTES);   // a multiple of 1024
-    static constexpr int S = (196608 / STAGE) > 6 ? 6 : (196608 / STAGE);
-    static constexpr int SMEM = S * STAGE + 1024;                       // + room to align to 1024
-    static constexpr int TMEM_COLS = NM * BN;                           // 64, 128 or 256
+    static constexpr int STAGE = MT * A_BYTES + NM * (B_BYTES + P_BYTES);   // a multiple of 1024
+    static constexpr int S = (225280 / STAGE) > 6 ? 6 : (225280 / STAGE);
+    static constexpr int SMEM = S * STAGE + 1024;                           // + room to align to 1024
+    static constexpr int TMEM_COLS = MT * NM * BN;                          // a power of two, 32..512
     static_assert(STAGE % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
     static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "tile width");
+    static_assert(MT == 1 || MT == 2, "token tiles per CTA (one epilogue warp group each)");
+    static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
+    static_assert(S >= 2, "ring depth");
+    static_assert(NM * BN <= 256, "one MMA covers the tensors' rows (N <= 256)");
 };
 
 struct GemmKParams {
@@ -67,6 +77,7 @@ struct GemmKParams {
     float* y;
     int M, N, K;
     int* error;
+    int tma_out;           // 1: outputs leave through the tensor maps tm_y / tm_d
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -135,6 +146,27 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, in
         : "memory");
 }
 
+// a 2-D TMA tile store from shared memory, tracked by the bulk-group counter
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(tm)),
+                 "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory"); }
+
+// one warp's 32 rows x 32 four-byte values (lane = row) into a 4 KB staging
+// box in the 128-byte swizzle the output tensor maps use: chunk j of row r
+// at chunk j ^ (r % 8); eight consecutive lanes cover all 32 banks
+__device__ __forceinline__ void stage_row32(uint8_t* box, int lane, const uint32_t (&v)[32]) {
+    #pragma unroll
+    for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<uint4*>(box + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+            make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -196,29 +228,32 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 // the codes of one packed word, field f: four int8 codes of consecutive elements
 __device__ __forceinline__ uint32_t field_codes(uint32_t w, int f) { return (w >> (6 - 2 * f)) & 0x03030303u; }
 
-template <int BN, bool PAIR>
+template <int BN, bool PAIR, int MT>
 __global__ void __launch_bounds__(kGmThreads, 1)
 i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
-                const __grid_constant__ CUtensorMap tm_w2, const GemmKParams p) {
-    using C = GemmCfg<BN, PAIR>;
+                const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_y,
+                const __grid_constant__ CUtensorMap tm_d, const GemmKParams p) {
+    using C = GemmCfg<BN, PAIR, MT>;
     extern __shared__ uint8_t gsm_raw[];
     __shared__ uint64_t bar_loaded[C::S], bar_unpacked[C::S], bar_empty[C::S], bar_acc;
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
     uint8_t* const gsm = gsm_raw + ((1024u - (smem_u32(gsm_raw) & 1023u)) & 1023u);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * (MT * kBM);
     const int KB = p.K / kBK;
-    auto A = [&](int s) { return gsm + (size_t)s * C::STAGE; };
-    auto B = [&](int s, int mat) { return gsm + (size_t)s * C::STAGE + C::A_BYTES + mat * C::B_BYTES; };
+    // token tiles of this CTA that hold tokens (the last CTA row may have fewer)
+    const int mt_live = min(MT, (p.M - m0 + kBM - 1) / kBM);
+    auto A = [&](int s, int mt) { return gsm + (size_t)s * C::STAGE + mt * C::A_BYTES; };
+    auto B = [&](int s, int mat) { return gsm + (size_t)s * C::STAGE + MT * C::A_BYTES + mat * C::B_BYTES; };
     auto P = [&](int s, int mat) {
-        return gsm + (size_t)s * C::STAGE + C::A_BYTES + C::NM * C::B_BYTES + mat * C::P_BYTES;
+        return gsm + (size_t)s * C::STAGE + MT * C::A_BYTES + C::NM * C::B_BYTES + mat * C::P_BYTES;
     };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::S; ++s) {
             mbar_init(&bar_loaded[s], 1);
-            mbar_init(&bar_unpacked[s], 4);
+            mbar_init(&bar_unpacked[s], kGmUnpackWarps);
             mbar_init(&bar_empty[s], 1);
         }
         mbar_init(&bar_acc, 1);
@@ -245,8 +280,8 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
                 const int s = kb % C::S;
                 const uint32_t use = (uint32_t)(kb / C::S);
                 if (use > 0 && !gm_wait(&bar_empty[s], (use - 1) & 1u, abort_v, p.error)) break;
-                mbar_expect_tx(&bar_loaded[s], (uint32_t)(C::A_BYTES + C::NM * C::P_BYTES));
-                tma_load_2d(A(s), &tm_a, kb * kBK, m0, &bar_loaded[s]);
+                mbar_expect_tx(&bar_loaded[s], (uint32_t)(mt_live * C::A_BYTES + C::NM * C::P_BYTES));
+                for (int mt = 0; mt < mt_live; ++mt) tma_load_2d(A(s, mt), &tm_a, kb * kBK, m0 + mt * kBM, &bar_loaded[s]);
                 tma_load_2d(P(s, 0), &tm_w, kb * kPK, n0, &bar_loaded[s]);
                 if (PAIR) tma_load_2d(P(s, 1), &tm_w2, kb * kPK, n0, &bar_loaded[s]);
                 ++issued;
@@ -258,7 +293,10 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_i8(kBM, BN);
+            // the gate and up tiles are adjacent in shared memory (rows 0..BN-1
+            // and BN..2BN-1 of one K-major tile), so one MMA of N = 2 BN
+            // computes both, into accumulator columns [0, BN) and [BN, 2 BN)
+            constexpr uint32_t idesc = umma_idesc_i8(kBM, C::NM * BN);
             int issued = 0;
             for (int kb = 0; kb < KB; ++kb) {
                 const int s = kb % C::S;
@@ -266,26 +304,28 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
                 if (!gm_wait(&bar_loaded[s], ph, abort_v, p.error)) break;
                 if (!gm_wait(&bar_unpacked[s], ph, abort_v, p.error)) break;
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(A(s));
+                const uint32_t b0 = smem_u32(B(s, 0));
                 #pragma unroll
-                for (int mat = 0; mat < C::NM; ++mat) {
-                    const uint32_t b0 = smem_u32(B(s, mat));
+                for (int kk = 0; kk < kBK / 32; ++kk) {
                     #pragma unroll
-                    for (int kk = 0; kk < kBK / 32; ++kk)
-                        umma_i8(tmem + (uint32_t)(mat * BN), umma_desc_sw128(a0 + 32u * kk),
-                                umma_desc_sw128(b0 + 32u * kk), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    for (int mt = 0; mt < MT; ++mt) {
+                        if (mt < mt_live)
+                            umma_i8(tmem + (uint32_t)(mt * C::NM * BN), umma_desc_sw128(smem_u32(A(s, mt)) + 32u * kk),
+                                    umma_desc_sw128(b0 + 32u * kk), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    }
                 }
                 umma_commit(&bar_empty[s]);     // the stage may be refilled once these MMAs have read it
                 ++issued;
             }
-            umma_commit(&bar_acc);              // the accumulator is complete (or the CTA aborted)
+            umma_commit(&bar_acc);              // the accumulators are complete (or the CTA aborted)
             // the MMAs issued have finished reading shared memory before exit
             if (issued > 0) gm_drain(&bar_empty[(issued - 1) % C::S], (uint32_t)((issued - 1) / C::S) & 1u);
         }
         __syncwarp();
     } else {
-        // ---------------- unpack, then epilogue (warps 2-5) ----------------
-        const int t = threadIdx.x - 64;     // 0..127
+        // ---------------- unpack, then epilogue (warps 2-9) ----------------
+        constexpr int NT = 32 * kGmUnpackWarps;
+        const int t = threadIdx.x - 64;     // 0..NT-1
         bool ok = true;
         for (int kb = 0; kb < KB && ok; ++kb) {
             const int s = kb % C::S;
@@ -296,7 +336,7 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
                 // consecutive rows, so their 16-byte stores hit eight distinct
                 // swizzled chunks (no bank conflict)
                 #pragma unroll
-                for (int it = t; it < C::NM * 2 * BN; it += 128) {
+                for (int it = t; it < C::NM * 2 * BN; it += NT) {
                     const int row = it % BN, h = (it / BN) & 1, mat = it / (2 * BN);
                     const uint4 v = *reinterpret_cast<const uint4*>(P(s, mat) + row * kPK + h * 16);
                     uint8_t* brow = B(s, mat) + row * kBK;
@@ -317,20 +357,39 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
             if (lane == 0) mbar_arrive(&bar_unpacked[s]);
             ok = __all_sync(0xffffffffu, ok);
         }
-        // epilogue
+        // epilogue: warp group mt (warps 2-5: 0, warps 6-9: 1) takes token tile mt
+        const int mt = (warp - 2) >> 2;
         const bool acc_ok = __all_sync(0xffffffffu, ok && gm_wait(&bar_acc, 0u, abort_v, p.error)) &&
                             __all_sync(0xffffffffu, *abort_v == 0);
-        if (acc_ok) {
+        if (acc_ok && mt < mt_live) {
             tc_fence_after();
             const int quarter = warp & 3;
-            const int m = m0 + 32 * quarter + lane;
+            const int row0 = m0 + mt * kBM + 32 * quarter;      // this warp's first token
+            const int m = row0 + lane;
             const bool live = m < p.M;
             sllm_cuda_act act{1.0f, 0};
             if (live) act = p.acts[m];
             // per-tensor scale over the token's activation scale (src/forward.c:653-655)
             const float post = __fdiv_rn(__ldg(p.ws), act.scale);
             const float post2 = PAIR ? __fdiv_rn(__ldg(p.ws2), act.scale) : 0.0f;
-            const uint32_t lane_base = tmem + ((uint32_t)(32 * quarter) << 16);
+            const uint32_t lane_base = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(mt * C::NM * BN);
+            // two 4 KB staging boxes per warp in the (now idle) ring: the store
+            // of one drains while the other fills
+            uint8_t* const stg = gsm + (size_t)(warp - 2) * 8192;
+            int nst = 0;        // stores committed by this warp
+            auto stage_out = [&](const CUtensorMap* tm, const uint32_t (&v)[32], int col) {
+                uint8_t* box = stg + (nst & 1) * 4096;
+                if (nst >= 2 && lane == 0) bulk_wait_read<1>();   // the store that last read this box
+                __syncwarp();
+                stage_row32(box, lane, v);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(tm, box, col, row0);    // rows >= M, columns >= N are clipped
+                    bulk_commit();
+                }
+                ++nst;
+            };
             #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 uint32_t g[32];
@@ -339,22 +398,32 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
                     uint32_t u[32];
                     tmem_ld32(lane_base + (uint32_t)(BN + c0), u);
                     tmem_ld_wait();
-                    if (live) {
+                    #pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        // h = silu(gate) * up (src/forward.c:765-778, src/ops.c:452-456)
+                        const float gv = __fmul_rn(__int2float_rn((int)g[j] - act.sum), post);
+                        const float uv = __fmul_rn(__int2float_rn((int)u[j] - act.sum), post2);
+                        u[j] = __float_as_uint(__fmul_rn(silu_block(gv), uv));
+                    }
+                    if (p.tma_out) {
+                        stage_out(&tm_y, u, n0 + c0);
+                    } else if (live) {
                         float* yrow = p.y + (size_t)m * p.N;
                         #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int n = n0 + c0 + j;
-                            if (n < p.N) {
-                                // h = silu(gate) * up (src/forward.c:765-778, src/ops.c:452-456)
-                                const float gv = __fmul_rn(__int2float_rn((int)g[j] - act.sum), post);
-                                const float uv = __fmul_rn(__int2float_rn((int)u[j] - act.sum), post2);
-                                yrow[n] = __fmul_rn(silu_block(gv), uv);
-                            }
-                        }
+                        for (int j = 0; j < 32; ++j)
+                            if (n0 + c0 + j < p.N) yrow[n0 + c0 + j] = __uint_as_float(u[j]);
                     }
                 } else {
                     tmem_ld_wait();
-                    if (live) {
+                    if (p.tma_out) {
+                        if (p.dots != nullptr) stage_out(&tm_d, g, n0 + c0);
+                        if (p.y != nullptr) {
+                            #pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                g[j] = __float_as_uint(__fmul_rn(__int2float_rn((int)g[j] - act.sum), post));
+                            stage_out(&tm_y, g, n0 + c0);
+                        }
+                    } else if (live) {
                         #pragma unroll
                         for (int j = 0; j < 32; ++j) {
                             const int n = n0 + c0 + j;
@@ -367,6 +436,9 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
                     }
                 }
             }
+            // the staging boxes are read before the CTA exits
+            if (lane == 0) bulk_wait_read<0>();
+            __syncwarp();
         }
     }
     tc_fence_before();
@@ -408,9 +480,23 @@ bool encode_2d(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, 
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, bool PAIR>
+// a row-major [rows][cols] matrix of 4-byte values for the epilogue's stores:
+// boxes of 32 rows x 32 values (128 bytes) in the 128-byte swizzle
+bool encode_out(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, CUtensorMapDataType type) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (enc == nullptr) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 4};
+    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(tm, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, bool PAIR, int MT>
 cudaError_t launch_tile(const GemmArgs& a, int* error, cudaStream_t st) {
-    using C = GemmCfg<BN, PAIR>;
+    using C = GemmCfg<BN, PAIR, MT>;
     CUtensorMap tm_a, tm_w, tm_w2;
     if (!encode_2d(&tm_a, a.q, (uint64_t)a.K, (uint64_t)a.m, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_2d(&tm_w, a.w, (uint64_t)(a.K / 4), (uint64_t)a.n_rows, kPK, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
@@ -432,10 +518,23 @@ cudaError_t launch_tile(const GemmArgs& a, int* error, cudaStream_t st) {
     p.N = a.n_rows;
     p.K = a.K;
     p.error = error;
-    cudaError_t e = cudaFuncSetAttribute(i2s_gemm_kernel<BN, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    // the epilogue stores through tensor maps when the outputs allow it
+    // (16-byte aligned rows); otherwise every thread stores its token's row
+    CUtensorMap tm_y = tm_w, tm_d = tm_w;
+    const bool rows16 = (a.n_rows % 4) == 0;
+    const auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    p.tma_out = rows16 && (a.y == nullptr || al16(a.y)) && (a.dots == nullptr || al16(a.dots));
+    if (p.tma_out && a.y != nullptr &&
+        !encode_out(&tm_y, a.y, (uint64_t)a.n_rows, (uint64_t)a.m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32))
+        p.tma_out = 0;
+    if (p.tma_out && a.dots != nullptr &&
+        !encode_out(&tm_d, a.dots, (uint64_t)a.n_rows, (uint64_t)a.m, CU_TENSOR_MAP_DATA_TYPE_INT32))
+        p.tma_out = 0;
+    cudaError_t e =
+        cudaFuncSetAttribute(i2s_gemm_kernel<BN, PAIR, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
-    const dim3 grid((unsigned)((a.n_rows + BN - 1) / BN), (unsigned)((a.m + kBM - 1) / kBM));
-    i2s_gemm_kernel<BN, PAIR><<<grid, kGmThreads, C::SMEM, st>>>(tm_a, tm_w, tm_w2, p);
+    const dim3 grid((unsigned)((a.n_rows + BN - 1) / BN), (unsigned)((a.m + MT * kBM - 1) / (MT * kBM)));
+    i2s_gemm_kernel<BN, PAIR, MT><<<grid, kGmThreads, C::SMEM, st>>>(tm_a, tm_w, tm_w2, tm_y, tm_d, p);
     return cudaGetLastError();
 }
 
@@ -466,9 +565,13 @@ int gemm_check(const GemmArgs& a, const char** why) {
     return SLLM_CUDA_OK;
 }
 
+// Tile shapes: the gate/up pair takes 128 weight rows x 256 tokens per CTA
+// (all 512 tensor-memory columns, MMAs of N = 256); a single tensor takes 128
+// rows x 128 tokens, so the 2560-row down projection spreads over 80 CTAs at
+// 512 tokens.
 cudaError_t launch_i2s_gemm(const GemmArgs& a, int* error, cudaStream_t st) {
-    if (a.w2 != nullptr) return launch_tile<128, true>(a, error, st);
-    return launch_tile<128, false>(a, error, st);
+    if (a.w2 != nullptr) return launch_tile<128, true, 2>(a, error, st);
+    return launch_tile<128, false, 1>(a, error, st);
 }
 
 }  // namespace sllm
