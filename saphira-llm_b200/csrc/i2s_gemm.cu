@@ -114,9 +114,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // bounded wait: false when the phase did not complete in time, or when the
-// CTA is aborting
-__device__ __noinline__ bool gm_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* error) {
+// CTA is aborting. The first check is inline: the single MMA-issuing thread
+// waits once per k-step, and an out-of-line call there cost ~0.1 us each.
+__device__ __noinline__ bool gm_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* error);
+__device__ __forceinline__ bool gm_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* error) {
     if (mbar_try_wait(bar, parity)) return true;
+    return gm_wait_slow(bar, parity, abort_flag, error);
+}
+__device__ __noinline__ bool gm_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* error) {
     const uint64_t t0 = gtimer();
     while (!mbar_try_wait(bar, parity)) {
         if (*abort_flag) return false;
@@ -301,7 +306,8 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
             for (int kb = 0; kb < KB; ++kb) {
                 const int s = kb % C::S;
                 const uint32_t ph = (uint32_t)(kb / C::S) & 1u;
-                if (!gm_wait(&bar_loaded[s], ph, abort_v, p.error)) break;
+                // the unpack warps arrive only after the stage's copies landed,
+                // so this one wait covers the activation tiles too
                 if (!gm_wait(&bar_unpacked[s], ph, abort_v, p.error)) break;
                 tc_fence_after();
                 const uint32_t b0 = smem_u32(B(s, 0));
