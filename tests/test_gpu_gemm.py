@@ -33,10 +33,14 @@ def _quant_rows(cuda, x):
     return q, acts
 
 
-def test_quant_act_rows_bit_exact(cuda, orc):
+@pytest.mark.parametrize("n", [384, 2560, 6912, 8192, 130])
+def test_quant_act_rows_bit_exact(cuda, orc, n):
+    """Per-token quantisation of a batch: every row length of the models
+    (the vectorised kernel, one to eight float4 per thread) and a length that
+    is not a multiple of 4 (the scalar kernel); a zero row, NaN and inf."""
     import torch
-    rng = np.random.default_rng(5)
-    x = (rng.standard_normal((37, 384)) * 2).astype(np.float32)
+    rng = np.random.default_rng(5 + n)
+    x = (rng.standard_normal((37, n)) * 2).astype(np.float32)
     x[3] = 0.0
     x[7, 5] = np.nan
     x[9, 11] = np.inf
