@@ -469,6 +469,9 @@ def main():
     ap.add_argument("--no-tp", action="store_true")
     ap.add_argument("--copies", type=int, default=N_COPIES,
                     help="layer copies per step (default 32; smaller only for profiler captures)")
+    ap.add_argument("--leg", choices=["decode", "prefill", "tp"], default=None,
+                    help="run only this secondary leg and print its object (for profiler captures; "
+                         "no headline line)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -485,6 +488,16 @@ def main():
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+
+    if args.leg is not None:
+        leg = {"decode": lambda: decode_leg(pkg, synth, local, rank, world, args),
+               "prefill": lambda: prefill_leg(pkg, synth, local, rank, world, args),
+               "tp": lambda: tp_decode_leg(pkg, local, rank, world, args)}[args.leg]()
+        if rank == 0:
+            print(json.dumps({"leg": args.leg, **leg}))
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
 
     copies = args.copies
     cfg = synth.Config(n_layer=copies, n_vocab=256)

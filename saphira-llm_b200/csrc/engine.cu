@@ -691,13 +691,17 @@ int engine_chunk_rows(int K, int epi) {
     return rows;
 }
 
+// The dynamic shared memory a program may use: 227 KB less the kernel's
+// static shared memory (EngSmem plus the few __shared__ words of the inlined
+// stage code; 256 bytes are reserved for the latter).
+constexpr int kEngDynLimit = 227 * 1024 - (int)sizeof(EngSmem) - 256;
+
 int engine_smem_bytes(int n_groups, int n_ops, int n_stages, int n_attn) {
     static_assert(kEngAttnMaxCtx * 4 + 2 * kHeadDim * 4 <= 8192, "attention scratch fits the activation area");
     const size_t b = (size_t)kEngSlots * kEngSlotBytes + 8192 + (size_t)n_ops * sizeof(EngOp) +
                      (size_t)n_groups * sizeof(EngGroup) + (size_t)n_stages * 2 * sizeof(EngCursor) +
                      (size_t)n_attn * sizeof(AttnParams);
-    const size_t limit = 227 * 1024 - sizeof(EngSmem) - 64;
-    return b <= limit ? (int)b : 0;
+    return b <= (size_t)kEngDynLimit ? (int)b : 0;
 }
 
 int engine_grid(int device) {
@@ -716,11 +720,18 @@ bool engine_supports(int wa, int wb) {
 }
 
 cudaError_t prepare_engine() {
-    // the largest dynamic shared memory any program may ask for
-    const int bytes = 227 * 1024 - (int)sizeof(EngSmem) - 64;
+    // the largest dynamic shared memory any program may ask for; the static
+    // part must fit the reserve
+    const int bytes = kEngDynLimit;
     cudaError_t e = cudaSuccess;
-#define SLLM_ENG_PREP(A, B) \
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(i2s_engine_kernel<A, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+#define SLLM_ENG_PREP(A, B)                                                                                     \
+    if (e == cudaSuccess) {                                                                                      \
+        cudaFuncAttributes fa{};                                                                                 \
+        e = cudaFuncGetAttributes(&fa, i2s_engine_kernel<A, B>);                                                 \
+        if (e == cudaSuccess && fa.sharedSizeBytes + (size_t)bytes > 227u * 1024u) e = cudaErrorInvalidValue;    \
+        if (e == cudaSuccess)                                                                                    \
+            e = cudaFuncSetAttribute(i2s_engine_kernel<A, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); \
+    }
     SLLM_ENGINE_SHAPES(SLLM_ENG_PREP)
 #undef SLLM_ENG_PREP
     return e;
