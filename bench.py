@@ -393,7 +393,9 @@ def tp_decode_leg(pkg, local, rank, world, args):
            "weight_gbs_per_gpu": round(per_gpu_bytes * steps / dt / 1e9, 1),
            "model_gb_per_gpu": round(model.bytes() / 1e9, 2), "build_s": round(build_s, 2),
            "token_checksum": int(sum((i + 1) * int(v) for i, v in enumerate(toks))),
-           "layer_gemvs": "persistent engine (one program per phase)" if ctx.uses_engine() else "per-GEMV kernels",
+           "layer_gemvs": ("persistent engine: per layer one program of four stages (Q/K/V, attention, O, "
+                           "gate/up) and one for down" if ctx.fused_layers() > 0 else
+                           "persistent engine (one program per phase)") if ctx.uses_engine() else "per-GEMV kernels",
            "exchange": {"none": "none (one rank)", "nccl": "NCCL all-gather / int32 all-reduce in the step graph",
                         "p2p": "one-shot peer-memory exchange (P2P stores + epoch flags) in the step graph"}[
                             ctx.exchange_kind()]}

@@ -41,6 +41,11 @@ SLLM_CUDA_API int sllm_cuda_test_gemm_error(void);
  * on the per-GEMV kernels (widths the engine is not compiled for) */
 SLLM_CUDA_API int sllm_cuda_test_tp_uses_engine(const sllm_cuda_tp_ctx * c);
 
+/* the number of layers that run as one fused engine program (Q/K/V,
+ * attention, O, gate/up behind grid barriers): n_layer on one rank with the
+ * engine, 0 otherwise */
+SLLM_CUDA_API int sllm_cuda_test_tp_fused_layers(const sllm_cuda_tp_ctx * c);
+
 /* how the context exchanges between ranks: 0 none (one rank), 1 NCCL
  * collectives, 2 the one-shot peer-memory exchange */
 SLLM_CUDA_API int sllm_cuda_test_tp_exchange_kind(const sllm_cuda_tp_ctx * c);

@@ -68,6 +68,7 @@ def lib():
     L.sllm_cuda_tp_last_logits.argtypes = [vp, vp]
     L.sllm_cuda_test_tp_generate_group.argtypes = [C.POINTER(vp), i32, vp, i32, i32, vp]
     L.sllm_cuda_test_tp_uses_engine.argtypes = [vp]
+    L.sllm_cuda_test_tp_fused_layers.argtypes = [vp]
     L.sllm_cuda_test_tp_exchange_kind.argtypes = [vp]
     L.sllm_cuda_model_upload.argtypes = [C.POINTER(abi.ModelDesc), C.c_int, C.POINTER(vp)]
     L.sllm_cuda_model_free.argtypes = [vp]
@@ -368,6 +369,9 @@ class TpCtx:
 
     def uses_engine(self):
         return bool(lib().sllm_cuda_test_tp_uses_engine(self.h))
+
+    def fused_layers(self):
+        return int(lib().sllm_cuda_test_tp_fused_layers(self.h))
 
     def exchange_kind(self):
         """'none' (one rank), 'nccl' or 'p2p' (the one-shot peer-memory exchange)."""

@@ -461,6 +461,12 @@ struct sllm_cuda_tp_ctx {
         int wa, wb;
     };
     std::vector<Prog> progs;
+    // one rank: per layer one four-stage program (Q/K/V, attention, O +
+    // residual, gate/up) behind grid barriers, in place of phases 0-2, their
+    // two norm/quantise and epilogue kernels and the local copies; each has
+    // its own barrier word, all zeroed once per step
+    std::vector<Prog> fused;
+    unsigned* fused_barriers = nullptr;
     int grid = 0;
     int* eng_error = nullptr;
     unsigned* eng_barrier = nullptr;
@@ -766,6 +772,9 @@ cudaError_t xchg_nccl(sllm_cuda_tp_ctx* c, int which, cudaStream_t st, ncclResul
     xchg_counts(c->m, which, &count, &gather);
     xchg_buffers(c, which, &src, &dst);
     if (c->m->n_ranks == 1) {
+        // the fused programs write the attention output and h where the
+        // gathers would copy them to
+        if (!c->fused.empty() && (which == X_ATTN || which == X_H)) return cudaSuccess;
         if (gather && src != dst) return cudaMemcpyAsync(dst, src, count * 4, cudaMemcpyDeviceToDevice, st);
         return cudaSuccess;
     }
@@ -865,7 +874,12 @@ cudaError_t enqueue_phase(sllm_cuda_tp_ctx* c, int ph, cudaStream_t st, bool cou
         tp_epilogue_kernel<<<(rows + 255) / 256, 256, 0, st>>>(dots, chunks, rows, act, ws, resid, y);
         return launch_count(cudaGetLastError(), cnt);
     };
-    if (ph == 0) return launch_count(launch_embed(m->tok_embd, c->tok_seq, c->pos, E, m->V, c->x, st), cnt);
+    if (ph == 0) {
+        cudaError_t e = launch_count(launch_embed(m->tok_embd, c->tok_seq, c->pos, E, m->V, c->x, st), cnt);
+        if (e == cudaSuccess && !c->fused.empty())
+            e = cudaMemsetAsync(c->fused_barriers, 0, sizeof(unsigned) * c->fused.size(), st);
+        return e;
+    }
     if (ph == n_phases(m) - 1) {
         tp_finalize_kernel<<<1, 1, 0, st>>>(c->trip_all, m->n_ranks, c->pos, c->tok_seq, c->prompt_end, c->argmax,
                                             c->hist, c->n_ctx);
@@ -898,6 +912,10 @@ cudaError_t enqueue_phase(sllm_cuda_tp_ctx* c, int ph, cudaStream_t st, bool cou
             cudaError_t e = epi(c->dots_d, m->down_c, c->act_h, tp.down[0], E, m->down_k, c->ffn_inp, c->x);
             if (e != cudaSuccess) return e;
         }
+        if (!c->fused.empty()) {
+            const sllm_cuda_tp_ctx::Prog& pr = c->fused[(size_t)l];
+            return launch_count(launch_engine(pr.p, c->grid, st, pr.wa, pr.wb), cnt);
+        }
         // attn_norm -> local Q, K, V (src/forward.c:631-666)
         p.K = E; p.nseg = 3;
         p.seg[0] = GemvSeg{t.wq, m->hq * D, c->q, nullptr};
@@ -918,6 +936,7 @@ cudaError_t enqueue_phase(sllm_cuda_tp_ctx* c, int ph, cudaStream_t st, bool cou
         ap.fallback_count = fb; ap.force_fallback = force;
         return launch_count(launch_attention(ap, m->hq, st), cnt);
     }
+    if (!c->fused.empty() && (sub == 1 || sub == 2)) return cudaSuccess;   // inside the layer's program
     if (sub == 1) {
         // attn_sub_norm + quantisation of the whole attention output, then
         // this rank's columns of O (src/forward.c:728-741)
@@ -1032,6 +1051,91 @@ int wpl_of(int K) { return engine_wpl(K); }
 // One single-stage engine program per layer and GEMV phase, tables in device
 // memory owned by the context. Returns OK and leaves c->progs empty when the
 // widths are not compiled in.
+// One rank: each layer's Q/K/V, attention, O and gate/up as one engine
+// program of four stages (src/forward.c:628-779), as the single-GPU decode
+// step runs them: the attention output and h go straight to the buffers the
+// rest of the step reads, O's epilogue adds the residual into ffn_inp. The
+// down projection (n_ff = 28672 is quantised by its own kernel) keeps its
+// phase. Results are identical: the same GEMV, attention and epilogue
+// arithmetic, in the same order.
+int build_fused_programs(sllm_cuda_tp_ctx* c, int wa, int wb) {
+    const sllm_cuda_tp_model* m = c->m;
+    const int D = kHeadDim, E = m->E;
+    int* fb = fallback_counter();
+    CK(ctx_alloc(c, &c->fused_barriers, (size_t)m->n_layer), "fused program barriers");
+    const size_t kv_layer = (size_t)m->hk * D * (size_t)c->n_ctx;
+    for (int l = 0; l < m->n_layer; ++l) {
+        const TpLayer& t = m->layers[l];
+        std::vector<EngGroup> groups;
+        std::vector<EngOp> ops;
+        std::vector<int> stage_first;
+        auto op = [&](const uint8_t* w, const uint8_t* w2, float* y, const float* resid, float* h, int rows, int K,
+                      int epi, int group) {
+            EngOp o{};
+            o.w = w; o.w2 = w2; o.y = y; o.resid = resid; o.h = h; o.rows = rows; o.K = K; o.epi = epi; o.group = group;
+            o.chunk_rows = epi == kEpiAttention ? 1 : engine_chunk_rows(K, epi);
+            o.ws = w != nullptr ? read_scale(w, rows, K) : 0.0f;
+            o.ws2 = w2 != nullptr ? read_scale(w2, rows, K) : 0.0f;
+            ops.push_back(o);
+        };
+        auto group = [&](const float* x, const float* norm_w) {
+            EngGroup g{}; g.x = x; g.norm_w = norm_w; g.K = E; g.pro = PRO_NORM;
+            groups.push_back(g);
+            return (int)groups.size() - 1;
+        };
+        stage_first.push_back((int)ops.size());         // attn_norm -> Q, K, V
+        int g = group(c->x, t.attn_norm);
+        op(t.wq, nullptr, c->q, nullptr, nullptr, m->hq * D, E, EPI_F32, g);
+        op(t.wk, nullptr, c->k, nullptr, nullptr, m->hk * D, E, EPI_F32, g);
+        op(t.wv, nullptr, c->v, nullptr, nullptr, m->hk * D, E, EPI_F32, g);
+        stage_first.push_back((int)ops.size());         // attention, one head per row
+        op(nullptr, nullptr, c->attn_full, nullptr, nullptr, m->hq, c->n_ctx, kEpiAttention, 0);
+        stage_first.push_back((int)ops.size());         // attn_sub_norm -> O, + x into ffn_inp
+        g = group(c->attn_full, t.attn_sub_norm);
+        op(t.wo, nullptr, c->ffn_inp, c->x, nullptr, E, E, EPI_RESID, g);
+        stage_first.push_back((int)ops.size());         // ffn_norm -> gate, up -> h
+        g = group(c->ffn_inp, t.ffn_norm);
+        op(t.gate, t.up, nullptr, nullptr, c->h_full, m->f_loc, E, EPI_SILU, g);
+        stage_first.push_back((int)ops.size());
+        AttnParams ap{};
+        ap.q = c->q; ap.k = c->k; ap.v = c->v;
+        ap.k_cache = c->k_cache + (size_t)l * kv_layer;
+        ap.v_cache = c->v_cache + (size_t)l * kv_layer;
+        ap.rope_cos = c->rope_cos; ap.rope_sin = c->rope_sin;
+        ap.pos_ptr = c->pos; ap.out = c->attn_full; ap.n_ctx = c->n_ctx;
+        ap.group = m->hq / m->hk;
+        ap.attn_scale = 1.0f / sqrtf((float)D);
+        ap.fallback_count = fb; ap.force_fallback = force_fallback_flag();
+        const int n_stages = (int)stage_first.size() - 1;
+        if (engine_smem_bytes((int)groups.size(), (int)ops.size(), n_stages, 1) == 0) {
+            c->fused.clear();       // does not fit: the per-phase programs stay in use
+            return SLLM_CUDA_OK;
+        }
+        const std::vector<EngCursor> st = engine_starts(ops, stage_first, c->grid);
+        EngGroup* dg = nullptr;
+        EngOp* dop = nullptr;
+        EngCursor* ds = nullptr;
+        AttnParams* da = nullptr;
+        CK(ctx_alloc(c, &dg, groups.size()), "fused program groups");
+        CK(ctx_alloc(c, &dop, ops.size()), "fused program ops");
+        CK(ctx_alloc(c, &ds, st.size()), "fused program cursors");
+        CK(ctx_alloc(c, &da, 1), "fused program attention");
+        CK(cudaMemcpy(dg, groups.data(), groups.size() * sizeof(EngGroup), cudaMemcpyHostToDevice), "tables");
+        CK(cudaMemcpy(dop, ops.data(), ops.size() * sizeof(EngOp), cudaMemcpyHostToDevice), "tables");
+        CK(cudaMemcpy(ds, st.data(), st.size() * sizeof(EngCursor), cudaMemcpyHostToDevice), "tables");
+        CK(cudaMemcpy(da, &ap, sizeof(AttnParams), cudaMemcpyHostToDevice), "tables");
+        sllm_cuda_tp_ctx::Prog pr{};
+        pr.p.groups = dg; pr.p.ops = dop; pr.p.starts = ds; pr.p.attn = da; pr.p.n_attn = 1;
+        pr.p.n_groups = (int)groups.size(); pr.p.n_ops = (int)ops.size(); pr.p.n_stages = n_stages;
+        pr.p.barrier = c->fused_barriers + l; pr.p.error = c->eng_error; pr.p.eps = m->eps;
+        pr.p.fallback_count = fb; pr.p.force_fallback = force_fallback_flag();
+        pr.wa = wa;
+        pr.wb = wb;
+        c->fused.push_back(pr);
+    }
+    return SLLM_CUDA_OK;
+}
+
 int build_engine_programs(sllm_cuda_tp_ctx* c) {
     const sllm_cuda_tp_model* m = c->m;
     // each phase's program needs a compiled (WA, WB) pair with WA = the n_embd
@@ -1112,6 +1216,10 @@ int build_engine_programs(sllm_cuda_tp_ctx* c) {
             pr.wb = ph == 1 ? wb_o : ph == 3 ? wb_d : wb_main;
             c->progs.push_back(pr);
         }
+    }
+    if (m->n_ranks == 1 && c->n_ctx <= kEngAttnMaxCtx) {
+        const int rc = build_fused_programs(c, wa, wb_main);
+        if (rc != SLLM_CUDA_OK) return rc;
     }
     return SLLM_CUDA_OK;
 }
@@ -1370,6 +1478,10 @@ extern "C" int sllm_cuda_test_tp_generate_group(sllm_cuda_tp_ctx** cs, int32_t n
 
 extern "C" int sllm_cuda_test_tp_uses_engine(const sllm_cuda_tp_ctx* c) {
     return c != nullptr && !c->progs.empty() ? 1 : 0;
+}
+
+extern "C" int sllm_cuda_test_tp_fused_layers(const sllm_cuda_tp_ctx* c) {
+    return c != nullptr ? (int)c->fused.size() : 0;
 }
 
 extern "C" int sllm_cuda_test_tp_exchange_kind(const sllm_cuda_tp_ctx* c) {

@@ -118,6 +118,7 @@ def test_tp_engine_path_matches_oracle(cuda, orc, synth):
     tm = cuda.TpModel(1, 0, 0, desc=m.desc())
     tc = tm.ctx(32)
     assert tc.uses_engine()
+    assert tc.fused_layers() == cfg.n_layer       # one rank: each layer is one four-stage program
     oc = orc.ctx(m.desc(), 32)
     prompt = _tokens(8, 5, cfg.n_vocab)
     r1, t1 = tc.generate(prompt, 6)
