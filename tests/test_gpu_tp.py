@@ -137,7 +137,9 @@ def test_tp_engine_ranks_agree(cuda):
     prompt = _tokens(9, 6, sd.n_vocab)
     rc1, t1, l1 = _group_run(cuda, sd, 1, prompt, 8)
     assert rc1 == 0
-    for n in (2, 4):
+    # 8 ranks: one kv head and 1024 O columns per rank (the widths the
+    # eight-GPU run uses)
+    for n in (2, 4, 8):
         rc, t, lg = _group_run(cuda, sd, n, prompt, 8)
         assert rc == 0
         assert t.tolist() == t1.tolist(), f"TP={n}"
