@@ -325,7 +325,7 @@ def prefill_leg(pkg, synth, local, rank, world, args):
                         "achieved": round(gtops, 1), "peak": round(peak, 1), "unit": "TOP/s",
                         "frac": round(gtops / peak, 4), "peak_source": kind,
                         "gemm_ms_per_step": round(gms / args.steps, 4)}}
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:     # N = 1 only
         import oracle
         if oracle.reference_available():
             ref = oracle.Reference()
@@ -436,7 +436,7 @@ def decode_leg(pkg, synth, local, rank, world, args):
            "weight_gbs": round(model.weight_bytes() * 320 * world / best / 1e9, 1),
            "api": "sllm_cuda_generate_greedy (host prompt in, ids out, wall clock; best of 3)",
            "token_checksum": int(np.sum(toks.astype(np.int64) * np.arange(1, 257)) % 1000003)}
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:     # N = 1 only
         import oracle
         if oracle.reference_available():
             ref = oracle.Reference()
@@ -593,7 +593,7 @@ def main():
                   "ms_per_step": round(cms / args.steps, 4),
                   "us_per_layer": round(cms / args.steps / copies * 1e3, 3)},
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:     # N = 1 only
         out["cpu_baseline"] = cpu_baseline_sample(cfg, m, xs_host)
     ctx.close()
     model.close()
