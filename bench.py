@@ -1,33 +1,41 @@
-"""Benchmark: I2_S GEMV HBM GB/s on bitnet-b1.58-2B-4T layers, plus greedy decode (B200).
+"""Benchmark: I2_S GEMV HBM GB/s on bitnet-b1.58-2B-4T layers, plus the other configs (B200).
 
 Headline workload (as stated there): the seven I2_S
 GEMV shapes of one 2B-4T layer at batch 1 -- Q 2560x2560, K/V 640x2560,
 O 2560x2560, gate/up 6912x2560, down 2560x6912 -- each on its own f32 N(0,1)
 activation, RMSNorm'd (eps 1e-5, norm weights N(1, 0.02)) and int8-quantised
 per token, run back to back (sllm_cuda_layer_projections_device). One STEP
-runs them through 32 distinct layer copies (556 MB of packed weights, more
+runs them through 32 distinct layer copies (564 MB of algorithmic bytes, more
 than 4x the 126 MB L2), so every step streams its weights from HBM and no
-L2 flush is needed.
+L2 flush is needed. Inputs are seeded synthetic data of the configs' shapes.
 
 Also in the same JSON line, measured in the same run:
-  chain    the decode layer's projection chain (each GEMV's input is the
-           previous one's output: norm -> QKV -> O + residual -> gate/up,
-           SiLU -> down + residual), sllm_cuda_layer_chain_device
-  decode   configs[2]: random-init 2B-4T model, 64-token prompt, 256 greedy
-           tokens, tokens/s through sllm_cuda_generate_greedy, with a bounded
-           sample of the reference CPU decode beside it
+  chain      the decode layer's projection chain (each GEMV's input is the
+             previous one's output: norm -> QKV -> O + residual -> gate/up,
+             SiLU -> down + residual), sllm_cuda_layer_chain_device
+  prefill    configs[3]: 512 tokens through gate/up (SiLU fused) and down on
+             the tcgen05 tensor cores, int8 TOP/s, with the reference CPU path
+  tp_decode  configs[4]: the 80-layer 8192 model, tensor-parallel over the
+             ranks (NCCL between GPUs), tokens/s at batch 1
+  decode     configs[2]: random-init 2B-4T model, 64-token prompt, 256 greedy
+             tokens, tokens/s through sllm_cuda_generate_greedy, with a bounded
+             sample of the reference CPU decode beside it
 
   value         whole-job GB/s: algorithmic bytes of all ranks / max device time
   e2e           the same metric through the host-buffer C ABI call
                 sllm_cuda_layer_projections (pinned inputs copied in, every
                 output copied back each step), wall clock
-  roofline      the GEMV kernel (every launch of the step is one)
+  roofline      the persistent engine kernel (one launch per step)
   cpu_baseline  the reference saphira-llm library (oracle/_ref, compiled from
-                its own sources) running the same projections on the host cores
+                its own sources) running the same projections on the host
+                cores (rank 0, one GPU only)
 
-  python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--no-decode]
-Multi-GPU: one process per GPU (torchrun); each rank runs its own replica
-(the projections do not shard: replicas only), weak scaling.
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+                  [--no-cpu-baseline] [--no-prefill] [--no-tp] [--no-decode]
+                  [--leg decode|prefill|tp]   (one leg only, for profiler captures)
+Multi-GPU: one process per GPU (torchrun); each rank runs its own replica of
+configs 0-3 (the projections do not shard: replicas only, weak scaling);
+configs[4] is sharded over all ranks.
 """
 import argparse
 import importlib
@@ -489,7 +497,8 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
 
     if args.leg is not None:
         leg = {"decode": lambda: decode_leg(pkg, synth, local, rank, world, args),
