@@ -497,8 +497,7 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
 
     if args.leg is not None:
         leg = {"decode": lambda: decode_leg(pkg, synth, local, rank, world, args),
