@@ -43,6 +43,7 @@
 #include <vector>
 
 #include <nccl.h>
+#include <cooperative_groups.h>
 
 #include "backend.cuh"
 #include "common.cuh"
@@ -195,6 +196,105 @@ tp_norm_quant_kernel(const float* __restrict__ x, const float* __restrict__ w, i
         act->scale = s;
         act->sum = total;
     }
+}
+
+// The same RMSNorm + quantisation on a cluster of eight CTAs: each CTA holds
+// one eighth of the vector (one float4 per thread, K % 32 == 0, K <= 32768),
+// and the three reductions (the f64 sum of squares, the absmax, the code sum)
+// pass per-CTA partials through distributed shared memory behind cluster
+// barriers. The results are the single CTA's: the sum is certified for any
+// order, max and the integer sum do not depend on it. Every CTA runs the same
+// straight-line code, so each one reaches every cluster barrier.
+constexpr int kNqCluster = 8;
+
+__global__ void __cluster_dims__(kNqCluster, 1, 1) __launch_bounds__(kNqThreads)
+tp_norm_quant_cluster_kernel(const float* __restrict__ x, const float* __restrict__ w, int K, float eps,
+                             double inv_k, int8_t* __restrict__ q, sllm_cuda_act* act, int* fb, int force) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    __shared__ double dred[32];
+    __shared__ float fred[32];
+    __shared__ int ired[32];
+    __shared__ double c_ss;          // this CTA's partials, read by the whole cluster
+    __shared__ float c_amax;
+    __shared__ int c_sum;
+    __shared__ float s_bcast;
+    const int rank = (int)cl.block_rank();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int per = (K >> 2) / kNqCluster;                 // float4 per CTA
+    const int i = rank * per + tid;
+    const bool live = tid < per;
+    float4 xv = live ? reinterpret_cast<const float4*>(x)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    double ss = __dadd_rn(__dadd_rn((double)__fmul_rn(xv.x, xv.x), (double)__fmul_rn(xv.y, xv.y)),
+                          __dadd_rn((double)__fmul_rn(xv.z, xv.z), (double)__fmul_rn(xv.w, xv.w)));
+    ss = warp_sum_d(ss);
+    if (lane == 0) dred[warp] = ss;
+    __syncthreads();
+    if (tid == 0) {
+        double S = 0.0;
+        for (int k = 0; k < kNqThreads / 32; ++k) S = __dadd_rn(S, dred[k]);
+        c_ss = S;
+    }
+    cl.sync();
+    if (tid == 0) {
+        double S = 0.0;
+        for (int r = 0; r < kNqCluster; ++r) S = __dadd_rn(S, *cl.map_shared_rank(&c_ss, r));
+        float mean;
+        if (!certify_mean_mul(S, K, inv_k, &mean) || force) {
+            // every CTA re-sums in the reference's order and gets the same mean
+            mean = __double2float_rn(__ddiv_rn(rms_ss_reference_order(x, K), (double)K));
+            if (fb != nullptr && rank == 0) atomicAdd(fb, 1);
+        }
+        s_bcast = rms_scale(mean, eps);
+    }
+    __syncthreads();
+    const float sc = s_bcast;
+    const float4 wv = live ? __ldg(reinterpret_cast<const float4*>(w) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    xv.x = __fmul_rn(__fmul_rn(sc, xv.x), wv.x);
+    xv.y = __fmul_rn(__fmul_rn(sc, xv.y), wv.y);
+    xv.z = __fmul_rn(__fmul_rn(sc, xv.z), wv.z);
+    xv.w = __fmul_rn(__fmul_rn(sc, xv.w), wv.w);
+    float amax = fmaxf(fmaxf(fabsf(xv.x), fabsf(xv.y)), fmaxf(fabsf(xv.z), fabsf(xv.w)));
+    amax = warp_max(amax);
+    if (lane == 0) fred[warp] = amax;
+    __syncthreads();
+    if (tid == 0) {
+        float m = 0.0f;
+        for (int k = 0; k < kNqThreads / 32; ++k) m = fmaxf(m, fred[k]);
+        c_amax = m;
+    }
+    cl.sync();
+    if (tid == 0) {
+        float m = 0.0f;
+        for (int r = 0; r < kNqCluster; ++r) m = fmaxf(m, *cl.map_shared_rank(&c_amax, r));
+        s_bcast = quant_scale(m);
+    }
+    __syncthreads();
+    const float s = s_bcast;
+    int sum = 0;
+    if (live) {
+        const int a = quant_one(xv.x, s), b = quant_one(xv.y, s);
+        const int c = quant_one(xv.z, s), d = quant_one(xv.w, s);
+        sum = (a + b) + (c + d);
+        reinterpret_cast<uint32_t*>(q)[i] = (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) |
+                                            ((uint32_t)(c & 0xff) << 16) | ((uint32_t)d << 24);
+    }
+    sum = __reduce_add_sync(0xffffffffu, sum);
+    if (lane == 0) ired[warp] = sum;
+    __syncthreads();
+    if (tid == 0) {
+        int t = 0;
+        for (int k = 0; k < kNqThreads / 32; ++k) t += ired[k];
+        c_sum = t;
+    }
+    cl.sync();
+    if (rank == 0 && tid == 0) {
+        int total = 0;
+        for (int r = 0; r < kNqCluster; ++r) total += *cl.map_shared_rank(&c_sum, r);
+        act->scale = s;
+        act->sum = total;
+    }
+    cl.sync();      // no CTA leaves while rank 0 may still read its shared memory
 }
 
 // y[r] = (float)(sum over chunks of dots - act.sum) * (ws / act.scale) + resid[r]
@@ -851,6 +951,18 @@ cudaError_t launch_count(cudaError_t e, int n) {
     return e;
 }
 
+// RMSNorm + quantisation of a whole vector: the eight-CTA cluster when the
+// length allows it (a multiple of 32, at most 32768), else one CTA
+cudaError_t launch_norm_quant(const float* x, const float* w, int K, float eps, int8_t* q, sllm_cuda_act* act,
+                              int* fb, int force, cudaStream_t st) {
+    const double inv_k = 1.0 / (double)K;
+    if (K % (4 * kNqCluster) == 0 && K <= 4 * kNqCluster * kNqThreads)
+        tp_norm_quant_cluster_kernel<<<kNqCluster, kNqThreads, 0, st>>>(x, w, K, eps, inv_k, q, act, fb, force);
+    else
+        tp_norm_quant_kernel<<<1, kNqThreads, 0, st>>>(x, w, K, eps, inv_k, q, act, fb, force);
+    return cudaGetLastError();
+}
+
 // a layer GEMV phase: the context's engine program when it has one, else the
 // per-GEMV kernel with parameters p
 cudaError_t gemv_or_engine(sllm_cuda_tp_ctx* c, int l, int phase, const GemvParams& p, int pro, int epi, int sms,
@@ -940,9 +1052,8 @@ cudaError_t enqueue_phase(sllm_cuda_tp_ctx* c, int ph, cudaStream_t st, bool cou
     if (sub == 1) {
         // attn_sub_norm + quantisation of the whole attention output, then
         // this rank's columns of O (src/forward.c:728-741)
-        tp_norm_quant_kernel<<<1, kNqThreads, 0, st>>>(c->attn_full, t.attn_sub_norm, E, m->eps, 1.0 / (double)E,
-                                                       c->qa, c->act_a, fb, force);
-        cudaError_t e = launch_count(cudaGetLastError(), cnt);
+        cudaError_t e = launch_count(
+            launch_norm_quant(c->attn_full, t.attn_sub_norm, E, m->eps, c->qa, c->act_a, fb, force, st), cnt);
         if (e != cudaSuccess) return e;
         p.K = m->e_loc; p.nseg = 1;
         p.seg[0] = GemvSeg{t.wo, E, nullptr, c->dots_o};
@@ -962,9 +1073,8 @@ cudaError_t enqueue_phase(sllm_cuda_tp_ctx* c, int ph, cudaStream_t st, bool cou
     }
     // ffn_sub_norm + quantisation of all of h, then this rank's columns of
     // down, chunk by chunk (src/forward.c:781-792)
-    tp_norm_quant_kernel<<<1, kNqThreads, 0, st>>>(c->h_full, t.ffn_sub_norm, m->F, m->eps, 1.0 / (double)m->F,
-                                                   c->qh, c->act_h, fb, force);
-    cudaError_t e = launch_count(cudaGetLastError(), cnt);
+    cudaError_t e =
+        launch_count(launch_norm_quant(c->h_full, t.ffn_sub_norm, m->F, m->eps, c->qh, c->act_h, fb, force, st), cnt);
     if (e == cudaSuccess && !c->progs.empty()) return launch_count(gemv_or_engine(c, l, 3, p, 0, 0, sms, st), cnt);
     for (int ch = 0; ch < m->down_c && e == cudaSuccess; ++ch) {
         GemvParams d = p;
