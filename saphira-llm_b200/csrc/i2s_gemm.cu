@@ -27,6 +27,14 @@
 //                       lanes 32 (w % 4) ..), minus the token's code sum, times
 //                       ws / scale, SiLU(gate) * up when fused.
 //
+// A long single-tensor contraction is split over a cluster of SK CTAs
+// (blockIdx.z): each takes a contiguous share of the k-steps, the others
+// store their int32 accumulators in their idle rings, and after a cluster
+// barrier the first CTA adds them through distributed shared memory before
+// its epilogue; a second barrier keeps the others resident until it has read
+// them. Every thread of every CTA reaches both barriers (the waits before
+// them are bounded).
+//
 // The integer sum is exact in any order, so every dot equals the reference's
 // per-token sllm_i2s_gemv bit for bit; the epilogue is the GEMV epilogue's
 // float sequence. Every wait is bounded by the global timer; a wait that
@@ -35,6 +43,8 @@
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
+
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 #include "gemm.cuh"
@@ -238,7 +248,7 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 // the codes of one packed word, field f: four int8 codes of consecutive elements
 __device__ __forceinline__ uint32_t field_codes(uint32_t w, int f) { return (w >> (6 - 2 * f)) & 0x03030303u; }
 
-template <int BN, bool PAIR, int MT>
+template <int BN, bool PAIR, int MT, int SK>
 __global__ void __launch_bounds__(kGmThreads, 1)
 i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
                 const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_y,
@@ -251,7 +261,11 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     uint8_t* const gsm = gsm_raw + ((1024u - (smem_u32(gsm_raw) & 1023u)) & 1023u);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * (MT * kBM);
-    const int KB = p.K / kBK;
+    // SK > 1: the CTAs of a cluster (blockIdx.z = 0..SK-1) split the
+    // contraction; this CTA takes k-steps [kb0, kb0 + KB)
+    const int KB_all = p.K / kBK;
+    const int kb0 = (int)((long long)blockIdx.z * KB_all / SK);
+    const int KB = (int)((long long)(blockIdx.z + 1) * KB_all / SK) - kb0;
     // token tiles of this CTA that hold tokens (the last CTA row may have fewer)
     const int mt_live = min(MT, (p.M - m0 + kBM - 1) / kBM);
     auto A = [&](int s, int mt) { return gsm + (size_t)s * C::STAGE + mt * C::A_BYTES; };
@@ -282,6 +296,7 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     const uint32_t tmem = tmem_slot;
     volatile int* const abort_v = &abort_flag;
 
+    bool ep_ok = false;     // epilogue warps: the accumulators are complete and no CTA aborted
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
@@ -291,9 +306,10 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
                 const uint32_t use = (uint32_t)(kb / C::S);
                 if (use > 0 && !gm_wait(&bar_empty[s], (use - 1) & 1u, abort_v, p.error)) break;
                 mbar_expect_tx(&bar_loaded[s], (uint32_t)(mt_live * C::A_BYTES + C::NM * C::P_BYTES));
-                for (int mt = 0; mt < mt_live; ++mt) tma_load_2d(A(s, mt), &tm_a, kb * kBK, m0 + mt * kBM, &bar_loaded[s]);
-                tma_load_2d(P(s, 0), &tm_w, kb * kPK, n0, &bar_loaded[s]);
-                if (PAIR) tma_load_2d(P(s, 1), &tm_w2, kb * kPK, n0, &bar_loaded[s]);
+                for (int mt = 0; mt < mt_live; ++mt)
+                    tma_load_2d(A(s, mt), &tm_a, (kb0 + kb) * kBK, m0 + mt * kBM, &bar_loaded[s]);
+                tma_load_2d(P(s, 0), &tm_w, (kb0 + kb) * kPK, n0, &bar_loaded[s]);
+                if (PAIR) tma_load_2d(P(s, 1), &tm_w2, (kb0 + kb) * kPK, n0, &bar_loaded[s]);
                 ++issued;
             }
             // every copy issued lands before the CTA may exit
@@ -369,12 +385,36 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
             ok = __all_sync(0xffffffffu, ok);
         }
         // epilogue: warp group mt (warps 2-5: 0, warps 6-9: 1) takes token tile mt
-        const int mt = (warp - 2) >> 2;
-        const bool acc_ok = __all_sync(0xffffffffu, ok && gm_wait(&bar_acc, 0u, abort_v, p.error)) &&
-                            __all_sync(0xffffffffu, *abort_v == 0);
-        if (acc_ok && mt < mt_live) {
+        ep_ok = __all_sync(0xffffffffu, ok && gm_wait(&bar_acc, 0u, abort_v, p.error)) &&
+                __all_sync(0xffffffffu, *abort_v == 0);
+    }
+    const int mt = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    // SK > 1: a split CTA's accumulator columns, [col][lane] per epilogue warp
+    // in its (now idle) ring, 32 lanes x BN columns
+    uint32_t* const part = reinterpret_cast<uint32_t*>(gsm + (size_t)(warp >= 2 ? warp - 2 : 0) * (BN * 128));
+    if constexpr (SK > 1) {
+        namespace cg = cooperative_groups;
+        cg::cluster_group cl = cg::this_cluster();
+        if (warp >= 2 && cl.block_rank() != 0 && ep_ok && mt < mt_live) {
             tc_fence_after();
-            const int quarter = warp & 3;
+            const uint32_t lane_base = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(mt * C::TILE_COLS);
+            #pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t g[32];
+                tmem_ld32(lane_base + (uint32_t)c0, g);
+                tmem_ld_wait();
+                #pragma unroll
+                for (int j = 0; j < 32; ++j) part[(c0 + j) * 32 + lane] = g[j];
+            }
+        }
+        cl.sync();      // every thread of every CTA of the cluster
+    }
+    bool lead = true;
+    if constexpr (SK > 1) lead = cooperative_groups::this_cluster().block_rank() == 0;
+    if (warp >= 2) {
+        if (ep_ok && lead && mt < mt_live) {
+            tc_fence_after();
             const int row0 = m0 + mt * kBM + 32 * quarter;      // this warp's first token
             const int m = row0 + lane;
             const bool live = m < p.M;
@@ -426,6 +466,17 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
                     }
                 } else {
                     tmem_ld_wait();
+                    if constexpr (SK > 1) {
+                        // the other CTAs' partial dots of these columns (int32: exact)
+                        namespace cg = cooperative_groups;
+                        cg::cluster_group cl = cg::this_cluster();
+                        #pragma unroll 1
+                        for (int r = 1; r < SK; ++r) {
+                            const uint32_t* rp = cl.map_shared_rank(part, r);
+                            #pragma unroll
+                            for (int j = 0; j < 32; ++j) g[j] += rp[(c0 + j) * 32 + lane];
+                        }
+                    }
                     if (p.tma_out) {
                         if (p.dots != nullptr) stage_out(&tm_d, g, n0 + c0);
                         if (p.y != nullptr) {
@@ -452,6 +503,7 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
             __syncwarp();
         }
     }
+    if constexpr (SK > 1) cooperative_groups::this_cluster().sync();   // the leader has read the partials
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -505,9 +557,11 @@ bool encode_out(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, bool PAIR, int MT>
+template <int BN, bool PAIR, int MT, int SK>
 cudaError_t launch_tile(const GemmArgs& a, int* error, cudaStream_t st) {
     using C = GemmCfg<BN, PAIR, MT>;
+    static_assert(SK == 1 || (!PAIR && C::S * C::STAGE >= 4 * MT * BN * 128),
+                  "a split CTA's partial accumulators (4 warps per token tile, 32 lanes x BN) fit its ring");
     CUtensorMap tm_a, tm_w, tm_w2;
     if (!encode_2d(&tm_a, a.q, (uint64_t)a.K, (uint64_t)a.m, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_2d(&tm_w, a.w, (uint64_t)(a.K / 4), (uint64_t)a.n_rows, kPK, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
@@ -541,12 +595,28 @@ cudaError_t launch_tile(const GemmArgs& a, int* error, cudaStream_t st) {
     if (p.tma_out && a.dots != nullptr &&
         !encode_out(&tm_d, a.dots, (uint64_t)a.n_rows, (uint64_t)a.m, CU_TENSOR_MAP_DATA_TYPE_INT32))
         p.tma_out = 0;
-    cudaError_t e =
-        cudaFuncSetAttribute(i2s_gemm_kernel<BN, PAIR, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(i2s_gemm_kernel<BN, PAIR, MT, SK>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
-    const dim3 grid((unsigned)((a.n_rows + BN - 1) / BN), (unsigned)((a.m + MT * kBM - 1) / (MT * kBM)));
-    i2s_gemm_kernel<BN, PAIR, MT><<<grid, kGmThreads, C::SMEM, st>>>(tm_a, tm_w, tm_w2, tm_y, tm_d, p);
-    return cudaGetLastError();
+    const dim3 grid((unsigned)((a.n_rows + BN - 1) / BN), (unsigned)((a.m + MT * kBM - 1) / (MT * kBM)), SK);
+    if (SK == 1) {
+        i2s_gemm_kernel<BN, PAIR, MT, SK><<<grid, kGmThreads, C::SMEM, st>>>(tm_a, tm_w, tm_w2, tm_y, tm_d, p);
+        return cudaGetLastError();
+    }
+    // the SK CTAs of one output tile form a cluster
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kGmThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = SK;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, i2s_gemm_kernel<BN, PAIR, MT, SK>, tm_a, tm_w, tm_w2, tm_y, tm_d, p);
 }
 
 }  // namespace
@@ -579,11 +649,16 @@ int gemm_check(const GemmArgs& a, const char** why) {
 // Tile shapes: the gate/up pair takes 96 weight rows x 256 tokens per CTA
 // (MMAs of N = 192; the 6912 FFN rows make 72 column tiles, 144 CTAs at 512
 // tokens: 51.6 us for both GEMMs against 55.8 us with 128-row tiles on 108
-// CTAs); a single tensor takes 128 rows x 128 tokens, so the 2560-row down
-// projection spreads over 80 CTAs at 512 tokens.
+// CTAs). A single tensor with a long contraction (six k-steps or more) takes
+// 128 rows x 256 tokens per CTA, the contraction split over a cluster of
+// three CTAs whose partial int32 sums the first adds: the 2560-row down
+// projection at 512 tokens runs on 120 CTAs (23.0 us, against 25.0 us for
+// 128 x 128 tiles on 80 CTAs and 27.1 us for 256-row tiles on 120). Short
+// contractions take 128 rows x 128 tokens, unsplit.
 cudaError_t launch_i2s_gemm(const GemmArgs& a, int* error, cudaStream_t st) {
-    if (a.w2 != nullptr) return launch_tile<96, true, 2>(a, error, st);
-    return launch_tile<128, false, 1>(a, error, st);
+    if (a.w2 != nullptr) return launch_tile<96, true, 2, 1>(a, error, st);
+    if (a.K / kBK >= 6) return launch_tile<128, false, 2, 3>(a, error, st);
+    return launch_tile<128, false, 1, 1>(a, error, st);
 }
 
 }  // namespace sllm
