@@ -780,14 +780,15 @@ static cudaError_t launch_layer(const sllm_cuda_model* m, int l, const ChainBufs
 static cudaError_t enqueue_step(sllm_cuda_ctx* c, cudaStream_t st) {
     const sllm_cuda_model* m = c->m;
     int* fb = fallback_counter();
-    cudaError_t e = launch_embed(m->tok_embd, c->tok_seq, c->pos, m->n_embd, m->n_vocab, c->x, st);
+    // the embedding kernel also zeroes the engine's grid barrier, which the
+    // engine launch behind it in the stream then counts up from
+    cudaError_t e = launch_embed(m->tok_embd, c->tok_seq, c->pos, m->n_embd, m->n_vocab, c->x, st,
+                                 c->eng_decode.built ? c->eng_decode.barrier : nullptr);
     if (e != cudaSuccess) return e;
     if (c->eng_decode.built) {
         // every layer in one engine launch: 5 stages each (Q/K/V, attention,
         // O, gate/up, down) behind grid barriers
-        e = cudaMemsetAsync(c->eng_decode.barrier, 0, sizeof(unsigned), st);
-        if (e == cudaSuccess)
-            e = launch_engine(c->eng_decode.params, c->eng_decode.grid, st, c->eng_decode.wa, c->eng_decode.wb);
+        e = launch_engine(c->eng_decode.params, c->eng_decode.grid, st, c->eng_decode.wa, c->eng_decode.wb);
         if (e != cudaSuccess) return e;
         LmParams lp{};
         lp.x = c->x; lp.norm_w = m->output_norm; lp.eps = m->eps; lp.embd = m->tok_embd;

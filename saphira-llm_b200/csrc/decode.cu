@@ -38,7 +38,9 @@ static cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaSt
 // embedding: x = f16_to_f32(tok_embd[token]) (src/forward.c:621-626)
 // ---------------------------------------------------------------------------
 __global__ void embed_kernel(const uint16_t* __restrict__ tok_embd, const int32_t* __restrict__ tok_seq,
-                             const int32_t* __restrict__ pos_ptr, int E, int V, float* __restrict__ x) {
+                             const int32_t* __restrict__ pos_ptr, int E, int V, float* __restrict__ x,
+                             unsigned* reset_word) {
+    if (reset_word != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *reset_word = 0u;
     int tok = tok_seq[*pos_ptr];
     // the host validates every token it writes and the argmax is in range;
     // this only keeps a corrupted id from reading outside the table
@@ -247,8 +249,8 @@ lm_head_kernel(const LmParams p) {
 // launchers
 // ---------------------------------------------------------------------------
 cudaError_t launch_embed(const uint16_t* tok_embd, const int32_t* tok_seq, const int32_t* pos_ptr, int E, int V,
-                         float* x, cudaStream_t st) {
-    embed_kernel<<<(E + 255) / 256, 256, 0, st>>>(tok_embd, tok_seq, pos_ptr, E, V, x);
+                         float* x, cudaStream_t st, unsigned* reset_word) {
+    embed_kernel<<<(E + 255) / 256, 256, 0, st>>>(tok_embd, tok_seq, pos_ptr, E, V, x, reset_word);
     return cudaGetLastError();
 }
 

@@ -49,8 +49,10 @@ struct LmParams {
     int row_base;
 };
 
+// reset_word (nullable): a word the kernel zeroes, the decode step's engine
+// barrier, so that the step graph needs no memset node before the engine
 cudaError_t launch_embed(const uint16_t* tok_embd, const int32_t* tok_seq, const int32_t* pos_ptr, int E, int V,
-                         float* x, cudaStream_t st);
+                         float* x, cudaStream_t st, unsigned* reset_word = nullptr);
 int attention_max_ctx();
 cudaError_t prepare_decode_kernels();
 cudaError_t launch_attention(const AttnParams& p, int n_head, cudaStream_t st);
