@@ -7,6 +7,7 @@
 // feedback live in device memory, so a whole prompt + generation is a run of
 // graph launches with no host round trip until the ids are copied back.
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -596,6 +597,8 @@ static cudaError_t engine_program_launch(const EngineProgram& p, cudaStream_t st
 // ---------------------------------------------------------------------------
 // context
 // ---------------------------------------------------------------------------
+static constexpr int kProjPieces = 2;
+
 struct sllm_cuda_ctx {
     const sllm_cuda_model* m = nullptr;
     int n_ctx = 0;
@@ -630,6 +633,11 @@ struct sllm_cuda_ctx {
     EngineProgram eng_chain;         // the layer chain on the persistent engine
     EngineProgram eng_proj;          // the independent projections on the persistent engine
     EngineProgram eng_decode;        // every layer of a decode step, attention included
+    // the host-buffer projections in two pieces, the first piece's outputs
+    // copied back on copy_stream behind the event its launch records
+    EngineProgram eng_piece[kProjPieces];
+    cudaEvent_t piece_done[kProjPieces] = {};
+    cudaStream_t copy_stream = nullptr;
 };
 
 // the reference's angle recurrence (src/ops.c:529-549), on the host libm
@@ -668,6 +676,11 @@ extern "C" void sllm_cuda_ctx_free(sllm_cuda_ctx* c) {
     engine_program_free(c->eng_chain);
     engine_program_free(c->eng_proj);
     engine_program_free(c->eng_decode);
+    for (int i = 0; i < kProjPieces; ++i) {
+        engine_program_free(c->eng_piece[i]);
+        if (c->piece_done[i]) cudaEventDestroy(c->piece_done[i]);
+    }
+    if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
     delete c;
 }
 
@@ -1146,8 +1159,8 @@ static cudaError_t launch_projections(const sllm_cuda_model* m, int l, const flo
 
 // The seven projections of each layer as one engine stage: every GEMV has its
 // own input, so nothing waits for anything and the weights stream back to back.
-static int projections_program(const sllm_cuda_model* m, sllm_cuda_ctx* c, int begin, int n, const float* x,
-                               float* y, int* fb) {
+static int projections_program(const sllm_cuda_model* m, sllm_cuda_ctx* c, EngineProgram& prog, int begin, int n,
+                               const float* x, float* y, int* fb) {
     const int E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa;
     size_t ystride = 0;
     sllm_cuda_layer_projections_sizes(m, &ystride);
@@ -1177,7 +1190,7 @@ static int projections_program(const sllm_cuda_model* m, sllm_cuda_ctx* c, int b
     }
     std::vector<int> stage_first{0, (int)ops.size()};
     g_engine_eps = m->eps;
-    return engine_program_build(c->eng_proj, groups, ops, stage_first, m->device, c->stream, fb,
+    return engine_program_build(prog, groups, ops, stage_first, m->device, c->stream, fb,
                                 engine_wpl(E), engine_wpl(F));
 }
 
@@ -1214,11 +1227,77 @@ extern "C" int sllm_cuda_layer_projections_device(const sllm_cuda_model* m, sllm
     }
     EngineProgram& p = c->eng_proj;
     if (!p.built || p.key_begin != layer_begin || p.key_n != n_layers || p.key_x != x || p.key_y != y) {
-        int rc = projections_program(m, c, layer_begin, n_layers, x, y, fb);
+        int rc = projections_program(m, c, p, layer_begin, n_layers, x, y, fb);
         if (rc != SLLM_CUDA_OK) return rc;
         p.key_begin = layer_begin; p.key_n = n_layers; p.key_x = x; p.key_y = y;
     }
     CK(engine_program_launch(p, (cudaStream_t)stream), "projections");
+    return SLLM_CUDA_OK;
+}
+
+// Where the host-buffer projections split into two pieces; 0 = run as one.
+// The first piece's outputs go back to the host on the copy stream while the
+// second piece computes, so only the second piece's copy is exposed. It is
+// made just large enough that the first piece's copy (host link, ~54 GB/s
+// measured) hides behind its compute (weights streamed at ~5.6 TB/s). Every
+// piece boundary costs about 11 us of engine tail and ramp, more than a
+// third piece would save, and below 16 layers more than the split saves.
+static int projection_split(const sllm_cuda_model* m, int n_layers) {
+    if (!engine_supports(engine_wpl(m->n_embd), engine_wpl(m->n_ff)) || n_layers < 16) return 0;
+    size_t ystride = 0;
+    sllm_cuda_layer_projections_sizes(m, &ystride);
+    const double E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa;
+    const double weight_bytes = (2.0 * E * E + 2.0 * G * E + 3.0 * E * F) / 4.0;   // 2-bit codes of a layer
+    const double copy_s = (double)ystride * 4.0 / 54e9, compute_s = weight_bytes / 5.6e12;
+    int last = (int)std::ceil(copy_s / (copy_s + compute_s) * n_layers);
+    last = std::max(1, std::min(last, n_layers / 2));
+    return n_layers - last;
+}
+
+static int projections_in_pieces(const sllm_cuda_model* m, sllm_cuda_ctx* c, int begin, int n, int split,
+                                 const float* dx, float* dy, float* y_host, size_t ystride) {
+    const int bound[kProjPieces + 1] = {0, split, n};
+    const int pieces = kProjPieces;
+    if (c->copy_stream == nullptr) {
+        CK(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking), "copy stream");
+        for (int i = 0; i < kProjPieces; ++i)
+            CK(cudaEventCreateWithFlags(&c->piece_done[i], cudaEventDisableTiming), "piece events");
+    }
+    int* fb = fallback_counter();
+    if (fb == nullptr) return fail(SLLM_CUDA_ERR_NOMEM, "layer_projections: diagnostics counter");
+    for (int i = 0; i < pieces; ++i) {
+        const int lo = bound[i], hi = bound[i + 1];
+        EngineProgram& p = c->eng_piece[i];
+        float* y = dy + (size_t)lo * ystride;
+        if (!p.built || p.key_begin != begin + lo || p.key_n != hi - lo || p.key_x != dx || p.key_y != y) {
+            const int rc = projections_program(m, c, p, begin + lo, hi - lo, dx, y, fb);
+            if (rc != SLLM_CUDA_OK) return rc;
+            p.key_begin = begin + lo; p.key_n = hi - lo; p.key_x = dx; p.key_y = y;
+        }
+        if (p.exec != nullptr) return fail(SLLM_CUDA_ERR_ARG, "layer_projections: a piece needs one stage");
+    }
+    // every piece reports a gave-up wait into the first piece's error word,
+    // which comes back behind the last copy
+    int* err = c->eng_piece[0].error;
+    for (int i = 0; i < pieces; ++i) {
+        const EngineProgram& p = c->eng_piece[i];
+        EngParams ep = p.params;
+        ep.error = err;
+        CK(launch_engine(ep, p.grid, c->stream, p.wa, p.wb), "projections piece");
+        count_launches(1);
+        CK(cudaEventRecord(c->piece_done[i], c->stream), "piece event");
+    }
+    for (int i = 0; i < pieces; ++i) {
+        const int lo = bound[i], hi = bound[i + 1];
+        CK(cudaStreamWaitEvent(c->copy_stream, c->piece_done[i], 0), "piece wait");
+        CK(cudaMemcpyAsync(y_host + (size_t)lo * ystride, dy + (size_t)lo * ystride, (size_t)(hi - lo) * ystride * 4,
+                           cudaMemcpyDeviceToHost, c->copy_stream), "projection outputs");
+    }
+    int32_t* err_host = &c->pinned[8];
+    CK(cudaMemcpyAsync(err_host, err, sizeof(int), cudaMemcpyDeviceToHost, c->copy_stream), "engine status");
+    CK(cudaStreamSynchronize(c->copy_stream), "projections sync");
+    if (*err_host != 0)
+        return fail(SLLM_CUDA_ERR_TIMEOUT, "engine: a bounded device wait gave up (code %d)", (int)*err_host);
     return SLLM_CUDA_OK;
 }
 
@@ -1250,6 +1329,8 @@ extern "C" int sllm_cuda_layer_projections(const sllm_cuda_model* m, sllm_cuda_c
         dy = (float*)((uint8_t*)c->io + ((xbytes + 255) & ~(size_t)255));
     }
     CK(cudaMemcpyAsync(dx, x_host, xbytes, cudaMemcpyHostToDevice, c->stream), "projection inputs");
+    const int split = projection_split(m, n_layers);
+    if (split > 0) return projections_in_pieces(m, c, layer_begin, n_layers, split, dx, dy, y_host, ystride);
     int rc = sllm_cuda_layer_projections_device(m, c, layer_begin, n_layers, dx, dy, c->stream);
     if (rc != SLLM_CUDA_OK) return rc;
     CK(cudaMemcpyAsync(y_host, dy, ybytes, cudaMemcpyDeviceToHost, c->stream), "projection outputs");

@@ -169,6 +169,44 @@ def test_layer_projections_match_oracle(cuda, orc, synth):
             yo += rows
 
 
+def test_layer_projections_in_pieces(cuda, orc, synth):
+    """The host-buffer call over 16 or more layers runs the layers as pieces
+    whose outputs return while the next piece computes: every layer's outputs
+    equal the oracle's and the device entry point's, into pageable and pinned
+    host memory, for spans that do not start at layer 0 or divide evenly."""
+    import torch
+    cfg = synth.small_config(n_layer=20, n_embd=256, n_ff=512, n_head=2, n_head_kv=1, n_vocab=64)
+    m = synth.SynthModel(cfg, seed=31)
+    model = cuda.Model(m.desc())
+    c = model.ctx(8)
+    xs_n, ys_n = cuda.projection_sizes(model)
+    E, F, G = cfg.n_embd, cfg.n_ff, cfg.n_embd_gqa
+    specs = [("attn_q", E, E, "attn_norm"), ("attn_k", G, E, "attn_norm"), ("attn_v", G, E, "attn_norm"),
+             ("attn_output", E, E, "attn_sub_norm"), ("ffn_gate", F, E, "ffn_norm"),
+             ("ffn_up", F, E, "ffn_norm"), ("ffn_down", E, F, "ffn_sub_norm")]
+    x = np.random.default_rng(31).standard_normal(xs_n).astype(np.float32)
+    for begin, n in [(0, 20), (3, 17), (0, 16)]:
+        y = c.layer_projections(begin, n, x)
+        for il in range(n):
+            xo = yo = 0
+            for name, rows, k, norm in specs:
+                xn = orc.rms_norm(x[xo:xo + k], m.tensors[f"blk.{begin + il}.{norm}.weight"].view(np.float32),
+                                  cfg.eps)
+                want, _ = orc.gemv_f32(m.tensors[f"blk.{begin + il}.{name}.weight"], rows, k, xn)
+                assert np.array_equal(bits(y[il, yo:yo + rows]), bits(want)), (begin, il, name)
+                xo += k
+                yo += rows
+        xd = torch.from_numpy(x).cuda()
+        yd = torch.empty(n * ys_n, dtype=torch.float32, device="cuda")
+        c.layer_projections_device(begin, n, xd, yd)
+        torch.cuda.synchronize()
+        assert np.array_equal(bits(y.reshape(-1)), bits(yd.cpu().numpy())), (begin, n)
+        xp = torch.from_numpy(x).pin_memory()
+        yp = torch.full((n * ys_n,), float("nan"), dtype=torch.float32).pin_memory()
+        assert cuda.lib().sllm_cuda_layer_projections(model.h, c.h, begin, n, xp.data_ptr(), yp.data_ptr()) == 0
+        assert np.array_equal(bits(yp.numpy()), bits(y.reshape(-1))), (begin, n)
+
+
 @pytest.mark.parametrize("cfg_kw", [
     dict(n_layer=2, n_embd=256, n_ff=512, n_head=2, n_head_kv=1, n_vocab=64),
     dict(n_layer=2, n_embd=1152, n_ff=3072, n_head=9, n_head_kv=3, n_vocab=64),
