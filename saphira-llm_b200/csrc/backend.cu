@@ -1334,6 +1334,16 @@ extern "C" int sllm_cuda_layer_projections(const sllm_cuda_model* m, sllm_cuda_c
     int rc = sllm_cuda_layer_projections_device(m, c, layer_begin, n_layers, dx, dy, c->stream);
     if (rc != SLLM_CUDA_OK) return rc;
     CK(cudaMemcpyAsync(y_host, dy, ybytes, cudaMemcpyDeviceToHost, c->stream), "projection outputs");
+    if (c->eng_proj.built && n_layers > 0) {
+        // the engine's status word comes back behind the outputs: one wait
+        int32_t* err_host = &c->pinned[8];
+        CK(cudaMemcpyAsync(err_host, c->eng_proj.error, sizeof(int), cudaMemcpyDeviceToHost, c->stream),
+           "engine status");
+        CK(cudaStreamSynchronize(c->stream), "projections sync");
+        if (*err_host != 0)
+            return fail(SLLM_CUDA_ERR_TIMEOUT, "engine: a bounded device wait gave up (code %d)", (int)*err_host);
+        return SLLM_CUDA_OK;
+    }
     CK(cudaStreamSynchronize(c->stream), "projections sync");
     return engine_error(c->eng_proj);
 }
