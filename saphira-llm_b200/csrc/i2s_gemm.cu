@@ -295,6 +295,11 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
     volatile int* const abort_v = &abort_flag;
+    // launched with programmatic stream serialisation: the set-up above
+    // overlaps the previous launch, whose outputs (the activation codes and
+    // their scales) are complete and visible past this point; a no-op in an
+    // ordinary launch
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     bool ep_ok = false;     // epilogue warps: the accumulators are complete and no CTA aborted
     if (warp == 0) {
@@ -599,23 +604,28 @@ cudaError_t launch_tile(const GemmArgs& a, int* error, cudaStream_t st) {
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     const dim3 grid((unsigned)((a.n_rows + BN - 1) / BN), (unsigned)((a.m + MT * kBM - 1) / (MT * kBM)), SK);
-    if (SK == 1) {
-        i2s_gemm_kernel<BN, PAIR, MT, SK><<<grid, kGmThreads, C::SMEM, st>>>(tm_a, tm_w, tm_w2, tm_y, tm_d, p);
-        return cudaGetLastError();
-    }
-    // the SK CTAs of one output tile form a cluster
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kGmThreads);
     cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = SK;
+    // programmatic dependent launch: the CTAs may be scheduled while the
+    // previous kernel runs (they wait for it after setting up); a CTA needs
+    // more shared memory than two GEMM CTAs could share, so two GEMM launches
+    // never hold one SM's tensor memory at once
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (SK > 1) {
+        // the SK CTAs of one output tile form a cluster
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 1;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = SK;
+        cfg.numAttrs = 2;
+    }
     return cudaLaunchKernelEx(&cfg, i2s_gemm_kernel<BN, PAIR, MT, SK>, tm_a, tm_w, tm_w2, tm_y, tm_d, p);
 }
 

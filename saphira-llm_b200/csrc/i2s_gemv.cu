@@ -355,6 +355,11 @@ quant_rows_vec_kernel(const float* x, int n, int8_t* q, sllm_cuda_act* act) {
     __shared__ int ired[kQrThreads / 32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n4 = n >> 2;
+    // launched with programmatic stream serialisation: the next launch (a
+    // GEMM, which waits for this one after its set-up) may be scheduled now,
+    // and x may come from the previous launch
+    pdl_trigger();
+    pdl_wait();
     const float4* xr = reinterpret_cast<const float4*>(x + (size_t)blockIdx.x * n);
     uint32_t* qr = reinterpret_cast<uint32_t*>(q + (size_t)blockIdx.x * n);
     float4 v[VPT];
@@ -473,8 +478,17 @@ cudaError_t launch_quant_act_rows(const float* x, int rows, int n, int8_t* q, sl
                      (reinterpret_cast<uintptr_t>(q) & 3u) == 0;
     if (vec) {
         const int vpt = (n / 4 + kQrThreads - 1) / kQrThreads;     // 1..8
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(rows);
+        cfg.blockDim = dim3(kQrThreads);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
         switch (vpt) {
-#define SLLM_QR_CASE(k) case k: quant_rows_vec_kernel<k><<<rows, kQrThreads, 0, st>>>(x, n, q, acts); break;
+#define SLLM_QR_CASE(k) case k: return cudaLaunchKernelEx(&cfg, quant_rows_vec_kernel<k>, x, n, q, acts);
             SLLM_QR_CASE(1) SLLM_QR_CASE(2) SLLM_QR_CASE(3) SLLM_QR_CASE(4)
             SLLM_QR_CASE(5) SLLM_QR_CASE(6) SLLM_QR_CASE(7) SLLM_QR_CASE(8)
 #undef SLLM_QR_CASE
