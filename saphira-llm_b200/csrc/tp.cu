@@ -122,6 +122,8 @@ tp_norm_quant_kernel(const float* __restrict__ x, const float* __restrict__ w, i
     __shared__ int ired[32];
     __shared__ float s_bcast;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // as the cluster form
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int K4 = K >> 2;
     float4 xv[kNqKpt];
     #pragma unroll
@@ -221,6 +223,11 @@ tp_norm_quant_cluster_kernel(const float* __restrict__ x, const float* __restric
     __shared__ float s_bcast;
     const int rank = (int)cl.block_rank();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // programmatic dependent launch: the next launch (the down program, whose
+    // consumers wait for this one) may be scheduled now, and x comes from the
+    // previous launch
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int per = (K >> 2) / kNqCluster;                 // float4 per CTA
     const int i = rank * per + tid;
     const bool live = tid < per;
@@ -301,6 +308,7 @@ tp_norm_quant_cluster_kernel(const float* __restrict__ x, const float* __restric
 // (src/forward.c:739-750, 790-801)
 __global__ void tp_epilogue_kernel(const int32_t* __restrict__ dots, int n_chunks, int rows, const sllm_cuda_act* act,
                                    const float* __restrict__ ws, const float* __restrict__ resid, float* __restrict__ y) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");      // the dots come from the previous launch
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) return;
     int d = 0;
@@ -946,6 +954,24 @@ int phase_xchg(const sllm_cuda_tp_model* m, int ph) {
     return (ph - 1) % 4;     // X_ATTN, X_DOTS_O, X_H, X_DOTS_D in order
 }
 
+// a launch with programmatic stream serialisation: it may be scheduled while
+// the previous kernel runs; the kernel waits for it (griddepcontrol.wait)
+// before its first global access
+cudaLaunchConfig_t pdl_config(int grid, int block, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.stream = st;
+    return cfg;
+}
+
+cudaLaunchAttribute pdl_attribute() {
+    cudaLaunchAttribute a = {};
+    a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    a.val.programmaticStreamSerializationAllowed = 1;
+    return a;
+}
+
 cudaError_t launch_count(cudaError_t e, int n) {
     if (e == cudaSuccess) count_launches(n);
     return e;
@@ -956,11 +982,14 @@ cudaError_t launch_count(cudaError_t e, int n) {
 cudaError_t launch_norm_quant(const float* x, const float* w, int K, float eps, int8_t* q, sllm_cuda_act* act,
                               int* fb, int force, cudaStream_t st) {
     const double inv_k = 1.0 / (double)K;
-    if (K % (4 * kNqCluster) == 0 && K <= 4 * kNqCluster * kNqThreads)
-        tp_norm_quant_cluster_kernel<<<kNqCluster, kNqThreads, 0, st>>>(x, w, K, eps, inv_k, q, act, fb, force);
-    else
-        tp_norm_quant_kernel<<<1, kNqThreads, 0, st>>>(x, w, K, eps, inv_k, q, act, fb, force);
-    return cudaGetLastError();
+    const bool cluster = K % (4 * kNqCluster) == 0 && K <= 4 * kNqCluster * kNqThreads;
+    cudaLaunchConfig_t cfg = pdl_config(cluster ? kNqCluster : 1, kNqThreads, st);
+    cudaLaunchAttribute attr = pdl_attribute();
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cluster)
+        return cudaLaunchKernelEx(&cfg, tp_norm_quant_cluster_kernel, x, w, K, eps, inv_k, q, act, fb, force);
+    return cudaLaunchKernelEx(&cfg, tp_norm_quant_kernel, x, w, K, eps, inv_k, q, act, fb, force);
 }
 
 // a layer GEMV phase: the context's engine program when it has one, else the
@@ -983,8 +1012,11 @@ cudaError_t enqueue_phase(sllm_cuda_tp_ctx* c, int ph, cudaStream_t st, bool cou
     auto epi = [&](const int32_t* dots, int chunks, const sllm_cuda_act* act, const uint8_t* w, int rows, int cols,
                    const float* resid, float* y) {
         const float* ws = reinterpret_cast<const float*>(w + (size_t)rows * cols / 4);
-        tp_epilogue_kernel<<<(rows + 255) / 256, 256, 0, st>>>(dots, chunks, rows, act, ws, resid, y);
-        return launch_count(cudaGetLastError(), cnt);
+        cudaLaunchConfig_t cfg = pdl_config((rows + 255) / 256, 256, st);
+        cudaLaunchAttribute attr = pdl_attribute();
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        return launch_count(cudaLaunchKernelEx(&cfg, tp_epilogue_kernel, dots, chunks, rows, act, ws, resid, y), cnt);
     };
     if (ph == 0) {
         cudaError_t e = launch_count(launch_embed(m->tok_embd, c->tok_seq, c->pos, E, m->V, c->x, st), cnt);
