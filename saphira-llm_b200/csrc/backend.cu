@@ -1258,10 +1258,11 @@ static int projections_in_pieces(const sllm_cuda_model* m, sllm_cuda_ctx* c, int
                                  const float* dx, float* dy, float* y_host, size_t ystride) {
     const int bound[kProjPieces + 1] = {0, split, n};
     const int pieces = kProjPieces;
-    if (c->copy_stream == nullptr) {
-        CK(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking), "copy stream");
+    if (c->copy_stream == nullptr) {     // created last: a stream means the events exist
         for (int i = 0; i < kProjPieces; ++i)
-            CK(cudaEventCreateWithFlags(&c->piece_done[i], cudaEventDisableTiming), "piece events");
+            if (c->piece_done[i] == nullptr)
+                CK(cudaEventCreateWithFlags(&c->piece_done[i], cudaEventDisableTiming), "piece events");
+        CK(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking), "copy stream");
     }
     int* fb = fallback_counter();
     if (fb == nullptr) return fail(SLLM_CUDA_ERR_NOMEM, "layer_projections: diagnostics counter");
