@@ -62,6 +62,20 @@ SLLM_CUDA_API int sllm_cuda_test_tp_generate_group(sllm_cuda_tp_ctx ** cs, int32
  */
 SLLM_CUDA_API long long sllm_cuda_test_kernel_launches(void);
 
+/*
+ * The persistent engine's split of each stage's rows over `grid` CTAs, the
+ * host computation every engine program is built with (no device is used).
+ * Op i has rows[i] rows of K[i] elements, epilogue epi[i] (0 dots, 1 f32,
+ * 2 residual, 3 gate/up pair, 4 attention heads) and input group group[i];
+ * stage s runs ops [stage_first[s], stage_first[s + 1]). `out` receives
+ * n_stages * (grid + 1) cursors as (op, row) pairs: CTA c of stage s runs
+ * the rows from cursor c up to cursor c + 1. Returns SLLM_CUDA_ERR_ARG for
+ * inconsistent arguments.
+ */
+SLLM_CUDA_API int sllm_cuda_test_engine_split(const int32_t * rows, const int32_t * K, const int32_t * epi,
+                                const int32_t * group, int32_t n_ops, const int32_t * stage_first,
+                                int32_t n_stages, int32_t grid, int32_t * out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -532,6 +532,30 @@ std::vector<EngCursor> sllm::engine_starts(const std::vector<EngOp>& ops, const 
     return st;
 }
 
+extern "C" int sllm_cuda_test_engine_split(const int32_t* rows, const int32_t* K, const int32_t* epi,
+                                           const int32_t* group, int32_t n_ops, const int32_t* stage_first,
+                                           int32_t n_stages, int32_t grid, int32_t* out) {
+    if (rows == nullptr || K == nullptr || epi == nullptr || group == nullptr || stage_first == nullptr ||
+        out == nullptr || n_ops < 0 || n_stages < 1 || grid < 1 || stage_first[0] != 0 ||
+        stage_first[n_stages] != n_ops)
+        return fail(SLLM_CUDA_ERR_ARG, "engine_split: bad arguments");
+    for (int s = 0; s < n_stages; ++s)
+        if (stage_first[s + 1] < stage_first[s]) return fail(SLLM_CUDA_ERR_ARG, "engine_split: stages out of order");
+    std::vector<EngOp> ops((size_t)n_ops);
+    for (int i = 0; i < n_ops; ++i) {
+        if (rows[i] < 1 || K[i] < 4 || epi[i] < 0 || epi[i] > kEpiAttention || group[i] < 0)
+            return fail(SLLM_CUDA_ERR_ARG, "engine_split: bad op %d", i);
+        ops[i].rows = rows[i]; ops[i].K = K[i]; ops[i].epi = epi[i]; ops[i].group = group[i];
+    }
+    const std::vector<int> sf(stage_first, stage_first + n_stages + 1);
+    const std::vector<EngCursor> st = engine_starts(ops, sf, grid);
+    for (size_t i = 0; i < st.size(); ++i) {
+        out[2 * i] = st[i].op;
+        out[2 * i + 1] = st[i].row;
+    }
+    return SLLM_CUDA_OK;
+}
+
 static int engine_program_build(EngineProgram& p, const std::vector<EngGroup>& groups, const std::vector<EngOp>& ops,
                                 const std::vector<int>& stage_first, int device, cudaStream_t capture_stream,
                                 int* fallback, int wa, int wb, const std::vector<AttnParams>* attn = nullptr,
