@@ -266,11 +266,18 @@ def time_device(fn, steps, warmup, stream, world):
         fn()
     ev1.record(stream)
     torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    return float(t.item()), None
+    return max_over_ranks(ev0.elapsed_time(ev1), world), None
+
+
+def max_over_ranks(value, world, device="cuda"):
+    """The largest of every rank's `value` (a duration): a multi-GPU figure
+    is the slowest rank's. One rank: the value itself, with no collective."""
+    if world <= 1:
+        return float(value)
+    import torch
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
 
 
 PREFILL_TOKENS = 512
@@ -387,10 +394,7 @@ def tp_decode_leg(pkg, local, rank, world, args):
     rc, toks = ctx.generate(prompt, n_new)
     dt = time.perf_counter() - t0
     assert rc == 0, rc
-    t = torch.tensor([dt], dtype=torch.float64, device="cuda")
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    dt = float(t.item())
+    dt = max_over_ranks(dt, world)
     E, F, H, Hkv, V = sd.n_embd, sd.n_ff, sd.n_head, sd.n_head_kv, sd.n_vocab
     i2s_layer = (E * E * 2 + 2 * (Hkv * 128) * E + 3 * F * E) // 4
     per_gpu_bytes = (sd.n_layer * i2s_layer + V * E * 2) / world
@@ -435,10 +439,7 @@ def decode_leg(pkg, synth, local, rank, world, args):
         runs.append(time.perf_counter() - t0)
         assert rc == 0 and toks2.tolist() == toks.tolist()
     best = min(runs)
-    tb = torch.tensor([best], dtype=torch.float64, device="cuda")
-    if world > 1:
-        torch.distributed.all_reduce(tb, op=torch.distributed.ReduceOp.MAX)
-    best = float(tb.item())
+    best = max_over_ranks(best, world)
     out = {"workload": "greedy_decode_2b4t", "prompt": 64, "new_tokens": 256,
            "tokens_per_s": round((64 + 256) * world / best, 1), "ms_per_token": round(best / 320 * 1e3, 4),
            "weight_gbs": round(model.weight_bytes() * 320 * world / best / 1e9, 1),
@@ -555,10 +556,8 @@ def main():
     for _ in range(args.steps):
         assert lib.sllm_cuda_layer_projections(model.h, ctx.h, 0, copies, host_in.data_ptr(),
                                                host_out.data_ptr()) == 0
-    te = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device="cuda")
-    if world > 1:
-        torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
-    e2e = step_bytes * args.steps * world / float(te.item()) / 1e9
+    te = max_over_ranks(time.perf_counter() - t0, world)
+    e2e = step_bytes * args.steps * world / te / 1e9
 
     # secondary: the dependent chain
     xc = torch.from_numpy(np.random.default_rng(rank).standard_normal(E).astype(np.float32)).cuda()
