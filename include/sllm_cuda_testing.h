@@ -72,6 +72,17 @@ SLLM_CUDA_API long long sllm_cuda_test_kernel_launches(void);
  * the rows from cursor c up to cursor c + 1. Returns SLLM_CUDA_ERR_ARG for
  * inconsistent arguments.
  */
+/*
+ * The tensor-parallel shard of rank `rank` of `n_ranks`, as
+ * sllm_cuda_tp_model_upload computes it (host code, no device is used):
+ * out[0..7] = query heads, kv heads, n_embd columns (of O), n_ff rows (of
+ * gate/up) and columns (of down), down chunks, columns per chunk, first
+ * vocabulary row, vocabulary rows. Returns the upload's error for a
+ * geometry it refuses.
+ */
+SLLM_CUDA_API int sllm_cuda_test_tp_plan(int32_t n_layer, int32_t E, int32_t F, int32_t H, int32_t Hkv,
+                           int32_t V, int32_t n_ranks, int32_t rank, int32_t * out);
+
 SLLM_CUDA_API int sllm_cuda_test_engine_split(const int32_t * rows, const int32_t * K, const int32_t * epi,
                                 const int32_t * group, int32_t n_ops, const int32_t * stage_first,
                                 int32_t n_stages, int32_t grid, int32_t * out);

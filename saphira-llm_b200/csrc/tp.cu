@@ -721,6 +721,18 @@ extern "C" void sllm_cuda_tp_comm_free(sllm_cuda_tp_comm* c) {
     delete c;
 }
 
+extern "C" int sllm_cuda_test_tp_plan(int32_t n_layer, int32_t E, int32_t F, int32_t H, int32_t Hkv, int32_t V,
+                                      int32_t n_ranks, int32_t rank, int32_t* out) {
+    if (out == nullptr) return fail(SLLM_CUDA_ERR_ARG, "tp_plan: null output");
+    const int rc = check_geometry(n_layer, E, F, H, Hkv, V, n_ranks, rank);
+    if (rc != SLLM_CUDA_OK) return rc;
+    sllm_cuda_tp_model m;
+    fill_geometry(&m, n_layer, E, F, H, Hkv, V, n_ranks, rank);
+    const int32_t v[8] = {m.hq, m.hk, m.e_loc, m.f_loc, m.down_c, m.down_k, m.v0, m.v_loc};
+    std::memcpy(out, v, sizeof v);
+    return SLLM_CUDA_OK;
+}
+
 static int tp_model_alloc(sllm_cuda_tp_model* m, int device) {
     m->device = device;
     const Layout L = shard_layout(m);
