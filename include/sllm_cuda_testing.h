@@ -83,6 +83,16 @@ SLLM_CUDA_API long long sllm_cuda_test_kernel_launches(void);
 SLLM_CUDA_API int sllm_cuda_test_tp_plan(int32_t n_layer, int32_t E, int32_t F, int32_t H, int32_t Hkv,
                            int32_t V, int32_t n_ranks, int32_t rank, int32_t * out);
 
+/*
+ * Where sllm_cuda_layer_projections cuts a call of n_layers layers into two
+ * engine launches (the first piece's outputs are copied back while the
+ * second computes): the first layer of the second piece, or 0 when the call
+ * runs as one launch (fewer than 16 layers, or widths the engine is not
+ * compiled for). -1 for nonsensical widths.
+ */
+SLLM_CUDA_API int sllm_cuda_test_projection_split(int32_t n_embd, int32_t n_ff, int32_t n_embd_gqa,
+                                    int32_t n_layers);
+
 SLLM_CUDA_API int sllm_cuda_test_engine_split(const int32_t * rows, const int32_t * K, const int32_t * epi,
                                 const int32_t * group, int32_t n_ops, const int32_t * stage_first,
                                 int32_t n_stages, int32_t grid, int32_t * out);

@@ -93,6 +93,7 @@ def lib():
     L.sllm_cuda_test_kernel_launches.restype = C.c_longlong
     L.sllm_cuda_test_engine_split.argtypes = [vp, vp, vp, vp, i32, vp, i32, i32, vp]
     L.sllm_cuda_test_tp_plan.argtypes = [i32, i32, i32, i32, i32, i32, i32, i32, vp]
+    L.sllm_cuda_test_projection_split.argtypes = [i32, i32, i32, i32]
     _lib = L
     return L
 

@@ -1266,16 +1266,25 @@ extern "C" int sllm_cuda_layer_projections_device(const sllm_cuda_model* m, sllm
 // measured) hides behind its compute (weights streamed at ~5.6 TB/s). Every
 // piece boundary costs about 11 us of engine tail and ramp, more than a
 // third piece would save, and below 16 layers more than the split saves.
-static int projection_split(const sllm_cuda_model* m, int n_layers) {
-    if (!engine_supports(engine_wpl(m->n_embd), engine_wpl(m->n_ff)) || n_layers < 16) return 0;
-    size_t ystride = 0;
-    sllm_cuda_layer_projections_sizes(m, &ystride);
-    const double E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa;
+static int projection_split_widths(int n_embd, int n_ff, int n_embd_gqa, int n_layers) {
+    if (!engine_supports(engine_wpl(n_embd), engine_wpl(n_ff)) || n_layers < 16) return 0;
+    const double E = n_embd, F = n_ff, G = n_embd_gqa;
     const double weight_bytes = (2.0 * E * E + 2.0 * G * E + 3.0 * E * F) / 4.0;   // 2-bit codes of a layer
-    const double copy_s = (double)ystride * 4.0 / 54e9, compute_s = weight_bytes / 5.6e12;
+    const double out_bytes = 4.0 * (3.0 * E + 2.0 * G + 2.0 * F);                  // f32 outputs of a layer
+    const double copy_s = out_bytes / 54e9, compute_s = weight_bytes / 5.6e12;
     int last = (int)std::ceil(copy_s / (copy_s + compute_s) * n_layers);
     last = std::max(1, std::min(last, n_layers / 2));
     return n_layers - last;
+}
+
+static int projection_split(const sllm_cuda_model* m, int n_layers) {
+    return projection_split_widths(m->n_embd, m->n_ff, m->n_embd_gqa, n_layers);
+}
+
+extern "C" int sllm_cuda_test_projection_split(int32_t n_embd, int32_t n_ff, int32_t n_embd_gqa,
+                                               int32_t n_layers) {
+    if (n_embd < 1 || n_ff < 1 || n_embd_gqa < 1 || n_layers < 0) return -1;
+    return projection_split_widths(n_embd, n_ff, n_embd_gqa, n_layers);
 }
 
 static int projections_in_pieces(const sllm_cuda_model* m, sllm_cuda_ctx* c, int begin, int n, int split,

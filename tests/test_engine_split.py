@@ -7,7 +7,8 @@ cursor names a real row, so every row runs exactly once -- and for balance:
 no CTA costs more than the average plus a few prologues and rows, in the
 split's own cost model (a row streams K/4 bytes, twice for a gate/up pair;
 an attention head counts as 64 KB; entering an input group costs its
-RMSNorm + quantisation prologue, worth 192 KB)."""
+RMSNorm + quantisation prologue, worth 192 KB). Also the host-buffer
+projections' cut of a call into two engine launches."""
 import ctypes as C
 
 import numpy as np
@@ -156,3 +157,25 @@ def test_bad_arguments(split):
     assert split([(0, 128, EPI_F32, 0)], [0, 1], 4)[0] == -1   # an op with no rows
     assert split([(4, 128, 9, 0)], [0, 1], 4)[0] == -1    # unknown epilogue
     assert split(ops, [0, 1], 0)[0] == -1                 # no CTAs
+
+
+def test_host_projection_split(pkg):
+    """The host-buffer projections' two-piece cut: none under 16 layers;
+    otherwise the second piece holds at least one layer and at most half,
+    sized so that the first piece's copy-back (f32 outputs at ~54 GB/s)
+    hides behind the second piece's compute (2-bit codes at ~5.6 TB/s):
+    20 + 12 layers for the 2B-4T benchmark's 32."""
+    L = pkg.lib()
+    E, F, G = 2560, 6912, 640
+    assert L.sllm_cuda_test_projection_split(E, F, G, 32) == 20
+    for n in range(0, 16):
+        assert L.sllm_cuda_test_projection_split(E, F, G, n) == 0
+    for n in range(16, 200):
+        split = L.sllm_cuda_test_projection_split(E, F, G, n)
+        last = n - split
+        assert 1 <= last <= n // 2, (n, split)
+        copy = 4.0 * (3 * E + 2 * G + 2 * F) / 54e9
+        compute = (2.0 * E * E + 2.0 * G * E + 3.0 * E * F) / 4.0 / 5.6e12
+        assert split * copy <= last * compute * 1.0001 or last == n // 2, n   # the first copy hides
+    assert L.sllm_cuda_test_projection_split(640, 1280, 640, 32) == 0       # widths the engine lacks
+    assert L.sllm_cuda_test_projection_split(0, F, G, 32) == -1
