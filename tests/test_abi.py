@@ -85,3 +85,17 @@ def test_probe_reports_no_device_here(built):
         pytest.skip("a device is present; covered by the gpu tests")
     rc, n, cc = built.probe()
     assert rc == -4 and n == 0
+
+
+def test_c11_caller_links_and_runs(built, tmp_path):
+    """The headers compile as strict C11 (no C++ in any declaration) and a C
+    program linked against the library runs the device-free calls:
+    tests/c/abi_caller.c, the way saphira-llm's own C host code binds it."""
+    exe = tmp_path / "abi_caller"
+    lib_dir = os.path.dirname(built.LIB_PATH)
+    cmd = ["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-pedantic", "-I", os.path.join(ROOT, "include"),
+           os.path.join(ROOT, "tests", "c", "abi_caller.c"), built.LIB_PATH, "-Wl,-rpath," + lib_dir, "-o", str(exe)]
+    out = subprocess.run(cmd, capture_output=True, text=True)
+    assert out.returncode == 0, out.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0 and run.stdout.strip() == "ok", run.stdout + run.stderr
