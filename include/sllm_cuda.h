@@ -289,7 +289,10 @@ SLLM_CUDA_API int sllm_cuda_layer_chain_device(const sllm_cuda_model * m, sllm_c
  *      Q (n_embd), K, V (n_embd_gqa), O (n_embd), gate, up (n_ff), down (n_embd).
  * sllm_cuda_layer_projections_sizes returns the input length and stores the
  * per-layer output length. The _device form takes 16-byte aligned device
- * vectors and is asynchronous on `stream`.
+ * vectors and is asynchronous on `stream`. The host form returns when y is on
+ * the host; from 16 layers up it runs them as two launches and copies the
+ * first launch's outputs back on a second stream of the context while the
+ * second computes (any host memory; pinned copies faster).
  */
 SLLM_CUDA_API size_t sllm_cuda_layer_projections_sizes(const sllm_cuda_model * m,
                                                        size_t * y_floats_per_layer);
