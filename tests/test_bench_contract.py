@@ -42,3 +42,21 @@ def test_reference_arm_json_line():
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
     assert d["config"]["workload"] == "layer_projections_2b4t"
+
+
+def test_headline_algorithmic_bytes():
+    """The roofline numerator of the headline: per 2B-4T layer, the seven
+    tensors' 2-bit codes with their 32-byte scale tails, each GEMV's input
+    and norm vector once, each f32 output once -- 17,636,576 bytes, so
+    564,370,432 bytes per step of 32 layer copies."""
+    import importlib
+    import bench
+    synth = importlib.import_module("saphira-llm_b200.synth")
+    cfg = synth.Config(n_layer=1, n_vocab=256)
+    m = synth.SynthModel(cfg, seed=1)
+    E, F, G = cfg.n_embd, cfg.n_ff, cfg.n_embd_gqa
+    assert (E, F, G) == (2560, 6912, 640)
+    codes = (2 * E * E + 2 * G * E + 3 * F * E) // 4 + 7 * 32
+    closed = codes + 2 * 4 * (6 * E + F) + 4 * (3 * E + 2 * G + 2 * F)
+    assert bench.projection_bytes(cfg, m) == closed == 17_636_576
+    assert bench.projection_bytes(cfg, m) * bench.N_COPIES == 564_370_432
