@@ -58,7 +58,7 @@ SLLM_CUDA_API const char * sllm_cuda_status_string(int status);
 SLLM_CUDA_API const char * sllm_cuda_last_error(void);
 
 /*
- * Capability probe for the dispatch row (src/dispatch.c:246
+ * Capability probe for the dispatch row (src/dispatch.c:133
  * sllm_dispatch_resolve, src/i2s_gemm.c:315 sllm_i2s_select_auto).
  * Reports the device count and the compute capability of device 0.
  * Returns SLLM_CUDA_ERR_UNSUPPORTED when no device of compute capability
@@ -306,10 +306,11 @@ SLLM_CUDA_API int sllm_cuda_layer_projections_device(const sllm_cuda_model * m, 
 /*
  * sllm_cuda_layer_chain_device without any allocation. This entry point has
  * no counterpart in the reference: it serves callers that cannot call
- * cudaMalloc -- code recording a CUDA graph under a strict capture mode, hosts
- * whose own allocator already holds the device's memory, loops that cannot
- * take cudaMalloc's implicit synchronisation -- and that hold a model but no
- * context. Same results as sllm_cuda_layer_chain_device, bit for bit.
+ * cudaMalloc -- hosts whose own allocator already holds the device's memory
+ * (a late cudaMalloc fails or fragments it), loops that cannot take
+ * cudaMalloc's implicit device synchronisation -- and that hold a model but
+ * no context. Same results as sllm_cuda_layer_chain_device, bit for bit. It
+ * calls no cudaMalloc, cudaFree or allocating library routine.
  *
  * Its scratch (2*n_embd + 2*n_embd_gqa + n_ff floats) is a fixed 128 KB
  * device array inside the library (32768 floats), held by every device that

@@ -22,6 +22,10 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 abi = importlib.import_module("saphira-llm_b200.abi")
 
+# Where the reference source tree lies. Read in this one place; the Makefile,
+# the build entry point and the tests take it from here.
+REFERENCE_DIR = os.environ.get("SLLM_REFERENCE_DIR", "/root/reference")
+
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libsllm_ref.so")
 
@@ -36,8 +40,8 @@ def build(ref=True):
     """Compile the restatement (and the reference, when its sources exist)."""
     import subprocess
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
-    if ref and os.path.isdir("/root/reference/src"):
-        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+    if ref and os.path.isdir(os.path.join(REFERENCE_DIR, "src")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={REFERENCE_DIR}"], check=True)
 
 
 def _a(x, dt):

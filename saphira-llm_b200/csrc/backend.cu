@@ -1435,8 +1435,12 @@ extern "C" int sllm_cuda_layer_chain_device_noalloc(const sllm_cuda_model* m, in
     // every scratch vector is written before it is read within one call
     // (Q/K/V -> q, k, v; O -> ffn_inp; gate/up -> h), so nothing is cleared
     ChainBufs b{x, s, s + E, s + E + G, s + E + 2 * G, s + 2 * E + 2 * G, nullptr};
-    for (int l = layer_begin; l < layer_begin + n_layers; ++l)
-        CK(launch_layer(m, l, b, nullptr, 0, (cudaStream_t)stream, false, nullptr), "layer_chain_noalloc");
+    // the fallback counter stays null (the kernels skip a null counter); the
+    // forced-fallback test switch is a host int and is honoured as elsewhere
+    for (int l = layer_begin; l < layer_begin + n_layers; ++l) {
+        CK(launch_layer(m, l, b, nullptr, g_force_fallback, (cudaStream_t)stream, false, nullptr),
+           "layer_chain_noalloc");
         g_kernel_launches += 4;
+    }
     return SLLM_CUDA_OK;
 }

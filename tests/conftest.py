@@ -17,8 +17,6 @@ for p in (ROOT, os.path.join(ROOT, "oracle")):
     if p not in sys.path:
         sys.path.insert(0, p)
 
-REFERENCE_TREE = "/root/reference"
-
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device of compute capability 10.x (B200)")
@@ -46,7 +44,7 @@ def orc():
 def ref():
     import oracle
     if not oracle.reference_available():
-        if os.path.isdir(os.path.join(REFERENCE_TREE, "src")):
+        if os.path.isdir(os.path.join(oracle.REFERENCE_DIR, "src")):
             oracle.build(ref=True)
         else:
             pytest.skip("reference library oracle/_ref/libsllm_ref.so not built and the reference tree is absent")

@@ -17,7 +17,8 @@ import struct
 import numpy as np
 import pytest
 
-from conftest import REFERENCE_TREE, bits
+import oracle
+from conftest import bits
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -73,7 +74,7 @@ def test_quantiser_known_answers(orc):
 
 
 def _converter_cases():
-    path = os.path.join(REFERENCE_TREE, "tests/golden/i2s-converter.txt")
+    path = os.path.join(oracle.REFERENCE_DIR, "tests/golden/i2s-converter.txt")
     if not os.path.exists(path):
         return []
     cases = []
