@@ -15,8 +15,12 @@ Also in the same JSON line, measured in the same run:
              SiLU -> down + residual), sllm_cuda_layer_chain_device
   prefill    configs[3]: 512 tokens through gate/up (SiLU fused) and down on
              the tcgen05 tensor cores, int8 TOP/s, with the reference CPU path
+  gemv       configs[0]: the single 6912x2560 GEMV over 128 distinct weight
+             copies per step (L2-cold), as 128 back-to-back launches and as
+             one persistent launch, with the reference CPU GEMV beside it
   tp_decode  configs[4]: the 80-layer 8192 model, tensor-parallel over the
-             ranks (NCCL between GPUs), tokens/s at batch 1
+             ranks (NCCL between GPUs), tokens/s at batch 1, with the
+             reference kernels chained on the CPU beside it (one rank)
   decode     configs[2]: random-init 2B-4T model, 64-token prompt, 256 greedy
              tokens, tokens/s through sllm_cuda_generate_greedy, with a bounded
              sample of the reference CPU decode beside it
@@ -31,8 +35,8 @@ Also in the same JSON line, measured in the same run:
                 cores (rank 0, one GPU only)
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
-                  [--no-cpu-baseline] [--no-prefill] [--no-tp] [--no-decode]
-                  [--leg decode|prefill|tp]   (one leg only, for profiler captures)
+                  [--no-cpu-baseline] [--no-gemv] [--no-prefill] [--no-tp] [--no-decode]
+                  [--leg decode|prefill|tp|gemv]   (one leg only, for profiler captures)
 Multi-GPU: one process per GPU (torchrun); each rank runs its own replica of
 configs 0-3 (the projections do not shard: replicas only, weak scaling);
 configs[4] is sharded over all ranks.
@@ -65,6 +69,17 @@ def peaks():
         return float(d["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def cpu_model():
+    """The host CPU's model name (the CPU baselines run on it)."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def projection_bytes(cfg, m):
@@ -204,7 +219,7 @@ def cpu_baseline_sample(cfg, m, x, seconds=10.0):
         n += 1
     dt = time.perf_counter() - t0
     return {"value": round(projection_bytes(cfg, m) * n / dt / 1e9, 3), "unit": "GB/s", "cores": rp.pool.threads,
-            "kind": "reference",
+            "kind": "reference", "cpu": cpu_model(),
             "sample": f"{n} layers' seven projections (of the same {cfg.n_layer} layer copies) in {dt:.1f} s, "
                       f"reference ISA level {rp.ref.isa}"}
 
@@ -240,6 +255,7 @@ def reference_arm(args, world, rank):
         "config": {"workload": "layer_projections_2b4t", "layers_per_step": per_step, "threads": rp.pool.threads,
                    "isa_level": rp.ref.isa},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": rp.pool.threads, "kind": "reference",
+                         "cpu": cpu_model(),
                          "sample": f"{per_step} of the {N_COPIES} layer copies per step, {args.steps} steps"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
@@ -283,14 +299,22 @@ def max_over_ranks(value, world, device="cuda"):
 PREFILL_TOKENS = 512
 
 
+INT8_NOMINAL_TOPS = 4500.0
+
+
 def int8_peak():
-    """Dense int8 tensor peak: twice the measured bf16 dense (cuBLAS burst)
-    rate, as on every Blackwell part (nominal 4.5 vs 2.25 P ops/s)."""
+    """Dense int8 tensor peak. The pool's measured peaks carry no int8 figure,
+    so this is the nominal B200 dense rate (4.5 P ops/s, the sparse figure
+    halved); 2x the measured bf16 burst rate is reported beside it."""
+    return INT8_NOMINAL_TOPS, "nominal B200 dense int8 (4.5 P ops/s; no measured int8 peak on this pool)"
+
+
+def bf16_x2_peak():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            return 2.0 * float(json.load(f)["bf16_tflops"]), "2x measured bf16 dense (burst)"
+            return 2.0 * float(json.load(f)["bf16_tflops"])
     except Exception:
-        return 2.0 * 1590.0, "2x fallback bf16 dense"
+        return 2.0 * 1590.0
 
 
 def prefill_leg(pkg, synth, local, rank, world, args):
@@ -333,12 +357,37 @@ def prefill_leg(pkg, synth, local, rank, world, args):
     peak, kind = int8_peak()
     tops = ops * args.steps * world / (ms / 1e3) / 1e12
     gtops = ops * args.steps / (gms / 1e3) / 1e12
+    # e2e: host activations in (pinned), the down projection's outputs back,
+    # every step, through the same C-ABI calls
+    xa_p, xd_p = torch.from_numpy(xa_h).pin_memory(), torch.from_numpy(xd_h).pin_memory()
+    y_p = torch.empty((M, E), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        xa.copy_(xa_p, non_blocking=True)
+        xd.copy_(xd_p, non_blocking=True)
+        step()
+        y_p.copy_(y, non_blocking=True)
+        st.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    if world > 1:
+        torch.distributed.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    te = max_over_ranks(time.perf_counter() - t0, world)
     out = {"workload": "prefill_ffn_2b4t (512 tokens: quant + gate/up SiLU + quant + down)",
            "value": round(tops, 2), "unit": "int8 TOP/s", "ms_per_step": round(ms / args.steps, 4),
            "ops_per_step": ops, "device_error": err,
+           "e2e": {"value": round(ops * args.steps * world / te / 1e12, 2), "unit": "int8 TOP/s",
+                   "h2d_bytes_per_step": int(xa_h.nbytes + xd_h.nbytes), "d2h_bytes_per_step": int(4 * M * E),
+                   "api": "sllm_cuda_i2s_quant_act_rows + sllm_cuda_i2s_gemm_silu + sllm_cuda_i2s_gemm, "
+                          "pinned host activations in and outputs back every step, wall clock"},
            "roofline": {"bound": "tensor", "kernel": "i2s_gemm_kernel (gate/up pair + down)",
                         "achieved": round(gtops, 1), "peak": round(peak, 1), "unit": "TOP/s",
                         "frac": round(gtops / peak, 4), "peak_source": kind,
+                        "frac_of_2x_measured_bf16": round(gtops / bf16_x2_peak(), 4),
                         "gemm_ms_per_step": round(gms / args.steps, 4)}}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:     # N = 1 only
         import oracle
@@ -359,9 +408,131 @@ def prefill_leg(pkg, synth, local, rank, world, args):
             dt = time.perf_counter() - t0
             out["cpu_reference"] = {"value": round(2.0 * (2 * F * E + E * F) * n_tok / dt / 1e12, 4),
                                     "unit": "int8 TOP/s", "cores": pool.threads, "kind": "reference",
+                                    "cpu": cpu_model(),
                                     "sample": f"{n_tok} of the 512 tokens, per-token quant + 3 pooled GEMVs, "
                                               f"{dt:.1f} s"}
     del m
+    return out
+
+
+GEMV_COPIES = 128
+
+
+def gemv_bytes(rows, n):
+    """Algorithmic bytes of one configs[0] GEMV: the packed codes, the f32
+    scale after them, the f32 input and the f32 outputs."""
+    return rows * n // 4 + 4 + 4 * n + 4 * rows
+
+
+def gemv_leg(pkg, synth, local, rank, world, args):
+    """the single 6912 x 2560 GEMV (quantise, ternary dot,
+    epilogue), L2-cold: a step runs it over 128 distinct weight copies
+    (566 MB, 4.5x the L2) with one shared f32 N(0,1) input. Timed two ways:
+    128 back-to-back sllm_cuda_i2s_gemv_f32 launches (one CUDA graph per step,
+    plain launches as a caller makes them), and one sllm_cuda_gemv_batch_run
+    (the 128 GEMVs as one persistent engine launch)."""
+    import torch
+    rows, n, count = 6912, 2560, GEMV_COPIES
+    nb = rows * n // 4
+    stride = (nb + 32 + 255) // 256 * 256
+    rng = np.random.default_rng(500 + rank)
+    host = np.zeros((count, stride), np.uint8)
+    host[:, :nb] = synth.LUT81[rng.integers(0, 81, size=(count, nb), dtype=np.uint8)]
+    scales = rng.uniform(0.01, 0.1, count).astype(np.float32)
+    host[:, nb:nb + 4] = scales.view(np.uint8).reshape(count, 4)
+    wdev = torch.from_numpy(host).cuda()
+    del host
+    ws = [wdev[i] for i in range(count)]
+    x_h = np.random.default_rng(600 + rank).standard_normal(n).astype(np.float32)
+    x = torch.from_numpy(x_h).cuda()
+    y = torch.empty((count, rows), dtype=torch.float32, device="cuda")
+    y1 = torch.empty((count, rows), dtype=torch.float32, device="cuda")
+    unit = gemv_bytes(rows, n)
+    side = torch.cuda.Stream()
+
+    # (a) back-to-back launches, recorded once into a graph
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        for i in range(count):               # warm-up outside the capture
+            pkg.gemv_f32(ws[i], rows, n, x, y1[i], None, side)
+        side.synchronize()
+        with torch.cuda.graph(g, stream=side):
+            for i in range(count):
+                pkg.gemv_f32(ws[i], rows, n, x, y1[i], None, side)
+    st = torch.cuda.current_stream()
+    ms_l, _ = time_device(g.replay, args.steps, args.warmup, st, world)
+
+    # (b) the same 128 GEMVs as one engine launch
+    batch = pkg.GemvBatch(ws, rows, n, local)
+    run = lambda: batch.run(x, y, 0, st)
+    ms_e, _ = time_device(run, args.steps, args.warmup, st, world)
+    torch.cuda.synchronize()
+    err = batch.error()
+    same = bool(torch.equal(y.view(torch.int32), y1.view(torch.int32)))
+
+    # e2e: the input up from pinned memory, the 128 GEMVs, every output back
+    x_p = torch.from_numpy(x_h).pin_memory()
+    y_p = torch.empty((count, rows), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        x.copy_(x_p, non_blocking=True)
+        batch.run(x, y, 0, st)
+        y_p.copy_(y, non_blocking=True)
+        st.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    if world > 1:
+        torch.distributed.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    te = max_over_ranks(time.perf_counter() - t0, world)
+    peak, peak_kind = peaks()
+    step_bytes = unit * count
+    gbs_e = step_bytes * args.steps * world / (ms_e / 1e3) / 1e9
+    gbs_l = step_bytes * args.steps * world / (ms_l / 1e3) / 1e9
+    per_e = step_bytes * args.steps / (ms_e / 1e3) / 1e9       # this rank's kernel
+    per_l = step_bytes * args.steps / (ms_l / 1e3) / 1e9
+    out = {"workload": "gemv_6912x2560 (configs[0]: one GEMV, 128 distinct weight copies per step, shared x)",
+           "value": round(gbs_e, 1), "unit": "GB/s", "bytes_per_gemv": unit, "gemvs_per_step": count,
+           "l2": "inputs larger than L2: 128 distinct copies (566 MB, 4.5x the 126 MB L2) per step, no flush",
+           "engine": {"api": "sllm_cuda_gemv_batch_run (one persistent launch of 128 GEMVs)",
+                      "ms_per_step": round(ms_e / args.steps, 4), "us_per_gemv": round(ms_e / args.steps / count * 1e3, 3),
+                      "gbs": round(gbs_e, 1), "device_error": err, "outputs_equal_launches": same},
+           "launches": {"api": "128 x sllm_cuda_i2s_gemv_f32 (plain launches, one CUDA graph per step)",
+                        "ms_per_step": round(ms_l / args.steps, 4),
+                        "us_per_gemv": round(ms_l / args.steps / count * 1e3, 3), "gbs": round(gbs_l, 1),
+                        "frac": round(per_l / peak, 4)},
+           "e2e": {"value": round(step_bytes * args.steps * world / te / 1e9, 1), "unit": "GB/s",
+                   "h2d_bytes_per_step": 4 * n, "d2h_bytes_per_step": 4 * rows * count,
+                   "api": "sllm_cuda_gemv_batch_run, pinned input up and every output back per step, wall clock"},
+           "roofline": {"bound": "hbm", "kernel": "i2s_engine_kernel<5,14> (128 GEMVs, one launch)",
+                        "achieved": round(per_e, 1), "peak": peak, "unit": "GB/s", "frac": round(per_e / peak, 4),
+                        "peak_source": peak_kind, "bytes_per_launch": step_bytes}}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+        if oracle.reference_available():
+            ref = oracle.Reference()
+            pool = ref.pool(os.cpu_count() or 1)
+            hw = wdev[:16].cpu().numpy()
+            dots = np.zeros(rows, np.int32)
+            k, t0 = 0, time.perf_counter()
+            while time.perf_counter() - t0 < 5.0:
+                # sllm_i2s_quant_act, pooled sllm_i2s_gemv (src/forward.c:196-205), the epilogue
+                q, s_, total = ref.quant_act(x_h)
+                w = hw[k % 16]
+                pool.gemv(w, rows, n, q, dots)
+                ws_ = np.float32(w[nb:nb + 4].view(np.float32)[0])
+                _ = (dots - total).astype(np.float32) * (ws_ / np.float32(s_))
+                k += 1
+            dt = time.perf_counter() - t0
+            out["cpu_reference"] = {"value": round(unit * k / dt / 1e9, 3), "unit": "GB/s", "cores": pool.threads,
+                                    "kind": "reference", "cpu": cpu_model(),
+                                    "sample": f"{k} GEMVs over 16 of the copies (70 MB, beyond the host caches) "
+                                              f"in {dt:.1f} s"}
+    batch.close()
+    del g
     return out
 
 
@@ -394,17 +565,28 @@ def tp_decode_leg(pkg, local, rank, world, args):
     rc, toks = ctx.generate(prompt, n_new)
     dt = time.perf_counter() - t0
     assert rc == 0, rc
+    dev_ms = max_over_ranks(ctx.last_run_ms(), world)
     dt = max_over_ranks(dt, world)
     E, F, H, Hkv, V = sd.n_embd, sd.n_ff, sd.n_head, sd.n_head_kv, sd.n_vocab
     i2s_layer = (E * E * 2 + 2 * (Hkv * 128) * E + 3 * F * E) // 4
     per_gpu_bytes = (sd.n_layer * i2s_layer + V * E * 2) / world
     steps = n_prompt + n_new
+    kv_row = 2 * sd.n_layer * Hkv * 128 * 4 / world
+    run_bytes_gpu = per_gpu_bytes * steps + kv_row * sum(range(1, steps + 1))
+    peak, peak_kind = peaks()
+    achieved = run_bytes_gpu / (dev_ms / 1e3) / 1e9
     out = {"workload": "tp_decode_80L_8192 (configs[4], batch 1)", "tp": world,
            "tokens_per_s": round(steps / dt, 2), "ms_per_token": round(dt / steps * 1e3, 4),
            "steps": f"{n_prompt} prompt + {n_new} greedy, one token per step",
            "weight_gbs_per_gpu": round(per_gpu_bytes * steps / dt / 1e9, 1),
            "model_gb_per_gpu": round(model.bytes() / 1e9, 2), "build_s": round(build_s, 2),
            "token_checksum": int(sum((i + 1) * int(v) for i, v in enumerate(toks))),
+           "device_ms_per_token": round(dev_ms / steps, 4),
+           "roofline": {"bound": "hbm", "kernel": "per-token step graph (engine layer programs, attention, "
+                                                  "exchanges, head), device time, slowest rank",
+                        "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s per GPU",
+                        "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                        "bytes_per_step_per_gpu": int(run_bytes_gpu / steps)},
            "layer_gemvs": ("persistent engine: per layer one program of four stages (Q/K/V, attention, O, "
                            "gate/up) and one for down" if ctx.fused_layers() > 0 else
                            "persistent engine (one program per phase)") if ctx.uses_engine() else "per-GEMV kernels",
@@ -415,7 +597,60 @@ def tp_decode_leg(pkg, local, rank, world, args):
     model.close()
     if comm is not None:
         comm.close()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_reference"] = tp_cpu_reference(sd, steps)
     return out
+
+
+def tp_cpu_reference(sd, steps):
+    """configs[4] on the host cores with the reference's own kernels. Its model
+    API refuses 80 layers (SLLM_LAYER_MAX 64), so the reference kernels run
+    chained per layer, pooled as src/forward.c:196-205 pools them: one layer
+    of the configs[4] geometry (sllm_rms_norm, sllm_i2s_quant_act, pooled
+    sllm_i2s_gemv and the epilogue for all seven projections, SiLU, residual
+    adds) is timed and multiplied by 80, and the pooled F16 head
+    (sllm_dot_f16_f32 per row, src/forward.c:215-233) is timed on 16384 of the
+    128256 rows and scaled. Attention at these lengths is a small share and
+    is left out, so the figure is an upper bound on the reference's speed."""
+    import oracle
+    if not oracle.reference_available():
+        return None
+    synth = importlib.import_module("saphira-llm_b200.synth")
+    ref = oracle.Reference()
+    cores = os.cpu_count() or 1
+    pool = ref.pool(cores)
+    cfg = synth.Config(n_layer=1, n_embd=sd.n_embd, n_ff=sd.n_ff, n_head=sd.n_head, n_head_kv=sd.n_head_kv,
+                       n_vocab=64)
+    m = synth.SynthModel(cfg, seed=sd.seed)
+    d = m.desc()
+    E, F, G = cfg.n_embd, cfg.n_ff, cfg.n_embd_gqa
+    x = np.random.default_rng(1).standard_normal(E).astype(np.float32)
+    scratch = np.zeros(4 * E + 2 * G + 3 * F, np.float32)
+    qbuf = np.zeros(max(E, F), np.int8)
+    dots = np.zeros(max(E, F), np.int32)
+    pool.layer_chain(d, 0, x, scratch, qbuf, dots)
+    n_l, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 4.0:
+        pool.layer_chain(d, 0, x, scratch, qbuf, dots)
+        n_l += 1
+    t_layer = (time.perf_counter() - t0) / n_l
+    rows = 16384
+    embd = (np.random.default_rng(2).standard_normal(rows * E).astype(np.float32) * 0.02).astype(np.float16)
+    embd = embd.view(np.uint16)
+    logits = np.zeros(rows, np.float32)
+    xn = np.random.default_rng(3).standard_normal(E).astype(np.float32)
+    pool.lm_head(embd, rows, E, xn, logits)
+    n_h, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 2.0:
+        pool.lm_head(embd, rows, E, xn, logits)
+        n_h += 1
+    t_head = (time.perf_counter() - t0) / n_h * (sd.n_vocab / rows)
+    t_tok = sd.n_layer * t_layer + t_head
+    return {"tokens_per_s": round(1.0 / t_tok, 3), "ms_per_token": round(t_tok * 1e3, 1), "cores": pool.threads,
+            "cpu": cpu_model(), "kind": "reference",
+            "sample": f"one {E}/{F} layer chained {n_l} times ({t_layer * 1e3:.1f} ms each) x {sd.n_layer} layers, "
+                      f"plus the F16 head timed on {rows} rows x {n_h} and scaled to {sd.n_vocab}; "
+                      "attention left out (upper bound on the reference's speed)"}
 
 
 def decode_leg(pkg, synth, local, rank, world, args):
@@ -428,7 +663,7 @@ def decode_leg(pkg, synth, local, rank, world, args):
     prompt = np.random.default_rng(7 + rank).integers(0, cfg.n_vocab, 64).astype(np.int32)
     rc, toks = ctx.generate(prompt, 256)         # warm-up (captures the step graph)
     assert rc == 0, pkg.lib().sllm_cuda_last_error()
-    runs = []
+    runs, dev = [], []
     for _ in range(3):
         ctx.reset()
         torch.cuda.synchronize()
@@ -437,14 +672,36 @@ def decode_leg(pkg, synth, local, rank, world, args):
         t0 = time.perf_counter()
         rc, toks2 = ctx.generate(prompt, 256)
         runs.append(time.perf_counter() - t0)
+        dev.append(ctx.last_run_ms())
         assert rc == 0 and toks2.tolist() == toks.tolist()
     best = min(runs)
     best = max_over_ranks(best, world)
+    dev_ms = max_over_ranks(min(dev), world)
+    # algorithmic bytes of the 320 steps: every weight once per step, and at
+    # step t the KV rows of positions 0..t (fp32 K and V of every layer)
+    kv_row = 2 * cfg.n_layer * cfg.n_embd_gqa * 4
+    run_bytes = model.weight_bytes() * 320 + kv_row * sum(range(1, 321))
+    peak, peak_kind = peaks()
+    achieved = run_bytes / (dev_ms / 1e3) / 1e9
     out = {"workload": "greedy_decode_2b4t", "prompt": 64, "new_tokens": 256,
            "tokens_per_s": round((64 + 256) * world / best, 1), "ms_per_token": round(best / 320 * 1e3, 4),
            "weight_gbs": round(model.weight_bytes() * 320 * world / best / 1e9, 1),
            "api": "sllm_cuda_generate_greedy (host prompt in, ids out, wall clock; best of 3)",
+           "device_ms_per_token": round(dev_ms / 320, 4),
+           "roofline": {"bound": "hbm", "kernel": "decode step graph (embed, i2s_engine_kernel<5,14> over the "
+                                                  "30 layers, lm_head_kernel), device time of the 320 steps",
+                        "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                        "bytes_per_step": int(run_bytes / 320)},
            "token_checksum": int(np.sum(toks.astype(np.int64) * np.arange(1, 257)) % 1000003)}
+    # the reference's own 256 tokens for this model and prompt (the fixture
+    # tests/golden/make_golden.py --large wrote from the compiled reference)
+    fx = os.path.join(ROOT, "tests", "golden", "decode_large.json")
+    if rank == 0 and os.path.exists(fx):
+        case = {c["name"]: c for c in json.load(open(fx))}.get("configs2-2b4t-30l-64+256")
+        if case is not None and case["prompt"] == prompt.tolist():
+            out["tokens_identical_to_reference"] = toks.tolist() == case["tokens"]
+            out["reference_tokens"] = "tests/golden/decode_large.json (all 256, same model seed and prompt)"
     if rank == 0 and world == 1 and not args.no_cpu_baseline:     # N = 1 only
         import oracle
         if oracle.reference_available():
@@ -459,7 +716,8 @@ def decode_leg(pkg, synth, local, rank, world, args):
             dt = time.perf_counter() - t0
             ctx.reset()
             rc, g = ctx.generate(prompt[:8], n_new)
-            out["cpu_reference"] = {"tokens_per_s": round((8 + n_new) / dt, 2), "cores": cores,
+            out["cpu_reference"] = {"tokens_per_s": round((8 + n_new) / dt, 2), "cores": cores, "cpu": cpu_model(),
+                                    "kind": "reference",
                                     "sample": f"prompt 8 + {n_new} greedy tokens through sllm_generate_greedy",
                                     "tokens_identical": bool(rcr == 0 and g.tolist() == rt.tolist())}
             del rm
@@ -478,9 +736,10 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-tp", action="store_true")
+    ap.add_argument("--no-gemv", action="store_true")
     ap.add_argument("--copies", type=int, default=N_COPIES,
                     help="layer copies per step (default 32; smaller only for profiler captures)")
-    ap.add_argument("--leg", choices=["decode", "prefill", "tp"], default=None,
+    ap.add_argument("--leg", choices=["decode", "prefill", "tp", "gemv"], default=None,
                     help="run only this secondary leg and print its object (for profiler captures; "
                          "no headline line)")
     args = ap.parse_args()
@@ -503,7 +762,8 @@ def main():
     if args.leg is not None:
         leg = {"decode": lambda: decode_leg(pkg, synth, local, rank, world, args),
                "prefill": lambda: prefill_leg(pkg, synth, local, rank, world, args),
-               "tp": lambda: tp_decode_leg(pkg, local, rank, world, args)}[args.leg]()
+               "tp": lambda: tp_decode_leg(pkg, local, rank, world, args),
+               "gemv": lambda: gemv_leg(pkg, synth, local, rank, world, args)}[args.leg]()
         if rank == 0:
             print(json.dumps({"leg": args.leg, **leg}))
         if world > 1:
@@ -605,6 +865,8 @@ def main():
     ctx.close()
     model.close()
     del m
+    if not args.no_gemv:
+        out["gemv"] = gemv_leg(pkg, synth, local, rank, world, args)
     if not args.no_prefill:
         out["prefill"] = prefill_leg(pkg, synth, local, rank, world, args)
     if not args.no_tp:

@@ -94,7 +94,9 @@ SLLM_CUDA_API int sllm_cuda_i2s_quant_act(const float * x, size_t n, int8_t * q_
  * the GGUF (rows of n/4 bytes, I2_S interleaved layout). Unlike the reference,
  * which silently returns 0 for n < 128, this returns SLLM_CUDA_ERR_ARG for
  * n % 128 != 0 (the loader refuses such tensors anyway, src/forward.c:306-316).
- * n must be <= 65536.
+ * n above 8192 is refused with SLLM_CUDA_ERR_UNSUPPORTED (the 2B-4T model's
+ * widths are 2560 and 6912; the tensor-parallel path splits wider
+ * contractions into chunks of at most 8192).
  */
 SLLM_CUDA_API int sllm_cuda_i2s_gemv(const uint8_t * w, size_t n_rows, size_t n,
                        const int8_t * q, int32_t * rows_out, void * stream);
@@ -110,6 +112,26 @@ SLLM_CUDA_API int sllm_cuda_i2s_gemv(const uint8_t * w, size_t n_rows, size_t n,
 SLLM_CUDA_API int sllm_cuda_i2s_gemv_f32(const uint8_t * w, size_t n_rows, size_t n,
                            const float * x, float * y, int32_t * dots,
                            void * stream);
+
+/*
+ * A batch of `count` (<= 256) independent float GEMVs of one shape, each as
+ * sllm_cuda_i2s_gemv_f32 computes it, run as one persistent launch: GEMV i
+ * reads the packed tensor w[i] (device, 16-byte aligned, scale tail after the
+ * codes), input x + i * x_stride (x_stride 0: every GEMV shares x, as Q, K and
+ * V share one quantised activation in src/forward.c:651-666) and writes
+ * y + i * n_rows. It replaces a host loop of sllm_i2s_quant_act +
+ * sllm_i2s_gemv + epilogue over tensors (src/i2s_gemm.c:45-83, :260-290;
+ * bench/kernel_bench.c:62-130 times such loops). n_rows % 4 == 0. The first
+ * run with given x, x_stride and y builds the launch's tables (device
+ * allocation); later runs with the same buffers only launch. Results are
+ * bit-identical to sllm_cuda_i2s_gemv_f32 on each tensor.
+ */
+typedef struct sllm_cuda_gemv_batch sllm_cuda_gemv_batch;
+SLLM_CUDA_API int sllm_cuda_gemv_batch_new(const uint8_t * const * w, size_t count, size_t n_rows,
+                                           size_t n, int device, sllm_cuda_gemv_batch ** out);
+SLLM_CUDA_API int sllm_cuda_gemv_batch_run(sllm_cuda_gemv_batch * b, const float * x, size_t x_stride,
+                                           float * y, void * stream);
+SLLM_CUDA_API void sllm_cuda_gemv_batch_free(sllm_cuda_gemv_batch * b);
 
 /* ------------------------------------------------------------------ */
 /* multi-token (prefill) kernels: device pointers                      */
@@ -203,7 +225,7 @@ typedef struct sllm_cuda_ctx   sllm_cuda_ctx;
  * be shared by several contexts. Validates the same shape rules as
  * sllm_model_load (src/forward.c:368-444): returns SLLM_CUDA_ERR_ARG for a
  * NULL desc or tensor, SLLM_CUDA_ERR_UNSUPPORTED for widths this backend does
- * not run (n_embd or n_ff not a multiple of 128 or above 65536, a head dim
+ * not run (n_embd or n_ff not a multiple of 128 or above 8192, a head dim
  * n_embd / n_head other than 128, n_rot other than the head dim,
  * n_head % n_head_kv != 0), SLLM_CUDA_ERR_NOMEM when device memory runs out.
  * Pairs with sllm_model_load / sllm_model_free (include/saphira_llm/forward.h:32-33).

@@ -63,6 +63,19 @@ SLLM_CUDA_API int sllm_cuda_test_tp_generate_group(sllm_cuda_tp_ctx ** cs, int32
 SLLM_CUDA_API long long sllm_cuda_test_kernel_launches(void);
 
 /*
+ * Device time (ms) of the decode steps of the last forward / generate call on
+ * a context: two events recorded on the context's stream around the step
+ * launches, so the host round trips before and after are excluded. -1 when
+ * nothing has run yet.
+ */
+SLLM_CUDA_API float sllm_cuda_test_ctx_last_run_ms(const sllm_cuda_ctx * c);
+SLLM_CUDA_API float sllm_cuda_test_tp_ctx_last_run_ms(const sllm_cuda_tp_ctx * c);
+
+/* The device error word of a GEMV batch's launch: SLLM_CUDA_OK, or
+ * SLLM_CUDA_ERR_TIMEOUT when a bounded wait gave up; -1 before its first run. */
+SLLM_CUDA_API int sllm_cuda_test_gemv_batch_error(sllm_cuda_gemv_batch * b);
+
+/*
  * The persistent engine's split of each stage's rows over `grid` CTAs, the
  * host computation every engine program is built with (no device is used).
  * Op i has rows[i] rows of K[i] elements, epilogue epi[i] (0 dots, 1 f32,

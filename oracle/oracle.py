@@ -241,6 +241,7 @@ class Reference:
         L.refg_gemv_pooled.argtypes = [C.c_void_p, _u8p, C.c_size_t, C.c_size_t, _i8p, _i32p]
         L.refg_layer_chain.argtypes = [C.c_void_p, C.POINTER(abi.ModelDesc), C.c_int32, _f32p, _f32p,
                                        _i8p, _i32p]
+        L.refg_lm_head_pooled.argtypes = [C.c_void_p, _u16p, C.c_size_t, C.c_size_t, _f32p, _f32p]
         self.isa = L.refg_select_auto()
 
     def quant_act(self, x):
@@ -303,6 +304,9 @@ class RefPool:
 
     def layer_chain(self, desc, layer, x, scratch, qbuf, dots):
         self.ref.lib.refg_layer_chain(self.p, C.byref(desc), layer, x, scratch, qbuf, dots)
+
+    def lm_head(self, embd, n_rows, n_embd, x, out):
+        self.ref.lib.refg_lm_head_pooled(self.p, embd, n_rows, n_embd, x, out)
 
 
 class RefModel:

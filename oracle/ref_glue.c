@@ -168,3 +168,33 @@ void refg_layer_chain(void * pool, const sllm_cuda_model_desc * m, int32_t layer
     refg_project(pool, L->ffn_down, E, F, qbuf, &act, dots, proj);
     sllm_add(x, proj, fi, E);
 }
+
+/* ------------------------------------------------------------------ */
+/* the tied F16 head, pooled the way src/forward.c:215-233,818-827     */
+/* pools it: rows of sllm_dot_f16_f32 over the pool's workers          */
+/* ------------------------------------------------------------------ */
+
+typedef struct {
+    const uint16_t * embd;
+    const float * x;
+    size_t n_embd;
+    float * out;
+} refg_head_job;
+
+static void refg_head_rows(void * vctx, size_t begin, size_t end) {
+    const refg_head_job * j = (const refg_head_job *) vctx;
+    for (size_t v = begin; v < end; ++v) {
+        j->out[v] = sllm_dot_f16_f32(j->embd + v * j->n_embd, j->x, j->n_embd);
+    }
+}
+
+void refg_lm_head_pooled(void * pool, const uint16_t * embd, size_t n_rows, size_t n_embd,
+                         const float * x, float * out) {
+    sllm_pool * p = (sllm_pool *) pool;
+    const refg_head_job j = { embd, x, n_embd, out };
+    if (p == NULL || sllm_pool_threads(p) < 2) {
+        refg_head_rows((void *) &j, 0, n_rows);
+        return;
+    }
+    sllm_parallel_rows(p, refg_head_rows, (void *) &j, n_rows, 64);
+}

@@ -94,6 +94,14 @@ def lib():
     L.sllm_cuda_test_engine_split.argtypes = [vp, vp, vp, vp, i32, vp, i32, i32, vp]
     L.sllm_cuda_test_tp_plan.argtypes = [i32, i32, i32, i32, i32, i32, i32, i32, vp]
     L.sllm_cuda_test_projection_split.argtypes = [i32, i32, i32, i32]
+    L.sllm_cuda_gemv_batch_new.argtypes = [vp, sz, sz, sz, C.c_int, C.POINTER(vp)]
+    L.sllm_cuda_gemv_batch_run.argtypes = [vp, vp, sz, vp, vp]
+    L.sllm_cuda_gemv_batch_free.argtypes = [vp]
+    L.sllm_cuda_test_gemv_batch_error.argtypes = [vp]
+    L.sllm_cuda_test_ctx_last_run_ms.argtypes = [vp]
+    L.sllm_cuda_test_ctx_last_run_ms.restype = C.c_float
+    L.sllm_cuda_test_tp_ctx_last_run_ms.argtypes = [vp]
+    L.sllm_cuda_test_tp_ctx_last_run_ms.restype = C.c_float
     _lib = L
     return L
 
@@ -161,6 +169,28 @@ def gemm_silu(w_gate, w_up, n_rows, n, m, q, acts, h, stream=None):
     """h = silu(gate) * up for m tokens at once (device pointers)."""
     _check(lib().sllm_cuda_i2s_gemm_silu(_ptr(w_gate), _ptr(w_up), n_rows, n, m, _ptr(q), _ptr(acts), _ptr(h),
                                          _stream(stream)), "gemm_silu")
+
+
+class GemvBatch:
+    """`count` independent GEMVs of one shape as one persistent launch
+    (sllm_cuda_gemv_batch_*). `ws` are device tensors or addresses."""
+
+    def __init__(self, ws, n_rows, n, device=0):
+        arr = (C.c_void_p * len(ws))(*[_ptr(w) for w in ws])
+        self._keep = ws
+        self.h = C.c_void_p()
+        _check(lib().sllm_cuda_gemv_batch_new(arr, len(ws), n_rows, n, device, C.byref(self.h)), "gemv_batch_new")
+
+    def run(self, x, y, x_stride=0, stream=None):
+        _check(lib().sllm_cuda_gemv_batch_run(self.h, _ptr(x), x_stride, _ptr(y), _stream(stream)), "gemv_batch_run")
+
+    def error(self):
+        return lib().sllm_cuda_test_gemv_batch_error(self.h)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().sllm_cuda_gemv_batch_free(self.h)
+            self.h = None
 
 
 def gemm_error():
@@ -261,6 +291,10 @@ class Ctx:
         out = np.empty(self.n_vocab, np.float32)
         rc = lib().sllm_cuda_ctx_last_logits(self.h, out.ctypes.data)
         return None if rc != 0 else out
+
+    def last_run_ms(self):
+        """Device time of the decode steps of the last forward / generate call."""
+        return float(lib().sllm_cuda_test_ctx_last_run_ms(self.h))
 
     def layer_chain(self, layer_begin, n_layers, x):
         np = self._np
@@ -369,6 +403,10 @@ class TpCtx:
 
     def reset(self):
         _check(lib().sllm_cuda_tp_ctx_reset(self.h), "tp_ctx_reset")
+
+    def last_run_ms(self):
+        """Device time of the decode steps of the last generate call on this rank."""
+        return float(lib().sllm_cuda_test_tp_ctx_last_run_ms(self.h))
 
     def uses_engine(self):
         return bool(lib().sllm_cuda_test_tp_uses_engine(self.h))

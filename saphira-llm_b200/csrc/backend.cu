@@ -35,7 +35,27 @@ using namespace sllm;
 static thread_local std::string g_last_error;
 static int g_force_fallback = 0;
 static float g_engine_eps = 0.0f;          // set just before an engine program is captured
-static int* g_fallback_counter = nullptr;   // device int, lazily allocated per process
+// Device words shared by every call in the process: one per device, since a
+// kernel must never write another device's memory.
+static std::mutex g_words_mu;
+static std::vector<int*> g_fallback_counters;   // how often a certified sum fell back
+static std::vector<int*> g_gemm_errors;         // why a GEMM's bounded wait gave up
+static int* device_word(std::vector<int*>& words) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lk(g_words_mu);
+    if ((int)words.size() <= dev) words.resize(dev + 1, nullptr);
+    if (words[dev] == nullptr) {
+        int* w = nullptr;
+        if (cudaMalloc(&w, sizeof(int)) != cudaSuccess) return nullptr;
+        if (cudaMemset(w, 0, sizeof(int)) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+            cudaFree(w);
+            return nullptr;
+        }
+        words[dev] = w;
+    }
+    return words[dev];
+}
 
 // Kernels this library has put on a stream, for the benchmark's launch count:
 // a graph adds its kernel nodes each time it is launched, a direct launch
@@ -167,14 +187,7 @@ extern "C" long long sllm_cuda_test_kernel_launches(void) { return g_kernel_laun
 void sllm::count_launches(long long n) { g_kernel_launches += n; }
 int sllm::force_fallback_flag() { return g_force_fallback; }
 
-int* sllm::fallback_counter() {
-    if (g_fallback_counter == nullptr) {
-        if (cudaMalloc(&g_fallback_counter, sizeof(int)) != cudaSuccess) { g_fallback_counter = nullptr; return nullptr; }
-        if (cudaMemset(g_fallback_counter, 0, sizeof(int)) != cudaSuccess) return nullptr;
-        if (cudaDeviceSynchronize() != cudaSuccess) return nullptr;
-    }
-    return g_fallback_counter;
-}
+int* sllm::fallback_counter() { return device_word(g_fallback_counters); }
 
 extern "C" void sllm_cuda_test_set_force_fallback(int on) { g_force_fallback = on; }
 
@@ -214,10 +227,20 @@ extern "C" int sllm_cuda_i2s_gemv(const uint8_t* w, size_t n_rows, size_t n, con
     if (q == nullptr || !aligned16(q)) return fail(SLLM_CUDA_ERR_ARG, "gemv: q must be 16-byte aligned");
     if (!aligned16(w)) return fail(SLLM_CUDA_ERR_ARG, "gemv: w must be 16-byte aligned");
     // The raw API has no act: an all-zero act makes the prologue a plain copy.
-    static sllm_cuda_act* zero_act = nullptr;
-    if (zero_act == nullptr) {
-        CK(cudaMalloc(&zero_act, sizeof(sllm_cuda_act)), "cudaMalloc");
-        CK(cudaMemset(zero_act, 0, sizeof(sllm_cuda_act)), "cudaMemset");
+    // One per device (a kernel must not read another device's memory).
+    static std::mutex zero_mu;
+    static std::vector<sllm_cuda_act*> zero_acts;
+    sllm_cuda_act* zero_act = nullptr;
+    {
+        int dev = 0;
+        CK(cudaGetDevice(&dev), "cudaGetDevice");
+        std::lock_guard<std::mutex> lk(zero_mu);
+        if ((int)zero_acts.size() <= dev) zero_acts.resize(dev + 1, nullptr);
+        if (zero_acts[dev] == nullptr) {
+            CK(cudaMalloc(&zero_acts[dev], sizeof(sllm_cuda_act)), "cudaMalloc");
+            CK(cudaMemset(zero_acts[dev], 0, sizeof(sllm_cuda_act)), "cudaMemset");
+        }
+        zero_act = zero_acts[dev];
     }
     GemvParams p{};
     p.K = (int)n;
@@ -248,15 +271,7 @@ extern "C" int sllm_cuda_i2s_gemv_f32(const uint8_t* w, size_t n_rows, size_t n,
 // ---------------------------------------------------------------------------
 // multi-token (prefill) kernels
 // ---------------------------------------------------------------------------
-static int* g_gemm_error = nullptr;     // device int: why a GEMM's bounded wait gave up
-
-static int* gemm_error_word() {
-    if (g_gemm_error == nullptr) {
-        if (cudaMalloc(&g_gemm_error, sizeof(int)) != cudaSuccess) { g_gemm_error = nullptr; return nullptr; }
-        if (cudaMemset(g_gemm_error, 0, sizeof(int)) != cudaSuccess) return nullptr;
-    }
-    return g_gemm_error;
-}
+static int* gemm_error_word() { return device_word(g_gemm_errors); }
 
 extern "C" int sllm_cuda_test_gemm_error(void) {
     int* p = gemm_error_word();
@@ -662,6 +677,9 @@ struct sllm_cuda_ctx {
     EngineProgram eng_piece[kProjPieces];
     cudaEvent_t piece_done[kProjPieces] = {};
     cudaStream_t copy_stream = nullptr;
+    // recorded on `stream` around the step launches of the last forward or
+    // generate call (device time of the decode steps alone)
+    cudaEvent_t run_ev[2] = {};
 };
 
 // the reference's angle recurrence (src/ops.c:529-549), on the host libm
@@ -705,6 +723,8 @@ extern "C" void sllm_cuda_ctx_free(sllm_cuda_ctx* c) {
         if (c->piece_done[i]) cudaEventDestroy(c->piece_done[i]);
     }
     if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
+    for (cudaEvent_t ev : c->run_ev)
+        if (ev) cudaEventDestroy(ev);
     delete c;
 }
 
@@ -734,6 +754,8 @@ extern "C" int sllm_cuda_ctx_new(const sllm_cuda_model* m, int32_t n_ctx, sllm_c
     A((void**)&c->pos, 4); A((void**)&c->tok_seq, (size_t)n_ctx * 4 + 4); A((void**)&c->prompt_end, 4);
     A((void**)&c->argmax_hist, (size_t)n_ctx * 4);
     if (e == cudaSuccess) e = cudaMallocHost(&c->pinned, 64);
+    if (e == cudaSuccess) e = cudaEventCreate(&c->run_ev[0]);
+    if (e == cudaSuccess) e = cudaEventCreate(&c->run_ev[1]);
     if (e == cudaSuccess) e = cudaMemset(c->k_cache, 0, kv * 4);
     if (e == cudaSuccess) e = cudaMemset(c->v_cache, 0, kv * 4);
     if (e == cudaSuccess) e = cudaMemset(c->counter, 0, 4);
@@ -886,13 +908,25 @@ static int run_steps(sllm_cuda_ctx* c, int base, int n, int prompt_end, float* c
     CK(cudaMemcpyAsync(c->pos, &c->pinned[0], 4, cudaMemcpyHostToDevice, c->stream), "set pos");
     CK(cudaMemcpyAsync(c->prompt_end, &c->pinned[1], 4, cudaMemcpyHostToDevice, c->stream), "set prompt end");
     const size_t V = c->m->n_vocab;
+    CK(cudaEventRecord(c->run_ev[0], c->stream), "run timer");
     for (int t = 0; t < n; ++t) {
         CK(graph_launch(c->step, c->stream), "decode step");
         if (chunk_logits_dev != nullptr)
             CK(cudaMemcpyAsync(chunk_logits_dev + (size_t)t * V, c->logits, V * 4, cudaMemcpyDeviceToDevice, c->stream),
                "copy logits");
     }
+    CK(cudaEventRecord(c->run_ev[1], c->stream), "run timer");
     return SLLM_CUDA_OK;
+}
+
+extern "C" float sllm_cuda_test_ctx_last_run_ms(const sllm_cuda_ctx* c) {
+    float ms = -1.0f;
+    if (c == nullptr || cudaSetDevice(c->m->device) != cudaSuccess) return -1.0f;
+    if (cudaEventElapsedTime(&ms, c->run_ev[0], c->run_ev[1]) != cudaSuccess) {
+        cudaGetLastError();
+        return -1.0f;
+    }
+    return ms;
 }
 
 extern "C" int sllm_cuda_forward_chunk(const sllm_cuda_model* m, sllm_cuda_ctx* c, const int32_t* tokens, int32_t n,
@@ -1380,6 +1414,97 @@ extern "C" int sllm_cuda_layer_projections(const sllm_cuda_model* m, sllm_cuda_c
     }
     CK(cudaStreamSynchronize(c->stream), "projections sync");
     return engine_error(c->eng_proj);
+}
+
+// ---------------------------------------------------------------------------
+// A batch of independent GEMVs of one shape as one persistent engine launch.
+// ---------------------------------------------------------------------------
+struct sllm_cuda_gemv_batch {
+    int device = 0;
+    int rows = 0, K = 0, count = 0, wa = 0, wb = 0;
+    std::vector<const uint8_t*> w;
+    std::vector<float> ws;
+    EngineProgram prog;
+    size_t key_stride = 0;
+};
+
+extern "C" int sllm_cuda_gemv_batch_new(const uint8_t* const* w, size_t count, size_t n_rows, size_t n, int device,
+                                        sllm_cuda_gemv_batch** out) {
+    if (out == nullptr) return fail(SLLM_CUDA_ERR_ARG, "gemv_batch_new: NULL out");
+    *out = nullptr;
+    if (w == nullptr || count == 0 || count > 256) return fail(SLLM_CUDA_ERR_ARG, "gemv_batch_new: count %zu outside [1, 256]", count);
+    int rc = check_gemv_shape(w[0], n_rows, n, w[0]);
+    if (rc != SLLM_CUDA_OK) return rc;
+    for (size_t i = 0; i < count; ++i)
+        if (w[i] == nullptr || !aligned16(w[i])) return fail(SLLM_CUDA_ERR_ARG, "gemv_batch_new: tensor %zu NULL or unaligned", i);
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+        cudaGetLastError();
+        return fail(SLLM_CUDA_ERR_UNSUPPORTED, "gemv_batch_new: no device %d", device);
+    }
+    CK(cudaSetDevice(device), "cudaSetDevice");
+    auto* b = new sllm_cuda_gemv_batch();
+    b->device = device;
+    b->rows = (int)n_rows;
+    b->K = (int)n;
+    b->count = (int)count;
+    if (!engine_pair_for_width(engine_wpl(b->K), &b->wa, &b->wb)) {
+        delete b;
+        return fail(SLLM_CUDA_ERR_UNSUPPORTED, "gemv_batch_new: no engine instance for width %zu", n);
+    }
+    b->w.assign(w, w + count);
+    b->ws.resize(count);
+    for (size_t i = 0; i < count; ++i) {
+        // the per-tensor scale after the packed codes (src/quant.c:102-106)
+        const cudaError_t e = cudaMemcpy(&b->ws[i], w[i] + n_rows * (n / 4), 4, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) { delete b; return cuda_fail(e, "gemv_batch_new: read scale"); }
+    }
+    *out = b;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" void sllm_cuda_gemv_batch_free(sllm_cuda_gemv_batch* b) {
+    if (b == nullptr) return;
+    cudaSetDevice(b->device);
+    engine_program_free(b->prog);
+    delete b;
+}
+
+extern "C" int sllm_cuda_gemv_batch_run(sllm_cuda_gemv_batch* b, const float* x, size_t x_stride, float* y,
+                                        void* stream) {
+    if (b == nullptr || x == nullptr || y == nullptr || !aligned16(x) || !aligned16(y) ||
+        (x_stride != 0 && (x_stride < (size_t)b->K || x_stride % 4 != 0)) || b->rows % 4 != 0)
+        return fail(SLLM_CUDA_ERR_ARG, "gemv_batch_run: bad arguments");
+    CK(cudaSetDevice(b->device), "cudaSetDevice");
+    EngineProgram& p = b->prog;
+    if (!p.built || p.key_x != x || p.key_y != y || b->key_stride != x_stride) {
+        int* fb = fallback_counter();
+        if (fb == nullptr) return fail(SLLM_CUDA_ERR_NOMEM, "gemv_batch_run: diagnostics counter");
+        std::vector<EngGroup> groups;
+        std::vector<EngOp> ops;
+        for (int i = 0; i < b->count; ++i) {
+            if (i == 0 || x_stride != 0)
+                groups.push_back(EngGroup{x + (size_t)i * x_stride, nullptr, b->K, PRO_QUANT});
+            EngOp o{};
+            o.w = b->w[i]; o.y = y + (size_t)i * b->rows; o.rows = b->rows; o.K = b->K; o.epi = EPI_F32;
+            o.ws = b->ws[i]; o.group = (int)groups.size() - 1;
+            o.chunk_rows = engine_chunk_rows(b->K, EPI_F32);
+            ops.push_back(o);
+        }
+        std::vector<int> stage_first{0, (int)ops.size()};
+        g_engine_eps = 0.0f;            // PRO_QUANT: no norm
+        const int rc = engine_program_build(p, groups, ops, stage_first, b->device, nullptr, fb, b->wa, b->wb);
+        if (rc != SLLM_CUDA_OK) return rc;
+        p.key_x = x; p.key_y = y; b->key_stride = x_stride;
+    }
+    CK(engine_program_launch(p, (cudaStream_t)stream), "gemv_batch launch");
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_test_gemv_batch_error(sllm_cuda_gemv_batch* b) {
+    if (b == nullptr || !b->prog.built) return -1;
+    if (cudaSetDevice(b->device) != cudaSuccess) return -1;
+    return engine_error(b->prog);
 }
 
 // ---------------------------------------------------------------------------

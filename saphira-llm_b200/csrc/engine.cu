@@ -719,6 +719,13 @@ bool engine_supports(int wa, int wb) {
     return false;
 }
 
+bool engine_pair_for_width(int wpl, int* wa, int* wb) {
+#define SLLM_ENG_FIND(A, B) if (wpl == A) { *wa = A; *wb = B; return true; }
+    SLLM_ENGINE_SHAPES(SLLM_ENG_FIND)
+#undef SLLM_ENG_FIND
+    return false;
+}
+
 cudaError_t prepare_engine() {
     // the largest dynamic shared memory any program may ask for; the static
     // part must fit the reserve

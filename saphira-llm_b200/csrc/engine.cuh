@@ -90,6 +90,8 @@ int engine_grid(int device);
 // wpl(K) = 32-bit words per lane = ceil(K / 512)
 int engine_wpl(int K);
 bool engine_supports(int wa, int wb);
+// a compiled pair whose first width is `wpl` (for programs of one width)
+bool engine_pair_for_width(int wpl, int* wa, int* wb);
 cudaError_t prepare_engine();     // once, outside any stream capture
 cudaError_t launch_engine(const EngParams& p, int grid, cudaStream_t st, int wa, int wb);
 

@@ -586,6 +586,8 @@ struct sllm_cuda_tp_ctx {
     size_t off_flags = 0, off_attn = 0, off_h = 0, off_dots_o = 0, off_dots_d = 0, off_trip = 0;
     uint32_t* epoch = nullptr;
     int* x_error = nullptr;
+    // recorded on `stream` around the step launches of the last generate call
+    cudaEvent_t run_ev[2] = {};
 };
 
 namespace {
@@ -1498,6 +1500,8 @@ extern "C" int sllm_cuda_tp_ctx_new(const sllm_cuda_tp_model* m, sllm_cuda_tp_co
     if (!e) e = ctx_alloc(c, &c->tok_seq, (size_t)n_ctx);
     if (!e) e = ctx_alloc(c, &c->hist, (size_t)n_ctx);
     if (!e) e = cudaMallocHost(&c->pinned, 16);
+    if (!e) e = cudaEventCreate(&c->run_ev[0]);
+    if (!e) e = cudaEventCreate(&c->run_ev[1]);
     if (!e) e = cudaMemset(c->counter, 0, 4);
     if (!e) e = cudaMemset(c->tok_seq, 0, (size_t)n_ctx * 4);
     if (!e) {
@@ -1530,6 +1534,8 @@ extern "C" void sllm_cuda_tp_ctx_free(sllm_cuda_tp_ctx* c) {
     if (c->region != nullptr) cudaFree(c->region);
     for (void* p : c->allocs) cudaFree(p);
     if (c->pinned) cudaFreeHost(c->pinned);
+    for (cudaEvent_t ev : c->run_ev)
+        if (ev) cudaEventDestroy(ev);
     delete c;
 }
 
@@ -1547,7 +1553,9 @@ extern "C" int sllm_cuda_tp_generate_greedy(sllm_cuda_tp_ctx* c, const int32_t* 
     rc = tp_seed(c, prompt, n_prompt);
     if (rc != SLLM_CUDA_OK) return rc;
     const int steps = n_prompt + n_new;
+    CK(cudaEventRecord(c->run_ev[0], c->stream), "run timer");
     for (int s = 0; s < steps; ++s) CK(graph_launch(c->step, c->stream), "tp step");
+    CK(cudaEventRecord(c->run_ev[1], c->stream), "run timer");
     if (n_new > 0)
         CK(cudaMemcpyAsync(out, c->tok_seq + base + n_prompt, (size_t)n_new * 4, cudaMemcpyDeviceToHost, c->stream), "ids");
     rc = tp_sync(c, 120.0);
@@ -1565,6 +1573,16 @@ extern "C" int sllm_cuda_tp_generate_greedy(sllm_cuda_tp_ctx* c, const int32_t* 
     c->n_past = base + steps;
     c->have_logits = steps > 0;
     return SLLM_CUDA_OK;
+}
+
+extern "C" float sllm_cuda_test_tp_ctx_last_run_ms(const sllm_cuda_tp_ctx* c) {
+    float ms = -1.0f;
+    if (c == nullptr || cudaSetDevice(c->m->device) != cudaSuccess) return -1.0f;
+    if (cudaEventElapsedTime(&ms, c->run_ev[0], c->run_ev[1]) != cudaSuccess) {
+        cudaGetLastError();
+        return -1.0f;
+    }
+    return ms;
 }
 
 extern "C" int sllm_cuda_tp_ctx_reset(sllm_cuda_tp_ctx* c) {

@@ -30,6 +30,28 @@ def sha(a) -> str:
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
 
 
+def probe_sha(image) -> str:
+    """SHA-256 of the first and last 16 MiB of a model image: enough to show
+    that a seeded generator still produces the bytes a fixture was made from,
+    without hashing a 1.2 GB image on every run."""
+    a = np.ascontiguousarray(image).view(np.uint8)
+    k = 16 << 20
+    return hashlib.sha256(a[:k].tobytes() + a[-k:].tobytes()).hexdigest()
+
+
+def load_large_decode_cases():
+    with open(os.path.join(GOLDEN, "decode_large.json")) as f:
+        return {c["name"]: c for c in json.load(f)}
+
+
+def large_decode_model(synth, case):
+    cfg = synth.Config(**case["config"])
+    m = synth.SynthModel(cfg, seed=case["seed"])
+    assert m.image.nbytes == case["image_bytes"], f"{case['name']}: model size drifted"
+    assert probe_sha(m.image) == case["image_probe_sha256"], f"{case['name']}: model generator drifted"
+    return m
+
+
 def gemv_inputs(synth, case):
     rng = np.random.default_rng(case["seed"])
     w = synth.random_i2s(rng, case["rows"], case["n"])

@@ -3,7 +3,8 @@
 Run in a tree where the reference sources exist (oracle/Makefile builds
 oracle/_ref/libsllm_ref.so from them):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py            # gemv_cases.json, decode_cases.json
+    python tests/golden/make_golden.py --large    # decode_large.json (a few minutes)
 
 Every output here comes from the REFERENCE's own functions
 (sllm_i2s_quant_act, sllm_i2s_gemv, sllm_i2s_epilogue, sllm_generate_greedy
@@ -53,8 +54,46 @@ def decode_case(ref, name, cfg_kw, seed, n_prompt, n_new, n_ctx):
                 last_logits_fnv=fixtures.fnv1a64(last.view(np.uint32).tobytes()))
 
 
+def large_decode_case(ref, name, cfg_kw, seed, prompt_seed, n_prompt, n_new, n_ctx, threads):
+    """A decode at a BASELINE configuration's full geometry. The model image is
+    too large to hash whole on every test run, so its first and last 16 MiB
+    are hashed instead (any drift of the seeded generator changes both)."""
+    cfg = synth.Config(**cfg_kw)
+    m = synth.SynthModel(cfg, seed=seed)
+    prompt = np.random.default_rng(prompt_seed).integers(0, cfg.n_vocab, n_prompt).astype(np.int32)
+    rm = ref.model(m.image, n_ctx, threads)
+    rc, toks = rm.generate(prompt, n_new)
+    assert rc == 0
+    last = rm.last_logits(cfg.n_vocab)
+    return dict(name=name, config=cfg_kw, seed=seed, prompt_seed=prompt_seed, n_ctx=n_ctx,
+                prompt=prompt.tolist(), n_new=n_new, image_bytes=int(m.image.nbytes),
+                image_probe_sha256=fixtures.probe_sha(m.image), tokens=toks.tolist(),
+                last_logits_fnv=fixtures.fnv1a64(last.view(np.uint32).tobytes()))
+
+
+def make_large(ref):
+    """decode_large.json: configs[2] exactly as stated (the 2B-4T geometry with
+    30 layers, 64-token prompt, 256 greedy tokens, 320 positions; the model
+    and prompt seeds bench.py's decode leg uses), and configs[4]'s geometry
+    (n_embd 8192, n_ff 28672, 64 query / 8 kv heads) with 2 layers and a small
+    vocabulary, which the reference's loader accepts (80 layers it refuses)."""
+    threads = os.cpu_count() or 1
+    cases = [
+        large_decode_case(ref, "configs2-2b4t-30l-64+256", {}, 4242, 7, 64, 256, 320, threads),
+        large_decode_case(ref, "configs4-geometry-2l",
+                          dict(n_layer=2, n_embd=8192, n_ff=28672, n_head=64, n_head_kv=8, n_vocab=4099),
+                          4343, 8, 24, 24, 64, threads),
+    ]
+    with open(os.path.join(HERE, "decode_large.json"), "w") as f:
+        json.dump(cases, f, indent=1)
+    print("wrote", len(cases), "large decode cases")
+
+
 def main():
     oracle.build(ref=True)
+    if "--large" in sys.argv:
+        make_large(oracle.Reference())
+        return
     ref = oracle.Reference()
     gemv = [
         gemv_case(ref, "q-rows-2560", 40, 2560, 101),

@@ -124,3 +124,48 @@ def test_argument_errors(cuda):
     with pytest.raises(cuda.SllmCudaError) as e:
         cuda.gemv(w, 16, 256, q[1:], out)              # misaligned activation
     assert e.value.status == -1
+
+
+@pytest.mark.parametrize("shared_x", [True, False])
+def test_gemv_batch_matches_single_gemvs(cuda, orc, synth, shared_x):
+    """configs[0]'s shape as a batch of independent GEMVs in one persistent
+    launch: every output equals the single-GEMV entry point's and the oracle's,
+    bit for bit, on two runs (the second reuses the launch tables)."""
+    import torch
+    rows, n, count = 6912, 2560, 5
+    rng = np.random.default_rng(4040 + shared_x)
+    ws = [synth.random_i2s(rng, rows, n) for _ in range(count)]
+    wd = [_dev(w) for w in ws]
+    xs = rng.standard_normal((count, n)).astype(np.float32)
+    xs[2] *= 40.0
+    xd = _dev(xs)
+    b = cuda.GemvBatch(wd, rows, n)
+    y = torch.empty((count, rows), dtype=torch.float32, device="cuda")
+    for _ in range(2):
+        y.zero_()
+        b.run(xd, y, 0 if shared_x else n)
+        torch.cuda.synchronize()
+        assert b.error() == 0
+        got = y.cpu().numpy()
+        for i in range(count):
+            x = xs[0] if shared_x else xs[i]
+            one = torch.empty(rows, dtype=torch.float32, device="cuda")
+            cuda.gemv_f32(wd[i], rows, n, _dev(x), one)
+            torch.cuda.synchronize()
+            want, _ = orc.gemv_f32(ws[i], rows, n, x)
+            assert np.array_equal(bits(got[i]), bits(one.cpu().numpy())), i
+            assert np.array_equal(bits(got[i]), bits(want)), i
+    b.close()
+
+
+def test_gemv_batch_argument_errors(cuda, synth):
+    import ctypes as C
+    L = cuda.lib()
+    w = _dev(synth.random_i2s(np.random.default_rng(1), 64, 256))
+    h = C.c_void_p()
+    arr = (C.c_void_p * 1)(w.data_ptr())
+    assert L.sllm_cuda_gemv_batch_new(arr, 0, 64, 256, 0, C.byref(h)) == -1
+    assert L.sllm_cuda_gemv_batch_new(arr, 1, 64, 200, 0, C.byref(h)) == -1
+    assert L.sllm_cuda_gemv_batch_new(arr, 1, 64, 256, 0, C.byref(h)) == 0
+    assert L.sllm_cuda_gemv_batch_run(h, None, 0, None, None) == -1
+    L.sllm_cuda_gemv_batch_free(h)
