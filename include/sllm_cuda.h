@@ -13,7 +13,8 @@
  * Conventions, held by every function below:
  *   - Status codes are numerically identical to saphira-llm's sllm_status
  *     (include/saphira_llm/status.h:26-56), so a caller can return them
- *     unchanged. Three new negative codes name device-side failures.
+ *     unchanged. Three new negative codes (-60, -61, -62) name device-side
+ *     failures.
  *   - The kernel-level functions take DEVICE pointers and are asynchronous on
  *     the given stream. The model-level functions take HOST pointers and
  *     return when their results are on the host.
@@ -46,6 +47,9 @@ extern "C" {
 #define SLLM_CUDA_ERR_NOMEM       (-2)  /* SLLM_ERR_NOMEM: host or device allocation failed */
 #define SLLM_CUDA_ERR_IO          (-3)  /* SLLM_ERR_IO              */
 #define SLLM_CUDA_ERR_UNSUPPORTED (-4)  /* SLLM_ERR_UNSUPPORTED: no sm_100 device, or a shape this backend does not run */
+#define SLLM_CUDA_ERR_TRUNCATED   (-12) /* SLLM_ERR_GGUF_TRUNCATED: a state file ends early */
+#define SLLM_CUDA_ERR_KV_TYPE     (-32) /* SLLM_ERR_KV_TYPE: not a state file, or another version */
+#define SLLM_CUDA_ERR_TENSOR_SHAPE (-34) /* SLLM_ERR_TENSOR_SHAPE: a state file of another geometry */
 #define SLLM_CUDA_ERR_TOO_LARGE   (-36) /* SLLM_ERR_TOO_LARGE       */
 #define SLLM_CUDA_ERR_DEVICE      (-60) /* a CUDA runtime call or kernel launch failed */
 #define SLLM_CUDA_ERR_TIMEOUT     (-61) /* a bounded device-side wait ran out; the context stays usable */
@@ -347,6 +351,34 @@ SLLM_CUDA_API int sllm_cuda_layer_projections_device(const sllm_cuda_model * m, 
 SLLM_CUDA_API int sllm_cuda_layer_chain_device_noalloc(const sllm_cuda_model * m,
                                                        int32_t layer_begin, int32_t n_layers,
                                                        float * x, void * stream);
+
+/*
+ * The KV cache of a context in the reference's host layout: k_out / v_out are
+ * n_layer * n_head_kv * n_ctx * 128 floats each, [layer][kv head][pos][dim]
+ * (src/forward.c:81-83, the layout sllm_ctx_new allocates at
+ * src/forward.c:480-487). Export writes the rows of positions below n_past
+ * and leaves the others untouched. Import replaces the device cache with the
+ * given rows below n_past, clears every row at or above it, and sets n_past
+ * and the last position's logits (n_vocab floats; NULL only when n_past is
+ * 0), so that a generation without a prompt continues from them, as after
+ * sllm_state_load (src/forward.c:1034-1123).
+ */
+SLLM_CUDA_API int sllm_cuda_ctx_kv_export(const sllm_cuda_ctx * c, float * k_out, float * v_out);
+SLLM_CUDA_API int sllm_cuda_ctx_kv_import(sllm_cuda_ctx * c, const float * k_in, const float * v_in,
+                                          int32_t n_past, const float * last_logits);
+
+/*
+ * Save / restore a context's state in the reference's own file format, SLKV
+ * version 1 (src/forward.c:963-1123): files written here load into a CPU
+ * context of the same model and back, and continue identically. Replaces
+ * sllm_state_save / sllm_state_load (include/saphira_llm/forward.h:155-156),
+ * with the same refusals: SLLM_CUDA_ERR_KV_TYPE for a file that is not SLKV
+ * v1, SLLM_CUDA_ERR_TENSOR_SHAPE for another model or context depth,
+ * SLLM_CUDA_ERR_TRUNCATED for a short file, SLLM_CUDA_ERR_IO when the file
+ * cannot be opened or written.
+ */
+SLLM_CUDA_API int sllm_cuda_state_save(const sllm_cuda_model * m, const sllm_cuda_ctx * c, const char * path);
+SLLM_CUDA_API int sllm_cuda_state_load(const sllm_cuda_model * m, sllm_cuda_ctx * c, const char * path);
 
 /* Bytes of weights one decode step streams: every I2_S tensor with its scale
  * tail, every norm, and the F16 embedding / output head. */

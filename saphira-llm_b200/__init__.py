@@ -94,6 +94,10 @@ def lib():
     L.sllm_cuda_test_engine_split.argtypes = [vp, vp, vp, vp, i32, vp, i32, i32, vp]
     L.sllm_cuda_test_tp_plan.argtypes = [i32, i32, i32, i32, i32, i32, i32, i32, vp]
     L.sllm_cuda_test_projection_split.argtypes = [i32, i32, i32, i32]
+    L.sllm_cuda_state_save.argtypes = [vp, vp, C.c_char_p]
+    L.sllm_cuda_state_load.argtypes = [vp, vp, C.c_char_p]
+    L.sllm_cuda_ctx_kv_export.argtypes = [vp, vp, vp]
+    L.sllm_cuda_ctx_kv_import.argtypes = [vp, vp, vp, i32, vp]
     L.sllm_cuda_gemv_batch_new.argtypes = [vp, sz, sz, sz, C.c_int, C.POINTER(vp)]
     L.sllm_cuda_gemv_batch_run.argtypes = [vp, vp, sz, vp, vp]
     L.sllm_cuda_gemv_batch_free.argtypes = [vp]
@@ -291,6 +295,13 @@ class Ctx:
         out = np.empty(self.n_vocab, np.float32)
         rc = lib().sllm_cuda_ctx_last_logits(self.h, out.ctypes.data)
         return None if rc != 0 else out
+
+    def state_save(self, path):
+        """sllm_cuda_state_save: the reference's SLKV v1 file."""
+        return lib().sllm_cuda_state_save(self.model.h, self.h, os.fsencode(path))
+
+    def state_load(self, path):
+        return lib().sllm_cuda_state_load(self.model.h, self.h, os.fsencode(path))
 
     def last_run_ms(self):
         """Device time of the decode steps of the last forward / generate call."""

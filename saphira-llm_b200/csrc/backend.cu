@@ -89,6 +89,9 @@ extern "C" const char* sllm_cuda_status_string(int st) {
         case SLLM_CUDA_ERR_NOMEM: return "out of memory";
         case SLLM_CUDA_ERR_IO: return "i/o error";
         case SLLM_CUDA_ERR_UNSUPPORTED: return "unsupported";
+        case SLLM_CUDA_ERR_TRUNCATED: return "truncated";
+        case SLLM_CUDA_ERR_KV_TYPE: return "wrong file type or version";
+        case SLLM_CUDA_ERR_TENSOR_SHAPE: return "geometry mismatch";
         case SLLM_CUDA_ERR_TOO_LARGE: return "too large";
         case SLLM_CUDA_ERR_DEVICE: return "CUDA device error";
         case SLLM_CUDA_ERR_TIMEOUT: return "device wait timed out";
@@ -248,7 +251,9 @@ extern "C" int sllm_cuda_i2s_gemv(const uint8_t* w, size_t n_rows, size_t n, con
     p.seg[0] = GemvSeg{w, (int)n_rows, nullptr, rows_out};
     p.q_in = q;
     p.act_in = zero_act;
-    CK(launch_gemv(p, PRO_Q8, EPI_DOTS, current_sms(), (cudaStream_t)stream), "gemv launch");
+    // a dependent launch: it may start while the kernel before it finishes,
+    // streams weights at once and waits for that kernel before it reads q
+    CK(launch_gemv(p, PRO_Q8, EPI_DOTS, current_sms(), (cudaStream_t)stream, GEMV_DEPENDENT), "gemv launch");
     ++g_kernel_launches;
     return SLLM_CUDA_OK;
 }
@@ -263,7 +268,7 @@ extern "C" int sllm_cuda_i2s_gemv_f32(const uint8_t* w, size_t n_rows, size_t n,
     p.nseg = 1;
     p.seg[0] = GemvSeg{w, (int)n_rows, y, dots};
     p.x = x;
-    CK(launch_gemv(p, PRO_QUANT, EPI_F32, current_sms(), (cudaStream_t)stream), "gemv_f32 launch");
+    CK(launch_gemv(p, PRO_QUANT, EPI_F32, current_sms(), (cudaStream_t)stream, GEMV_DEPENDENT), "gemv_f32 launch");
     ++g_kernel_launches;
     return SLLM_CUDA_OK;
 }
@@ -1003,6 +1008,147 @@ extern "C" int sllm_cuda_ctx_last_logits(const sllm_cuda_ctx* c, float* host_out
     CK(cudaSetDevice(c->m->device), "cudaSetDevice");
     CK(cudaMemcpy(host_out, c->logits, (size_t)c->m->n_vocab * 4, cudaMemcpyDeviceToHost), "last logits");
     return SLLM_CUDA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// the KV cache in the reference's layout, and state files (src/forward.c:963-1123)
+// ---------------------------------------------------------------------------
+// The device keeps K transposed ([layer][kvh][dim][n_ctx]) and V as
+// [layer][kvh][n_ctx][dim]; the reference keeps both as [layer][kvh][pos][dim]
+// (src/forward.c:81-83). These copy the live prefix between the two.
+extern "C" int sllm_cuda_ctx_kv_export(const sllm_cuda_ctx* c, float* k_out, float* v_out) {
+    if (c == nullptr || k_out == nullptr || v_out == nullptr) return fail(SLLM_CUDA_ERR_ARG, "kv_export: NULL argument");
+    CK(cudaSetDevice(c->m->device), "cudaSetDevice");
+    CK(cudaStreamSynchronize(c->stream), "kv_export sync");
+    const sllm_cuda_model* m = c->m;
+    const size_t D = m->head_dim, N = c->n_ctx, P = c->n_past;
+    const size_t heads = (size_t)m->n_layer * (size_t)m->n_head_kv;
+    if (P == 0) return SLLM_CUDA_OK;
+    std::vector<float> kt(D * P);
+    for (size_t lh = 0; lh < heads; ++lh) {
+        const float* kd = c->k_cache + lh * D * N;        // [dim][n_ctx]
+        const float* vd = c->v_cache + lh * N * D;        // [n_ctx][dim]
+        CK(cudaMemcpy2D(kt.data(), P * 4, kd, N * 4, P * 4, D, cudaMemcpyDeviceToHost), "kv_export K");
+        CK(cudaMemcpy(v_out + lh * N * D, vd, P * D * 4, cudaMemcpyDeviceToHost), "kv_export V");
+        float* kh = k_out + lh * N * D;                    // [pos][dim]
+        for (size_t pos = 0; pos < P; ++pos)
+            for (size_t d = 0; d < D; ++d) kh[pos * D + d] = kt[d * P + pos];
+    }
+    return SLLM_CUDA_OK;
+}
+
+// the reference's sllm_argmax (src/forward.c:876-883): the first maximum by '>'
+static int32_t host_argmax(const float* v, int32_t n) {
+    int32_t best = 0;
+    float bv = v[0];
+    for (int32_t i = 1; i < n; ++i)
+        if (v[i] > bv) { bv = v[i]; best = i; }
+    return best;
+}
+
+extern "C" int sllm_cuda_ctx_kv_import(sllm_cuda_ctx* c, const float* k_in, const float* v_in, int32_t n_past,
+                                       const float* last_logits) {
+    if (c == nullptr || (n_past > 0 && (k_in == nullptr || v_in == nullptr || last_logits == nullptr)))
+        return fail(SLLM_CUDA_ERR_ARG, "kv_import: NULL argument");
+    if (n_past < 0 || n_past > c->n_ctx)
+        return fail(SLLM_CUDA_ERR_ARG, "kv_import: n_past %d outside [0, n_ctx=%d]", n_past, c->n_ctx);
+    CK(cudaSetDevice(c->m->device), "cudaSetDevice");
+    CK(cudaStreamSynchronize(c->stream), "kv_import sync");
+    const sllm_cuda_model* m = c->m;
+    const size_t D = m->head_dim, N = c->n_ctx, P = n_past;
+    const size_t heads = (size_t)m->n_layer * (size_t)m->n_head_kv;
+    std::vector<float> kt(D * (P > 0 ? P : 1));
+    for (size_t lh = 0; lh < heads; ++lh) {
+        float* kd = c->k_cache + lh * D * N;
+        float* vd = c->v_cache + lh * N * D;
+        if (P > 0) {
+            const float* kh = k_in + lh * N * D;
+            for (size_t pos = 0; pos < P; ++pos)
+                for (size_t d = 0; d < D; ++d) kt[d * P + pos] = kh[pos * D + d];
+            CK(cudaMemcpy2D(kd, N * 4, kt.data(), P * 4, P * 4, D, cudaMemcpyHostToDevice), "kv_import K");
+            CK(cudaMemcpy(vd, v_in + lh * N * D, P * D * 4, cudaMemcpyHostToDevice), "kv_import V");
+        }
+        // positions past n_past read as absent (src/forward.c:1104-1118)
+        if (P < N) {
+            CK(cudaMemset2D(kd + P, N * 4, 0, (N - P) * 4, D), "kv_import clear K");
+            CK(cudaMemset(vd + P * D, 0, (N - P) * D * 4), "kv_import clear V");
+        }
+    }
+    if (P > 0) {
+        CK(cudaMemcpy(c->logits, last_logits, (size_t)m->n_vocab * 4, cudaMemcpyHostToDevice), "kv_import logits");
+        // a continuation without a prompt starts from the argmax of these
+        // logits, which a decode step would have left at tok_seq[n_past]
+        const int32_t next = host_argmax(last_logits, m->n_vocab);
+        CK(cudaMemcpy(c->tok_seq + P, &next, 4, cudaMemcpyHostToDevice), "kv_import next token");
+    }
+    c->n_past = n_past;
+    c->have_logits = n_past > 0;
+    return SLLM_CUDA_OK;
+}
+
+// SLKV version 1, the reference's state format (src/forward.c:963-993): a
+// header of eight 32-bit fields, then per layer and kv head the live K rows
+// and V rows as [pos][dim] floats, then the last position's n_vocab logits.
+static constexpr uint32_t kStateMagic = 0x564B4C53u;   // "SLKV"
+static constexpr uint32_t kStateVersion = 1u;
+
+extern "C" int sllm_cuda_state_save(const sllm_cuda_model* m, const sllm_cuda_ctx* c, const char* path) {
+    if (m == nullptr || c == nullptr || path == nullptr || c->m != m) return fail(SLLM_CUDA_ERR_ARG, "state_save: bad arguments");
+    const size_t D = m->head_dim, N = c->n_ctx, P = c->n_past, V = m->n_vocab;
+    const size_t heads = (size_t)m->n_layer * (size_t)m->n_head_kv;
+    std::vector<float> k(heads * N * D), v(heads * N * D), logits(V, 0.0f);
+    int rc = sllm_cuda_ctx_kv_export(c, k.data(), v.data());
+    if (rc != SLLM_CUDA_OK) return rc;
+    // the reference writes whatever its last-logits buffer holds; a context
+    // that never ran has none here, and zeros stand in for them
+    if (c->have_logits) CK(cudaMemcpy(logits.data(), c->logits, V * 4, cudaMemcpyDeviceToHost), "state_save logits");
+    FILE* f = fopen(path, "wb");
+    if (f == nullptr) return fail(SLLM_CUDA_ERR_IO, "state_save: cannot open %s", path);
+    const int32_t hdr[8] = {(int32_t)kStateMagic, (int32_t)kStateVersion, m->n_layer, c->n_ctx, m->n_head_kv,
+                            m->head_dim, c->n_past, m->n_vocab};
+    bool ok = fwrite(hdr, 4, 8, f) == 8;
+    for (size_t lh = 0; ok && lh < heads; ++lh) {
+        if (P > 0 && fwrite(k.data() + lh * N * D, 4, P * D, f) != P * D) ok = false;
+        if (ok && P > 0 && fwrite(v.data() + lh * N * D, 4, P * D, f) != P * D) ok = false;
+    }
+    if (ok && fwrite(logits.data(), 4, V, f) != V) ok = false;
+    if (fclose(f) != 0) ok = false;
+    return ok ? SLLM_CUDA_OK : fail(SLLM_CUDA_ERR_IO, "state_save: write to %s failed", path);
+}
+
+extern "C" int sllm_cuda_state_load(const sllm_cuda_model* m, sllm_cuda_ctx* c, const char* path) {
+    if (m == nullptr || c == nullptr || path == nullptr || c->m != m) return fail(SLLM_CUDA_ERR_ARG, "state_load: bad arguments");
+    FILE* f = fopen(path, "rb");
+    if (f == nullptr) return fail(SLLM_CUDA_ERR_IO, "state_load: cannot open %s", path);
+    uint32_t hdr[8] = {};
+    // the reference's status for each refusal (src/forward.c:1034-1068)
+    if (fread(hdr, 4, 2, f) != 2 || hdr[0] != kStateMagic || hdr[1] != kStateVersion) {
+        fclose(f);
+        return fail(SLLM_CUDA_ERR_KV_TYPE, "state_load: %s is not an SLKV v1 file", path);
+    }
+    if (fread(hdr + 2, 4, 6, f) != 6) {
+        fclose(f);
+        return fail(SLLM_CUDA_ERR_TRUNCATED, "state_load: %s: truncated header", path);
+    }
+    const int32_t n_layer = (int32_t)hdr[2], n_ctx = (int32_t)hdr[3], n_head_kv = (int32_t)hdr[4];
+    const int32_t head_dim = (int32_t)hdr[5], n_past = (int32_t)hdr[6], n_vocab = (int32_t)hdr[7];
+    if (n_layer != m->n_layer || n_head_kv != m->n_head_kv || head_dim != m->head_dim || n_ctx != c->n_ctx ||
+        n_vocab != m->n_vocab || n_past < 0 || n_past > c->n_ctx) {
+        fclose(f);
+        return fail(SLLM_CUDA_ERR_TENSOR_SHAPE, "state_load: %s was saved for another geometry", path);
+    }
+    const size_t D = head_dim, N = n_ctx, P = n_past, V = n_vocab;
+    const size_t heads = (size_t)n_layer * (size_t)n_head_kv;
+    std::vector<float> k(heads * N * D, 0.0f), v(heads * N * D, 0.0f), logits(V);
+    bool ok = true;
+    for (size_t lh = 0; ok && lh < heads; ++lh) {
+        if (P > 0 && fread(k.data() + lh * N * D, 4, P * D, f) != P * D) ok = false;
+        if (ok && P > 0 && fread(v.data() + lh * N * D, 4, P * D, f) != P * D) ok = false;
+    }
+    if (ok && fread(logits.data(), 4, V, f) != V) ok = false;
+    fclose(f);
+    if (!ok) return fail(SLLM_CUDA_ERR_TRUNCATED, "state_load: %s is truncated", path);
+    return sllm_cuda_ctx_kv_import(c, k.data(), v.data(), n_past, logits.data());
 }
 
 // The decode step's layers as one engine program: per layer Q/K/V, attention,

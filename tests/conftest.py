@@ -64,6 +64,15 @@ def cuda(pkg):
     return pkg
 
 
+@pytest.fixture(scope="session")
+def cuda_absent(pkg):
+    """For CPU tests of behaviour without a device: skipped where one exists."""
+    rc, n, cc = pkg.probe()
+    if rc == 0:
+        pytest.skip("a CUDA device is present")
+    return pkg
+
+
 def bits(a):
     """Bit patterns of a float32 array, for exact comparisons. Every NaN maps
     to one pattern: x86 produces the negative default NaN (0xffc00000) where a
