@@ -71,6 +71,19 @@ SLLM_CUDA_API long long sllm_cuda_test_kernel_launches(void);
 SLLM_CUDA_API float sllm_cuda_test_ctx_last_run_ms(const sllm_cuda_ctx * c);
 SLLM_CUDA_API float sllm_cuda_test_tp_ctx_last_run_ms(const sllm_cuda_tp_ctx * c);
 
+/*
+ * Failure injection without a GPU fault. sllm_cuda_test_fail_next: the next
+ * `count` device allocations of a model or context (what = 1) or the next
+ * `count` communicator set-ups (what = 2) fail as if refused (NOMEM, COMM).
+ * sllm_cuda_test_engine_faults on `device`: every bounded wait of the
+ * persistent engine gives up after wait_ms (<= 0: the default 2 s), and CTA
+ * skip_arrival_cta (-1: none) leaves out its first grid-barrier arrival, so
+ * the other CTAs' barrier waits run out; the call that ran reports
+ * SLLM_CUDA_ERR_TIMEOUT and the context stays usable. Read by every launch.
+ */
+SLLM_CUDA_API void sllm_cuda_test_fail_next(int what, int count);
+SLLM_CUDA_API int sllm_cuda_test_engine_faults(int device, int skip_arrival_cta, double wait_ms);
+
 /* The device error word of a GEMV batch's launch: SLLM_CUDA_OK, or
  * SLLM_CUDA_ERR_TIMEOUT when a bounded wait gave up; -1 before its first run. */
 SLLM_CUDA_API int sllm_cuda_test_gemv_batch_error(sllm_cuda_gemv_batch * b);

@@ -94,6 +94,8 @@ def lib():
     L.sllm_cuda_test_engine_split.argtypes = [vp, vp, vp, vp, i32, vp, i32, i32, vp]
     L.sllm_cuda_test_tp_plan.argtypes = [i32, i32, i32, i32, i32, i32, i32, i32, vp]
     L.sllm_cuda_test_projection_split.argtypes = [i32, i32, i32, i32]
+    L.sllm_cuda_test_fail_next.argtypes = [C.c_int, C.c_int]
+    L.sllm_cuda_test_engine_faults.argtypes = [C.c_int, C.c_int, C.c_double]
     L.sllm_cuda_state_save.argtypes = [vp, vp, C.c_char_p]
     L.sllm_cuda_state_load.argtypes = [vp, vp, C.c_char_p]
     L.sllm_cuda_ctx_kv_export.argtypes = [vp, vp, vp]

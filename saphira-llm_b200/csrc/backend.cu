@@ -190,6 +190,36 @@ extern "C" long long sllm_cuda_test_kernel_launches(void) { return g_kernel_laun
 void sllm::count_launches(long long n) { g_kernel_launches += n; }
 int sllm::force_fallback_flag() { return g_force_fallback; }
 
+// host-side failure injection (tests): the next n device allocations of a
+// model or context, or the next n communicator set-ups, fail as if the
+// device or the library had refused them
+static std::atomic<int> g_fail_alloc{0};
+static std::atomic<int> g_fail_comm{0};
+
+cudaError_t sllm::dev_malloc(void** p, size_t bytes) {
+    int n = g_fail_alloc.load();
+    while (n > 0 && !g_fail_alloc.compare_exchange_weak(n, n - 1)) {}
+    if (n > 0) { *p = nullptr; return cudaErrorMemoryAllocation; }
+    return cudaMalloc(p, bytes);
+}
+
+bool sllm::fail_next_comm_init() {
+    int n = g_fail_comm.load();
+    while (n > 0 && !g_fail_comm.compare_exchange_weak(n, n - 1)) {}
+    return n > 0;
+}
+
+extern "C" void sllm_cuda_test_fail_next(int what, int count) {
+    if (what == 1) g_fail_alloc = count;
+    if (what == 2) g_fail_comm = count;
+}
+
+extern "C" int sllm_cuda_test_engine_faults(int device, int skip_arrival_cta, double wait_ms) {
+    CK(cudaSetDevice(device), "cudaSetDevice");
+    CK(engine_test_faults(skip_arrival_cta, wait_ms), "engine test hooks");
+    return SLLM_CUDA_OK;
+}
+
 int* sllm::fallback_counter() { return device_word(g_fallback_counters); }
 
 extern "C" void sllm_cuda_test_set_force_fallback(int on) { g_force_fallback = on; }
@@ -409,8 +439,8 @@ extern "C" int sllm_cuda_model_upload(const sllm_cuda_model_desc* d, int device,
         idx.push_back(add(L.ffn_sub_norm, (size_t)F * 4));
     }
     const size_t out_norm = add(d->output_norm, (size_t)E * 4);
-    cudaError_t e = cudaMalloc(&m->blob, total);
-    if (e == cudaSuccess) e = cudaMalloc(&m->tok_embd, (size_t)d->n_vocab * (size_t)E * 2);
+    cudaError_t e = dev_malloc((void**)&m->blob, total);
+    if (e == cudaSuccess) e = dev_malloc((void**)&m->tok_embd, (size_t)d->n_vocab * (size_t)E * 2);
     if (e != cudaSuccess) { sllm_cuda_model_free(m); return cuda_fail(e, "model_upload: cudaMalloc"); }
     for (const Item& it : items) {
         e = cudaMemcpy(m->blob + it.off, it.src, it.bytes, cudaMemcpyHostToDevice);
@@ -631,6 +661,8 @@ static int engine_program_build(EngineProgram& p, const std::vector<EngGroup>& g
     return SLLM_CUDA_OK;
 }
 
+static int engine_error(const EngineProgram& p);
+
 static cudaError_t engine_program_launch(const EngineProgram& p, cudaStream_t st) {
     if (p.exec != nullptr) return graph_launch(p.exec, st);
     const cudaError_t e = launch_engine(p.params, p.grid, st, p.wa, p.wb);
@@ -748,7 +780,7 @@ extern "C" int sllm_cuda_ctx_new(const sllm_cuda_model* m, int32_t n_ctx, sllm_c
     const size_t E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa, V = m->n_vocab;
     c->lm_grid = lm_head_grid(num_sms_of(m->device));
     cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
-    auto A = [&](void** p, size_t bytes) { if (e == cudaSuccess) e = cudaMalloc(p, bytes); };
+    auto A = [&](void** p, size_t bytes) { if (e == cudaSuccess) e = dev_malloc(p, bytes); };
     A((void**)&c->k_cache, kv * 4); A((void**)&c->v_cache, kv * 4);
     A((void**)&c->rope_cos, (size_t)n_ctx * 64 * 4); A((void**)&c->rope_sin, (size_t)n_ctx * 64 * 4);
     A((void**)&c->x, E * 4); A((void**)&c->q, E * 4); A((void**)&c->k, G * 4); A((void**)&c->v, G * 4);
@@ -962,6 +994,10 @@ extern "C" int sllm_cuda_forward_chunk(const sllm_cuda_model* m, sllm_cuda_ctx* 
     if (argmax_out != nullptr)
         CK(cudaMemcpyAsync(argmax_out, c->argmax_hist + base, (size_t)n * 4, cudaMemcpyDeviceToHost, c->stream), "argmax");
     CK(cudaStreamSynchronize(c->stream), "forward_chunk sync");
+    if (c->eng_decode.built) {
+        const int rc_e = engine_error(c->eng_decode);
+        if (rc_e != SLLM_CUDA_OK) return rc_e;
+    }
     c->n_past = base + n;
     c->have_logits = true;
     return SLLM_CUDA_OK;
@@ -998,6 +1034,10 @@ extern "C" int sllm_cuda_generate_greedy(const sllm_cuda_model* m, sllm_cuda_ctx
     if (n_new > 0)
         CK(cudaMemcpyAsync(out, c->tok_seq + base + n_prompt, (size_t)n_new * 4, cudaMemcpyDeviceToHost, c->stream), "ids");
     CK(cudaStreamSynchronize(c->stream), "generate sync");
+    if (c->eng_decode.built) {
+        const int rc_e = engine_error(c->eng_decode);
+        if (rc_e != SLLM_CUDA_OK) return rc_e;
+    }
     c->n_past = base + steps;
     if (steps > 0) c->have_logits = true;
     return SLLM_CUDA_OK;
@@ -1255,10 +1295,15 @@ static int chain_program(const sllm_cuda_model* m, sllm_cuda_ctx* c, int begin, 
                                 engine_wpl(E), engine_wpl(F));
 }
 
+// A program's error word after its launches have completed: a bounded wait
+// that gave up is reported once and the word cleared, so the context's next
+// call starts clean.
 static int engine_error(const EngineProgram& p) {
     int err = 0;
-    if (p.error != nullptr && cudaMemcpy(&err, p.error, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && err != 0)
+    if (p.error != nullptr && cudaMemcpy(&err, p.error, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && err != 0) {
+        cudaMemset(p.error, 0, sizeof(int));
         return fail(SLLM_CUDA_ERR_TIMEOUT, "engine: a bounded device wait gave up (code %d)", err);
+    }
     return SLLM_CUDA_OK;
 }
 

@@ -24,6 +24,11 @@ cudaError_t instantiate(cudaGraphExec_t* exec, cudaGraph_t g);
 cudaError_t graph_launch(cudaGraphExec_t exec, cudaStream_t st);
 void graph_exec_destroy(cudaGraphExec_t exec);
 void count_launches(long long n);
+// cudaMalloc for the model and context allocations, with the test hook that
+// makes the next n of them fail (sllm_cuda_test_fail_next)
+cudaError_t dev_malloc(void** p, size_t bytes);
+// the test hook for communicator set-up: true when this one must fail
+bool fail_next_comm_init();
 // split every stage's rows over `grid` CTAs by weight bytes (engine programs)
 std::vector<EngCursor> engine_starts(const std::vector<EngOp>& ops, const std::vector<int>& stage_first, int grid);
 

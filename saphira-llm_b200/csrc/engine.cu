@@ -18,7 +18,8 @@
 // Exactness is the same as i2s_gemv.cu: integer dots in any order, the
 // reference's float op order in the prologue and epilogues.
 //
-// Every wait is bounded by the global timer (2 s). A wait that gives up
+// Every wait is bounded by the global timer (2 s; a test hook may shorten
+// it). A wait that gives up
 // records why in *error and puts the CTA in a skip mode that still reaches
 // every barrier, so the kernel always terminates; the producer then waits
 // (bounded) for its own copies in flight before it exits.
@@ -30,6 +31,13 @@
 namespace sllm {
 
 constexpr uint64_t kEngWaitNs = 2000000000ull;
+
+// Test hooks, read by every launch (so a context's captured graphs see them):
+// the budget of every bounded wait, and a CTA that leaves out its first
+// grid-barrier arrival (-1: none), so that a test can make the other CTAs'
+// waits run out without faulting or hanging anything.
+__device__ unsigned long long g_eng_wait_ns = kEngWaitNs;
+__device__ int g_eng_skip_arrival = -1;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -64,12 +72,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// bounded: false when the phase did not complete within kEngWaitNs
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// bounded: false when the phase did not complete within `budget` ns
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t budget) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = gtimer();
     while (!mbar_try_wait(bar, parity)) {
-        if (gtimer() - t0 > kEngWaitNs) return false;
+        if (gtimer() - t0 > budget) return false;
     }
     return true;
 }
@@ -329,10 +337,11 @@ __host__ __device__ constexpr int eng_rows_per_warp(int wpl, bool pair) {
 __device__ __noinline__ bool consumer_wait_full_slow(EngSmem& es, const EngParams& P, uint64_t* bar,
                                                      uint32_t parity) {
     if (*(volatile int*)&es.abort_flag) return false;
+    const uint64_t budget = *(volatile unsigned long long*)&g_eng_wait_ns;
     const uint64_t t0 = gtimer();
     while (!mbar_try_wait(bar, parity)) {
         if (*(volatile int*)&es.abort_flag) return false;
-        if (gtimer() - t0 > kEngWaitNs) {
+        if (gtimer() - t0 > budget) {
             es.abort_flag = 1;
             atomicExch(P.error, ENG_TIMEOUT_FULL);
             return false;
@@ -540,6 +549,7 @@ i2s_engine_kernel(const EngParams P) {
     if (warp == kEngConsumerWarps) {
         // ---------------- producer ----------------
         if (lane == 0) {
+            const uint64_t budget = *(volatile unsigned long long*)&g_eng_wait_ns;
             uint32_t k = 0;
             for (int s = 0; s < P.n_stages; ++s) {
                 ChunkWalk walk{s_ops, s_cur[2 * s].op, s_cur[2 * s].row, s_cur[2 * s + 1]};
@@ -571,7 +581,7 @@ i2s_engine_kernel(const EngParams P) {
                     const int slot = (int)(k % kEngSlots);
                     const uint32_t use = k / kEngSlots;
                     if (*(volatile int*)&es.abort_flag) break;
-                    if (use > 0 && !mbar_wait(&es.empty[slot], (use - 1) & 1)) {
+                    if (use > 0 && !mbar_wait(&es.empty[slot], (use - 1) & 1, budget)) {
                         es.abort_flag = 1;
                         atomicExch(P.error, ENG_TIMEOUT_EMPTY);
                         break;
@@ -594,7 +604,7 @@ i2s_engine_kernel(const EngParams P) {
             }
             // every copy this CTA issued lands before the CTA may exit
             const uint32_t first = k > (uint32_t)kEngSlots ? k - kEngSlots : 0;
-            for (uint32_t j = first; j < k; ++j) mbar_wait(&es.full[j % kEngSlots], (j / kEngSlots) & 1);
+            for (uint32_t j = first; j < k; ++j) mbar_wait(&es.full[j % kEngSlots], (j / kEngSlots) & 1, budget);
         }
         return;
     }
@@ -604,6 +614,12 @@ i2s_engine_kernel(const EngParams P) {
     // the buffers this program writes are complete from here on; the producer
     // streams only weights, which no kernel writes, and needs no such wait
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    uint64_t budget = 0;
+    int skip_arrival = -1;
+    if (tid == 0) {
+        budget = *(volatile unsigned long long*)&g_eng_wait_ns;
+        skip_arrival = *(volatile int*)&g_eng_skip_arrival;
+    }
     RingPos rp;
     int cur_group = -1;
     sllm_cuda_act act{0.0f, 0};
@@ -616,7 +632,7 @@ i2s_engine_kernel(const EngParams P) {
                     const unsigned target = (unsigned)s * (unsigned)G;
                     const uint64_t t0 = gtimer();
                     while (ld_acquire(P.barrier) < target) {
-                        if (gtimer() - t0 > kEngWaitNs) { ok = false; break; }
+                        if (gtimer() - t0 > budget) { ok = false; break; }
                         __nanosleep(20);
                     }
                 }
@@ -666,7 +682,7 @@ i2s_engine_kernel(const EngParams P) {
         }
         // publish this CTA's outputs of the stage, then arrive
         consumer_sync();
-        if (tid == 0 && s + 1 < P.n_stages) red_release_add(P.barrier, 1u);
+        if (tid == 0 && s + 1 < P.n_stages && !(s == 0 && c == skip_arrival)) red_release_add(P.barrier, 1u);
     }
 }
 
@@ -717,6 +733,14 @@ bool engine_supports(int wa, int wb) {
     SLLM_ENGINE_SHAPES(SLLM_ENG_SUP)
 #undef SLLM_ENG_SUP
     return false;
+}
+
+cudaError_t engine_test_faults(int skip_arrival_cta, double wait_ms) {
+    const unsigned long long ns =
+        wait_ms > 0.0 ? (unsigned long long)(wait_ms * 1.0e6) : (unsigned long long)kEngWaitNs;
+    cudaError_t e = cudaMemcpyToSymbol(g_eng_wait_ns, &ns, sizeof ns);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_eng_skip_arrival, &skip_arrival_cta, sizeof(int));
+    return e;
 }
 
 bool engine_pair_for_width(int wpl, int* wa, int* wb) {

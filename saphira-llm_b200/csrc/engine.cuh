@@ -93,6 +93,10 @@ bool engine_supports(int wa, int wb);
 // a compiled pair whose first width is `wpl` (for programs of one width)
 bool engine_pair_for_width(int wpl, int* wa, int* wb);
 cudaError_t prepare_engine();     // once, outside any stream capture
+// test hook on the current device: every bounded wait gives up after wait_ms
+// (<= 0: the default 2 s), and CTA skip_arrival_cta (-1: none) leaves out its
+// first grid-barrier arrival
+cudaError_t engine_test_faults(int skip_arrival_cta, double wait_ms);
 cudaError_t launch_engine(const EngParams& p, int grid, cudaStream_t st, int wa, int wb);
 
 }  // namespace sllm

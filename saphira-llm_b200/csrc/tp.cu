@@ -702,6 +702,7 @@ extern "C" int sllm_cuda_tp_comm_init(const uint8_t* id, int32_t n_ranks, int32_
         return fail(SLLM_CUDA_ERR_ARG, "tp_comm_init: bad arguments");
     *out = nullptr;
     if (nccl() == nullptr) return fail(SLLM_CUDA_ERR_UNSUPPORTED, "tp_comm_init: libnccl.so.2 not found");
+    if (fail_next_comm_init()) return fail(SLLM_CUDA_ERR_COMM, "ncclCommInitRank: refused (injected by a test)");
     CK(cudaSetDevice(device), "cudaSetDevice");
     ncclUniqueId uid;
     memcpy(&uid, id, sizeof(uid));
@@ -740,7 +741,7 @@ static int tp_model_alloc(sllm_cuda_tp_model* m, int device) {
     const Layout L = shard_layout(m);
     m->blob_bytes = L.total;
     CK(cudaSetDevice(device), "cudaSetDevice");
-    CK(cudaMalloc(&m->blob, L.total), "tp model blob");
+    CK(dev_malloc((void**)&m->blob, L.total), "tp model blob");
     bind_pointers(m, L);
     return SLLM_CUDA_OK;
 }
@@ -855,7 +856,7 @@ namespace {
 template <class T>
 cudaError_t ctx_alloc(sllm_cuda_tp_ctx* c, T** p, size_t count) {
     void* v = nullptr;
-    const cudaError_t e = cudaMalloc(&v, align256(count * sizeof(T)));
+    const cudaError_t e = dev_malloc(&v, align256(count * sizeof(T)));
     if (e == cudaSuccess) {
         c->allocs.push_back(v);
         *p = static_cast<T*>(v);
@@ -1563,12 +1564,18 @@ extern "C" int sllm_cuda_tp_generate_greedy(sllm_cuda_tp_ctx* c, const int32_t* 
     if (c->x_error != nullptr) {
         int err = 0;
         CK(cudaMemcpy(&err, c->x_error, 4, cudaMemcpyDeviceToHost), "exchange error word");
-        if (err != 0) return fail(SLLM_CUDA_ERR_TIMEOUT, "tp step: a peer's exchange flag did not arrive in time");
+        if (err != 0) {
+            cudaMemset(c->x_error, 0, 4);
+            return fail(SLLM_CUDA_ERR_TIMEOUT, "tp step: a peer's exchange flag did not arrive in time");
+        }
     }
     if (c->eng_error != nullptr) {
         int err = 0;
         CK(cudaMemcpy(&err, c->eng_error, 4, cudaMemcpyDeviceToHost), "engine error word");
-        if (err != 0) return fail(SLLM_CUDA_ERR_TIMEOUT, "tp step: an engine wait gave up (code %d)", err);
+        if (err != 0) {
+            cudaMemset(c->eng_error, 0, 4);
+            return fail(SLLM_CUDA_ERR_TIMEOUT, "tp step: an engine wait gave up (code %d)", err);
+        }
     }
     c->n_past = base + steps;
     c->have_logits = steps > 0;
