@@ -658,7 +658,15 @@ def decode_leg(pkg, synth, local, rank, world, args):
     import torch
     cfg = synth.Config()
     m = synth.SynthModel(cfg, seed=4242 + rank)
-    model = pkg.Model(m.desc(), local)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    model = pkg.Model(m.desc(), local)           # sllm_cuda_model_upload: pinned, double-buffered staging
+    up_s = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    plain = torch.from_numpy(m.image).to(f"cuda:{local}")   # one pageable copy of the same image, for scale
+    torch.cuda.synchronize()
+    pg_s = time.perf_counter() - t0
+    del plain
     ctx = model.ctx(64 + 256)
     prompt = np.random.default_rng(7 + rank).integers(0, cfg.n_vocab, 64).astype(np.int32)
     rc, toks = ctx.generate(prompt, 256)         # warm-up (captures the step graph)
@@ -693,7 +701,11 @@ def decode_leg(pkg, synth, local, rank, world, args):
                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                         "bytes_per_step": int(run_bytes / 320)},
-           "token_checksum": int(np.sum(toks.astype(np.int64) * np.arange(1, 257)) % 1000003)}
+           "token_checksum": int(np.sum(toks.astype(np.int64) * np.arange(1, 257)) % 1000003),
+           "upload": {"api": "sllm_cuda_model_upload (pinned double-buffered staging, host copy threads)",
+                      "bytes": int(model.weight_bytes()), "s": round(up_s, 3),
+                      "gbs": round(model.weight_bytes() / up_s / 1e9, 2),
+                      "pageable_copy_gbs": round(m.image.nbytes / pg_s / 1e9, 2)}}
     # the reference's own 256 tokens for this model and prompt (the fixture
     # tests/golden/make_golden.py --large wrote from the compiled reference)
     fx = os.path.join(ROOT, "tests", "golden", "decode_large.json")

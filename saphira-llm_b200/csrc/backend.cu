@@ -24,6 +24,7 @@
 #include "engine.cuh"
 #include "gemm.cuh"
 #include "gemv.cuh"
+#include "upload.cuh"
 #include "../../include/sllm_cuda.h"
 #include "../../include/sllm_cuda_testing.h"
 
@@ -442,12 +443,18 @@ extern "C" int sllm_cuda_model_upload(const sllm_cuda_model_desc* d, int device,
     cudaError_t e = dev_malloc((void**)&m->blob, total);
     if (e == cudaSuccess) e = dev_malloc((void**)&m->tok_embd, (size_t)d->n_vocab * (size_t)E * 2);
     if (e != cudaSuccess) { sllm_cuda_model_free(m); return cuda_fail(e, "model_upload: cudaMalloc"); }
-    for (const Item& it : items) {
-        e = cudaMemcpy(m->blob + it.off, it.src, it.bytes, cudaMemcpyHostToDevice);
+    {
+        // through pinned staging: host threads fill one buffer while the
+        // device copies the other in
+        Uploader up(device);
+        for (const Item& it : items) {
+            e = up.put(m->blob + it.off, it.src, it.bytes);
+            if (e != cudaSuccess) break;
+        }
+        if (e == cudaSuccess) e = up.put(m->tok_embd, d->tok_embd, (size_t)d->n_vocab * (size_t)E * 2);
+        if (e == cudaSuccess) e = up.finish();
         if (e != cudaSuccess) { sllm_cuda_model_free(m); return cuda_fail(e, "model_upload: weights"); }
     }
-    e = cudaMemcpy(m->tok_embd, d->tok_embd, (size_t)d->n_vocab * (size_t)E * 2, cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) { sllm_cuda_model_free(m); return cuda_fail(e, "model_upload: tok_embd"); }
     m->layers.resize(d->n_layer);
     for (int l = 0; l < d->n_layer; ++l) {
         const size_t* ix = &idx[(size_t)l * 11];

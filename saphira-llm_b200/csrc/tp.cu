@@ -46,6 +46,7 @@
 #include <cooperative_groups.h>
 
 #include "backend.cuh"
+#include "upload.cuh"
 #include "common.cuh"
 #include "decode.cuh"
 #include "engine.cuh"
@@ -762,9 +763,8 @@ extern "C" int sllm_cuda_tp_model_upload(const sllm_cuda_model_desc* d, int32_t 
     if (rc != SLLM_CUDA_OK) { delete m; return rc; }
     const int E = m->E, F = m->F, D = kHeadDim, G = m->Hkv * D;
     std::vector<uint8_t> buf;
-    auto put = [&](const void* dst, const void* src, size_t n) {
-        return cudaMemcpy(const_cast<void*>(dst), src, n, cudaMemcpyHostToDevice);
-    };
+    Uploader up(device);     // pinned, double-buffered staging (the slices are re-packed in buf first)
+    auto put = [&](const void* dst, const void* src, size_t n) { return up.put(const_cast<void*>(dst), src, n); };
     cudaError_t e = cudaSuccess;
     for (int l = 0; l < m->n_layer && e == cudaSuccess; ++l) {
         const sllm_cuda_layer_desc& h = d->layers[l];
@@ -786,6 +786,7 @@ extern "C" int sllm_cuda_tp_model_upload(const sllm_cuda_model_desc* d, int32_t 
     }
     if (!e) e = put(m->tok_embd, d->tok_embd, (size_t)m->V * E * 2);
     if (!e) e = put(m->output_norm, d->output_norm, (size_t)E * 4);
+    if (!e) e = up.finish();
     if (e != cudaSuccess) {
         cudaFree(m->blob);
         delete m;
