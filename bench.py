@@ -706,6 +706,21 @@ def decode_leg(pkg, synth, local, rank, world, args):
                       "bytes": int(model.weight_bytes()), "s": round(up_s, 3),
                       "gbs": round(model.weight_bytes() / up_s / 1e9, 2),
                       "pageable_copy_gbs": round(m.image.nbytes / pg_s / 1e9, 2)}}
+    # the fp16 KV option: the same decode with every cached value rounded to
+    # half; it has no reference output, so it reports its token agreement
+    c16 = model.ctx(64 + 256, kv_f16=True)
+    rc16, t16 = c16.generate(prompt, 256)
+    c16.reset()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    rc16, t16 = c16.generate(prompt, 256)
+    w16 = time.perf_counter() - t0
+    if rc16 == 0:
+        first = next((i for i in range(256) if t16[i] != toks[i]), 256)
+        out["kv_f16"] = {"tokens_per_s": round(320 / w16, 1), "device_ms_per_token": round(c16.last_run_ms() / 320, 4),
+                         "tokens_equal_to_fp32": int(np.sum(t16 == toks)), "first_difference": first,
+                         "kv_bytes_per_position": int(kv_row // 2)}
+    c16.close()
     # the reference's own 256 tokens for this model and prompt (the fixture
     # tests/golden/make_golden.py --large wrote from the compiled reference)
     fx = os.path.join(ROOT, "tests", "golden", "decode_large.json")

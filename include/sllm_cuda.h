@@ -246,6 +246,21 @@ SLLM_CUDA_API void sllm_cuda_model_free(sllm_cuda_model * m);
  */
 SLLM_CUDA_API int  sllm_cuda_ctx_new(const sllm_cuda_model * m, int32_t n_ctx,
                        sllm_cuda_ctx ** out);
+
+/*
+ * The same with a choice of KV cache type. SLLM_CUDA_KV_F32 is the
+ * reference's cache and sllm_cuda_ctx_new's. SLLM_CUDA_KV_F16 is an option the
+ * reference does not have: every cached K and V value is stored rounded to
+ * the nearest half (ties to even) and read back exactly, halving the cache.
+ * Everything else is computed as in the fp32 context, so the logits differ
+ * from the reference's only through that rounding; the benchmark reports how
+ * many greedy tokens still agree. State files stay SLKV v1 with f32 values
+ * (export widens exactly, import rounds).
+ */
+#define SLLM_CUDA_KV_F32 0
+#define SLLM_CUDA_KV_F16 1
+SLLM_CUDA_API int  sllm_cuda_ctx_new_kv(const sllm_cuda_model * m, int32_t n_ctx, int32_t kv_type,
+                                        sllm_cuda_ctx ** out);
 SLLM_CUDA_API void sllm_cuda_ctx_free(sllm_cuda_ctx * c);
 SLLM_CUDA_API void sllm_cuda_ctx_reset(sllm_cuda_ctx * c);
 

@@ -81,6 +81,9 @@ class Oracle:
         L.orc_ctx_new.argtypes = [C.POINTER(abi.ModelDesc), C.c_int32, C.POINTER(C.c_void_p)]
         L.orc_ctx_free.argtypes = [C.c_void_p]
         L.orc_ctx_reset.argtypes = [C.c_void_p]
+        L.orc_ctx_set_kv_f16.argtypes = [C.c_void_p, C.c_int]
+        L.orc_fp32_to_fp16.argtypes = [C.c_float]
+        L.orc_fp32_to_fp16.restype = C.c_uint16
         L.orc_ctx_n_past.argtypes = [C.c_void_p]
         L.orc_ctx_n_past.restype = C.c_int32
         L.orc_ctx_last_logits.argtypes = [C.c_void_p]
@@ -150,17 +153,22 @@ class Oracle:
         self.lib.orc_layer_chain(C.byref(desc), layer, x, scratch)
         return x
 
-    def ctx(self, desc, n_ctx):
-        return OracleCtx(self, desc, n_ctx)
+    def ctx(self, desc, n_ctx, kv_f16=False):
+        return OracleCtx(self, desc, n_ctx, kv_f16)
+
+    def fp32_to_fp16(self, f):
+        return int(self.lib.orc_fp32_to_fp16(float(f)))
 
 
 class OracleCtx:
-    def __init__(self, orc, desc, n_ctx):
+    def __init__(self, orc, desc, n_ctx, kv_f16=False):
         self.orc, self.desc, self.n_vocab = orc, desc, desc.n_vocab
         self.h = C.c_void_p()
         rc = orc.lib.orc_ctx_new(C.byref(desc), n_ctx, C.byref(self.h))
         if rc != 0:
             raise RuntimeError(f"orc_ctx_new: {rc}")
+        if kv_f16:
+            orc.lib.orc_ctx_set_kv_f16(self.h, 1)
 
     def __del__(self):
         if getattr(self, "h", None):

@@ -352,6 +352,7 @@ int32_t orc_argmax(const float * logits, int32_t n) {
 
 struct orc_ctx {
     int32_t n_ctx, n_past, n_layer, kv_dim, n_embd, n_ff, n_vocab;
+    int     kv_f16;       /* this project's fp16-KV variant: cache values rounded to half */
     float * k_cache;      /* [layer][head_kv][pos][head_dim] (src/forward.c:81-83) */
     float * v_cache;
     float * last_logits;
@@ -406,6 +407,49 @@ void orc_ctx_free(orc_ctx * c) {
     free(c->qa); free(c->dots);
     free(c);
 }
+
+/*
+ * Not in the reference: the fp16 KV option of the CUDA backend, restated so
+ * that it can be checked bit for bit. Every value stored into the cache is
+ * rounded to the nearest IEEE half (ties to even) and widened back exactly;
+ * everything else is the reference's order. float -> half by the standard
+ * round-to-nearest-even rules (overflow to infinity from 65520 up, gradual
+ * underflow to the half subnormals).
+ */
+static uint16_t orc_fp32_to_fp16_rne(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const uint32_t ax = x & 0x7fffffffu;
+    if (ax >= 0x7f800000u) {     /* infinity or NaN */
+        return (uint16_t) (sign | 0x7c00u | (ax > 0x7f800000u ? (0x200u | ((ax >> 13) & 0x3ffu)) : 0u));
+    }
+    if (ax >= 0x477ff000u) { return (uint16_t) (sign | 0x7c00u); }   /* >= 65520 */
+    if (ax >= 0x38800000u) {     /* a normal half: rebias, keep 10 mantissa bits */
+        const uint32_t v = ax - 0x38000000u;
+        uint32_t h = v >> 13;
+        const uint32_t rem = v & 0x1fffu;
+        if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) { h += 1u; }
+        return (uint16_t) (sign | h);
+    }
+    const uint32_t e = ax >> 23;
+    if (e < 102u) { return (uint16_t) sign; }          /* below 2^-25: zero */
+    const uint32_t mant = (ax & 0x7fffffu) | 0x800000u;
+    const uint32_t shift = 126u - e;                    /* 14 .. 24 */
+    uint32_t h = mant >> shift;
+    const uint32_t rem = mant & ((1u << shift) - 1u);
+    const uint32_t mid = 1u << (shift - 1u);
+    if (rem > mid || (rem == mid && (h & 1u))) { h += 1u; }
+    return (uint16_t) (sign | h);
+}
+
+static float orc_kv_round(const orc_ctx * c, float v) {
+    return c->kv_f16 ? orc_fp16_to_fp32(orc_fp32_to_fp16_rne(v)) : v;
+}
+
+void orc_ctx_set_kv_f16(orc_ctx * c, int on) { if (c != NULL) { c->kv_f16 = on ? 1 : 0; } }
+
+uint16_t orc_fp32_to_fp16(float f) { return orc_fp32_to_fp16_rne(f); }
 
 /* src/forward.c:530-562: clear the live prefix of every layer, rewind. */
 void orc_ctx_reset(orc_ctx * c) {
@@ -467,8 +511,12 @@ static void forward_one(const sllm_cuda_model_desc * m, orc_ctx * c,
         float * kb = c->k_cache + (size_t) il * kv_layer;             /* :683-696 */
         float * vb = c->v_cache + (size_t) il * kv_layer;
         for (int32_t h = 0; h < m->n_head_kv; ++h) {
-            memcpy(kb + ((size_t) h * c->n_ctx + pos) * hd, c->k + (size_t) h * hd, (size_t) hd * 4);
-            memcpy(vb + ((size_t) h * c->n_ctx + pos) * hd, c->v + (size_t) h * hd, (size_t) hd * 4);
+            float * kd = kb + ((size_t) h * c->n_ctx + pos) * hd;
+            float * vd = vb + ((size_t) h * c->n_ctx + pos) * hd;
+            for (int32_t d = 0; d < hd; ++d) {
+                kd[d] = orc_kv_round(c, c->k[(size_t) h * hd + d]);
+                vd[d] = orc_kv_round(c, c->v[(size_t) h * hd + d]);
+            }
         }
         const int32_t npast = pos + 1;                                /* :698-726 */
         for (int32_t h = 0; h < m->n_head; ++h) {

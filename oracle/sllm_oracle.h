@@ -66,6 +66,9 @@ int      orc_ctx_new(const sllm_cuda_model_desc * m, int32_t n_ctx, orc_ctx ** o
 void     orc_ctx_free(orc_ctx * c);
 void     orc_ctx_reset(orc_ctx * c);
 int32_t  orc_ctx_n_past(const orc_ctx * c);
+/* this project's fp16-KV variant (not the reference): round cached values to half */
+void     orc_ctx_set_kv_f16(orc_ctx * c, int on);
+uint16_t orc_fp32_to_fp16(float f);
 const float * orc_ctx_last_logits(const orc_ctx * c);
 int      orc_forward_chunk(const sllm_cuda_model_desc * m, orc_ctx * c,
                            const int32_t * tokens, int32_t n, int32_t base,

@@ -75,6 +75,7 @@ def lib():
     L.sllm_cuda_model_weight_bytes.argtypes = [vp]
     L.sllm_cuda_model_weight_bytes.restype = sz
     L.sllm_cuda_ctx_new.argtypes = [vp, i32, C.POINTER(vp)]
+    L.sllm_cuda_ctx_new_kv.argtypes = [vp, i32, i32, C.POINTER(vp)]
     L.sllm_cuda_ctx_free.argtypes = [vp]
     L.sllm_cuda_ctx_reset.argtypes = [vp]
     L.sllm_cuda_ctx_n_past.argtypes = [vp]
@@ -242,21 +243,21 @@ class Model:
     def __del__(self):
         self.close()
 
-    def ctx(self, n_ctx):
-        return Ctx(self, n_ctx)
+    def ctx(self, n_ctx, kv_f16=False):
+        return Ctx(self, n_ctx, kv_f16)
 
 
 class Ctx:
     """One sequence's device state: KV cache, scratch, decode graph."""
 
-    def __init__(self, model, n_ctx):
+    def __init__(self, model, n_ctx, kv_f16=False):
         import numpy as np
         self._np = np
         self.model = model
         self.n_vocab = model.desc.n_vocab
         self.n_embd = model.desc.n_embd
         self.h = C.c_void_p()
-        _check(lib().sllm_cuda_ctx_new(model.h, n_ctx, C.byref(self.h)), "ctx_new")
+        _check(lib().sllm_cuda_ctx_new_kv(model.h, n_ctx, 1 if kv_f16 else 0, C.byref(self.h)), "ctx_new")
 
     def close(self):
         if getattr(self, "h", None):

@@ -21,6 +21,8 @@
 // certified reciprocal itself.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "decode.cuh"
 #include "libm_expf.h"
@@ -29,9 +31,32 @@ namespace sllm {
 
 constexpr int kHeadDim = 128;
 
-template <int NT, class Sync>
-__device__ __forceinline__ void attention_head(const AttnParams& p, int h, int t, float* sc, float* qs, float* kcur,
-                                               float* fred, double* dred, Sync sync) {
+// The cache's element type. The reference keeps K and V in fp32
+// (src/forward.c:486-487), which is the default and bit-exact. The fp16 option
+// stores each value rounded to the nearest half (ties to even) and reads it
+// back exactly; the current position's k and v are rounded the same way, as if
+// stored and read back, so every use sees the cached value.
+// A cache is addressed by element index; f16 selects the element type (one
+// body for both, so the kernels that inline it keep one copy).
+template <class T>
+struct KvRef {
+    T* base;
+    __device__ __forceinline__ float ld(size_t i) const;
+    __device__ __forceinline__ void st(size_t i, float v) const;
+    __device__ __forceinline__ float round(float v) const;
+};
+template <> __device__ __forceinline__ float KvRef<float>::ld(size_t i) const { return base[i]; }
+template <> __device__ __forceinline__ void KvRef<float>::st(size_t i, float v) const { base[i] = v; }
+template <> __device__ __forceinline__ float KvRef<float>::round(float v) const { return v; }
+template <> __device__ __forceinline__ float KvRef<__half>::ld(size_t i) const { return __half2float(base[i]); }
+template <> __device__ __forceinline__ void KvRef<__half>::st(size_t i, float v) const { base[i] = __float2half_rn(v); }
+template <> __device__ __forceinline__ float KvRef<__half>::round(float v) const {
+    return __half2float(__float2half_rn(v));
+}
+
+template <int NT, class KV, class Sync>
+__device__ __forceinline__ void attention_head_t(const AttnParams& p, int h, int t, float* sc, float* qs, float* kcur,
+                                                 float* fred, double* dred, Sync sync) {
     static_assert(NT % 32 == 0 && NT >= 2 * kHeadDim, "two 128-thread teams at least");
     const int kvh = h / p.group;
     const int pos = *(volatile const int32_t*)p.pos_ptr;
@@ -39,8 +64,8 @@ __device__ __forceinline__ void attention_head(const AttnParams& p, int h, int t
     const int nctx = p.n_ctx;
     const float* cs = p.rope_cos + (size_t)pos * (kHeadDim / 2);
     const float* sn = p.rope_sin + (size_t)pos * (kHeadDim / 2);
-    float* kT = p.k_cache + (size_t)kvh * kHeadDim * nctx;   // [d][pos]
-    float* vC = p.v_cache + (size_t)kvh * nctx * kHeadDim;   // [pos][d]
+    const KvRef<KV> kT{reinterpret_cast<KV*>(p.k_cache) + (size_t)kvh * kHeadDim * nctx};   // [d][pos]
+    const KvRef<KV> vC{reinterpret_cast<KV*>(p.v_cache) + (size_t)kvh * nctx * kHeadDim};   // [pos][d]
     const int pv_d = t - (NT - kHeadDim);                   // this thread's P.V dimension, < 0: none
 
 
@@ -56,28 +81,27 @@ __device__ __forceinline__ void attention_head(const AttnParams& p, int h, int t
         const int i = t - 64;
         const float c = cs[i], s = sn[i];
         const float ka = __ldcg(p.k + kvh * kHeadDim + i), kb = __ldcg(p.k + kvh * kHeadDim + i + 64);
-        kcur[i] = __fsub_rn(__fmul_rn(ka, c), __fmul_rn(kb, s));
-        kcur[i + 64] = __fadd_rn(__fmul_rn(ka, s), __fmul_rn(kb, c));
+        kcur[i] = kT.round(__fsub_rn(__fmul_rn(ka, c), __fmul_rn(kb, s)));
+        kcur[i + 64] = kT.round(__fadd_rn(__fmul_rn(ka, s), __fmul_rn(kb, c)));
     }
     sync();
 
     // the first query head of the group stores this position's K and V
     // (src/forward.c:683-696); every head uses kcur / v directly for pos
     if (h % p.group == 0 && t < kHeadDim) {
-        kT[(size_t)t * nctx + pos] = kcur[t];
-        vC[(size_t)pos * kHeadDim + t] = __ldcg(p.v + kvh * kHeadDim + t);
+        kT.st((size_t)t * nctx + pos, kcur[t]);
+        vC.st((size_t)pos * kHeadDim + t, __ldcg(p.v + kvh * kHeadDim + t));
     }
 
     // scores: sequential f32 dot over d, then * 1/sqrt(hd) (src/forward.c:710-715)
     float mx = -INFINITY;
     if (t < pos) {
         float acc = 0.0f;
-        const float* col = kT + t;
         #pragma unroll
         for (int d0 = 0; d0 < kHeadDim; d0 += 32) {
             float kv[32];
             #pragma unroll
-            for (int j = 0; j < 32; ++j) kv[j] = col[(size_t)(d0 + j) * nctx];
+            for (int j = 0; j < 32; ++j) kv[j] = kT.ld((size_t)(d0 + j) * nctx + t);
             #pragma unroll
             for (int j = 0; j < 32; ++j) acc = __fadd_rn(acc, __fmul_rn(qs[d0 + j], kv[j]));
         }
@@ -97,12 +121,11 @@ __device__ __forceinline__ void attention_head(const AttnParams& p, int h, int t
             #pragma unroll 8
             for (int d = 0; d < kHeadDim; ++d) acc = __fadd_rn(acc, __fmul_rn(qs[d], kcur[d]));
         } else {
-            const float* col = kT + s;
             #pragma unroll
             for (int d0 = 0; d0 < kHeadDim; d0 += 32) {
                 float kv[32];
                 #pragma unroll
-                for (int j = 0; j < 32; ++j) kv[j] = col[(size_t)(d0 + j) * nctx];
+                for (int j = 0; j < 32; ++j) kv[j] = kT.ld((size_t)(d0 + j) * nctx + s);
                 #pragma unroll
                 for (int j = 0; j < 32; ++j) acc = __fadd_rn(acc, __fmul_rn(qs[d0 + j], kv[j]));
             }
@@ -161,15 +184,14 @@ __device__ __forceinline__ void attention_head(const AttnParams& p, int h, int t
     // as it has been added (no bounds predicates in that loop). Then the rows
     // left in r, and the last ones in batches of 16.
     if (pv_d >= 0) {
-        const float* vp = vC + pv_d;
-        const float vcur = __ldcg(p.v + kvh * kHeadDim + pv_d);
+        const float vcur = vC.round(__ldcg(p.v + kvh * kHeadDim + pv_d));
         const int last = pos > 0 ? pos - 1 : 0;     // loads past the last stored row read that row
         float r[64];
         float o = 0.0f;
         int s = 0;
         if (pos > 0) {
             #pragma unroll
-            for (int j = 0; j < 64; ++j) r[j] = vp[(size_t)min(j, last) * kHeadDim];
+            for (int j = 0; j < 64; ++j) r[j] = vC.ld((size_t)min(j, last) * kHeadDim + pv_d);
             #pragma unroll 1
             for (; s + 64 < pos; s += 64) {
                 // rows s .. s+63 are all stored; refill with the next block
@@ -180,7 +202,7 @@ __device__ __forceinline__ void attention_head(const AttnParams& p, int h, int t
                         o = __fadd_rn(o, __fmul_rn(__fmul_rn(sc[s + 16 * b + j], inv), r[16 * b + j]));
                     #pragma unroll
                     for (int j = 0; j < 16; ++j)
-                        r[16 * b + j] = vp[(size_t)min(s + 64 + 16 * b + j, last) * kHeadDim];
+                        r[16 * b + j] = vC.ld((size_t)min(s + 64 + 16 * b + j, last) * kHeadDim + pv_d);
                 }
             }
             // the last block: rows s .. pos-1
@@ -197,6 +219,23 @@ __device__ __forceinline__ void attention_head(const AttnParams& p, int h, int t
         o = __fadd_rn(o, __fmul_rn(__fmul_rn(sc[pos], inv), vcur));
         p.out[h * kHeadDim + pv_d] = o;
     }
+}
+
+// The fp16 cache out of line: a kernel that inlines the fp32 head keeps its
+// registers, and the fp16 head costs one call per head.
+template <int NT, class Sync>
+__device__ __noinline__ void attention_head_f16(const AttnParams& p, int h, int t, float* sc, float* qs, float* kcur,
+                                                float* fred, double* dred, Sync sync) {
+    attention_head_t<NT, __half>(p, h, t, sc, qs, kcur, fred, dred, sync);
+}
+
+template <int NT, class Sync>
+__device__ __forceinline__ void attention_head(const AttnParams& p, int h, int t, float* sc, float* qs, float* kcur,
+                                               float* fred, double* dred, Sync sync) {
+    if (p.kv_f16)
+        attention_head_f16<NT>(p, h, t, sc, qs, kcur, fred, dred, sync);
+    else
+        attention_head_t<NT, float>(p, h, t, sc, qs, kcur, fred, dred, sync);
 }
 
 }  // namespace sllm

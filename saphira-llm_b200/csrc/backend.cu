@@ -18,6 +18,8 @@
 #include <unordered_map>
 #include <vector>
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "decode.cuh"
 #include "backend.cuh"
@@ -689,6 +691,7 @@ struct sllm_cuda_ctx {
     bool have_logits = false;
     cudaStream_t stream = nullptr;
     float *k_cache = nullptr, *v_cache = nullptr;   // [layer][kvh][128][n_ctx], [layer][kvh][n_ctx][128]
+    int kv_f16 = 0;                                  // the caches hold __half values (the fp16 KV option)
     float *rope_cos = nullptr, *rope_sin = nullptr;
     float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *ffn_inp = nullptr, *h = nullptr;
     float* logits = nullptr;
@@ -725,6 +728,13 @@ struct sllm_cuda_ctx {
     // generate call (device time of the decode steps alone)
     cudaEvent_t run_ev[2] = {};
 };
+
+// bytes of one cached value, and the cache of layer l
+static size_t kv_elt(const sllm_cuda_ctx* c) { return c->kv_f16 ? 2 : 4; }
+static float* kv_layer_ptr(const sllm_cuda_ctx* c, float* base, int l) {
+    const size_t per = (size_t)c->m->n_embd_gqa * (size_t)c->n_ctx;
+    return reinterpret_cast<float*>(reinterpret_cast<char*>(base) + (size_t)l * per * kv_elt(c));
+}
 
 // the reference's angle recurrence (src/ops.c:529-549), on the host libm
 void sllm::rope_table(int n_ctx, int n_rot, float base, std::vector<float>& cs, std::vector<float>& sn) {
@@ -773,7 +783,13 @@ extern "C" void sllm_cuda_ctx_free(sllm_cuda_ctx* c) {
 }
 
 extern "C" int sllm_cuda_ctx_new(const sllm_cuda_model* m, int32_t n_ctx, sllm_cuda_ctx** out) {
+    return sllm_cuda_ctx_new_kv(m, n_ctx, SLLM_CUDA_KV_F32, out);
+}
+
+extern "C" int sllm_cuda_ctx_new_kv(const sllm_cuda_model* m, int32_t n_ctx, int32_t kv_type, sllm_cuda_ctx** out) {
     if (m == nullptr || out == nullptr || n_ctx <= 0) return fail(SLLM_CUDA_ERR_ARG, "ctx_new: bad arguments");
+    if (kv_type != SLLM_CUDA_KV_F32 && kv_type != SLLM_CUDA_KV_F16)
+        return fail(SLLM_CUDA_ERR_ARG, "ctx_new: kv_type %d is neither SLLM_CUDA_KV_F32 nor SLLM_CUDA_KV_F16", kv_type);
     *out = nullptr;
     if (n_ctx > attention_max_ctx())
         return fail(SLLM_CUDA_ERR_TOO_LARGE, "ctx_new: n_ctx %d above %d", n_ctx, attention_max_ctx());
@@ -783,12 +799,13 @@ extern "C" int sllm_cuda_ctx_new(const sllm_cuda_model* m, int32_t n_ctx, sllm_c
     auto* c = new sllm_cuda_ctx();
     c->m = m;
     c->n_ctx = n_ctx;
-    const size_t kv = (size_t)m->n_layer * (size_t)m->n_embd_gqa * (size_t)n_ctx;
+    c->kv_f16 = kv_type == SLLM_CUDA_KV_F16 ? 1 : 0;
+    const size_t kvb = (size_t)m->n_layer * (size_t)m->n_embd_gqa * (size_t)n_ctx * kv_elt(c);   // bytes of each cache
     const size_t E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa, V = m->n_vocab;
     c->lm_grid = lm_head_grid(num_sms_of(m->device));
     cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
     auto A = [&](void** p, size_t bytes) { if (e == cudaSuccess) e = dev_malloc(p, bytes); };
-    A((void**)&c->k_cache, kv * 4); A((void**)&c->v_cache, kv * 4);
+    A((void**)&c->k_cache, kvb); A((void**)&c->v_cache, kvb);
     A((void**)&c->rope_cos, (size_t)n_ctx * 64 * 4); A((void**)&c->rope_sin, (size_t)n_ctx * 64 * 4);
     A((void**)&c->x, E * 4); A((void**)&c->q, E * 4); A((void**)&c->k, G * 4); A((void**)&c->v, G * 4);
     A((void**)&c->attn, E * 4); A((void**)&c->ffn_inp, E * 4); A((void**)&c->h, F * 4);
@@ -800,8 +817,8 @@ extern "C" int sllm_cuda_ctx_new(const sllm_cuda_model* m, int32_t n_ctx, sllm_c
     if (e == cudaSuccess) e = cudaMallocHost(&c->pinned, 64);
     if (e == cudaSuccess) e = cudaEventCreate(&c->run_ev[0]);
     if (e == cudaSuccess) e = cudaEventCreate(&c->run_ev[1]);
-    if (e == cudaSuccess) e = cudaMemset(c->k_cache, 0, kv * 4);
-    if (e == cudaSuccess) e = cudaMemset(c->v_cache, 0, kv * 4);
+    if (e == cudaSuccess) e = cudaMemset(c->k_cache, 0, kvb);
+    if (e == cudaSuccess) e = cudaMemset(c->v_cache, 0, kvb);
     if (e == cudaSuccess) e = cudaMemset(c->counter, 0, 4);
     if (e == cudaSuccess) e = cudaMemset(c->pos, 0, 4);
     if (e == cudaSuccess) e = cudaMemset(c->tok_seq, 0, (size_t)n_ctx * 4 + 4);
@@ -822,9 +839,9 @@ extern "C" void sllm_cuda_ctx_reset(sllm_cuda_ctx* c) {
     // written before it is read); clearing the cache is defence in depth,
     // as in src/forward.c:530-562.
     cudaSetDevice(c->m->device);
-    const size_t kv = (size_t)c->m->n_layer * (size_t)c->m->n_embd_gqa * (size_t)c->n_ctx;
-    cudaMemsetAsync(c->k_cache, 0, kv * 4, c->stream);
-    cudaMemsetAsync(c->v_cache, 0, kv * 4, c->stream);
+    const size_t kvb = (size_t)c->m->n_layer * (size_t)c->m->n_embd_gqa * (size_t)c->n_ctx * kv_elt(c);
+    cudaMemsetAsync(c->k_cache, 0, kvb, c->stream);
+    cudaMemsetAsync(c->v_cache, 0, kvb, c->stream);
     cudaStreamSynchronize(c->stream);
     c->n_past = 0;
     c->have_logits = false;
@@ -901,12 +918,12 @@ static cudaError_t enqueue_step(sllm_cuda_ctx* c, cudaStream_t st) {
         lp.n_ctx = c->n_ctx; lp.fallback_count = fb; lp.force_fallback = g_force_fallback;
         return launch_lm_head(lp, c->lm_grid, st);
     }
-    const size_t kv_layer = (size_t)m->n_embd_gqa * (size_t)c->n_ctx;
     for (int l = 0; l < m->n_layer; ++l) {
         AttnParams ap{};
         ap.q = c->q; ap.k = c->k; ap.v = c->v;
-        ap.k_cache = c->k_cache + (size_t)l * kv_layer;
-        ap.v_cache = c->v_cache + (size_t)l * kv_layer;
+        ap.k_cache = kv_layer_ptr(c, c->k_cache, l);
+        ap.v_cache = kv_layer_ptr(c, c->v_cache, l);
+        ap.kv_f16 = c->kv_f16;
         ap.rope_cos = c->rope_cos; ap.rope_sin = c->rope_sin;
         ap.pos_ptr = c->pos; ap.out = c->attn; ap.n_ctx = c->n_ctx;
         ap.group = m->n_head / m->n_head_kv;
@@ -1071,15 +1088,26 @@ extern "C" int sllm_cuda_ctx_kv_export(const sllm_cuda_ctx* c, float* k_out, flo
     const size_t D = m->head_dim, N = c->n_ctx, P = c->n_past;
     const size_t heads = (size_t)m->n_layer * (size_t)m->n_head_kv;
     if (P == 0) return SLLM_CUDA_OK;
-    std::vector<float> kt(D * P);
+    const size_t eb = kv_elt(c);
+    std::vector<unsigned char> kt(D * P * eb), vt(P * D * eb);
+    const char* kbase = reinterpret_cast<const char*>(c->k_cache);
+    const char* vbase = reinterpret_cast<const char*>(c->v_cache);
+    // an f16 cache's values widen exactly
+    auto val = [&](const unsigned char* b, size_t i) {
+        return eb == 4 ? reinterpret_cast<const float*>(b)[i] : __half2float(reinterpret_cast<const __half*>(b)[i]);
+    };
     for (size_t lh = 0; lh < heads; ++lh) {
-        const float* kd = c->k_cache + lh * D * N;        // [dim][n_ctx]
-        const float* vd = c->v_cache + lh * N * D;        // [n_ctx][dim]
-        CK(cudaMemcpy2D(kt.data(), P * 4, kd, N * 4, P * 4, D, cudaMemcpyDeviceToHost), "kv_export K");
-        CK(cudaMemcpy(v_out + lh * N * D, vd, P * D * 4, cudaMemcpyDeviceToHost), "kv_export V");
+        const char* kd = kbase + lh * D * N * eb;          // [dim][n_ctx]
+        const char* vd = vbase + lh * N * D * eb;          // [n_ctx][dim]
+        CK(cudaMemcpy2D(kt.data(), P * eb, kd, N * eb, P * eb, D, cudaMemcpyDeviceToHost), "kv_export K");
+        CK(cudaMemcpy(vt.data(), vd, P * D * eb, cudaMemcpyDeviceToHost), "kv_export V");
         float* kh = k_out + lh * N * D;                    // [pos][dim]
+        float* vh = v_out + lh * N * D;
         for (size_t pos = 0; pos < P; ++pos)
-            for (size_t d = 0; d < D; ++d) kh[pos * D + d] = kt[d * P + pos];
+            for (size_t d = 0; d < D; ++d) {
+                kh[pos * D + d] = val(kt.data(), d * P + pos);
+                vh[pos * D + d] = val(vt.data(), pos * D + d);
+            }
     }
     return SLLM_CUDA_OK;
 }
@@ -1104,21 +1132,33 @@ extern "C" int sllm_cuda_ctx_kv_import(sllm_cuda_ctx* c, const float* k_in, cons
     const sllm_cuda_model* m = c->m;
     const size_t D = m->head_dim, N = c->n_ctx, P = n_past;
     const size_t heads = (size_t)m->n_layer * (size_t)m->n_head_kv;
-    std::vector<float> kt(D * (P > 0 ? P : 1));
+    const size_t eb = kv_elt(c);
+    std::vector<unsigned char> kt(D * (P > 0 ? P : 1) * eb), vt((P > 0 ? P : 1) * D * eb);
+    char* kbase = reinterpret_cast<char*>(c->k_cache);
+    char* vbase = reinterpret_cast<char*>(c->v_cache);
+    // an f16 cache stores each value rounded to the nearest half (ties to even)
+    auto put = [&](unsigned char* b, size_t i, float v) {
+        if (eb == 4) reinterpret_cast<float*>(b)[i] = v;
+        else reinterpret_cast<__half*>(b)[i] = __float2half_rn(v);
+    };
     for (size_t lh = 0; lh < heads; ++lh) {
-        float* kd = c->k_cache + lh * D * N;
-        float* vd = c->v_cache + lh * N * D;
+        char* kd = kbase + lh * D * N * eb;
+        char* vd = vbase + lh * N * D * eb;
         if (P > 0) {
             const float* kh = k_in + lh * N * D;
+            const float* vh = v_in + lh * N * D;
             for (size_t pos = 0; pos < P; ++pos)
-                for (size_t d = 0; d < D; ++d) kt[d * P + pos] = kh[pos * D + d];
-            CK(cudaMemcpy2D(kd, N * 4, kt.data(), P * 4, P * 4, D, cudaMemcpyHostToDevice), "kv_import K");
-            CK(cudaMemcpy(vd, v_in + lh * N * D, P * D * 4, cudaMemcpyHostToDevice), "kv_import V");
+                for (size_t d = 0; d < D; ++d) {
+                    put(kt.data(), d * P + pos, kh[pos * D + d]);
+                    put(vt.data(), pos * D + d, vh[pos * D + d]);
+                }
+            CK(cudaMemcpy2D(kd, N * eb, kt.data(), P * eb, P * eb, D, cudaMemcpyHostToDevice), "kv_import K");
+            CK(cudaMemcpy(vd, vt.data(), P * D * eb, cudaMemcpyHostToDevice), "kv_import V");
         }
         // positions past n_past read as absent (src/forward.c:1104-1118)
         if (P < N) {
-            CK(cudaMemset2D(kd + P, N * 4, 0, (N - P) * 4, D), "kv_import clear K");
-            CK(cudaMemset(vd + P * D, 0, (N - P) * D * 4), "kv_import clear V");
+            CK(cudaMemset2D(kd + P * eb, N * eb, 0, (N - P) * eb, D), "kv_import clear K");
+            CK(cudaMemset(vd + P * D * eb, 0, (N - P) * D * eb), "kv_import clear V");
         }
     }
     if (P > 0) {
@@ -1207,7 +1247,8 @@ static int decode_program(sllm_cuda_ctx* c) {
     const sllm_cuda_model* m = c->m;
     if (c->eng_decode.built) return SLLM_CUDA_OK;
     const int E = m->n_embd, F = m->n_ff, G = m->n_embd_gqa;
-    if (!engine_supports(engine_wpl(E), engine_wpl(F)) || c->n_ctx > kEngAttnMaxCtx || m->head_dim != 128)
+    if (!engine_supports(engine_wpl(E), engine_wpl(F)) || c->n_ctx > kEngAttnMaxCtx || m->head_dim != 128 ||
+        (c->kv_f16 && !engine_supports_kv16(engine_wpl(E), engine_wpl(F))))
         return SLLM_CUDA_OK;
     int* fb = fallback_counter();
     std::vector<EngGroup> groups;
@@ -1222,7 +1263,6 @@ static int decode_program(sllm_cuda_ctx* c) {
         o.ws = ws; o.ws2 = ws2;
         ops.push_back(o);
     };
-    const size_t kv_layer = (size_t)G * (size_t)c->n_ctx;
     for (int l = 0; l < m->n_layer; ++l) {
         const DevLayer& L = m->layers[l];
         stage_first.push_back((int)ops.size());
@@ -1233,8 +1273,9 @@ static int decode_program(sllm_cuda_ctx* c) {
         stage_first.push_back((int)ops.size());
         AttnParams ap{};
         ap.q = c->q; ap.k = c->k; ap.v = c->v;
-        ap.k_cache = c->k_cache + (size_t)l * kv_layer;
-        ap.v_cache = c->v_cache + (size_t)l * kv_layer;
+        ap.k_cache = kv_layer_ptr(c, c->k_cache, l);
+        ap.v_cache = kv_layer_ptr(c, c->v_cache, l);
+        ap.kv_f16 = c->kv_f16;
         ap.rope_cos = c->rope_cos; ap.rope_sin = c->rope_sin;
         ap.pos_ptr = c->pos; ap.out = c->attn; ap.n_ctx = c->n_ctx;
         ap.group = m->n_head / m->n_head_kv;
@@ -1256,8 +1297,10 @@ static int decode_program(sllm_cuda_ctx* c) {
     if (engine_smem_bytes((int)groups.size(), (int)ops.size(), (int)stage_first.size() - 1, (int)attn.size()) == 0)
         return SLLM_CUDA_OK;       // too many layers for the tables: the per-GEMV step
     g_engine_eps = m->eps;
-    return engine_program_build(c->eng_decode, groups, ops, stage_first, m->device, c->stream, fb, engine_wpl(E),
-                                engine_wpl(F), &attn, false);
+    const int rc = engine_program_build(c->eng_decode, groups, ops, stage_first, m->device, c->stream, fb,
+                                        engine_wpl(E), engine_wpl(F), &attn, false);
+    c->eng_decode.params.kv16 = c->kv_f16;     // the instance whose attention reads f16 caches
+    return rc;
 }
 
 // ---------------------------------------------------------------------------

@@ -10,8 +10,8 @@ struct AttnParams {
     const float* q;          // [n_head * 128] projected, before RoPE
     const float* k;          // [n_head_kv * 128]
     const float* v;          // [n_head_kv * 128]
-    float* k_cache;          // this layer: [n_head_kv][128][n_ctx] (K stored transposed)
-    float* v_cache;          // this layer: [n_head_kv][n_ctx][128]
+    float* k_cache;          // this layer: [n_head_kv][128][n_ctx] (K stored transposed); __half when kv_f16
+    float* v_cache;          // this layer: [n_head_kv][n_ctx][128]; __half when kv_f16
     const float* rope_cos;   // [n_ctx][64]
     const float* rope_sin;   // [n_ctx][64]
     const int32_t* pos_ptr;  // absolute position of the query (device)
@@ -21,6 +21,7 @@ struct AttnParams {
     float attn_scale;        // 1.0f / sqrtf(128.0f)
     int* fallback_count;     // nullable
     int force_fallback;
+    int kv_f16;              // 1: the cache holds f16 (the fp16 KV option), 0: f32 (the reference's)
 };
 
 struct LmParams {

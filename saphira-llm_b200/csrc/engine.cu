@@ -24,6 +24,8 @@
 // every barrier, so the kernel always terminates; the producer then waits
 // (bounded) for its own copies in flight before it exits.
 
+#include <type_traits>
+
 #include "attn.cuh"
 #include "common.cuh"
 #include "engine.cuh"
@@ -498,7 +500,7 @@ __device__ __forceinline__ void eng_skip_op(const EngOp& op, int r0, int r_end, 
 // the kernel: WA, WB are the two row widths (in 32-bit words per lane) of a
 // model's programs -- n_embd (every projection but down) and n_ff (down)
 // ---------------------------------------------------------------------------
-template <int WA, int WB>
+template <int WA, int WB, bool KV16>
 __global__ void __launch_bounds__(kEngThreads, 1)
 i2s_engine_kernel(const EngParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -560,14 +562,17 @@ i2s_engine_kernel(const EngParams P) {
                         // will read (positions < pos), into L2 a stage ahead
                         const AttnParams& ap = s_attn[s_ops[o].group];
                         const int pos = *(volatile const int32_t*)ap.pos_ptr;
+                        const uint32_t eb = ap.kv_f16 ? 2u : 4u;     // bytes per cached value
                         for (int h = r; h < r + n && pos > 0; ++h) {
                             const int kvh = h / ap.group;
-                            const float* vC = ap.v_cache + (size_t)kvh * ap.n_ctx * 128;
-                            prefetch_l2(vC, (uint32_t)pos * 128u * 4u);
-                            if ((ap.n_ctx & 3) == 0) {
-                                const float* kT = ap.k_cache + (size_t)kvh * 128 * ap.n_ctx;
-                                const uint32_t bytes = ((uint32_t)pos * 4u + 15u) & ~15u;
-                                for (int d = 0; d < 128; ++d) prefetch_l2(kT + (size_t)d * ap.n_ctx, bytes);
+                            const char* vC = reinterpret_cast<const char*>(ap.v_cache) +
+                                             (size_t)kvh * ap.n_ctx * 128 * eb;
+                            prefetch_l2(vC, (uint32_t)pos * 128u * eb);
+                            if (((size_t)ap.n_ctx * eb) % 16 == 0) {
+                                const char* kT = reinterpret_cast<const char*>(ap.k_cache) +
+                                                 (size_t)kvh * 128 * ap.n_ctx * eb;
+                                const uint32_t bytes = ((uint32_t)pos * eb + 15u) & ~15u;
+                                for (int d = 0; d < 128; ++d) prefetch_l2(kT + (size_t)d * ap.n_ctx * eb, bytes);
                             }
                         }
                         continue;
@@ -657,8 +662,8 @@ i2s_engine_kernel(const EngParams P) {
                 float* sc = reinterpret_cast<float*>(qs);
                 float* hq = sc + kEngAttnMaxCtx;
                 for (int head = r; head < r_end; ++head)
-                    attention_head<kEngConsumerWarps * 32>(s_attn[op.group], head, tid, sc, hq, hq + kHeadDim,
-                                                           es.fred, es.dred, ConsumerSync());
+                    attention_head_t<kEngConsumerWarps * 32, typename std::conditional<KV16, __half, float>::type>(
+                        s_attn[op.group], head, tid, sc, hq, hq + kHeadDim, es.fred, es.dred, ConsumerSync());
                 consumer_sync();
                 cur_group = -1;
                 continue;
@@ -689,6 +694,8 @@ i2s_engine_kernel(const EngParams P) {
 // the (WA, WB) pairs compiled in: the 2B-4T model and the widths the tests use
 #define SLLM_ENGINE_SHAPES(X) \
     X(5, 14) X(1, 1) X(1, 2) X(1, 3) X(2, 6) X(3, 6) X(16, 16) X(16, 14) X(16, 7) X(16, 8) X(16, 4) X(16, 2)
+// and the pairs with an fp16-KV instance (the single-GPU decode step's widths)
+#define SLLM_ENGINE_KV16_SHAPES(X) X(5, 14) X(1, 1) X(1, 2) X(1, 3) X(2, 6) X(3, 6)
 
 // ---------------------------------------------------------------------------
 // host side
@@ -735,6 +742,13 @@ bool engine_supports(int wa, int wb) {
     return false;
 }
 
+bool engine_supports_kv16(int wa, int wb) {
+#define SLLM_ENG_SUP16(A, B) if (wa == A && wb == B) return true;
+    SLLM_ENGINE_KV16_SHAPES(SLLM_ENG_SUP16)
+#undef SLLM_ENG_SUP16
+    return false;
+}
+
 cudaError_t engine_test_faults(int skip_arrival_cta, double wait_ms) {
     const unsigned long long ns =
         wait_ms > 0.0 ? (unsigned long long)(wait_ms * 1.0e6) : (unsigned long long)kEngWaitNs;
@@ -755,16 +769,22 @@ cudaError_t prepare_engine() {
     // part must fit the reserve
     const int bytes = kEngDynLimit;
     cudaError_t e = cudaSuccess;
-#define SLLM_ENG_PREP(A, B)                                                                                     \
+#define SLLM_ENG_PREP_ONE(A, B, KV)                                                                             \
     if (e == cudaSuccess) {                                                                                      \
         cudaFuncAttributes fa{};                                                                                 \
-        e = cudaFuncGetAttributes(&fa, i2s_engine_kernel<A, B>);                                                 \
+        e = cudaFuncGetAttributes(&fa, i2s_engine_kernel<A, B, KV>);                                             \
         if (e == cudaSuccess && fa.sharedSizeBytes + (size_t)bytes > 227u * 1024u) e = cudaErrorInvalidValue;    \
         if (e == cudaSuccess)                                                                                    \
-            e = cudaFuncSetAttribute(i2s_engine_kernel<A, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); \
+            e = cudaFuncSetAttribute(i2s_engine_kernel<A, B, KV>, cudaFuncAttributeMaxDynamicSharedMemorySize,     \
+                                     bytes);                                                                     \
     }
+#define SLLM_ENG_PREP(A, B) SLLM_ENG_PREP_ONE(A, B, false)
+#define SLLM_ENG_PREP16(A, B) SLLM_ENG_PREP_ONE(A, B, true)
     SLLM_ENGINE_SHAPES(SLLM_ENG_PREP)
+    SLLM_ENGINE_KV16_SHAPES(SLLM_ENG_PREP16)
+#undef SLLM_ENG_PREP16
 #undef SLLM_ENG_PREP
+#undef SLLM_ENG_PREP_ONE
     return e;
 }
 
@@ -789,8 +809,15 @@ cudaError_t launch_engine(const EngParams& p, int grid, cudaStream_t st, int wa,
     }
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (p.kv16) {
+#define SLLM_ENG_LAUNCH16(A, B) \
+        if (wa == A && wb == B) return cudaLaunchKernelEx(&cfg, i2s_engine_kernel<A, B, true>, p);
+        SLLM_ENGINE_KV16_SHAPES(SLLM_ENG_LAUNCH16)
+#undef SLLM_ENG_LAUNCH16
+        return cudaErrorNotSupported;
+    }
 #define SLLM_ENG_LAUNCH(A, B) \
-    if (wa == A && wb == B) return cudaLaunchKernelEx(&cfg, i2s_engine_kernel<A, B>, p);
+    if (wa == A && wb == B) return cudaLaunchKernelEx(&cfg, i2s_engine_kernel<A, B, false>, p);
     SLLM_ENGINE_SHAPES(SLLM_ENG_LAUNCH)
 #undef SLLM_ENG_LAUNCH
     return cudaErrorNotSupported;

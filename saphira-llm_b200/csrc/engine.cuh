@@ -76,6 +76,7 @@ struct EngParams {
     int force_fallback;
     const AttnParams* attn;      // [n_attn]: the attention ops' layers
     int n_attn;
+    int kv16;                    // the attention ops' caches hold f16 (a separate kernel instance)
 };
 
 enum EngError { ENG_OK = 0, ENG_TIMEOUT_FULL = 1, ENG_TIMEOUT_EMPTY = 2, ENG_TIMEOUT_GRID = 3, ENG_BAD_PROGRAM = 4 };
@@ -90,6 +91,8 @@ int engine_grid(int device);
 // wpl(K) = 32-bit words per lane = ceil(K / 512)
 int engine_wpl(int K);
 bool engine_supports(int wa, int wb);
+// the pairs that also have an instance for f16 KV caches
+bool engine_supports_kv16(int wa, int wb);
 // a compiled pair whose first width is `wpl` (for programs of one width)
 bool engine_pair_for_width(int wpl, int* wa, int* wb);
 cudaError_t prepare_engine();     // once, outside any stream capture

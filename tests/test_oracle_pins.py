@@ -245,3 +245,22 @@ def test_oracle_matches_committed_fixtures(orc, synth):
         rc, toks = oc.generate(np.array(case["prompt"], np.int32), case["n_new"])
         assert rc == 0 and toks.tolist() == case["tokens"], case["name"]
         assert fixtures.fnv1a64(bits(oc.last_logits()).tobytes()) == case["last_logits_fnv"], case["name"]
+
+
+def test_fp16_rounding_matches_numpy(orc):
+    """The oracle's float -> half conversion (its fp16-KV variant, not part of
+    the reference) is IEEE round-to-nearest-even: numpy's astype(float16) on
+    every float of a seeded sample, the half boundaries, the subnormal range,
+    ties and overflow."""
+    rng = np.random.default_rng(5)
+    xs = np.concatenate([
+        rng.standard_normal(20000).astype(np.float32) * np.float32(3.0),
+        (rng.standard_normal(5000) * 1e-5).astype(np.float32),
+        (rng.standard_normal(5000) * 3e4).astype(np.float32),
+        np.array([0.0, -0.0, 65504.0, 65519.996, 65520.0, -65520.0, 1e9, np.inf, -np.inf,
+                  2.0 ** -24, 2.0 ** -25, 3 * 2.0 ** -26, 2.0 ** -14, 2.0 ** -14 * 1.00048828125,
+                  1.0 + 2.0 ** -11, 1.0 + 3 * 2.0 ** -11, 6.1035156e-05, 5.9604645e-08], np.float32),
+    ])
+    got = np.array([orc.fp32_to_fp16(v) for v in xs], np.uint16)
+    want = xs.astype(np.float16).view(np.uint16)
+    assert np.array_equal(got, want)
