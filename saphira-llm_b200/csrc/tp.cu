@@ -763,8 +763,11 @@ extern "C" int sllm_cuda_tp_model_upload(const sllm_cuda_model_desc* d, int32_t 
     if (rc != SLLM_CUDA_OK) { delete m; return rc; }
     const int E = m->E, F = m->F, D = kHeadDim, G = m->Hkv * D;
     std::vector<uint8_t> buf;
-    Uploader up(device);     // pinned, double-buffered staging (the slices are re-packed in buf first)
-    auto put = [&](const void* dst, const void* src, size_t n) { return up.put(const_cast<void*>(dst), src, n); };
+    Uploader up(device);     // pinned, double-buffered staging
+    // the slices are re-packed in buf, which the next slice reuses
+    auto put = [&](const void* dst, const void* src, size_t n) {
+        return up.put(const_cast<void*>(dst), src, n, src == buf.data());
+    };
     cudaError_t e = cudaSuccess;
     for (int l = 0; l < m->n_layer && e == cudaSuccess; ++l) {
         const sllm_cuda_layer_desc& h = d->layers[l];

@@ -9,22 +9,35 @@ namespace sllm {
 
 namespace {
 
-// a large host copy split over a few threads (one thread moves ~10 GB/s)
-void parallel_memcpy(unsigned char* dst, const unsigned char* src, size_t n) {
-    constexpr size_t kMinPerThread = 4u << 20;
+// Copy the pieces' source bytes to buf + piece.off, over a few threads: the
+// batch's bytes are cut into equal contiguous shares, each thread copying the
+// parts of the pieces that fall in its share (one thread moves ~10 GB/s).
+template <class P>
+void fill_batch(unsigned char* buf, const std::vector<P>& pieces) {
+    size_t total = 0;
+    for (const P& p : pieces) total += p.src != nullptr ? p.n : 0;
+    if (total == 0) return;
+    constexpr size_t kMinPerThread = 2u << 20;
     const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-    const size_t t = std::min<size_t>({(size_t)8, (size_t)hw, std::max<size_t>(1, n / kMinPerThread)});
-    if (t <= 1) {
-        std::memcpy(dst, src, n);
-        return;
-    }
+    const size_t t = std::min<size_t>({(size_t)16, (size_t)hw, std::max<size_t>(1, total / kMinPerThread)});
+    const size_t share = (total + t - 1) / t;
+    auto work = [&](size_t lo, size_t hi) {        // bytes [lo, hi) of the batch, in piece order
+        size_t at = 0;
+        for (const P& p : pieces) {
+            if (p.src == nullptr) continue;      // copied at put()
+            const size_t a = std::max(lo, at), b = std::min(hi, at + p.n);
+            if (a < b)
+                std::memcpy(buf + p.off + (a - at), static_cast<const unsigned char*>(p.src) + (a - at), b - a);
+            at += p.n;
+            if (at >= hi) break;
+        }
+    };
     std::vector<std::thread> ths;
-    const size_t per = (n + t - 1) / t;
     for (size_t i = 1; i < t; ++i) {
-        const size_t a = i * per, b = std::min(n, a + per);
-        if (a < b) ths.emplace_back([=] { std::memcpy(dst + a, src + a, b - a); });
+        const size_t lo = i * share, hi = std::min(total, lo + share);
+        if (lo < hi) ths.emplace_back(work, lo, hi);
     }
-    std::memcpy(dst, src, std::min(n, per));
+    work(0, std::min(total, share));
     for (auto& th : ths) th.join();
 }
 
@@ -59,6 +72,7 @@ cudaError_t Uploader::acquire() {
 
 cudaError_t Uploader::flush() {
     if (pieces_.empty()) return cudaSuccess;
+    fill_batch(buf_[cur_], pieces_);
     for (const Piece& p : pieces_) {
         const cudaError_t e = cudaMemcpyAsync(p.dst, buf_[cur_] + p.off, p.n, cudaMemcpyHostToDevice, stream_);
         if (e != cudaSuccess) return e;
@@ -72,7 +86,7 @@ cudaError_t Uploader::flush() {
     return acquire();
 }
 
-cudaError_t Uploader::put(void* dst, const void* src, size_t bytes) {
+cudaError_t Uploader::put(void* dst, const void* src, size_t bytes, bool transient) {
     if (err_ != cudaSuccess) return err_;
     total_ += bytes;
     auto* d = static_cast<unsigned char*>(dst);
@@ -81,8 +95,8 @@ cudaError_t Uploader::put(void* dst, const void* src, size_t bytes) {
         if (used_ == kStageBytes && (err_ = flush()) != cudaSuccess) return err_;
         // 256-byte alignment of each piece inside the buffer keeps the copies fast
         const size_t n = std::min(bytes, kStageBytes - used_);
-        parallel_memcpy(buf_[cur_] + used_, s, n);
-        pieces_.push_back(Piece{d, used_, n});
+        if (transient) std::memcpy(buf_[cur_] + used_, s, n);
+        pieces_.push_back(Piece{d, transient ? nullptr : s, used_, n});
         used_ = std::min(kStageBytes, (used_ + n + 255) & ~(size_t)255);
         d += n;
         s += n;

@@ -9,24 +9,29 @@
 
 namespace sllm {
 
-// Two pinned buffers of kStageBytes. While the device copies one buffer in
-// (an async copy on the uploader's stream), host threads fill the other from
-// the source tensors. Small tensors are packed into one buffer and go up with
-// one copy each from it. Copies larger than a buffer stream through both in
-// turn. finish() waits for the last copy and reports the first error.
+// Two pinned buffers of kStageBytes. Queued copies are packed into the
+// current buffer's batch without being touched; when the batch is full, a
+// team of host threads copies it into the buffer (each thread a contiguous
+// share of the batch's bytes, whatever the tensor boundaries), and one async
+// copy per piece sends it up while the next batch fills the other buffer.
+// Copies larger than a buffer stream through both in turn. finish() sends the
+// last batch, waits, and reports the first error.
 class Uploader {
 public:
     static constexpr size_t kStageBytes = 64u << 20;
     explicit Uploader(int device);
     ~Uploader();
-    // queue a copy of `bytes` from host `src` to device `dst`
-    cudaError_t put(void* dst, const void* src, size_t bytes);
+    // queue a copy of `bytes` from host `src` to device `dst`. The source is
+    // read when its batch is sent (by finish() at the latest) and must stay
+    // valid until then, unless `transient`: then it is copied into the
+    // staging buffer before put returns and may be reused at once.
+    cudaError_t put(void* dst, const void* src, size_t bytes, bool transient = false);
     cudaError_t finish();
     size_t bytes() const { return total_; }
 
 private:
-    struct Piece { void* dst; size_t off; size_t n; };
-    cudaError_t flush();             // send the current buffer's pieces
+    struct Piece { void* dst; const void* src; size_t off; size_t n; };   // src null: already in the buffer
+    cudaError_t flush();             // fill the current buffer and send its pieces
     cudaError_t acquire();           // make the current buffer free to fill
     cudaStream_t stream_ = nullptr;
     unsigned char* buf_[2] = {nullptr, nullptr};

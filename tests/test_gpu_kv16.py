@@ -63,3 +63,19 @@ def test_kv16_state_round_trip(cuda, orc, synth, tmp_path):
     a.close()
     b.close()
     model.close()
+
+
+def test_kv16_2b_shape_matches_rounded_oracle(cuda, orc, synth):
+    """The 2B-4T widths: the fp16 instance of the engine the benchmark runs."""
+    cfg = synth.Config(n_layer=2)
+    m = synth.SynthModel(cfg, seed=2024)
+    model = cuda.Model(m.desc())
+    c16 = model.ctx(40, kv_f16=True)
+    o16 = orc.ctx(m.desc(), 40, kv_f16=True)
+    prompt = np.random.default_rng(4).integers(0, cfg.n_vocab, 6).astype(np.int32)
+    r1, t1 = c16.generate(prompt, 4)
+    r2, t2 = o16.generate(prompt, 4)
+    assert r1 == r2 == 0 and t1.tolist() == t2.tolist()
+    assert np.array_equal(bits(c16.last_logits()), bits(o16.last_logits()))
+    c16.close()
+    model.close()
