@@ -46,6 +46,11 @@ SLLM_CUDA_API int sllm_cuda_test_tp_uses_engine(const sllm_cuda_tp_ctx * c);
  * engine, 0 otherwise */
 SLLM_CUDA_API int sllm_cuda_test_tp_fused_layers(const sllm_cuda_tp_ctx * c);
 
+/* 1 when the context's step runs the fused peer exchange: per layer one
+ * program that stores its results into every rank's memory and waits on
+ * flags inside its stages, instead of separate exchange kernels */
+SLLM_CUDA_API int sllm_cuda_test_tp_fused_exchange(const sllm_cuda_tp_ctx * c);
+
 /* how the context exchanges between ranks: 0 none (one rank), 1 NCCL
  * collectives, 2 the one-shot peer-memory exchange */
 SLLM_CUDA_API int sllm_cuda_test_tp_exchange_kind(const sllm_cuda_tp_ctx * c);

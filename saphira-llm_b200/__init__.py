@@ -70,6 +70,7 @@ def lib():
     L.sllm_cuda_test_tp_uses_engine.argtypes = [vp]
     L.sllm_cuda_test_tp_fused_layers.argtypes = [vp]
     L.sllm_cuda_test_tp_exchange_kind.argtypes = [vp]
+    L.sllm_cuda_test_tp_fused_exchange.argtypes = [vp]
     L.sllm_cuda_model_upload.argtypes = [C.POINTER(abi.ModelDesc), C.c_int, C.POINTER(vp)]
     L.sllm_cuda_model_free.argtypes = [vp]
     L.sllm_cuda_model_weight_bytes.argtypes = [vp]
@@ -427,6 +428,9 @@ class TpCtx:
 
     def fused_layers(self):
         return int(lib().sllm_cuda_test_tp_fused_layers(self.h))
+
+    def fused_exchange(self):
+        return bool(lib().sllm_cuda_test_tp_fused_exchange(self.h))
 
     def exchange_kind(self):
         """'none' (one rank), 'nccl' or 'p2p' (the one-shot peer-memory exchange)."""

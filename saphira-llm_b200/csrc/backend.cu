@@ -540,6 +540,7 @@ std::vector<EngCursor> sllm::engine_starts(const std::vector<EngOp>& ops, const 
     // the heads of a layer spread over separate CTAs
     auto row_cost = [&](int o) {
         if (ops[o].epi == kEpiAttention) return 65536.0;
+        if (ops[o].epi == kEpiReduce) return 4.0 * ops[o].K;       // its slots' int32 words
         return (double)(ops[o].K / 4) * (ops[o].epi == EPI_SILU ? 2 : 1);
     };
     for (int s = 0; s < n_stages; ++s) {
@@ -602,7 +603,8 @@ extern "C" int sllm_cuda_test_engine_split(const int32_t* rows, const int32_t* K
         if (stage_first[s + 1] < stage_first[s]) return fail(SLLM_CUDA_ERR_ARG, "engine_split: stages out of order");
     std::vector<EngOp> ops((size_t)n_ops);
     for (int i = 0; i < n_ops; ++i) {
-        if (rows[i] < 1 || K[i] < 4 || epi[i] < 0 || epi[i] > kEpiAttention || group[i] < 0)
+        if (rows[i] < 1 || K[i] < 1 || epi[i] < 0 || epi[i] > kEpiReduce || group[i] < 0 ||
+            (K[i] < 4 && epi[i] != kEpiReduce))
             return fail(SLLM_CUDA_ERR_ARG, "engine_split: bad op %d", i);
         ops[i].rows = rows[i]; ops[i].K = K[i]; ops[i].epi = epi[i]; ops[i].group = group[i];
     }

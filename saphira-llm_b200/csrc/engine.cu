@@ -175,6 +175,55 @@ __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// --- exchange with peers (XCH instances) -------------------------------------
+__device__ __forceinline__ uint32_t x_ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void x_st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned x_atom_add_acq_rel(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// this rank has published exchange `kind` with value `val`: flag[kind][rank]
+// of every rank's region (its own included)
+__device__ __forceinline__ void x_signal(const EngX& x, int kind, uint32_t val) {
+    for (int q = 0; q < x.n_peer; ++q) {
+        uint32_t* f = reinterpret_cast<uint32_t*>(x.peer[q] + x.flag_off) + kind * kEngMaxPeers + x.rank;
+        x_st_release_sys(f, val);
+    }
+}
+
+// every rank has published `kind` up to `val` (bounded by the wait budget;
+// at once false when an earlier wait of this context already gave up, so a
+// dead peer costs one budget, not one per exchange)
+__device__ __forceinline__ bool x_wait(const EngX& x, int kind, uint32_t val, uint64_t budget, const int* error) {
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(x.peer[x.rank] + x.flag_off) + kind * kEngMaxPeers;
+    const uint64_t t0 = gtimer();
+    for (int q = 0; q < x.n_peer; ++q) {
+        while (x_ld_acquire_sys(f + q) < val) {
+            if (gtimer() - t0 > budget || *(volatile const int*)error != 0) return false;
+            __nanosleep(32);
+        }
+    }
+    return true;
+}
+
+// the same float or int word at the same offset of every other rank's region
+template <class T>
+__device__ __forceinline__ void x_scatter(const EngX& x, const T* local, T v) {
+    const ptrdiff_t off = reinterpret_cast<const char*>(local) - x.peer[x.rank];
+    for (int q = 0; q < x.n_peer; ++q)
+        if (q != x.rank) *reinterpret_cast<T*>(x.peer[q] + off) = v;
+}
+
 // ---------------------------------------------------------------------------
 // consumer-side prologue (512 threads): int8 activations of a group into qs
 // ---------------------------------------------------------------------------
@@ -420,7 +469,7 @@ struct RingPos {
 // Every chunk of op `o` that this CTA runs in the current stage, from row r0
 // to r_end, activations loaded once into registers. The chunks follow the
 // producer's order (ChunkWalk::next): n = min(chunk_rows, r_end - r).
-template <int WPL, bool PAIR>
+template <int WPL, bool PAIR, bool XCH>
 __device__ __forceinline__ void eng_run_op(const EngOp& op, int r0, int r_end, RingPos& rp, uint8_t* ring,
                                            EngSmem& es, const int8_t* qs, int asum, float post, float post2,
                                            const EngParams& P, int warp, int lane) {
@@ -429,13 +478,18 @@ __device__ __forceinline__ void eng_run_op(const EngOp& op, int r0, int r_end, R
     float* const out = PAIR ? op.h : op.y;
     const float* const resid = op.epi == EPI_RESID ? op.resid : nullptr;
     const bool dots_out = op.epi == EPI_DOTS;
+    const bool scatter = XCH && (op.k0x & kOpScatter) != 0;
+    // the op's slice of the activations (a contraction split over ranks reads
+    // its columns of the whole quantised vector; 128-element blocks keep
+    // their lane-major layout, so a block-aligned slice is a byte offset)
+    const int8_t* qa = XCH ? qs + (op.k0x & kOpK0Mask) : qs;
     // this lane's last word lies in the row: else it reads past the row and is masked
     const uint32_t last_mask = lane + 32 * (WPL - 1) < W ? 0xffffffffu : 0u;
     int4 aq[WPL];
     #pragma unroll
     for (int i = 0; i < WPL; ++i) {
         const int wi = lane + 32 * i;
-        aq[i] = wi < W ? reinterpret_cast<const int4*>(qs)[wi] : make_int4(0, 0, 0, 0);
+        aq[i] = wi < W ? reinterpret_cast<const int4*>(qa)[wi] : make_int4(0, 0, 0, 0);
     }
     for (int r = r0; r < r_end;) {
         const int n = min(chunk_rows, r_end - r);
@@ -453,7 +507,9 @@ __device__ __forceinline__ void eng_run_op(const EngOp& op, int r0, int r_end, R
                 if (lane < R && j < n) {
                     const float g = __fmul_rn(__int2float_rn(mg - asum), post);
                     const float u = __fmul_rn(__int2float_rn(mu - asum), post2);
-                    out[r + j] = __fmul_rn(silu_block(g), u);
+                    const float hv = __fmul_rn(silu_block(g), u);
+                    out[r + j] = hv;
+                    if (scatter) x_scatter(P.x, out + r + j, hv);
                 }
             } else {
                 int dot[R];
@@ -465,11 +521,14 @@ __device__ __forceinline__ void eng_run_op(const EngOp& op, int r0, int r_end, R
                 const int j = warp + kEngConsumerWarps * lane;
                 if (lane < R && j < n) {
                     if (dots_out) {
-                        reinterpret_cast<int*>(out)[r + j] = mine;     // raw code dot (src/i2s_gemm.c:260-269)
+                        int* dp = reinterpret_cast<int*>(out) + r + j;
+                        *dp = mine;     // raw code dot (src/i2s_gemm.c:260-269)
+                        if (scatter) x_scatter(P.x, dp, mine);
                     } else {
                         float v = __fmul_rn(__int2float_rn(mine - asum), post);
                         if (resid != nullptr) v = __fadd_rn(v, __ldcg(resid + r + j));
                         out[r + j] = v;
+                        if (scatter) x_scatter(P.x, out + r + j, v);
                     }
                 }
             }
@@ -500,7 +559,7 @@ __device__ __forceinline__ void eng_skip_op(const EngOp& op, int r0, int r_end, 
 // the kernel: WA, WB are the two row widths (in 32-bit words per lane) of a
 // model's programs -- n_embd (every projection but down) and n_ff (down)
 // ---------------------------------------------------------------------------
-template <int WA, int WB, bool KV16>
+template <int WA, int WB, bool KV16, bool XCH>
 __global__ void __launch_bounds__(kEngThreads, 1)
 i2s_engine_kernel(const EngParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -521,6 +580,7 @@ i2s_engine_kernel(const EngParams P) {
     // critical path ever goes to L2 again
     {
         static_assert(sizeof(EngOp) % 8 == 0 && sizeof(EngGroup) % 4 == 0, "table copy granularity");
+        static_assert(sizeof(EngOp) == 72, "the op table's size bounds the programs that fit in shared memory");
         const int2* src = reinterpret_cast<const int2*>(P.ops);
         int2* dst = reinterpret_cast<int2*>(s_ops);
         for (int i = tid; i < (int)(P.n_ops * sizeof(EngOp) / 8); i += blockDim.x) dst[i] = __ldg(src + i);
@@ -557,6 +617,7 @@ i2s_engine_kernel(const EngParams P) {
                 ChunkWalk walk{s_ops, s_cur[2 * s].op, s_cur[2 * s].row, s_cur[2 * s + 1]};
                 int o, r, n, last_group = -1;
                 while (walk.next(o, r, n)) {
+                    if (XCH && s_ops[o].epi == kEpiReduce) continue;     // no weights
                     if (s_ops[o].epi == kEpiAttention) {
                         // no weights to stream; instead the KV cache its heads
                         // will read (positions < pos), into L2 a stage ahead
@@ -621,9 +682,11 @@ i2s_engine_kernel(const EngParams P) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     uint64_t budget = 0;
     int skip_arrival = -1;
+    uint32_t xval = 0;      // this layer's exchange value in this step (XCH)
     if (tid == 0) {
         budget = *(volatile unsigned long long*)&g_eng_wait_ns;
         skip_arrival = *(volatile int*)&g_eng_skip_arrival;
+        if (XCH) xval = *(volatile const uint32_t*)P.x.steps * (uint32_t)P.x.n_layer + (uint32_t)P.x.layer + 1u;
     }
     RingPos rp;
     int cur_group = -1;
@@ -649,6 +712,21 @@ i2s_engine_kernel(const EngParams P) {
             consumer_sync();
             cur_group = -1;
         }
+        if (XCH && s < kEngMaxXStages && (P.x.xs[s] & kXsWaitMask) != 0) {
+            // the stage reads what every rank published: after the local
+            // barrier CTA 0 publishes this rank's part, then all CTAs wait
+            // for every rank's flag (bounded)
+            if (tid == 0 && !*(volatile int*)&es.abort_flag) {
+                const int kind = (P.x.xs[s] & kXsWaitMask) - 1;
+                if ((P.x.xs[s] & kXsSignal) != 0 && c == 0) x_signal(P.x, kind, xval);
+                // a peer may still be launching its step: five budgets
+                if (!x_wait(P.x, kind, xval, 5 * budget, P.error)) {
+                    es.abort_flag = 1;
+                    atomicExch(P.error, ENG_TIMEOUT_PEER);
+                }
+            }
+            consumer_sync();
+        }
         ChunkWalk walk{s_ops, s_cur[2 * s].op, s_cur[2 * s].row, s_cur[2 * s + 1]};
         int o, r, n;
         while (walk.next(o, r, n)) {
@@ -665,29 +743,64 @@ i2s_engine_kernel(const EngParams P) {
                     attention_head_t<kEngConsumerWarps * 32, typename std::conditional<KV16, __half, float>::type>(
                         s_attn[op.group], head, tid, sc, hq, hq + kHeadDim, es.fred, es.dred, ConsumerSync());
                 consumer_sync();
+                if (XCH && (op.k0x & kOpScatter) != 0) {
+                    // this CTA's heads to every other rank's region (the
+                    // outputs just stored are visible to the CTA after the barrier)
+                    for (int i = r * kHeadDim + tid; i < r_end * kHeadDim; i += kEngConsumerWarps * 32)
+                        x_scatter(P.x, op.y + i, __ldcg(op.y + i));
+                }
                 cur_group = -1;
+                continue;
+            }
+            if (XCH && op.epi == kEpiReduce) {
+                // the epilogue of a contraction split over ranks: integer sums
+                // of the slots (exact in any order), then the single-GPU float
+                // sequence (src/forward.c:739-750, 790-801)
+                const sllm_cuda_act a = {__ldcg(&reinterpret_cast<const sllm_cuda_act*>(op.w2)->scale),
+                                         __ldcg(&reinterpret_cast<const sllm_cuda_act*>(op.w2)->sum)};
+                const float pr = __fdiv_rn(op.ws, a.scale);
+                const int32_t* slots = reinterpret_cast<const int32_t*>(op.w);
+                for (int i = r + tid; i < r_end; i += kEngConsumerWarps * 32) {
+                    int d = 0;
+                    for (int q = 0; q < op.K; ++q) d += __ldcg(slots + (size_t)q * op.rows + i);
+                    float v = __fmul_rn(__int2float_rn(d - a.sum), pr);
+                    if (op.resid != nullptr) v = __fadd_rn(v, __ldcg(op.resid + i));
+                    op.y[i] = v;
+                }
                 continue;
             }
             if (op.group != cur_group) {
                 act = eng_prologue(s_groups[op.group], P, qs, es, tid, warp, lane);
                 cur_group = op.group;
+                if (XCH && c == 0 && tid == 0 && s_groups[op.group].pro != PRO_Q8 && s_groups[op.group].act8 != nullptr)
+                    *const_cast<sllm_cuda_act*>(s_groups[op.group].act8) = act;
             }
             // per-tensor scales (src/quant.c:102-106): one division per tensor
             const float post = __fdiv_rn(op.ws, act.scale);
             const float post2 = op.epi == EPI_SILU ? __fdiv_rn(op.ws2, act.scale) : 0.0f;
             const int wpl = ((op.K >> 4) + 31) >> 5;
             if (wpl == WA && op.epi == EPI_SILU)
-                eng_run_op<WA, true>(op, r, r_end, rp, ring, es, qs, act.sum, post, post2, P, warp, lane);
+                eng_run_op<WA, true, XCH>(op, r, r_end, rp, ring, es, qs, act.sum, post, post2, P, warp, lane);
             else if (wpl == WA)
-                eng_run_op<WA, false>(op, r, r_end, rp, ring, es, qs, act.sum, post, post2, P, warp, lane);
+                eng_run_op<WA, false, XCH>(op, r, r_end, rp, ring, es, qs, act.sum, post, post2, P, warp, lane);
             else if (wpl == WB && op.epi != EPI_SILU)
-                eng_run_op<WB, false>(op, r, r_end, rp, ring, es, qs, act.sum, post, post2, P, warp, lane);
+                eng_run_op<WB, false, XCH>(op, r, r_end, rp, ring, es, qs, act.sum, post, post2, P, warp, lane);
             else
                 eng_skip_op(op, r, r_end, rp, es, P, lane);
         }
         // publish this CTA's outputs of the stage, then arrive
         consumer_sync();
+        if (XCH && tid == 0 && s < kEngMaxXStages && (P.x.xs[s] & kXsFence) != 0)
+            __threadfence_system();     // the stores into peers' regions, before the arrival that orders them
         if (tid == 0 && s + 1 < P.n_stages && !(s == 0 && c == skip_arrival)) red_release_add(P.barrier, 1u);
+    }
+    if (XCH && P.x.end_kind >= 0 && tid == 0) {
+        // the last CTA to finish publishes the kernel's exchange
+        __threadfence_system();
+        if (x_atom_add_acq_rel(P.x.done, 1u) == (unsigned)G - 1u) {
+            x_signal(P.x, P.x.end_kind, xval);
+            atomicExch(P.x.done, 0u);
+        }
     }
 }
 
@@ -696,6 +809,9 @@ i2s_engine_kernel(const EngParams P) {
     X(5, 14) X(1, 1) X(1, 2) X(1, 3) X(2, 6) X(3, 6) X(16, 16) X(16, 14) X(16, 7) X(16, 8) X(16, 4) X(16, 2)
 // and the pairs with an fp16-KV instance (the single-GPU decode step's widths)
 #define SLLM_ENGINE_KV16_SHAPES(X) X(5, 14) X(1, 1) X(1, 2) X(1, 3) X(2, 6) X(3, 6)
+// and the pairs with an instance that exchanges with peers (tensor-parallel
+// programs at n_embd 8192: the O slice at 2, 4 or 8 ranks, the down chunks)
+#define SLLM_ENGINE_XCH_SHAPES(X) X(16, 16) X(16, 14) X(16, 7) X(16, 8) X(16, 4) X(16, 2)
 
 // ---------------------------------------------------------------------------
 // host side
@@ -742,6 +858,13 @@ bool engine_supports(int wa, int wb) {
     return false;
 }
 
+bool engine_supports_xch(int wa, int wb) {
+#define SLLM_ENG_SUPX(A, B) if (wa == A && wb == B) return true;
+    SLLM_ENGINE_XCH_SHAPES(SLLM_ENG_SUPX)
+#undef SLLM_ENG_SUPX
+    return false;
+}
+
 bool engine_supports_kv16(int wa, int wb) {
 #define SLLM_ENG_SUP16(A, B) if (wa == A && wb == B) return true;
     SLLM_ENGINE_KV16_SHAPES(SLLM_ENG_SUP16)
@@ -769,19 +892,22 @@ cudaError_t prepare_engine() {
     // part must fit the reserve
     const int bytes = kEngDynLimit;
     cudaError_t e = cudaSuccess;
-#define SLLM_ENG_PREP_ONE(A, B, KV)                                                                             \
+#define SLLM_ENG_PREP_ONE(A, B, KV, X)                                                                          \
     if (e == cudaSuccess) {                                                                                      \
         cudaFuncAttributes fa{};                                                                                 \
-        e = cudaFuncGetAttributes(&fa, i2s_engine_kernel<A, B, KV>);                                             \
+        e = cudaFuncGetAttributes(&fa, i2s_engine_kernel<A, B, KV, X>);                                          \
         if (e == cudaSuccess && fa.sharedSizeBytes + (size_t)bytes > 227u * 1024u) e = cudaErrorInvalidValue;    \
         if (e == cudaSuccess)                                                                                    \
-            e = cudaFuncSetAttribute(i2s_engine_kernel<A, B, KV>, cudaFuncAttributeMaxDynamicSharedMemorySize,     \
+            e = cudaFuncSetAttribute(i2s_engine_kernel<A, B, KV, X>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
                                      bytes);                                                                     \
     }
-#define SLLM_ENG_PREP(A, B) SLLM_ENG_PREP_ONE(A, B, false)
-#define SLLM_ENG_PREP16(A, B) SLLM_ENG_PREP_ONE(A, B, true)
+#define SLLM_ENG_PREP(A, B) SLLM_ENG_PREP_ONE(A, B, false, false)
+#define SLLM_ENG_PREP16(A, B) SLLM_ENG_PREP_ONE(A, B, true, false)
+#define SLLM_ENG_PREPX(A, B) SLLM_ENG_PREP_ONE(A, B, false, true)
     SLLM_ENGINE_SHAPES(SLLM_ENG_PREP)
     SLLM_ENGINE_KV16_SHAPES(SLLM_ENG_PREP16)
+    SLLM_ENGINE_XCH_SHAPES(SLLM_ENG_PREPX)
+#undef SLLM_ENG_PREPX
 #undef SLLM_ENG_PREP16
 #undef SLLM_ENG_PREP
 #undef SLLM_ENG_PREP_ONE
@@ -811,13 +937,20 @@ cudaError_t launch_engine(const EngParams& p, int grid, cudaStream_t st, int wa,
     cfg.numAttrs = 1;
     if (p.kv16) {
 #define SLLM_ENG_LAUNCH16(A, B) \
-        if (wa == A && wb == B) return cudaLaunchKernelEx(&cfg, i2s_engine_kernel<A, B, true>, p);
+        if (wa == A && wb == B) return cudaLaunchKernelEx(&cfg, i2s_engine_kernel<A, B, true, false>, p);
         SLLM_ENGINE_KV16_SHAPES(SLLM_ENG_LAUNCH16)
 #undef SLLM_ENG_LAUNCH16
         return cudaErrorNotSupported;
     }
+    if (p.xch) {
+#define SLLM_ENG_LAUNCHX(A, B) \
+        if (wa == A && wb == B) return cudaLaunchKernelEx(&cfg, i2s_engine_kernel<A, B, false, true>, p);
+        SLLM_ENGINE_XCH_SHAPES(SLLM_ENG_LAUNCHX)
+#undef SLLM_ENG_LAUNCHX
+        return cudaErrorNotSupported;
+    }
 #define SLLM_ENG_LAUNCH(A, B) \
-    if (wa == A && wb == B) return cudaLaunchKernelEx(&cfg, i2s_engine_kernel<A, B, false>, p);
+    if (wa == A && wb == B) return cudaLaunchKernelEx(&cfg, i2s_engine_kernel<A, B, false, false>, p);
     SLLM_ENGINE_SHAPES(SLLM_ENG_LAUNCH)
 #undef SLLM_ENG_LAUNCH
     return cudaErrorNotSupported;

@@ -210,9 +210,43 @@ tp_norm_quant_kernel(const float* __restrict__ x, const float* __restrict__ w, i
 // straight-line code, so each one reaches every cluster barrier.
 constexpr int kNqCluster = 8;
 
+// A kernel's wait for an exchange every rank published (the fused peer
+// exchange): flag[kind][r] of this rank's region reaching steps * n_layer +
+// layer + 1 for every rank r, bounded; flags == nullptr: no wait.
+struct XWait {
+    const uint32_t* flags;     // this rank's flags of the kind: [kMaxRanks]
+    const uint32_t* steps;
+    int n_peer, n_layer, layer;
+    int* error;                // set when the wait gave up
+};
+constexpr uint64_t kXWaitNs = 10000000000ull;     // 10 s: a peer may still be launching
+
+__device__ __forceinline__ void xwait_block(const XWait& w) {
+    if (w.flags == nullptr) return;
+    if (threadIdx.x == 0) {
+        const uint32_t val = *(volatile const uint32_t*)w.steps * (uint32_t)w.n_layer + (uint32_t)w.layer + 1u;
+        const uint64_t t0 = gtimer_d();
+        for (int q = 0; q < w.n_peer; ++q) {
+            uint32_t f;
+            while (true) {
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(w.flags + q) : "memory");
+                if (f >= val) break;
+                if (gtimer_d() - t0 > kXWaitNs || *(volatile const int*)w.error != 0) {
+                    atomicExch(w.error, ENG_TIMEOUT_PEER);
+                    q = w.n_peer;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+    }
+    __syncthreads();
+}
+
 __global__ void __cluster_dims__(kNqCluster, 1, 1) __launch_bounds__(kNqThreads)
 tp_norm_quant_cluster_kernel(const float* __restrict__ x, const float* __restrict__ w, int K, float eps,
-                             double inv_k, int8_t* __restrict__ q, sllm_cuda_act* act, int* fb, int force) {
+                             double inv_k, int8_t* __restrict__ q, sllm_cuda_act* act, int* fb, int force,
+                             XWait xw) {
     namespace cg = cooperative_groups;
     cg::cluster_group cl = cg::this_cluster();
     __shared__ double dred[32];
@@ -229,6 +263,7 @@ tp_norm_quant_cluster_kernel(const float* __restrict__ x, const float* __restric
     // previous launch
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    xwait_block(xw);     // x gathered from every rank's stores (the fused peer exchange)
     const int per = (K >> 2) / kNqCluster;                 // float4 per CTA
     const int i = rank * per + tid;
     const bool live = tid < per;
@@ -319,6 +354,23 @@ __global__ void tp_epilogue_kernel(const int32_t* __restrict__ dots, int n_chunk
     y[r] = __fadd_rn(__fmul_rn(__int2float_rn(d - a.sum), post), resid[r]);
 }
 
+// The same epilogue over every rank's slots of a contraction split over ranks
+// and column chunks, once the exchange that filled them is complete
+// (the fused peer exchange; the step's last down projection).
+__global__ void tp_xreduce_kernel(XWait xw, const int32_t* __restrict__ slots, int n_slots, int rows,
+                                  const sllm_cuda_act* act, const float* __restrict__ ws,
+                                  const float* __restrict__ resid, float* __restrict__ y) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    xwait_block(xw);
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    int d = 0;
+    for (int c = 0; c < n_slots; ++c) d += __ldcg(slots + (size_t)c * rows + r);
+    const sllm_cuda_act a = *act;
+    const float post = __fdiv_rn(*ws, a.scale);
+    y[r] = __fadd_rn(__fmul_rn(__int2float_rn(d - a.sum), post), resid[r]);
+}
+
 // first maximum over the slices' bests, in rank (= row) order, then the
 // greedy feedback and position advance of the step (as lm_head_kernel)
 __device__ __forceinline__ bool tp_better(float v, int i, float bv, int bi) {
@@ -328,7 +380,8 @@ __device__ __forceinline__ bool tp_better(float v, int i, float bv, int bi) {
 }
 
 __global__ void tp_finalize_kernel(const int32_t* trip_all, int n_ranks, int32_t* pos_ptr, int32_t* tok_seq,
-                                   const int32_t* prompt_end, int32_t* argmax_out, int32_t* hist, int n_ctx) {
+                                   const int32_t* prompt_end, int32_t* argmax_out, int32_t* hist, int n_ctx,
+                                   uint32_t* steps) {
     float bv = NAN;
     int bi = 0x7fffffff;
     for (int r = 0; r < n_ranks; ++r) {
@@ -343,6 +396,7 @@ __global__ void tp_finalize_kernel(const int32_t* trip_all, int n_ranks, int32_t
     if (pos + 1 >= *prompt_end && pos + 1 < n_ctx) tok_seq[pos + 1] = next;
     if (hist != nullptr) hist[pos] = next;
     *pos_ptr = pos + 1;
+    if (steps != nullptr) *steps += 1u;      // the fused exchange's flag values move on
 }
 
 // element-wise int32 sum of up to kMaxRanks buffers into each of them (the
@@ -587,6 +641,17 @@ struct sllm_cuda_tp_ctx {
     size_t off_flags = 0, off_attn = 0, off_h = 0, off_dots_o = 0, off_dots_d = 0, off_trip = 0;
     uint32_t* epoch = nullptr;
     int* x_error = nullptr;
+    // the fused peer exchange (more than one rank over peer memory, widths
+    // with an exchanging engine instance): per layer one program A (the
+    // reduce of the previous layer's down, Q/K/V, attention, O's partial
+    // dots, their reduce, gate/up) and one program D (down's partial dots),
+    // with the norm/quantisation of h between them; every exchange is stores
+    // into every rank's region plus flags, inside those launches
+    std::vector<Prog> xa, xd;
+    unsigned* x_barriers = nullptr;   // one grid barrier word per A program
+    unsigned* x_done = nullptr;       // end-of-kernel arrival counter of the A and D programs
+    uint32_t* x_steps = nullptr;      // steps completed: the flag values
+    size_t off_xflags = 0;            // flags [kind][kMaxRanks] in every region
     // recorded on `stream` around the step launches of the last generate call
     cudaEvent_t run_ev[2] = {};
 };
@@ -999,7 +1064,7 @@ cudaError_t launch_count(cudaError_t e, int n) {
 // RMSNorm + quantisation of a whole vector: the eight-CTA cluster when the
 // length allows it (a multiple of 32, at most 32768), else one CTA
 cudaError_t launch_norm_quant(const float* x, const float* w, int K, float eps, int8_t* q, sllm_cuda_act* act,
-                              int* fb, int force, cudaStream_t st) {
+                              int* fb, int force, cudaStream_t st, const XWait& xw = XWait{}) {
     const double inv_k = 1.0 / (double)K;
     const bool cluster = K % (4 * kNqCluster) == 0 && K <= 4 * kNqCluster * kNqThreads;
     cudaLaunchConfig_t cfg = pdl_config(cluster ? kNqCluster : 1, kNqThreads, st);
@@ -1007,7 +1072,7 @@ cudaError_t launch_norm_quant(const float* x, const float* w, int K, float eps, 
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     if (cluster)
-        return cudaLaunchKernelEx(&cfg, tp_norm_quant_cluster_kernel, x, w, K, eps, inv_k, q, act, fb, force);
+        return cudaLaunchKernelEx(&cfg, tp_norm_quant_cluster_kernel, x, w, K, eps, inv_k, q, act, fb, force, xw);
     return cudaLaunchKernelEx(&cfg, tp_norm_quant_kernel, x, w, K, eps, inv_k, q, act, fb, force);
 }
 
@@ -1045,7 +1110,8 @@ cudaError_t enqueue_phase(sllm_cuda_tp_ctx* c, int ph, cudaStream_t st, bool cou
     }
     if (ph == n_phases(m) - 1) {
         tp_finalize_kernel<<<1, 1, 0, st>>>(c->trip_all, m->n_ranks, c->pos, c->tok_seq, c->prompt_end, c->argmax,
-                                            c->hist, c->n_ctx);
+                                            c->hist, c->n_ctx,
+                                            c->x_steps);
         return launch_count(cudaGetLastError(), cnt);
     }
     if (ph == n_phases(m) - 2) {
@@ -1158,6 +1224,7 @@ int setup_peer_exchange(sllm_cuda_tp_ctx* c) {
     c->off_dots_o = take(4 * E * N);
     c->off_dots_d = take(4 * E * m->down_c * N);
     c->off_trip = take(4 * 3 * (size_t)N);
+    c->off_xflags = take(4 * 4 * (size_t)kMaxRanks);
     int ok = 1;
     cudaIpcMemHandle_t mine{};
     if (cudaMalloc(&c->region, off) != cudaSuccess) { c->region = nullptr; ok = 0; }
@@ -1385,16 +1452,250 @@ int build_engine_programs(sllm_cuda_tp_ctx* c) {
     return SLLM_CUDA_OK;
 }
 
+// Exchange kinds of the fused peer exchange (one of each per layer).
+enum XKind { XK_ATTN = 0, XK_DOTS_O = 1, XK_H = 2, XK_DOTS_D = 3 };
+
+// The fused peer exchange's programs (see sllm_cuda_tp_ctx::xa). Built when
+// the peer exchange is set up and the widths have an exchanging instance;
+// otherwise the per-phase programs and exchange kernels stay in use.
+int build_xch_programs(sllm_cuda_tp_ctx* c) {
+    const sllm_cuda_tp_model* m = c->m;
+    const int N = m->n_ranks, E = m->E, D = kHeadDim, C = m->down_c;
+    if (!c->p2p || c->progs.empty() || N > kEngMaxPeers || c->n_ctx > kEngAttnMaxCtx) return SLLM_CUDA_OK;
+    const int wa = wpl_of(E), wo = wpl_of(m->e_loc), wd = wpl_of(m->down_k);
+    if (!engine_supports_xch(wa, wo) || !engine_supports_xch(wa, wd) || m->F % (4 * 8) != 0 ||
+        m->F > 4 * 8 * kNqThreads || m->e_loc % 128 != 0)
+        return SLLM_CUDA_OK;
+    int* fb = fallback_counter();
+    CK(ctx_alloc(c, &c->x_barriers, (size_t)m->n_layer), "exchange program barriers");
+    CK(ctx_alloc(c, &c->x_done, 1), "exchange program counter");
+    CK(ctx_alloc(c, &c->x_steps, 1), "exchange step counter");
+    CK(cudaMemset(c->x_done, 0, 4), "exchange program counter");
+    CK(cudaMemset(c->x_steps, 0, 4), "exchange step counter");
+    char* region = c->region;
+    float* attn_full = reinterpret_cast<float*>(region + c->off_attn);
+    float* h_full = reinterpret_cast<float*>(region + c->off_h);
+    int32_t* dots_o = reinterpret_cast<int32_t*>(region + c->off_dots_o);   // [N][E]
+    int32_t* dots_d = reinterpret_cast<int32_t*>(region + c->off_dots_d);   // [N][C][E]
+    EngX xb{};
+    for (int q = 0; q < N; ++q) xb.peer[q] = c->peer[q];
+    xb.flag_off = (uint32_t)c->off_xflags;
+    xb.steps = c->x_steps;
+    xb.done = c->x_done;
+    xb.n_peer = N;
+    xb.rank = m->rank;
+    xb.n_layer = m->n_layer;
+    const size_t kv_layer = (size_t)m->hk * D * (size_t)c->n_ctx;
+    auto upload = [&](const std::vector<EngGroup>& groups, const std::vector<EngOp>& ops,
+                      const std::vector<int>& stage_first, const AttnParams* ap, EngParams& p) -> int {
+        const std::vector<EngCursor> st = engine_starts(ops, stage_first, c->grid);
+        const int n_stages = (int)stage_first.size() - 1;
+        if (engine_smem_bytes((int)groups.size(), (int)ops.size(), n_stages, ap ? 1 : 0) == 0)
+            return fail(SLLM_CUDA_ERR_TOO_LARGE, "tp exchange program does not fit in shared memory");
+        EngGroup* dg = nullptr;
+        EngOp* dop = nullptr;
+        EngCursor* ds = nullptr;
+        AttnParams* da = nullptr;
+        CK(ctx_alloc(c, &dg, groups.size()), "exchange program groups");
+        CK(ctx_alloc(c, &dop, ops.size()), "exchange program ops");
+        CK(ctx_alloc(c, &ds, st.size()), "exchange program cursors");
+        CK(cudaMemcpy(dg, groups.data(), groups.size() * sizeof(EngGroup), cudaMemcpyHostToDevice), "tables");
+        CK(cudaMemcpy(dop, ops.data(), ops.size() * sizeof(EngOp), cudaMemcpyHostToDevice), "tables");
+        CK(cudaMemcpy(ds, st.data(), st.size() * sizeof(EngCursor), cudaMemcpyHostToDevice), "tables");
+        if (ap != nullptr) {
+            CK(ctx_alloc(c, &da, 1), "exchange program attention");
+            CK(cudaMemcpy(da, ap, sizeof(AttnParams), cudaMemcpyHostToDevice), "tables");
+        }
+        p.groups = dg; p.ops = dop; p.starts = ds; p.attn = da; p.n_attn = ap ? 1 : 0;
+        p.n_groups = (int)groups.size(); p.n_ops = (int)ops.size(); p.n_stages = n_stages;
+        p.error = c->eng_error; p.eps = m->eps; p.fallback_count = fb; p.force_fallback = force_fallback_flag();
+        p.xch = 1;
+        return SLLM_CUDA_OK;
+    };
+    for (int l = 0; l < m->n_layer; ++l) {
+        const TpLayer& t = m->layers[l];
+        std::vector<EngGroup> groups;
+        std::vector<EngOp> ops;
+        std::vector<int> stage_first;
+        EngX x = xb;
+        x.layer = l;
+        x.end_kind = XK_H;
+        auto op = [&](const uint8_t* w, const uint8_t* w2, float* y, const float* resid, float* h, int rows, int K,
+                      int epi, int group, int k0x) {
+            EngOp o{};
+            o.w = w; o.w2 = w2; o.y = y; o.resid = resid; o.h = h; o.rows = rows; o.K = K; o.epi = epi;
+            o.group = group; o.k0x = k0x;
+            o.chunk_rows = epi == kEpiAttention ? 1 : epi == kEpiReduce ? rows : engine_chunk_rows(K, epi);
+            o.ws = (w != nullptr && epi != kEpiReduce) ? read_scale(w, rows, K) : 0.0f;
+            o.ws2 = (w2 != nullptr && epi != kEpiReduce) ? read_scale(w2, rows, K) : 0.0f;
+            ops.push_back(o);
+        };
+        auto group = [&](const float* xv, const float* norm_w, sllm_cuda_act* act_out) {
+            EngGroup g{}; g.x = xv; g.norm_w = norm_w; g.K = E; g.pro = PRO_NORM; g.act8 = act_out;
+            groups.push_back(g);
+            return (int)groups.size() - 1;
+        };
+        int si = 0;
+        if (l > 0) {
+            // the previous layer's down: x = its reduce + ffn_inp, once every
+            // rank's partial dots have arrived (published by its program D)
+            const TpLayer& tp = m->layers[l - 1];
+            stage_first.push_back((int)ops.size());
+            op(reinterpret_cast<const uint8_t*>(dots_d), reinterpret_cast<const uint8_t*>(c->act_h), c->x,
+               c->ffn_inp, nullptr, E, N * C, kEpiReduce, 0, 0);
+            ops.back().ws = read_scale(tp.down[0], E, m->down_k);
+            x.xs[si++] = (int8_t)(XK_DOTS_D + 1);
+        }
+        // attn_norm -> local Q, K, V (src/forward.c:631-666)
+        stage_first.push_back((int)ops.size());
+        int g = group(c->x, t.attn_norm, nullptr);
+        op(t.wq, nullptr, c->q, nullptr, nullptr, m->hq * D, E, EPI_F32, g, 0);
+        op(t.wk, nullptr, c->k, nullptr, nullptr, m->hk * D, E, EPI_F32, g, 0);
+        op(t.wv, nullptr, c->v, nullptr, nullptr, m->hk * D, E, EPI_F32, g, 0);
+        x.xs[si++] = 0;
+        // attention over the local heads; the outputs into this rank's slice
+        // of the whole attention vector in every region
+        float* attn_slice = attn_full + (size_t)m->rank * m->hq * D;
+        stage_first.push_back((int)ops.size());
+        op(nullptr, nullptr, attn_slice, nullptr, nullptr, m->hq, c->n_ctx, kEpiAttention, 0, kOpScatter);
+        x.xs[si++] = kXsFence;
+        // attn_sub_norm + quantisation of the whole vector, this rank's
+        // columns of O: partial dots into slot `rank` of every region
+        stage_first.push_back((int)ops.size());
+        g = group(attn_full, t.attn_sub_norm, c->act_a);
+        op(t.wo, nullptr, reinterpret_cast<float*>(dots_o + (size_t)m->rank * E), nullptr, nullptr, E, m->e_loc,
+           EPI_DOTS, g, (m->rank * m->e_loc) | kOpScatter);
+        x.xs[si++] = (int8_t)((XK_ATTN + 1) | kXsSignal | kXsFence);
+        // O's epilogue + residual (src/forward.c:739-750) from every rank's dots
+        stage_first.push_back((int)ops.size());
+        op(reinterpret_cast<const uint8_t*>(dots_o), reinterpret_cast<const uint8_t*>(c->act_a), c->ffn_inp, c->x,
+           nullptr, E, N, kEpiReduce, 0, 0);
+        ops.back().ws = read_scale(t.wo, E, m->e_loc);
+        x.xs[si++] = (int8_t)((XK_DOTS_O + 1) | kXsSignal);
+        // ffn_norm -> local gate, up -> h, into this rank's slice of h in
+        // every region (src/forward.c:752-779)
+        stage_first.push_back((int)ops.size());
+        g = group(c->ffn_inp, t.ffn_norm, nullptr);
+        op(t.gate, t.up, nullptr, nullptr, h_full + (size_t)m->rank * m->f_loc, m->f_loc, E, EPI_SILU, g, kOpScatter);
+        x.xs[si++] = kXsFence;
+        stage_first.push_back((int)ops.size());
+        AttnParams ap{};
+        ap.q = c->q; ap.k = c->k; ap.v = c->v;
+        ap.k_cache = c->k_cache + (size_t)l * kv_layer;
+        ap.v_cache = c->v_cache + (size_t)l * kv_layer;
+        ap.rope_cos = c->rope_cos; ap.rope_sin = c->rope_sin;
+        ap.pos_ptr = c->pos; ap.out = attn_slice; ap.n_ctx = c->n_ctx;
+        ap.group = m->hq / m->hk;
+        ap.attn_scale = 1.0f / sqrtf((float)D);
+        ap.fallback_count = fb; ap.force_fallback = force_fallback_flag();
+        sllm_cuda_tp_ctx::Prog pa{};
+        int rc = upload(groups, ops, stage_first, &ap, pa.p);
+        if (rc != SLLM_CUDA_OK) return rc;
+        pa.p.barrier = c->x_barriers + l;
+        pa.p.x = x;
+        pa.wa = wa;
+        pa.wb = wo;
+        c->xa.push_back(pa);
+
+        // program D: this rank's columns of down (pre-quantised h slices),
+        // partial dots into slot [rank][chunk] of every region
+        std::vector<EngGroup> dgs;
+        std::vector<EngOp> dops;
+        for (int ch = 0; ch < C; ++ch) {
+            EngGroup dg{};
+            dg.q8 = c->qh + (size_t)m->rank * m->f_loc + (size_t)ch * m->down_k;
+            dg.act8 = c->act_h; dg.K = m->down_k; dg.pro = PRO_Q8;
+            dgs.push_back(dg);
+            EngOp o{};
+            o.w = t.down[ch];
+            o.y = reinterpret_cast<float*>(dots_d + ((size_t)m->rank * C + ch) * E);
+            o.rows = E; o.K = m->down_k; o.epi = EPI_DOTS; o.group = ch; o.k0x = kOpScatter;
+            o.chunk_rows = engine_chunk_rows(m->down_k, EPI_DOTS);
+            o.ws = read_scale(t.down[ch], E, m->down_k);
+            dops.push_back(o);
+        }
+        sllm_cuda_tp_ctx::Prog pd{};
+        rc = upload(dgs, dops, std::vector<int>{0, (int)dops.size()}, nullptr, pd.p);
+        if (rc != SLLM_CUDA_OK) return rc;
+        pd.p.barrier = c->eng_barrier;
+        EngX xd = xb;
+        xd.layer = l;
+        xd.end_kind = XK_DOTS_D;
+        pd.p.x = xd;
+        pd.wa = wa;
+        pd.wb = wd;
+        c->xd.push_back(pd);
+    }
+    return SLLM_CUDA_OK;
+}
+
+// The step of the fused peer exchange: embedding; per layer program A (a
+// cooperative launch), the norm/quantisation of h once every rank's slice
+// has arrived, program D; the last layer's down reduce; the head and the
+// argmax exchange; the finalize (which advances the flag values).
+cudaError_t enqueue_xstep(sllm_cuda_tp_ctx* c, cudaStream_t st) {
+    const sllm_cuda_tp_model* m = c->m;
+    const int N = m->n_ranks, E = m->E, C = m->down_c;
+    int* fb = fallback_counter();
+    const int force = force_fallback_flag();
+    cudaError_t e = launch_embed(m->tok_embd, c->tok_seq, c->pos, E, m->V, c->x, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(c->x_barriers, 0, sizeof(unsigned) * m->n_layer, st);
+    const uint32_t* flags = reinterpret_cast<const uint32_t*>(c->region + c->off_xflags);
+    for (int l = 0; l < m->n_layer && e == cudaSuccess; ++l) {
+        e = launch_engine(c->xa[l].p, c->grid, st, c->xa[l].wa, c->xa[l].wb);
+        XWait xw{flags + XK_H * kMaxRanks, c->x_steps, N, m->n_layer, l, c->eng_error};
+        if (e == cudaSuccess)
+            e = launch_norm_quant(reinterpret_cast<const float*>(c->region + c->off_h), m->layers[l].ffn_sub_norm,
+                                  m->F, m->eps, c->qh, c->act_h, fb, force, st, xw);
+        if (e == cudaSuccess) e = launch_engine(c->xd[l].p, c->grid, st, c->xd[l].wa, c->xd[l].wb);
+    }
+    if (e != cudaSuccess) return e;
+    const TpLayer& t = m->layers[m->n_layer - 1];
+    {
+        XWait xw{flags + XK_DOTS_D * kMaxRanks, c->x_steps, N, m->n_layer, m->n_layer - 1, c->eng_error};
+        cudaLaunchConfig_t cfg = pdl_config((E + 255) / 256, 256, st);
+        cudaLaunchAttribute attr = pdl_attribute();
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        const float* ws = reinterpret_cast<const float*>(t.down[0] + (size_t)E * m->down_k / 4);
+        e = cudaLaunchKernelEx(&cfg, tp_xreduce_kernel, xw,
+                               reinterpret_cast<const int32_t*>(c->region + c->off_dots_d), N * C, E,
+                               (const sllm_cuda_act*)c->act_h, ws, (const float*)c->ffn_inp, c->x);
+    }
+    if (e != cudaSuccess) return e;
+    LmParams lp{};
+    lp.x = c->x; lp.norm_w = m->output_norm; lp.eps = m->eps;
+    lp.embd = m->tok_embd + (size_t)m->v0 * E;
+    lp.E = E; lp.V = m->v_loc; lp.logits = c->logits;
+    lp.part_v = c->part_v; lp.part_i = c->part_i; lp.counter = c->counter; lp.argmax_out = c->argmax;
+    lp.pos_ptr = c->pos; lp.tok_seq = c->tok_seq; lp.prompt_end = c->prompt_end; lp.argmax_hist = nullptr;
+    lp.n_ctx = c->n_ctx; lp.fallback_count = fb; lp.force_fallback = force;
+    lp.tp_out = c->trip; lp.row_base = m->v0;
+    e = launch_lm_head(lp, c->lm_grid, st);
+    ncclResult_t nr = ncclSuccess;
+    if (e == cudaSuccess) e = xchg_nccl(c, X_ARGMAX, st, &nr);
+    if (e == cudaSuccess) {
+        tp_finalize_kernel<<<1, 1, 0, st>>>(c->trip_all, N, c->pos, c->tok_seq, c->prompt_end, c->argmax, c->hist,
+                                            c->n_ctx, c->x_steps);
+        e = cudaGetLastError();
+    }
+    return e;
+}
+
 int ensure_tp_graph(sllm_cuda_tp_ctx* c) {
     if (c->step != nullptr) return SLLM_CUDA_OK;
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
     cudaError_t e = cudaSuccess;
     ncclResult_t nr = ncclSuccess;
-    for (int ph = 0; ph < n_phases(c->m) && e == cudaSuccess; ++ph) {
-        e = enqueue_phase(c, ph, c->stream, false);
-        const int x = phase_xchg(c->m, ph);
-        if (e == cudaSuccess && x >= 0) e = xchg_nccl(c, x, c->stream, &nr);
+    if (!c->xa.empty()) {
+        e = enqueue_xstep(c, c->stream);
+    } else {
+        for (int ph = 0; ph < n_phases(c->m) && e == cudaSuccess; ++ph) {
+            e = enqueue_phase(c, ph, c->stream, false);
+            const int x = phase_xchg(c->m, ph);
+            if (e == cudaSuccess && x >= 0) e = xchg_nccl(c, x, c->stream, &nr);
+        }
     }
     const cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
     if (nr != ncclSuccess) { if (g) cudaGraphDestroy(g); return fail(SLLM_CUDA_ERR_COMM, "tp step: %s", nccl_err(nr)); }
@@ -1521,6 +1822,7 @@ extern "C" int sllm_cuda_tp_ctx_new(const sllm_cuda_tp_model* m, sllm_cuda_tp_co
     }
     int rc = build_engine_programs(c);
     if (rc == SLLM_CUDA_OK) rc = setup_peer_exchange(c);
+    if (rc == SLLM_CUDA_OK) rc = build_xch_programs(c);
     if (rc != SLLM_CUDA_OK) {
         sllm_cuda_tp_ctx_free(c);
         return rc;
@@ -1595,6 +1897,8 @@ extern "C" float sllm_cuda_test_tp_ctx_last_run_ms(const sllm_cuda_tp_ctx* c) {
     }
     return ms;
 }
+
+extern "C" int sllm_cuda_test_tp_fused_exchange(const sllm_cuda_tp_ctx* c) { return c != nullptr && !c->xa.empty(); }
 
 extern "C" int sllm_cuda_tp_ctx_reset(sllm_cuda_tp_ctx* c) {
     if (c == nullptr) return fail(SLLM_CUDA_ERR_ARG, "tp_ctx_reset: null");

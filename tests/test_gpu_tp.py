@@ -146,16 +146,25 @@ def test_tp_engine_ranks_agree(cuda):
         assert np.array_equal(bits(lg), bits(l1)), f"TP={n}"
 
 
-def _nccl_rank(rank, n, uid, prompt, n_new, kind, q):
+def _wide_desc(cuda):
+    # n_embd 8192: the widths with an exchanging engine instance, so two
+    # ranks over peer memory run the fused exchange
+    return cuda.abi.TpSynthDesc(n_layer=2, n_embd=8192, n_ff=16384, n_head=64, n_head_kv=8, n_vocab=3001,
+                                f_rms_eps=1e-5, rope_freq_base=500000.0, seed=77)
+
+
+def _nccl_rank(rank, n, uid, prompt, n_new, kind, q, wide=False):
     import importlib
     import torch  # noqa: F401  (a process with torch keeps one NCCL copy)
     try:
         os.environ["SLLM_CUDA_TP_EXCHANGE"] = kind
         cuda = importlib.import_module("saphira-llm_b200")
         comm = cuda.TpComm(uid, n, rank, rank)
-        tm = cuda.TpModel(n, rank, rank, synth=_synth_desc(cuda))
+        tm = cuda.TpModel(n, rank, rank, synth=_wide_desc(cuda) if wide else _synth_desc(cuda))
         tc = tm.ctx(64, comm)
         got = tc.exchange_kind()
+        if wide and kind == "p2p" and not tc.fused_exchange():
+            got = "not fused"
         rc, toks = tc.generate(prompt, n_new)
         v0, lg = tc.last_logits()
         q.put((rank, rc if got == kind else -998, toks.tolist(), v0, lg))
@@ -182,6 +191,42 @@ def test_tp_two_gpus_matches_one(cuda, kind):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     procs = [ctx.Process(target=_nccl_rank, args=(r, 2, uid, prompt, 12, kind, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            rank, rc, toks, v0, lg = q.get(timeout=300)
+            res[rank] = (rc, toks, v0, lg)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert all(res[r][0] == 0 for r in range(2)), res
+    assert res[0][1] == res[1][1] == t1.tolist()
+    lg = np.concatenate([res[r][3] for r in range(2)])
+    assert np.array_equal(bits(lg), bits(l1))
+
+
+@pytest.mark.parametrize("kind", ["p2p", "nccl"])
+def test_tp_two_gpus_wide_matches_one(cuda, kind):
+    """The 8192-wide model on two GPUs: with the peer exchange the step runs
+    the fused exchange (stores into every rank's memory and flag waits inside
+    the layer programs); with NCCL the per-phase collectives. Both give the
+    single-GPU bits, tokens and logits."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("one GPU on this box: the exchange is covered by the multi-GPU bench and runs")
+    sd = _wide_desc(cuda)
+    prompt = _tokens(10, 7, sd.n_vocab)
+    rc1, t1, l1 = _group_run(cuda, sd, 1, prompt, 12)
+    assert rc1 == 0
+    uid = cuda.tp_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_nccl_rank, args=(r, 2, uid, prompt, 12, kind, q, True)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
