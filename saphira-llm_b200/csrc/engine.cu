@@ -718,9 +718,10 @@ i2s_engine_kernel(const EngParams P) {
             // for every rank's flag (bounded)
             if (tid == 0 && !*(volatile int*)&es.abort_flag) {
                 const int kind = (P.x.xs[s] & kXsWaitMask) - 1;
-                if ((P.x.xs[s] & kXsSignal) != 0 && c == 0) x_signal(P.x, kind, xval);
+                const uint32_t want = (P.x.xs[s] & kXsPrev) != 0 ? xval - 1u : xval;
+                if ((P.x.xs[s] & kXsSignal) != 0 && c == 0) x_signal(P.x, kind, want);
                 // a peer may still be launching its step: five budgets
-                if (!x_wait(P.x, kind, xval, 5 * budget, P.error)) {
+                if (!x_wait(P.x, kind, want, 5 * budget, P.error)) {
                     es.abort_flag = 1;
                     atomicExch(P.error, ENG_TIMEOUT_PEER);
                 }

@@ -55,6 +55,7 @@ constexpr int kOpK0Mask = (1 << 24) - 1;   // EngOp::k0x: byte offset of the op'
 constexpr int kXsWaitMask = 0x0f;          // EngX::xs: kind + 1 to wait for at the stage's start
 constexpr int kXsSignal = 0x10;            // EngX::xs: CTA 0 publishes that kind first (after the grid barrier)
 constexpr int kXsFence = 0x20;             // EngX::xs: the stage stored to peers: system fence before arriving
+constexpr int kXsPrev = 0x40;              // EngX::xs: the awaited exchange is the previous layer's
 
 struct EngX {
     char* peer[kEngMaxPeers];   // every rank's exchange region; peer[rank] is this rank's

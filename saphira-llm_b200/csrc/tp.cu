@@ -1544,7 +1544,7 @@ int build_xch_programs(sllm_cuda_tp_ctx* c) {
             op(reinterpret_cast<const uint8_t*>(dots_d), reinterpret_cast<const uint8_t*>(c->act_h), c->x,
                c->ffn_inp, nullptr, E, N * C, kEpiReduce, 0, 0);
             ops.back().ws = read_scale(tp.down[0], E, m->down_k);
-            x.xs[si++] = (int8_t)(XK_DOTS_D + 1);
+            x.xs[si++] = (int8_t)((XK_DOTS_D + 1) | kXsPrev);     // published by layer l - 1's program D
         }
         // attn_norm -> local Q, K, V (src/forward.c:631-666)
         stage_first.push_back((int)ops.size());
