@@ -88,7 +88,7 @@ __device__ __forceinline__ void attention_head_t(const AttnParams& p, int h, int
 
     // the first query head of the group stores this position's K and V
     // (src/forward.c:683-696); every head uses kcur / v directly for pos
-    if (h % p.group == 0 && t < kHeadDim) {
+    if (h % p.group == 0 && t < kHeadDim && (p.kv_f16 & kAttnKvStored) == 0) {
         kT.st((size_t)t * nctx + pos, kcur[t]);
         vC.st((size_t)pos * kHeadDim + t, __ldcg(p.v + kvh * kHeadDim + t));
     }
@@ -232,7 +232,7 @@ __device__ __noinline__ void attention_head_f16(const AttnParams& p, int h, int 
 template <int NT, class Sync>
 __device__ __forceinline__ void attention_head(const AttnParams& p, int h, int t, float* sc, float* qs, float* kcur,
                                                float* fred, double* dred, Sync sync) {
-    if (p.kv_f16)
+    if (p.kv_f16 & kAttnKvF16)
         attention_head_f16<NT>(p, h, t, sc, qs, kcur, fred, dred, sync);
     else
         attention_head_t<NT, float>(p, h, t, sc, qs, kcur, fred, dred, sync);

@@ -729,6 +729,18 @@ struct sllm_cuda_ctx {
     // recorded on `stream` around the step launches of the last forward or
     // generate call (device time of the decode steps alone)
     cudaEvent_t run_ev[2] = {};
+    // the multi-token chunk path (allocated at its first use): every token's
+    // residual, projections, attention output and FFN state as row-major
+    // [chunk][width] buffers, the per-token int8 activations and positions
+    struct Chunk {
+        int cap = 0;
+        float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *proj = nullptr,
+              *ffn_inp = nullptr, *h = nullptr;
+        int8_t* qa = nullptr;
+        sllm_cuda_act* acts = nullptr;
+        int32_t* pos = nullptr;
+        int32_t* pos_host = nullptr;      // pinned staging of the positions
+    } ch;
 };
 
 // bytes of one cached value, and the cache of layer l
@@ -781,6 +793,11 @@ extern "C" void sllm_cuda_ctx_free(sllm_cuda_ctx* c) {
     if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
     for (cudaEvent_t ev : c->run_ev)
         if (ev) cudaEventDestroy(ev);
+    for (void* p : {(void*)c->ch.x, (void*)c->ch.q, (void*)c->ch.k, (void*)c->ch.v, (void*)c->ch.attn,
+                    (void*)c->ch.proj, (void*)c->ch.ffn_inp, (void*)c->ch.h, (void*)c->ch.qa, (void*)c->ch.acts,
+                    (void*)c->ch.pos})
+        cudaFree(p);
+    if (c->ch.pos_host) cudaFreeHost(c->ch.pos_host);
     delete c;
 }
 
@@ -963,7 +980,8 @@ static int ensure_step_graph(sllm_cuda_ctx* c) {
 }
 
 // Run positions [base, base + n) whose tokens are already in tok_seq.
-static int run_steps(sllm_cuda_ctx* c, int base, int n, int prompt_end, float* chunk_logits_dev) {
+static int run_steps(sllm_cuda_ctx* c, int base, int n, int prompt_end, float* chunk_logits_dev,
+                     bool start_timer = true) {
     int rc = ensure_step_graph(c);
     if (rc != SLLM_CUDA_OK) return rc;
     c->pinned[0] = base;
@@ -971,7 +989,7 @@ static int run_steps(sllm_cuda_ctx* c, int base, int n, int prompt_end, float* c
     CK(cudaMemcpyAsync(c->pos, &c->pinned[0], 4, cudaMemcpyHostToDevice, c->stream), "set pos");
     CK(cudaMemcpyAsync(c->prompt_end, &c->pinned[1], 4, cudaMemcpyHostToDevice, c->stream), "set prompt end");
     const size_t V = c->m->n_vocab;
-    CK(cudaEventRecord(c->run_ev[0], c->stream), "run timer");
+    if (start_timer) CK(cudaEventRecord(c->run_ev[0], c->stream), "run timer");
     for (int t = 0; t < n; ++t) {
         CK(graph_launch(c->step, c->stream), "decode step");
         if (chunk_logits_dev != nullptr)
@@ -990,6 +1008,145 @@ extern "C" float sllm_cuda_test_ctx_last_run_ms(const sllm_cuda_ctx* c) {
         return -1.0f;
     }
     return ms;
+}
+
+// ---------------------------------------------------------------------------
+// The multi-token chunk (src/forward.c:589-835 with n > 1) on the tensor
+// cores: per layer, every token's RMSNorm + quantisation, the projections of
+// all tokens as tcgen05 GEMMs (each weight byte read once for the chunk
+// instead of once per token), RoPE and the cache stores of every token, then
+// causal attention for every (head, token). Every value equals the
+// one-token-at-a-time path's: the same per-token prologue arithmetic, integer
+// dots, epilogues, attention order. A chunk is not a semantic boundary
+// (src/forward.c:572-588), and neither is this.
+// ---------------------------------------------------------------------------
+static constexpr int kChunkMax = 256;      // SLLM_MAX_CHUNK (include/saphira_llm/forward.h:90)
+
+static int chunk_alloc(sllm_cuda_ctx* c) {
+    if (c->ch.cap >= kChunkMax) return SLLM_CUDA_OK;
+    const sllm_cuda_model* m = c->m;
+    const size_t T = kChunkMax, E = m->n_embd, G = m->n_embd_gqa, F = m->n_ff;
+    cudaError_t e = cudaSuccess;
+    auto A = [&](void** p, size_t bytes) { if (e == cudaSuccess) e = dev_malloc(p, bytes); };
+    A((void**)&c->ch.x, T * E * 4); A((void**)&c->ch.q, T * E * 4); A((void**)&c->ch.k, T * G * 4);
+    A((void**)&c->ch.v, T * G * 4); A((void**)&c->ch.attn, T * E * 4); A((void**)&c->ch.proj, T * E * 4);
+    A((void**)&c->ch.ffn_inp, T * E * 4); A((void**)&c->ch.h, T * F * 4);
+    A((void**)&c->ch.qa, T * std::max(E, F)); A((void**)&c->ch.acts, T * sizeof(sllm_cuda_act));
+    A((void**)&c->ch.pos, T * 4);
+    if (e == cudaSuccess) e = cudaMallocHost(&c->ch.pos_host, T * 4);
+    if (e != cudaSuccess) return cuda_fail(e, "chunk buffers");
+    c->ch.cap = kChunkMax;
+    return SLLM_CUDA_OK;
+}
+
+// the chunk path runs where the GEMM and the attention kernels do
+static bool chunk_path_ok(const sllm_cuda_ctx* c) {
+    const sllm_cuda_model* m = c->m;
+    return m->head_dim == 128 && m->n_embd % 128 == 0 && m->n_ff % 128 == 0 && c->n_ctx <= attention_max_ctx();
+}
+
+// Positions [base, base + n) whose tokens are in tok_seq. heads: -1 every
+// position's head (logits into logits_dev rows when it is not null), or the
+// number of trailing positions whose head runs (0: none). The head of the
+// last position leaves the greedy next token at tok_seq[base + n] when
+// base + n >= prompt_end, as a decode step does.
+static int run_chunk(sllm_cuda_ctx* c, int base, int n, int prompt_end, int heads, float* logits_dev) {
+    const sllm_cuda_model* m = c->m;
+    const cudaStream_t st = c->stream;
+    const int E = m->n_embd, G = m->n_embd_gqa, F = m->n_ff;
+    int rc = chunk_alloc(c);
+    if (rc != SLLM_CUDA_OK) return rc;
+    int* fb = fallback_counter();
+    int* gerr = gemm_error_word();
+    if (fb == nullptr || gerr == nullptr) return fail(SLLM_CUDA_ERR_NOMEM, "chunk: diagnostics words");
+    CK(cudaStreamSynchronize(st), "chunk positions");        // the pinned staging is free again
+    for (int t = 0; t < n; ++t) c->ch.pos_host[t] = base + t;
+    CK(cudaMemcpyAsync(c->ch.pos, c->ch.pos_host, (size_t)n * 4, cudaMemcpyHostToDevice, st), "chunk positions");
+    CK(launch_embed_rows(m->tok_embd, c->tok_seq + base, n, E, m->n_vocab, c->ch.x, st), "chunk embed");
+    auto gemm = [&](const uint8_t* w, const uint8_t* w2, int rows, int K, float* y) {
+        GemmArgs a{};
+        a.w = w; a.w2 = w2; a.q = c->ch.qa; a.acts = c->ch.acts; a.dots = nullptr; a.y = y;
+        a.m = n; a.n_rows = rows; a.K = K;
+        const char* why = nullptr;
+        const int r = gemm_check(a, &why);
+        if (r != SLLM_CUDA_OK) return fail(r, "chunk gemm: %s", why);
+        CK(launch_i2s_gemm(a, gerr, st), "chunk gemm");
+        return (int)SLLM_CUDA_OK;
+    };
+    const int force = g_force_fallback;
+    for (int l = 0; l < m->n_layer; ++l) {
+        const DevLayer& L = m->layers[l];
+        // attn_norm -> Q, K, V of every token (src/forward.c:631-666)
+        CK(launch_norm_quant_rows(c->ch.x, L.attn_norm, E, m->eps, n, c->ch.qa, c->ch.acts, fb, force, st), "chunk norm");
+        if ((rc = gemm(L.wq, nullptr, E, E, c->ch.q)) != SLLM_CUDA_OK) return rc;
+        if ((rc = gemm(L.wk, nullptr, G, E, c->ch.k)) != SLLM_CUDA_OK) return rc;
+        if ((rc = gemm(L.wv, nullptr, G, E, c->ch.v)) != SLLM_CUDA_OK) return rc;
+        // RoPE, the cache stores of every token, then attention (src/forward.c:668-726)
+        AttnParams ap{};
+        ap.q = c->ch.q; ap.k = c->ch.k; ap.v = c->ch.v;
+        ap.k_cache = kv_layer_ptr(c, c->k_cache, l);
+        ap.v_cache = kv_layer_ptr(c, c->v_cache, l);
+        ap.kv_f16 = c->kv_f16 ? kAttnKvF16 : 0;
+        ap.rope_cos = c->rope_cos; ap.rope_sin = c->rope_sin;
+        ap.out = c->ch.attn; ap.n_ctx = c->n_ctx;
+        ap.group = m->n_head / m->n_head_kv;
+        ap.attn_scale = 1.0f / sqrtf((float)m->head_dim);
+        ap.fallback_count = fb; ap.force_fallback = force;
+        CK(launch_chunk_kv_store(ap, c->ch.pos, n, m->n_head_kv, E, G, st), "chunk kv store");
+        CK(launch_attention_chunk(ap, c->ch.pos, n, m->n_head, E, G, st), "chunk attention");
+        // attn_sub_norm -> O, + x (src/forward.c:728-750)
+        CK(launch_norm_quant_rows(c->ch.attn, L.attn_sub_norm, E, m->eps, n, c->ch.qa, c->ch.acts, fb, force, st),
+           "chunk norm");
+        if ((rc = gemm(L.wo, nullptr, E, E, c->ch.proj)) != SLLM_CUDA_OK) return rc;
+        CK(launch_add(c->ch.proj, c->ch.x, c->ch.ffn_inp, (size_t)n * E, st), "chunk residual");
+        // ffn_norm -> gate, up, silu(gate) * up (src/forward.c:752-779)
+        CK(launch_norm_quant_rows(c->ch.ffn_inp, L.ffn_norm, E, m->eps, n, c->ch.qa, c->ch.acts, fb, force, st),
+           "chunk norm");
+        if ((rc = gemm(L.gate, L.up, F, E, c->ch.h)) != SLLM_CUDA_OK) return rc;
+        // ffn_sub_norm -> down, + ffn_inp (src/forward.c:781-801)
+        CK(launch_norm_quant_rows(c->ch.h, L.ffn_sub_norm, F, m->eps, n, c->ch.qa, c->ch.acts, fb, force, st),
+           "chunk norm");
+        if ((rc = gemm(L.down, nullptr, E, F, c->ch.proj)) != SLLM_CUDA_OK) return rc;
+        CK(launch_add(c->ch.proj, c->ch.ffn_inp, c->ch.x, (size_t)n * E, st), "chunk residual");
+    }
+    count_launches((long long)m->n_layer * 15 + 1);
+    // the heads: output_norm + the tied F16 head + argmax of each position
+    // wanted, in position order (src/forward.c:803-833)
+    const int h0 = heads < 0 ? 0 : n - std::min(heads, n);
+    if (h0 < n) {
+        // slots of the pinned staging of their own: a decode step enqueued
+        // right after this may rewrite slots 0 and 1 before these copies run
+        c->pinned[4] = base + h0;
+        c->pinned[5] = prompt_end;
+        CK(cudaMemcpyAsync(c->pos, &c->pinned[4], 4, cudaMemcpyHostToDevice, st), "set pos");
+        CK(cudaMemcpyAsync(c->prompt_end, &c->pinned[5], 4, cudaMemcpyHostToDevice, st), "set prompt end");
+        const size_t V = m->n_vocab;
+        for (int t = h0; t < n; ++t) {
+            LmParams lp{};
+            lp.x = c->ch.x + (size_t)t * E; lp.norm_w = m->output_norm; lp.eps = m->eps; lp.embd = m->tok_embd;
+            lp.E = E; lp.V = m->n_vocab; lp.logits = c->logits;
+            lp.part_v = c->part_v; lp.part_i = c->part_i; lp.counter = c->counter; lp.argmax_out = c->argmax;
+            lp.pos_ptr = c->pos; lp.tok_seq = c->tok_seq; lp.prompt_end = c->prompt_end;
+            lp.argmax_hist = c->argmax_hist; lp.n_ctx = c->n_ctx; lp.fallback_count = fb; lp.force_fallback = force;
+            CK(launch_lm_head(lp, c->lm_grid, st), "chunk head");
+            count_launches(1);
+            if (logits_dev != nullptr)
+                CK(cudaMemcpyAsync(logits_dev + (size_t)t * V, c->logits, V * 4, cudaMemcpyDeviceToDevice, st),
+                   "copy logits");
+        }
+    }
+    return SLLM_CUDA_OK;
+}
+
+// a GEMM whose bounded wait gave up reports it once (the word is cleared)
+static int chunk_error() {
+    int* w = gemm_error_word();
+    int v = 0;
+    if (w != nullptr && cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && v != 0) {
+        cudaMemset(w, 0, sizeof(int));
+        return fail(SLLM_CUDA_ERR_TIMEOUT, "chunk: a GEMM's bounded wait gave up (code %d)", v);
+    }
+    return SLLM_CUDA_OK;
 }
 
 extern "C" int sllm_cuda_forward_chunk(const sllm_cuda_model* m, sllm_cuda_ctx* c, const int32_t* tokens, int32_t n,
@@ -1013,7 +1170,15 @@ extern "C" int sllm_cuda_forward_chunk(const sllm_cuda_model* m, sllm_cuda_ctx* 
         c->chunk_cap = n;
     }
     CK(cudaMemcpyAsync(c->tok_seq + base, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream), "tokens");
-    int rc = run_steps(c, base, n, base + n, logits_out ? c->chunk_logits : nullptr);
+    int rc;
+    if (n >= 2 && chunk_path_ok(c)) {
+        // every position's head runs: each position's logits and argmax are outputs
+        CK(cudaEventRecord(c->run_ev[0], c->stream), "run timer");
+        rc = run_chunk(c, base, n, base + n, -1, logits_out ? c->chunk_logits : nullptr);
+        if (rc == SLLM_CUDA_OK) CK(cudaEventRecord(c->run_ev[1], c->stream), "run timer");
+    } else {
+        rc = run_steps(c, base, n, base + n, logits_out ? c->chunk_logits : nullptr);
+    }
     if (rc != SLLM_CUDA_OK) return rc;
     if (logits_out != nullptr)
         CK(cudaMemcpyAsync(logits_out, c->chunk_logits, (size_t)n * V * 4, cudaMemcpyDeviceToHost, c->stream), "logits");
@@ -1024,6 +1189,7 @@ extern "C" int sllm_cuda_forward_chunk(const sllm_cuda_model* m, sllm_cuda_ctx* 
         const int rc_e = engine_error(c->eng_decode);
         if (rc_e != SLLM_CUDA_OK) return rc_e;
     }
+    if ((rc = chunk_error()) != SLLM_CUDA_OK) return rc;
     c->n_past = base + n;
     c->have_logits = true;
     return SLLM_CUDA_OK;
@@ -1053,7 +1219,25 @@ extern "C" int sllm_cuda_generate_greedy(const sllm_cuda_model* m, sllm_cuda_ctx
     // with no prompt and a history, tok_seq[base] already holds the argmax of
     // the last logits, written by the step that produced them
     const int steps = n_prompt + n_new;
-    if (steps > 0) {
+    if (n_prompt >= 2 && chunk_path_ok(c)) {
+        // the prompt as chunks of up to 256 tokens on the tensor cores; only
+        // the last position's head matters (its logits and next token), then
+        // one decode step per new token
+        CK(cudaEventRecord(c->run_ev[0], c->stream), "run timer");
+        for (int done = 0; done < n_prompt;) {
+            const int take = std::min(kChunkMax, n_prompt - done);
+            const bool last = done + take == n_prompt;
+            int rc = run_chunk(c, base + done, take, base + n_prompt, last ? 1 : 0, nullptr);
+            if (rc != SLLM_CUDA_OK) return rc;
+            done += take;
+        }
+        if (n_new > 0) {
+            int rc = run_steps(c, base + n_prompt, n_new, base + n_prompt, nullptr, false);
+            if (rc != SLLM_CUDA_OK) return rc;
+        } else {
+            CK(cudaEventRecord(c->run_ev[1], c->stream), "run timer");
+        }
+    } else if (steps > 0) {
         int rc = run_steps(c, base, steps, base + n_prompt, nullptr);
         if (rc != SLLM_CUDA_OK) return rc;
     }
@@ -1063,6 +1247,10 @@ extern "C" int sllm_cuda_generate_greedy(const sllm_cuda_model* m, sllm_cuda_ctx
     if (c->eng_decode.built) {
         const int rc_e = engine_error(c->eng_decode);
         if (rc_e != SLLM_CUDA_OK) return rc_e;
+    }
+    {
+        const int rc_c = chunk_error();
+        if (rc_c != SLLM_CUDA_OK) return rc_c;
     }
     c->n_past = base + steps;
     if (steps > 0) c->have_logits = true;

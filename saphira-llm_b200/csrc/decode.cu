@@ -12,6 +12,8 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "libm_expf.h"
+#include <algorithm>
+
 #include "attn.cuh"
 
 namespace sllm {
@@ -50,6 +52,58 @@ __global__ void embed_kernel(const uint16_t* __restrict__ tok_embd, const int32_
         x[d] = f16_embd(row[d]);
 }
 
+// the embeddings of n tokens, one CTA per token
+__global__ void embed_rows_kernel(const uint16_t* __restrict__ tok_embd, const int32_t* __restrict__ tok_seq, int E,
+                                  int V, float* __restrict__ x) {
+    pdl_wait_d();
+    int tok = tok_seq[blockIdx.x];
+    if ((unsigned)tok >= (unsigned)V) tok = 0;
+    const uint16_t* row = tok_embd + (size_t)tok * (size_t)E;
+    float* xr = x + (size_t)blockIdx.x * E;
+    for (int d = threadIdx.x; d < E; d += blockDim.x) xr[d] = f16_embd(row[d]);
+}
+
+// RoPE NEOX on the k of every token of a chunk and the store of k and v at
+// its position, exactly as attention_head does for one position (the same
+// products and sums, the same rounding of an f16 cache); one CTA of 128
+// threads per (token, kv head)
+__global__ void chunk_kv_store_kernel(const AttnParams p, const int32_t* __restrict__ pos_arr, int E, int G) {
+    pdl_wait_d();
+    const int t = blockIdx.x, kvh = blockIdx.y, i = threadIdx.x;
+    const int pos = pos_arr[t];
+    const int nctx = p.n_ctx;
+    const float* kr = p.k + (size_t)t * G + kvh * kHeadDim;
+    const float* vr = p.v + (size_t)t * G + kvh * kHeadDim;
+    const bool f16 = (p.kv_f16 & kAttnKvF16) != 0;
+    const size_t elt = f16 ? 2 : 4;
+    char* kT = reinterpret_cast<char*>(p.k_cache) + (size_t)kvh * kHeadDim * nctx * elt;
+    char* vC = reinterpret_cast<char*>(p.v_cache) + (size_t)kvh * nctx * kHeadDim * elt;
+    float k;
+    if (i < kHeadDim / 2) {
+        const float c = p.rope_cos[(size_t)pos * (kHeadDim / 2) + i], s = p.rope_sin[(size_t)pos * (kHeadDim / 2) + i];
+        k = __fsub_rn(__fmul_rn(kr[i], c), __fmul_rn(kr[i + 64], s));
+    } else {
+        const int j = i - 64;
+        const float c = p.rope_cos[(size_t)pos * (kHeadDim / 2) + j], s = p.rope_sin[(size_t)pos * (kHeadDim / 2) + j];
+        k = __fadd_rn(__fmul_rn(kr[j], s), __fmul_rn(kr[j + 64], c));
+    }
+    const float v = vr[i];
+    if (f16) {
+        reinterpret_cast<__half*>(kT)[(size_t)i * nctx + pos] = __float2half_rn(k);
+        reinterpret_cast<__half*>(vC)[(size_t)pos * kHeadDim + i] = __float2half_rn(v);
+    } else {
+        reinterpret_cast<float*>(kT)[(size_t)i * nctx + pos] = k;
+        reinterpret_cast<float*>(vC)[(size_t)pos * kHeadDim + i] = v;
+    }
+}
+
+__global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ out,
+                           size_t n) {
+    pdl_wait_d();
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = __fadd_rn(a[i], b[i]);
+}
+
 // ---------------------------------------------------------------------------
 // attention for one query position, one CTA per query head
 // ---------------------------------------------------------------------------
@@ -68,6 +122,25 @@ attention_kernel(const AttnParams p) {
     pdl_trigger_d();
     pdl_wait_d();                 // q, k, v come from the previous kernel
     attention_head<kAttnThreads>(p, blockIdx.x, threadIdx.x, sc, qs, kcur, fred, dred, CtaSync());
+}
+
+// every (head, token) of a chunk whose K and V are already in the cache
+__global__ void __launch_bounds__(kAttnThreads)
+attention_chunk_kernel(const AttnParams p, const int32_t* __restrict__ pos_arr, int E, int G) {
+    extern __shared__ __align__(16) float sc[];
+    __shared__ float qs[kHeadDim], kcur[kHeadDim];
+    __shared__ float fred[32];
+    __shared__ double dred[32];
+    pdl_wait_d();
+    const int t = blockIdx.y;
+    AttnParams pt = p;
+    pt.q = p.q + (size_t)t * E;
+    pt.k = p.k + (size_t)t * G;
+    pt.v = p.v + (size_t)t * G;
+    pt.out = p.out + (size_t)t * E;
+    pt.pos_ptr = pos_arr + t;
+    pt.kv_f16 = p.kv_f16 | kAttnKvStored;
+    attention_head<kAttnThreads>(pt, blockIdx.x, threadIdx.x, sc, qs, kcur, fred, dred, CtaSync());
 }
 
 // ---------------------------------------------------------------------------
@@ -268,6 +341,30 @@ cudaError_t prepare_decode_kernels() {
 cudaError_t launch_attention(const AttnParams& p, int n_head, cudaStream_t st) {
     const size_t smem = (size_t)p.n_ctx * sizeof(float);
     return launch_pdl(attention_kernel, dim3(n_head), dim3(kAttnThreads), smem, st, true, p);
+}
+
+cudaError_t launch_embed_rows(const uint16_t* tok_embd, const int32_t* tok_seq, int n, int E, int V, float* x,
+                              cudaStream_t st) {
+    return launch_pdl(embed_rows_kernel, dim3(n), dim3(256), 0, st, false, tok_embd, tok_seq, E, V, x);
+}
+
+cudaError_t launch_chunk_kv_store(const AttnParams& p, const int32_t* pos, int n, int n_head_kv, int E, int G,
+                                  cudaStream_t st) {
+    return launch_pdl(chunk_kv_store_kernel, dim3(n, n_head_kv), dim3(kHeadDim), 0, st, false, p, pos, E, G);
+}
+
+cudaError_t launch_attention_chunk(const AttnParams& p, const int32_t* pos, int n, int n_head, int E, int G,
+                                   cudaStream_t st) {
+    const size_t smem = (size_t)p.n_ctx * sizeof(float);
+    cudaError_t e = cudaFuncSetAttribute(attention_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         attention_max_ctx() * (int)sizeof(float));
+    if (e != cudaSuccess) return e;
+    return launch_pdl(attention_chunk_kernel, dim3(n_head, n), dim3(kAttnThreads), smem, st, false, p, pos, E, G);
+}
+
+cudaError_t launch_add(const float* a, const float* b, float* out, size_t n, cudaStream_t st) {
+    const int grid = (int)std::min<size_t>((n + 255) / 256, 1184);
+    return launch_pdl(add_kernel, dim3(grid), dim3(256), 0, st, false, a, b, out, n);
 }
 
 int lm_head_grid(int num_sms) { return 2 * num_sms; }

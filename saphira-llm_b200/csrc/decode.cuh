@@ -21,8 +21,11 @@ struct AttnParams {
     float attn_scale;        // 1.0f / sqrtf(128.0f)
     int* fallback_count;     // nullable
     int force_fallback;
-    int kv_f16;              // 1: the cache holds f16 (the fp16 KV option), 0: f32 (the reference's)
+    int kv_f16;              // kAttnKvF16: the cache holds f16 (the fp16 KV option), else f32 (the
+                             // reference's); | kAttnKvStored: this position's k, v are already stored
 };
+constexpr int kAttnKvF16 = 1;
+constexpr int kAttnKvStored = 2;
 
 struct LmParams {
     const float* x;          // residual stream [E]
@@ -57,6 +60,19 @@ cudaError_t launch_embed(const uint16_t* tok_embd, const int32_t* tok_seq, const
 int attention_max_ctx();
 cudaError_t prepare_decode_kernels();
 cudaError_t launch_attention(const AttnParams& p, int n_head, cudaStream_t st);
+// The multi-token (chunk) forms, n tokens at positions pos[0..n): the f16
+// embedding rows of tok_seq[base..base+n) into x [n][E]; RoPE + store of every
+// token's K and V (p.q/k/v/out are the chunk's row-major [n][...] buffers);
+// then attention for every (head, token) with the cache already holding the
+// chunk (src/forward.c:684-726 per column).
+cudaError_t launch_embed_rows(const uint16_t* tok_embd, const int32_t* tok_seq, int n, int E, int V, float* x,
+                              cudaStream_t st);
+cudaError_t launch_chunk_kv_store(const AttnParams& p, const int32_t* pos, int n, int n_head_kv, int E, int G,
+                                  cudaStream_t st);
+cudaError_t launch_attention_chunk(const AttnParams& p, const int32_t* pos, int n, int n_head, int E, int G,
+                                   cudaStream_t st);
+// out[i] = a[i] + b[i] (the residual adds, src/forward.c:745-750, 796-801)
+cudaError_t launch_add(const float* a, const float* b, float* out, size_t n, cudaStream_t st);
 int lm_head_grid(int num_sms);
 cudaError_t launch_lm_head(const LmParams& p, int grid, cudaStream_t st);
 

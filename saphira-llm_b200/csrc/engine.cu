@@ -623,7 +623,7 @@ i2s_engine_kernel(const EngParams P) {
                         // will read (positions < pos), into L2 a stage ahead
                         const AttnParams& ap = s_attn[s_ops[o].group];
                         const int pos = *(volatile const int32_t*)ap.pos_ptr;
-                        const uint32_t eb = ap.kv_f16 ? 2u : 4u;     // bytes per cached value
+                        const uint32_t eb = (ap.kv_f16 & kAttnKvF16) ? 2u : 4u;     // bytes per cached value
                         for (int h = r; h < r + n && pos > 0; ++h) {
                             const int kvh = h / ap.group;
                             const char* vC = reinterpret_cast<const char*>(ap.v_cache) +

@@ -51,6 +51,10 @@ int gemv_max_k();
 cudaError_t launch_gemv(const GemvParams& p, int pro, int epi, int num_sms, cudaStream_t st,
                         int mode = GEMV_PLAIN);
 cudaError_t launch_quant_act(const float* x, int n, int8_t* q, sllm_cuda_act* act, cudaStream_t st);
+// RMSNorm (certified, as the GEMV prologue) + quantisation of each row of a
+// row-major [rows][K] batch; K % 128 == 0, K <= gemv_max_k()
+cudaError_t launch_norm_quant_rows(const float* x, const float* w, int K, float eps, int rows, int8_t* q,
+                                   sllm_cuda_act* acts, int* fb, int force, cudaStream_t st);
 // rows independent vectors of a row-major [rows][n] batch, one block each
 cudaError_t launch_quant_act_rows(const float* x, int rows, int n, int8_t* q, sllm_cuda_act* acts, cudaStream_t st);
 

@@ -318,6 +318,26 @@ i2s_gemv_kernel(const GemvParams p) {
     if (!DEP) pdl_wait();   // complete in stream order
 }
 
+// RMSNorm + quantisation of every row of a row-major [rows][K] batch, one CTA
+// per row: the per-column prologue of a multi-token chunk (src/forward.c:
+// 631-666, 728-741, 752-764, 781-792, column by column), with the GEMV
+// prologue's arithmetic; q in natural order for the GEMM.
+template <int KPT>
+__global__ void __launch_bounds__(kGemvThreads)
+norm_quant_rows_kernel(const GemvParams p, int8_t* q, sllm_cuda_act* acts) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ ProSmem ps;
+    const int K = p.K;
+    int8_t* qs = reinterpret_cast<int8_t*>(smem);
+    float* xs = reinterpret_cast<float*>(smem + K);
+    GemvParams pr = p;
+    pr.x = p.x + (size_t)blockIdx.x * K;
+    const sllm_cuda_act act = gemv_prologue<PRO_NORM, KPT, true>(pr, qs, xs, ps);
+    int4* dst = reinterpret_cast<int4*>(q + (size_t)blockIdx.x * K);
+    for (int i = threadIdx.x; i < K / 16; i += kGemvThreads) dst[i] = reinterpret_cast<const int4*>(qs)[i];
+    if (threadIdx.x == 0) acts[blockIdx.x] = act;
+}
+
 // standalone quantisation (sllm_cuda_i2s_quant_act): one CTA
 __global__ void __launch_bounds__(kGemvThreads)
 quant_act_kernel(const float* x, int n, int8_t* q, sllm_cuda_act* act) {
@@ -466,6 +486,28 @@ cudaError_t launch_gemv(const GemvParams& p_in, int pro, int epi, int num_sms, c
     if (pro == PRO_NORM && epi == EPI_RESID) return launch_wpl<U, PRO_NORM, EPI_RESID, true>(p, wpl, grid, st, pdl);
     if (pro == PRO_NORM && epi == EPI_SILU) return launch_wpl<U, PRO_NORM, EPI_SILU, true>(p, wpl, grid, st, pdl);
     return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_norm_quant_rows(const float* x, const float* w, int K, float eps, int rows, int8_t* q,
+                                   sllm_cuda_act* acts, int* fb, int force, cudaStream_t st) {
+    if (K % kQK != 0 || K > gemv_max_k() || rows < 1) return cudaErrorInvalidValue;
+    GemvParams p{};
+    p.K = K;
+    p.x = x;
+    p.norm_w = w;
+    p.eps = eps;
+    p.inv_k = 1.0 / (double)K;
+    p.fallback_count = fb;
+    p.force_fallback = force;
+    const int kpt = (K / 4 + kGemvThreads - 1) / kGemvThreads;    // 1..4
+    const size_t smem = (size_t)K * 5;                              // qs, then the fallback's floats
+    switch (kpt) {
+        case 1: norm_quant_rows_kernel<1><<<rows, kGemvThreads, smem, st>>>(p, q, acts); break;
+        case 2: norm_quant_rows_kernel<2><<<rows, kGemvThreads, smem, st>>>(p, q, acts); break;
+        case 3: norm_quant_rows_kernel<3><<<rows, kGemvThreads, smem, st>>>(p, q, acts); break;
+        default: norm_quant_rows_kernel<4><<<rows, kGemvThreads, smem, st>>>(p, q, acts); break;
+    }
+    return cudaGetLastError();
 }
 
 cudaError_t launch_quant_act(const float* x, int n, int8_t* q, sllm_cuda_act* act, cudaStream_t st) {

@@ -278,3 +278,41 @@ def test_decode_step_runs_on_the_engine(cuda, orc, synth):
     assert r1 == r2 == 0 and t1.tolist() == t2.tolist()
     assert np.array_equal(bits(gc.last_logits()), bits(oc.last_logits()))
     assert per_step == 3, per_step
+
+
+def test_chunk_path_long_prompt_and_boundaries(cuda, orc, synth):
+    """The multi-token chunk path on the tensor cores: a 300-token prompt
+    runs as two chunks (256 + 44), a forward_chunk split at another boundary
+    gives the same bits as one chunk, and decoding continues from either,
+    all equal to the oracle's one-token-at-a-time order (a chunk is not a
+    semantic boundary, src/forward.c:572-588)."""
+    cfg = synth.small_config(n_layer=2, n_embd=512, n_ff=1536, n_head=4, n_head_kv=2, n_vocab=2003)
+    m = synth.SynthModel(cfg, seed=303)
+    model = cuda.Model(m.desc())
+    gc, oc = model.ctx(340), orc.ctx(m.desc(), 340)
+    prompt = np.random.default_rng(303).integers(0, cfg.n_vocab, 300).astype(np.int32)
+    r1, t1 = gc.generate(prompt, 12)
+    r2, t2 = oc.generate(prompt, 12)
+    assert r1 == r2 == 0 and t1.tolist() == t2.tolist()
+    assert np.array_equal(bits(gc.last_logits()), bits(oc.last_logits()))
+    # the same 40 tokens as one chunk and as chunks of 23 + 17
+    toks = prompt[:40]
+    a = model.ctx(64)
+    r, la, _ = a.forward_chunk(toks, 0)
+    assert r == 0
+    b = model.ctx(64)
+    r, lb1, _ = b.forward_chunk(toks[:23], 0)
+    assert r == 0
+    r, lb2, _ = b.forward_chunk(toks[23:], 23)
+    assert r == 0
+    assert np.array_equal(bits(la), bits(np.concatenate([lb1, lb2])))
+    ra, ta = a.generate(np.zeros(0, np.int32), 6)
+    rb, tb = b.generate(np.zeros(0, np.int32), 6)
+    o2 = orc.ctx(m.desc(), 64)
+    ro, lo = o2.forward_chunk(toks, 0)
+    ro2, to = o2.generate(np.zeros(0, np.int32), 6)
+    assert ra == rb == ro2 == 0 and ta.tolist() == tb.tolist() == to.tolist()
+    assert np.array_equal(bits(la), bits(lo))
+    for c in (gc, a, b):
+        c.close()
+    model.close()
