@@ -29,7 +29,7 @@ from . import abi
 
 GGUF_ALIGN = 32
 TYPE_F32, TYPE_F16, TYPE_I2_S = 0, 1, 36
-VT_UINT32, VT_FLOAT32, VT_STRING = 4, 6, 8
+VT_UINT32, VT_FLOAT32, VT_STRING, VT_ARRAY = 4, 6, 8, 9
 ARCH = "bitnet-b1.58"
 
 
@@ -143,7 +143,22 @@ def _nbytes(ttype, dims):
     return {TYPE_F32: 4 * n, TYPE_F16: 2 * n, TYPE_I2_S: n // 4 + 32}[ttype]
 
 
-def _kv_bytes(cfg):
+def byte_level_tokens():
+    """The 256 single-byte tokens of a GPT-2 byte-level BPE vocabulary: the
+    published byte -> printable-character mapping (printable Latin-1 bytes map
+    to themselves, the other 68 to U+0100 upwards, in byte order)."""
+    keep = list(range(0x21, 0x7F)) + list(range(0xA1, 0xAD)) + list(range(0xAE, 0x100))
+    table, extra = {}, 0
+    for b in range(256):
+        if b in keep:
+            table[b] = b
+        else:
+            table[b] = 0x100 + extra
+            extra += 1
+    return [chr(table[b]) for b in range(256)]
+
+
+def _kv_bytes(cfg, tokenizer=False):
     out = bytearray()
 
     def key(k):
@@ -172,7 +187,20 @@ def _kv_bytes(cfg):
     u32(a + "vocab_size", cfg.n_vocab)
     f32(a + "attention.layer_norm_rms_epsilon", cfg.eps)
     f32(a + "rope.freq_base", cfg.rope_base)
-    return bytes(out), 11
+    n_kv = 11
+    if tokenizer:
+        # a byte-level BPE vocabulary without merges: every byte its own token
+        # (the first 256 ids), the rest placeholders, so that the reference's
+        # tokenizer loads it (src/tokenizer.c: model "gpt2", >= 256 tokens)
+        s("tokenizer.ggml.model", "gpt2")
+        toks = byte_level_tokens() + [f"<|synthetic_{i}|>" for i in range(256, cfg.n_vocab)]
+        key("tokenizer.ggml.tokens")
+        out.extend(struct.pack("<IIQ", VT_ARRAY, VT_STRING, len(toks)))
+        for t in toks:
+            tb = t.encode()
+            out.extend(struct.pack("<Q", len(tb)) + tb)
+        n_kv += 2
+    return bytes(out), n_kv
 
 
 class SynthModel:
@@ -182,7 +210,7 @@ class SynthModel:
     C ABI takes (pointers into the image, which must stay alive).
     """
 
-    def __init__(self, cfg: Config, seed: int = 1234):
+    def __init__(self, cfg: Config, seed: int = 1234, tokenizer: bool = False):
         self.cfg = cfg
         self.seed = seed
         rng = np.random.Generator(np.random.PCG64(seed))
@@ -190,7 +218,7 @@ class SynthModel:
                  ("output_norm.weight", TYPE_F32, (cfg.n_embd,))]
         for il in range(cfg.n_layer):
             specs += _layer_tensors(cfg, il)
-        kv, n_kv = _kv_bytes(cfg)
+        kv, n_kv = _kv_bytes(cfg, tokenizer)
         info = bytearray()
         offs, off = [], 0
         for name, tt, dims in specs:

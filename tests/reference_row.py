@@ -8,7 +8,10 @@ import os
 import numpy as np
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-ROW_SO = os.path.join(ROOT, "saphira-llm_b200", "reference_row", "_build", "libsaphira_llm_row.so")
+ROW_DIR = os.path.join(ROOT, "saphira-llm_b200", "reference_row", "_build")
+ROW_SO = os.path.join(ROW_DIR, "libsaphira_llm_row.so")
+CLI = os.path.join(ROW_DIR, "saphira-llm")
+TGBENCH = os.path.join(ROW_DIR, "saphira-llm-tgbench")
 CPU, CUDA, AUTO = 0, 1, 2
 
 _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
@@ -97,3 +100,25 @@ class RowModel:
             self.L.sllm_model_free(self.m)
             self.m = C.c_void_p()
         self.L.sllm_gguf_close(self.g)
+
+
+def run_cli(model_path, backend, prompt="Hello world", n=8):
+    """The reference's CLI (src/main.c with --backend): (exit code, generated text, stderr)."""
+    import subprocess
+    r = subprocess.run([CLI, "-m", model_path, "-p", prompt, "-n", str(n), "-t", "1", "--backend", backend],
+                       capture_output=True, text=True, timeout=300)
+    text = r.stdout.split("\nsllm_bench")[0]
+    return r.returncode, text, r.stderr
+
+
+def run_tgbench(model_path, backend, n=16):
+    """The reference's decode benchmark (bench/tg_bench.c with --backend):
+    (exit code, token checksum or None, stdout)."""
+    import subprocess
+    r = subprocess.run([TGBENCH, "-m", model_path, "-n", str(n), "-t", "1", "-r", "2", "-w", "1", "--no-calibrate",
+                        "--backend", backend], capture_output=True, text=True, timeout=300)
+    cs = None
+    for line in r.stdout.splitlines():
+        if line.startswith("token_checksum"):
+            cs = int(line.split()[1])
+    return r.returncode, cs, r.stdout

@@ -9,6 +9,8 @@ the device must have done the work (this library's kernel counter moves),
 and state files must cross between the rows byte for byte: a file the CUDA
 row writes equals the CPU row's for the same history, and each row continues
 identically from the other's file."""
+import os
+
 import numpy as np
 import pytest
 
@@ -125,3 +127,23 @@ def test_state_load_refusals(cuda, synth, tmp_path):
     other.close()
     c.close()
     model.close()
+
+
+def test_cli_and_tgbench_on_the_cuda_row(cuda, synth, tmp_path):
+    """The reference's own CLI and decode benchmark with --backend cuda: the
+    same generated text as the CPU row, and tg_bench's token checksum (its
+    witness that a faster row produced the same tokens) equal across rows."""
+    assert rr.available() and os.path.exists(rr.CLI), "build saphira-llm_b200/reference_row first"
+    cfg = synth.small_config(n_layer=2, n_embd=512, n_ff=1536, n_head=4, n_head_kv=2, n_vocab=1000)
+    m = synth.SynthModel(cfg, seed=6, tokenizer=True)
+    path = str(tmp_path / "synth.gguf")
+    m.image.tofile(path)
+    rc1, text_gpu, err1 = rr.run_cli(path, "cuda", n=16)
+    rc2, text_cpu, err2 = rr.run_cli(path, "cpu", n=16)
+    assert rc1 == 0, err1
+    assert rc2 == 0, err2
+    assert text_gpu == text_cpu and len(text_gpu) > 0
+    rc1, cs_gpu, out1 = rr.run_tgbench(path, "cuda")
+    rc2, cs_cpu, out2 = rr.run_tgbench(path, "cpu")
+    assert rc1 == rc2 == 0, (out1, out2)
+    assert cs_gpu is not None and cs_gpu == cs_cpu

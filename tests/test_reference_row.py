@@ -21,7 +21,7 @@ def _row():
     return rr.Row()
 
 
-@pytest.mark.parametrize("name", ["forward.c.patch", "dispatch.c.patch"])
+@pytest.mark.parametrize("name", ["forward.c.patch", "dispatch.c.patch", "main.c.patch", "tg_bench.c.patch"])
 def test_patches_insert_only(name):
     body = open(os.path.join(ROW_DIR, name)).read().splitlines()
     hunks = [l for l in body if l.startswith("@@")]
@@ -69,3 +69,24 @@ def test_cuda_row_refuses_widths_it_does_not_run(synth):
     rm = row.open(m.image, rr.CUDA, 16)
     assert rm.rc == -4
     rm.close()
+
+
+def test_cli_and_tgbench_backend_flag(synth, tmp_path, cuda_absent):
+    """The CLI and tg_bench take --backend: the CPU row runs, "cuda" without
+    a device is refused (exit status, no output), an unknown row is a usage
+    error. The model file carries a byte-level BPE vocabulary so that the
+    reference's tokenizer loads it."""
+    if not os.path.exists(rr.CLI):
+        pytest.skip("the reference row CLI is not built (needs the reference source tree)")
+    cfg = synth.small_config(n_layer=2, n_vocab=1000)
+    m = synth.SynthModel(cfg, seed=5, tokenizer=True)
+    path = str(tmp_path / "synth.gguf")
+    m.image.tofile(path)
+    rc, text, err = rr.run_cli(path, "cpu")
+    assert rc == 0 and len(text) > 0, err
+    rc, text, err = rr.run_cli(path, "cuda")
+    assert rc != 0 and "CUDA row" in err
+    rc, _, err = rr.run_cli(path, "bogus")
+    assert rc == 2 and "--backend" in err
+    rc, cs, out = rr.run_tgbench(path, "cpu")
+    assert rc == 0 and cs is not None, out
