@@ -591,8 +591,10 @@ def tp_decode_leg(pkg, local, rank, world, args):
                            "gate/up) and one for down" if ctx.fused_layers() > 0 else
                            "persistent engine (one program per phase)") if ctx.uses_engine() else "per-GEMV kernels",
            "exchange": {"none": "none (one rank)", "nccl": "NCCL all-gather / int32 all-reduce in the step graph",
-                        "p2p": "one-shot peer-memory exchange (P2P stores + epoch flags) in the step graph"}[
-                            ctx.exchange_kind()]}
+                        "p2p": ("fused peer exchange: per layer one engine program storing into every rank's "
+                                "memory and waiting on flags inside its stages" if ctx.fused_exchange() else
+                                "one-shot peer-memory exchange kernels (P2P stores + epoch flags) in the step "
+                                "graph")}[ctx.exchange_kind()]}
     ctx.close()
     model.close()
     if comm is not None:
