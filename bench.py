@@ -831,6 +831,18 @@ def main():
         ms, per = time_device(fn, args.steps, args.warmup, stream, world)
     clocks = clk.summary()
     value = step_bytes * args.steps * world / (ms / 1e3) / 1e9
+    # one launch alone (idle device before and after, events around it): the
+    # figure without the overlap of consecutive launches that `value` includes
+    singles = []
+    for _ in range(10):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        singles.append(e0.elapsed_time(e1))
+    single_ms = float(np.median(singles))
 
     # e2e: host buffers through sllm_cuda_layer_projections
     host_in = torch.from_numpy(xs_host).pin_memory()
@@ -878,7 +890,13 @@ def main():
                                f"i2s_gemv_kernel ({launches} launches per step)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                     "bytes_per_launch": int(per_launch_bytes), "traffic": traffic},
+                     "bytes_per_launch": int(per_launch_bytes), "traffic": traffic,
+                     "timing": f"{args.steps} back-to-back launches between two events (consecutive launches "
+                               "overlap: each takes the SMs as the previous one's CTAs exit)",
+                     "single_launch": {"ms": round(single_ms, 4),
+                                       "achieved": round(step_bytes / (single_ms / 1e3) / 1e9, 1),
+                                       "frac": round(step_bytes / (single_ms / 1e3) / 1e9 / peak, 4),
+                                       "timing": "one launch between two events on an idle device, median of 10"}},
         "e2e": {"value": round(e2e, 3), "unit": "GB/s", "h2d_bytes_per_step": 4 * xs_n,
                 "d2h_bytes_per_step": 4 * ys_n * copies,
                 "api": "sllm_cuda_layer_projections (host buffers, wall clock)"},
