@@ -67,7 +67,8 @@ __global__ void embed_rows_kernel(const uint16_t* __restrict__ tok_embd, const i
 // its position, exactly as attention_head does for one position (the same
 // products and sums, the same rounding of an f16 cache); one CTA of 128
 // threads per (token, kv head)
-__global__ void chunk_kv_store_kernel(const AttnParams p, const int32_t* __restrict__ pos_arr, int E, int G) {
+__global__ void chunk_kv_store_kernel(const AttnParams p, const int32_t* __restrict__ pos_arr, int E, int G,
+                                      size_t seq_stride) {
     pdl_wait_d();
     const int t = blockIdx.x, kvh = blockIdx.y, i = threadIdx.x;
     const int pos = pos_arr[t];
@@ -76,8 +77,9 @@ __global__ void chunk_kv_store_kernel(const AttnParams p, const int32_t* __restr
     const float* vr = p.v + (size_t)t * G + kvh * kHeadDim;
     const bool f16 = (p.kv_f16 & kAttnKvF16) != 0;
     const size_t elt = f16 ? 2 : 4;
-    char* kT = reinterpret_cast<char*>(p.k_cache) + (size_t)kvh * kHeadDim * nctx * elt;
-    char* vC = reinterpret_cast<char*>(p.v_cache) + (size_t)kvh * nctx * kHeadDim * elt;
+    // token t's sequence: the same cache for a chunk, its own for a batch
+    char* kT = reinterpret_cast<char*>(p.k_cache) + (size_t)t * seq_stride + (size_t)kvh * kHeadDim * nctx * elt;
+    char* vC = reinterpret_cast<char*>(p.v_cache) + (size_t)t * seq_stride + (size_t)kvh * nctx * kHeadDim * elt;
     float k;
     if (i < kHeadDim / 2) {
         const float c = p.rope_cos[(size_t)pos * (kHeadDim / 2) + i], s = p.rope_sin[(size_t)pos * (kHeadDim / 2) + i];
@@ -126,7 +128,7 @@ attention_kernel(const AttnParams p) {
 
 // every (head, token) of a chunk whose K and V are already in the cache
 __global__ void __launch_bounds__(kAttnThreads)
-attention_chunk_kernel(const AttnParams p, const int32_t* __restrict__ pos_arr, int E, int G) {
+attention_chunk_kernel(const AttnParams p, const int32_t* __restrict__ pos_arr, int E, int G, size_t seq_stride) {
     extern __shared__ __align__(16) float sc[];
     __shared__ float qs[kHeadDim], kcur[kHeadDim];
     __shared__ float fred[32];
@@ -140,6 +142,8 @@ attention_chunk_kernel(const AttnParams p, const int32_t* __restrict__ pos_arr, 
     pt.out = p.out + (size_t)t * E;
     pt.pos_ptr = pos_arr + t;
     pt.kv_f16 = p.kv_f16 | kAttnKvStored;
+    pt.k_cache = reinterpret_cast<float*>(reinterpret_cast<char*>(p.k_cache) + (size_t)t * seq_stride);
+    pt.v_cache = reinterpret_cast<float*>(reinterpret_cast<char*>(p.v_cache) + (size_t)t * seq_stride);
     attention_head<kAttnThreads>(pt, blockIdx.x, threadIdx.x, sc, qs, kcur, fred, dred, CtaSync());
 }
 
@@ -349,17 +353,19 @@ cudaError_t launch_embed_rows(const uint16_t* tok_embd, const int32_t* tok_seq, 
 }
 
 cudaError_t launch_chunk_kv_store(const AttnParams& p, const int32_t* pos, int n, int n_head_kv, int E, int G,
-                                  cudaStream_t st) {
-    return launch_pdl(chunk_kv_store_kernel, dim3(n, n_head_kv), dim3(kHeadDim), 0, st, false, p, pos, E, G);
+                                  cudaStream_t st, size_t seq_stride) {
+    return launch_pdl(chunk_kv_store_kernel, dim3(n, n_head_kv), dim3(kHeadDim), 0, st, false, p, pos, E, G,
+                      seq_stride);
 }
 
 cudaError_t launch_attention_chunk(const AttnParams& p, const int32_t* pos, int n, int n_head, int E, int G,
-                                   cudaStream_t st) {
+                                   cudaStream_t st, size_t seq_stride) {
     const size_t smem = (size_t)p.n_ctx * sizeof(float);
     cudaError_t e = cudaFuncSetAttribute(attention_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          attention_max_ctx() * (int)sizeof(float));
     if (e != cudaSuccess) return e;
-    return launch_pdl(attention_chunk_kernel, dim3(n_head, n), dim3(kAttnThreads), smem, st, false, p, pos, E, G);
+    return launch_pdl(attention_chunk_kernel, dim3(n_head, n), dim3(kAttnThreads), smem, st, false, p, pos, E, G,
+                      seq_stride);
 }
 
 cudaError_t launch_add(const float* a, const float* b, float* out, size_t n, cudaStream_t st) {

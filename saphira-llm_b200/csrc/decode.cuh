@@ -67,10 +67,12 @@ cudaError_t launch_attention(const AttnParams& p, int n_head, cudaStream_t st);
 // chunk (src/forward.c:684-726 per column).
 cudaError_t launch_embed_rows(const uint16_t* tok_embd, const int32_t* tok_seq, int n, int E, int V, float* x,
                               cudaStream_t st);
+// seq_stride: bytes from token t's caches to token t+1's (0: one sequence,
+// the chunk's; a batch of sequences each with its own cache otherwise)
 cudaError_t launch_chunk_kv_store(const AttnParams& p, const int32_t* pos, int n, int n_head_kv, int E, int G,
-                                  cudaStream_t st);
+                                  cudaStream_t st, size_t seq_stride = 0);
 cudaError_t launch_attention_chunk(const AttnParams& p, const int32_t* pos, int n, int n_head, int E, int G,
-                                   cudaStream_t st);
+                                   cudaStream_t st, size_t seq_stride = 0);
 // out[i] = a[i] + b[i] (the residual adds, src/forward.c:745-750, 796-801)
 cudaError_t launch_add(const float* a, const float* b, float* out, size_t n, cudaStream_t st);
 int lm_head_grid(int num_sms);

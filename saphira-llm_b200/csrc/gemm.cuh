@@ -23,6 +23,7 @@ struct GemmArgs {
     int32_t* dots;               // [m][n_rows] or null (single tensor only)
     float* y;                    // [m][n_rows] or null; gate/up: h
     int m, n_rows, K;
+    int lda;                     // bytes from one token's q row to the next (0: K); a multiple of 16
 };
 
 // 0 when the shapes are supported (K % 128 == 0, 16-byte aligned rows and

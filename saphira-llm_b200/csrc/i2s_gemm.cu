@@ -536,11 +536,11 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 // a row-major [rows][cols] byte matrix, tiles of box_rows x box_cols bytes
 bool encode_2d(CUtensorMap* tm, const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
-               CUtensorMapSwizzle swizzle) {
+               CUtensorMapSwizzle swizzle, uint64_t row_bytes = 0) {
     PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
     if (enc == nullptr) return false;
     const cuuint64_t dims[2] = {cols, rows};
-    const cuuint64_t strides[1] = {cols};
+    const cuuint64_t strides[1] = {row_bytes != 0 ? row_bytes : cols};
     const cuuint32_t box[2] = {box_cols, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
@@ -568,7 +568,8 @@ cudaError_t launch_tile(const GemmArgs& a, int* error, cudaStream_t st) {
     static_assert(SK == 1 || (!PAIR && C::S * C::STAGE >= 4 * MT * BN * 128),
                   "a split CTA's partial accumulators (4 warps per token tile, 32 lanes x BN) fit its ring");
     CUtensorMap tm_a, tm_w, tm_w2;
-    if (!encode_2d(&tm_a, a.q, (uint64_t)a.K, (uint64_t)a.m, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+    if (!encode_2d(&tm_a, a.q, (uint64_t)a.K, (uint64_t)a.m, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B,
+                   (uint64_t)(a.lda > 0 ? a.lda : a.K)) ||
         !encode_2d(&tm_w, a.w, (uint64_t)(a.K / 4), (uint64_t)a.n_rows, kPK, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
     if (PAIR) {
@@ -647,6 +648,10 @@ int gemm_check(const GemmArgs& a, const char** why) {
     }
     if (!al16(a.w) || !al16(a.q) || (a.w2 != nullptr && !al16(a.w2))) {
         *why = "gemm: w and q must be 16-byte aligned";
+        return SLLM_CUDA_ERR_ARG;
+    }
+    if (a.lda != 0 && (a.lda < a.K || a.lda % 16 != 0)) {
+        *why = "gemm: the row stride of q must be at least K and a multiple of 16 bytes";
         return SLLM_CUDA_ERR_ARG;
     }
     if (a.w2 != nullptr ? a.y == nullptr : (a.y == nullptr && a.dots == nullptr)) {

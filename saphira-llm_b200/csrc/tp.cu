@@ -258,6 +258,13 @@ tp_norm_quant_cluster_kernel(const float* __restrict__ x, const float* __restric
     __shared__ float s_bcast;
     const int rank = (int)cl.block_rank();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // several clusters: one row each of a row-major [rows][K] batch
+    {
+        const int row = blockIdx.x / kNqCluster;
+        x += (size_t)row * K;
+        q += (size_t)row * K;
+        act += row;
+    }
     // programmatic dependent launch: the next launch (the down program, whose
     // consumers wait for this one) may be scheduled now, and x comes from the
     // previous launch
@@ -1064,10 +1071,11 @@ cudaError_t launch_count(cudaError_t e, int n) {
 // RMSNorm + quantisation of a whole vector: the eight-CTA cluster when the
 // length allows it (a multiple of 32, at most 32768), else one CTA
 cudaError_t launch_norm_quant(const float* x, const float* w, int K, float eps, int8_t* q, sllm_cuda_act* act,
-                              int* fb, int force, cudaStream_t st, const XWait& xw = XWait{}) {
+                              int* fb, int force, cudaStream_t st, const XWait& xw = XWait{}, int rows = 1) {
     const double inv_k = 1.0 / (double)K;
     const bool cluster = K % (4 * kNqCluster) == 0 && K <= 4 * kNqCluster * kNqThreads;
-    cudaLaunchConfig_t cfg = pdl_config(cluster ? kNqCluster : 1, kNqThreads, st);
+    if (rows > 1 && !cluster) return cudaErrorInvalidValue;      // several rows: the cluster form only
+    cudaLaunchConfig_t cfg = pdl_config(cluster ? kNqCluster * rows : 1, kNqThreads, st);
     cudaLaunchAttribute attr = pdl_attribute();
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
