@@ -484,6 +484,32 @@ SLLM_CUDA_API int sllm_cuda_tp_generate_greedy(sllm_cuda_tp_ctx * c, const int32
 /* the last step's logits of this shard's vocabulary rows */
 SLLM_CUDA_API int sllm_cuda_tp_last_logits(const sllm_cuda_tp_ctx * c, float * host_out);
 
+/*
+ * Batch decode over one shard: n_seq <= 16 sequences, each with its own KV
+ * cache of n_ctx positions, stepped together. The reference serves a batch
+ * as one context per sequence (src/forward.c:78-84, :466-562); here each
+ * layer GEMV of a step is one GEMM over the n_seq tokens on the tensor cores
+ * (every weight byte read once per step), and each sequence's tokens and
+ * logits equal, bit for bit, those of sllm_cuda_tp_generate_greedy on its own
+ * context. E <= 8192 and F <= 32768 (a multiple of 32). Needs comm as a
+ * context does.
+ */
+typedef struct sllm_cuda_tp_batch sllm_cuda_tp_batch;
+SLLM_CUDA_API int sllm_cuda_tp_batch_new(const sllm_cuda_tp_model * m, sllm_cuda_tp_comm * comm,
+                                         int32_t n_seq, int32_t n_ctx, sllm_cuda_tp_batch ** out);
+SLLM_CUDA_API void sllm_cuda_tp_batch_free(sllm_cuda_tp_batch * b);
+SLLM_CUDA_API int sllm_cuda_tp_batch_reset(sllm_cuda_tp_batch * b);
+/*
+ * sllm_generate_greedy (src/forward.c:885-938) for every sequence at once:
+ * prompts is row-major [n_seq][n_prompt] (the same length for every
+ * sequence; n_prompt may be 0 only to continue after an earlier call), out
+ * receives row-major [n_seq][n_new]. Failures as sllm_cuda_tp_generate_greedy.
+ */
+SLLM_CUDA_API int sllm_cuda_tp_batch_generate_greedy(sllm_cuda_tp_batch * b, const int32_t * prompts,
+                                                     int32_t n_prompt, int32_t n_new, int32_t * out);
+/* sequence seq's last-step logits of this shard's vocabulary rows */
+SLLM_CUDA_API int sllm_cuda_tp_batch_last_logits(const sllm_cuda_tp_batch * b, int32_t seq, float * host_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -30,6 +30,15 @@ SLLM_CUDA_API int sllm_cuda_test_fallback_count(void);
  * the device; -1 without a device.
  */
 SLLM_CUDA_API int sllm_cuda_test_gemm_error(void);
+/* The prefill GEMM's form: 0 by size (at most 16 tokens: weight rows as the
+ * MMA's M operand, tokens as N = 16), 1 the 128-token tiles, 2 the skinny
+ * form only. */
+SLLM_CUDA_API void sllm_cuda_test_gemm_form(int form);
+/* sllm_cuda_i2s_gemm over columns of a wider activation matrix: row t of the
+ * k contracted bytes starts at q + t * lda (lda >= k, a multiple of 16). */
+SLLM_CUDA_API int sllm_cuda_test_gemm_strided(const uint8_t * w, int32_t n_rows, int32_t k, int32_t m,
+                                              const int8_t * q, int32_t lda, const sllm_cuda_act * acts,
+                                              int32_t * dots, float * y, void * stream);
 
 /*
  * Greedy decode over the N contexts of ranks 0..N-1 of one tensor-parallel
@@ -127,6 +136,14 @@ SLLM_CUDA_API int sllm_cuda_test_projection_split(int32_t n_embd, int32_t n_ff, 
 SLLM_CUDA_API int sllm_cuda_test_engine_split(const int32_t * rows, const int32_t * K, const int32_t * epi,
                                 const int32_t * group, int32_t n_ops, const int32_t * stage_first,
                                 int32_t n_stages, int32_t grid, int32_t * out);
+
+/* device time of the last sllm_cuda_tp_batch_generate_greedy's steps (ms) */
+SLLM_CUDA_API float sllm_cuda_test_tp_batch_last_run_ms(const sllm_cuda_tp_batch * b);
+/* N batches of the N shards of one model on one device, the exchanges by
+ * device copies (as sllm_cuda_test_tp_generate_group) */
+SLLM_CUDA_API int sllm_cuda_test_tp_batch_generate_group(sllm_cuda_tp_batch ** bs, int32_t n,
+                                                         const int32_t * prompts, int32_t n_prompt,
+                                                         int32_t n_new, int32_t * out);
 
 #ifdef __cplusplus
 }

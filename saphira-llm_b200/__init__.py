@@ -52,6 +52,9 @@ def lib():
     L.sllm_cuda_i2s_gemm.argtypes = [vp, sz, sz, sz, vp, vp, vp, vp, vp]
     L.sllm_cuda_i2s_gemm_silu.argtypes = [vp, vp, sz, sz, sz, vp, vp, vp, vp]
     L.sllm_cuda_test_gemm_error.restype = C.c_int
+    L.sllm_cuda_test_gemm_form.argtypes = [C.c_int]
+    L.sllm_cuda_test_gemm_form.restype = None
+    L.sllm_cuda_test_gemm_strided.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp, vp, vp]
     L.sllm_cuda_tp_unique_id.argtypes = [vp]
     L.sllm_cuda_tp_comm_init.argtypes = [vp, i32, i32, i32, C.POINTER(vp)]
     L.sllm_cuda_tp_comm_free.argtypes = [vp]
@@ -63,6 +66,15 @@ def lib():
     L.sllm_cuda_tp_vocab_range.argtypes = [vp, C.POINTER(i32), C.POINTER(i32)]
     L.sllm_cuda_tp_ctx_new.argtypes = [vp, vp, i32, C.POINTER(vp)]
     L.sllm_cuda_tp_ctx_free.argtypes = [vp]
+    L.sllm_cuda_tp_batch_new.argtypes = [vp, vp, i32, i32, C.POINTER(vp)]
+    L.sllm_cuda_tp_batch_free.argtypes = [vp]
+    L.sllm_cuda_tp_batch_free.restype = None
+    L.sllm_cuda_tp_batch_reset.argtypes = [vp]
+    L.sllm_cuda_tp_batch_generate_greedy.argtypes = [vp, vp, i32, i32, vp]
+    L.sllm_cuda_tp_batch_last_logits.argtypes = [vp, i32, vp]
+    L.sllm_cuda_test_tp_batch_last_run_ms.argtypes = [vp]
+    L.sllm_cuda_test_tp_batch_last_run_ms.restype = C.c_float
+    L.sllm_cuda_test_tp_batch_generate_group.argtypes = [vp, i32, vp, i32, i32, vp]
     L.sllm_cuda_tp_ctx_reset.argtypes = [vp]
     L.sllm_cuda_tp_generate_greedy.argtypes = [vp, vp, i32, i32, vp]
     L.sllm_cuda_tp_last_logits.argtypes = [vp, vp]
@@ -199,6 +211,18 @@ class GemvBatch:
         if getattr(self, "h", None):
             lib().sllm_cuda_gemv_batch_free(self.h)
             self.h = None
+
+
+def gemm_strided(w, n_rows, k, m, q, lda, acts, dots=None, y=None, stream=None):
+    """The GEMM over k columns of a row-major activation matrix whose rows
+    are lda bytes apart (device pointers)."""
+    _check(lib().sllm_cuda_test_gemm_strided(_ptr(w), n_rows, k, m, _ptr(q), lda, _ptr(acts), _ptr(dots), _ptr(y),
+                                             _stream(stream)), "gemm_strided")
+
+
+def set_gemm_form(form):
+    """0: by size; 1: the 128-token tiles; 2: the skinny (<= 16 tokens) form."""
+    lib().sllm_cuda_test_gemm_form(int(form))
 
 
 def gemm_error():
@@ -390,6 +414,9 @@ class TpModel:
     def ctx(self, n_ctx, comm=None):
         return TpCtx(self, n_ctx, comm)
 
+    def batch(self, n_seq, n_ctx, comm=None):
+        return TpBatch(self, n_seq, n_ctx, comm)
+
     def close(self):
         if self.h:
             lib().sllm_cuda_tp_model_free(self.h)
@@ -440,6 +467,55 @@ class TpCtx:
         if self.h:
             lib().sllm_cuda_tp_ctx_free(self.h)
             self.h = C.c_void_p()
+
+
+class TpBatch:
+    """n_seq <= 16 sequences decoded together over one shard
+    (sllm_cuda_tp_batch_*), each with its own KV cache."""
+
+    def __init__(self, model, n_seq, n_ctx, comm=None):
+        self.model = model
+        self.n_seq = n_seq
+        self.h = C.c_void_p()
+        _check(lib().sllm_cuda_tp_batch_new(model.h, comm.h if comm is not None else None, n_seq, n_ctx,
+                                            C.byref(self.h)), "tp_batch_new")
+
+    def generate(self, prompts, n_new):
+        """prompts: [n_seq][n_prompt] token ids; returns (status, [n_seq][n_new])."""
+        prompts = np.ascontiguousarray(prompts, np.int32).reshape(self.n_seq, -1)
+        out = np.zeros((self.n_seq, max(n_new, 1)), np.int32)
+        rc = lib().sllm_cuda_tp_batch_generate_greedy(self.h, prompts.ctypes.data if prompts.size else None,
+                                                      prompts.shape[1], n_new, out.ctypes.data)
+        return rc, out[:, :n_new].copy() if n_new > 0 else out[:, :0]
+
+    def last_logits(self, seq):
+        v0, n = self.model.vocab_range()
+        out = np.zeros(n, np.float32)
+        _check(lib().sllm_cuda_tp_batch_last_logits(self.h, seq, out.ctypes.data), "tp_batch_last_logits")
+        return v0, out
+
+    def reset(self):
+        _check(lib().sllm_cuda_tp_batch_reset(self.h), "tp_batch_reset")
+
+    def last_run_ms(self):
+        return float(lib().sllm_cuda_test_tp_batch_last_run_ms(self.h))
+
+    def close(self):
+        if self.h:
+            lib().sllm_cuda_tp_batch_free(self.h)
+            self.h = C.c_void_p()
+
+
+def tp_batch_generate_group(batches, prompts, n_new):
+    """Batch decode over the batches of ranks 0..N-1 on one device (device
+    copies instead of NCCL)."""
+    n_seq = batches[0].n_seq
+    prompts = np.ascontiguousarray(prompts, np.int32).reshape(n_seq, -1)
+    arr = (C.c_void_p * len(batches))(*[b.h.value for b in batches])
+    out = np.zeros((n_seq, max(n_new, 1)), np.int32)
+    rc = lib().sllm_cuda_test_tp_batch_generate_group(arr, len(batches), prompts.ctypes.data if prompts.size else None,
+                                                      prompts.shape[1], n_new, out.ctypes.data)
+    return rc, out[:, :n_new].copy()
 
 
 def tp_generate_group(ctxs, prompt, n_new):

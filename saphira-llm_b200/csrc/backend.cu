@@ -309,7 +309,7 @@ extern "C" int sllm_cuda_i2s_gemv_f32(const uint8_t* w, size_t n_rows, size_t n,
 // ---------------------------------------------------------------------------
 // multi-token (prefill) kernels
 // ---------------------------------------------------------------------------
-static int* gemm_error_word() { return device_word(g_gemm_errors); }
+int* sllm::gemm_error_word() { return device_word(g_gemm_errors); }
 
 extern "C" int sllm_cuda_test_gemm_error(void) {
     int* p = gemm_error_word();
@@ -358,6 +358,17 @@ extern "C" int sllm_cuda_i2s_gemm_silu(const uint8_t* w_gate, const uint8_t* w_u
     GemmArgs a{};
     a.w = w_gate; a.w2 = w_up; a.q = q; a.acts = acts; a.dots = nullptr; a.y = h;
     a.m = (int)m; a.n_rows = (int)n_rows; a.K = (int)n;
+    return gemm_run(a, stream);
+}
+
+extern "C" void sllm_cuda_test_gemm_form(int form) { gemm_set_form(form); }
+
+extern "C" int sllm_cuda_test_gemm_strided(const uint8_t* w, int32_t n_rows, int32_t k, int32_t m, const int8_t* q,
+                                           int32_t lda, const sllm_cuda_act* acts, int32_t* dots, float* y,
+                                           void* stream) {
+    GemmArgs a{};
+    a.w = w; a.q = q; a.acts = acts; a.dots = dots; a.y = y;
+    a.m = m; a.n_rows = n_rows; a.K = k; a.lda = lda;
     return gemm_run(a, stream);
 }
 

@@ -19,6 +19,8 @@ void rope_table(int n_ctx, int n_rot, float base, std::vector<float>& cs, std::v
 // the per-process certified-sum fallback counter and the test switch
 int* fallback_counter();
 int force_fallback_flag();
+// the per-device error word of the prefill GEMM's bounded waits
+int* gemm_error_word();
 // CUDA graphs whose kernel nodes are counted for sllm_cuda_test_kernel_launches
 cudaError_t instantiate(cudaGraphExec_t* exec, cudaGraph_t g);
 cudaError_t graph_launch(cudaGraphExec_t exec, cudaStream_t st);

@@ -323,6 +323,174 @@ lm_head_kernel(const LmParams p) {
 }
 
 // ---------------------------------------------------------------------------
+// lm_head of a batch of sequences: CTA (g, c) takes tokens [g T, g T + T) and
+// the row groups c, c + G, ... of the slice, so the T-token groups of one row
+// range run side by side and share its table reads in L2. Each token's
+// output_norm and each row's four-lane FMA chains and tree are lm_head_kernel's,
+// token by token; the last CTA reduces every token's per-CTA bests and writes
+// {best value bits, best global row, isnan(logits[b][0])} per token (the
+// slice's candidate; the argmax across slices and the feedback are the
+// caller's, as for a tensor-parallel slice above).
+// ---------------------------------------------------------------------------
+constexpr int kLmbTokens = 4;
+
+__global__ void __launch_bounds__(kLmThreads)
+lm_head_batch_kernel(const LmBatchParams p) {
+    constexpr int T = kLmbTokens;
+    extern __shared__ __align__(16) float xs[];                 // T x E floats
+    __shared__ double dred[32];
+    __shared__ float s_scale;
+    __shared__ float bv_s[T][kLmWarps];
+    __shared__ int bi_s[T][kLmWarps];
+    __shared__ int s_last;
+    const int E = p.E, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int t0 = blockIdx.x * T, nt = min(T, p.B - t0);
+    const int ncta = gridDim.y, cta = blockIdx.y;
+    pdl_wait_d();
+    for (int t = 0; t < T; ++t) {
+        float* xt = xs + (size_t)t * E;
+        if (t >= nt) {
+            for (int i = tid; i < E; i += kLmThreads) xt[i] = 0.0f;
+            continue;
+        }
+        const float* xg = p.x + (size_t)(t0 + t) * E;
+        double ss = 0.0;
+        for (int i = tid; i < E; i += kLmThreads) {
+            const float v = xg[i];
+            xt[i] = v;
+            ss = __dadd_rn(ss, (double)__fmul_rn(v, v));
+        }
+        ss = warp_sum_d(ss);
+        if (lane == 0) dred[warp] = ss;
+        __syncthreads();
+        if (tid == 0) {
+            double S = 0.0;
+            for (int i = 0; i < kLmWarps; ++i) S = __dadd_rn(S, dred[i]);
+            float mean;
+            if (!certify_mean_mul(S, E, 1.0 / (double)E, &mean) || p.force_fallback) {
+                mean = __double2float_rn(__ddiv_rn(rms_ss_reference_order(xt, E), (double)E));
+                if (p.fallback_count != nullptr && cta == 0) atomicAdd(p.fallback_count, 1);
+            }
+            s_scale = rms_scale(mean, p.eps);
+        }
+        __syncthreads();
+        const float sc = s_scale;
+        for (int i = tid; i < E; i += kLmThreads) xt[i] = __fmul_rn(__fmul_rn(sc, xt[i]), p.norm_w[i]);
+        __syncthreads();
+    }
+
+    const int sub = lane >> 2, j4 = lane & 3;
+    const int nsteps = E >> 5;
+    const int ngroups = (p.V + 7) >> 3;
+    float bv[T];
+    int bi[T];
+    #pragma unroll
+    for (int t = 0; t < T; ++t) { bv[t] = NAN; bi[t] = 0x7fffffff; }
+    constexpr int U = 4;
+    for (int grp = cta * kLmWarps + warp; grp < ngroups; grp += ncta * kLmWarps) {
+        const int row = 8 * grp + sub;
+        const bool valid = row < p.V;
+        const uint8_t* wrow = reinterpret_cast<const uint8_t*>(p.embd + (size_t)(valid ? row : 0) * (size_t)E) + 16 * j4;
+        float a[T][8];
+        #pragma unroll
+        for (int t = 0; t < T; ++t)
+            #pragma unroll
+            for (int l = 0; l < 8; ++l) a[t][l] = 0.0f;
+        for (int m0 = 0; m0 < nsteps; m0 += U) {
+            uint4 wv[U];
+            #pragma unroll
+            for (int u = 0; u < U; ++u) wv[u] = (m0 + u < nsteps) ? ld_stream_u128(wrow + 64 * (m0 + u)) : make_uint4(0, 0, 0, 0);
+            #pragma unroll
+            for (int u = 0; u < U; ++u) {
+                if (m0 + u < nsteps) {
+                    const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u].x));
+                    const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u].y));
+                    const float2 w45 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u].z));
+                    const float2 w67 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u].w));
+                    #pragma unroll
+                    for (int t = 0; t < T; ++t) {
+                        const float4* xv = reinterpret_cast<const float4*>(xs + (size_t)t * E + 32 * (m0 + u) + 8 * j4);
+                        const float4 x0 = xv[0], x1 = xv[1];
+                        a[t][0] = __fmaf_rn(w01.x, x0.x, a[t][0]);
+                        a[t][1] = __fmaf_rn(w01.y, x0.y, a[t][1]);
+                        a[t][2] = __fmaf_rn(w23.x, x0.z, a[t][2]);
+                        a[t][3] = __fmaf_rn(w23.y, x0.w, a[t][3]);
+                        a[t][4] = __fmaf_rn(w45.x, x1.x, a[t][4]);
+                        a[t][5] = __fmaf_rn(w45.y, x1.y, a[t][5]);
+                        a[t][6] = __fmaf_rn(w67.x, x1.z, a[t][6]);
+                        a[t][7] = __fmaf_rn(w67.y, x1.w, a[t][7]);
+                    }
+                }
+            }
+        }
+        #pragma unroll
+        for (int t = 0; t < T; ++t) {
+            // the reference's tree (src/ops.c:135-143), as lm_head_kernel
+            #pragma unroll
+            for (int l = 0; l < 8; ++l) a[t][l] = __fadd_rn(a[t][l], __shfl_down_sync(0xffffffffu, a[t][l], 2));
+            #pragma unroll
+            for (int l = 0; l < 8; ++l) a[t][l] = __fadd_rn(a[t][l], __shfl_down_sync(0xffffffffu, a[t][l], 1));
+            const float q0 = __fadd_rn(a[t][0], a[t][4]), q1 = __fadd_rn(a[t][1], a[t][5]);
+            const float q2 = __fadd_rn(a[t][2], a[t][6]), q3 = __fadd_rn(a[t][3], a[t][7]);
+            const float logit = __fadd_rn(__fadd_rn(q0, q1), __fadd_rn(q2, q3));
+            if (j4 == 0 && valid && t < nt) {
+                p.logits[(size_t)(t0 + t) * p.V + row] = logit;
+                if (better(logit, row, bv[t], bi[t])) { bv[t] = logit; bi[t] = row; }
+            }
+        }
+    }
+    #pragma unroll
+    for (int t = 0; t < T; ++t) {
+        #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv[t], o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi[t], o);
+            if (better(ov, oi, bv[t], bi[t])) { bv[t] = ov; bi[t] = oi; }
+        }
+        if (lane == 0) { bv_s[t][warp] = bv[t]; bi_s[t][warp] = bi[t]; }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int t = 0; t < nt; ++t) {
+            float v = bv_s[t][0];
+            int i = bi_s[t][0];
+            for (int w = 1; w < kLmWarps; ++w) if (better(bv_s[t][w], bi_s[t][w], v, i)) { v = bv_s[t][w]; i = bi_s[t][w]; }
+            p.part_v[(size_t)(t0 + t) * ncta + cta] = v;
+            p.part_i[(size_t)(t0 + t) * ncta + cta] = i;
+        }
+        __threadfence();
+        const int done = atomicAdd(p.counter, 1);
+        s_last = (done == (int)(gridDim.x * gridDim.y) - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    // the last CTA: each token's per-CTA partials, one warp per token
+    __threadfence();
+    for (int b = warp; b < p.B; b += kLmWarps) {
+        float v = NAN;
+        int i = 0x7fffffff;
+        for (int c = lane; c < ncta; c += 32) {
+            const float cv = __ldcg(&p.part_v[(size_t)b * ncta + c]);
+            const int ci = __ldcg(&p.part_i[(size_t)b * ncta + c]);
+            if (better(cv, ci, v, i)) { v = cv; i = ci; }
+        }
+        #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+            if (better(ov, oi, v, i)) { v = ov; i = oi; }
+        }
+        if (lane == 0) {
+            p.out[3 * b] = __float_as_int(v);
+            p.out[3 * b + 1] = i == 0x7fffffff ? 0x7fffffff : i + p.row_base;
+            p.out[3 * b + 2] = isnan(__ldcg(&p.logits[(size_t)b * p.V])) ? 1 : 0;
+        }
+    }
+    __syncthreads();
+    if (tid == 0) *p.counter = 0;
+}
+
+// ---------------------------------------------------------------------------
 // launchers
 // ---------------------------------------------------------------------------
 cudaError_t launch_embed(const uint16_t* tok_embd, const int32_t* tok_seq, const int32_t* pos_ptr, int E, int V,
@@ -374,6 +542,21 @@ cudaError_t launch_add(const float* a, const float* b, float* out, size_t n, cud
 }
 
 int lm_head_grid(int num_sms) { return 2 * num_sms; }
+
+cudaError_t launch_lm_head_batch(const LmBatchParams& p, int num_sms, cudaStream_t st) {
+    const size_t smem = (size_t)kLmbTokens * p.E * sizeof(float);
+    if (p.B < 1 || smem > 160 * 1024) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(lm_head_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    const int groups = (p.B + kLmbTokens - 1) / kLmbTokens;
+    return launch_pdl(lm_head_batch_kernel, dim3(groups, lm_head_batch_ctas(p.B, num_sms)), dim3(kLmThreads), smem, st,
+                      false, p);
+}
+
+int lm_head_batch_ctas(int B, int num_sms) {
+    const int groups = (B + kLmbTokens - 1) / kLmbTokens;
+    return std::max(1, num_sms / groups);
+}
 
 // An ordinary launch, not a programmatic dependent one: measured in the decode
 // step, the head's CTAs launched early behind the layer program streamed the

@@ -53,6 +53,24 @@ struct LmParams {
     int row_base;
 };
 
+// The head of a batch of B sequences' residual streams x [B][E]: every
+// token's logits and per-slice best as LmParams's tensor-parallel form.
+struct LmBatchParams {
+    const float* x;          // [B][E]
+    const float* norm_w;
+    float eps;
+    const uint16_t* embd;    // f16 [V][E]: the slice's first row
+    int E, V, B;
+    float* logits;           // [B][V]
+    float* part_v;           // [B][lm_head_batch_ctas]
+    int* part_i;
+    int* counter;            // zero between launches
+    int32_t* out;            // [B][3]: {best value bits, best global row, isnan(logits[b][0])}
+    int row_base;
+    int* fallback_count;
+    int force_fallback;
+};
+
 // reset_word (nullable): a word the kernel zeroes, the decode step's engine
 // barrier, so that the step graph needs no memset node before the engine
 cudaError_t launch_embed(const uint16_t* tok_embd, const int32_t* tok_seq, const int32_t* pos_ptr, int E, int V,
@@ -77,5 +95,8 @@ cudaError_t launch_attention_chunk(const AttnParams& p, const int32_t* pos, int 
 cudaError_t launch_add(const float* a, const float* b, float* out, size_t n, cudaStream_t st);
 int lm_head_grid(int num_sms);
 cudaError_t launch_lm_head(const LmParams& p, int grid, cudaStream_t st);
+// CTAs per token group of the batch head (the per-token partials' length)
+int lm_head_batch_ctas(int B, int num_sms);
+cudaError_t launch_lm_head_batch(const LmBatchParams& p, int num_sms, cudaStream_t st);
 
 }  // namespace sllm

@@ -30,5 +30,11 @@ struct GemmArgs {
 // pointers); a negative sllm status and a message otherwise
 int gemm_check(const GemmArgs& a, const char** why);
 cudaError_t launch_i2s_gemm(const GemmArgs& a, int* error, cudaStream_t st);
+// the same results for at most 16 tokens (a.m <= 16), weight rows as the
+// MMA's M operand and the tokens as its N = 16 operand
+cudaError_t launch_i2s_gemm_skinny(const GemmArgs& a, int* error, cudaStream_t st);
+// test hook: 0 picks the form by size (skinny for m <= 16), 1 forces the
+// 128-token tiles, 2 the skinny form
+void gemm_set_form(int form);
 
 }  // namespace sllm

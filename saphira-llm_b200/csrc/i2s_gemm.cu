@@ -519,6 +519,257 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
 }
 
 // ---------------------------------------------------------------------------
+// The skinny form: at most 16 tokens (a decode step of a batch of sequences).
+// The roles swap: 128 weight rows are the MMA's M operand, unpacked into
+// shared memory as above, and the tokens are its N = 16 operand (one TMA box
+// of 16 rows x 128 bytes, zero past m), so no MMA column is padding and the
+// tensor pipe does 1/8 of the work of a 128-token tile. The accumulator is
+// 128 TMEM lanes (weight rows) x 16 columns (tokens), gate at column 0 and up
+// at column 16 for the fused pair. The same warp roles; the epilogue runs on
+// warps 2-5 (one TMEM lane quarter each), a lane per weight row, so the
+// stores of one token's outputs are 32 consecutive words per warp.
+//
+// Unpack order: thread t takes half t & 1 of row t >> 1 (eight threads read
+// 128 contiguous bytes), and stores field f ^ 2 (row & 1) first, so the eight
+// 16-byte stores of a quarter warp land on eight distinct swizzled chunks.
+//
+// A short grid (few 128-row tiles) splits the contraction over a cluster of
+// SK CTAs as above: the others leave their 128 x 16 (x 2) partial sums in
+// their idle rings and the first adds them through distributed shared memory.
+// ---------------------------------------------------------------------------
+constexpr int kSkM = 128;       // weight rows per tile (MMA M, TMEM lanes)
+constexpr int kSkN = 16;        // tokens (MMA N)
+
+template <bool PAIR>
+struct SkinnyCfg {
+    static constexpr int NM = PAIR ? 2 : 1;
+    static constexpr int A_BYTES = kSkM * kBK;      // unpacked codes of one matrix
+    static constexpr int B_BYTES = kSkN * kBK;      // the tokens' activation bytes
+    static constexpr int P_BYTES = kSkM * kPK;      // packed codes of one matrix
+    static constexpr int STAGE = NM * A_BYTES + B_BYTES + NM * P_BYTES;
+    static constexpr int S = (225280 / STAGE) > 10 ? 10 : (225280 / STAGE);
+    static constexpr int SMEM = S * STAGE + 1024;
+    static constexpr int TMEM_COLS = 32;
+    static_assert(STAGE % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
+    static_assert(S >= 2, "ring depth");
+    static_assert(S * STAGE >= NM * kSkN * kSkM * 4, "a split CTA's partial sums fit its ring");
+};
+
+// 16 consecutive accumulator columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+template <bool PAIR, int SK>
+__global__ void __launch_bounds__(kGmThreads, 1)
+i2s_gemm_skinny_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
+                       const __grid_constant__ CUtensorMap tm_w2, const GemmKParams p) {
+    using C = SkinnyCfg<PAIR>;
+    extern __shared__ uint8_t gsm_raw[];
+    __shared__ uint64_t bar_loaded[C::S], bar_unpacked[C::S], bar_empty[C::S], bar_acc;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int abort_flag;
+    uint8_t* const gsm = gsm_raw + ((1024u - (smem_u32(gsm_raw) & 1023u)) & 1023u);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * kSkM;
+    const int KB_all = p.K / kBK;
+    const int kb0 = (int)((long long)blockIdx.z * KB_all / SK);
+    const int KB = (int)((long long)(blockIdx.z + 1) * KB_all / SK) - kb0;     // >= 1: the host keeps SK <= KB_all
+    auto A = [&](int s, int mat) { return gsm + (size_t)s * C::STAGE + mat * C::A_BYTES; };
+    auto Bt = [&](int s) { return gsm + (size_t)s * C::STAGE + C::NM * C::A_BYTES; };
+    auto P = [&](int s, int mat) {
+        return gsm + (size_t)s * C::STAGE + C::NM * C::A_BYTES + C::B_BYTES + mat * C::P_BYTES;
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::S; ++s) {
+            mbar_init(&bar_loaded[s], 1);
+            mbar_init(&bar_unpacked[s], kGmUnpackWarps);
+            mbar_init(&bar_empty[s], 1);
+        }
+        mbar_init(&bar_acc, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                     "r"((uint32_t)C::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    volatile int* const abort_v = &abort_flag;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    bool ep_ok = false;
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int issued = 0;
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % C::S;
+                const uint32_t use = (uint32_t)(kb / C::S);
+                if (use > 0 && !gm_wait(&bar_empty[s], (use - 1) & 1u, abort_v, p.error)) break;
+                mbar_expect_tx(&bar_loaded[s], (uint32_t)(C::B_BYTES + C::NM * C::P_BYTES));
+                tma_load_2d(Bt(s), &tm_a, (kb0 + kb) * kBK, 0, &bar_loaded[s]);
+                tma_load_2d(P(s, 0), &tm_w, (kb0 + kb) * kPK, n0, &bar_loaded[s]);
+                if (PAIR) tma_load_2d(P(s, 1), &tm_w2, (kb0 + kb) * kPK, n0, &bar_loaded[s]);
+                ++issued;
+            }
+            for (int kb = issued > C::S ? issued - C::S : 0; kb < issued; ++kb)
+                gm_drain(&bar_loaded[kb % C::S], (uint32_t)(kb / C::S) & 1u);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_i8(kSkM, kSkN);
+            int issued = 0;
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % C::S;
+                const uint32_t ph = (uint32_t)(kb / C::S) & 1u;
+                if (!gm_wait(&bar_unpacked[s], ph, abort_v, p.error)) break;
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(A(s, 0)), b0 = smem_u32(Bt(s));
+                #pragma unroll
+                for (int kk = 0; kk < kBK / 32; ++kk) {
+                    const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+                    umma_i8(tmem, umma_desc_sw128(a0 + 32u * kk), umma_desc_sw128(b0 + 32u * kk), idesc, acc);
+                    if (PAIR)
+                        umma_i8(tmem + (uint32_t)kSkN, umma_desc_sw128(a0 + (uint32_t)C::A_BYTES + 32u * kk),
+                                umma_desc_sw128(b0 + 32u * kk), idesc, acc);
+                }
+                umma_commit(&bar_empty[s]);
+                ++issued;
+            }
+            umma_commit(&bar_acc);
+            if (issued > 0) gm_drain(&bar_empty[(issued - 1) % C::S], (uint32_t)((issued - 1) / C::S) & 1u);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- unpack (warps 2-9) ----------------
+        constexpr int NT = 32 * kGmUnpackWarps;
+        const int t = threadIdx.x - 64;
+        bool ok = true;
+        for (int kb = 0; kb < KB && ok; ++kb) {
+            const int s = kb % C::S;
+            const uint32_t ph = (uint32_t)(kb / C::S) & 1u;
+            ok = gm_wait(&bar_loaded[s], ph, abort_v, p.error);
+            if (ok) {
+                #pragma unroll
+                for (int it = t; it < C::NM * 2 * kSkM; it += NT) {
+                    const int h = it & 1, row = (it >> 1) & (kSkM - 1), mat = it / (2 * kSkM);
+                    const uint4 v = *reinterpret_cast<const uint4*>(P(s, mat) + row * kPK + h * 16);
+                    uint8_t* arow = A(s, mat) + row * kBK;
+                    #pragma unroll
+                    for (int f = 0; f < 4; ++f) {
+                        const int fs = f ^ ((row & 1) << 1);
+                        uint4 o;
+                        o.x = field_codes(v.x, fs);
+                        o.y = field_codes(v.y, fs);
+                        o.z = field_codes(v.z, fs);
+                        o.w = field_codes(v.w, fs);
+                        const int chunk = (2 * fs + h) ^ (row & 7);
+                        *reinterpret_cast<uint4*>(arow + chunk * 16) = o;
+                    }
+                }
+                fence_proxy_async_smem();
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_unpacked[s]);
+            ok = __all_sync(0xffffffffu, ok);
+        }
+        ep_ok = __all_sync(0xffffffffu, ok && gm_wait(&bar_acc, 0u, abort_v, p.error)) &&
+                __all_sync(0xffffffffu, *abort_v == 0);
+    }
+    const int quarter = warp & 3;
+    const bool ep_warp = warp >= 2 && warp < 6;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * quarter) << 16);
+    // a split CTA's partial sums in its idle ring: [column][128 rows]
+    uint32_t* const part = reinterpret_cast<uint32_t*>(gsm);
+    if constexpr (SK > 1) {
+        namespace cg = cooperative_groups;
+        cg::cluster_group cl = cg::this_cluster();
+        if (ep_warp && cl.block_rank() != 0 && ep_ok) {
+            tc_fence_after();
+            uint32_t g[16];
+            tmem_ld16(lane_base, g);
+            tmem_ld_wait();
+            #pragma unroll
+            for (int j = 0; j < kSkN; ++j) part[j * kSkM + 32 * quarter + lane] = g[j];
+            if (PAIR) {
+                tmem_ld16(lane_base + (uint32_t)kSkN, g);
+                tmem_ld_wait();
+                #pragma unroll
+                for (int j = 0; j < kSkN; ++j) part[(kSkN + j) * kSkM + 32 * quarter + lane] = g[j];
+            }
+        }
+        cl.sync();
+    }
+    bool lead = true;
+    if constexpr (SK > 1) lead = cooperative_groups::this_cluster().block_rank() == 0;
+    if (ep_warp && ep_ok && lead) {
+        tc_fence_after();
+        uint32_t g[16], u[16];
+        tmem_ld16(lane_base, g);
+        if (PAIR) tmem_ld16(lane_base + (uint32_t)kSkN, u);
+        tmem_ld_wait();
+        if constexpr (SK > 1) {
+            namespace cg = cooperative_groups;
+            cg::cluster_group cl = cg::this_cluster();
+            #pragma unroll 1
+            for (int r = 1; r < SK; ++r) {
+                const uint32_t* rp = cl.map_shared_rank(part, r);
+                #pragma unroll
+                for (int j = 0; j < kSkN; ++j) {
+                    g[j] += rp[j * kSkM + 32 * quarter + lane];
+                    if (PAIR) u[j] += rp[(kSkN + j) * kSkM + 32 * quarter + lane];
+                }
+            }
+        }
+        const int n = n0 + 32 * quarter + lane;       // this lane's weight row
+        if (n < p.N) {
+            const float ws = __ldg(p.ws);
+            const float ws2 = PAIR ? __ldg(p.ws2) : 0.0f;
+            #pragma unroll
+            for (int j = 0; j < kSkN; ++j) {
+                if (j < p.M) {
+                    const sllm_cuda_act act = p.acts[j];
+                    // per-tensor scale over the token's activation scale (src/forward.c:653-655)
+                    const float post = __fdiv_rn(ws, act.scale);
+                    const size_t o = (size_t)j * p.N + n;
+                    if (PAIR) {
+                        // h = silu(gate) * up (src/forward.c:765-778, src/ops.c:452-456)
+                        const float post2 = __fdiv_rn(ws2, act.scale);
+                        const float gv = __fmul_rn(__int2float_rn((int)g[j] - act.sum), post);
+                        const float uv = __fmul_rn(__int2float_rn((int)u[j] - act.sum), post2);
+                        p.y[o] = __fmul_rn(silu_block(gv), uv);
+                    } else {
+                        if (p.dots != nullptr) p.dots[o] = (int)g[j];
+                        if (p.y != nullptr) p.y[o] = __fmul_rn(__int2float_rn((int)g[j] - act.sum), post);
+                    }
+                }
+            }
+        }
+    }
+    if constexpr (SK > 1) cooperative_groups::this_cluster().sync();   // the leader has read the partials
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -630,6 +881,72 @@ cudaError_t launch_tile(const GemmArgs& a, int* error, cudaStream_t st) {
     return cudaLaunchKernelEx(&cfg, i2s_gemm_kernel<BN, PAIR, MT, SK>, tm_a, tm_w, tm_w2, tm_y, tm_d, p);
 }
 
+template <bool PAIR, int SK>
+cudaError_t launch_skinny(const GemmArgs& a, int* error, cudaStream_t st) {
+    using C = SkinnyCfg<PAIR>;
+    CUtensorMap tm_a, tm_w, tm_w2;
+    if (!encode_2d(&tm_a, a.q, (uint64_t)a.K, (uint64_t)a.m, kBK, kSkN, CU_TENSOR_MAP_SWIZZLE_128B,
+                   (uint64_t)(a.lda > 0 ? a.lda : a.K)) ||
+        !encode_2d(&tm_w, a.w, (uint64_t)(a.K / 4), (uint64_t)a.n_rows, kPK, kSkM, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return cudaErrorInvalidValue;
+    if (PAIR) {
+        if (!encode_2d(&tm_w2, a.w2, (uint64_t)(a.K / 4), (uint64_t)a.n_rows, kPK, kSkM, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return cudaErrorInvalidValue;
+    } else {
+        tm_w2 = tm_w;
+    }
+    GemmKParams p{};
+    p.acts = a.acts;
+    const size_t tail = (size_t)a.n_rows * (size_t)(a.K / 4);
+    p.ws = reinterpret_cast<const float*>(a.w + tail);
+    p.ws2 = PAIR ? reinterpret_cast<const float*>(a.w2 + tail) : p.ws;
+    p.dots = a.dots;
+    p.y = a.y;
+    p.M = a.m;
+    p.N = a.n_rows;
+    p.K = a.K;
+    p.error = error;
+    cudaError_t e = cudaFuncSetAttribute(i2s_gemm_skinny_kernel<PAIR, SK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((a.n_rows + kSkM - 1) / kSkM), 1, SK);
+    cfg.blockDim = dim3(kGmThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (SK > 1) {
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 1;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = SK;
+        cfg.numAttrs = 2;
+    }
+    return cudaLaunchKernelEx(&cfg, i2s_gemm_skinny_kernel<PAIR, SK>, tm_a, tm_w, tm_w2, p);
+}
+
+template <bool PAIR>
+cudaError_t launch_skinny_split(const GemmArgs& a, int sk, int* error, cudaStream_t st) {
+    switch (sk) {
+        case 8: return launch_skinny<PAIR, 8>(a, error, st);
+        case 4: return launch_skinny<PAIR, 4>(a, error, st);
+        case 2: return launch_skinny<PAIR, 2>(a, error, st);
+        default: return launch_skinny<PAIR, 1>(a, error, st);
+    }
+}
+
+int sm_count() {
+    static int n[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (n[dev] == 0 && cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n[dev] = 148;
+    return n[dev];
+}
+
 }  // namespace
 
 int gemm_check(const GemmArgs& a, const char** why) {
@@ -670,7 +987,24 @@ int gemm_check(const GemmArgs& a, const char** why) {
 // projection at 512 tokens runs on 120 CTAs (23.0 us, against 25.0 us for
 // 128 x 128 tiles on 80 CTAs and 27.1 us for 256-row tiles on 120). Short
 // contractions take 128 rows x 128 tokens, unsplit.
+// The skinny form: one CTA per 128 weight rows, the contraction split over a
+// cluster of 2, 4 or 8 CTAs while that still fits the grid in one wave (and
+// leaves every CTA at least two k-steps).
+cudaError_t launch_i2s_gemm_skinny(const GemmArgs& a, int* error, cudaStream_t st) {
+    if (a.m < 1 || a.m > kSkN) return cudaErrorInvalidValue;
+    const int tiles = (a.n_rows + kSkM - 1) / kSkM, kb = a.K / kBK, sms = sm_count();
+    int sk = 1;
+    while (sk < 8 && tiles * sk * 2 <= sms && kb >= 2 * sk * 2) sk *= 2;
+    return a.w2 != nullptr ? launch_skinny_split<true>(a, sk, error, st) : launch_skinny_split<false>(a, sk, error, st);
+}
+
+int g_gemm_form = 0;     // test hook: 0 by size, 1 the 128-token tiles, 2 the skinny form
+
+void gemm_set_form(int form) { g_gemm_form = form; }
+
 cudaError_t launch_i2s_gemm(const GemmArgs& a, int* error, cudaStream_t st) {
+    if (g_gemm_form != 1 && a.m <= kSkN) return launch_i2s_gemm_skinny(a, error, st);
+    if (g_gemm_form == 2) return cudaErrorInvalidValue;
     if (a.w2 != nullptr) return launch_tile<96, true, 2, 1>(a, error, st);
     if (a.K / kBK >= 6) return launch_tile<128, false, 2, 3>(a, error, st);
     return launch_tile<128, false, 1, 1>(a, error, st);

@@ -50,6 +50,7 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "engine.cuh"
+#include "gemm.cuh"
 #include "gemv.cuh"
 #include "../../include/sllm_cuda.h"
 #include "../../include/sllm_cuda_testing.h"
@@ -1982,4 +1983,571 @@ extern "C" int sllm_cuda_test_tp_fused_layers(const sllm_cuda_tp_ctx* c) {
 extern "C" int sllm_cuda_test_tp_exchange_kind(const sllm_cuda_tp_ctx* c) {
     if (c == nullptr || c->m->n_ranks < 2) return 0;
     return c->p2p ? 2 : 1;
+}
+
+// ---------------------------------------------------------------------------
+// Batch decode: B <= 16 sequences, one KV cache each, stepped together. A
+// step is the single-sequence step with every GEMV of the layer turned into
+// one GEMM over the B tokens (the skinny tcgen05 form: each weight byte is
+// read once per step for all sequences), the attention per (head, sequence)
+// over that sequence's cache and position, and the exchanges carrying B rows.
+// Each sequence's tokens and logits are, bit for bit, those of its own batch-1
+// run: the int32 dots are exact in any grouping and every float operation is
+// the single-token kernels', token by token. The reference runs one sequence
+// per context (src/forward.c:78-84, :466-562); a batch of B is B of those.
+// ---------------------------------------------------------------------------
+namespace {
+
+__global__ void tp_embed_batch_kernel(const uint16_t* __restrict__ tok_embd, const int32_t* __restrict__ tok_seq,
+                                      const int32_t* __restrict__ pos, int n_ctx, int E, int V, float* __restrict__ x) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int b = blockIdx.x;
+    int tok = tok_seq[(size_t)b * n_ctx + pos[b]];
+    if ((unsigned)tok >= (unsigned)V) tok = 0;
+    const uint16_t* row = tok_embd + (size_t)tok * (size_t)E;
+    float* xr = x + (size_t)b * E;
+    for (int d = threadIdx.x; d < E; d += blockDim.x) xr[d] = f16_embd(row[d]);
+}
+
+// [N][B][c] (rank-major, as an all-gather leaves it) -> [B][N c]
+__global__ void tp_unshard_kernel(const float* __restrict__ src, float* __restrict__ dst, int N, int B, int c) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const size_t total = (size_t)N * B * c;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int j = (int)(i % c);
+        const size_t rb = i / c;
+        const int b = (int)(rb % B), r = (int)(rb / B);
+        dst[((size_t)b * N + r) * c + j] = src[i];
+    }
+}
+
+// tp_epilogue_kernel for B rows: dots [C][B][rows], act [B], resid and y [B][rows]
+__global__ void tp_epilogue_rows_kernel(const int32_t* __restrict__ dots, int n_chunks, int B, int rows,
+                                        const sllm_cuda_act* act, const float* __restrict__ ws,
+                                        const float* __restrict__ resid, float* __restrict__ y) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int r = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
+    if (r >= rows) return;
+    const size_t o = (size_t)b * rows + r;
+    int d = 0;
+    for (int c = 0; c < n_chunks; ++c) d += dots[(size_t)c * B * rows + o];
+    const sllm_cuda_act a = act[b];
+    const float post = __fdiv_rn(*ws, a.scale);
+    y[o] = __fadd_rn(__fmul_rn(__int2float_rn(d - a.sum), post), resid[o]);
+}
+
+// tp_finalize_kernel per sequence: trip_all [N][B][3]
+__global__ void tp_finalize_batch_kernel(const int32_t* trip_all, int n_ranks, int B, int32_t* pos, int32_t* tok_seq,
+                                         const int32_t* prompt_end, int32_t* argmax_out, int n_ctx) {
+    const int b = threadIdx.x;
+    if (b >= B) return;
+    float bv = NAN;
+    int bi = 0x7fffffff;
+    for (int r = 0; r < n_ranks; ++r) {
+        const int32_t* t = trip_all + ((size_t)r * B + b) * 3;
+        const float v = __int_as_float(t[0]);
+        if (t[1] != 0x7fffffff && tp_better(v, t[1], bv, bi)) { bv = v; bi = t[1]; }
+    }
+    int next = bi;
+    if (bi == 0x7fffffff || trip_all[(size_t)b * 3 + 2] != 0) next = 0;   // rank 0 holds row 0
+    argmax_out[b] = next;
+    const int p = pos[b];
+    if (p + 1 >= prompt_end[b] && p + 1 < n_ctx) tok_seq[(size_t)b * n_ctx + p + 1] = next;
+    pos[b] = p + 1;
+}
+
+constexpr int kMaxBatch = 16;
+
+}  // namespace
+
+struct sllm_cuda_tp_batch {
+    const sllm_cuda_tp_model* m = nullptr;
+    sllm_cuda_tp_comm* comm = nullptr;
+    int B = 0, n_ctx = 0, n_past = 0, head_ctas = 0;
+    bool have_logits = false;
+    cudaStream_t stream = nullptr;
+    float *k_cache = nullptr, *v_cache = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    float *x = nullptr, *ffn_inp = nullptr, *q = nullptr, *k = nullptr, *v = nullptr;
+    float *attn_loc = nullptr, *attn_full = nullptr, *h_loc = nullptr, *h_full = nullptr, *gather = nullptr;
+    float* logits = nullptr;
+    int8_t *qa = nullptr, *qh = nullptr;
+    sllm_cuda_act *act_a = nullptr, *act_h = nullptr;
+    int32_t *dots_o = nullptr, *dots_d = nullptr;
+    float* part_v = nullptr;
+    int* part_i = nullptr;
+    int* counter = nullptr;
+    int32_t *trip = nullptr, *trip_all = nullptr, *argmax = nullptr, *pos = nullptr, *prompt_end = nullptr;
+    int32_t* tok_seq = nullptr;
+    int32_t* pinned = nullptr;
+    cudaGraphExec_t step = nullptr;
+    std::vector<void*> allocs;
+    cudaEvent_t run_ev[2] = {};
+};
+
+namespace {
+
+template <class T>
+cudaError_t batch_alloc(sllm_cuda_tp_batch* b, T** p, size_t count) {
+    void* v = nullptr;
+    const cudaError_t e = dev_malloc(&v, align256(count * sizeof(T)));
+    if (e == cudaSuccess) {
+        b->allocs.push_back(v);
+        *p = static_cast<T*>(v);
+    }
+    return e;
+}
+
+// the exchanges of a batch step (X_ATTN, X_DOTS_O, X_H, X_DOTS_D, X_ARGMAX):
+// element counts per rank, and whether they are gathered (else summed)
+void bxchg_counts(const sllm_cuda_tp_batch* b, int which, size_t* count, bool* gather) {
+    const sllm_cuda_tp_model* m = b->m;
+    const size_t B = (size_t)b->B;
+    switch (which) {
+        case X_ATTN: *count = B * m->hq * kHeadDim; *gather = true; break;
+        case X_DOTS_O: *count = B * m->E; *gather = false; break;
+        case X_H: *count = B * m->f_loc; *gather = true; break;
+        case X_DOTS_D: *count = B * m->E * m->down_c; *gather = false; break;
+        default: *count = B * 3; *gather = true; break;
+    }
+}
+
+void bxchg_buffers(sllm_cuda_tp_batch* b, int which, void** src, void** dst) {
+    switch (which) {
+        case X_ATTN: *src = b->attn_loc; *dst = b->gather; break;
+        case X_DOTS_O: *src = b->dots_o; *dst = b->dots_o; break;
+        case X_H: *src = b->h_loc; *dst = b->gather; break;
+        case X_DOTS_D: *src = b->dots_d; *dst = b->dots_d; break;
+        default: *src = b->trip; *dst = b->trip_all; break;
+    }
+}
+
+cudaError_t bxchg_nccl(sllm_cuda_tp_batch* b, int which, cudaStream_t st, ncclResult_t* nr) {
+    if (b->m->n_ranks == 1) return cudaSuccess;       // one rank: the buffers alias
+    size_t count;
+    bool gather;
+    void *src, *dst;
+    bxchg_counts(b, which, &count, &gather);
+    bxchg_buffers(b, which, &src, &dst);
+    if (gather)
+        *nr = nccl()->all_gather(src, dst, count, which == X_ARGMAX ? ncclInt32 : ncclFloat32, b->comm->comm, st);
+    else
+        *nr = nccl()->all_reduce(src, dst, count, ncclInt32, ncclSum, b->comm->comm, st);
+    return *nr == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
+}
+
+cudaError_t bxchg_group(sllm_cuda_tp_batch** bs, int n, int which, cudaStream_t st) {
+    if (n == 1) return cudaSuccess;
+    size_t count;
+    bool gather;
+    bxchg_counts(bs[0], which, &count, &gather);
+    if (gather) {
+        for (int r = 0; r < n; ++r) {
+            void *dst, *unused;
+            bxchg_buffers(bs[r], which, &unused, &dst);
+            for (int s = 0; s < n; ++s) {
+                void *src, *unused2;
+                bxchg_buffers(bs[s], which, &src, &unused2);
+                const cudaError_t e = cudaMemcpyAsync(static_cast<char*>(dst) + (size_t)s * count * 4, src, count * 4,
+                                                      cudaMemcpyDeviceToDevice, st);
+                if (e != cudaSuccess) return e;
+            }
+        }
+        return cudaSuccess;
+    }
+    SumArgs a{};
+    a.n = n;
+    a.count = count;
+    for (int r = 0; r < n; ++r) {
+        void *src, *dst;
+        bxchg_buffers(bs[r], which, &src, &dst);
+        a.buf[r] = static_cast<int32_t*>(dst);
+    }
+    tp_group_sum_kernel<<<64, 256, 0, st>>>(a);
+    count_launches(1);
+    return cudaGetLastError();
+}
+
+template <class K, class... Args>
+cudaError_t launch_pdl_k(K kernel, dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = st;
+    cudaLaunchAttribute attr = pdl_attribute();
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+cudaError_t bgemm(const uint8_t* w, const uint8_t* w2, int rows, int K, const int8_t* q, int lda,
+                  const sllm_cuda_act* acts, int B, int32_t* dots, float* y, cudaStream_t st) {
+    GemmArgs a{};
+    a.w = w; a.w2 = w2; a.q = q; a.acts = acts; a.dots = dots; a.y = y;
+    a.m = B; a.n_rows = rows; a.K = K; a.lda = lda;
+    const char* why = nullptr;
+    if (gemm_check(a, &why) != SLLM_CUDA_OK) return cudaErrorInvalidValue;
+    return launch_i2s_gemm_skinny(a, gemm_error_word(), st);
+}
+
+// phases as the single-sequence step's (n_phases, phase_xchg), B rows each
+cudaError_t enqueue_bphase(sllm_cuda_tp_batch* b, int ph, cudaStream_t st) {
+    const sllm_cuda_tp_model* m = b->m;
+    const int E = m->E, D = kHeadDim, B = b->B, N = m->n_ranks;
+    int* fb = fallback_counter();
+    const int force = force_fallback_flag();
+    auto epi = [&](const int32_t* dots, int chunks, const sllm_cuda_act* act, const uint8_t* w, int rows, int cols,
+                   const float* resid, float* y) {
+        const float* ws = reinterpret_cast<const float*>(w + (size_t)rows * cols / 4);
+        return launch_pdl_k(tp_epilogue_rows_kernel, dim3((rows + 255) / 256, B), dim3(256), st, dots, chunks, B, rows,
+                            act, ws, resid, y);
+    };
+    if (ph == 0) return launch_pdl_k(tp_embed_batch_kernel, dim3(B), dim3(256), st, m->tok_embd,
+                                     (const int32_t*)b->tok_seq, (const int32_t*)b->pos, b->n_ctx, E, m->V, b->x);
+    if (ph == n_phases(m) - 1) {
+        tp_finalize_batch_kernel<<<1, kMaxBatch * 2, 0, st>>>(b->trip_all, N, B, b->pos, b->tok_seq, b->prompt_end,
+                                                              b->argmax, b->n_ctx);
+        return cudaGetLastError();
+    }
+    if (ph == n_phases(m) - 2) {
+        const TpLayer& t = m->layers[m->n_layer - 1];
+        cudaError_t e = epi(b->dots_d, m->down_c, b->act_h, t.down[0], E, m->down_k, b->ffn_inp, b->x);
+        if (e != cudaSuccess) return e;
+        LmBatchParams lp{};
+        lp.x = b->x; lp.norm_w = m->output_norm; lp.eps = m->eps;
+        lp.embd = m->tok_embd + (size_t)m->v0 * E;
+        lp.E = E; lp.V = m->v_loc; lp.B = B; lp.logits = b->logits;
+        lp.part_v = b->part_v; lp.part_i = b->part_i; lp.counter = b->counter; lp.out = b->trip;
+        lp.row_base = m->v0; lp.fallback_count = fb; lp.force_fallback = force;
+        return launch_lm_head_batch(lp, num_sms_of(m->device), st);
+    }
+    const int l = (ph - 1) / 4, sub = (ph - 1) % 4;
+    const TpLayer& t = m->layers[l];
+    cudaError_t e = cudaSuccess;
+    if (sub == 0) {
+        if (l > 0) {
+            const TpLayer& tp = m->layers[l - 1];
+            e = epi(b->dots_d, m->down_c, b->act_h, tp.down[0], E, m->down_k, b->ffn_inp, b->x);
+            if (e != cudaSuccess) return e;
+        }
+        // attn_norm -> local Q, K, V for every sequence (src/forward.c:631-666)
+        e = launch_norm_quant_rows(b->x, t.attn_norm, E, m->eps, B, b->qa, b->act_a, fb, force, st);
+        if (e == cudaSuccess) e = bgemm(t.wq, nullptr, m->hq * D, E, b->qa, 0, b->act_a, B, nullptr, b->q, st);
+        if (e == cudaSuccess) e = bgemm(t.wk, nullptr, m->hk * D, E, b->qa, 0, b->act_a, B, nullptr, b->k, st);
+        if (e == cudaSuccess) e = bgemm(t.wv, nullptr, m->hk * D, E, b->qa, 0, b->act_a, B, nullptr, b->v, st);
+        if (e != cudaSuccess) return e;
+        const size_t kv_layer = (size_t)m->hk * D * (size_t)b->n_ctx;
+        AttnParams ap{};
+        ap.q = b->q; ap.k = b->k; ap.v = b->v;
+        ap.k_cache = b->k_cache + (size_t)l * kv_layer;
+        ap.v_cache = b->v_cache + (size_t)l * kv_layer;
+        ap.rope_cos = b->rope_cos; ap.rope_sin = b->rope_sin;
+        ap.out = b->attn_loc; ap.n_ctx = b->n_ctx;
+        ap.group = m->hq / m->hk;
+        ap.attn_scale = 1.0f / sqrtf((float)D);
+        ap.fallback_count = fb; ap.force_fallback = force;
+        const size_t seq_stride = (size_t)m->n_layer * kv_layer * sizeof(float);
+        e = launch_chunk_kv_store(ap, b->pos, B, m->hk, m->hq * D, m->hk * D, st, seq_stride);
+        if (e == cudaSuccess) e = launch_attention_chunk(ap, b->pos, B, m->hq, m->hq * D, m->hk * D, st, seq_stride);
+        return e;
+    }
+    if (sub == 1) {
+        // attn_sub_norm + quantisation of every whole attention output, then
+        // this rank's columns of O (src/forward.c:728-741)
+        if (N > 1)
+            e = launch_pdl_k(tp_unshard_kernel, dim3(148), dim3(256), st, (const float*)b->gather, b->attn_full, N, B,
+                             m->hq * D);
+        if (e == cudaSuccess)
+            e = launch_norm_quant_rows(b->attn_full, t.attn_sub_norm, E, m->eps, B, b->qa, b->act_a, fb, force, st);
+        if (e == cudaSuccess)
+            e = bgemm(t.wo, nullptr, E, m->e_loc, b->qa + (size_t)m->rank * m->e_loc, E, b->act_a, B, b->dots_o,
+                      nullptr, st);
+        return e;
+    }
+    if (sub == 2) {
+        // O epilogue + residual, ffn_norm -> local gate, up -> h (src/forward.c:742-779)
+        e = epi(b->dots_o, 1, b->act_a, t.wo, E, m->e_loc, b->x, b->ffn_inp);
+        if (e == cudaSuccess)
+            e = launch_norm_quant_rows(b->ffn_inp, t.ffn_norm, E, m->eps, B, b->qa, b->act_a, fb, force, st);
+        if (e == cudaSuccess) e = bgemm(t.gate, t.up, m->f_loc, E, b->qa, 0, b->act_a, B, nullptr, b->h_loc, st);
+        return e;
+    }
+    // ffn_sub_norm + quantisation of all of h, this rank's columns of down,
+    // chunk by chunk (src/forward.c:781-792)
+    if (N > 1)
+        e = launch_pdl_k(tp_unshard_kernel, dim3(148), dim3(256), st, (const float*)b->gather, b->h_full, N, B,
+                         m->f_loc);
+    if (e == cudaSuccess)
+        e = launch_norm_quant(b->h_full, t.ffn_sub_norm, m->F, m->eps, b->qh, b->act_h, fb, force, st, XWait{}, B);
+    for (int ch = 0; ch < m->down_c && e == cudaSuccess; ++ch)
+        e = bgemm(t.down[ch], nullptr, E, m->down_k, b->qh + (size_t)m->rank * m->f_loc + (size_t)ch * m->down_k,
+                  m->F, b->act_h, B, b->dots_d + (size_t)ch * B * E, nullptr, st);
+    return e;
+}
+
+int ensure_batch_graph(sllm_cuda_tp_batch* b) {
+    if (b->step != nullptr) return SLLM_CUDA_OK;
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    cudaError_t e = cudaSuccess;
+    ncclResult_t nr = ncclSuccess;
+    for (int ph = 0; ph < n_phases(b->m) && e == cudaSuccess; ++ph) {
+        e = enqueue_bphase(b, ph, b->stream);
+        const int x = phase_xchg(b->m, ph);
+        if (e == cudaSuccess && x >= 0) e = bxchg_nccl(b, x, b->stream, &nr);
+    }
+    const cudaError_t e2 = cudaStreamEndCapture(b->stream, &g);
+    if (nr != ncclSuccess) { if (g) cudaGraphDestroy(g); return fail(SLLM_CUDA_ERR_COMM, "batch step: %s", nccl_err(nr)); }
+    if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); return cuda_fail(e, "capture batch step"); }
+    if (e2 != cudaSuccess) return cuda_fail(e2, "end capture");
+    e = instantiate(&b->step, g);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) { b->step = nullptr; return cuda_fail(e, "instantiate batch step"); }
+    return SLLM_CUDA_OK;
+}
+
+int batch_validate(const sllm_cuda_tp_batch* b, const int32_t* prompts, int32_t n_prompt, int32_t n_new,
+                   const int32_t* out) {
+    if (b == nullptr || (out == nullptr && n_new > 0) || n_prompt < 0 || n_new < 0 ||
+        (n_prompt > 0 && prompts == nullptr))
+        return fail(SLLM_CUDA_ERR_ARG, "tp_batch_generate: bad arguments");
+    if (n_prompt == 0 && b->n_past == 0 && n_new > 0)
+        return fail(SLLM_CUDA_ERR_ARG, "tp_batch_generate: the first call needs a prompt for every sequence");
+    if ((int64_t)n_prompt + n_new + b->n_past > b->n_ctx)
+        return fail(SLLM_CUDA_ERR_TOO_LARGE, "tp_batch_generate: %d + %d tokens after %d exceed n_ctx %d", n_prompt,
+                    n_new, b->n_past, b->n_ctx);
+    for (int64_t i = 0; i < (int64_t)n_prompt * b->B; ++i)
+        if (prompts[i] < 0 || prompts[i] >= b->m->V)
+            return fail(SLLM_CUDA_ERR_ARG, "tp_batch_generate: token %d out of range", prompts[i]);
+    return SLLM_CUDA_OK;
+}
+
+int batch_seed(sllm_cuda_tp_batch* b, const int32_t* prompts, int32_t n_prompt, cudaStream_t st) {
+    const int base = b->n_past;
+    if (n_prompt > 0)
+        CK(cudaMemcpy2DAsync(b->tok_seq + base, (size_t)b->n_ctx * 4, prompts, (size_t)n_prompt * 4,
+                             (size_t)n_prompt * 4, (size_t)b->B, cudaMemcpyHostToDevice, st),
+           "prompts");
+    for (int i = 0; i < b->B; ++i) {
+        b->pinned[i] = base;
+        b->pinned[kMaxBatch + i] = base + n_prompt;
+    }
+    CK(cudaMemcpyAsync(b->pos, b->pinned, (size_t)b->B * 4, cudaMemcpyHostToDevice, st), "positions");
+    CK(cudaMemcpyAsync(b->prompt_end, b->pinned + kMaxBatch, (size_t)b->B * 4, cudaMemcpyHostToDevice, st),
+       "prompt ends");
+    return SLLM_CUDA_OK;
+}
+
+int batch_sync(sllm_cuda_tp_batch* b, double seconds) {
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        const cudaError_t e = cudaStreamQuery(b->stream);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) return cuda_fail(e, "batch step");
+        if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > seconds) {
+            if (b->comm != nullptr && b->comm->comm != nullptr) {
+                nccl()->comm_abort(b->comm->comm);
+                b->comm->comm = nullptr;
+            }
+            return fail(SLLM_CUDA_ERR_TIMEOUT, "batch step: no progress in %.0f s (communicator aborted)", seconds);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    return SLLM_CUDA_OK;
+}
+
+int batch_gemm_status() {
+    int* w = gemm_error_word();
+    int v = 0;
+    if (w != nullptr && cudaMemcpy(&v, w, 4, cudaMemcpyDeviceToHost) == cudaSuccess && v != 0) {
+        cudaMemset(w, 0, 4);
+        return fail(SLLM_CUDA_ERR_TIMEOUT, "batch step: a GEMM wait gave up (code %d)", v);
+    }
+    return SLLM_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" int sllm_cuda_tp_batch_new(const sllm_cuda_tp_model* m, sllm_cuda_tp_comm* comm, int32_t n_seq,
+                                      int32_t n_ctx, sllm_cuda_tp_batch** out) {
+    if (m == nullptr || out == nullptr || n_seq < 1 || n_seq > kMaxBatch || n_ctx < 1 || n_ctx > attention_max_ctx())
+        return fail(SLLM_CUDA_ERR_ARG, "tp_batch_new: bad arguments (n_seq %d, n_ctx %d)", n_seq, n_ctx);
+    *out = nullptr;
+    if (comm != nullptr && (comm->n_ranks != m->n_ranks || comm->rank != m->rank || comm->device != m->device))
+        return fail(SLLM_CUDA_ERR_ARG, "tp_batch_new: the communicator's rank does not match the shard's");
+    if (m->E > 8192 || m->E % 128 != 0 || m->F % 32 != 0 || m->F > 32768)
+        return fail(SLLM_CUDA_ERR_UNSUPPORTED, "tp_batch_new: widths %d / %d", m->E, m->F);
+    CK(cudaSetDevice(m->device), "cudaSetDevice");
+    CK(prepare_decode_kernels(), "decode kernel attributes");
+    if (fallback_counter() == nullptr || gemm_error_word() == nullptr)
+        return fail(SLLM_CUDA_ERR_NOMEM, "tp_batch_new: diagnostics words");
+    auto* b = new sllm_cuda_tp_batch();
+    b->m = m;
+    b->comm = comm;
+    b->B = n_seq;
+    b->n_ctx = n_ctx;
+    b->head_ctas = lm_head_batch_ctas(n_seq, num_sms_of(m->device));
+    const int D = kHeadDim, E = m->E, N = m->n_ranks;
+    const size_t B = (size_t)n_seq;
+    const size_t kv = B * m->n_layer * m->hk * D * n_ctx;
+    cudaError_t e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
+    if (!e) e = batch_alloc(b, &b->k_cache, kv);
+    if (!e) e = batch_alloc(b, &b->v_cache, kv);
+    if (!e) e = batch_alloc(b, &b->rope_cos, (size_t)n_ctx * D / 2);
+    if (!e) e = batch_alloc(b, &b->rope_sin, (size_t)n_ctx * D / 2);
+    if (!e) e = batch_alloc(b, &b->x, B * E);
+    if (!e) e = batch_alloc(b, &b->ffn_inp, B * E);
+    if (!e) e = batch_alloc(b, &b->q, B * m->hq * D);
+    if (!e) e = batch_alloc(b, &b->k, B * m->hk * D);
+    if (!e) e = batch_alloc(b, &b->v, B * m->hk * D);
+    if (!e) e = batch_alloc(b, &b->attn_loc, B * m->hq * D);
+    if (!e) e = batch_alloc(b, &b->h_loc, B * m->f_loc);
+    if (N > 1) {
+        if (!e) e = batch_alloc(b, &b->attn_full, B * E);
+        if (!e) e = batch_alloc(b, &b->h_full, B * m->F);
+        if (!e) e = batch_alloc(b, &b->gather, (size_t)N * B * std::max(m->hq * D, m->f_loc));
+        if (!e) e = batch_alloc(b, &b->trip_all, (size_t)N * B * 3);
+    }
+    if (!e) e = batch_alloc(b, &b->logits, B * (size_t)(m->v_loc > 0 ? m->v_loc : 1));
+    if (!e) e = batch_alloc(b, &b->qa, B * E);
+    if (!e) e = batch_alloc(b, &b->qh, B * m->F);
+    if (!e) e = batch_alloc(b, &b->act_a, B);
+    if (!e) e = batch_alloc(b, &b->act_h, B);
+    if (!e) e = batch_alloc(b, &b->dots_o, B * E);
+    if (!e) e = batch_alloc(b, &b->dots_d, B * E * m->down_c);
+    if (!e) e = batch_alloc(b, &b->part_v, B * b->head_ctas);
+    if (!e) e = batch_alloc(b, &b->part_i, B * b->head_ctas);
+    if (!e) e = batch_alloc(b, &b->counter, 1);
+    if (!e) e = batch_alloc(b, &b->trip, B * 3);
+    if (!e) e = batch_alloc(b, &b->argmax, B);
+    if (!e) e = batch_alloc(b, &b->pos, B);
+    if (!e) e = batch_alloc(b, &b->prompt_end, B);
+    if (!e) e = batch_alloc(b, &b->tok_seq, B * n_ctx);
+    if (!e) e = cudaMallocHost(&b->pinned, 2 * kMaxBatch * sizeof(int32_t));
+    if (!e) e = cudaEventCreate(&b->run_ev[0]);
+    if (!e) e = cudaEventCreate(&b->run_ev[1]);
+    if (!e) e = cudaMemset(b->counter, 0, 4);
+    if (!e) e = cudaMemset(b->tok_seq, 0, B * n_ctx * 4);
+    if (!e && N == 1) {
+        // one rank: nothing is gathered, the local buffers are the whole ones
+        b->attn_full = b->attn_loc;
+        b->h_full = b->h_loc;
+        b->trip_all = b->trip;
+    }
+    if (!e) {
+        std::vector<float> cs, sn;
+        rope_table(n_ctx, D, m->rope_base, cs, sn);
+        e = cudaMemcpy(b->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+        if (!e) e = cudaMemcpy(b->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+    }
+    if (e != cudaSuccess) {
+        sllm_cuda_tp_batch_free(b);
+        return cuda_fail(e, "tp_batch_new");
+    }
+    *out = b;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" void sllm_cuda_tp_batch_free(sllm_cuda_tp_batch* b) {
+    if (b == nullptr) return;
+    cudaSetDevice(b->m->device);
+    graph_exec_destroy(b->step);
+    if (b->stream) cudaStreamDestroy(b->stream);
+    for (void* p : b->allocs) cudaFree(p);
+    if (b->pinned) cudaFreeHost(b->pinned);
+    for (cudaEvent_t ev : b->run_ev)
+        if (ev) cudaEventDestroy(ev);
+    delete b;
+}
+
+extern "C" int sllm_cuda_tp_batch_reset(sllm_cuda_tp_batch* b) {
+    if (b == nullptr) return fail(SLLM_CUDA_ERR_ARG, "tp_batch_reset: null");
+    b->n_past = 0;
+    b->have_logits = false;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_tp_batch_generate_greedy(sllm_cuda_tp_batch* b, const int32_t* prompts, int32_t n_prompt,
+                                                  int32_t n_new, int32_t* out) {
+    int rc = batch_validate(b, prompts, n_prompt, n_new, out);
+    if (rc != SLLM_CUDA_OK) return rc;
+    if (n_prompt == 0 && n_new == 0) return SLLM_CUDA_OK;
+    CK(cudaSetDevice(b->m->device), "cudaSetDevice");
+    if (b->m->n_ranks > 1 && (b->comm == nullptr || b->comm->comm == nullptr))
+        return fail(SLLM_CUDA_ERR_COMM, "tp_batch_generate: no communicator");
+    rc = ensure_batch_graph(b);
+    if (rc != SLLM_CUDA_OK) return rc;
+    const int base = b->n_past;
+    rc = batch_seed(b, prompts, n_prompt, b->stream);
+    if (rc != SLLM_CUDA_OK) return rc;
+    const int steps = n_prompt + n_new;
+    CK(cudaEventRecord(b->run_ev[0], b->stream), "run timer");
+    for (int s = 0; s < steps; ++s) CK(graph_launch(b->step, b->stream), "batch step");
+    CK(cudaEventRecord(b->run_ev[1], b->stream), "run timer");
+    if (n_new > 0)
+        CK(cudaMemcpy2DAsync(out, (size_t)n_new * 4, b->tok_seq + base + n_prompt, (size_t)b->n_ctx * 4,
+                             (size_t)n_new * 4, (size_t)b->B, cudaMemcpyDeviceToHost, b->stream),
+           "ids");
+    rc = batch_sync(b, 120.0);
+    if (rc != SLLM_CUDA_OK) return rc;
+    rc = batch_gemm_status();
+    if (rc != SLLM_CUDA_OK) return rc;
+    b->n_past = base + steps;
+    b->have_logits = true;
+    return SLLM_CUDA_OK;
+}
+
+extern "C" int sllm_cuda_tp_batch_last_logits(const sllm_cuda_tp_batch* b, int32_t seq, float* host_out) {
+    if (b == nullptr || host_out == nullptr || seq < 0 || seq >= b->B)
+        return fail(SLLM_CUDA_ERR_ARG, "tp_batch_last_logits: bad arguments");
+    if (!b->have_logits) return fail(SLLM_CUDA_ERR_ARG, "tp_batch_last_logits: nothing forwarded");
+    CK(cudaSetDevice(b->m->device), "cudaSetDevice");
+    CK(cudaMemcpy(host_out, b->logits + (size_t)seq * b->m->v_loc, (size_t)b->m->v_loc * 4, cudaMemcpyDeviceToHost),
+       "logits");
+    return SLLM_CUDA_OK;
+}
+
+extern "C" float sllm_cuda_test_tp_batch_last_run_ms(const sllm_cuda_tp_batch* b) {
+    float ms = -1.0f;
+    if (b == nullptr || cudaEventElapsedTime(&ms, b->run_ev[0], b->run_ev[1]) != cudaSuccess) return -1.0f;
+    return ms;
+}
+
+extern "C" int sllm_cuda_test_tp_batch_generate_group(sllm_cuda_tp_batch** bs, int32_t n, const int32_t* prompts,
+                                                      int32_t n_prompt, int32_t n_new, int32_t* out) {
+    if (bs == nullptr || n < 1 || n > kMaxRanks) return fail(SLLM_CUDA_ERR_ARG, "tp batch group: bad arguments");
+    for (int r = 0; r < n; ++r) {
+        if (bs[r] == nullptr || bs[r]->m->n_ranks != n || bs[r]->m->rank != r ||
+            bs[r]->m->device != bs[0]->m->device || bs[r]->n_past != bs[0]->n_past || bs[r]->n_ctx != bs[0]->n_ctx ||
+            bs[r]->B != bs[0]->B)
+            return fail(SLLM_CUDA_ERR_ARG, "tp batch group: not ranks 0..%d of one model and batch on one device", n - 1);
+        const int rc = batch_validate(bs[r], prompts, n_prompt, n_new, out);
+        if (rc != SLLM_CUDA_OK) return rc;
+    }
+    if (n_prompt == 0 && n_new == 0) return SLLM_CUDA_OK;
+    CK(cudaSetDevice(bs[0]->m->device), "cudaSetDevice");
+    cudaStream_t st = bs[0]->stream;
+    for (int r = 0; r < n; ++r) {
+        const int rc = batch_seed(bs[r], prompts, n_prompt, st);
+        if (rc != SLLM_CUDA_OK) return rc;
+    }
+    const int base = bs[0]->n_past, steps = n_prompt + n_new;
+    for (int s = 0; s < steps; ++s) {
+        for (int ph = 0; ph < n_phases(bs[0]->m); ++ph) {
+            for (int r = 0; r < n; ++r) CK(enqueue_bphase(bs[r], ph, st), "tp batch group phase");
+            const int x = phase_xchg(bs[0]->m, ph);
+            if (x >= 0) CK(bxchg_group(bs, n, x, st), "tp batch group exchange");
+        }
+    }
+    if (n_new > 0)
+        CK(cudaMemcpy2DAsync(out, (size_t)n_new * 4, bs[0]->tok_seq + base + n_prompt, (size_t)bs[0]->n_ctx * 4,
+                             (size_t)n_new * 4, (size_t)bs[0]->B, cudaMemcpyDeviceToHost, st),
+           "ids");
+    CK(cudaStreamSynchronize(st), "tp batch group sync");
+    const int rc = batch_gemm_status();
+    if (rc != SLLM_CUDA_OK) return rc;
+    for (int r = 0; r < n; ++r) {
+        bs[r]->n_past = base + steps;
+        bs[r]->have_logits = true;
+    }
+    return SLLM_CUDA_OK;
 }

@@ -116,3 +116,81 @@ def test_gemm_config3_sizes_match_per_token_gemv(cuda, orc, synth, rows, n):
     qh = q.cpu().numpy()
     for t in (0, 1, 255, 511):
         assert np.array_equal(d[t], orc.gemv(w, rows, n, qh[t])), f"token {t}"
+
+
+# (weight rows, K, tokens) of the skinny form (at most 16 tokens): one tile
+# and one token; ragged rows; the contraction split over clusters of 2, 4 and
+# 8 CTAs (64, 28 and 8 row tiles); the tensor-parallel widths of configs[4]
+SKINNY = [(128, 128, 1), (200, 256, 5), (8192, 1024, 16), (640, 2560, 7), (1024, 8192, 16), (3584, 1024, 3),
+          (8192, 3584, 16)]
+
+
+@pytest.fixture
+def skinny(cuda):
+    cuda.set_gemm_form(2)
+    yield
+    cuda.set_gemm_form(0)
+
+
+@pytest.mark.parametrize("rows,n,m", SKINNY)
+def test_gemm_skinny_bit_exact(cuda, orc, synth, skinny, rows, n, m):
+    """At most 16 tokens, weight rows as the MMA's M operand: the same dots
+    and epilogue bits as the per-token GEMV."""
+    import torch
+    rng = np.random.default_rng(rows + 3 * n + 17 * m)
+    w = synth.random_i2s(rng, rows, n)
+    x = rng.standard_normal((m, n)).astype(np.float32)
+    q, acts = _quant_rows(cuda, x)
+    dots = torch.empty((m, rows), dtype=torch.int32, device="cuda")
+    y = torch.empty((m, rows), dtype=torch.float32, device="cuda")
+    cuda.gemm(_dev(w), rows, n, m, q, acts, dots, y)
+    assert cuda.gemm_error() == 0
+    d = dots.cpu().numpy()
+    yy = y.cpu().numpy()
+    for t in range(m):
+        wy, wd = orc.gemv_f32(w, rows, n, x[t])
+        assert np.array_equal(d[t], wd), f"token {t}"
+        assert np.array_equal(bits(yy[t]), bits(wy)), f"token {t}"
+
+
+@pytest.mark.parametrize("rows,n,m", [(256, 384, 16), (3584, 8192, 16), (384, 2560, 1)])
+def test_gemm_skinny_silu_bit_exact(cuda, orc, synth, skinny, rows, n, m):
+    import torch
+    rng = np.random.default_rng(rows * 3 + n + m)
+    wg = synth.random_i2s(rng, rows, n)
+    wu = synth.random_i2s(rng, rows, n)
+    x = rng.standard_normal((m, n)).astype(np.float32)
+    q, acts = _quant_rows(cuda, x)
+    h = torch.empty((m, rows), dtype=torch.float32, device="cuda")
+    cuda.gemm_silu(_dev(wg), _dev(wu), rows, n, m, q, acts, h)
+    assert cuda.gemm_error() == 0
+    hh = h.cpu().numpy()
+    for t in range(m):
+        g, _ = orc.gemv_f32(wg, rows, n, x[t])
+        u, _ = orc.gemv_f32(wu, rows, n, x[t])
+        want = (orc.silu(g) * u).astype(np.float32)
+        assert np.array_equal(bits(hh[t]), bits(want)), f"token {t}"
+
+
+@pytest.mark.parametrize("form", [1, 2])
+def test_gemm_strided_columns(cuda, orc, synth, form):
+    """A contraction over columns [c0, c0 + k) of a wider activation matrix
+    (the tensor-parallel slice of O or down): both forms give the oracle's
+    dots of that slice."""
+    import torch
+    rows, k, width, c0, m = 512, 1024, 4096, 2048, 12
+    rng = np.random.default_rng(99 + form)
+    w = synth.random_i2s(rng, rows, k)
+    x = rng.standard_normal((m, width)).astype(np.float32)
+    q, acts = _quant_rows(cuda, x)
+    dots = torch.empty((m, rows), dtype=torch.int32, device="cuda")
+    cuda.set_gemm_form(form)
+    try:
+        cuda.gemm_strided(_dev(w), rows, k, m, q[:, c0:], width, acts, dots, None)
+        assert cuda.gemm_error() == 0
+    finally:
+        cuda.set_gemm_form(0)
+    d = dots.cpu().numpy()
+    qh = q.cpu().numpy()
+    for t in range(m):
+        assert np.array_equal(d[t], orc.gemv(w, rows, k, qh[t, c0:c0 + k])), f"token {t}"
