@@ -596,12 +596,54 @@ def tp_decode_leg(pkg, local, rank, world, args):
                                 "one-shot peer-memory exchange kernels (P2P stores + epoch flags) in the step "
                                 "graph")}[ctx.exchange_kind()]}
     ctx.close()
+    out["batch16"] = tp_batch_run(pkg, model, comm, sd, prompt, n_new, world, rank, per_gpu_bytes, kv_row)
     model.close()
     if comm is not None:
         comm.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_reference"] = tp_cpu_reference(sd, steps)
     return out
+
+
+def tp_batch_run(pkg, model, comm, sd, prompt, n_new, world, rank, per_gpu_bytes, kv_row, n_seq=16):
+    """configs[4] at batch 16: 16 sequences (the batch-1 prompt and 15 more
+    seeded prompts of the same length) stepped together, every layer GEMV one
+    16-token GEMM on the tensor cores. tokens/s counts every sequence's
+    tokens (prompt and generated) over the wall clock of the generate call,
+    max over ranks. Sequence 0's tokens are the batch-1 run's."""
+    import torch
+    n_prompt = len(prompt)
+    prompts = np.random.default_rng(11).integers(0, sd.n_vocab, (n_seq, n_prompt)).astype(np.int32)
+    prompts[0] = prompt
+    b = model.batch(n_seq, n_prompt + n_new + 8, comm)
+    rc, _ = b.generate(prompts[:, :8], 8)          # warm-up: builds the step graph
+    assert rc == 0, rc
+    b.reset()
+    if world > 1:
+        torch.distributed.barrier()
+    t0 = time.perf_counter()
+    rc, toks = b.generate(prompts, n_new)
+    dt = time.perf_counter() - t0
+    assert rc == 0, rc
+    dev_ms = max_over_ranks(b.last_run_ms(), world)
+    dt = max_over_ranks(dt, world)
+    b.close()
+    steps = n_prompt + n_new
+    run_bytes_gpu = per_gpu_bytes * steps + n_seq * kv_row * sum(range(1, steps + 1))
+    peak, peak_kind = peaks()
+    achieved = run_bytes_gpu / (dev_ms / 1e3) / 1e9
+    return {"workload": f"tp_decode_80L_8192 (configs[4], batch {n_seq})", "tp": world, "batch": n_seq,
+            "tokens_per_s": round(n_seq * steps / dt, 1), "ms_per_step": round(dt / steps * 1e3, 4),
+            "device_ms_per_step": round(dev_ms / steps, 4),
+            "steps": f"{n_prompt} prompt + {n_new} greedy positions per sequence, {n_seq} sequences per step",
+            "token_checksum_seq0": int(sum((i + 1) * int(v) for i, v in enumerate(toks[0]))),
+            "token_checksum_all": int(sum((i + 1) * int(v) for i, v in enumerate(toks.reshape(-1)))),
+            "roofline": {"bound": "hbm", "kernel": "batch step graph (skinny tcgen05 GEMMs, attention, exchanges, "
+                                                  "batched head), device time, slowest rank",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s per GPU",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                         "bytes_per_step_per_gpu": int(run_bytes_gpu / steps)},
+            "layer_gemms": "skinny tcgen05 kind::i8 GEMM: 128 weight rows (M) x 16 tokens (N) per CTA"}
 
 
 def tp_cpu_reference(sd, steps):

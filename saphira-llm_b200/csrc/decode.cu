@@ -386,6 +386,8 @@ lm_head_batch_kernel(const LmBatchParams p) {
     int bi[T];
     #pragma unroll
     for (int t = 0; t < T; ++t) { bv[t] = NAN; bi[t] = 0x7fffffff; }
+    // U steps per iteration, the next iteration's weights loaded before this
+    // one's FMAs (a row's loads are otherwise exposed once per iteration)
     constexpr int U = 4;
     for (int grp = cta * kLmWarps + warp; grp < ngroups; grp += ncta * kLmWarps) {
         const int row = 8 * grp + sub;
@@ -396,10 +398,16 @@ lm_head_batch_kernel(const LmBatchParams p) {
         for (int t = 0; t < T; ++t)
             #pragma unroll
             for (int l = 0; l < 8; ++l) a[t][l] = 0.0f;
+        uint4 nx[U];
+        #pragma unroll
+        for (int u = 0; u < U; ++u) nx[u] = (u < nsteps) ? ld_stream_u128(wrow + 64 * u) : make_uint4(0, 0, 0, 0);
         for (int m0 = 0; m0 < nsteps; m0 += U) {
             uint4 wv[U];
             #pragma unroll
-            for (int u = 0; u < U; ++u) wv[u] = (m0 + u < nsteps) ? ld_stream_u128(wrow + 64 * (m0 + u)) : make_uint4(0, 0, 0, 0);
+            for (int u = 0; u < U; ++u) wv[u] = nx[u];
+            #pragma unroll
+            for (int u = 0; u < U; ++u)
+                nx[u] = (m0 + U + u < nsteps) ? ld_stream_u128(wrow + 64 * (m0 + U + u)) : make_uint4(0, 0, 0, 0);
             #pragma unroll
             for (int u = 0; u < U; ++u) {
                 if (m0 + u < nsteps) {

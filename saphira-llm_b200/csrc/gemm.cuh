@@ -33,6 +33,22 @@ cudaError_t launch_i2s_gemm(const GemmArgs& a, int* error, cudaStream_t st);
 // the same results for at most 16 tokens (a.m <= 16), weight rows as the
 // MMA's M operand and the tokens as its N = 16 operand
 cudaError_t launch_i2s_gemm_skinny(const GemmArgs& a, int* error, cudaStream_t st);
+
+// One tensor of a multi-tensor skinny launch: rows of w (and of w2, the up
+// tensor of a gate/up pair: then y receives h = silu(gate) * up and every
+// segment is a pair), contracted with activation columns [kx, kx + K) of q.
+struct SkinnySeg {
+    const uint8_t* w;
+    const uint8_t* w2;
+    int n_rows;
+    int kx;                      // a multiple of 16
+    int32_t* dots;               // [m][n_rows] or null
+    float* y;                    // [m][n_rows] or null
+};
+// up to four segments sharing q (row stride lda bytes, 0: K), K and the
+// token count m <= 16
+cudaError_t launch_i2s_gemm_skinny_segs(const SkinnySeg* segs, int nseg, const int8_t* q, int lda, int m, int K,
+                                        const sllm_cuda_act* acts, int* error, cudaStream_t st);
 // test hook: 0 picks the form by size (skinny for m <= 16), 1 forces the
 // 128-token tiles, 2 the skinny form
 void gemm_set_form(int form);

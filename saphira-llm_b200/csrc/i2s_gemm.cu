@@ -41,6 +41,7 @@
 // gives up records an error, the CTA stops issuing work, drains what it has
 // in flight (bounded) and frees its tensor memory before it exits.
 
+#include <algorithm>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -522,37 +523,72 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
 // The skinny form: at most 16 tokens (a decode step of a batch of sequences).
 // The roles swap: 128 weight rows are the MMA's M operand, unpacked into
 // shared memory as above, and the tokens are its N = 16 operand (one TMA box
-// of 16 rows x 128 bytes, zero past m), so no MMA column is padding and the
-// tensor pipe does 1/8 of the work of a 128-token tile. The accumulator is
-// 128 TMEM lanes (weight rows) x 16 columns (tokens), gate at column 0 and up
-// at column 16 for the fused pair. The same warp roles; the epilogue runs on
-// warps 2-5 (one TMEM lane quarter each), a lane per weight row, so the
-// stores of one token's outputs are 32 consecutive words per warp.
+// of 16 rows x 128 bytes, zero past m), so no MMA column is padding. The
+// accumulator is 128 TMEM lanes (weight rows) x 16 columns (tokens).
 //
-// Unpack order: thread t takes half t & 1 of row t >> 1 (eight threads read
-// 128 contiguous bytes), and stores field f ^ 2 (row & 1) first, so the eight
-// 16-byte stores of a quarter warp land on eight distinct swizzled chunks.
+// One launch covers up to four weight tensors ("segments") that share the
+// activation matrix: Q, K and V, or the column chunks of down, each with its
+// own column offset into the activations. A tile is 128 rows of one tensor,
+// or, for the gate/up pair, 64 rows of gate over the same 64 rows of up
+// (TMEM lanes 0-63 and 64-127). The grid is persistent: CTA c takes tiles
+// c, c + G, ..., two CTAs per SM.
 //
-// A short grid (few 128-row tiles) splits the contraction over a cluster of
-// SK CTAs as above: the others leave their 128 x 16 (x 2) partial sums in
-// their idle rings and the first adds them through distributed shared memory.
+//   warp 0 (one lane)   TMA: per stage of four k-steps, the four activation
+//                       boxes and the next 128 bytes of every weight row of
+//                       the tile (128-byte swizzle), three stages in flight.
+//   warps 2-9           unpack a k-step's packed bytes into one of two 16 KB
+//                       operand stages (a quarter warp takes rows r, r + 2,
+//                       r + 4, r + 6, both halves: its loads and stores land on
+//                       eight distinct 16-byte chunks).
+//   warp 1 (one lane)   tcgen05.mma kind::i8, M = 128, N = 16, K = 32, x 4 per
+//                       k-step into one of two accumulators (tile parity);
+//                       commits free the operand stage, the packed stage and,
+//                       after a tile's last k-step, fill the accumulator.
+//                       (Issuing from the unpack warps behind a named barrier
+//                       measured slower.)
+//   warps 10-13         epilogue: tcgen05.ld of the accumulator (warp w: TMEM
+//                       lanes 32 (w % 4) ..), which then returns to the MMA
+//                       warp, so a tile's epilogue overlaps the next tile's
+//                       k-loop; one lane per weight row, the stores of a
+//                       token's outputs coalesced. For the pair the up lanes
+//                       hand their sums to the gate lanes through shared
+//                       memory (bounded mbarrier hand-over).
+//
+// A grid shorter than two CTAs per SM instead splits the contraction over a
+// cluster of SK CTAs, one tile each, as the 128-token form does.
 // ---------------------------------------------------------------------------
-constexpr int kSkM = 128;       // weight rows per tile (MMA M, TMEM lanes)
+constexpr int kSkM = 128;       // operand rows per tile (MMA M, TMEM lanes)
 constexpr int kSkN = 16;        // tokens (MMA N)
+constexpr int kSkMaxSeg = 4;
+constexpr int kSkSp = 3;        // packed stages
+constexpr int kSkSa = 2;        // operand stages
+constexpr int kSkG = 4;         // k-steps per packed stage: 128-byte segments of every weight row
+constexpr int kSkPStage = kSkG * kSkN * kBK + kSkM * kSkG * kPK;    // 4 activation boxes + packed weights: 24 KB
+constexpr int kSkAStage = kSkM * kBK;                   // unpacked codes: 16 KB
+__host__ __device__ constexpr int skinny_packed_stages(bool) { return kSkSp; }
+__host__ __device__ constexpr int skinny_smem(bool pair) {
+    return kSkSa * kSkAStage + skinny_packed_stages(pair) * kSkPStage + 1024;
+}
+constexpr int kSkEpiWarp0 = 2 + kGmUnpackWarps;        // warps 10-13
+constexpr int kSkThreads = 32 * (kSkEpiWarp0 + 4);
+constexpr int kSkTmemCols = 32;                         // two accumulators of 16 columns
+static_assert(kSkPStage % 1024 == 0 && kSkAStage % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+static_assert(kSkSa * kSkAStage >= kSkN * kSkM * 4, "a split CTA's partial sums fit the operand ring");
 
-template <bool PAIR>
-struct SkinnyCfg {
-    static constexpr int NM = PAIR ? 2 : 1;
-    static constexpr int A_BYTES = kSkM * kBK;      // unpacked codes of one matrix
-    static constexpr int B_BYTES = kSkN * kBK;      // the tokens' activation bytes
-    static constexpr int P_BYTES = kSkM * kPK;      // packed codes of one matrix
-    static constexpr int STAGE = NM * A_BYTES + B_BYTES + NM * P_BYTES;
-    static constexpr int S = (225280 / STAGE) > 10 ? 10 : (225280 / STAGE);
-    static constexpr int SMEM = S * STAGE + 1024;
-    static constexpr int TMEM_COLS = 32;
-    static_assert(STAGE % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
-    static_assert(S >= 2, "ring depth");
-    static_assert(S * STAGE >= NM * kSkN * kSkM * 4, "a split CTA's partial sums fit its ring");
+struct SkParams {
+    CUtensorMap act;                    // [m][cols] int8, box 128 x 16, 128-byte swizzle
+    CUtensorMap w[kSkMaxSeg];           // packed rows, box 32 B x (128 or 64 for the pair)
+    CUtensorMap w2[kSkMaxSeg];          // the pair's up tensor
+    int tile_end[kSkMaxSeg];            // cumulative tile counts
+    int n_rows[kSkMaxSeg];
+    int kx[kSkMaxSeg];                  // the segment's first activation column
+    const float* ws[kSkMaxSeg];
+    const float* ws2[kSkMaxSeg];
+    int32_t* dots[kSkMaxSeg];
+    float* y[kSkMaxSeg];
+    const sllm_cuda_act* acts;
+    int* error;
+    int nseg, tiles, M, K;
 };
 
 // 16 consecutive accumulator columns of this warp's 32 TMEM lanes
@@ -565,40 +601,55 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
 }
 
+__device__ __forceinline__ void umma_commit_to(uint64_t* bar) { umma_commit(bar); }
+
 template <bool PAIR, int SK>
-__global__ void __launch_bounds__(kGmThreads, 1)
-i2s_gemm_skinny_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
-                       const __grid_constant__ CUtensorMap tm_w2, const GemmKParams p) {
-    using C = SkinnyCfg<PAIR>;
+__global__ void __launch_bounds__(kSkThreads, 2)
+i2s_gemm_skinny_kernel(const __grid_constant__ SkParams P) {
+    constexpr int TR = PAIR ? 64 : 128;          // weight rows per tile (of each tensor)
+    constexpr int SP = skinny_packed_stages(PAIR);
     extern __shared__ uint8_t gsm_raw[];
-    __shared__ uint64_t bar_loaded[C::S], bar_unpacked[C::S], bar_empty[C::S], bar_acc;
+    __shared__ uint64_t bar_loaded[kSkSp], bar_pempty[kSkSp], bar_unpacked[kSkSa], bar_aempty[kSkSa];
+    __shared__ uint64_t bar_full[2], bar_drained[2], bar_xfull, bar_xfree;
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
+    __shared__ float s_up[PAIR ? kSkN * 64 : 1];          // [token][64 rows]
     uint8_t* const gsm = gsm_raw + ((1024u - (smem_u32(gsm_raw) & 1023u)) & 1023u);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kSkM;
-    const int KB_all = p.K / kBK;
-    const int kb0 = (int)((long long)blockIdx.z * KB_all / SK);
-    const int KB = (int)((long long)(blockIdx.z + 1) * KB_all / SK) - kb0;     // >= 1: the host keeps SK <= KB_all
-    auto A = [&](int s, int mat) { return gsm + (size_t)s * C::STAGE + mat * C::A_BYTES; };
-    auto Bt = [&](int s) { return gsm + (size_t)s * C::STAGE + C::NM * C::A_BYTES; };
-    auto P = [&](int s, int mat) {
-        return gsm + (size_t)s * C::STAGE + C::NM * C::A_BYTES + C::B_BYTES + mat * C::P_BYTES;
+    auto A = [&](int sa) { return gsm + (size_t)sa * kSkAStage; };
+    auto PS = [&](int sp) { return gsm + (size_t)kSkSa * kSkAStage + (size_t)sp * kSkPStage; };
+    const int KB_all = P.K / kBK;
+    const int kb0 = SK > 1 ? (int)((long long)blockIdx.z * KB_all / SK) : 0;
+    const int KB = SK > 1 ? (int)((long long)(blockIdx.z + 1) * KB_all / SK) - kb0 : KB_all;   // >= 2
+    const int t_first = blockIdx.x, t_step = SK > 1 ? P.tiles : gridDim.x;
+    auto seg_of = [&](int t, int* row0) {
+        int sg = 0;
+        while (sg + 1 < P.nseg && t >= P.tile_end[sg]) ++sg;
+        *row0 = (t - (sg > 0 ? P.tile_end[sg - 1] : 0)) * TR;
+        return sg;
     };
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::S; ++s) {
-            mbar_init(&bar_loaded[s], 1);
-            mbar_init(&bar_unpacked[s], kGmUnpackWarps);
-            mbar_init(&bar_empty[s], 1);
+        for (int i = 0; i < SP; ++i) {
+            mbar_init(&bar_loaded[i], 1);
+            mbar_init(&bar_pempty[i], 1);
         }
-        mbar_init(&bar_acc, 1);
+        for (int i = 0; i < kSkSa; ++i) {
+            mbar_init(&bar_unpacked[i], kGmUnpackWarps);
+            mbar_init(&bar_aempty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bar_full[i], 1);
+            mbar_init(&bar_drained[i], 4);
+        }
+        mbar_init(&bar_xfull, 2);
+        mbar_init(&bar_xfree, 2);
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
-                     "r"((uint32_t)C::TMEM_COLS)
+                     "r"((uint32_t)kSkTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -609,162 +660,218 @@ i2s_gemm_skinny_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_co
     volatile int* const abort_v = &abort_flag;
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
+    const int quarter = warp & 3;
+    uint32_t g[16];                      // SK > 1: the epilogue warps' one tile
     bool ep_ok = false;
+
+    // the outputs of tile t (j: this CTA's tile count, for the hand-over
+    // buffer's parity) from this lane's 16 sums
+    auto finish_tile = [&](int j, int t, const uint32_t (&v)[16]) -> bool {
+        int row0;
+        const int sg = seg_of(t, &row0);
+        if (PAIR) {
+            const uint32_t par = (uint32_t)j & 1u;
+            float* up = s_up;
+            if (quarter >= 2) {
+                // up rows 0..63 of the tile are TMEM lanes 64..127
+                if (j >= 1 && !gm_wait(&bar_xfree, par ^ 1u, abort_v, P.error)) return false;
+                #pragma unroll
+                for (int jj = 0; jj < kSkN; ++jj) up[jj * 64 + 32 * (quarter - 2) + lane] = __int_as_float((int)v[jj]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bar_xfull);
+                return true;
+            }
+            if (!gm_wait(&bar_xfull, par, abort_v, P.error)) return false;
+            const int n = row0 + 32 * quarter + lane;
+            if (n < P.n_rows[sg]) {
+                const float ws = __ldg(P.ws[sg]), ws2 = __ldg(P.ws2[sg]);
+                float* y = P.y[sg];
+                #pragma unroll
+                for (int jj = 0; jj < kSkN; ++jj) {
+                    if (jj < P.M) {
+                        const sllm_cuda_act act = P.acts[jj];
+                        // h = silu(gate) * up (src/forward.c:765-778, src/ops.c:452-456)
+                        const float post = __fdiv_rn(ws, act.scale), post2 = __fdiv_rn(ws2, act.scale);
+                        const int uv_i = __float_as_int(up[jj * 64 + 32 * quarter + lane]);
+                        const float gv = __fmul_rn(__int2float_rn((int)v[jj] - act.sum), post);
+                        const float uv = __fmul_rn(__int2float_rn(uv_i - act.sum), post2);
+                        y[(size_t)jj * P.n_rows[sg] + n] = __fmul_rn(silu_block(gv), uv);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_xfree);
+            return true;
+        }
+        const int n = row0 + 32 * quarter + lane;
+        if (n < P.n_rows[sg]) {
+            const float ws = __ldg(P.ws[sg]);
+            int32_t* dots = P.dots[sg];
+            float* y = P.y[sg];
+            #pragma unroll
+            for (int jj = 0; jj < kSkN; ++jj) {
+                if (jj < P.M) {
+                    const size_t o = (size_t)jj * P.n_rows[sg] + n;
+                    if (dots != nullptr) dots[o] = (int)v[jj];
+                    if (y != nullptr) {
+                        const sllm_cuda_act act = P.acts[jj];
+                        // per-tensor scale over the token's activation scale (src/forward.c:653-655)
+                        y[o] = __fmul_rn(__int2float_rn((int)v[jj] - act.sum), __fdiv_rn(ws, act.scale));
+                    }
+                }
+            }
+        }
+        return true;
+    };
+
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            int issued = 0;
-            for (int kb = 0; kb < KB; ++kb) {
-                const int s = kb % C::S;
-                const uint32_t use = (uint32_t)(kb / C::S);
-                if (use > 0 && !gm_wait(&bar_empty[s], (use - 1) & 1u, abort_v, p.error)) break;
-                mbar_expect_tx(&bar_loaded[s], (uint32_t)(C::B_BYTES + C::NM * C::P_BYTES));
-                tma_load_2d(Bt(s), &tm_a, (kb0 + kb) * kBK, 0, &bar_loaded[s]);
-                tma_load_2d(P(s, 0), &tm_w, (kb0 + kb) * kPK, n0, &bar_loaded[s]);
-                if (PAIR) tma_load_2d(P(s, 1), &tm_w2, (kb0 + kb) * kPK, n0, &bar_loaded[s]);
-                ++issued;
+            int gs = 0;      // packed stages issued
+            bool ok = true;
+            for (int t = t_first; t < P.tiles && ok; t += t_step) {
+                int row0;
+                const int sg = seg_of(t, &row0);
+                for (int kb = kb0; kb < kb0 + KB; kb += kSkG, ++gs) {
+                    const int sp = gs % SP;
+                    const uint32_t use = (uint32_t)(gs / SP);
+                    if (use > 0 && !gm_wait(&bar_pempty[sp], (use - 1) & 1u, abort_v, P.error)) { ok = false; break; }
+                    mbar_expect_tx(&bar_loaded[sp], (uint32_t)kSkPStage);
+                    uint8_t* st = PS(sp);
+                    #pragma unroll
+                    for (int i = 0; i < kSkG; ++i)      // columns past the contraction read as zeros
+                        tma_load_2d(st + i * (kSkN * kBK), &P.act, P.kx[sg] + (kb + i) * kBK, 0, &bar_loaded[sp]);
+                    uint8_t* pw = st + kSkG * kSkN * kBK;
+                    tma_load_2d(pw, &P.w[sg], kb * kPK, row0, &bar_loaded[sp]);
+                    if (PAIR) tma_load_2d(pw + 64 * kSkG * kPK, &P.w2[sg], kb * kPK, row0, &bar_loaded[sp]);
+                }
             }
-            for (int kb = issued > C::S ? issued - C::S : 0; kb < issued; ++kb)
-                gm_drain(&bar_loaded[kb % C::S], (uint32_t)(kb / C::S) & 1u);
+            for (int i = gs > SP ? gs - SP : 0; i < gs; ++i)
+                gm_drain(&bar_loaded[i % SP], (uint32_t)(i / SP) & 1u);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_i8(kSkM, kSkN);
-            int issued = 0;
-            for (int kb = 0; kb < KB; ++kb) {
-                const int s = kb % C::S;
-                const uint32_t ph = (uint32_t)(kb / C::S) & 1u;
-                if (!gm_wait(&bar_unpacked[s], ph, abort_v, p.error)) break;
+            int gk = 0, gs = 0, j = 0;
+            bool ok = true;
+            for (int t = t_first; t < P.tiles && ok; t += t_step, ++j) {
+                const int buf = j & 1;
+                if (j >= 2 && !gm_wait(&bar_drained[buf], (uint32_t)((j >> 1) - 1) & 1u, abort_v, P.error)) break;
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(A(s, 0)), b0 = smem_u32(Bt(s));
-                #pragma unroll
-                for (int kk = 0; kk < kBK / 32; ++kk) {
-                    const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
-                    umma_i8(tmem, umma_desc_sw128(a0 + 32u * kk), umma_desc_sw128(b0 + 32u * kk), idesc, acc);
-                    if (PAIR)
-                        umma_i8(tmem + (uint32_t)kSkN, umma_desc_sw128(a0 + (uint32_t)C::A_BYTES + 32u * kk),
-                                umma_desc_sw128(b0 + 32u * kk), idesc, acc);
-                }
-                umma_commit(&bar_empty[s]);
-                ++issued;
-            }
-            umma_commit(&bar_acc);
-            if (issued > 0) gm_drain(&bar_empty[(issued - 1) % C::S], (uint32_t)((issued - 1) / C::S) & 1u);
-        }
-        __syncwarp();
-    } else {
-        // ---------------- unpack (warps 2-9) ----------------
-        constexpr int NT = 32 * kGmUnpackWarps;
-        const int t = threadIdx.x - 64;
-        bool ok = true;
-        for (int kb = 0; kb < KB && ok; ++kb) {
-            const int s = kb % C::S;
-            const uint32_t ph = (uint32_t)(kb / C::S) & 1u;
-            ok = gm_wait(&bar_loaded[s], ph, abort_v, p.error);
-            if (ok) {
-                #pragma unroll
-                for (int it = t; it < C::NM * 2 * kSkM; it += NT) {
-                    const int h = it & 1, row = (it >> 1) & (kSkM - 1), mat = it / (2 * kSkM);
-                    const uint4 v = *reinterpret_cast<const uint4*>(P(s, mat) + row * kPK + h * 16);
-                    uint8_t* arow = A(s, mat) + row * kBK;
+                const uint32_t d = tmem + (uint32_t)(buf * kSkN);
+                for (int kb = 0; kb < KB; ++kb, ++gk) {
+                    const int sa = gk % kSkSa, sp = gs % SP, sub = kb % kSkG;
+                    if (!gm_wait(&bar_unpacked[sa], (uint32_t)(gk / kSkSa) & 1u, abort_v, P.error)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(A(sa)), b0 = smem_u32(PS(sp) + sub * (kSkN * kBK));
                     #pragma unroll
-                    for (int f = 0; f < 4; ++f) {
-                        const int fs = f ^ ((row & 1) << 1);
-                        uint4 o;
-                        o.x = field_codes(v.x, fs);
-                        o.y = field_codes(v.y, fs);
-                        o.z = field_codes(v.z, fs);
-                        o.w = field_codes(v.w, fs);
-                        const int chunk = (2 * fs + h) ^ (row & 7);
-                        *reinterpret_cast<uint4*>(arow + chunk * 16) = o;
+                    for (int kk = 0; kk < kBK / 32; ++kk)
+                        umma_i8(d, umma_desc_sw128(a0 + 32u * kk), umma_desc_sw128(b0 + 32u * kk), idesc,
+                                (kb > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit_to(&bar_aempty[sa]);
+                    if (sub == kSkG - 1 || kb == KB - 1) {      // the packed stage's last k-step
+                        umma_commit_to(&bar_pempty[sp]);
+                        ++gs;
                     }
                 }
-                fence_proxy_async_smem();
+                if (ok) umma_commit_to(&bar_full[buf]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bar_unpacked[s]);
-            ok = __all_sync(0xffffffffu, ok);
+            if (gk > 0) gm_drain(&bar_aempty[(gk - 1) % kSkSa], (uint32_t)((gk - 1) / kSkSa) & 1u);
         }
-        ep_ok = __all_sync(0xffffffffu, ok && gm_wait(&bar_acc, 0u, abort_v, p.error)) &&
-                __all_sync(0xffffffffu, *abort_v == 0);
+        __syncwarp();
+    } else if (warp < kSkEpiWarp0) {
+        // ---------------- unpack (warps 2-9) ----------------
+        // one 16-byte item per thread and k-step: half h of the row's 32 packed
+        // bytes; a quarter warp takes rows r, r + 2, r + 4, r + 6 (both
+        // halves), so its eight 16-byte loads (128-byte swizzle) and each of
+        // its stores land on eight distinct chunks
+        const int tt = threadIdx.x - 64;
+        const int h = tt & 1, row = (tt >> 4) * 8 + ((tt >> 1) & 3) * 2 + ((tt >> 3) & 1);
+        const int prow_off = kSkG * kSkN * kBK + row * (kSkG * kPK);     // the row's 128 bytes in a packed stage
+        int gk = 0, gs = 0;
+        bool ok = true;
+        for (int t = t_first; t < P.tiles && ok; t += t_step) {
+            for (int kb = 0; kb < KB; ++kb, ++gk) {
+                const int sp = gs % SP, sa = gk % kSkSa, sub = kb % kSkG;
+                if (sub == 0) ok = gm_wait(&bar_loaded[sp], (uint32_t)(gs / SP) & 1u, abort_v, P.error);
+                if (ok && gk >= kSkSa) ok = gm_wait(&bar_aempty[sa], (uint32_t)((gk / kSkSa) - 1) & 1u, abort_v, P.error);
+                if (ok) {
+                    const int chunk = (2 * sub + h) ^ (row & 7);
+                    const uint4 v = *reinterpret_cast<const uint4*>(PS(sp) + prow_off + (chunk << 4));
+                    uint8_t* arow = A(sa) + row * kBK;
+                    #pragma unroll
+                    for (int f = 0; f < 4; ++f) {
+                        uint4 o;
+                        o.x = field_codes(v.x, f);
+                        o.y = field_codes(v.y, f);
+                        o.z = field_codes(v.z, f);
+                        o.w = field_codes(v.w, f);
+                        *reinterpret_cast<uint4*>(arow + (((2 * f + h) ^ (row & 7)) << 4)) = o;
+                    }
+                    fence_proxy_async_smem();
+                }
+                if (sub == kSkG - 1 || kb == KB - 1) ++gs;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bar_unpacked[sa]);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 10-13) ----------------
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * quarter) << 16);
+        int j = 0;
+        bool ok = true;
+        for (int t = t_first; t < P.tiles && ok; t += t_step, ++j) {
+            const int buf = j & 1;
+            ok = __all_sync(0xffffffffu, gm_wait(&bar_full[buf], (uint32_t)(j >> 1) & 1u, abort_v, P.error));
+            if (!ok) break;
+            tc_fence_after();
+            uint32_t v[16];
+            tmem_ld16(lane_base + (uint32_t)(buf * kSkN), v);
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_drained[buf]);
+            if (SK > 1) {
+                #pragma unroll
+                for (int jj = 0; jj < kSkN; ++jj) g[jj] = v[jj];
+                ep_ok = true;
+            } else {
+                ok = __all_sync(0xffffffffu, finish_tile(j, t, v));
+            }
+        }
+        ep_ok = __all_sync(0xffffffffu, ep_ok && ok && *abort_v == 0);
     }
-    const int quarter = warp & 3;
-    const bool ep_warp = warp >= 2 && warp < 6;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * quarter) << 16);
-    // a split CTA's partial sums in its idle ring: [column][128 rows]
-    uint32_t* const part = reinterpret_cast<uint32_t*>(gsm);
     if constexpr (SK > 1) {
+        // one tile per CTA: the other CTAs' partial sums through distributed
+        // shared memory (the operand ring is idle once the tile is complete)
         namespace cg = cooperative_groups;
         cg::cluster_group cl = cg::this_cluster();
+        uint32_t* const part = reinterpret_cast<uint32_t*>(gsm);
+        const bool ep_warp = warp >= kSkEpiWarp0;
         if (ep_warp && cl.block_rank() != 0 && ep_ok) {
-            tc_fence_after();
-            uint32_t g[16];
-            tmem_ld16(lane_base, g);
-            tmem_ld_wait();
             #pragma unroll
-            for (int j = 0; j < kSkN; ++j) part[j * kSkM + 32 * quarter + lane] = g[j];
-            if (PAIR) {
-                tmem_ld16(lane_base + (uint32_t)kSkN, g);
-                tmem_ld_wait();
-                #pragma unroll
-                for (int j = 0; j < kSkN; ++j) part[(kSkN + j) * kSkM + 32 * quarter + lane] = g[j];
-            }
+            for (int jj = 0; jj < kSkN; ++jj) part[jj * kSkM + 32 * quarter + lane] = g[jj];
         }
         cl.sync();
-    }
-    bool lead = true;
-    if constexpr (SK > 1) lead = cooperative_groups::this_cluster().block_rank() == 0;
-    if (ep_warp && ep_ok && lead) {
-        tc_fence_after();
-        uint32_t g[16], u[16];
-        tmem_ld16(lane_base, g);
-        if (PAIR) tmem_ld16(lane_base + (uint32_t)kSkN, u);
-        tmem_ld_wait();
-        if constexpr (SK > 1) {
-            namespace cg = cooperative_groups;
-            cg::cluster_group cl = cg::this_cluster();
+        if (ep_warp && cl.block_rank() == 0 && ep_ok) {
             #pragma unroll 1
             for (int r = 1; r < SK; ++r) {
                 const uint32_t* rp = cl.map_shared_rank(part, r);
                 #pragma unroll
-                for (int j = 0; j < kSkN; ++j) {
-                    g[j] += rp[j * kSkM + 32 * quarter + lane];
-                    if (PAIR) u[j] += rp[(kSkN + j) * kSkM + 32 * quarter + lane];
-                }
+                for (int jj = 0; jj < kSkN; ++jj) g[jj] += rp[jj * kSkM + 32 * quarter + lane];
             }
+            finish_tile(0, blockIdx.x, g);
         }
-        const int n = n0 + 32 * quarter + lane;       // this lane's weight row
-        if (n < p.N) {
-            const float ws = __ldg(p.ws);
-            const float ws2 = PAIR ? __ldg(p.ws2) : 0.0f;
-            #pragma unroll
-            for (int j = 0; j < kSkN; ++j) {
-                if (j < p.M) {
-                    const sllm_cuda_act act = p.acts[j];
-                    // per-tensor scale over the token's activation scale (src/forward.c:653-655)
-                    const float post = __fdiv_rn(ws, act.scale);
-                    const size_t o = (size_t)j * p.N + n;
-                    if (PAIR) {
-                        // h = silu(gate) * up (src/forward.c:765-778, src/ops.c:452-456)
-                        const float post2 = __fdiv_rn(ws2, act.scale);
-                        const float gv = __fmul_rn(__int2float_rn((int)g[j] - act.sum), post);
-                        const float uv = __fmul_rn(__int2float_rn((int)u[j] - act.sum), post2);
-                        p.y[o] = __fmul_rn(silu_block(gv), uv);
-                    } else {
-                        if (p.dots != nullptr) p.dots[o] = (int)g[j];
-                        if (p.y != nullptr) p.y[o] = __fmul_rn(__int2float_rn((int)g[j] - act.sum), post);
-                    }
-                }
-            }
-        }
+        cl.sync();
     }
-    if constexpr (SK > 1) cooperative_groups::this_cluster().sync();   // the leader has read the partials
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kSkTmemCols)
                      : "memory");
     }
 }
@@ -882,37 +989,14 @@ cudaError_t launch_tile(const GemmArgs& a, int* error, cudaStream_t st) {
 }
 
 template <bool PAIR, int SK>
-cudaError_t launch_skinny(const GemmArgs& a, int* error, cudaStream_t st) {
-    using C = SkinnyCfg<PAIR>;
-    CUtensorMap tm_a, tm_w, tm_w2;
-    if (!encode_2d(&tm_a, a.q, (uint64_t)a.K, (uint64_t)a.m, kBK, kSkN, CU_TENSOR_MAP_SWIZZLE_128B,
-                   (uint64_t)(a.lda > 0 ? a.lda : a.K)) ||
-        !encode_2d(&tm_w, a.w, (uint64_t)(a.K / 4), (uint64_t)a.n_rows, kPK, kSkM, CU_TENSOR_MAP_SWIZZLE_NONE))
-        return cudaErrorInvalidValue;
-    if (PAIR) {
-        if (!encode_2d(&tm_w2, a.w2, (uint64_t)(a.K / 4), (uint64_t)a.n_rows, kPK, kSkM, CU_TENSOR_MAP_SWIZZLE_NONE))
-            return cudaErrorInvalidValue;
-    } else {
-        tm_w2 = tm_w;
-    }
-    GemmKParams p{};
-    p.acts = a.acts;
-    const size_t tail = (size_t)a.n_rows * (size_t)(a.K / 4);
-    p.ws = reinterpret_cast<const float*>(a.w + tail);
-    p.ws2 = PAIR ? reinterpret_cast<const float*>(a.w2 + tail) : p.ws;
-    p.dots = a.dots;
-    p.y = a.y;
-    p.M = a.m;
-    p.N = a.n_rows;
-    p.K = a.K;
-    p.error = error;
+cudaError_t launch_skinny(const SkParams& P, int grid, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(i2s_gemm_skinny_kernel<PAIR, SK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::SMEM);
+                                         skinny_smem(PAIR));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((a.n_rows + kSkM - 1) / kSkM), 1, SK);
-    cfg.blockDim = dim3(kGmThreads);
-    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.gridDim = dim3((unsigned)grid, 1, SK);
+    cfg.blockDim = dim3(kSkThreads);
+    cfg.dynamicSmemBytes = skinny_smem(PAIR);
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -926,16 +1010,16 @@ cudaError_t launch_skinny(const GemmArgs& a, int* error, cudaStream_t st) {
         attr[1].val.clusterDim.z = SK;
         cfg.numAttrs = 2;
     }
-    return cudaLaunchKernelEx(&cfg, i2s_gemm_skinny_kernel<PAIR, SK>, tm_a, tm_w, tm_w2, p);
+    return cudaLaunchKernelEx(&cfg, i2s_gemm_skinny_kernel<PAIR, SK>, P);
 }
 
 template <bool PAIR>
-cudaError_t launch_skinny_split(const GemmArgs& a, int sk, int* error, cudaStream_t st) {
+cudaError_t launch_skinny_split(const SkParams& P, int grid, int sk, cudaStream_t st) {
     switch (sk) {
-        case 8: return launch_skinny<PAIR, 8>(a, error, st);
-        case 4: return launch_skinny<PAIR, 4>(a, error, st);
-        case 2: return launch_skinny<PAIR, 2>(a, error, st);
-        default: return launch_skinny<PAIR, 1>(a, error, st);
+        case 8: return launch_skinny<PAIR, 8>(P, grid, st);
+        case 4: return launch_skinny<PAIR, 4>(P, grid, st);
+        case 2: return launch_skinny<PAIR, 2>(P, grid, st);
+        default: return launch_skinny<PAIR, 1>(P, grid, st);
     }
 }
 
@@ -987,15 +1071,64 @@ int gemm_check(const GemmArgs& a, const char** why) {
 // projection at 512 tokens runs on 120 CTAs (23.0 us, against 25.0 us for
 // 128 x 128 tiles on 80 CTAs and 27.1 us for 256-row tiles on 120). Short
 // contractions take 128 rows x 128 tokens, unsplit.
-// The skinny form: one CTA per 128 weight rows, the contraction split over a
-// cluster of 2, 4 or 8 CTAs while that still fits the grid in one wave (and
-// leaves every CTA at least two k-steps).
-cudaError_t launch_i2s_gemm_skinny(const GemmArgs& a, int* error, cudaStream_t st) {
-    if (a.m < 1 || a.m > kSkN) return cudaErrorInvalidValue;
-    const int tiles = (a.n_rows + kSkM - 1) / kSkM, kb = a.K / kBK, sms = sm_count();
+// The skinny form over up to four segments. Tiles: ceil(rows / 128) per
+// tensor (64 for the pair). Two CTAs per SM are resident; with at least that
+// many tiles the grid is persistent over them, otherwise the contraction is
+// split over clusters of 2, 4 or 8 CTAs while that still fits (each CTA keeps
+// at least two k-steps).
+cudaError_t launch_i2s_gemm_skinny_segs(const SkinnySeg* segs, int nseg, const int8_t* q, int lda, int m, int K,
+                                        const sllm_cuda_act* acts, int* error, cudaStream_t st) {
+    if (nseg < 1 || nseg > kSkMaxSeg || m < 1 || m > kSkN || K < kBK || K % kBK != 0 || q == nullptr ||
+        acts == nullptr)
+        return cudaErrorInvalidValue;
+    const bool pair = segs[0].w2 != nullptr;
+    const int TR = pair ? 64 : kSkM;
+    SkParams P{};
+    int tiles = 0, cols = 0;
+    for (int i = 0; i < nseg; ++i) {
+        const SkinnySeg& sg = segs[i];
+        if ((sg.w2 != nullptr) != pair || sg.w == nullptr || sg.n_rows < 1 || sg.kx < 0 || sg.kx % 16 != 0 ||
+            (sg.dots == nullptr && sg.y == nullptr) || (pair && (sg.y == nullptr || sg.dots != nullptr)))
+            return cudaErrorInvalidValue;
+        if (!encode_2d(&P.w[i], sg.w, (uint64_t)(K / 4), (uint64_t)sg.n_rows, kSkG * kPK, TR,
+                       CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorInvalidValue;
+        if (pair && !encode_2d(&P.w2[i], sg.w2, (uint64_t)(K / 4), (uint64_t)sg.n_rows, kSkG * kPK, TR,
+                               CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorInvalidValue;
+        if (!pair) P.w2[i] = P.w[i];
+        tiles += (sg.n_rows + TR - 1) / TR;
+        P.tile_end[i] = tiles;
+        P.n_rows[i] = sg.n_rows;
+        P.kx[i] = sg.kx;
+        const size_t tail = (size_t)sg.n_rows * (size_t)(K / 4);
+        P.ws[i] = reinterpret_cast<const float*>(sg.w + tail);
+        P.ws2[i] = pair ? reinterpret_cast<const float*>(sg.w2 + tail) : P.ws[i];
+        P.dots[i] = sg.dots;
+        P.y[i] = sg.y;
+        cols = std::max(cols, sg.kx + K);
+    }
+    const int stride = lda > 0 ? lda : K;
+    if (cols > stride) return cudaErrorInvalidValue;
+    // the activation map spans exactly the columns the segments read
+    if (!encode_2d(&P.act, q, (uint64_t)cols, (uint64_t)m, kBK, kSkN, CU_TENSOR_MAP_SWIZZLE_128B, (uint64_t)stride))
+        return cudaErrorInvalidValue;
+    P.acts = acts;
+    P.error = error;
+    P.nseg = nseg;
+    P.tiles = tiles;
+    P.M = m;
+    P.K = K;
+    const int slots = 2 * sm_count(), kb = K / kBK;
     int sk = 1;
-    while (sk < 8 && tiles * sk * 2 <= sms && kb >= 2 * sk * 2) sk *= 2;
-    return a.w2 != nullptr ? launch_skinny_split<true>(a, sk, error, st) : launch_skinny_split<false>(a, sk, error, st);
+    while (sk < 8 && tiles * sk * 2 <= slots && kb >= 4 * sk) sk *= 2;
+    const int grid = sk > 1 ? tiles : std::min(tiles, slots);
+    return pair ? launch_skinny_split<true>(P, grid, sk, st) : launch_skinny_split<false>(P, grid, sk, st);
+}
+
+cudaError_t launch_i2s_gemm_skinny(const GemmArgs& a, int* error, cudaStream_t st) {
+    SkinnySeg sg{a.w, a.w2, a.n_rows, 0, a.w2 != nullptr ? nullptr : a.dots, a.y};
+    return launch_i2s_gemm_skinny_segs(&sg, 1, a.q, a.lda, a.m, a.K, a.acts, error, st);
 }
 
 int g_gemm_form = 0;     // test hook: 0 by size, 1 the 128-token tiles, 2 the skinny form

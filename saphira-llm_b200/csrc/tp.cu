@@ -2231,9 +2231,12 @@ cudaError_t enqueue_bphase(sllm_cuda_tp_batch* b, int ph, cudaStream_t st) {
         }
         // attn_norm -> local Q, K, V for every sequence (src/forward.c:631-666)
         e = launch_norm_quant_rows(b->x, t.attn_norm, E, m->eps, B, b->qa, b->act_a, fb, force, st);
-        if (e == cudaSuccess) e = bgemm(t.wq, nullptr, m->hq * D, E, b->qa, 0, b->act_a, B, nullptr, b->q, st);
-        if (e == cudaSuccess) e = bgemm(t.wk, nullptr, m->hk * D, E, b->qa, 0, b->act_a, B, nullptr, b->k, st);
-        if (e == cudaSuccess) e = bgemm(t.wv, nullptr, m->hk * D, E, b->qa, 0, b->act_a, B, nullptr, b->v, st);
+        if (e == cudaSuccess) {
+            const SkinnySeg segs[3] = {{t.wq, nullptr, m->hq * D, 0, nullptr, b->q},
+                                       {t.wk, nullptr, m->hk * D, 0, nullptr, b->k},
+                                       {t.wv, nullptr, m->hk * D, 0, nullptr, b->v}};
+            e = launch_i2s_gemm_skinny_segs(segs, 3, b->qa, 0, B, E, b->act_a, gemm_error_word(), st);
+        }
         if (e != cudaSuccess) return e;
         const size_t kv_layer = (size_t)m->hk * D * (size_t)b->n_ctx;
         AttnParams ap{};
@@ -2278,9 +2281,14 @@ cudaError_t enqueue_bphase(sllm_cuda_tp_batch* b, int ph, cudaStream_t st) {
                          m->f_loc);
     if (e == cudaSuccess)
         e = launch_norm_quant(b->h_full, t.ffn_sub_norm, m->F, m->eps, b->qh, b->act_h, fb, force, st, XWait{}, B);
-    for (int ch = 0; ch < m->down_c && e == cudaSuccess; ++ch)
-        e = bgemm(t.down[ch], nullptr, E, m->down_k, b->qh + (size_t)m->rank * m->f_loc + (size_t)ch * m->down_k,
-                  m->F, b->act_h, B, b->dots_d + (size_t)ch * B * E, nullptr, st);
+    if (e == cudaSuccess) {
+        // the column chunks of down as the segments of one launch
+        SkinnySeg segs[4];
+        for (int ch = 0; ch < m->down_c; ++ch)
+            segs[ch] = SkinnySeg{t.down[ch], nullptr, E, m->rank * m->f_loc + ch * m->down_k,
+                                 b->dots_d + (size_t)ch * B * E, nullptr};
+        e = launch_i2s_gemm_skinny_segs(segs, m->down_c, b->qh, m->F, B, m->down_k, b->act_h, gemm_error_word(), st);
+    }
     return e;
 }
 
@@ -2374,7 +2382,7 @@ extern "C" int sllm_cuda_tp_batch_new(const sllm_cuda_tp_model* m, sllm_cuda_tp_
     *out = nullptr;
     if (comm != nullptr && (comm->n_ranks != m->n_ranks || comm->rank != m->rank || comm->device != m->device))
         return fail(SLLM_CUDA_ERR_ARG, "tp_batch_new: the communicator's rank does not match the shard's");
-    if (m->E > 8192 || m->E % 128 != 0 || m->F % 32 != 0 || m->F > 32768)
+    if (m->E > 8192 || m->E % 128 != 0 || m->F % 32 != 0 || m->F > 32768 || m->down_c > 4)
         return fail(SLLM_CUDA_ERR_UNSUPPORTED, "tp_batch_new: widths %d / %d", m->E, m->F);
     CK(cudaSetDevice(m->device), "cudaSetDevice");
     CK(prepare_decode_kernels(), "decode kernel attributes");

@@ -119,10 +119,11 @@ def test_gemm_config3_sizes_match_per_token_gemv(cuda, orc, synth, rows, n):
 
 
 # (weight rows, K, tokens) of the skinny form (at most 16 tokens): one tile
-# and one token; ragged rows; the contraction split over clusters of 2, 4 and
-# 8 CTAs (64, 28 and 8 row tiles); the tensor-parallel widths of configs[4]
+# and one token; ragged rows; the contraction split over clusters of 2 and 8
+# CTAs; the tensor-parallel widths of configs[4]; more tiles than resident
+# CTAs (the persistent grid, two tiles for some CTAs)
 SKINNY = [(128, 128, 1), (200, 256, 5), (8192, 1024, 16), (640, 2560, 7), (1024, 8192, 16), (3584, 1024, 3),
-          (8192, 3584, 16)]
+          (8192, 3584, 16), (40000, 256, 16)]
 
 
 @pytest.fixture
@@ -153,7 +154,7 @@ def test_gemm_skinny_bit_exact(cuda, orc, synth, skinny, rows, n, m):
         assert np.array_equal(bits(yy[t]), bits(wy)), f"token {t}"
 
 
-@pytest.mark.parametrize("rows,n,m", [(256, 384, 16), (3584, 8192, 16), (384, 2560, 1)])
+@pytest.mark.parametrize("rows,n,m", [(256, 384, 16), (3584, 8192, 16), (384, 2560, 1), (20000, 256, 9)])
 def test_gemm_skinny_silu_bit_exact(cuda, orc, synth, skinny, rows, n, m):
     import torch
     rng = np.random.default_rng(rows * 3 + n + m)
