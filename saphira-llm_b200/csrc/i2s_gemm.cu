@@ -132,12 +132,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // bounded wait: false when the phase did not complete in time, or when the
 // CTA is aborting. The first check is inline: the single MMA-issuing thread
 // waits once per k-step, and an out-of-line call there cost ~0.1 us each.
-__device__ __noinline__ bool gm_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* error);
-__device__ __forceinline__ bool gm_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* error) {
+__device__ __noinline__ bool gm_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* error,
+                                         bool sleep);
+__device__ __forceinline__ bool gm_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* error,
+                                        bool sleep = false) {
     if (mbar_try_wait(bar, parity)) return true;
-    return gm_wait_slow(bar, parity, abort_flag, error);
+    return gm_wait_slow(bar, parity, abort_flag, error, sleep);
 }
-__device__ __noinline__ bool gm_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* error) {
+__device__ __noinline__ bool gm_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* error,
+                                         bool sleep) {
     const uint64_t t0 = gtimer();
     while (!mbar_try_wait(bar, parity)) {
         if (*abort_flag) return false;
@@ -146,8 +149,17 @@ __device__ __noinline__ bool gm_wait_slow(uint64_t* bar, uint32_t parity, volati
             atomicExch(error, GM_TIMEOUT);
             return false;
         }
+        // waits off the k-loop's critical path (the epilogue's, the
+        // producer's) poll less often
+        if (sleep) __nanosleep(32);
     }
     return true;
+}
+
+// a whole warp's wait, the same answer in every lane
+__device__ __forceinline__ bool gm_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* error,
+                                             bool sleep = false) {
+    return __all_sync(0xffffffffu, gm_wait(bar, parity, abort_flag, error, sleep));
 }
 
 // drain: wait for a phase that must complete (work already in flight);
@@ -310,7 +322,7 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
             for (int kb = 0; kb < KB; ++kb) {
                 const int s = kb % C::S;
                 const uint32_t use = (uint32_t)(kb / C::S);
-                if (use > 0 && !gm_wait(&bar_empty[s], (use - 1) & 1u, abort_v, p.error)) break;
+                if (use > 0 && !gm_wait(&bar_empty[s], (use - 1) & 1u, abort_v, p.error, true)) break;
                 mbar_expect_tx(&bar_loaded[s], (uint32_t)(mt_live * C::A_BYTES + C::NM * C::P_BYTES));
                 for (int mt = 0; mt < mt_live; ++mt)
                     tma_load_2d(A(s, mt), &tm_a, (kb0 + kb) * kBK, m0 + mt * kBM, &bar_loaded[s]);
@@ -363,7 +375,7 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
         for (int kb = 0; kb < KB && ok; ++kb) {
             const int s = kb % C::S;
             const uint32_t ph = (uint32_t)(kb / C::S) & 1u;
-            ok = gm_wait(&bar_loaded[s], ph, abort_v, p.error);
+            ok = gm_wait_warp(&bar_loaded[s], ph, abort_v, p.error);
             if (ok) {
                 // items: (matrix, half, row); eight consecutive threads take eight
                 // consecutive rows, so their 16-byte stores hit eight distinct
@@ -391,7 +403,7 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
             ok = __all_sync(0xffffffffu, ok);
         }
         // epilogue: warp group mt (warps 2-5: 0, warps 6-9: 1) takes token tile mt
-        ep_ok = __all_sync(0xffffffffu, ok && gm_wait(&bar_acc, 0u, abort_v, p.error)) &&
+        ep_ok = __all_sync(0xffffffffu, ok && gm_wait_warp(&bar_acc, 0u, abort_v, p.error, true)) &&
                 __all_sync(0xffffffffu, *abort_v == 0);
     }
     const int mt = (warp - 2) >> 2;
@@ -560,20 +572,20 @@ i2s_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
 constexpr int kSkM = 128;       // operand rows per tile (MMA M, TMEM lanes)
 constexpr int kSkN = 16;        // tokens (MMA N)
 constexpr int kSkMaxSeg = 4;
-constexpr int kSkSp = 3;        // packed stages
-constexpr int kSkSa = 2;        // operand stages
+constexpr int kSkSp = 4;        // packed stages in shared memory
+constexpr int kSkSa = 6;        // operand stages in tensor memory
 constexpr int kSkG = 4;         // k-steps per packed stage: 128-byte segments of every weight row
 constexpr int kSkPStage = kSkG * kSkN * kBK + kSkM * kSkG * kPK;    // 4 activation boxes + packed weights: 24 KB
-constexpr int kSkAStage = kSkM * kBK;                   // unpacked codes: 16 KB
-__host__ __device__ constexpr int skinny_packed_stages(bool) { return kSkSp; }
-__host__ __device__ constexpr int skinny_smem(bool pair) {
-    return kSkSa * kSkAStage + skinny_packed_stages(pair) * kSkPStage + 1024;
-}
+constexpr int kSkACols = kBK / 4;                       // TMEM columns of one operand stage (4 codes each)
+constexpr int kSkAcc = 2 * kSkN;                        // two accumulators of 16 columns at column 0
+constexpr int kSkTmemCols = 256;                        // accumulators + operand stages; two CTAs per SM
+__host__ __device__ constexpr int skinny_smem(bool) { return kSkSp * kSkPStage + 1024; }
 constexpr int kSkEpiWarp0 = 2 + kGmUnpackWarps;        // warps 10-13
 constexpr int kSkThreads = 32 * (kSkEpiWarp0 + 4);
-constexpr int kSkTmemCols = 32;                         // two accumulators of 16 columns
-static_assert(kSkPStage % 1024 == 0 && kSkAStage % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
-static_assert(kSkSa * kSkAStage >= kSkN * kSkM * 4, "a split CTA's partial sums fit the operand ring");
+static_assert(kSkPStage % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+static_assert(kSkAcc + kSkSa * kSkACols <= kSkTmemCols, "operand stages fit the allocation");
+static_assert(kGmUnpackWarps == 8, "two unpack warps per TMEM lane quarter, one half of each row");
+static_assert(kSkSp * kSkPStage >= kSkN * kSkM * 4, "a split CTA's partial sums fit the packed ring");
 
 struct SkParams {
     CUtensorMap act;                    // [m][cols] int8, box 128 x 16, 128-byte swizzle
@@ -603,11 +615,32 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 
 __device__ __forceinline__ void umma_commit_to(uint64_t* bar) { umma_commit(bar); }
 
+// the MMA with its A operand (M = 128 lanes x K = 32 int8, four per column)
+// in tensor memory
+__device__ __forceinline__ void umma_i8_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// four consecutive 32-bit columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(a), "r"(b), "r"(c),
+                 "r"(d)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 template <bool PAIR, int SK>
 __global__ void __launch_bounds__(kSkThreads, 2)
 i2s_gemm_skinny_kernel(const __grid_constant__ SkParams P) {
     constexpr int TR = PAIR ? 64 : 128;          // weight rows per tile (of each tensor)
-    constexpr int SP = skinny_packed_stages(PAIR);
+    constexpr int SP = kSkSp;
     extern __shared__ uint8_t gsm_raw[];
     __shared__ uint64_t bar_loaded[kSkSp], bar_pempty[kSkSp], bar_unpacked[kSkSa], bar_aempty[kSkSa];
     __shared__ uint64_t bar_full[2], bar_drained[2], bar_xfull, bar_xfree;
@@ -616,8 +649,7 @@ i2s_gemm_skinny_kernel(const __grid_constant__ SkParams P) {
     __shared__ float s_up[PAIR ? kSkN * 64 : 1];          // [token][64 rows]
     uint8_t* const gsm = gsm_raw + ((1024u - (smem_u32(gsm_raw) & 1023u)) & 1023u);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    auto A = [&](int sa) { return gsm + (size_t)sa * kSkAStage; };
-    auto PS = [&](int sp) { return gsm + (size_t)kSkSa * kSkAStage + (size_t)sp * kSkPStage; };
+    auto PS = [&](int sp) { return gsm + (size_t)sp * kSkPStage; };
     const int KB_all = P.K / kBK;
     const int kb0 = SK > 1 ? (int)((long long)blockIdx.z * KB_all / SK) : 0;
     const int KB = SK > 1 ? (int)((long long)(blockIdx.z + 1) * KB_all / SK) - kb0 : KB_all;   // >= 2
@@ -628,6 +660,12 @@ i2s_gemm_skinny_kernel(const __grid_constant__ SkParams P) {
         *row0 = (t - (sg > 0 ? P.tile_end[sg - 1] : 0)) * TR;
         return sg;
     };
+    // each tile walks its packed stages (groups of four k-steps) starting at
+    // group t % NG, so the CTAs running at one time read different columns of
+    // the shared activation matrix (it sits in a few L2 slices otherwise);
+    // the int32 sums do not depend on the order
+    const int NG = (KB + kSkG - 1) / kSkG;
+    auto group_of = [&](int t, int gi) { return (gi + t) % NG; };
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < SP; ++i) {
@@ -674,14 +712,14 @@ i2s_gemm_skinny_kernel(const __grid_constant__ SkParams P) {
             float* up = s_up;
             if (quarter >= 2) {
                 // up rows 0..63 of the tile are TMEM lanes 64..127
-                if (j >= 1 && !gm_wait(&bar_xfree, par ^ 1u, abort_v, P.error)) return false;
+                if (j >= 1 && !gm_wait_warp(&bar_xfree, par ^ 1u, abort_v, P.error, true)) return false;
                 #pragma unroll
                 for (int jj = 0; jj < kSkN; ++jj) up[jj * 64 + 32 * (quarter - 2) + lane] = __int_as_float((int)v[jj]);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bar_xfull);
                 return true;
             }
-            if (!gm_wait(&bar_xfull, par, abort_v, P.error)) return false;
+            if (!gm_wait_warp(&bar_xfull, par, abort_v, P.error, true)) return false;
             const int n = row0 + 32 * quarter + lane;
             if (n < P.n_rows[sg]) {
                 const float ws = __ldg(P.ws[sg]), ws2 = __ldg(P.ws2[sg]);
@@ -732,10 +770,11 @@ i2s_gemm_skinny_kernel(const __grid_constant__ SkParams P) {
             for (int t = t_first; t < P.tiles && ok; t += t_step) {
                 int row0;
                 const int sg = seg_of(t, &row0);
-                for (int kb = kb0; kb < kb0 + KB; kb += kSkG, ++gs) {
+                for (int gi = 0; gi < NG; ++gi, ++gs) {
+                    const int kb = kb0 + kSkG * group_of(t, gi);
                     const int sp = gs % SP;
                     const uint32_t use = (uint32_t)(gs / SP);
-                    if (use > 0 && !gm_wait(&bar_pempty[sp], (use - 1) & 1u, abort_v, P.error)) { ok = false; break; }
+                    if (use > 0 && !gm_wait(&bar_pempty[sp], (use - 1) & 1u, abort_v, P.error, true)) { ok = false; break; }
                     mbar_expect_tx(&bar_loaded[sp], (uint32_t)kSkPStage);
                     uint8_t* st = PS(sp);
                     #pragma unroll
@@ -760,19 +799,23 @@ i2s_gemm_skinny_kernel(const __grid_constant__ SkParams P) {
                 if (j >= 2 && !gm_wait(&bar_drained[buf], (uint32_t)((j >> 1) - 1) & 1u, abort_v, P.error)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(buf * kSkN);
-                for (int kb = 0; kb < KB; ++kb, ++gk) {
-                    const int sa = gk % kSkSa, sp = gs % SP, sub = kb % kSkG;
-                    if (!gm_wait(&bar_unpacked[sa], (uint32_t)(gk / kSkSa) & 1u, abort_v, P.error)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint32_t a0 = smem_u32(A(sa)), b0 = smem_u32(PS(sp) + sub * (kSkN * kBK));
-                    #pragma unroll
-                    for (int kk = 0; kk < kBK / 32; ++kk)
-                        umma_i8(d, umma_desc_sw128(a0 + 32u * kk), umma_desc_sw128(b0 + 32u * kk), idesc,
-                                (kb > 0 || kk > 0) ? 1u : 0u);
-                    umma_commit_to(&bar_aempty[sa]);
-                    if (sub == kSkG - 1 || kb == KB - 1) {      // the packed stage's last k-step
-                        umma_commit_to(&bar_pempty[sp]);
-                        ++gs;
+                for (int gi = 0; gi < NG && ok; ++gi) {
+                    const int g = group_of(t, gi), nk = min(kSkG, KB - kSkG * g);
+                    for (int sub = 0; sub < nk; ++sub, ++gk) {
+                        const int sa = gk % kSkSa, sp = gs % SP;
+                        if (!gm_wait(&bar_unpacked[sa], (uint32_t)(gk / kSkSa) & 1u, abort_v, P.error)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t a0 = tmem + (uint32_t)(kSkAcc + sa * kSkACols);
+                        const uint32_t b0 = smem_u32(PS(sp) + sub * (kSkN * kBK));
+                        #pragma unroll
+                        for (int kk = 0; kk < kBK / 32; ++kk)
+                            umma_i8_ta(d, a0 + 8u * kk, umma_desc_sw128(b0 + 32u * kk), idesc,
+                                       (gi > 0 || sub > 0 || kk > 0) ? 1u : 0u);
+                        umma_commit_to(&bar_aempty[sa]);
+                        if (sub == nk - 1) {      // the packed stage's last k-step
+                            umma_commit_to(&bar_pempty[sp]);
+                            ++gs;
+                        }
                     }
                 }
                 if (ok) umma_commit_to(&bar_full[buf]);
@@ -782,40 +825,45 @@ i2s_gemm_skinny_kernel(const __grid_constant__ SkParams P) {
         __syncwarp();
     } else if (warp < kSkEpiWarp0) {
         // ---------------- unpack (warps 2-9) ----------------
-        // one 16-byte item per thread and k-step: half h of the row's 32 packed
-        // bytes; a quarter warp takes rows r, r + 2, r + 4, r + 6 (both
-        // halves), so its eight 16-byte loads (128-byte swizzle) and each of
-        // its stores land on eight distinct chunks
-        const int tt = threadIdx.x - 64;
-        const int h = tt & 1, row = (tt >> 4) * 8 + ((tt >> 1) & 3) * 2 + ((tt >> 3) & 1);
-        const int prow_off = kSkG * kSkN * kBK + row * (kSkG * kPK);     // the row's 128 bytes in a packed stage
+        // warp w writes TMEM lanes 32 (w % 4) .. + 31 (rows of the tile), lane
+        // i row 32 (w % 4) + i; warps 2-5 take the first 16 packed bytes of
+        // each row, warps 6-9 the second. Packed word i, field f holds the
+        // codes of natural word 8 f + i of the k-step (elements 32 f + 4 i ..),
+        // so each field of the thread's four words is four consecutive
+        // operand columns: four 32x32b.x4 stores per k-step. The eight lanes
+        // of a quarter warp read eight consecutive rows' same logical chunk,
+        // eight distinct swizzled chunks.
+        const int row = 32 * (warp & 3) + lane, hh = (warp - 2) >> 2;
+        const uint32_t lane_addr = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
         int gk = 0, gs = 0;
         bool ok = true;
         for (int t = t_first; t < P.tiles && ok; t += t_step) {
-            for (int kb = 0; kb < KB; ++kb, ++gk) {
-                const int sp = gs % SP, sa = gk % kSkSa, sub = kb % kSkG;
-                if (sub == 0) ok = gm_wait(&bar_loaded[sp], (uint32_t)(gs / SP) & 1u, abort_v, P.error);
-                if (ok && gk >= kSkSa) ok = gm_wait(&bar_aempty[sa], (uint32_t)((gk / kSkSa) - 1) & 1u, abort_v, P.error);
-                if (ok) {
-                    const int chunk = (2 * sub + h) ^ (row & 7);
-                    const uint4 v = *reinterpret_cast<const uint4*>(PS(sp) + prow_off + (chunk << 4));
-                    uint8_t* arow = A(sa) + row * kBK;
-                    #pragma unroll
-                    for (int f = 0; f < 4; ++f) {
-                        uint4 o;
-                        o.x = field_codes(v.x, f);
-                        o.y = field_codes(v.y, f);
-                        o.z = field_codes(v.z, f);
-                        o.w = field_codes(v.w, f);
-                        *reinterpret_cast<uint4*>(arow + (((2 * f + h) ^ (row & 7)) << 4)) = o;
+            for (int gi = 0; gi < NG && ok; ++gi) {
+                const int g = group_of(t, gi), nk = min(kSkG, KB - kSkG * g);
+                for (int sub = 0; sub < nk; ++sub, ++gk) {
+                    const int sp = gs % SP, sa = gk % kSkSa;
+                    if (sub == 0) ok = gm_wait_warp(&bar_loaded[sp], (uint32_t)(gs / SP) & 1u, abort_v, P.error);
+                    if (ok && gk >= kSkSa)
+                        ok = gm_wait_warp(&bar_aempty[sa], (uint32_t)((gk / kSkSa) - 1) & 1u, abort_v, P.error);
+                    if (ok) {
+                        tc_fence_after();
+                        const int chunk = (2 * sub + hh) ^ (row & 7);
+                        const uint4 v = *reinterpret_cast<const uint4*>(PS(sp) + kSkG * kSkN * kBK +
+                                                                        row * (kSkG * kPK) + (chunk << 4));
+                        const uint32_t col = lane_addr + (uint32_t)(kSkAcc + sa * kSkACols + 4 * hh);
+                        #pragma unroll
+                        for (int f = 0; f < 4; ++f)
+                            tmem_st4(col + 8u * f, field_codes(v.x, f), field_codes(v.y, f), field_codes(v.z, f),
+                                     field_codes(v.w, f));
+                        tmem_st_wait();
+                        tc_fence_before();
                     }
-                    fence_proxy_async_smem();
+                    if (sub == nk - 1) ++gs;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bar_unpacked[sa]);
+                    ok = __all_sync(0xffffffffu, ok);
+                    if (!ok) break;
                 }
-                if (sub == kSkG - 1 || kb == KB - 1) ++gs;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bar_unpacked[sa]);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) break;
             }
         }
     } else {
@@ -825,7 +873,7 @@ i2s_gemm_skinny_kernel(const __grid_constant__ SkParams P) {
         bool ok = true;
         for (int t = t_first; t < P.tiles && ok; t += t_step, ++j) {
             const int buf = j & 1;
-            ok = __all_sync(0xffffffffu, gm_wait(&bar_full[buf], (uint32_t)(j >> 1) & 1u, abort_v, P.error));
+            ok = gm_wait_warp(&bar_full[buf], (uint32_t)(j >> 1) & 1u, abort_v, P.error, true);
             if (!ok) break;
             tc_fence_after();
             uint32_t v[16];
