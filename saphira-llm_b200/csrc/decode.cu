@@ -381,69 +381,92 @@ lm_head_batch_kernel(const LmBatchParams p) {
 
     const int sub = lane >> 2, j4 = lane & 3;
     const int nsteps = E >> 5;
-    const int ngroups = (p.V + 7) >> 3;
+    // R groups of eight rows per warp iteration: each lane's x loads (the
+    // shared-memory reads bound this kernel) serve R rows
+    constexpr int R = 2;
+    const int ngroups = (p.V + 8 * R - 1) / (8 * R);
     float bv[T];
     int bi[T];
     #pragma unroll
     for (int t = 0; t < T; ++t) { bv[t] = NAN; bi[t] = 0x7fffffff; }
     // U steps per iteration, the next iteration's weights loaded before this
     // one's FMAs (a row's loads are otherwise exposed once per iteration)
-    constexpr int U = 4;
+    constexpr int U = 1;
     for (int grp = cta * kLmWarps + warp; grp < ngroups; grp += ncta * kLmWarps) {
-        const int row = 8 * grp + sub;
-        const bool valid = row < p.V;
-        const uint8_t* wrow = reinterpret_cast<const uint8_t*>(p.embd + (size_t)(valid ? row : 0) * (size_t)E) + 16 * j4;
-        float a[T][8];
+        int rows[R];
+        bool valid[R];
+        const uint8_t* wrow[R];
         #pragma unroll
-        for (int t = 0; t < T; ++t)
+        for (int r = 0; r < R; ++r) {
+            rows[r] = 8 * (R * grp + r) + sub;
+            valid[r] = rows[r] < p.V;
+            wrow[r] = reinterpret_cast<const uint8_t*>(p.embd + (size_t)(valid[r] ? rows[r] : 0) * (size_t)E) + 16 * j4;
+        }
+        float a[R][T][8];
+        #pragma unroll
+        for (int r = 0; r < R; ++r)
             #pragma unroll
-            for (int l = 0; l < 8; ++l) a[t][l] = 0.0f;
-        uint4 nx[U];
+            for (int t = 0; t < T; ++t)
+                #pragma unroll
+                for (int l = 0; l < 8; ++l) a[r][t][l] = 0.0f;
+        uint4 nx[U][R];
         #pragma unroll
-        for (int u = 0; u < U; ++u) nx[u] = (u < nsteps) ? ld_stream_u128(wrow + 64 * u) : make_uint4(0, 0, 0, 0);
+        for (int u = 0; u < U; ++u)
+            #pragma unroll
+            for (int r = 0; r < R; ++r) nx[u][r] = (u < nsteps) ? ld_stream_u128(wrow[r] + 64 * u) : make_uint4(0, 0, 0, 0);
         for (int m0 = 0; m0 < nsteps; m0 += U) {
-            uint4 wv[U];
-            #pragma unroll
-            for (int u = 0; u < U; ++u) wv[u] = nx[u];
+            uint4 wv[U][R];
             #pragma unroll
             for (int u = 0; u < U; ++u)
-                nx[u] = (m0 + U + u < nsteps) ? ld_stream_u128(wrow + 64 * (m0 + U + u)) : make_uint4(0, 0, 0, 0);
+                #pragma unroll
+                for (int r = 0; r < R; ++r) wv[u][r] = nx[u][r];
+            #pragma unroll
+            for (int u = 0; u < U; ++u)
+                #pragma unroll
+                for (int r = 0; r < R; ++r)
+                    nx[u][r] = (m0 + U + u < nsteps) ? ld_stream_u128(wrow[r] + 64 * (m0 + U + u)) : make_uint4(0, 0, 0, 0);
             #pragma unroll
             for (int u = 0; u < U; ++u) {
                 if (m0 + u < nsteps) {
-                    const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u].x));
-                    const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u].y));
-                    const float2 w45 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u].z));
-                    const float2 w67 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u].w));
+                    float w[R][8];
+                    #pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u][r].x));
+                        const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u][r].y));
+                        const float2 w45 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u][r].z));
+                        const float2 w67 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u][r].w));
+                        w[r][0] = w01.x; w[r][1] = w01.y; w[r][2] = w23.x; w[r][3] = w23.y;
+                        w[r][4] = w45.x; w[r][5] = w45.y; w[r][6] = w67.x; w[r][7] = w67.y;
+                    }
                     #pragma unroll
                     for (int t = 0; t < T; ++t) {
                         const float4* xv = reinterpret_cast<const float4*>(xs + (size_t)t * E + 32 * (m0 + u) + 8 * j4);
                         const float4 x0 = xv[0], x1 = xv[1];
-                        a[t][0] = __fmaf_rn(w01.x, x0.x, a[t][0]);
-                        a[t][1] = __fmaf_rn(w01.y, x0.y, a[t][1]);
-                        a[t][2] = __fmaf_rn(w23.x, x0.z, a[t][2]);
-                        a[t][3] = __fmaf_rn(w23.y, x0.w, a[t][3]);
-                        a[t][4] = __fmaf_rn(w45.x, x1.x, a[t][4]);
-                        a[t][5] = __fmaf_rn(w45.y, x1.y, a[t][5]);
-                        a[t][6] = __fmaf_rn(w67.x, x1.z, a[t][6]);
-                        a[t][7] = __fmaf_rn(w67.y, x1.w, a[t][7]);
+                        const float xx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                        #pragma unroll
+                        for (int r = 0; r < R; ++r)
+                            #pragma unroll
+                            for (int l = 0; l < 8; ++l) a[r][t][l] = __fmaf_rn(w[r][l], xx[l], a[r][t][l]);
                     }
                 }
             }
         }
         #pragma unroll
-        for (int t = 0; t < T; ++t) {
-            // the reference's tree (src/ops.c:135-143), as lm_head_kernel
+        for (int r = 0; r < R; ++r) {
             #pragma unroll
-            for (int l = 0; l < 8; ++l) a[t][l] = __fadd_rn(a[t][l], __shfl_down_sync(0xffffffffu, a[t][l], 2));
-            #pragma unroll
-            for (int l = 0; l < 8; ++l) a[t][l] = __fadd_rn(a[t][l], __shfl_down_sync(0xffffffffu, a[t][l], 1));
-            const float q0 = __fadd_rn(a[t][0], a[t][4]), q1 = __fadd_rn(a[t][1], a[t][5]);
-            const float q2 = __fadd_rn(a[t][2], a[t][6]), q3 = __fadd_rn(a[t][3], a[t][7]);
-            const float logit = __fadd_rn(__fadd_rn(q0, q1), __fadd_rn(q2, q3));
-            if (j4 == 0 && valid && t < nt) {
-                p.logits[(size_t)(t0 + t) * p.V + row] = logit;
-                if (better(logit, row, bv[t], bi[t])) { bv[t] = logit; bi[t] = row; }
+            for (int t = 0; t < T; ++t) {
+                // the reference's tree (src/ops.c:135-143), as lm_head_kernel
+                #pragma unroll
+                for (int l = 0; l < 8; ++l) a[r][t][l] = __fadd_rn(a[r][t][l], __shfl_down_sync(0xffffffffu, a[r][t][l], 2));
+                #pragma unroll
+                for (int l = 0; l < 8; ++l) a[r][t][l] = __fadd_rn(a[r][t][l], __shfl_down_sync(0xffffffffu, a[r][t][l], 1));
+                const float q0 = __fadd_rn(a[r][t][0], a[r][t][4]), q1 = __fadd_rn(a[r][t][1], a[r][t][5]);
+                const float q2 = __fadd_rn(a[r][t][2], a[r][t][6]), q3 = __fadd_rn(a[r][t][3], a[r][t][7]);
+                const float logit = __fadd_rn(__fadd_rn(q0, q1), __fadd_rn(q2, q3));
+                if (j4 == 0 && valid[r] && t < nt) {
+                    p.logits[(size_t)(t0 + t) * p.V + rows[r]] = logit;
+                    if (better(logit, rows[r], bv[t], bi[t])) { bv[t] = logit; bi[t] = rows[r]; }
+                }
             }
         }
     }
