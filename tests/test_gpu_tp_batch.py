@@ -116,3 +116,63 @@ def test_batch16_config4_widths(cuda):
         assert np.array_equal(bits(b.last_logits(s)[1]), bits(lg)), f"sequence {s}"
     b.close()
     tm.close()
+
+
+def _nccl_batch_rank(rank, n, uid, prompts, n_new, q):
+    import importlib
+    import torch  # noqa: F401  (a process with torch keeps one NCCL copy)
+    try:
+        cuda = importlib.import_module("saphira-llm_b200")
+        comm = cuda.TpComm(uid, n, rank, rank)
+        sd = cuda.abi.TpSynthDesc(n_layer=2, n_embd=1024, n_ff=16384, n_head=8, n_head_kv=4, n_vocab=3001,
+                                  f_rms_eps=1e-5, rope_freq_base=500000.0, seed=1234)
+        tm = cuda.TpModel(n, rank, rank, synth=sd)
+        b = tm.batch(prompts.shape[0], 32, comm)
+        rc, toks = b.generate(prompts, n_new)
+        lg = [b.last_logits(s)[1] for s in range(prompts.shape[0])]
+        q.put((rank, rc, toks.tolist(), lg))
+        b.close()
+        tm.close()
+        comm.close()
+    except Exception as e:  # report, never hang the parent
+        q.put((rank, -999, repr(e), None))
+
+
+def test_batch_two_gpus_nccl_matches_one(cuda):
+    """Two processes, one GPU each, the exchanges NCCL collectives carrying
+    every sequence's rows: the one-GPU batch's tokens and logits."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("one GPU on this box: the NCCL batch exchange is covered by the multi-GPU bench")
+    sd = cuda.abi.TpSynthDesc(n_layer=2, n_embd=1024, n_ff=16384, n_head=8, n_head_kv=4, n_vocab=3001,
+                              f_rms_eps=1e-5, rope_freq_base=500000.0, seed=1234)
+    prompts = _prompts(12, 5, 6, sd.n_vocab)
+    one = cuda.TpModel(1, 0, 0, synth=sd)
+    b1 = one.batch(5, 32)
+    rc, t1 = b1.generate(prompts, 8)
+    assert rc == 0
+    l1 = [b1.last_logits(s)[1] for s in range(5)]
+    b1.close()
+    one.close()
+    uid = cuda.tp_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_nccl_batch_rank, args=(r, 2, uid, prompts, 8, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            rank, rc, toks, lg = q.get(timeout=300)
+            res[rank] = (rc, toks, lg)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert all(res[r][0] == 0 for r in range(2)), res
+    assert res[0][1] == res[1][1] == t1.tolist()
+    for s in range(5):
+        lg = np.concatenate([res[r][2][s] for r in range(2)])
+        assert np.array_equal(bits(lg), bits(l1[s])), f"sequence {s}"
