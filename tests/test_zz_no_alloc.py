@@ -55,3 +55,26 @@ def test_noalloc_chain_refuses_a_model_beyond_its_scratch(cuda, synth):
     rc = fn(model.h, 0, 1, xd.data_ptr(), None)
     assert rc == -36                                     # SLLM_ERR_TOO_LARGE
     assert b"scratch" in cuda.lib().sllm_cuda_last_error()
+
+
+def test_noalloc_chain_with_the_reference_order_fallback_forced(cuda, synth):
+    """The forced reference-order RMSNorm sums (the rare ambiguous case of
+    the certified sum) reach this entry point too, and give the bits of the
+    context chain under the same switch."""
+    import torch
+    fn = _noalloc(cuda)
+    cfg = synth.Config(n_layer=2, n_vocab=256)
+    m = synth.SynthModel(cfg, seed=92)
+    model = cuda.Model(m.desc())
+    ctx = model.ctx(8)
+    x = np.random.default_rng(92).standard_normal(cfg.n_embd).astype(np.float32)
+    cuda.set_force_fallback(True)
+    try:
+        want = ctx.layer_chain(0, 2, x)
+        xd = torch.from_numpy(x).cuda()
+        rc = fn(model.h, 0, 2, xd.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, cuda.lib().sllm_cuda_last_error()
+        torch.cuda.synchronize()
+    finally:
+        cuda.set_force_fallback(False)
+    assert np.array_equal(bits(xd.cpu().numpy()), bits(want))
