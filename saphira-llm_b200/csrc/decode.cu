@@ -126,8 +126,9 @@ attention_kernel(const AttnParams p) {
     attention_head<kAttnThreads>(p, blockIdx.x, threadIdx.x, sc, qs, kcur, fred, dred, CtaSync());
 }
 
-// every (head, token) of a chunk whose K and V are already in the cache
-__global__ void __launch_bounds__(kAttnThreads)
+// every (head, token) of a chunk whose K and V are already in the cache;
+// two CTAs per SM (128 registers): a batch step launches 1024 of them
+__global__ void __launch_bounds__(kAttnThreads, 2)
 attention_chunk_kernel(const AttnParams p, const int32_t* __restrict__ pos_arr, int E, int G, size_t seq_stride) {
     extern __shared__ __align__(16) float sc[];
     __shared__ float qs[kHeadDim], kcur[kHeadDim];
