@@ -186,6 +186,12 @@ __device__ __forceinline__ void x_st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// system-scope release fence: orders this CTA's stores (into peers' memory
+// too; the CTA barrier before it makes them this thread's) before its next
+// release. acq_rel, not the sequentially consistent fence.sc.sys of
+// __threadfence_system, which also waits for a global ordering point.
+__device__ __forceinline__ void x_fence_release_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 __device__ __forceinline__ unsigned x_atom_add_acq_rel(unsigned* p, unsigned v) {
     unsigned old;
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
@@ -792,12 +798,12 @@ i2s_engine_kernel(const EngParams P) {
         // publish this CTA's outputs of the stage, then arrive
         consumer_sync();
         if (XCH && tid == 0 && s < kEngMaxXStages && (P.x.xs[s] & kXsFence) != 0)
-            __threadfence_system();     // the stores into peers' regions, before the arrival that orders them
+            x_fence_release_sys();      // the stores into peers' regions, before the arrival that orders them
         if (tid == 0 && s + 1 < P.n_stages && !(s == 0 && c == skip_arrival)) red_release_add(P.barrier, 1u);
     }
     if (XCH && P.x.end_kind >= 0 && tid == 0) {
         // the last CTA to finish publishes the kernel's exchange
-        __threadfence_system();
+        x_fence_release_sys();
         if (x_atom_add_acq_rel(P.x.done, 1u) == (unsigned)G - 1u) {
             x_signal(P.x, P.x.end_kind, xval);
             atomicExch(P.x.done, 0u);

@@ -176,3 +176,32 @@ def test_batch_two_gpus_nccl_matches_one(cuda):
     for s in range(5):
         lg = np.concatenate([res[r][2][s] for r in range(2)])
         assert np.array_equal(bits(lg), bits(l1[s])), f"sequence {s}"
+
+
+def test_batch_group_eight_ranks_config4_widths(cuda):
+    """Eight ranks of the configs[4] layer geometry (one kv head, 1024 O
+    columns, 3584 FFN rows and one down chunk per rank: the shapes of the
+    eight-GPU run), batch 16, on one GPU: TP = 1's tokens and logits."""
+    sd = cuda.abi.TpSynthDesc(n_layer=2, n_embd=8192, n_ff=28672, n_head=64, n_head_kv=8, n_vocab=3001,
+                              f_rms_eps=1e-5, rope_freq_base=500000.0, seed=99)
+    prompts = _prompts(13, 16, 5, sd.n_vocab)
+    one = cuda.TpModel(1, 0, 0, synth=sd)
+    b1 = one.batch(16, 32)
+    rc, t1 = b1.generate(prompts, 6)
+    assert rc == 0
+    l1 = [b1.last_logits(s)[1] for s in range(16)]
+    b1.close()
+    one.close()
+    shards = [cuda.TpModel(8, r, 0, synth=sd) for r in range(8)]
+    bs = [s.batch(16, 32) for s in shards]
+    rc, t = cuda.tp_batch_generate_group(bs, prompts, 6)
+    assert rc == 0
+    assert cuda.gemm_error() == 0
+    assert t.tolist() == t1.tolist()
+    for s in range(16):
+        lg = np.concatenate([b.last_logits(s)[1] for b in bs])
+        assert np.array_equal(bits(lg), bits(l1[s])), f"sequence {s}"
+    for b in bs:
+        b.close()
+    for s in shards:
+        s.close()
