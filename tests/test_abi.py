@@ -65,6 +65,11 @@ def test_argument_errors_need_no_device(built, synth):
     assert b"generate_greedy" in L.sllm_cuda_last_error()
     assert L.sllm_cuda_i2s_gemv(1024, 10, 200, 2048, 4096, None) == -1
     assert b"multiple of 128" in L.sllm_cuda_last_error()
+    # the batch decode API: no shard, too many sequences, no batch
+    assert L.sllm_cuda_tp_batch_new(None, None, 16, 64, C.byref(vp)) == -1
+    assert L.sllm_cuda_tp_batch_new(None, None, 17, 64, C.byref(vp)) == -1
+    assert L.sllm_cuda_tp_batch_generate_greedy(None, None, 4, 4, None) == -1
+    assert L.sllm_cuda_tp_batch_last_logits(None, 0, None) == -1
 
 
 def test_unsupported_shapes_are_refused(built, synth):
