@@ -348,6 +348,127 @@ tp_norm_quant_cluster_kernel(const float* __restrict__ x, const float* __restric
     cl.sync();      // no CTA leaves while rank 0 may still read its shared memory
 }
 
+// The batch form of the whole-row norm + quantisation, one cluster per row
+// of a [rows][K] batch (the h rows before down), reading the row as it is
+// or, after an all-gather, straight from the gather's rank-major layout
+// x[b][j] = g[(j / c) B c + b c + j % c] while also writing the whole row to
+// out, so the unshard copy is not a launch of its own. The reference-order
+// fallback reads the row back from out after a cluster barrier (every CTA's
+// slice written). (Folding the O and down epilogues in as well measured
+// slower at 8192-wide rows than the separate epilogue and one-CTA norm.)
+enum RowSrcMode { RS_ROWS = 0, RS_GATHER = 2 };
+
+struct RowSrc {
+    const float* x;                 // RS_ROWS: [rows][K]
+    const float* g;                 // RS_GATHER: [N][rows][c]
+    int c;
+    int rows;
+    float* out;                     // RS_GATHER: [rows][K]
+};
+
+template <int MODE>
+__global__ void __cluster_dims__(kNqCluster, 1, 1) __launch_bounds__(kNqThreads)
+tp_rows_norm_quant_kernel(const RowSrc src, const float* __restrict__ w, int K, float eps, double inv_k,
+                          int8_t* __restrict__ q, sllm_cuda_act* act, int* fb, int force) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    __shared__ double dred[32];
+    __shared__ float fred[32];
+    __shared__ int ired[32];
+    __shared__ double c_ss;
+    __shared__ float c_amax;
+    __shared__ int c_sum;
+    __shared__ float s_bcast;
+    const int rank = (int)cl.block_rank();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int row = blockIdx.x / kNqCluster;
+    q += (size_t)row * K;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int per = (K >> 2) / kNqCluster;                 // float4 per CTA
+    const int i = rank * per + tid;
+    const bool live = tid < per;
+    float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* xrow = MODE == RS_ROWS ? src.x + (size_t)row * K : src.out + (size_t)row * K;
+    if (MODE == RS_ROWS) {
+        if (live) xv = reinterpret_cast<const float4*>(xrow)[i];
+    } else if (live) {
+        // element j = 4 i of the row lies in rank j / c's slice (c % 4 == 0)
+        const int j = 4 * i, r = j / src.c, jj = j - r * src.c;
+        xv = *reinterpret_cast<const float4*>(src.g + ((size_t)r * src.rows + row) * src.c + jj);
+        *reinterpret_cast<float4*>(src.out + (size_t)row * K + j) = xv;
+    }
+    double ss = __dadd_rn(__dadd_rn((double)__fmul_rn(xv.x, xv.x), (double)__fmul_rn(xv.y, xv.y)),
+                          __dadd_rn((double)__fmul_rn(xv.z, xv.z), (double)__fmul_rn(xv.w, xv.w)));
+    ss = warp_sum_d(ss);
+    if (lane == 0) dred[warp] = ss;
+    __syncthreads();
+    if (tid == 0) {
+        double S = 0.0;
+        for (int k = 0; k < kNqThreads / 32; ++k) S = __dadd_rn(S, dred[k]);
+        c_ss = S;
+    }
+    cl.sync();      // also: every CTA's slice of out is written
+    if (tid == 0) {
+        double S = 0.0;
+        for (int r = 0; r < kNqCluster; ++r) S = __dadd_rn(S, *cl.map_shared_rank(&c_ss, r));
+        float mean;
+        if (!certify_mean_mul(S, K, inv_k, &mean) || force) {
+            mean = __double2float_rn(__ddiv_rn(rms_ss_reference_order(xrow, K), (double)K));
+            if (fb != nullptr && rank == 0) atomicAdd(fb, 1);
+        }
+        s_bcast = rms_scale(mean, eps);
+    }
+    __syncthreads();
+    const float sc = s_bcast;
+    const float4 wv = live ? __ldg(reinterpret_cast<const float4*>(w) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    xv.x = __fmul_rn(__fmul_rn(sc, xv.x), wv.x);
+    xv.y = __fmul_rn(__fmul_rn(sc, xv.y), wv.y);
+    xv.z = __fmul_rn(__fmul_rn(sc, xv.z), wv.z);
+    xv.w = __fmul_rn(__fmul_rn(sc, xv.w), wv.w);
+    float amax = fmaxf(fmaxf(fabsf(xv.x), fabsf(xv.y)), fmaxf(fabsf(xv.z), fabsf(xv.w)));
+    amax = warp_max(amax);
+    if (lane == 0) fred[warp] = amax;
+    __syncthreads();
+    if (tid == 0) {
+        float m = 0.0f;
+        for (int k = 0; k < kNqThreads / 32; ++k) m = fmaxf(m, fred[k]);
+        c_amax = m;
+    }
+    cl.sync();
+    if (tid == 0) {
+        float m = 0.0f;
+        for (int r = 0; r < kNqCluster; ++r) m = fmaxf(m, *cl.map_shared_rank(&c_amax, r));
+        s_bcast = quant_scale(m);
+    }
+    __syncthreads();
+    const float s = s_bcast;
+    int sum = 0;
+    if (live) {
+        const int a = quant_one(xv.x, s), b = quant_one(xv.y, s);
+        const int c = quant_one(xv.z, s), d = quant_one(xv.w, s);
+        sum = (a + b) + (c + d);
+        reinterpret_cast<uint32_t*>(q)[i] = (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) |
+                                            ((uint32_t)(c & 0xff) << 16) | ((uint32_t)d << 24);
+    }
+    sum = __reduce_add_sync(0xffffffffu, sum);
+    if (lane == 0) ired[warp] = sum;
+    __syncthreads();
+    if (tid == 0) {
+        int t = 0;
+        for (int k = 0; k < kNqThreads / 32; ++k) t += ired[k];
+        c_sum = t;
+    }
+    cl.sync();
+    if (rank == 0 && tid == 0) {
+        int total = 0;
+        for (int r = 0; r < kNqCluster; ++r) total += *cl.map_shared_rank(&c_sum, r);
+        act[row].scale = s;
+        act[row].sum = total;
+    }
+    cl.sync();      // no CTA leaves while rank 0 may still read its shared memory
+}
+
 // y[r] = (float)(sum over chunks of dots - act.sum) * (ws / act.scale) + resid[r]
 // (src/forward.c:739-750, 790-801)
 __global__ void tp_epilogue_kernel(const int32_t* __restrict__ dots, int n_chunks, int rows, const sllm_cuda_act* act,
@@ -2189,6 +2310,18 @@ cudaError_t bgemm(const uint8_t* w, const uint8_t* w2, int rows, int K, const in
     return launch_i2s_gemm_skinny(a, gemm_error_word(), st);
 }
 
+template <int MODE>
+cudaError_t launch_rows_norm_quant(const RowSrc& src, const float* w, int K, float eps, int8_t* q, sllm_cuda_act* act,
+                                   int* fb, int force, cudaStream_t st) {
+    if (K % (4 * kNqCluster) != 0 || K > 4 * kNqCluster * kNqThreads || src.rows < 1) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = pdl_config(kNqCluster * src.rows, kNqThreads, st);
+    cudaLaunchAttribute attr = pdl_attribute();
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tp_rows_norm_quant_kernel<MODE>, src, w, K, eps, 1.0 / (double)K, q, act, fb,
+                              force);
+}
+
 // phases as the single-sequence step's (n_phases, phase_xchg), B rows each
 cudaError_t enqueue_bphase(sllm_cuda_tp_batch* b, int ph, cudaStream_t st) {
     const sllm_cuda_tp_model* m = b->m;
@@ -2223,6 +2356,8 @@ cudaError_t enqueue_bphase(sllm_cuda_tp_batch* b, int ph, cudaStream_t st) {
     const int l = (ph - 1) / 4, sub = (ph - 1) % 4;
     const TpLayer& t = m->layers[l];
     cudaError_t e = cudaSuccess;
+    RowSrc rs{};
+    rs.rows = B;
     if (sub == 0) {
         if (l > 0) {
             const TpLayer& tp = m->layers[l - 1];
@@ -2276,11 +2411,13 @@ cudaError_t enqueue_bphase(sllm_cuda_tp_batch* b, int ph, cudaStream_t st) {
     }
     // ffn_sub_norm + quantisation of all of h, this rank's columns of down,
     // chunk by chunk (src/forward.c:781-792)
-    if (N > 1)
-        e = launch_pdl_k(tp_unshard_kernel, dim3(148), dim3(256), st, (const float*)b->gather, b->h_full, N, B,
-                         m->f_loc);
-    if (e == cudaSuccess)
-        e = launch_norm_quant(b->h_full, t.ffn_sub_norm, m->F, m->eps, b->qh, b->act_h, fb, force, st, XWait{}, B);
+    if (N > 1) {
+        rs.g = b->gather; rs.c = m->f_loc; rs.out = b->h_full;
+        e = launch_rows_norm_quant<RS_GATHER>(rs, t.ffn_sub_norm, m->F, m->eps, b->qh, b->act_h, fb, force, st);
+    } else {
+        rs.x = b->h_full;
+        e = launch_rows_norm_quant<RS_ROWS>(rs, t.ffn_sub_norm, m->F, m->eps, b->qh, b->act_h, fb, force, st);
+    }
     if (e == cudaSuccess) {
         // the column chunks of down as the segments of one launch
         SkinnySeg segs[4];
