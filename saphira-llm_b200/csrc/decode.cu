@@ -549,12 +549,12 @@ cudaError_t launch_attention(const AttnParams& p, int n_head, cudaStream_t st) {
 
 cudaError_t launch_embed_rows(const uint16_t* tok_embd, const int32_t* tok_seq, int n, int E, int V, float* x,
                               cudaStream_t st) {
-    return launch_pdl(embed_rows_kernel, dim3(n), dim3(256), 0, st, false, tok_embd, tok_seq, E, V, x);
+    return launch_pdl(embed_rows_kernel, dim3(n), dim3(256), 0, st, true, tok_embd, tok_seq, E, V, x);
 }
 
 cudaError_t launch_chunk_kv_store(const AttnParams& p, const int32_t* pos, int n, int n_head_kv, int E, int G,
                                   cudaStream_t st, size_t seq_stride) {
-    return launch_pdl(chunk_kv_store_kernel, dim3(n, n_head_kv), dim3(kHeadDim), 0, st, false, p, pos, E, G,
+    return launch_pdl(chunk_kv_store_kernel, dim3(n, n_head_kv), dim3(kHeadDim), 0, st, true, p, pos, E, G,
                       seq_stride);
 }
 
@@ -564,13 +564,13 @@ cudaError_t launch_attention_chunk(const AttnParams& p, const int32_t* pos, int 
     cudaError_t e = cudaFuncSetAttribute(attention_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          attention_max_ctx() * (int)sizeof(float));
     if (e != cudaSuccess) return e;
-    return launch_pdl(attention_chunk_kernel, dim3(n_head, n), dim3(kAttnThreads), smem, st, false, p, pos, E, G,
+    return launch_pdl(attention_chunk_kernel, dim3(n_head, n), dim3(kAttnThreads), smem, st, true, p, pos, E, G,
                       seq_stride);
 }
 
 cudaError_t launch_add(const float* a, const float* b, float* out, size_t n, cudaStream_t st) {
     const int grid = (int)std::min<size_t>((n + 255) / 256, 1184);
-    return launch_pdl(add_kernel, dim3(grid), dim3(256), 0, st, false, a, b, out, n);
+    return launch_pdl(add_kernel, dim3(grid), dim3(256), 0, st, true, a, b, out, n);
 }
 
 int lm_head_grid(int num_sms) { return 2 * num_sms; }

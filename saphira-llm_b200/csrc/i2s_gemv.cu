@@ -328,6 +328,11 @@ norm_quant_rows_kernel(const GemvParams p, int8_t* q, sllm_cuda_act* acts) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ ProSmem ps;
     const int K = p.K;
+    // launched with programmatic stream serialisation: the next launch (a
+    // GEMM, which waits for this one after its set-up) may be scheduled now,
+    // and x may come from the previous launch
+    pdl_trigger();
+    pdl_wait();
     int8_t* qs = reinterpret_cast<int8_t*>(smem);
     float* xs = reinterpret_cast<float*>(smem + K);
     GemvParams pr = p;
@@ -501,13 +506,22 @@ cudaError_t launch_norm_quant_rows(const float* x, const float* w, int K, float 
     p.force_fallback = force;
     const int kpt = (K / 4 + kGemvThreads - 1) / kGemvThreads;    // 1..4
     const size_t smem = (size_t)K * 5;                              // qs, then the fallback's floats
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rows);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     switch (kpt) {
-        case 1: norm_quant_rows_kernel<1><<<rows, kGemvThreads, smem, st>>>(p, q, acts); break;
-        case 2: norm_quant_rows_kernel<2><<<rows, kGemvThreads, smem, st>>>(p, q, acts); break;
-        case 3: norm_quant_rows_kernel<3><<<rows, kGemvThreads, smem, st>>>(p, q, acts); break;
-        default: norm_quant_rows_kernel<4><<<rows, kGemvThreads, smem, st>>>(p, q, acts); break;
+        case 1: return cudaLaunchKernelEx(&cfg, norm_quant_rows_kernel<1>, p, q, acts);
+        case 2: return cudaLaunchKernelEx(&cfg, norm_quant_rows_kernel<2>, p, q, acts);
+        case 3: return cudaLaunchKernelEx(&cfg, norm_quant_rows_kernel<3>, p, q, acts);
+        default: return cudaLaunchKernelEx(&cfg, norm_quant_rows_kernel<4>, p, q, acts);
     }
-    return cudaGetLastError();
 }
 
 cudaError_t launch_quant_act(const float* x, int n, int8_t* q, sllm_cuda_act* act, cudaStream_t st) {
