@@ -349,17 +349,16 @@ tp_norm_quant_cluster_kernel(const float* __restrict__ x, const float* __restric
 }
 
 // The batch form of the whole-row norm + quantisation, one cluster per row
-// of a [rows][K] batch (the h rows before down), reading the row as it is
-// or, after an all-gather, straight from the gather's rank-major layout
+// of a [rows][K] batch (the h rows before down) after an all-gather, reading
+// the row straight from the gather's rank-major layout
 // x[b][j] = g[(j / c) B c + b c + j % c] while also writing the whole row to
 // out, so the unshard copy is not a launch of its own. The reference-order
 // fallback reads the row back from out after a cluster barrier (every CTA's
 // slice written). (Folding the O and down epilogues in as well measured
 // slower at 8192-wide rows than the separate epilogue and one-CTA norm.)
-enum RowSrcMode { RS_ROWS = 0, RS_GATHER = 2 };
+enum RowSrcMode { RS_GATHER = 2 };
 
 struct RowSrc {
-    const float* x;                 // RS_ROWS: [rows][K]
     const float* g;                 // RS_GATHER: [N][rows][c]
     int c;
     int rows;
@@ -389,10 +388,8 @@ tp_rows_norm_quant_kernel(const RowSrc src, const float* __restrict__ w, int K, 
     const int i = rank * per + tid;
     const bool live = tid < per;
     float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);
-    const float* xrow = MODE == RS_ROWS ? src.x + (size_t)row * K : src.out + (size_t)row * K;
-    if (MODE == RS_ROWS) {
-        if (live) xv = reinterpret_cast<const float4*>(xrow)[i];
-    } else if (live) {
+    const float* xrow = src.out + (size_t)row * K;
+    if (live) {
         // element j = 4 i of the row lies in rank j / c's slice (c % 4 == 0)
         const int j = 4 * i, r = j / src.c, jj = j - r * src.c;
         xv = *reinterpret_cast<const float4*>(src.g + ((size_t)r * src.rows + row) * src.c + jj);
@@ -2415,8 +2412,7 @@ cudaError_t enqueue_bphase(sllm_cuda_tp_batch* b, int ph, cudaStream_t st) {
         rs.g = b->gather; rs.c = m->f_loc; rs.out = b->h_full;
         e = launch_rows_norm_quant<RS_GATHER>(rs, t.ffn_sub_norm, m->F, m->eps, b->qh, b->act_h, fb, force, st);
     } else {
-        rs.x = b->h_full;
-        e = launch_rows_norm_quant<RS_ROWS>(rs, t.ffn_sub_norm, m->F, m->eps, b->qh, b->act_h, fb, force, st);
+        e = launch_norm_quant(b->h_full, t.ffn_sub_norm, m->F, m->eps, b->qh, b->act_h, fb, force, st, XWait{}, B);
     }
     if (e == cudaSuccess) {
         // the column chunks of down as the segments of one launch
