@@ -334,11 +334,32 @@ lm_head_kernel(const LmParams p) {
 // caller's, as for a tensor-parallel slice above).
 // ---------------------------------------------------------------------------
 constexpr int kLmbTokens = 4;
+constexpr int kLmbRows = 2;         // R: groups of eight rows a warp takes per iteration
 
+// the weight ring of lm_head_batch_kernel: D steps x R rows x one 16-byte slot
+// per thread, behind the T x E floats of normalised activations
+__host__ __device__ constexpr size_t lm_head_batch_smem(int E, int D) {
+    return (size_t)kLmbTokens * (size_t)E * sizeof(float) + (size_t)D * kLmbRows * kLmThreads * 16u;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+                 "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// D: depth of the weight ring. Each thread copies its own 16-byte pieces of
+// the table into its own slots (cp.async) and reads them back after its own
+// wait, so no other thread is involved; D - 1 steps of copies stay in flight
+// per thread without holding registers (a register prefetch of one step left
+// the kernel waiting on the table's latency).
+template <int D>
 __global__ void __launch_bounds__(kLmThreads)
 lm_head_batch_kernel(const LmBatchParams p) {
     constexpr int T = kLmbTokens;
-    extern __shared__ __align__(16) float xs[];                 // T x E floats
+    extern __shared__ __align__(16) float xs[];                 // T x E floats, then the weight ring
     __shared__ double dred[32];
     __shared__ float s_scale;
     __shared__ float bv_s[T][kLmWarps];
@@ -382,17 +403,14 @@ lm_head_batch_kernel(const LmBatchParams p) {
 
     const int sub = lane >> 2, j4 = lane & 3;
     const int nsteps = E >> 5;
-    // R groups of eight rows per warp iteration: each lane's x loads (the
-    // shared-memory reads bound this kernel) serve R rows
-    constexpr int R = 2;
+    // R groups of eight rows per warp iteration: each lane's x loads serve R rows
+    constexpr int R = kLmbRows;
+    uint4* ring = reinterpret_cast<uint4*>(xs + (size_t)T * E) + tid;   // slot (d, r): ring[(d R + r) kLmThreads]
     const int ngroups = (p.V + 8 * R - 1) / (8 * R);
     float bv[T];
     int bi[T];
     #pragma unroll
     for (int t = 0; t < T; ++t) { bv[t] = NAN; bi[t] = 0x7fffffff; }
-    // U steps per iteration, the next iteration's weights loaded before this
-    // one's FMAs (a row's loads are otherwise exposed once per iteration)
-    constexpr int U = 1;
     for (int grp = cta * kLmWarps + warp; grp < ngroups; grp += ncta * kLmWarps) {
         int rows[R];
         bool valid[R];
@@ -410,46 +428,47 @@ lm_head_batch_kernel(const LmBatchParams p) {
             for (int t = 0; t < T; ++t)
                 #pragma unroll
                 for (int l = 0; l < 8; ++l) a[r][t][l] = 0.0f;
-        uint4 nx[U][R];
+        // steps 0 .. D-2 in flight; one commit group per step (empty past the row's end)
         #pragma unroll
-        for (int u = 0; u < U; ++u)
-            #pragma unroll
-            for (int r = 0; r < R; ++r) nx[u][r] = (u < nsteps) ? ld_stream_u128(wrow[r] + 64 * u) : make_uint4(0, 0, 0, 0);
-        for (int m0 = 0; m0 < nsteps; m0 += U) {
-            uint4 wv[U][R];
-            #pragma unroll
-            for (int u = 0; u < U; ++u)
+        for (int m = 0; m < D - 1; ++m) {
+            if (m < nsteps) {
                 #pragma unroll
-                for (int r = 0; r < R; ++r) wv[u][r] = nx[u][r];
+                for (int r = 0; r < R; ++r) cp_async16(ring + (m * R + r) * kLmThreads, wrow[r] + 64 * m);
+            }
+            cp_async_commit();
+        }
+        for (int m0 = 0; m0 < nsteps; ++m0) {
+            // the slot of step m0 + D - 1 last held step m0 - 1, whose reads
+            // this thread finished before its FMAs of the previous iteration
+            const int mf = m0 + D - 1;
+            if (mf < nsteps) {
+                const int sf = mf % D;
+                #pragma unroll
+                for (int r = 0; r < R; ++r) cp_async16(ring + (sf * R + r) * kLmThreads, wrow[r] + 64 * mf);
+            }
+            cp_async_commit();
+            cp_async_wait<D - 1>();         // step m0's group is complete
+            const int sc = m0 % D;
+            float w[R][8];
             #pragma unroll
-            for (int u = 0; u < U; ++u)
+            for (int r = 0; r < R; ++r) {
+                const uint4 wv = ring[(sc * R + r) * kLmThreads];
+                const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+                const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+                const float2 w45 = __half22float2(*reinterpret_cast<const __half2*>(&wv.z));
+                const float2 w67 = __half22float2(*reinterpret_cast<const __half2*>(&wv.w));
+                w[r][0] = w01.x; w[r][1] = w01.y; w[r][2] = w23.x; w[r][3] = w23.y;
+                w[r][4] = w45.x; w[r][5] = w45.y; w[r][6] = w67.x; w[r][7] = w67.y;
+            }
+            #pragma unroll
+            for (int t = 0; t < T; ++t) {
+                const float4* xv = reinterpret_cast<const float4*>(xs + (size_t)t * E + 32 * m0 + 8 * j4);
+                const float4 x0 = xv[0], x1 = xv[1];
+                const float xx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
                 #pragma unroll
                 for (int r = 0; r < R; ++r)
-                    nx[u][r] = (m0 + U + u < nsteps) ? ld_stream_u128(wrow[r] + 64 * (m0 + U + u)) : make_uint4(0, 0, 0, 0);
-            #pragma unroll
-            for (int u = 0; u < U; ++u) {
-                if (m0 + u < nsteps) {
-                    float w[R][8];
                     #pragma unroll
-                    for (int r = 0; r < R; ++r) {
-                        const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u][r].x));
-                        const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u][r].y));
-                        const float2 w45 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u][r].z));
-                        const float2 w67 = __half22float2(*reinterpret_cast<const __half2*>(&wv[u][r].w));
-                        w[r][0] = w01.x; w[r][1] = w01.y; w[r][2] = w23.x; w[r][3] = w23.y;
-                        w[r][4] = w45.x; w[r][5] = w45.y; w[r][6] = w67.x; w[r][7] = w67.y;
-                    }
-                    #pragma unroll
-                    for (int t = 0; t < T; ++t) {
-                        const float4* xv = reinterpret_cast<const float4*>(xs + (size_t)t * E + 32 * (m0 + u) + 8 * j4);
-                        const float4 x0 = xv[0], x1 = xv[1];
-                        const float xx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                        #pragma unroll
-                        for (int r = 0; r < R; ++r)
-                            #pragma unroll
-                            for (int l = 0; l < 8; ++l) a[r][t][l] = __fmaf_rn(w[r][l], xx[l], a[r][t][l]);
-                    }
-                }
+                    for (int l = 0; l < 8; ++l) a[r][t][l] = __fmaf_rn(w[r][l], xx[l], a[r][t][l]);
             }
         }
         #pragma unroll
@@ -576,13 +595,23 @@ cudaError_t launch_add(const float* a, const float* b, float* out, size_t n, cud
 int lm_head_grid(int num_sms) { return 2 * num_sms; }
 
 cudaError_t launch_lm_head_batch(const LmBatchParams& p, int num_sms, cudaStream_t st) {
-    const size_t smem = (size_t)kLmbTokens * p.E * sizeof(float);
-    if (p.B < 1 || smem > 160 * 1024) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(lm_head_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+    if (p.B < 1 || p.E < 32 || p.E % 32 != 0) return cudaErrorInvalidValue;
     const int groups = (p.B + kLmbTokens - 1) / kLmbTokens;
-    return launch_pdl(lm_head_batch_kernel, dim3(groups, lm_head_batch_ctas(p.B, num_sms)), dim3(kLmThreads), smem, st,
-                      false, p);
+    const dim3 grid(groups, lm_head_batch_ctas(p.B, num_sms));
+    // six steps in flight per thread where they fit beside the activations
+    // (n_embd up to 8192), else two
+    constexpr size_t kMax = 227u * 1024u - 1024u;
+    size_t smem = lm_head_batch_smem(p.E, 6);
+    if (smem <= kMax) {
+        cudaError_t e = cudaFuncSetAttribute(lm_head_batch_kernel<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(lm_head_batch_kernel<6>, grid, dim3(kLmThreads), smem, st, false, p);
+    }
+    smem = lm_head_batch_smem(p.E, 2);
+    if (smem > kMax) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(lm_head_batch_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(lm_head_batch_kernel<2>, grid, dim3(kLmThreads), smem, st, false, p);
 }
 
 int lm_head_batch_ctas(int B, int num_sms) {
