@@ -696,6 +696,27 @@ i2s_gemm_skinny_kernel(const __grid_constant__ SkParams P) {
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
     volatile int* const abort_v = &abort_flag;
+    // no kernel writes the weights, so the weight boxes of the first SP packed
+    // stages go out before the wait for the previous launch (programmatic
+    // serialisation: that launch may still be running); each stage's barrier
+    // expects the whole stage, so it completes only once the activation boxes
+    // issued after the wait have landed too. The producer loop issues those
+    // first SP stages' activations before its first wait, so every box sent
+    // here lands before the CTA can exit.
+    int pre = 0;
+    if (warp == 0 && lane == 0) {
+        for (int t = t_first; t < P.tiles && pre < SP; t += t_step) {
+            int row0;
+            const int sg = seg_of(t, &row0);
+            for (int gi = 0; gi < NG && pre < SP; ++gi, ++pre) {
+                const int kb = kb0 + kSkG * group_of(t, gi);
+                mbar_expect_tx(&bar_loaded[pre], (uint32_t)kSkPStage);
+                uint8_t* pw = PS(pre) + kSkG * kSkN * kBK;
+                tma_load_2d(pw, &P.w[sg], kb * kPK, row0, &bar_loaded[pre]);
+                if (PAIR) tma_load_2d(pw + 64 * kSkG * kPK, &P.w2[sg], kb * kPK, row0, &bar_loaded[pre]);
+            }
+        }
+    }
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
     const int quarter = warp & 3;
@@ -775,14 +796,16 @@ i2s_gemm_skinny_kernel(const __grid_constant__ SkParams P) {
                     const int sp = gs % SP;
                     const uint32_t use = (uint32_t)(gs / SP);
                     if (use > 0 && !gm_wait(&bar_pempty[sp], (use - 1) & 1u, abort_v, P.error, true)) { ok = false; break; }
-                    mbar_expect_tx(&bar_loaded[sp], (uint32_t)kSkPStage);
+                    if (gs >= pre) mbar_expect_tx(&bar_loaded[sp], (uint32_t)kSkPStage);
                     uint8_t* st = PS(sp);
                     #pragma unroll
                     for (int i = 0; i < kSkG; ++i)      // columns past the contraction read as zeros
                         tma_load_2d(st + i * (kSkN * kBK), &P.act, P.kx[sg] + (kb + i) * kBK, 0, &bar_loaded[sp]);
-                    uint8_t* pw = st + kSkG * kSkN * kBK;
-                    tma_load_2d(pw, &P.w[sg], kb * kPK, row0, &bar_loaded[sp]);
-                    if (PAIR) tma_load_2d(pw + 64 * kSkG * kPK, &P.w2[sg], kb * kPK, row0, &bar_loaded[sp]);
+                    if (gs >= pre) {             // else its weights went out before the wait
+                        uint8_t* pw = st + kSkG * kSkN * kBK;
+                        tma_load_2d(pw, &P.w[sg], kb * kPK, row0, &bar_loaded[sp]);
+                        if (PAIR) tma_load_2d(pw + 64 * kSkG * kPK, &P.w2[sg], kb * kPK, row0, &bar_loaded[sp]);
+                    }
                 }
             }
             for (int i = gs > SP ? gs - SP : 0; i < gs; ++i)
