@@ -116,7 +116,7 @@ struct CtaSync {
 };
 
 __global__ void __launch_bounds__(kAttnThreads)
-attention_kernel(const AttnParams p) {
+attention_kernel(const __grid_constant__ AttnParams p) {
     extern __shared__ __align__(16) float sc[];          // n_ctx scores
     __shared__ float qs[kHeadDim], kcur[kHeadDim];
     __shared__ float fred[32];
@@ -129,22 +129,29 @@ attention_kernel(const AttnParams p) {
 // every (head, token) of a chunk whose K and V are already in the cache;
 // two CTAs per SM (128 registers): a batch step launches 1024 of them
 __global__ void __launch_bounds__(kAttnThreads, 2)
-attention_chunk_kernel(const AttnParams p, const int32_t* __restrict__ pos_arr, int E, int G, size_t seq_stride) {
+attention_chunk_kernel(const __grid_constant__ AttnParams p, const int32_t* __restrict__ pos_arr, int E, int G,
+                       size_t seq_stride) {
     extern __shared__ __align__(16) float sc[];
     __shared__ float qs[kHeadDim], kcur[kHeadDim];
     __shared__ float fred[32];
     __shared__ double dred[32];
+    // token t's parameters, once per CTA in shared memory (a per-thread copy
+    // would sit in local memory: the head body takes them by reference)
+    __shared__ AttnParams pt;
     pdl_wait_d();
     const int t = blockIdx.y;
-    AttnParams pt = p;
-    pt.q = p.q + (size_t)t * E;
-    pt.k = p.k + (size_t)t * G;
-    pt.v = p.v + (size_t)t * G;
-    pt.out = p.out + (size_t)t * E;
-    pt.pos_ptr = pos_arr + t;
-    pt.kv_f16 = p.kv_f16 | kAttnKvStored;
-    pt.k_cache = reinterpret_cast<float*>(reinterpret_cast<char*>(p.k_cache) + (size_t)t * seq_stride);
-    pt.v_cache = reinterpret_cast<float*>(reinterpret_cast<char*>(p.v_cache) + (size_t)t * seq_stride);
+    if (threadIdx.x == 0) {
+        pt = p;
+        pt.q = p.q + (size_t)t * E;
+        pt.k = p.k + (size_t)t * G;
+        pt.v = p.v + (size_t)t * G;
+        pt.out = p.out + (size_t)t * E;
+        pt.pos_ptr = pos_arr + t;
+        pt.kv_f16 = p.kv_f16 | kAttnKvStored;
+        pt.k_cache = reinterpret_cast<float*>(reinterpret_cast<char*>(p.k_cache) + (size_t)t * seq_stride);
+        pt.v_cache = reinterpret_cast<float*>(reinterpret_cast<char*>(p.v_cache) + (size_t)t * seq_stride);
+    }
+    __syncthreads();
     attention_head<kAttnThreads>(pt, blockIdx.x, threadIdx.x, sc, qs, kcur, fred, dred, CtaSync());
 }
 

@@ -567,7 +567,7 @@ __device__ __forceinline__ void eng_skip_op(const EngOp& op, int r0, int r_end, 
 // ---------------------------------------------------------------------------
 template <int WA, int WB, bool KV16, bool XCH>
 __global__ void __launch_bounds__(kEngThreads, 1)
-i2s_engine_kernel(const EngParams P) {
+i2s_engine_kernel(const __grid_constant__ EngParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ EngSmem es;
     // dependents may launch now: they take each SM as this kernel's CTA there

@@ -532,7 +532,7 @@ struct SumArgs {
     int n;
     size_t count;
 };
-__global__ void tp_group_sum_kernel(SumArgs a) {
+__global__ void tp_group_sum_kernel(const __grid_constant__ SumArgs a) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < a.count; i += (size_t)gridDim.x * blockDim.x) {
         int s = 0;
         for (int r = 0; r < a.n; ++r) s += a.buf[r][i];
@@ -574,7 +574,7 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-__global__ void __launch_bounds__(1024) tp_exchange_kernel(const XParams x) {
+__global__ void __launch_bounds__(1024) tp_exchange_kernel(const __grid_constant__ XParams x) {
     __shared__ int s_ok;
     const int tid = threadIdx.x;
     const uint32_t epoch = *x.epoch + 1;
