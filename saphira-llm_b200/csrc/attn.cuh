@@ -21,6 +21,7 @@
 // certified reciprocal itself.
 #pragma once
 
+#include <type_traits>
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -179,36 +180,39 @@ __device__ __forceinline__ void attention_head_t(const AttnParams& p, int h, int
 
     // o[d] = sum over s of w_s * v[s][d], sequential in s, with
     // w_s = fl(e_s * inv) (src/ops.c:418-421, src/forward.c:718-724).
-    // r holds rows s .. s+63 as four batches of 16; while whole blocks of 64
-    // rows follow, each batch is refilled with the rows 64 further on as soon
+    // r holds rows s .. s+RB-1 as batches of 16; while whole blocks of RB
+    // rows follow, each batch is refilled with the rows RB further on as soon
     // as it has been added (no bounds predicates in that loop). Then the rows
-    // left in r, and the last ones in batches of 16.
+    // left in r, and the last ones in batches of 16. RB = 64 for the fp32
+    // cache; 32 for the f16 one, whose engine instance has fewer registers
+    // to spare.
     if (pv_d >= 0) {
+        constexpr int RB = std::is_same<KV, float>::value ? 64 : 32;
         const float vcur = vC.round(__ldcg(p.v + kvh * kHeadDim + pv_d));
         const int last = pos > 0 ? pos - 1 : 0;     // loads past the last stored row read that row
-        float r[64];
+        float r[RB];
         float o = 0.0f;
         int s = 0;
         if (pos > 0) {
             #pragma unroll
-            for (int j = 0; j < 64; ++j) r[j] = vC.ld((size_t)min(j, last) * kHeadDim + pv_d);
+            for (int j = 0; j < RB; ++j) r[j] = vC.ld((size_t)min(j, last) * kHeadDim + pv_d);
             #pragma unroll 1
-            for (; s + 64 < pos; s += 64) {
-                // rows s .. s+63 are all stored; refill with the next block
+            for (; s + RB < pos; s += RB) {
+                // rows s .. s+RB-1 are all stored; refill with the next block
                 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
+                for (int b = 0; b < RB / 16; ++b) {
                     #pragma unroll
                     for (int j = 0; j < 16; ++j)
                         o = __fadd_rn(o, __fmul_rn(__fmul_rn(sc[s + 16 * b + j], inv), r[16 * b + j]));
                     #pragma unroll
                     for (int j = 0; j < 16; ++j)
-                        r[16 * b + j] = vC.ld((size_t)min(s + 64 + 16 * b + j, last) * kHeadDim + pv_d);
+                        r[16 * b + j] = vC.ld((size_t)min(s + RB + 16 * b + j, last) * kHeadDim + pv_d);
                 }
             }
             // the last block: rows s .. pos-1
             const int rem = pos - s;
             #pragma unroll
-            for (int b = 0; b < 4; ++b) {
+            for (int b = 0; b < RB / 16; ++b) {
                 if (16 * b < rem) {
                     #pragma unroll
                     for (int j = 0; j < 16; ++j)
