@@ -1,9 +1,9 @@
 """sllm_cuda_layer_chain_device_noalloc: the layer chain for callers that
-cannot allocate device memory (strict graph capture, a host allocator that
-owns the device's memory, no-sync real-time loops). Its scratch is a static
-128 KB device array in the library, so it must give the same bits as the
-context-backed sllm_cuda_layer_chain_device, call after call, and refuse a
-model whose scratch would not fit.
+cannot call cudaMalloc (a host whose allocator already owns the device's
+memory, loops that cannot take cudaMalloc's implicit synchronisation). Its
+scratch is a static 128 KB device array in the library, so it must give the
+same bits as the context-backed sllm_cuda_layer_chain_device, call after
+call, and refuse a model whose scratch would not fit.
 
 Collected last on purpose (file name), so a failure here cannot hide others.
 """
